@@ -1,0 +1,30 @@
+"""Test configuration: the ``gpu`` marker and shared paths.
+
+``-m "not gpu"`` runs the oracle-vs-golden pins, host logic and library-load checks on the CPU;
+``-m gpu`` runs the CUDA parity tests (they need a B200 and the built extension).
+"""
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+for p in (ROOT, ROOT / "tests" / "golden"):
+    if str(p) not in sys.path:
+        sys.path.insert(0, str(p))
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA device (B200) and the built extension")
+
+
+@pytest.fixture(scope="session")
+def golden_gdn():
+    import torch
+    return torch.load(ROOT / "tests" / "golden" / "golden_gdn.pt", weights_only=False)
+
+
+@pytest.fixture(scope="session")
+def golden_layer():
+    import torch
+    return torch.load(ROOT / "tests" / "golden" / "golden_layer.pt", weights_only=False)
