@@ -1,0 +1,16 @@
+"""heimdall_b200: Heimdall's Bifrost converted-layer hot path on NVIDIA B200 (sm_100a).
+
+Host code is Python/PyTorch (device memory, streams, torch.distributed); all arithmetic of the path
+runs in hand-written CUDA kernels behind the C ABI in ``include/bifrost_b200.h``
+(``heimdall_b200/lib/libbifrost_b200.so``, built with ``python -m heimdall_b200.build``).
+There is no CPU fallback: every op raises on CPU tensors or when the library is missing.
+
+Public API (mirrors of the reference ``heimdall`` package):
+  delta_rule_step                    heimdall/kernels.py:132-138
+  BifrostLayer.student               heimdall/hibrit.py:363-424 (HybridAttention._student)
+  BifrostLayer.mem_inputs            heimdall/hibrit.py:327-334
+"""
+from .functional import delta_rule_step, delta_rule_step_gqa  # noqa: F401
+from .layer import BifrostLayer  # noqa: F401
+
+__all__ = ["delta_rule_step", "delta_rule_step_gqa", "BifrostLayer"]

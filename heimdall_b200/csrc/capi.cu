@@ -1,0 +1,96 @@
+// C ABI entry points: argument validation, status codes, per-device state, launch sequencing.
+// Every entry point validates its arguments completely before the first launch and returns a
+// BF_* status; nothing here allocates device memory.
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+#include "capi_internal.h"
+
+namespace bfb {
+
+// device error word (one per device context); kernels receive its address as an argument
+__device__ unsigned int g_bf_error_word = 0;
+
+static std::mutex g_dev_mu;
+static unsigned int* g_err_ptr[64] = {nullptr};
+static int g_sm_count[64] = {0};
+static int g_cc_major[64] = {0};
+
+int device_state(DeviceState* st) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return BF_ERR_NO_DEVICE;
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (!g_err_ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_bf_error_word) != cudaSuccess) return BF_ERR_CUDA;
+    int sms = 0, major = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return BF_ERR_CUDA;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return BF_ERR_CUDA;
+    g_err_ptr[dev] = static_cast<unsigned int*>(p);
+    g_sm_count[dev] = sms;
+    g_cc_major[dev] = major;
+  }
+  if (g_cc_major[dev] != 10) return BF_ERR_NO_DEVICE;
+  st->device = dev;
+  st->err = g_err_ptr[dev];
+  st->sm_count = g_sm_count[dev];
+  return BF_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace bfb
+
+using namespace bfb;
+
+extern "C" {
+
+const char* bf_strerror(int code) {
+  switch (code) {
+    case BF_OK: return "ok";
+    case BF_ERR_INVALID_ARGUMENT: return "invalid argument (null pointer, shape or size)";
+    case BF_ERR_UNSUPPORTED: return "unsupported shape or configuration for this build";
+    case BF_ERR_ALIGNMENT: return "pointer is not 16-byte aligned";
+    case BF_ERR_WORKSPACE: return "workspace too small";
+    case BF_ERR_CUDA: return "CUDA runtime error";
+    case BF_ERR_TIMEOUT: return "a bounded device-side wait gave up";
+    case BF_ERR_NO_DEVICE: return "no sm_100 device is current";
+    default: return "unknown status";
+  }
+}
+
+int bf_abi_version(void) { return BF_ABI_VERSION; }
+
+int bf_device_error(unsigned int* word, bf_stream_t stream) {
+  if (!word) return BF_ERR_INVALID_ARGUMENT;
+  DeviceState st;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  if (cudaStreamSynchronize(stream) != cudaSuccess) return BF_ERR_CUDA;
+  unsigned int v = 0;
+  if (cudaMemcpy(&v, st.err, sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess) return BF_ERR_CUDA;
+  *word = v;
+  if (v) {
+    const unsigned int zero = 0;
+    if (cudaMemcpy(st.err, &zero, sizeof(zero), cudaMemcpyHostToDevice) != cudaSuccess) return BF_ERR_CUDA;
+  }
+  return BF_OK;
+}
+
+int bf_gdn_decode_step(const float* q, const float* k, const void* v, int v_dtype, const float* g,
+                       const float* beta, const float* s_in, float* s_out, float* o, int B, int G, int R,
+                       int D, bf_stream_t stream) {
+  if (!q || !k || !v || !g || !beta || !s_in || !s_out || !o) return BF_ERR_INVALID_ARGUMENT;
+  if (B <= 0 || G <= 0 || R <= 0 || R > 8 || D <= 0 || D > 256 || (D % 32) != 0) return BF_ERR_INVALID_ARGUMENT;
+  if (v_dtype != BF_F32 && v_dtype != BF_BF16) return BF_ERR_INVALID_ARGUMENT;
+  if (!aligned16(s_in) || !aligned16(s_out)) return BF_ERR_ALIGNMENT;
+  if ((long long)B * G > 65535) return BF_ERR_UNSUPPORTED;
+  DeviceState st;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  return launch_gdn_decode(q, k, v, v_dtype == BF_BF16, g, beta, s_in, s_out, o, B, G, R, D, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,398 @@
+// Memory-path input projections (heimdall/hibrit.py:327-334, _mem_inputs) on the 5th-gen tensor core.
+//
+//  head_proj: qm = unit(q_h fq_h) D^-1/2 (h < H) and km = unit(k_g fk_g) (g < G).  Per head a GEMM
+//             [tokens x 256] x [256 x 256]; the weights are pre-transposed to fp16 (K-major B operand)
+//             and stay resident in shared memory while a CTA walks its token tiles; q/k arrive in
+//             bf16 and are converted to fp16 while being staged (both MMA operands must share a type,
+//             and fp16 keeps the weights to 11 significant bits).  The L2 normalisation is the
+//             epilogue: one thread owns one accumulator row (one TMEM lane).
+//  x_proj:    [a | b | mix] = x [ab_w; mix_w]^T (+ bias), d = hidden size.  x is bf16, the fp32 weights
+//             are split into bf16 hi + lo rows (x*hi + x*lo carries ~16 significant bits), so one
+//             N=64 GEMM produces both halves; the epilogue forms g, beta and the gate logit.
+#include "capi_internal.h"
+#include "common.cuh"
+#include "tmap.h"
+
+namespace bfb {
+
+// ============================================================================ weight preparation
+// fq [nh][D][D] fp32 (d, e) -> wt [nh][D][D] fp16 (e, d) : B operand rows = output feature e
+__global__ void prep_head_weights_kernel(const float* __restrict__ w, __half* __restrict__ wt, int D) {
+  __shared__ float tile[32][33];
+  const int h = blockIdx.z;
+  const int d0 = blockIdx.y * 32, e0 = blockIdx.x * 32;
+  const float* src = w + (size_t)h * D * D;
+  __half* dst = wt + (size_t)h * D * D;
+  for (int i = threadIdx.y; i < 32; i += 8) tile[i][threadIdx.x] = src[(size_t)(d0 + i) * D + e0 + threadIdx.x];
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += 8)
+    dst[(size_t)(e0 + i) * D + d0 + threadIdx.x] = __float2half_rn(tile[threadIdx.x][i]);
+}
+
+// [ab_w; mix_w] (nout rows x d) fp32 -> hi/lo bf16 [64][d] (rows 0..31 hi, 32..63 lo, zero padded)
+__global__ void prep_x_weights_kernel(const float* __restrict__ ab_w, const float* __restrict__ mix_w, int n_ab,
+                                      int n_mix, int d, __nv_bfloat16* __restrict__ out) {
+  const int row = blockIdx.y;  // 0..31
+  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < d; c += gridDim.x * blockDim.x) {
+    float w = 0.f;
+    if (row < n_ab) w = ab_w[(size_t)row * d + c];
+    else if (row < n_ab + n_mix) w = mix_w[(size_t)(row - n_ab) * d + c];
+    const __nv_bfloat16 hi = __float2bfloat16_rn(w);
+    const __nv_bfloat16 lo = __float2bfloat16_rn(w - __bfloat162float(hi));
+    out[(size_t)row * d + c] = hi;
+    out[(size_t)(row + 32) * d + c] = lo;
+  }
+}
+
+// ============================================================================ head projection
+constexpr int kHP_M = 128;                  // tokens per tile
+constexpr int kHP_D = 256;                  // head dim (K and N)
+constexpr int kHP_Threads = 256;            // warps 0-3 epilogue, warps 4-7 staging + MMA issue
+constexpr int kHP_SmemA = kHP_M * kHP_D * 2;        // 64 KB
+constexpr int kHP_SmemB = kHP_D * kHP_D * 2;        // 128 KB
+constexpr int kHP_Smem = kHP_SmemA + kHP_SmemB + 1024 + 256;
+
+struct HeadProjArgs {
+  const __nv_bfloat16* q;  // [B,T,H,D]
+  const __nv_bfloat16* k;  // [B,T,G,D]
+  float* qm;               // [B,T,H,D]
+  float* km;               // [B,T,G,D]
+  int B, T, H, G;
+  int tiles_per_cta;       // token tiles walked by one CTA
+  unsigned int* err;
+};
+
+__global__ void __launch_bounds__(kHP_Threads, 1)
+    head_proj_kernel(const __grid_constant__ CUtensorMap wmap, HeadProjArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + kHP_SmemA;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + kHP_SmemB);
+  uint64_t* bar_b = bars + 0;      // weights landed (TMA)
+  uint64_t* bar_mma = bars + 1;    // MMA finished reading A
+  uint64_t* bar_full = bars + 2;   // [2] accumulator ready
+  uint64_t* bar_free = bars + 4;   // [2] accumulator drained (128 arrivals)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 6);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 7);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int head = blockIdx.y;     // 0..H+G-1
+  const int b = blockIdx.z;
+  const bool is_q = head < a.H;
+  const int nheads_src = is_q ? a.H : a.G;
+  const int hsrc = is_q ? head : head - a.H;
+  const __nv_bfloat16* src = is_q ? a.q : a.k;
+  float* dst = is_q ? a.qm : a.km;
+  const float out_scale = is_q ? rsqrtf((float)kHP_D) : 1.f;
+  const int ntiles = (a.T + kHP_M - 1) / kHP_M;
+  const int tile0 = blockIdx.x * a.tiles_per_cta;
+  const int tile1 = min(ntiles, tile0 + a.tiles_per_cta);
+
+  if (tid == 0) {
+    mbar_init(bar_b, 1);
+    mbar_init(bar_mma, 1);
+    mbar_init(&bar_full[0], 1);
+    mbar_init(&bar_full[1], 1);
+    mbar_init(&bar_free[0], 128);
+    mbar_init(&bar_free[1], 128);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp >= 4) {
+    // ---------------------------------------------------------------- staging + MMA issue
+    const int st = tid - 128;  // 0..127: one row each
+    if (st == 0) {
+      tma_prefetch(&wmap);
+      mbar_expect_tx(bar_b, kHP_SmemB);
+      tma_load_3d(sB, &wmap, bar_b, 0, head * kHP_D, 0);
+    }
+    for (int it = tile0; it < tile1; ++it) {
+      const int i = it - tile0;
+      if (i > 0 && !mbar_wait(bar_mma, (i - 1) & 1, abort_flag, a.err, 0x11)) break;
+      // row st of this tile: 256 bf16 -> fp16, 16-byte chunks into the SW128 layout
+      const int t = it * kHP_M + st;
+      if (t < a.T) {
+        const uint4* rp = reinterpret_cast<const uint4*>(src + (((size_t)b * a.T + t) * nheads_src + hsrc) * kHP_D);
+#pragma unroll 4
+        for (int c = 0; c < 32; ++c) {  // 32 chunks of 8 elements
+          uint4 u = rp[c];
+          uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float lo = __uint_as_float(w[j] << 16), hi = __uint_as_float(w[j] & 0xffff0000u);
+            w[j] = pack_half2(lo, hi);
+          }
+          const int atom = c >> 3, col = (c & 7) * 8;
+          *reinterpret_cast<uint4*>(sA + atom * (kHP_M * 128) + sw128_offset(st, col)) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      } else {
+#pragma unroll 4
+        for (int c = 0; c < 32; ++c) {
+          const int atom = c >> 3, col = (c & 7) * 8;
+          *reinterpret_cast<uint4*>(sA + atom * (kHP_M * 128) + sw128_offset(st, col)) = make_uint4(0, 0, 0, 0);
+        }
+      }
+      fence_async_smem();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (*abort_flag) break;
+      if (st == 0) {
+        bool ok = true;
+        if (i == 0) ok = mbar_wait(bar_b, 0, abort_flag, a.err, 0x12);
+        const int buf = i & 1;
+        if (ok && i >= 2) ok = mbar_wait(&bar_free[buf], ((i >> 1) - 1) & 1, abort_flag, a.err, 0x13);
+        if (ok) {
+          tc_fence_after();
+          const uint32_t d = tmem + buf * 256;
+          const uint32_t aB = smem_u32(sA), bB = smem_u32(sB);
+          constexpr uint32_t idesc = idesc_f16(kHP_M, kHP_D, 0);
+#pragma unroll
+          for (int ks = 0; ks < kHP_D / 16; ++ks)
+            umma_f16_ss(d, sdesc_kstep(aB, kHP_M, ks), sdesc_kstep(bB, kHP_D, ks), idesc, ks > 0);
+          umma_commit(bar_mma);
+          umma_commit(&bar_full[buf]);
+        }
+      }
+    }
+    // drain: the weights TMA must have landed before the CTA may exit
+    if (st == 0) mbar_wait(bar_b, 0, nullptr, a.err, 0x14);
+  } else {
+    // ---------------------------------------------------------------- epilogue: one row per thread
+    const int row = tid;  // TMEM lane
+    for (int it = tile0; it < tile1; ++it) {
+      const int i = it - tile0, buf = i & 1;
+      if (!mbar_wait(&bar_full[buf], (i >> 1) & 1, abort_flag, a.err, 0x15)) break;
+      tc_fence_after();
+      const uint32_t base = tmem + ((uint32_t)(warp * 32) << 16) + buf * 256;
+      float ss = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < kHP_D; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(base + c, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float x = __uint_as_float(r[j]);
+          ss += x * x;
+        }
+      }
+      const float inv = out_scale / fmaxf(sqrtf(ss), 1e-12f);
+      const int t = it * kHP_M + row;
+      float* op = dst + (((size_t)b * a.T + t) * nheads_src + hsrc) * kHP_D;
+#pragma unroll 1
+      for (int c = 0; c < kHP_D; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(base + c, r);
+        tmem_wait_ld();
+        if (t < a.T) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<float4*>(op + c + j) =
+                make_float4(__uint_as_float(r[j]) * inv, __uint_as_float(r[j + 1]) * inv,
+                            __uint_as_float(r[j + 2]) * inv, __uint_as_float(r[j + 3]) * inv);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&bar_free[buf]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ============================================================================ x projection
+constexpr int kXP_M = 128;
+constexpr int kXP_N = 64;        // 32 hi + 32 lo
+constexpr int kXP_Stages = 4;
+constexpr int kXP_StageA = kXP_M * 64 * 2;   // 16 KB
+constexpr int kXP_StageB = kXP_N * 64 * 2;   // 8 KB
+constexpr int kXP_Smem = kXP_Stages * (kXP_StageA + kXP_StageB) + 1024 + 256;
+
+struct XProjArgs {
+  const float* ab_b;      // [2G]
+  const float* mix_b;     // [H]
+  const float* A_log;     // [G]
+  const float* dt_bias;   // [G]
+  const float* decay_mask;// [G]
+  const float* mix_lse;   // unused here
+  float* g;               // [M, G]
+  float* beta;            // [M, G]
+  float* mixx;            // [M, H]
+  const int64_t* pos;     // [M] or null
+  long long pos0;         // position of row 0 of each batch when pos == null
+  int M, T, d, G, H, sinks;
+  unsigned int* err;
+};
+
+__global__ void __launch_bounds__(192, 1)
+    x_proj_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap, XProjArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + kXP_Stages * kXP_StageA;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + kXP_Stages * kXP_StageB);
+  uint64_t* full = bars;                 // [stages]
+  uint64_t* empty = bars + kXP_Stages;   // [stages]
+  uint64_t* done = bars + 2 * kXP_Stages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kXP_Stages + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * kXP_Stages + 2);
+
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int m0 = blockIdx.x * kXP_M;
+  const int nk = (a.d + 63) / 64;
+  if (tid == 0) {
+    for (int s = 0; s < kXP_Stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 64);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (tid == 0) {
+      tma_prefetch(&xmap);
+      tma_prefetch(&wmap);
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % kXP_Stages;
+        if (kb >= kXP_Stages && !mbar_wait(&empty[s], ((kb / kXP_Stages) - 1) & 1, abort_flag, a.err, 0x21)) break;
+        mbar_expect_tx(&full[s], kXP_StageA + kXP_StageB);
+        tma_load_3d(sA + s * kXP_StageA, &xmap, &full[s], 0, m0, kb);
+        tma_load_3d(sB + s * kXP_StageB, &wmap, &full[s], 0, 0, kb);
+      }
+      // drain: every issued load must have landed before exit
+      const int last = nk - 1;
+      for (int kb = (last - kXP_Stages + 1 > 0 ? last - kXP_Stages + 1 : 0); kb <= last; ++kb)
+        mbar_wait(&full[kb % kXP_Stages], (kb / kXP_Stages) & 1, nullptr, a.err, 0x22);
+    }
+  } else if (warp == 1) {
+    if (tid == 32) {
+      constexpr uint32_t idesc = idesc_f16(kXP_M, kXP_N, 1);
+      bool ok = true;
+      for (int kb = 0; kb < nk && ok; ++kb) {
+        const int s = kb % kXP_Stages;
+        ok = mbar_wait(&full[s], (kb / kXP_Stages) & 1, abort_flag, a.err, 0x23);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t aB = smem_u32(sA + s * kXP_StageA), bB = smem_u32(sB + s * kXP_StageB);
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          umma_f16_ss(tmem, sdesc_kstep(aB, kXP_M, ks), sdesc_kstep(bB, kXP_N, ks), idesc, (kb | ks) > 0);
+        umma_commit(&empty[s]);
+      }
+      if (ok) umma_commit(done);
+    }
+  } else {
+    // epilogue warps 2..5 -> TMEM lane quarter (warp % 4)
+    const int q4 = warp & 3;
+    const int row = q4 * 32 + (tid & 31);
+    if (mbar_wait(done, 0, abort_flag, a.err, 0x24)) {
+      tc_fence_after();
+      uint32_t ra[32], rb[32];  // columns 0..31: x*hi, 32..63: x*lo
+      const uint32_t base = tmem + ((uint32_t)(q4 * 32) << 16);
+      tmem_ld32(base, ra);
+      tmem_ld32(base + 32, rb);
+      tmem_wait_ld();
+      float r[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) r[j] = __uint_as_float(ra[j]) + __uint_as_float(rb[j]);
+      const int m = m0 + row;
+      if (m < a.M) {
+        const int G = a.G, H = a.H;
+        const long long p = a.pos ? (long long)a.pos[m] : a.pos0 + (m % a.T);
+        for (int gi = 0; gi < G; ++gi) {
+          const float av = r[gi] + a.ab_b[gi];
+          const float bv = r[G + gi] + a.ab_b[G + gi];
+          const float z = av + a.dt_bias[gi];
+          const float sp = z > 20.f ? z : log1pf(__expf(z));
+          a.g[(size_t)m * G + gi] = -__expf(a.A_log[gi]) * sp * a.decay_mask[gi];
+          a.beta[(size_t)m * G + gi] = (p >= a.sinks) ? 1.f / (1.f + __expf(-bv)) : 0.f;
+        }
+        for (int h = 0; h < H; ++h)
+          a.mixx[(size_t)m * H + h] = r[2 * G + h] + a.mix_b[h];
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 64);
+  }
+}
+
+// ============================================================================ launchers
+int launch_prep_weights(const float* fq, const float* fk, const float* ab_w, const float* mix_w, int H, int G,
+                        int D, int d, __half* w_heads, __nv_bfloat16* w_x, cudaStream_t stream) {
+  dim3 blk(32, 8);
+  prep_head_weights_kernel<<<dim3(D / 32, D / 32, H), blk, 0, stream>>>(fq, w_heads, D);
+  prep_head_weights_kernel<<<dim3(D / 32, D / 32, G), blk, 0, stream>>>(fk, w_heads + (size_t)H * D * D, D);
+  prep_x_weights_kernel<<<dim3((d + 255) / 256, 32), 256, 0, stream>>>(ab_w, mix_w, 2 * G, H, d, w_x);
+  return cudaGetLastError() == cudaSuccess ? BF_OK : BF_ERR_CUDA;
+}
+
+int launch_head_proj(const __nv_bfloat16* q, const __nv_bfloat16* k, const __half* w_heads, float* qm, float* km,
+                     int B, int T, int H, int G, int sm_count, unsigned int* err, cudaStream_t stream) {
+  CUtensorMap wmap;
+  int rc = make_tmap_kmajor(&wmap, w_heads, BF_F16, (uint64_t)(H + G) * kHP_D, kHP_D, kHP_D, kHP_D, 4);
+  if (rc) return rc;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(head_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kHP_Smem) != cudaSuccess)
+      return BF_ERR_CUDA;
+    attr = true;
+  }
+  const int ntiles = (T + kHP_M - 1) / kHP_M;
+  // enough CTAs to fill the GPU once, each walking a run of token tiles with its weights resident
+  const long long units = (long long)(H + G) * B;
+  int per = (int)((ntiles * units + sm_count - 1) / sm_count);
+  per = per < 1 ? 1 : (per > ntiles ? ntiles : per);
+  HeadProjArgs a{q, k, qm, km, B, T, H, G, per, err};
+  dim3 grid((ntiles + per - 1) / per, H + G, B);
+  head_proj_kernel<<<grid, kHP_Threads, kHP_Smem, stream>>>(wmap, a);
+  return cudaGetLastError() == cudaSuccess ? BF_OK : BF_ERR_CUDA;
+}
+
+int launch_x_proj(const __nv_bfloat16* x, const __nv_bfloat16* w_x, const float* ab_b, const float* mix_b,
+                  const float* A_log, const float* dt_bias, const float* decay_mask, float* g, float* beta,
+                  float* mixx, const int64_t* pos, long long pos0, int M, int T, int d, int G, int H, int sinks,
+                  unsigned int* err, cudaStream_t stream) {
+  CUtensorMap xmap, wmap;
+  int rc = make_tmap_kmajor(&xmap, x, BF_BF16, (uint64_t)M, d, d, kXP_M, 1);
+  if (rc) return rc;
+  rc = make_tmap_kmajor(&wmap, w_x, BF_BF16, 64, d, d, kXP_N, 1);
+  if (rc) return rc;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(x_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kXP_Smem) != cudaSuccess)
+      return BF_ERR_CUDA;
+    attr = true;
+  }
+  XProjArgs a{ab_b, mix_b, A_log, dt_bias, decay_mask, nullptr, g, beta, mixx, pos, pos0, M, T, d, G, H, sinks, err};
+  x_proj_kernel<<<(M + kXP_M - 1) / kXP_M, 192, kXP_Smem, stream>>>(xmap, wmap, a);
+  return cudaGetLastError() == cudaSuccess ? BF_OK : BF_ERR_CUDA;
+}
+
+}  // namespace bfb

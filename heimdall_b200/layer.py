@@ -1,0 +1,170 @@
+"""The converted Bifrost layer core on B200: the host mirror of ``HybridAttention._student``.
+
+``BifrostLayer`` holds a converted layer's parameters on the device plus their tensor-core operand
+layout, and ``BifrostLayer.student`` has the signature and cache-dict semantics of the reference's
+``HybridAttention._student(x, q, k, v, qr, kr, start, cache, memory)`` (heimdall/hibrit.py:363-424):
+the cache keeps the reference's keys and layouts (ring_k, ring_v, ring_km, ring_g, ring_beta, ring_pos,
+sink_k, sink_v, S), so caches are interchangeable with the reference's and ``HybridLM.cache_bytes``
+sees the same constant footprint.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from .functional import check_cuda, ptr, stream_handle
+from .structs import BfLayer, BfRingCache
+
+PARAM_NAMES = ("fq", "fk", "ab_w", "ab_b", "mix_w", "mix_b", "mix_lse", "mem_scale", "A_log", "dt_bias",
+               "decay_mask")
+
+
+def _aligned_bytes(n: int, device, align: int = 1024) -> torch.Tensor:
+    buf = torch.empty(n + align, dtype=torch.uint8, device=device)
+    off = (-buf.data_ptr()) % align
+    return buf[off:off + n]
+
+
+class BifrostLayer:
+    """A converted layer's parameters on one CUDA device.
+
+    ``params`` maps the names in ``PARAM_NAMES`` to tensors (any device/dtype; stored fp32), shaped as
+    HybridAttention.convert creates them (heimdall/hibrit.py:211-240): fq [H,D,D], fk [G,D,D],
+    ab_w [2G,d], ab_b [2G], mix_w [H,d], mix_b [H], mix_lse [H], mem_scale [H], A_log [G], dt_bias [G],
+    decay_mask [G].
+    """
+
+    def __init__(self, params: dict, window: int, sinks: int, device=None):
+        device = torch.device(device or "cuda")
+        if device.type != "cuda":
+            raise RuntimeError("heimdall_b200 runs on CUDA only (there is no CPU fallback)")
+        self.device = device
+        self.p = {n: params[n].detach().to(device=device, dtype=torch.float32).contiguous() for n in PARAM_NAMES}
+        self.window, self.sinks = int(window), int(sinks)
+        self.H, D = self.p["fq"].shape[0], self.p["fq"].shape[-1]
+        self.G, self.D, self.d = self.p["fk"].shape[0], D, self.p["ab_w"].shape[1]
+        self.R = self.H // self.G
+        nbytes = _lib.size("bf_layer_weights_bytes", self.H, self.G, self.D, self.d)
+        self.wbuf = _aligned_bytes(nbytes, device)
+        self.refresh()
+
+    @classmethod
+    def from_module(cls, attn, device=None) -> "BifrostLayer":
+        """From a converted reference ``HybridAttention`` (its new parameters and decay_mask buffer)."""
+        params = dict(fq=attn.fq, fk=attn.fk, ab_w=attn.ab.weight, ab_b=attn.ab.bias, mix_w=attn.mix.weight,
+                      mix_b=attn.mix.bias, mix_lse=attn.mix_lse, mem_scale=attn.mem_scale, A_log=attn.A_log,
+                      dt_bias=attn.dt_bias, decay_mask=attn.decay_mask)
+        return cls(params, attn.window, attn.sinks, device)
+
+    @classmethod
+    def from_params(cls, lp, device=None) -> "BifrostLayer":
+        """From any object with the parameter attributes (e.g. the test oracle's ``LayerParams``)."""
+        return cls({n: getattr(lp, n) for n in PARAM_NAMES}, lp.window, lp.sinks, device)
+
+    def refresh(self) -> None:
+        """Rebuild the operand layouts after the parameters changed."""
+        p = self.p
+        with torch.cuda.device(self.device):
+            _lib.call("bf_prepare_layer_weights", ptr(p["fq"]), ptr(p["fk"]), ptr(p["ab_w"]), ptr(p["mix_w"]),
+                      self.H, self.G, self.D, self.d, ptr(self.wbuf), self.wbuf.numel(), stream_handle())
+        self._struct = BfLayer(ptr(self.wbuf), ptr(p["ab_b"]), ptr(p["mix_b"]), ptr(p["mix_lse"]),
+                               ptr(p["mem_scale"]), ptr(p["A_log"]), ptr(p["dt_bias"]), ptr(p["decay_mask"]),
+                               self.H, self.G, self.D, self.d, self.window, self.sinks)
+
+    @property
+    def struct(self) -> BfLayer:
+        return self._struct
+
+    # ------------------------------------------------------------------ memory inputs
+    def mem_inputs(self, x, q, k, pos0: int = 0, pos=None):
+        """qm, km, g, beta, mixx for tokens at positions pos0.. (mirror of _mem_inputs, hibrit.py:327-334).
+
+        x [B,t,d], q [B,t,H,D], k [B,t,G,D] (bf16); returns qm [B,t,H,D], km [B,t,G,D], g, beta [B,t,G],
+        mixx [B,t,H] (= mix(x), the input term of the gate), all fp32.
+        """
+        check_cuda(x, q, k)
+        B, t = x.shape[:2]
+        dev = x.device
+        xb, qb, kb = (z.to(torch.bfloat16).contiguous() for z in (x, q, k))
+        qm = torch.empty(B, t, self.H, self.D, device=dev, dtype=torch.float32)
+        km = torch.empty(B, t, self.G, self.D, device=dev, dtype=torch.float32)
+        g = torch.empty(B, t, self.G, device=dev, dtype=torch.float32)
+        beta = torch.empty_like(g)
+        mixx = torch.empty(B, t, self.H, device=dev, dtype=torch.float32)
+        posp = None if pos is None else pos.to(device=dev, dtype=torch.int64).contiguous()
+        _lib.call("bf_mem_inputs", ctypes_ref(self._struct), ptr(xb), ptr(qb), ptr(kb), ptr(posp), int(pos0), B, t,
+                  ptr(qm), ptr(km), ptr(g), ptr(beta), ptr(mixx), stream_handle())
+        return qm, km, g, beta, mixx
+
+    # ------------------------------------------------------------------ the layer core
+    def student(self, x, q, k, v, qr, kr, start: int, cache=None, memory: bool = True):
+        """Mirror of ``HybridAttention._student`` (heimdall/hibrit.py:363-424); returns o [B,t,H,D] fp32."""
+        check_cuda(x, q, k, v, qr, kr)
+        t = x.shape[1]
+        if cache is not None and t == 1 and "ring_k" in cache:
+            return self._decode(x, q, k, v, qr, kr, int(start), cache, memory)
+        raise NotImplementedError("prefill path not built yet")
+
+    def _decode(self, x, q, k, v, qr, kr, start, cache, memory):
+        B = x.shape[0]
+        H, G, D, W, S = self.H, self.G, self.D, self.window, self.sinks
+        dev = x.device
+        bf = torch.bfloat16
+        xb = x.reshape(B, -1).to(bf).contiguous()
+        qb = q.reshape(B, H, D).to(bf).contiguous()
+        kb = k.reshape(B, G, D).to(bf).contiguous()
+        vb = v.reshape(B, G, D).to(bf).contiguous()
+        qrb = qr.reshape(B, H, D).to(bf).contiguous()
+        krb = kr.reshape(B, G, D).to(bf).contiguous()
+        # sinks: the first S tokens are kept (hibrit.py:369-373)
+        if start < S:
+            nk, nv = krb[:, :, None], vb[:, :, None]
+            sk, sv = cache.get("sink_k"), cache.get("sink_v")
+            cache["sink_k"] = nk if sk is None else torch.cat((sk.to(bf), nk), 2)
+            cache["sink_v"] = nv if sv is None else torch.cat((sv.to(bf), nv), 2)
+        sk, sv = cache.get("sink_k"), cache.get("sink_v")
+        if sk is not None:
+            sk, sv = sk.to(bf).contiguous(), sv.to(bf).contiguous()
+            cache["sink_k"], cache["sink_v"] = sk, sv
+        ns = 0 if sk is None else sk.shape[2]
+        use_mem = bool(memory) and start + 1 > W
+        for key, dt in (("ring_k", bf), ("ring_v", bf), ("ring_km", torch.float32), ("ring_g", torch.float32),
+                        ("ring_beta", torch.float32), ("ring_pos", torch.int64)):
+            tns = cache[key]
+            if tns.dtype != dt or not tns.is_contiguous() or tns.device != dev:
+                cache[key] = tns.to(device=dev, dtype=dt).contiguous()
+        if use_mem:
+            s0 = cache.get("S")
+            if s0 is None:
+                cache["S"] = torch.zeros(B, G, D, D, device=dev, dtype=torch.float32)
+            elif s0.dtype != torch.float32 or not s0.is_contiguous():
+                cache["S"] = s0.float().contiguous()
+        Sst = cache.get("S") if use_mem else None
+        rc = BfRingCache(ptr(cache["ring_k"]), ptr(cache["ring_v"]), ptr(cache["ring_km"]), ptr(cache["ring_g"]),
+                         ptr(cache["ring_beta"]), ptr(cache["ring_pos"]), 0, ptr(sk), ptr(sv), ns,
+                         ptr(Sst) if Sst is not None else ptr(_dummy_state(dev)))
+        pos = torch.full((B,), start, device=dev, dtype=torch.int64)
+        o = torch.empty(B, H, D, device=dev, dtype=torch.float32)
+        nws = _lib.size("bf_layer_decode_workspace", B, H, G, D, W)
+        ws = torch.empty(nws, dtype=torch.uint8, device=dev)
+        _lib.call("bf_bifrost_layer_decode", ctypes_ref(self._struct), ptr(xb), ptr(qb), ptr(kb), ptr(vb), ptr(qrb),
+                  ptr(krb), ptr(pos), B, ctypes_ref(rc), 1 if use_mem else 0, ptr(o), 0, ptr(ws), nws,
+                  stream_handle())
+        return o.reshape(B, 1, H, D)
+
+
+_DUMMY = {}
+
+
+def _dummy_state(dev):
+    # a 16-byte-aligned placeholder for the state pointer when memory is off (never read or written)
+    key = str(dev)
+    if key not in _DUMMY:
+        _DUMMY[key] = torch.zeros(4, device=dev, dtype=torch.float32)
+    return _DUMMY[key]
+
+
+def ctypes_ref(s):
+    """Address of a ctypes struct, for the c_void_p struct-pointer arguments (the struct outlives the call)."""
+    import ctypes
+    return ctypes.addressof(s)

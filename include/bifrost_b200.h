@@ -1,0 +1,142 @@
+/*
+ * bifrost_b200.h -- C ABI of the B200 (sm_100a) implementation of Heimdall's Bifrost
+ * converted-layer hot path.
+ *
+ * Conventions (every entry point):
+ *   - all tensor arguments are device pointers to contiguous row-major arrays in the layouts
+ *     written beside each argument; sizes are plain ints;
+ *   - work is enqueued on the caller's `stream` (NULL = legacy default stream); nothing blocks
+ *     except bf_device_error();
+ *   - outputs and scratch (`ws`, `ws_bytes`) are allocated by the caller; the matching
+ *     *_workspace() call returns the scratch bytes needed; no entry point allocates memory;
+ *   - return value: BF_OK (0) or a BF_ERR_* code; bf_strerror() names it; arguments are
+ *     validated (shapes, alignment, sizes) before anything is launched;
+ *   - outputs are fp32, as in the reference (o, state, lse).
+ * Element-type codes: BF_F32, BF_BF16 (and BF_F16 where stated).
+ *
+ * Reference interfaces each entry point replaces are cited as path:line inside the reference
+ * project ValeroisAI/Heimdall.
+ */
+#ifndef BIFROST_B200_H
+#define BIFROST_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#ifndef BF_STREAM_T_DEFINED
+#define BF_STREAM_T_DEFINED
+typedef struct CUstream_st* bf_stream_t; /* == cudaStream_t */
+#endif
+
+enum {
+  BF_OK = 0,
+  BF_ERR_INVALID_ARGUMENT = 1, /* null pointer, bad shape or size */
+  BF_ERR_UNSUPPORTED = 2,      /* a shape this build does not implement (e.g. D != 256 on a tensor-core path) */
+  BF_ERR_ALIGNMENT = 3,        /* pointer not 16-byte aligned */
+  BF_ERR_WORKSPACE = 4,        /* ws_bytes smaller than the *_workspace() size */
+  BF_ERR_CUDA = 5,             /* a CUDA runtime call failed (launch, attribute, tensor map) */
+  BF_ERR_TIMEOUT = 6,          /* a bounded device-side wait gave up (see bf_device_error) */
+  BF_ERR_NO_DEVICE = 7         /* no sm_100 device is current */
+};
+
+enum { BF_F32 = 0, BF_BF16 = 1, BF_F16 = 2 };
+
+/* Human-readable name of a status code. */
+const char* bf_strerror(int code);
+
+/* ABI version of this library (bumped on any signature change). */
+int bf_abi_version(void);
+
+/* Synchronises `stream`, then reads and clears this device's error word.  *word = 0 when no
+ * kernel gave up a wait; otherwise (site << 8) | BF_ERR_TIMEOUT.  Returns BF_OK or BF_ERR_CUDA. */
+int bf_device_error(unsigned int* word, bf_stream_t stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Gated delta rule, recurrent decode step (one token), GQA-native.
+ * Replaces heimdall/kernels.py:132-138 (delta_rule_step) and the inline decode update of
+ * heimdall/hibrit.py:398-403.
+ *   S <- e^{g} S;  delta = (v - S^T k) * beta;  S <- S + k delta^T;  o_r = S^T q_r  (r < R)
+ * q    [B,G,R,D] fp32          k [B,G,D] fp32        v [B,G,D] (v_dtype: BF_F32 or BF_BF16)
+ * g, beta [B,G] fp32           s_in, s_out [B,G,D,D] fp32 (may alias)      o [B,G,R,D] fp32
+ * D must be 256 or a multiple of 32 not above 256.
+ */
+int bf_gdn_decode_step(const float* q, const float* k, const void* v, int v_dtype, const float* g,
+                       const float* beta, const float* s_in, float* s_out, float* o, int B, int G, int R,
+                       int D, bf_stream_t stream);
+
+
+/* ------------------------------------------------------------------------------------------
+ * Per-layer parameters (device pointers; fp32 unless stated).  Shapes follow
+ * HybridAttention.convert (heimdall/hibrit.py:211-240).
+ */
+typedef struct bf_layer {
+  const void* wbuf;          /* prepared operand weights (bf_prepare_layer_weights) */
+  const float* ab_b;         /* [2G]  bias of ab = Linear(d, 2G) */
+  const float* mix_b;        /* [H]   bias of mix = Linear(d, H) */
+  const float* mix_lse;      /* [H] */
+  const float* mem_scale;    /* [H] */
+  const float* A_log;        /* [G] */
+  const float* dt_bias;      /* [G] */
+  const float* decay_mask;   /* [G]   0 = archival (never-forgetting) head */
+  int H, G, D, d, window, sinks;
+} bf_layer;
+
+/* Decode cache in the reference's per-layer cache-dict layout (heimdall/hibrit.py:414-423). */
+typedef struct bf_ring_cache {
+  void* ring_k;              /* [B,G,W,D] bf16, slot = position % W */
+  void* ring_v;              /* [B,G,W,D] bf16 */
+  float* ring_km;            /* [B,W,G,D] */
+  float* ring_g;             /* [B,W,G] */
+  float* ring_beta;          /* [B,W,G] */
+  int64_t* ring_pos;         /* [W] (ring_pos_bstride 0) or [B,W] (ring_pos_bstride W); -1 = empty */
+  long long ring_pos_bstride;
+  const void* sink_k;        /* [B,G,ns,D] bf16 (positions 0..ns-1) or NULL */
+  const void* sink_v;
+  int ns;
+  float* S;                  /* [B,G,D,D] memory state, updated in place */
+} bf_ring_cache;
+
+/* Bytes of the prepared weight buffer of one layer. */
+size_t bf_layer_weights_bytes(int H, int G, int D, int d);
+
+/* Convert the fp32 parameters fq [H,D,D], fk [G,D,D], ab_w [2G,d], mix_w [H,d] into the operand
+ * layouts of the tensor-core kernels (fp16 transposed head maps, bf16 hi/lo split of the x maps).
+ * Call once per layer (and again after the parameters change). */
+int bf_prepare_layer_weights(const float* fq, const float* fk, const float* ab_w, const float* mix_w, int H,
+                             int G, int D, int d, void* wbuf, size_t wbytes, bf_stream_t stream);
+
+/* Memory inputs and gate logit, replacing heimdall/hibrit.py:327-334 (_mem_inputs) and the
+ * mix(x) term of heimdall/hibrit.py:409:
+ *   qm = unit(q_h fq_h) D^-1/2 [B,T,H,D]; km = unit(k_g fk_g) [B,T,G,D];
+ *   g = -e^{A_log} softplus(a + dt_bias) decay_mask, beta = sigmoid(b) [pos >= sinks]  [B,T,G];
+ *   mixx = x mix_w^T + mix_b [B,T,H]   where [a | b] = x ab_w^T + ab_b.
+ * x [B,T,d], q [B,T,H,D], k [B,T,G,D] are bf16.  pos [B*T] int64 or NULL (then pos0 + t).
+ * D must be 256; d a multiple of 64. */
+int bf_mem_inputs(const bf_layer* L, const void* x, const void* q, const void* k, const int64_t* pos,
+                  long long pos0, int B, int T, float* qm, float* km, float* g, float* beta, float* mixx,
+                  bf_stream_t stream);
+
+/* Scratch bytes of bf_bifrost_layer_decode. */
+size_t bf_layer_decode_workspace(int B, int H, int G, int D, int window);
+
+/* One decode step (one new token per sequence) of the converted layer core, replacing
+ * HybridAttention._student with t == 1 (heimdall/hibrit.py:363-424): memory inputs, the state update
+ * with the token leaving the window, sliding-window + sink attention, LSE gate and mix, and the
+ * write of the new token into the ring.  Each sequence b has its own position pos[b] (int64, device);
+ * the reference's batched decode is the case of equal positions.  The sinks buffer must already hold
+ * the new token when pos < sinks (the reference appends it before attending).
+ * x [B,d], q/qr [B,H,D], k/kr/v [B,G,D] bf16.  memory = 0 is the reference's "window" mode.
+ * o [B,H,D] fp32, lse [B,H] fp32 or NULL. */
+int bf_bifrost_layer_decode(const bf_layer* L, const void* x, const void* q, const void* k, const void* v,
+                            const void* qr, const void* kr, const int64_t* pos, int B, bf_ring_cache* cache,
+                            int memory, float* o, float* lse, void* ws, size_t ws_bytes, bf_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BIFROST_B200_H */
