@@ -6,11 +6,15 @@ runs in hand-written CUDA kernels behind the C ABI in ``include/bifrost_b200.h``
 There is no CPU fallback: every op raises on CPU tensors or when the library is missing.
 
 Public API (mirrors of the reference ``heimdall`` package):
+  delta_rule                         heimdall/kernels.py:94-129, 152-155
+  delta_rule_gqa                     heimdall/motor.py:70-102
   delta_rule_step                    heimdall/kernels.py:132-138
+  window_attention                   heimdall/hibrit.py:336-361 (the math of _window_fp32)
   BifrostLayer.student               heimdall/hibrit.py:363-424 (HybridAttention._student)
   BifrostLayer.mem_inputs            heimdall/hibrit.py:327-334
 """
-from .functional import delta_rule_step, delta_rule_step_gqa  # noqa: F401
+from .functional import delta_rule, delta_rule_gqa, delta_rule_step, delta_rule_step_gqa, window_attention  # noqa: F401
 from .layer import BifrostLayer  # noqa: F401
 
-__all__ = ["delta_rule_step", "delta_rule_step_gqa", "BifrostLayer"]
+__all__ = ["delta_rule", "delta_rule_gqa", "delta_rule_step", "delta_rule_step_gqa", "window_attention",
+           "BifrostLayer"]

@@ -15,6 +15,7 @@ LIB_PATH = Path(__file__).resolve().parent / "lib" / "libbifrost_b200.so"
 _P = ctypes.c_void_p
 _I = ctypes.c_int
 _Z = ctypes.c_size_t
+_L = ctypes.c_longlong
 
 # name -> (argtypes); every entry point returns int (status) unless listed in _RESTYPE
 SIGNATURES = {
@@ -27,8 +28,16 @@ SIGNATURES = {
     "bf_mem_inputs": [_P, _P, _P, _P, _P, ctypes.c_longlong, _I, _I, _P, _P, _P, _P, _P, _P],
     "bf_layer_decode_workspace": [_I, _I, _I, _I, _I],
     "bf_bifrost_layer_decode": [_P, _P, _P, _P, _P, _P, _P, _P, _I, _P, _I, _P, _P, _P, _Z, _P],
+    "bf_gdn_chunk_workspace": [_I, _I, _I, _I, _I],
+    "bf_gdn_chunk_fwd": [_P, _I, _P, _I, _P, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _Z, _P],
+    "bf_window_workspace": [_I, _I, _I, _I],
+    "bf_window_attn_fwd": [_P, _P, _P, _L, _L, _L, _P, _P, _I, _L, _L, _L, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P,
+                           _Z, _P],
+    "bf_layer_prefill_workspace": [_I, _I, _I, _I, _I, _I, _I],
+    "bf_bifrost_layer_prefill": [_P, _P, _P, _P, _P, _P, _P, _L, _I, _I, _P, _P, _P, _I, _I, _P, _P, _P, _Z, _P],
 }
-_RESTYPE = {"bf_strerror": ctypes.c_char_p, "bf_layer_weights_bytes": _Z, "bf_layer_decode_workspace": _Z}
+_RESTYPE = {"bf_strerror": ctypes.c_char_p, "bf_layer_weights_bytes": _Z, "bf_layer_decode_workspace": _Z,
+            "bf_gdn_chunk_workspace": _Z, "bf_window_workspace": _Z, "bf_layer_prefill_workspace": _Z}
 
 _lock = threading.Lock()
 _lib = None

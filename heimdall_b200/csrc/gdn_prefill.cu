@@ -1,0 +1,725 @@
+// Chunked gated delta rule (prefill), GQA-native: one 256x256 fp32 state per KV head, read by R query heads.
+//
+// Math (heimdall/kernels.py:94-129, delta_rule_reference; GQA form heimdall/motor.py:70-102), per chunk of
+// C = 128 steps with c_i = cumulative log-decay inside the chunk:
+//   A = strict_lower(beta_i k_i.k_j e^{c_i - c_j}),  T = (I + A)^-1,  u = T (beta v),  w = T (beta e^{c} k)
+//   v' = u - w S,   o_i = e^{c_i} q_i S + sum_{j<=i} (q_i.k_j) e^{c_i - c_j} v'_j,   S <- e^{c_C} S + (e^{c_C - c} k)^T v'
+// The chunk length is an implementation choice (the result is the same recurrence); 128 makes every
+// tensor-core tile M = 128.  MMA operands are fp16 (11 significant bits; bf16 is too coarse for the state
+// budget), accumulation and the state are fp32.
+//
+// P1 (parallel, CTA = chunk x (b, KV head)): K K^T on tcgen05, A masked/decayed in the epilogue, T by blocked
+//     forward substitution in shared memory (16-row blocks), u and w on tcgen05; also writes fp16 keys,
+//     (e^{c_C - c} k)^T and the cumulative decays.
+// P2 (sequential over chunks, CTA = (b, KV head, 16 state columns)): the state block lives in registers (fp32),
+//     v' = u - w S and dS = k_tail^T v' run on tcgen05 with fp16 copies of S^T / v'^T staged in shared memory;
+//     the state at each chunk start and v' are written (fp16, transposed) for P3.
+// P3 (parallel, CTA = chunk x (b, query head)): Q K^T (-> decayed causal P in fp16), then per half of the value
+//     columns o = e^{c} (Q S_chunk) + P v' with the two products in separate TMEM accumulators.
+#include "capi_internal.h"
+#include "common.cuh"
+#include "gdn_prefill.h"
+#include "tmap.h"
+
+namespace bfb {
+
+// ------------------------------------------------------------------------------------------ helpers
+struct RowSrc {
+  const float* k;               // fp32 key row (256)
+  const __nv_bfloat16* v;       // bf16 value row (256), or
+  const float* v32;             // fp32 value row
+  float g, beta;
+  bool zero;
+};
+
+__device__ __forceinline__ RowSrc write_row(const GdnStreams& s, int b, int gg, int u) {
+  RowSrc r{nullptr, nullptr, nullptr, 0.f, 0.f, true};
+  if (u >= s.n_steps) return r;
+  if (u < s.nring) {
+    const long long kp = s.ring_pos0 + u;
+    if (kp < 0) return r;
+    const int slot = (int)(kp % s.W);
+    if (s.ring_pos[slot] != kp) return r;
+    r.k = s.ring_km + (((size_t)b * s.W + slot) * s.G + gg) * kGD;
+    r.v = s.ring_v + (((size_t)b * s.G + gg) * s.W + slot) * kGD;
+    r.g = s.ring_g[((size_t)b * s.W + slot) * s.G + gg];
+    r.beta = s.ring_beta[((size_t)b * s.W + slot) * s.G + gg];
+  } else {
+    const int tok = u - s.nring;
+    r.k = s.km + (((size_t)b * s.T + tok) * s.G + gg) * kGD;
+    if (s.v32) r.v32 = s.v32 + (((size_t)b * s.T + tok) * s.G + gg) * kGD;
+    else r.v = s.v + (((size_t)b * s.T + tok) * s.G + gg) * kGD;
+    r.g = s.g[((size_t)b * s.T + tok) * s.G + gg];
+    r.beta = s.beta[((size_t)b * s.T + tok) * s.G + gg];
+  }
+  r.zero = false;
+  return r;
+}
+
+__device__ __forceinline__ void st_half_sw128(uint8_t* tile, int rows, int row, int col, float x) {
+  // element (row, col) of a K-major SW128 tile with `rows` rows; col in 16-bit elements
+  const int atom = col >> 6, c = col & 63;
+  uint8_t* p = tile + atom * rows * 128 + row * 128 + ((((c >> 3) ^ (row & 7)) << 4)) + (c & 7) * 2;
+  *reinterpret_cast<__half*>(p) = __float2half_rn(x);
+}
+
+__device__ __forceinline__ void tmem_ld16_wait(uint32_t taddr, float (&f)[16]) {
+  uint32_t r[16];
+  tmem_ld16(taddr, r);
+  tmem_wait_ld();
+#pragma unroll
+  for (int i = 0; i < 16; ++i) f[i] = __uint_as_float(r[i]);
+}
+
+// ============================================================================================ P1
+constexpr int kP1_Threads = 256;
+constexpr int kP1_Reg0 = 0;                 // k tile (64 KB) -> T fp32 -> (beta v)^T (64 KB)
+constexpr int kP1_Reg1 = 69632;             // A fp32 (67.6 KB) -> (beta e^c k)^T (64 KB)
+constexpr int kP1_RegW = 69632 * 2;         // T fp16 (32 KB)
+constexpr int kP1_Small = kP1_RegW + 32768; // gc/g/beta (3 x 512 B) + barriers
+constexpr int kP1_Smem = kP1_Small + 2048 + 1024;
+constexpr int kAS = 132;                    // row stride (floats) of A and T in shared memory
+
+__global__ void __launch_bounds__(kP1_Threads, 1) gdn_p1_kernel(GdnStreams s) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* reg0 = smem + kP1_Reg0;
+  uint8_t* reg1 = smem + kP1_Reg1;
+  uint8_t* regW = smem + kP1_RegW;
+  float* s_gc = reinterpret_cast<float*>(smem + kP1_Small);
+  float* s_g = s_gc + 128;
+  float* s_beta = s_g + 128;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_beta + 128);
+  uint64_t* bar_kk = bars + 0;
+  uint64_t* bar_uw = bars + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2);
+  float* A = reinterpret_cast<float*>(reg1);   // [128][kAS]
+  float* Tm = reinterpret_cast<float*>(reg0);  // [128][kAS]
+
+  const int c = blockIdx.x, bg = blockIdx.y, b = bg / s.G, gg = bg % s.G;
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const size_t rowbase = (size_t)bg * s.n_pad + (size_t)c * kGC;
+
+  if (t == 0) {
+    mbar_init(bar_kk, 1);
+    mbar_init(bar_uw, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  // ---- (a) key rows -> fp16 K tile (SW128, 4 atoms) and the fp16 write keys in global memory
+  {
+    const int r = t >> 1, hh = t & 1;
+    const RowSrc src = write_row(s, b, gg, c * kGC + r);
+    if (hh == 0) {
+      s_g[r] = src.zero ? 0.f : src.g;
+      s_beta[r] = src.zero ? 0.f : src.beta;
+    }
+    __half* kwrow = s.kw + (rowbase + r) * kGD + hh * 128;
+#pragma unroll 4
+    for (int ch = 0; ch < 16; ++ch) {  // 16 chunks of 8 elements = 128 columns
+      float x[8];
+      if (src.zero) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[e] = 0.f;
+      } else {
+        const float4 a0 = *reinterpret_cast<const float4*>(src.k + hh * 128 + ch * 8);
+        const float4 a1 = *reinterpret_cast<const float4*>(src.k + hh * 128 + ch * 8 + 4);
+        x[0] = a0.x; x[1] = a0.y; x[2] = a0.z; x[3] = a0.w; x[4] = a1.x; x[5] = a1.y; x[6] = a1.z; x[7] = a1.w;
+      }
+      const uint4 pk = make_uint4(pack_half2(x[0], x[1]), pack_half2(x[2], x[3]), pack_half2(x[4], x[5]),
+                                  pack_half2(x[6], x[7]));
+      const int col = hh * 128 + ch * 8;
+      *reinterpret_cast<uint4*>(reg0 + (col >> 6) * (128 * 128) + sw128_offset(r, col & 63)) = pk;
+      *reinterpret_cast<uint4*>(kwrow + ch * 8) = pk;
+    }
+  }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (t == 0) {
+    const uint32_t aK = smem_u32(reg0);
+    constexpr uint32_t idesc = idesc_f16(128, 128, 0);
+#pragma unroll
+    for (int ks = 0; ks < kGD / 16; ++ks)
+      umma_f16_ss(tmem, sdesc_kstep(aK, 128, ks), sdesc_kstep(aK, 128, ks), idesc, ks > 0);
+    umma_commit(bar_kk);
+  }
+  // cumulative decay inside the chunk (thread r < 128)
+  if (t < 128) {
+    float acc = 0.f;
+    for (int j = 0; j <= t; ++j) acc += s_g[j];
+    s_gc[t] = acc;
+    s.gc[rowbase + t] = acc;
+  }
+  __syncthreads();
+  const float gamma_last = s_gc[127];
+  // ---- (b) A = strict_lower(beta_i e^{c_i - c_j} (k_i . k_j)) from TMEM (warps 0-3, row = lane)
+  bool alive = true;
+  if (warp < 4) {
+    const int r = t;
+    alive = mbar_wait(bar_kk, 0, nullptr, s.err, 0x41);
+    tc_fence_after();
+    const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+    const float br = s_beta[r], cr = s_gc[r];
+#pragma unroll 1
+    for (int c0 = 0; c0 < 128; c0 += 16) {
+      float f[16];
+      tmem_ld16_wait(trow + c0, f);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const int j = c0 + e;
+        A[r * kAS + j] = (j < r && alive) ? br * __expf(cr - s_gc[j]) * f[e] : 0.f;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();  // A complete; the K tile (reg0) is free (K K^T finished)
+  // ---- (c) T = (I + A)^-1 by blocked forward substitution (16-row blocks)
+  for (int i = t; i < 128 * kAS; i += kP1_Threads) Tm[i] = 0.f;
+  __syncthreads();
+  for (int I = 0; I < 8; ++I) {
+    const int r0 = I * 16;
+    // contribution of earlier blocks: T[i][col] = -sum_{j < r0} A[i][j] T[j][col], i in block, col < r0
+    for (int p = t; p < 16 * r0; p += kP1_Threads) {
+      const int i = r0 + p / r0, col = p % r0;
+      float acc = 0.f;
+      for (int j = col; j < r0; ++j) acc += A[i * kAS + j] * Tm[j * kAS + col];
+      Tm[i * kAS + col] = -acc;
+    }
+    __syncthreads();
+    // inside the block: each column is a sequential chain owned by one thread
+    if (t < r0 + 16) {
+      const int col = t;
+      for (int ii = 0; ii < 16; ++ii) {
+        const int i = r0 + ii;
+        if (col > i) break;
+        if (col == i) {
+          Tm[i * kAS + col] = 1.f;
+          continue;
+        }
+        float acc = Tm[i * kAS + col];
+        for (int j = max(r0, col); j < i; ++j) acc -= A[i * kAS + j] * Tm[j * kAS + col];
+        Tm[i * kAS + col] = acc;
+      }
+    }
+    __syncthreads();
+  }
+  // ---- T -> fp16 SW128 tile (rows i, K = j) in regW
+  for (int p = t; p < 128 * 16; p += kP1_Threads) {
+    const int i = p >> 4, ch = p & 15;  // chunk of 8 columns
+    const float* tr = Tm + i * kAS + ch * 8;
+    const uint4 pk = make_uint4(pack_half2(tr[0], tr[1]), pack_half2(tr[2], tr[3]), pack_half2(tr[4], tr[5]),
+                                pack_half2(tr[6], tr[7]));
+    *reinterpret_cast<uint4*>(regW + (ch >> 3) * (128 * 128) + sw128_offset(i, (ch & 7) * 8)) = pk;
+  }
+  __syncthreads();  // Tm (reg0) and A (reg1) are free now
+  // ---- (d) B operands: (beta v)^T -> reg0, (beta e^c k)^T -> reg1 ([256 dims][128 tokens] K-major);
+  //      and k_tail^T = (e^{c_C - c} k)^T to global (P2's A operand)
+  {
+    const int r = t >> 1, hh = t & 1;
+    const RowSrc src = write_row(s, b, gg, c * kGC + r);
+    const float br = s_beta[r], ec = __expf(s_gc[r]), et = __expf(gamma_last - s_gc[r]);
+    __half* ktT = s.ktT + ((size_t)bg * s.n_chunks + c) * kGD * kGC;
+    for (int d0 = hh * 128; d0 < hh * 128 + 128; d0 += 8) {
+      float kx[8], vx[8];
+      if (src.zero) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) kx[e] = vx[e] = 0.f;
+      } else {
+        const float4 a0 = *reinterpret_cast<const float4*>(src.k + d0);
+        const float4 a1 = *reinterpret_cast<const float4*>(src.k + d0 + 4);
+        kx[0] = a0.x; kx[1] = a0.y; kx[2] = a0.z; kx[3] = a0.w; kx[4] = a1.x; kx[5] = a1.y; kx[6] = a1.z; kx[7] = a1.w;
+        if (src.v32) {
+          const float4 b0 = *reinterpret_cast<const float4*>(src.v32 + d0);
+          const float4 b1 = *reinterpret_cast<const float4*>(src.v32 + d0 + 4);
+          vx[0] = b0.x; vx[1] = b0.y; vx[2] = b0.z; vx[3] = b0.w; vx[4] = b1.x; vx[5] = b1.y; vx[6] = b1.z; vx[7] = b1.w;
+        } else {
+          const uint4 vv = *reinterpret_cast<const uint4*>(src.v + d0);
+          const uint32_t vw[4] = {vv.x, vv.y, vv.z, vv.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            vx[2 * e] = __uint_as_float(vw[e] << 16);
+            vx[2 * e + 1] = __uint_as_float(vw[e] & 0xffff0000u);
+          }
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        st_half_sw128(reg0, 256, d0 + e, r, br * vx[e]);
+        st_half_sw128(reg1, 256, d0 + e, r, br * ec * kx[e]);
+        ktT[(size_t)(d0 + e) * kGC + r] = __float2half_rn(kx[e] * et);
+      }
+    }
+  }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (t == 0) {
+    constexpr uint32_t idesc = idesc_f16(128, 256, 0);
+    const uint32_t aT = smem_u32(regW), bV = smem_u32(reg0), bK = smem_u32(reg1);
+#pragma unroll
+    for (int ks = 0; ks < kGC / 16; ++ks)
+      umma_f16_ss(tmem, sdesc_kstep(aT, 128, ks), sdesc_kstep(bV, 256, ks), idesc, ks > 0);
+#pragma unroll
+    for (int ks = 0; ks < kGC / 16; ++ks)
+      umma_f16_ss(tmem + 256, sdesc_kstep(aT, 128, ks), sdesc_kstep(bK, 256, ks), idesc, ks > 0);
+    umma_commit(bar_uw);
+  }
+  // ---- (e) u, w rows -> fp16 global (warps 0-3)
+  if (warp < 4) {
+    const int r = t;
+    alive = mbar_wait(bar_uw, 0, nullptr, s.err, 0x42) && alive;
+    tc_fence_after();
+    const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+    __half* urow = s.u + (rowbase + r) * kGD;
+    __half* wrow = s.w + (rowbase + r) * kGD;
+#pragma unroll 1
+    for (int c0 = 0; c0 < 256; c0 += 16) {
+      float f[16];
+      tmem_ld16_wait(trow + c0, f);
+      uint4* up = reinterpret_cast<uint4*>(urow + c0);
+      up[0] = make_uint4(pack_half2(f[0], f[1]), pack_half2(f[2], f[3]), pack_half2(f[4], f[5]), pack_half2(f[6], f[7]));
+      up[1] = make_uint4(pack_half2(f[8], f[9]), pack_half2(f[10], f[11]), pack_half2(f[12], f[13]),
+                         pack_half2(f[14], f[15]));
+      tmem_ld16_wait(trow + 256 + c0, f);
+      uint4* wp = reinterpret_cast<uint4*>(wrow + c0);
+      wp[0] = make_uint4(pack_half2(f[0], f[1]), pack_half2(f[2], f[3]), pack_half2(f[4], f[5]), pack_half2(f[6], f[7]));
+      wp[1] = make_uint4(pack_half2(f[8], f[9]), pack_half2(f[10], f[11]), pack_half2(f[12], f[13]),
+                         pack_half2(f[14], f[15]));
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ============================================================================================ P2
+constexpr int kP2_NB = 16;               // state columns per CTA
+constexpr int kP2_Threads = 192;         // warps 0-3 state/epilogue, warp 4 TMA, warp 5 MMA
+constexpr int kP2_SmemW = kGC * kGD * 2;          // 64 KB
+constexpr int kP2_SmemKT = kGD * kGC * 2;         // 64 KB
+constexpr int kP2_SmemST = kP2_NB * kGD * 2;      // 8 KB
+constexpr int kP2_SmemVT = kP2_NB * kGC * 2;      // 4 KB
+constexpr int kP2_Smem = kP2_SmemW + kP2_SmemKT + kP2_SmemST + kP2_SmemVT + 1024 + 256;
+
+__global__ void __launch_bounds__(kP2_Threads, 1)
+    gdn_p2_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap ktmap, GdnStreams s) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sW = smem;
+  uint8_t* sKT = sW + kP2_SmemW;
+  uint8_t* sST = sKT + kP2_SmemKT;
+  uint8_t* sVT = sST + kP2_SmemST;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sVT + kP2_SmemVT);
+  uint64_t* bar_w = bars + 0;      // w tile landed
+  uint64_t* bar_kt = bars + 1;     // k_tail^T tile landed
+  uint64_t* bar_st = bars + 2;     // S^T staged (128)
+  uint64_t* bar_vt = bars + 3;     // v'^T staged (128)
+  uint64_t* bar_m1 = bars + 4;     // v' product done
+  uint64_t* bar_m2 = bars + 5;     // state product done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 6);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 7);
+
+  const int blk = blockIdx.x, bg = blockIdx.y;
+  const int col0 = blk * kP2_NB;
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int nch = s.n_chunks;
+  if (t == 0) {
+    mbar_init(bar_w, 1);
+    mbar_init(bar_kt, 1);
+    mbar_init(bar_st, 128);
+    mbar_init(bar_vt, 128);
+    mbar_init(bar_m1, 1);
+    mbar_init(bar_m2, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 64);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      tma_prefetch(&wmap);
+      tma_prefetch(&ktmap);
+      int iw = 0, ik = 0;
+      for (int c = 0; c < nch; ++c) {
+        if (c >= 1 && !mbar_wait(bar_m1, (c - 1) & 1, abort_flag, s.err, 0x51)) break;
+        mbar_expect_tx(bar_w, kP2_SmemW);
+        tma_load_3d(sW, &wmap, bar_w, 0, bg * s.n_pad + c * kGC, 0);
+        iw = c + 1;
+        if (c >= 1 && !mbar_wait(bar_m2, (c - 1) & 1, abort_flag, s.err, 0x52)) break;
+        mbar_expect_tx(bar_kt, kP2_SmemKT);
+        tma_load_3d(sKT, &ktmap, bar_kt, 0, (bg * nch + c) * kGD, 0);
+        ik = c + 1;
+      }
+      if (iw > 0) mbar_wait(bar_w, (iw - 1) & 1, nullptr, s.err, 0x53);
+      if (ik > 0) mbar_wait(bar_kt, (ik - 1) & 1, nullptr, s.err, 0x54);
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      constexpr uint32_t id1 = idesc_f16(128, kP2_NB, 0);
+      const uint32_t aW = smem_u32(sW), bST = smem_u32(sST), aKT = smem_u32(sKT), bVT = smem_u32(sVT);
+      for (int c = 0; c < nch; ++c) {
+        if (!mbar_wait(bar_w, c & 1, abort_flag, s.err, 0x55)) break;
+        if (!mbar_wait(bar_st, c & 1, abort_flag, s.err, 0x56)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < kGD / 16; ++ks)
+          umma_f16_ss(tmem, sdesc_kstep(aW, 128, ks), sdesc_kstep(bST, kP2_NB, ks), id1, ks > 0);
+        umma_commit(bar_m1);
+        if (!mbar_wait(bar_kt, c & 1, abort_flag, s.err, 0x57)) break;
+        if (!mbar_wait(bar_vt, c & 1, abort_flag, s.err, 0x58)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+#pragma unroll
+          for (int ks = 0; ks < kGC / 16; ++ks) {
+            const uint32_t a = aKT + (ks >> 2) * (kGD * 128) + mt * (128 * 128) + (ks & 3) * 32;
+            umma_f16_ss(tmem + kP2_NB * (1 + mt), sdesc_sw128(a), sdesc_kstep(bVT, kP2_NB, ks), id1, ks > 0);
+          }
+        }
+        umma_commit(bar_m2);
+      }
+    }
+  } else {
+    // warps 0-3: thread r owns state rows r and r + 128 (columns col0 .. col0+15) and token row r
+    const int r = t;
+    const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+    float S0[kP2_NB], S1[kP2_NB];
+    if (s.s0) {
+      const float* sp = s.s0 + (size_t)bg * kGD * kGD;
+#pragma unroll
+      for (int e = 0; e < kP2_NB; e += 4) {
+        const float4 x0 = *reinterpret_cast<const float4*>(sp + (size_t)r * kGD + col0 + e);
+        const float4 x1 = *reinterpret_cast<const float4*>(sp + (size_t)(r + 128) * kGD + col0 + e);
+        S0[e] = x0.x; S0[e + 1] = x0.y; S0[e + 2] = x0.z; S0[e + 3] = x0.w;
+        S1[e] = x1.x; S1[e + 1] = x1.y; S1[e + 2] = x1.z; S1[e + 3] = x1.w;
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < kP2_NB; ++e) S0[e] = S1[e] = 0.f;
+    }
+    bool alive = true;
+    for (int c = 0; c < nch && alive; ++c) {
+      // stage S^T (fp16) as the B operand of v' = u - w S, and store it for P3
+      __half* stg = s.ST + (((size_t)bg * nch + c) * kGD + col0) * kGD;
+#pragma unroll
+      for (int e = 0; e < kP2_NB; ++e) {
+        st_half_sw128(sST, kP2_NB, e, r, S0[e]);
+        st_half_sw128(sST, kP2_NB, e, r + 128, S1[e]);
+        stg[(size_t)e * kGD + r] = __float2half_rn(S0[e]);
+        stg[(size_t)e * kGD + r + 128] = __float2half_rn(S1[e]);
+      }
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(bar_st);
+      // u row r (this chunk), columns col0..+15
+      const __half* up = s.u + ((size_t)bg * s.n_pad + (size_t)c * kGC + r) * kGD + col0;
+      float uu[kP2_NB];
+      {
+        const uint4 a0 = *reinterpret_cast<const uint4*>(up);
+        const uint4 a1 = *reinterpret_cast<const uint4*>(up + 8);
+        const uint32_t w[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const __half2 h2 = *reinterpret_cast<const __half2*>(&w[e]);
+          const float2 f2 = __half22float2(h2);
+          uu[2 * e] = f2.x;
+          uu[2 * e + 1] = f2.y;
+        }
+      }
+      if (!mbar_wait(bar_m1, c & 1, abort_flag, s.err, 0x59)) { alive = false; break; }
+      tc_fence_after();
+      float dv[kP2_NB];
+      tmem_ld16_wait(trow, dv);
+      __half* vtg = s.VT + (((size_t)bg * nch + c) * kGD + col0) * kGC;
+#pragma unroll
+      for (int e = 0; e < kP2_NB; ++e) {
+        const float vn = uu[e] - dv[e];
+        st_half_sw128(sVT, kP2_NB, e, r, vn);
+        vtg[(size_t)e * kGC + r] = __float2half_rn(vn);
+      }
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(bar_vt);
+      const float decay = __expf(s.gc[(size_t)bg * s.n_pad + (size_t)c * kGC + kGC - 1]);
+      if (!mbar_wait(bar_m2, c & 1, abort_flag, s.err, 0x5a)) { alive = false; break; }
+      tc_fence_after();
+      float d0[kP2_NB], d1[kP2_NB];
+      tmem_ld16_wait(trow + kP2_NB, d0);
+      tmem_ld16_wait(trow + 2 * kP2_NB, d1);
+#pragma unroll
+      for (int e = 0; e < kP2_NB; ++e) {
+        S0[e] = decay * S0[e] + d0[e];
+        S1[e] = decay * S1[e] + d1[e];
+      }
+      tc_fence_before();
+    }
+    if (alive) {
+      float* so = s.s_out + (size_t)bg * kGD * kGD;
+#pragma unroll
+      for (int e = 0; e < kP2_NB; e += 4) {
+        *reinterpret_cast<float4*>(so + (size_t)r * kGD + col0 + e) = make_float4(S0[e], S0[e + 1], S0[e + 2], S0[e + 3]);
+        *reinterpret_cast<float4*>(so + (size_t)(r + 128) * kGD + col0 + e) =
+            make_float4(S1[e], S1[e + 1], S1[e + 2], S1[e + 3]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 64);
+  }
+}
+
+// ============================================================================================ P3
+constexpr int kP3_Threads = 192;   // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr int kP3_SmemQ = kGC * kGD * 2;      // 64 KB
+constexpr int kP3_SmemKS = kGD * kGD;         // 64 KB: k tile, then S^T half (128 x 256 fp16)
+constexpr int kP3_SmemVN = 128 * kGC * 2;     // 32 KB: v'^T half
+constexpr int kP3_SmemP = kGC * kGC * 2;      // 32 KB
+constexpr int kP3_Smem = kP3_SmemQ + kP3_SmemKS + kP3_SmemVN + kP3_SmemP + 1024 + 256;
+
+__global__ void __launch_bounds__(kP3_Threads, 1)
+    gdn_p3_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
+                  const __grid_constant__ CUtensorMap smap, const __grid_constant__ CUtensorMap vmap, GdnStreams s) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sKS = sQ + kP3_SmemQ;
+  uint8_t* sVN = sKS + kP3_SmemKS;
+  uint8_t* sP = sVN + kP3_SmemVN;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kP3_SmemP);
+  uint64_t* bar_qk = bars + 0;     // q and k landed
+  uint64_t* bar_qkd = bars + 1;    // Q K^T done (k buffer free)
+  uint64_t* bar_s = bars + 2;      // S^T half landed
+  uint64_t* bar_vn = bars + 3;     // v'^T half landed
+  uint64_t* bar_p = bars + 4;      // P staged (128)
+  uint64_t* bar_o = bars + 5;      // half products done
+  uint64_t* bar_of = bars + 6;     // accumulators drained (128)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 7);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 8);
+
+  const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int R = s.R, G = s.G, H = G * R, gg = h / R;
+  const int bg = b * G + gg;
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int nch = s.n_chunks;
+  if (t == 0) {
+    for (int i = 0; i < 7; ++i) mbar_init(bars + i, (i == 4 || i == 6) ? 128 : 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // TMEM: QK^T cols 0..127, inter 128..255, intra 256..383
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch(&qmap);
+      tma_prefetch(&kmap);
+      tma_prefetch(&smap);
+      tma_prefetch(&vmap);
+      // read rows c*128.. of query stream -> query token qoff + c*128 + i (4-D map: d, token, atom, head)
+      mbar_expect_tx(bar_qk, kP3_SmemQ + kGC * kGD * 2);
+      tma_load_4d(sQ, &qmap, bar_qk, 0, b * s.T + s.qoff + c * kGC, 0, h);
+      tma_load_3d(sKS, &kmap, bar_qk, 0, bg * s.n_pad + c * kGC, 0);
+      int ns_ = 0, nv_ = 0;
+      bool ok = mbar_wait(bar_qkd, 0, abort_flag, s.err, 0x61);
+      for (int half = 0; half < 2 && ok; ++half) {
+        if (half == 1) ok = mbar_wait(bar_o, 0, abort_flag, s.err, 0x62);
+        if (!ok) break;
+        mbar_expect_tx(bar_s, 128 * kGD * 2);
+        tma_load_3d(sKS, &smap, bar_s, 0, ((bg * nch + c) * kGD) + half * 128, 0);
+        ns_ = half + 1;
+        mbar_expect_tx(bar_vn, kP3_SmemVN);
+        tma_load_3d(sVN, &vmap, bar_vn, 0, ((bg * nch + c) * kGD) + half * 128, 0);
+        nv_ = half + 1;
+      }
+      mbar_wait(bar_qk, 0, nullptr, s.err, 0x63);
+      if (ns_ > 0) mbar_wait(bar_s, (ns_ - 1) & 1, nullptr, s.err, 0x64);
+      if (nv_ > 0) mbar_wait(bar_vn, (nv_ - 1) & 1, nullptr, s.err, 0x65);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t id128 = idesc_f16(128, 128, 0);
+      const uint32_t aQ = smem_u32(sQ), bKS = smem_u32(sKS), aP = smem_u32(sP), bVN = smem_u32(sVN);
+      bool ok = mbar_wait(bar_qk, 0, abort_flag, s.err, 0x66);
+      if (ok) {
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < kGD / 16; ++ks)
+          umma_f16_ss(tmem, sdesc_kstep(aQ, 128, ks), sdesc_kstep(bKS, 128, ks), id128, ks > 0);
+        umma_commit(bar_qkd);
+      }
+      for (int half = 0; half < 2 && ok; ++half) {
+        ok = mbar_wait(bar_s, half & 1, abort_flag, s.err, 0x67);
+        if (ok && half == 1) ok = mbar_wait(bar_of, 0, abort_flag, s.err, 0x68);
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < kGD / 16; ++ks)
+          umma_f16_ss(tmem + 128, sdesc_kstep(aQ, 128, ks), sdesc_kstep(bKS, 128, ks), id128, ks > 0);
+        ok = mbar_wait(bar_p, 0, abort_flag, s.err, 0x69) && mbar_wait(bar_vn, half & 1, abort_flag, s.err, 0x6a);
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < kGC / 16; ++ks)
+          umma_f16_ss(tmem + 256, sdesc_kstep(aP, 128, ks), sdesc_kstep(bVN, 128, ks), id128, ks > 0);
+        umma_commit(bar_o);
+      }
+    }
+  } else {
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;  // row i of the chunk (query step c*128 + r)
+    const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
+    const float* gcc = s.gc + (size_t)bg * s.n_pad + (size_t)c * kGC;
+    const float ci = gcc[r];
+    bool alive = mbar_wait(bar_qkd, 0, abort_flag, s.err, 0x6b);
+    if (alive) {
+      tc_fence_after();
+#pragma unroll 1
+      for (int c0 = 0; c0 < kGC; c0 += 16) {
+        float f[16];
+        tmem_ld16_wait(trow + c0, f);
+        uint32_t pk[8];
+#pragma unroll
+        for (int e = 0; e < 16; e += 2) {
+          const int j = c0 + e;
+          const float p0 = (j <= r) ? f[e] * __expf(ci - gcc[j]) : 0.f;
+          const float p1 = (j + 1 <= r) ? f[e + 1] * __expf(ci - gcc[j + 1]) : 0.f;
+          pk[e / 2] = pack_half2(p0, p1);
+        }
+        const int atom = c0 >> 6, col = c0 & 63;
+        *reinterpret_cast<uint4*>(sP + atom * (128 * 128) + sw128_offset(r, col)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        *reinterpret_cast<uint4*>(sP + atom * (128 * 128) + sw128_offset(r, col + 8)) =
+            make_uint4(pk[4], pk[5], pk[6], pk[7]);
+      }
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(bar_p);
+    }
+    const int step = c * kGC + r;
+    const bool row_ok = step < s.n_steps;
+    const float eci = __expf(ci);
+    float* orow = s.o + (((size_t)b * s.T + s.qoff + step) * H + h) * kGD;
+    for (int half = 0; half < 2 && alive; ++half) {
+      alive = mbar_wait(bar_o, half & 1, abort_flag, s.err, 0x6c);
+      if (!alive) break;
+      tc_fence_after();
+#pragma unroll 1
+      for (int c0 = 0; c0 < 128; c0 += 16) {
+        float fi[16], fa[16];
+        tmem_ld16_wait(trow + 128 + c0, fi);
+        tmem_ld16_wait(trow + 256 + c0, fa);
+        if (row_ok) {
+#pragma unroll
+          for (int e = 0; e < 16; e += 4)
+            *reinterpret_cast<float4*>(orow + half * 128 + c0 + e) =
+                make_float4(eci * fi[e] + fa[e], eci * fi[e + 1] + fa[e + 1], eci * fi[e + 2] + fa[e + 2],
+                            eci * fi[e + 3] + fa[e + 3]);
+        }
+      }
+      tc_fence_before();
+      if (half == 0) mbar_arrive(bar_of);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ============================================================================================ launch
+size_t gdn_prefill_workspace(int B, int G, int T_steps) {
+  const size_t n_pad = (size_t)((T_steps + kGC - 1) / kGC) * kGC;
+  const size_t nch = n_pad / kGC;
+  auto al = [](size_t x) { return (x + 1023) & ~size_t(1023); };
+  size_t n = 0;
+  n += al((size_t)B * G * n_pad * kGD * 2) * 3;       // kw, w, u
+  n += al((size_t)B * G * nch * kGD * kGC * 2);       // ktT
+  n += al((size_t)B * G * n_pad * 4);                 // gc
+  n += al((size_t)B * G * nch * kGD * kGD * 2);       // ST
+  n += al((size_t)B * G * nch * kGD * kGC * 2);       // VT
+  return n;
+}
+
+int gdn_prefill_carve(GdnStreams& s, void* ws) {
+  auto al = [](size_t x) { return (x + 1023) & ~size_t(1023); };
+  uint8_t* p = static_cast<uint8_t*>(ws);
+  const size_t n_pad = (size_t)s.n_pad, nch = (size_t)s.n_chunks;
+  s.kw = reinterpret_cast<__half*>(p); p += al((size_t)s.B * s.G * n_pad * kGD * 2);
+  s.w = reinterpret_cast<__half*>(p); p += al((size_t)s.B * s.G * n_pad * kGD * 2);
+  s.u = reinterpret_cast<__half*>(p); p += al((size_t)s.B * s.G * n_pad * kGD * 2);
+  s.ktT = reinterpret_cast<__half*>(p); p += al((size_t)s.B * s.G * nch * kGD * kGC * 2);
+  s.gc = reinterpret_cast<float*>(p); p += al((size_t)s.B * s.G * n_pad * 4);
+  s.ST = reinterpret_cast<__half*>(p); p += al((size_t)s.B * s.G * nch * kGD * kGD * 2);
+  s.VT = reinterpret_cast<__half*>(p); p += al((size_t)s.B * s.G * nch * kGD * kGC * 2);
+  return BF_OK;
+}
+
+static bool g_p_attr[3] = {false, false, false};
+
+int launch_gdn_prefill(GdnStreams s, cudaStream_t stream) {
+  if (s.n_steps <= 0) return BF_OK;
+  const int H = s.G * s.R;
+  if (!g_p_attr[0]) {
+    if (cudaFuncSetAttribute(gdn_p1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kP1_Smem) != cudaSuccess ||
+        cudaFuncSetAttribute(gdn_p2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kP2_Smem) != cudaSuccess ||
+        cudaFuncSetAttribute(gdn_p3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kP3_Smem) != cudaSuccess)
+      return BF_ERR_CUDA;
+    g_p_attr[0] = true;
+  }
+  gdn_p1_kernel<<<dim3(s.n_chunks, s.B * s.G), kP1_Threads, kP1_Smem, stream>>>(s);
+  if (cudaGetLastError() != cudaSuccess) return BF_ERR_CUDA;
+  CUtensorMap wmap, ktmap;
+  int rc = make_tmap_kmajor(&wmap, s.w, BF_F16, (uint64_t)s.B * s.G * s.n_pad, kGD, kGD, kGC, 4);
+  if (rc) return rc;
+  rc = make_tmap_kmajor(&ktmap, s.ktT, BF_F16, (uint64_t)s.B * s.G * s.n_chunks * kGD, kGC, kGC, kGD, 2);
+  if (rc) return rc;
+  gdn_p2_kernel<<<dim3(kGD / kP2_NB, s.B * s.G), kP2_Threads, kP2_Smem, stream>>>(wmap, ktmap, s);
+  if (cudaGetLastError() != cudaSuccess) return BF_ERR_CUDA;
+  // P3 maps: q [B,T,H,D] fp16 as (d, token, atom, head); k/kw; S^T; v'^T
+  CUtensorMap qmap, kmap, smap, vmap;
+  {
+    const uint64_t dims[4] = {64, (uint64_t)s.B * s.T, 4, (uint64_t)H};
+    const uint64_t strides[3] = {(uint64_t)H * kGD * 2, 128, (uint64_t)kGD * 2};
+    const uint32_t box[4] = {64, (uint32_t)kGC, 4, 1};
+    rc = make_tmap(&qmap, s.qm, BF_F16, 4, dims, strides, box, true);
+    if (rc) return rc;
+  }
+  rc = make_tmap_kmajor(&kmap, s.kw, BF_F16, (uint64_t)s.B * s.G * s.n_pad, kGD, kGD, kGC, 4);
+  if (rc) return rc;
+  rc = make_tmap_kmajor(&smap, s.ST, BF_F16, (uint64_t)s.B * s.G * s.n_chunks * kGD, kGD, kGD, 128, 4);
+  if (rc) return rc;
+  rc = make_tmap_kmajor(&vmap, s.VT, BF_F16, (uint64_t)s.B * s.G * s.n_chunks * kGD, kGC, kGC, 128, 2);
+  if (rc) return rc;
+  gdn_p3_kernel<<<dim3(s.n_chunks, H, s.B), kP3_Threads, kP3_Smem, stream>>>(qmap, kmap, smap, vmap, s);
+  return cudaGetLastError() == cudaSuccess ? BF_OK : BF_ERR_CUDA;
+}
+
+}  // namespace bfb

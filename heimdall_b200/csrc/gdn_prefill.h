@@ -1,0 +1,46 @@
+// Argument blocks of the chunked gated delta-rule prefill kernels (gdn_prefill.cu).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace bfb {
+
+constexpr int kGC = 128;   // chunk length of the GPU scan (tokens)
+constexpr int kGD = 256;   // head dim (Dk == Dv)
+
+// The write stream (step u writes one key/value into memory) and the read stream (step u reads with
+// R query heads).  Write step u comes from the ring when u < nring (ring position ring_pos0 + u,
+// a no-op when that slot is not valid) and otherwise from new token u - nring; read step u is query
+// u + qoff.  Steps >= n_steps are padding (no-ops).
+struct GdnStreams {
+  int B, G, R, T;              // T = new tokens per sequence
+  int n_steps, n_pad, n_chunks;
+  int nring, W, qoff;
+  long long ring_pos0;
+  const float* km;             // [B,T,G,D] fp32
+  const __nv_bfloat16* v;      // [B,T,G,D] bf16 values (or null when v32 is set)
+  const float* v32;            // [B,T,G,D] fp32 values (optional)
+  const float* g;              // [B,T,G]
+  const float* beta;           // [B,T,G]
+  const float* ring_km;        // [B,W,G,D]
+  const __nv_bfloat16* ring_v; // [B,G,W,D]
+  const float* ring_g;         // [B,W,G]
+  const float* ring_beta;      // [B,W,G]
+  const int64_t* ring_pos;     // [W]
+  // per-chunk products (workspace)
+  __half* kw;                  // [B,G,n_pad,D]   write keys (fp16)
+  __half* w;                   // [B,G,n_pad,D]   T (beta e^gc k)
+  __half* u;                   // [B,G,n_pad,D]   T (beta v)
+  __half* ktT;                 // [B,G,n_chunks,D,kGC]  (e^{gc_last - gc} k)^T
+  float* gc;                   // [B,G,n_pad]     cumulative log-decay inside the chunk
+  __half* ST;                  // [B,G,n_chunks,D(dv),D(dk)]  state at chunk start, transposed
+  __half* VT;                  // [B,G,n_chunks,D(dv),kGC]    v_new, transposed
+  const float* s0;             // [B,G,D,D] or null
+  float* s_out;                // [B,G,D,D]
+  const __half* qm;            // [B,T,H,D] fp16 (read queries, unit-norm * D^-1/2)
+  float* o;                    // [B,T,H,D] memory read of query u + qoff
+  unsigned int* err;
+};
+
+}  // namespace bfb

@@ -7,8 +7,8 @@ namespace bfb {
 
 int launch_prep_weights(const float* fq, const float* fk, const float* ab_w, const float* mix_w, int H, int G,
                         int D, int d, __half* w_heads, __nv_bfloat16* w_x, cudaStream_t stream);
-int launch_head_proj(const __nv_bfloat16* q, const __nv_bfloat16* k, const __half* w_heads, float* qm, float* km,
-                     int B, int T, int H, int G, int sm_count, unsigned int* err, cudaStream_t stream);
+int launch_head_proj(const __nv_bfloat16* q, const __nv_bfloat16* k, const __half* w_heads, float* qm, __half* qm16,
+                     float* km, int B, int T, int H, int G, int sm_count, unsigned int* err, cudaStream_t stream);
 int launch_x_proj(const __nv_bfloat16* x, const __nv_bfloat16* w_x, const float* ab_b, const float* mix_b,
                   const float* A_log, const float* dt_bias, const float* decay_mask, float* g, float* beta,
                   float* mixx, const int64_t* pos, long long pos0, int M, int T, int d, int G, int H, int sinks,
@@ -44,13 +44,13 @@ int check_layer(const bf_layer* L) {
 
 int mem_inputs_impl(const DeviceState& st, const bf_layer* L, const void* x, const void* q, const void* k,
                     const int64_t* pos, long long pos0, int B, int T, float* qm, float* km, float* g, float* beta,
-                    float* mixx, cudaStream_t stream) {
+                    float* mixx, cudaStream_t stream, __half* qm16) {
   int rc = launch_x_proj(static_cast<const __nv_bfloat16*>(x), weights_x(L->wbuf, L->H, L->G, L->D), L->ab_b,
                          L->mix_b, L->A_log, L->dt_bias, L->decay_mask, g, beta, mixx, pos, pos0, B * T, T, L->d,
                          L->G, L->H, L->sinks, st.err, stream);
   if (rc) return rc;
   return launch_head_proj(static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
-                          weights_heads(L->wbuf), qm, km, B, T, L->H, L->G, st.sm_count, st.err, stream);
+                          weights_heads(L->wbuf), qm, qm16, km, B, T, L->H, L->G, st.sm_count, st.err, stream);
 }
 
 }  // namespace bfb
@@ -96,7 +96,7 @@ int bf_mem_inputs(const bf_layer* L, const void* x, const void* q, const void* k
   DeviceState st;
   rc = device_state(&st);
   if (rc) return rc;
-  return mem_inputs_impl(st, L, x, q, k, pos, pos0, B, T, qm, km, g, beta, mixx, stream);
+  return mem_inputs_impl(st, L, x, q, k, pos, pos0, B, T, qm, km, g, beta, mixx, stream, nullptr);
 }
 
 size_t bf_layer_decode_workspace(int B, int H, int G, int D, int window) {
@@ -152,7 +152,7 @@ int bf_bifrost_layer_decode(const bf_layer* L, const void* x, const void* q, con
   float* part = reinterpret_cast<float*>(take(win_dec_workspace(B, G, R, D, W)));
 
   // memory inputs of the new tokens (T = 1 per sequence, per-sequence positions)
-  rc = mem_inputs_impl(st, L, x, q, k, pos, 0, B, 1, qm, km, g, beta, mixx, stream);
+  rc = mem_inputs_impl(st, L, x, q, k, pos, 0, B, 1, qm, km, g, beta, mixx, stream, nullptr);
   if (rc) return rc;
   if (memory) {
     // the token leaving the window (position p - W) is written into memory before the read

@@ -55,7 +55,8 @@ constexpr int kHP_Smem = kHP_SmemA + kHP_SmemB + 1024 + 256;
 struct HeadProjArgs {
   const __nv_bfloat16* q;  // [B,T,H,D]
   const __nv_bfloat16* k;  // [B,T,G,D]
-  float* qm;               // [B,T,H,D]
+  float* qm;               // [B,T,H,D] fp32 (or null when qm16 is set)
+  __half* qm16;            // [B,T,H,D] fp16 (optional)
   float* km;               // [B,T,G,D]
   int B, T, H, G;
   int tiles_per_cta;       // token tiles walked by one CTA
@@ -187,18 +188,30 @@ __global__ void __launch_bounds__(kHP_Threads, 1)
       }
       const float inv = out_scale / fmaxf(sqrtf(ss), 1e-12f);
       const int t = it * kHP_M + row;
-      float* op = dst + (((size_t)b * a.T + t) * nheads_src + hsrc) * kHP_D;
+      const size_t ooff = (((size_t)b * a.T + t) * nheads_src + hsrc) * kHP_D;
+      const bool half_out = is_q && a.qm16 != nullptr;
 #pragma unroll 1
       for (int c = 0; c < kHP_D; c += 32) {
         uint32_t r[32];
         tmem_ld32(base + c, r);
         tmem_wait_ld();
         if (t < a.T) {
+          if (half_out) {
 #pragma unroll
-          for (int j = 0; j < 32; j += 4)
-            *reinterpret_cast<float4*>(op + c + j) =
-                make_float4(__uint_as_float(r[j]) * inv, __uint_as_float(r[j + 1]) * inv,
-                            __uint_as_float(r[j + 2]) * inv, __uint_as_float(r[j + 3]) * inv);
+            for (int j = 0; j < 32; j += 8)
+              *reinterpret_cast<uint4*>(a.qm16 + ooff + c + j) = make_uint4(
+                  pack_half2(__uint_as_float(r[j]) * inv, __uint_as_float(r[j + 1]) * inv),
+                  pack_half2(__uint_as_float(r[j + 2]) * inv, __uint_as_float(r[j + 3]) * inv),
+                  pack_half2(__uint_as_float(r[j + 4]) * inv, __uint_as_float(r[j + 5]) * inv),
+                  pack_half2(__uint_as_float(r[j + 6]) * inv, __uint_as_float(r[j + 7]) * inv));
+          } else {
+            float* op = dst + ooff;
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+              *reinterpret_cast<float4*>(op + c + j) =
+                  make_float4(__uint_as_float(r[j]) * inv, __uint_as_float(r[j + 1]) * inv,
+                              __uint_as_float(r[j + 2]) * inv, __uint_as_float(r[j + 3]) * inv);
+          }
         }
       }
       tc_fence_before();
@@ -353,8 +366,8 @@ int launch_prep_weights(const float* fq, const float* fk, const float* ab_w, con
   return cudaGetLastError() == cudaSuccess ? BF_OK : BF_ERR_CUDA;
 }
 
-int launch_head_proj(const __nv_bfloat16* q, const __nv_bfloat16* k, const __half* w_heads, float* qm, float* km,
-                     int B, int T, int H, int G, int sm_count, unsigned int* err, cudaStream_t stream) {
+int launch_head_proj(const __nv_bfloat16* q, const __nv_bfloat16* k, const __half* w_heads, float* qm, __half* qm16,
+                     float* km, int B, int T, int H, int G, int sm_count, unsigned int* err, cudaStream_t stream) {
   CUtensorMap wmap;
   int rc = make_tmap_kmajor(&wmap, w_heads, BF_F16, (uint64_t)(H + G) * kHP_D, kHP_D, kHP_D, kHP_D, 4);
   if (rc) return rc;
@@ -369,7 +382,7 @@ int launch_head_proj(const __nv_bfloat16* q, const __nv_bfloat16* k, const __hal
   const long long units = (long long)(H + G) * B;
   int per = (int)((ntiles * units + sm_count - 1) / sm_count);
   per = per < 1 ? 1 : (per > ntiles ? ntiles : per);
-  HeadProjArgs a{q, k, qm, km, B, T, H, G, per, err};
+  HeadProjArgs a{q, k, qm, qm16, km, B, T, H, G, per, err};
   dim3 grid((ntiles + per - 1) / per, H + G, B);
   head_proj_kernel<<<grid, kHP_Threads, kHP_Smem, stream>>>(wmap, a);
   return cudaGetLastError() == cudaSuccess ? BF_OK : BF_ERR_CUDA;

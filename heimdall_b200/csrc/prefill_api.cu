@@ -1,0 +1,308 @@
+// C ABI: chunked delta-rule op, window-attention op and the fused layer prefill.
+// Host-side orchestration only: validation, workspace carving, launch order on the caller's stream.
+#include "capi_internal.h"
+#include "common.cuh"
+#include "gdn_prefill.h"
+#include "window_prefill.h"
+
+namespace bfb {
+
+int launch_head_proj(const __nv_bfloat16* q, const __nv_bfloat16* k, const __half* w_heads, float* qm, __half* qm16,
+                     float* km, int B, int T, int H, int G, int sm_count, unsigned int* err, cudaStream_t stream);
+int mem_inputs_impl(const DeviceState& st, const bf_layer* L, const void* x, const void* q, const void* k,
+                    const int64_t* pos, long long pos0, int B, int T, float* qm, float* km, float* g, float* beta,
+                    float* mixx, cudaStream_t stream, __half* qm16);
+int check_layer(const bf_layer* L);
+size_t gdn_prefill_workspace(int B, int G, int T_steps);
+int gdn_prefill_carve(GdnStreams& s, void* ws);
+int launch_gdn_prefill(GdnStreams s, cudaStream_t stream);
+int launch_vt_prep(const __nv_bfloat16* v, long long vb, long long vg, long long vj, const __nv_bfloat16* ring_v,
+                   int nring, long long ring_pos0, int W, int B, int G, int Tk, int Tkp, __half* vt,
+                   cudaStream_t stream);
+int launch_kext_prep(const __nv_bfloat16* kr, const __nv_bfloat16* ring_k, int nring, long long ring_pos0, int W, int B,
+                     int T, int G, __nv_bfloat16* kext, cudaStream_t stream);
+int launch_window_prefill(const void* qr, const void* kext, const __half* vt, WinPreArgs a, cudaStream_t stream);
+
+static size_t al1k(size_t x) { return (x + 1023) & ~size_t(1023); }
+
+// ---------------------------------------------------------------------------------------- small kernels
+// q [B,T,H,D] (fp32 or bf16) -> fp16; k bf16 -> fp32
+__global__ void to_half_kernel(const void* __restrict__ src, int src_bf16, __half* __restrict__ dst, size_t n) {
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const float x = src_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(src)[i])
+                             : reinterpret_cast<const float*>(src)[i];
+    dst[i] = __float2half_rn(x);
+  }
+}
+__global__ void bf16_to_f32_kernel(const __nv_bfloat16* __restrict__ src, float* __restrict__ dst, size_t n) {
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    dst[i] = __bfloat162float(src[i]);
+}
+__global__ void zero_rows_kernel(float* __restrict__ o, int T, int rows, size_t row_elems) {
+  // o [B,T,row_elems]: zero rows 0..rows-1 of every batch
+  const int b = blockIdx.y;
+  const size_t n = (size_t)rows * row_elems;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    o[(size_t)b * T * row_elems + i] = 0.f;
+}
+// write the last m new tokens into their ring slots (heimdall/hibrit.py:414-422)
+__global__ void ring_write_kernel(const __nv_bfloat16* __restrict__ kr, const __nv_bfloat16* __restrict__ v,
+                                  const float* __restrict__ km, const float* __restrict__ g, const float* __restrict__ beta,
+                                  long long start, int T, int m, int G, int W, __nv_bfloat16* ring_k, __nv_bfloat16* ring_v,
+                                  float* ring_km, float* ring_g, float* ring_beta, int64_t* ring_pos) {
+  const int i = T - m + blockIdx.x;
+  const int bg = blockIdx.y, b = bg / G, gg = bg % G;
+  const long long p = start + i;
+  const int slot = (int)(p % W);
+  const int c = threadIdx.x * 8;
+  *reinterpret_cast<uint4*>(ring_k + (((size_t)b * G + gg) * W + slot) * 256 + c) =
+      *reinterpret_cast<const uint4*>(kr + (((size_t)b * G + gg) * T + i) * 256 + c);
+  *reinterpret_cast<uint4*>(ring_v + (((size_t)b * G + gg) * W + slot) * 256 + c) =
+      *reinterpret_cast<const uint4*>(v + (((size_t)b * T + i) * G + gg) * 256 + c);
+  float* kmd = ring_km + (((size_t)b * W + slot) * G + gg) * 256 + c;
+  const float* kms = km + (((size_t)b * T + i) * G + gg) * 256 + c;
+  *reinterpret_cast<float4*>(kmd) = *reinterpret_cast<const float4*>(kms);
+  *reinterpret_cast<float4*>(kmd + 4) = *reinterpret_cast<const float4*>(kms + 4);
+  if (threadIdx.x == 0) {
+    ring_g[((size_t)b * W + slot) * G + gg] = g[((size_t)b * T + i) * G + gg];
+    ring_beta[((size_t)b * W + slot) * G + gg] = beta[((size_t)b * T + i) * G + gg];
+    if (bg == 0) ring_pos[slot] = p;
+  }
+}
+
+static int grid_for(size_t n) {
+  size_t g = (n + 255) / 256;
+  return (int)(g > 4096 ? 4096 : (g < 1 ? 1 : g));
+}
+
+}  // namespace bfb
+
+using namespace bfb;
+
+extern "C" {
+
+// ================================================================================ delta rule op
+size_t bf_gdn_chunk_workspace(int B, int T, int G, int R, int D) {
+  if (B <= 0 || T <= 0 || G <= 0 || R <= 0 || D != 256) return 0;
+  return al1k((size_t)B * T * G * R * D * 2) + al1k((size_t)B * T * G * D * 4) + gdn_prefill_workspace(B, G, T);
+}
+
+int bf_gdn_chunk_fwd(const void* q, int q_dtype, const void* k, int k_dtype, const void* v, int v_dtype,
+                     const float* g, const float* beta, const float* s0, float* o, float* s_out, int B, int T, int G,
+                     int R, int D, void* ws, size_t ws_bytes, bf_stream_t stream) {
+  if (!q || !k || !v || !g || !beta || !o || !s_out || !ws) return BF_ERR_INVALID_ARGUMENT;
+  if (B <= 0 || T <= 0 || G <= 0 || R <= 0 || R > 8) return BF_ERR_INVALID_ARGUMENT;
+  if (D != 256) return BF_ERR_UNSUPPORTED;
+  for (int dt : {q_dtype, k_dtype, v_dtype})
+    if (dt != BF_F32 && dt != BF_BF16) return BF_ERR_INVALID_ARGUMENT;
+  if (ws_bytes < bf_gdn_chunk_workspace(B, T, G, R, D)) return BF_ERR_WORKSPACE;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || !aligned16(s_out) || !aligned16(ws) ||
+      (s0 && !aligned16(s0)))
+    return BF_ERR_ALIGNMENT;
+  if ((long long)B * G > 65535 || (long long)B * T * G * R > (1LL << 40)) return BF_ERR_UNSUPPORTED;
+  DeviceState st;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  uint8_t* p = static_cast<uint8_t*>(ws);
+  __half* q16 = reinterpret_cast<__half*>(p);
+  p += al1k((size_t)B * T * G * R * D * 2);
+  float* k32 = reinterpret_cast<float*>(p);
+  p += al1k((size_t)B * T * G * D * 4);
+  const size_t nq = (size_t)B * T * G * R * D;
+  to_half_kernel<<<grid_for(nq), 256, 0, stream>>>(q, q_dtype == BF_BF16, q16, nq);
+  const float* kf = static_cast<const float*>(k);
+  if (k_dtype == BF_BF16) {
+    const size_t nk = (size_t)B * T * G * D;
+    bf16_to_f32_kernel<<<grid_for(nk), 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(k), k32, nk);
+    kf = k32;
+  }
+  if (cudaGetLastError() != cudaSuccess) return BF_ERR_CUDA;
+  GdnStreams s{};
+  s.B = B; s.G = G; s.R = R; s.T = T;
+  s.n_steps = T;
+  s.n_chunks = (T + kGC - 1) / kGC;
+  s.n_pad = s.n_chunks * kGC;
+  s.nring = 0; s.W = 1; s.qoff = 0; s.ring_pos0 = 0;
+  s.km = kf;
+  if (v_dtype == BF_BF16) s.v = static_cast<const __nv_bfloat16*>(v);
+  else s.v32 = static_cast<const float*>(v);
+  s.g = g; s.beta = beta;
+  s.s0 = s0; s.s_out = s_out;
+  s.qm = q16; s.o = o;
+  s.err = st.err;
+  gdn_prefill_carve(s, p);
+  return launch_gdn_prefill(s, stream);
+}
+
+// ================================================================================ window op
+size_t bf_window_workspace(int B, int G, int Tk, int D) {
+  if (B <= 0 || G <= 0 || Tk <= 0 || D != 256) return 0;
+  const size_t Tkp = (size_t)((Tk + 63) / 64) * 64;
+  return al1k((size_t)B * G * D * Tkp * 2);
+}
+
+static int window_common(const void* qr, const void* k_ext, const __half* vt, const void* sink_k, const void* sink_v,
+                         int ns, long long qpos0, long long kpos0, long long klo, int B, int H, int G, int Tq, int Tk,
+                         int window, float* o, float* lse, const float* o_mem, const float* mixx, const float* mix_lse,
+                         const float* mem_scale, unsigned int* err, cudaStream_t stream) {
+  WinPreArgs a{};
+  a.B = B; a.H = H; a.G = G; a.Tq = Tq; a.Tk = Tk; a.Tkp = ((Tk + 63) / 64) * 64; a.W = window;
+  a.qpos0 = qpos0; a.kpos0 = kpos0; a.klo = klo;
+  a.sink_k = static_cast<const __nv_bfloat16*>(sink_k);
+  a.sink_v = static_cast<const __nv_bfloat16*>(sink_v);
+  a.ns = ns;
+  a.sk_b = (long long)G * ns * 256; a.sk_h = (long long)ns * 256; a.sk_k = 256;
+  a.sv_b = a.sk_b; a.sv_h = a.sk_h; a.sv_k = 256;
+  a.o = o; a.lse = lse;
+  a.o_mem = o_mem; a.mixx = mixx; a.mix_lse = mix_lse; a.mem_scale = mem_scale;
+  a.err = err;
+  return launch_window_prefill(qr, k_ext, vt, a, stream);
+}
+
+int bf_window_attn_fwd(const void* qr, const void* k_ext, const void* v_ext, long long vb, long long vg, long long vj,
+                       const void* sink_k, const void* sink_v, int ns, long long qpos0, long long kpos0, long long klo,
+                       int B, int H, int G, int Tq, int Tk, int D, int window, float* o, float* lse, void* ws,
+                       size_t ws_bytes, bf_stream_t stream) {
+  if (!qr || !k_ext || !v_ext || !o || !ws) return BF_ERR_INVALID_ARGUMENT;
+  if (B <= 0 || H <= 0 || G <= 0 || H % G || H / G > 8 || Tq <= 0 || Tk <= 0 || window <= 0 || ns < 0 || ns > 8)
+    return BF_ERR_INVALID_ARGUMENT;
+  if (ns > 0 && (!sink_k || !sink_v)) return BF_ERR_INVALID_ARGUMENT;
+  if (D != 256) return BF_ERR_UNSUPPORTED;
+  if (ws_bytes < bf_window_workspace(B, G, Tk, D)) return BF_ERR_WORKSPACE;
+  if (!aligned16(qr) || !aligned16(k_ext) || !aligned16(v_ext) || !aligned16(o) || !aligned16(ws) ||
+      (ns && (!aligned16(sink_k) || !aligned16(sink_v))) || (vj % 8) || (vg % 8) || (vb % 8))
+    return BF_ERR_ALIGNMENT;
+  if ((long long)B * H > 65535 || B > 65535) return BF_ERR_UNSUPPORTED;
+  DeviceState st;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  const int Tkp = ((Tk + 63) / 64) * 64;
+  __half* vt = static_cast<__half*>(ws);
+  rc = launch_vt_prep(static_cast<const __nv_bfloat16*>(v_ext), vb, vg, vj, nullptr, 0, 0, 1, B, G, Tk, Tkp, vt, stream);
+  if (rc) return rc;
+  return window_common(qr, k_ext, vt, sink_k, sink_v, ns, qpos0, kpos0, klo, B, H, G, Tq, Tk, window, o, lse, nullptr,
+                       nullptr, nullptr, nullptr, st.err, stream);
+}
+
+// ================================================================================ fused layer prefill
+size_t bf_layer_prefill_workspace(int B, int T, int H, int G, int D, int window, int with_ring) {
+  if (B <= 0 || T <= 0 || H <= 0 || G <= 0 || D != 256 || window <= 0) return 0;
+  const size_t Tk = (size_t)T + (with_ring ? window : 0);
+  const size_t Tkp = (Tk + 63) / 64 * 64;
+  const int steps = with_ring ? T : (T > window ? T - window : 1);
+  size_t n = 0;
+  n += al1k((size_t)B * T * H * D * 2);     // qm16
+  n += al1k((size_t)B * T * G * D * 4);     // km
+  n += al1k((size_t)B * T * G * 4) * 2;     // g, beta
+  n += al1k((size_t)B * T * H * 4);         // mixx
+  n += al1k((size_t)B * T * H * D * 4);     // o_mem
+  n += al1k((size_t)B * G * D * D * 4);     // state when there is no cache
+  n += al1k((size_t)B * G * D * Tkp * 2);   // V^T
+  if (with_ring) n += al1k((size_t)B * G * Tk * D * 2);  // K of the extended sequence
+  n += gdn_prefill_workspace(B, G, steps);
+  return n;
+}
+
+int bf_bifrost_layer_prefill(const bf_layer* L, const void* x, const void* q, const void* k, const void* v,
+                             const void* qr, const void* kr, long long start, int B, int T, bf_ring_cache* C,
+                             const void* sink_k, const void* sink_v, int ns, int memory, float* o, float* lse,
+                             void* ws, size_t ws_bytes, bf_stream_t stream) {
+  int rc = check_layer(L);
+  if (rc) return rc;
+  if (!x || !q || !k || !v || !qr || !kr || !o || !ws || B <= 0 || T <= 0 || start < 0) return BF_ERR_INVALID_ARGUMENT;
+  if (ns < 0 || ns > 8 || (ns > 0 && (!sink_k || !sink_v))) return BF_ERR_INVALID_ARGUMENT;
+  const int H = L->H, G = L->G, D = L->D, W = L->window, R = H / G;
+  const bool ring_case = C != nullptr && start > 0;
+  if (C && (!C->ring_k || !C->ring_v || !C->ring_km || !C->ring_g || !C->ring_beta || !C->ring_pos || !C->S))
+    return BF_ERR_INVALID_ARGUMENT;
+  if (C && C->ring_pos_bstride != 0) return BF_ERR_UNSUPPORTED;
+  if (ws_bytes < bf_layer_prefill_workspace(B, T, H, G, D, W, ring_case ? 1 : 0)) return BF_ERR_WORKSPACE;
+  for (const void* pp : {x, q, k, v, qr, kr, (const void*)o, (const void*)ws})
+    if (!aligned16(pp)) return BF_ERR_ALIGNMENT;
+  if (ns && (!aligned16(sink_k) || !aligned16(sink_v))) return BF_ERR_ALIGNMENT;
+  if ((long long)B * (H + G) > 65535) return BF_ERR_UNSUPPORTED;
+  DeviceState st;
+  rc = device_state(&st);
+  if (rc) return rc;
+
+  const bool use_mem = memory && start + T > W;
+  const int Tk = T + (ring_case ? W : 0);
+  const int Tkp = ((Tk + 63) / 64) * 64;
+  uint8_t* p = static_cast<uint8_t*>(ws);
+  auto take = [&](size_t bytes) {
+    uint8_t* r = p;
+    p += al1k(bytes);
+    return r;
+  };
+  __half* qm16 = reinterpret_cast<__half*>(take((size_t)B * T * H * D * 2));
+  float* km = reinterpret_cast<float*>(take((size_t)B * T * G * D * 4));
+  float* g = reinterpret_cast<float*>(take((size_t)B * T * G * 4));
+  float* beta = reinterpret_cast<float*>(take((size_t)B * T * G * 4));
+  float* mixx = reinterpret_cast<float*>(take((size_t)B * T * H * 4));
+  float* o_mem = reinterpret_cast<float*>(take((size_t)B * T * H * D * 4));
+  float* s_tmp = reinterpret_cast<float*>(take((size_t)B * G * D * D * 4));
+  __half* vt = reinterpret_cast<__half*>(take((size_t)B * G * D * Tkp * 2));
+  __nv_bfloat16* kext = ring_case ? reinterpret_cast<__nv_bfloat16*>(take((size_t)B * G * Tk * D * 2)) : nullptr;
+  void* gws = p;
+
+  // 1. memory inputs (projections on tcgen05)
+  if (use_mem || C) {
+    rc = mem_inputs_impl(st, L, x, q, k, nullptr, start, B, T, nullptr, km, g, beta, mixx, stream, qm16);
+    if (rc) return rc;
+  }
+  // 2. memory: the write stream is delayed by W (token i enters memory when it leaves the window)
+  if (use_mem) {
+    GdnStreams s{};
+    s.B = B; s.G = G; s.R = R; s.T = T; s.W = W;
+    if (ring_case) {
+      s.nring = W; s.qoff = 0; s.n_steps = T; s.ring_pos0 = start - W;
+      s.ring_km = C->ring_km;
+      s.ring_v = static_cast<const __nv_bfloat16*>(C->ring_v);
+      s.ring_g = C->ring_g; s.ring_beta = C->ring_beta; s.ring_pos = C->ring_pos;
+      s.s0 = C->S;
+    } else {
+      // no history: the first W write steps are no-ops, so queries before W read the zero state
+      s.nring = 0; s.qoff = W; s.n_steps = T - W; s.ring_pos0 = 0;
+      s.s0 = nullptr;
+      const int zr = T < W ? T : W;
+      zero_rows_kernel<<<dim3(grid_for((size_t)zr * H * D), B), 256, 0, stream>>>(o_mem, T, zr, (size_t)H * D);
+    }
+    s.n_chunks = (s.n_steps + kGC - 1) / kGC;
+    s.n_pad = s.n_chunks * kGC;
+    s.km = km; s.v = static_cast<const __nv_bfloat16*>(v); s.g = g; s.beta = beta;
+    s.s_out = C ? C->S : s_tmp;
+    s.qm = qm16; s.o = o_mem; s.err = st.err;
+    if (s.n_steps > 0) {
+      gdn_prefill_carve(s, gws);
+      rc = launch_gdn_prefill(s, stream);
+      if (rc) return rc;
+    }
+  }
+  // 3. window attention over the extended keys, with the gate and mix fused into its epilogue
+  const void* kx = kr;
+  if (ring_case) {
+    rc = launch_kext_prep(static_cast<const __nv_bfloat16*>(kr), static_cast<const __nv_bfloat16*>(C->ring_k), W,
+                          start - W, W, B, T, G, kext, stream);
+    if (rc) return rc;
+    kx = kext;
+  }
+  rc = launch_vt_prep(static_cast<const __nv_bfloat16*>(v), (long long)T * G * D, D, (long long)G * D,
+                      ring_case ? static_cast<const __nv_bfloat16*>(C->ring_v) : nullptr, ring_case ? W : 0,
+                      start - W, W, B, G, Tk, Tkp, vt, stream);
+  if (rc) return rc;
+  rc = window_common(qr, kx, vt, sink_k, sink_v, ns, start, ring_case ? start - W : start, L->sinks, B, H, G, T, Tk, W,
+                     o, lse, use_mem ? o_mem : nullptr, mixx, L->mix_lse, L->mem_scale, st.err, stream);
+  if (rc) return rc;
+  // 4. cache: the last min(T, W) tokens go to their ring slots (the state was updated in place)
+  if (C) {
+    const int m = T < W ? T : W;
+    ring_write_kernel<<<dim3(m, B * G), 32, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(kr), static_cast<const __nv_bfloat16*>(v), km, g, beta, start, T, m, G, W,
+        static_cast<__nv_bfloat16*>(C->ring_k), static_cast<__nv_bfloat16*>(C->ring_v), C->ring_km, C->ring_g,
+        C->ring_beta, C->ring_pos);
+    if (cudaGetLastError() != cudaSuccess) return BF_ERR_CUDA;
+  }
+  return BF_OK;
+}
+
+}  // extern "C"

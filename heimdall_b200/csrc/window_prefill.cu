@@ -1,0 +1,454 @@
+// Sliding-window + sink attention over a block of queries (prefill), on the 5th-gen tensor core.
+//
+// Semantics: HybridAttention._window_fp32 (heimdall/hibrit.py:341-361).  A query at position p sees a key
+// at position kp when kp <= p and either kp is a sink (kp < S, taken from the sink buffer) or
+// (p - kp < W and kp >= S).  Scores use q . k / sqrt(D).  Returns o and lse = log sum exp.
+// The fused-layer epilogue also applies the LSE gate and the mix of heimdall/hibrit.py:409-411.
+//
+// Keys come as one "extended" sequence (ring in time order, then the new tokens; key j has position
+// kpos0 + j; positions below `klo` are not valid window keys).  K is bf16 [B,G,Tk,D]; V is pre-transposed
+// to fp16 [B,G,D,Tkp] so that both MMA operands are K-major.
+//
+// CTA = (128-query tile, query head, batch).  Warp roles (224 threads):
+//   warp 0: TMA producer of Q and K tiles;   warp 6: TMA producer of V tiles;
+//   warp 1: MMA issuer (one elected thread): S = Q K^T (bf16, M128 N128 K256) into a double-buffered TMEM
+//           score tile, then O += P V (fp16, M128 N256 K128) into a TMEM accumulator;
+//   warps 2-5: softmax / epilogue, one thread per query row (= TMEM lane): online softmax with lazy
+//           rescaling (O is rescaled in TMEM only when the running max grows by more than e^8, so P stays
+//           within fp16 range), fp16 P written to shared memory in the 128-byte-swizzled K-major layout.
+//   Epilogue: the sink keys (<= 8) are folded in exactly in fp32 per row, then o / lse are written, or the
+//   gate and mix with the memory read are applied and the layer output is written.
+// TMEM: S buffers at columns 0 and 128, O at columns 256..511.
+// Shared memory: Q 64 KB, K 64 KB, V 64 KB, P 32 KB.
+#include "capi_internal.h"
+#include "common.cuh"
+#include "tmap.h"
+#include "window_prefill.h"
+
+namespace bfb {
+
+constexpr int kWP_M = 128;       // queries per tile
+constexpr int kWP_N = 128;       // keys per tile
+constexpr int kWP_D = 256;
+constexpr int kWP_Threads = 224;
+constexpr int kWP_SmemQ = kWP_M * kWP_D * 2;
+constexpr int kWP_SmemK = kWP_N * kWP_D * 2;
+constexpr int kWP_SmemV = kWP_D * kWP_N * 2;
+constexpr int kWP_SmemP = kWP_M * kWP_N * 2;
+constexpr int kWP_Smem = kWP_SmemQ + kWP_SmemK + kWP_SmemV + kWP_SmemP + 1024 + 256;
+constexpr float kRescaleThresh = 8.0f;  // natural-log units
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+__global__ void __launch_bounds__(kWP_Threads, 1)
+    window_prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
+                          const __grid_constant__ CUtensorMap vmap, WinPreArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + kWP_SmemQ;
+  uint8_t* sV = sK + kWP_SmemK;
+  uint8_t* sP = sV + kWP_SmemV;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kWP_SmemP);
+  uint64_t* bar_q = bars + 0;
+  uint64_t* bar_k_full = bars + 1;
+  uint64_t* bar_k_empty = bars + 2;
+  uint64_t* bar_v_full = bars + 3;
+  uint64_t* bar_pv = bars + 4;       // PV_j finished (O stable, P and V buffers free)
+  uint64_t* bar_s_full = bars + 5;   // [2]
+  uint64_t* bar_s_free = bars + 7;   // [2] (128 arrivals)
+  uint64_t* bar_p_full = bars + 9;   // (128 arrivals)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 11);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int i0 = blockIdx.x * kWP_M;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int R = a.H / a.G, g = h / R;
+  const long long P0 = a.qpos0 + i0;
+  const long long Plast = a.qpos0 + min(i0 + kWP_M, a.Tq) - 1;
+  // key tiles covering positions [max(klo, P0 - W + 1), Plast] of the extended key sequence
+  const long long kp_lo = max(a.klo, P0 - a.W + 1);
+  long long jlo = kp_lo - a.kpos0, jhi = min(Plast - a.kpos0, (long long)a.Tk - 1);
+  int jt0 = 0, n = 0;
+  if (kp_lo <= Plast && jhi >= 0 && jlo <= jhi) {
+    if (jlo < 0) jlo = 0;
+    jt0 = (int)(jlo / kWP_N);
+    n = (int)(jhi / kWP_N) - jt0 + 1;
+  }
+
+  if (tid == 0) {
+    for (int i = 0; i < 10; ++i) mbar_init(bars + i, (i == 7 || i == 8 || i == 9) ? 128 : 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch(&qmap);
+      tma_prefetch(&kmap);
+      mbar_expect_tx(bar_q, kWP_SmemQ);
+      tma_load_3d(sQ, &qmap, bar_q, 0, (b * a.H + h) * a.Tq + i0, 0);
+      int issued = 0;
+      for (int j = 0; j < n; ++j) {
+        if (j >= 1 && !mbar_wait(bar_k_empty, (j - 1) & 1, abort_flag, a.err, 0x31)) break;
+        mbar_expect_tx(bar_k_full, kWP_SmemK);
+        tma_load_3d(sK, &kmap, bar_k_full, 0, (b * a.G + g) * a.Tk + (jt0 + j) * kWP_N, 0);
+        issued = j + 1;
+      }
+      // drain our copies before the CTA can exit
+      mbar_wait(bar_q, 0, nullptr, a.err, 0x32);
+      if (issued > 0) mbar_wait(bar_k_full, (issued - 1) & 1, nullptr, a.err, 0x33);
+    }
+  } else if (warp == 6) {
+    if (lane == 0) {
+      tma_prefetch(&vmap);
+      int issued = 0;
+      for (int j = 0; j < n; ++j) {
+        if (j >= 1 && !mbar_wait(bar_pv, (j - 1) & 1, abort_flag, a.err, 0x34)) break;
+        mbar_expect_tx(bar_v_full, kWP_SmemV);
+        tma_load_3d(sV, &vmap, bar_v_full, 0, (b * a.G + g) * kWP_D, ((jt0 + j) * kWP_N) / 64);
+        issued = j + 1;
+      }
+      if (issued > 0) mbar_wait(bar_v_full, (issued - 1) & 1, nullptr, a.err, 0x35);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && n > 0) {
+      constexpr uint32_t idesc_qk = idesc_f16(kWP_M, kWP_N, 1);
+      constexpr uint32_t idesc_pv = idesc_f16(kWP_M, kWP_D, 0);
+      const uint32_t aQ = smem_u32(sQ), bK = smem_u32(sK), aP = smem_u32(sP), bV = smem_u32(sV);
+      bool ok = mbar_wait(bar_q, 0, abort_flag, a.err, 0x36);
+      auto issue_pv = [&](int jj) -> bool {
+        if (!mbar_wait(bar_p_full, jj & 1, abort_flag, a.err, 0x37)) return false;
+        if (!mbar_wait(bar_v_full, jj & 1, abort_flag, a.err, 0x38)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < kWP_N / 16; ++ks)
+          umma_f16_ss(tmem + 256, sdesc_kstep(aP, kWP_M, ks), sdesc_kstep(bV, kWP_D, ks), idesc_pv, (jj | ks) > 0);
+        umma_commit(bar_pv);
+        return true;
+      };
+      for (int j = 0; j < n && ok; ++j) {
+        const int buf = j & 1;
+        ok = mbar_wait(bar_k_full, j & 1, abort_flag, a.err, 0x39);
+        if (ok && j >= 2) ok = mbar_wait(&bar_s_free[buf], ((j >> 1) - 1) & 1, abort_flag, a.err, 0x3a);
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < kWP_D / 16; ++ks)
+          umma_f16_ss(tmem + buf * 128, sdesc_kstep(aQ, kWP_M, ks), sdesc_kstep(bK, kWP_N, ks), idesc_qk, ks > 0);
+        umma_commit(bar_k_empty);
+        umma_commit(&bar_s_full[buf]);
+        if (j >= 1) ok = issue_pv(j - 1);
+      }
+      if (ok) issue_pv(n - 1);
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax + epilogue (warps 2..5)
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;                // query row in the tile == TMEM lane
+    const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
+    const long long p = P0 + r;                  // position of this query
+    const float scale = rsqrtf((float)kWP_D);
+    float m_ref = -INFINITY, l = 0.f;
+    bool alive = true;
+    for (int j = 0; j < n && alive; ++j) {
+      const int buf = j & 1;
+      if (!mbar_wait(&bar_s_full[buf], (j >> 1) & 1, abort_flag, a.err, 0x3b)) { alive = false; break; }
+      tc_fence_after();
+      float s[kWP_N];
+#pragma unroll
+      for (int c = 0; c < kWP_N; c += 32) {
+        uint32_t u[32];
+        tmem_ld32(trow + buf * 128 + c, u);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) s[c + e] = __uint_as_float(u[e]) * scale;
+      }
+      tc_fence_before();
+      mbar_arrive(&bar_s_free[buf]);
+      // mask: key position kp = kpos0 + (jt0 + j) * 128 + c
+      const long long kt = a.kpos0 + (long long)(jt0 + j) * kWP_N;
+      const bool full = kt >= a.klo && kt + kWP_N - 1 <= P0 && (Plast - kt) < a.W;
+      float mt = -INFINITY;
+      if (full) {
+#pragma unroll
+        for (int c = 0; c < kWP_N; ++c) mt = fmaxf(mt, s[c]);
+      } else {
+#pragma unroll
+        for (int c = 0; c < kWP_N; ++c) {
+          const long long kp = kt + c;
+          const bool ok = kp >= a.klo && kp <= p && (p - kp) < a.W;
+          s[c] = ok ? s[c] : -INFINITY;
+          mt = fmaxf(mt, s[c]);
+        }
+      }
+      float factor = 1.f;
+      bool rescale = false;
+      if (m_ref == -INFINITY) {
+        m_ref = mt;  // O holds nothing yet (or only zeros)
+      } else if (mt > m_ref + kRescaleThresh) {
+        factor = __expf(m_ref - mt);
+        rescale = true;
+        m_ref = mt;
+        l *= factor;
+      }
+      // probabilities (fp32 sum, fp16 operand)
+      uint32_t pk[kWP_N / 2];
+      if (m_ref == -INFINITY) {
+#pragma unroll
+        for (int c = 0; c < kWP_N / 2; ++c) pk[c] = 0u;
+      } else {
+#pragma unroll
+        for (int c = 0; c < kWP_N; c += 2) {
+          const float e0 = __expf(s[c] - m_ref), e1 = __expf(s[c + 1] - m_ref);
+          l += e0 + e1;
+          pk[c / 2] = pack_half2(e0, e1);
+        }
+      }
+      // the P buffer and O are free once PV_{j-1} has completed
+      if (j >= 1 && !mbar_wait(bar_pv, (j - 1) & 1, abort_flag, a.err, 0x3c)) { alive = false; break; }
+      tc_fence_after();
+      if (rescale) {
+#pragma unroll 1
+        for (int c = 0; c < kWP_D; c += 32) {
+          uint32_t u[32];
+          tmem_ld32(trow + 256 + c, u);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) u[e] = __float_as_uint(__uint_as_float(u[e]) * factor);
+          tmem_st32(trow + 256 + c, u);
+        }
+        tmem_wait_st();
+      }
+#pragma unroll
+      for (int ch = 0; ch < kWP_N / 8; ++ch) {  // 16 chunks of 8 fp16
+        const int atom = ch >> 3, col = (ch & 7) * 8;
+        *reinterpret_cast<uint4*>(sP + atom * (kWP_M * 128) + sw128_offset(r, col)) =
+            make_uint4(pk[ch * 4], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
+      }
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(bar_p_full);
+    }
+    // ------------------------------------------------------------------ epilogue
+    if (alive && n > 0) alive = mbar_wait(bar_pv, (n - 1) & 1, abort_flag, a.err, 0x3d);
+    tc_fence_after();
+    if (alive) {
+      // sink keys (positions 0..ns-1), exact in fp32
+      float se[8];
+      int nsv = 0;
+      for (int e = 0; e < a.ns; ++e) {
+        const __nv_bfloat16* kp = a.sink_k + (size_t)b * a.sk_b + (size_t)g * a.sk_h + (size_t)e * a.sk_k;
+        float acc = 0.f;
+#pragma unroll 4
+        for (int c = 0; c < kWP_D / 8; ++c) {
+          const int atom = c >> 3, col = (c & 7) * 8;
+          const uint4 qv = *reinterpret_cast<const uint4*>(sQ + atom * (kWP_M * 128) + sw128_offset(r, col));
+          const uint4 kv = __ldg(reinterpret_cast<const uint4*>(kp) + c);
+          const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w}, kw[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+          for (int t2 = 0; t2 < 4; ++t2) {
+            acc += __uint_as_float(qw[t2] << 16) * __uint_as_float(kw[t2] << 16);
+            acc += __uint_as_float(qw[t2] & 0xffff0000u) * __uint_as_float(kw[t2] & 0xffff0000u);
+          }
+        }
+        se[e] = (e <= p) ? acc * scale : -INFINITY;
+        nsv = e + 1;
+      }
+      float mf = m_ref;
+      for (int e = 0; e < nsv; ++e) mf = fmaxf(mf, se[e]);
+      const float fo = (m_ref == -INFINITY) ? 0.f : __expf(m_ref - mf);
+      float lf = l * fo;
+      float we[8];
+      for (int e = 0; e < nsv; ++e) {
+        we[e] = (se[e] == -INFINITY) ? 0.f : __expf(se[e] - mf);
+        lf += we[e];
+      }
+      const float inv = lf > 0.f ? 1.f / lf : 0.f;
+      const float lse = lf > 0.f ? mf + logf(lf) : -INFINITY;
+      const int qi = i0 + r;
+      const bool row_ok = qi < a.Tq;
+      float gam = 0.f;
+      const size_t orow = (((size_t)b * a.Tq + qi) * a.H + h) * kWP_D;
+      if (row_ok) {
+        if (a.lse) a.lse[((size_t)b * a.H + h) * a.Tq + qi] = lse;
+        if (a.o_mem && p >= a.W) {
+          const float z = a.mixx[((size_t)b * a.Tq + qi) * a.H + h] + a.mix_lse[h] * (lse - logf((float)a.W));
+          gam = 1.f / (1.f + __expf(-z));
+        }
+      }
+      const float rho = a.o_mem ? a.mem_scale[h] : 0.f;
+#pragma unroll 1
+      for (int c = 0; c < kWP_D; c += 32) {
+        uint32_t u[32];
+        if (n > 0) {
+          tmem_ld32(trow + 256 + c, u);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) u[e] = 0u;
+        }
+        float ov[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) ov[e] = __uint_as_float(u[e]) * fo;
+        for (int e2 = 0; e2 < nsv; ++e2) {
+          if (we[e2] == 0.f) continue;
+          const __nv_bfloat16* vp = a.sink_v + (size_t)b * a.sv_b + (size_t)g * a.sv_h + (size_t)e2 * a.sv_k + c;
+#pragma unroll
+          for (int e = 0; e < 32; e += 8) {
+            const uint4 vv = __ldg(reinterpret_cast<const uint4*>(vp + e));
+            const uint32_t vw[4] = {vv.x, vv.y, vv.z, vv.w};
+#pragma unroll
+            for (int t2 = 0; t2 < 4; ++t2) {
+              ov[e + 2 * t2] += we[e2] * __uint_as_float(vw[t2] << 16);
+              ov[e + 2 * t2 + 1] += we[e2] * __uint_as_float(vw[t2] & 0xffff0000u);
+            }
+          }
+        }
+        if (row_ok) {
+          float* op = a.o + orow + c;
+          if (a.o_mem && p >= a.W) {
+            const float* mp = a.o_mem + orow + c;
+#pragma unroll
+            for (int e = 0; e < 32; e += 4) {
+              const float4 mv = *reinterpret_cast<const float4*>(mp + e);
+              float w0 = ov[e] * inv, w1 = ov[e + 1] * inv, w2 = ov[e + 2] * inv, w3 = ov[e + 3] * inv;
+              *reinterpret_cast<float4*>(op + e) =
+                  make_float4(w0 + gam * (rho * mv.x - w0), w1 + gam * (rho * mv.y - w1), w2 + gam * (rho * mv.z - w2),
+                              w3 + gam * (rho * mv.w - w3));
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; e += 4)
+              *reinterpret_cast<float4*>(op + e) =
+                  make_float4(ov[e] * inv, ov[e + 1] * inv, ov[e + 2] * inv, ov[e + 3] * inv);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// V (time-major [B,T,G,D] bf16, optionally preceded by a ring [B,G,W,D] read in time order) ->
+// V^T fp16 [B,G,D,Tkp], keys beyond Tk zero.  One CTA = 64 keys x 256 columns of one (b, g).
+__global__ void __launch_bounds__(256) vt_prep_kernel(const __nv_bfloat16* __restrict__ v, long long vb, long long vg,
+                                                      long long vj, const __nv_bfloat16* __restrict__ ring_v, int nring,
+                                                      long long ring_pos0, int W, int G, int Tk, int Tkp,
+                                                      __half* __restrict__ vt) {
+  __shared__ __half tile[64][256 + 8];
+  const int jb = blockIdx.x * 64, bg = blockIdx.y, b = bg / G, g = bg % G;
+  const int t = threadIdx.x;
+  // load 64 key rows (8 threads per row, 32 columns each)
+  for (int rr = t >> 3; rr < 64; rr += 32) {
+    const int j = jb + rr;
+    const int c0 = (t & 7) * 32;
+    const __nv_bfloat16* src = nullptr;
+    if (j < nring) {
+      const long long kp = ring_pos0 + j;
+      const int slot = (int)(((kp % W) + W) % W);
+      src = ring_v + (((size_t)b * G + g) * W + slot) * 256 + c0;
+    } else if (j < Tk) {
+      src = v + (size_t)b * vb + (size_t)g * vg + (size_t)(j - nring) * vj + c0;
+    }
+#pragma unroll
+    for (int c = 0; c < 32; c += 8) {
+      uint4 u = src ? *reinterpret_cast<const uint4*>(src + c) : make_uint4(0, 0, 0, 0);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        tile[rr][c0 + c + 2 * e] = __float2half_rn(__uint_as_float(w[e] << 16));
+        tile[rr][c0 + c + 2 * e + 1] = __float2half_rn(__uint_as_float(w[e] & 0xffff0000u));
+      }
+    }
+  }
+  __syncthreads();
+  // write 256 rows (columns of V) x 64 keys: each thread one column, 64 keys = 128 bytes
+  const int d = t;
+  __half* dst = vt + (((size_t)b * G + g) * 256 + d) * Tkp + jb;
+  uint32_t w[32];
+#pragma unroll
+  for (int e = 0; e < 32; ++e) {
+    __half2 h2 = __halves2half2(tile[2 * e][d], tile[2 * e + 1][d]);
+    w[e] = *reinterpret_cast<uint32_t*>(&h2);
+  }
+#pragma unroll
+  for (int e = 0; e < 32; e += 4) *reinterpret_cast<uint4*>(dst + 2 * e) = make_uint4(w[e], w[e + 1], w[e + 2], w[e + 3]);
+}
+
+// K of the extended sequence: ring (time order) then kr [B,G,T,D] -> kext [B,G,W+T,D] (only with a ring)
+__global__ void kext_prep_kernel(const __nv_bfloat16* __restrict__ kr, const __nv_bfloat16* __restrict__ ring_k,
+                                 int nring, long long ring_pos0, int W, int T, int G, __nv_bfloat16* __restrict__ kext) {
+  const int j = blockIdx.x, bg = blockIdx.y, b = bg / G, g = bg % G;
+  const int Tk = nring + T;
+  const __nv_bfloat16* src;
+  if (j < nring) {
+    const long long kp = ring_pos0 + j;
+    const int slot = (int)(((kp % W) + W) % W);
+    src = ring_k + (((size_t)b * G + g) * W + slot) * 256;
+  } else {
+    src = kr + (((size_t)b * G + g) * T + (j - nring)) * 256;
+  }
+  const int c = threadIdx.x * 8;
+  *reinterpret_cast<uint4*>(kext + (((size_t)b * G + g) * Tk + j) * 256 + c) = *reinterpret_cast<const uint4*>(src + c);
+}
+
+int window_prefill_smem() { return kWP_Smem; }
+
+int launch_vt_prep(const __nv_bfloat16* v, long long vb, long long vg, long long vj, const __nv_bfloat16* ring_v,
+                   int nring, long long ring_pos0, int W, int B, int G, int Tk, int Tkp, __half* vt,
+                   cudaStream_t stream) {
+  vt_prep_kernel<<<dim3(Tkp / 64, B * G), 256, 0, stream>>>(v, vb, vg, vj, ring_v, nring, ring_pos0, W, G, Tk, Tkp, vt);
+  return cudaGetLastError() == cudaSuccess ? BF_OK : BF_ERR_CUDA;
+}
+
+int launch_kext_prep(const __nv_bfloat16* kr, const __nv_bfloat16* ring_k, int nring, long long ring_pos0, int W, int B,
+                     int T, int G, __nv_bfloat16* kext, cudaStream_t stream) {
+  kext_prep_kernel<<<dim3(nring + T, B * G), 32, 0, stream>>>(kr, ring_k, nring, ring_pos0, W, T, G, kext);
+  return cudaGetLastError() == cudaSuccess ? BF_OK : BF_ERR_CUDA;
+}
+
+int launch_window_prefill(const void* qr, const void* kext, const __half* vt, WinPreArgs a, cudaStream_t stream) {
+  CUtensorMap qmap, kmap, vmap;
+  int rc = make_tmap_kmajor(&qmap, qr, BF_BF16, (uint64_t)a.B * a.H * a.Tq, kWP_D, kWP_D, kWP_M, 4);
+  if (rc) return rc;
+  rc = make_tmap_kmajor(&kmap, kext, BF_BF16, (uint64_t)a.B * a.G * a.Tk, kWP_D, kWP_D, kWP_N, 4);
+  if (rc) return rc;
+  rc = make_tmap_kmajor(&vmap, vt, BF_F16, (uint64_t)a.B * a.G * kWP_D, a.Tkp, a.Tkp, kWP_D, 2);
+  if (rc) return rc;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(window_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kWP_Smem) !=
+        cudaSuccess)
+      return BF_ERR_CUDA;
+    attr = true;
+  }
+  dim3 grid((a.Tq + kWP_M - 1) / kWP_M, a.H, a.B);
+  window_prefill_kernel<<<grid, kWP_Threads, kWP_Smem, stream>>>(qmap, kmap, vmap, a);
+  return cudaGetLastError() == cudaSuccess ? BF_OK : BF_ERR_CUDA;
+}
+
+}  // namespace bfb

@@ -66,3 +66,84 @@ def delta_rule_step_gqa(q, k, v, g, beta, state, out_state=None):
               ptr(g.float().contiguous()), ptr(beta.float().contiguous()), ptr(s_in), ptr(s_out), ptr(o),
               B, G, R, D, stream_handle())
     return o, s_out
+
+
+def _ws(nbytes: int, device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=device)
+
+
+def _dt(t) -> int:
+    return 1 if t.dtype == torch.bfloat16 else 0
+
+
+def _as_kernel_dtype(t):
+    return t.contiguous() if t.dtype == torch.bfloat16 else t.float().contiguous()
+
+
+def delta_rule_gqa(q, k, v, g, beta, chunk: int = 64, state=None):
+    """GQA-native chunked gated delta rule (mirror of ``heimdall.motor.delta_rule_gqa``, motor.py:70-102).
+
+    q [B,T,G,R,Dk]; k [B,T,G,Dk]; v [B,T,G,Dv]; g, beta [B,T,G]; state [B,G,Dk,Dv] or None.
+    Returns o [B,T,G,R,Dv] and the final state [B,G,Dk,Dv], both fp32.  ``chunk`` is accepted for signature
+    compatibility: the GPU scan always uses 128-token chunks (the recurrence, hence the result, does not
+    depend on the chunk length).
+    """
+    check_cuda(q, k, v, g, beta, state)
+    B, T, G, R, D = q.shape
+    if k.shape[-1] != D or v.shape[-1] != D:
+        raise NotImplementedError("heimdall_b200 implements square states (Dk == Dv)")
+    if D != 256:
+        raise NotImplementedError("the tensor-core delta rule is built for head dim 256")
+    dev = q.device
+    qq, kk, vv = _as_kernel_dtype(q), _as_kernel_dtype(k), _as_kernel_dtype(v)
+    gg, bb = g.float().contiguous(), beta.float().contiguous()
+    s0 = None if state is None else state.float().contiguous()
+    o = torch.empty(B, T, G, R, D, device=dev, dtype=torch.float32)
+    s_out = torch.empty(B, G, D, D, device=dev, dtype=torch.float32)
+    nws = _lib.size("bf_gdn_chunk_workspace", B, T, G, R, D)
+    ws = _ws(nws, dev)
+    _lib.call("bf_gdn_chunk_fwd", ptr(qq), _dt(qq), ptr(kk), _dt(kk), ptr(vv), _dt(vv), ptr(gg), ptr(bb), ptr(s0),
+              ptr(o), ptr(s_out), B, T, G, R, D, ptr(ws), nws, stream_handle())
+    return o, s_out
+
+
+def delta_rule(q, k, v, g, beta, chunk_size: int = 64, initial_state=None, backend: str = "auto"):
+    """Chunked gated delta rule (mirror of ``heimdall.kernels.delta_rule``, kernels.py:94-129 / 152-155).
+
+    q, k: [B,T,H,Dk]; v: [B,T,H,Dv]; g, beta: [B,T,H]; initial_state [B,H,Dk,Dv] or None.
+    Returns o [B,T,H,Dv] and the final state [B,H,Dk,Dv] (fp32).  ``backend`` is accepted for signature
+    compatibility; this implementation always runs the CUDA kernels (there is no CPU path).
+    """
+    B, T, H, D = q.shape
+    o, s = delta_rule_gqa(q.reshape(B, T, H, 1, D), k, v, g, beta, chunk_size, initial_state)
+    return o.reshape(B, T, H, D), s
+
+
+def window_attention(qr, ext_k, ext_v, qpos0: int, kpos0: int, klo: int, window: int, sink_k=None, sink_v=None,
+                     with_lse: bool = True):
+    """Sliding-window + sink attention (the math of ``HybridAttention._window_fp32``, hibrit.py:341-361).
+
+    qr [B,H,Tq,D] (query i at position qpos0 + i); ext_k [B,G,Tk,D] and ext_v [B,G,Tk,D] or any strided view
+    (key j at position kpos0 + j); keys with position < klo are not window keys; sink_k/sink_v [B,G,ns,D]
+    (positions 0..ns-1) or None.  Returns o [B,Tq,H,D] and lse [B,H,Tq] (fp32).
+    """
+    check_cuda(qr, ext_k, ext_v, sink_k, sink_v)
+    B, H, Tq, D = qr.shape
+    G, Tk = ext_k.shape[1], ext_k.shape[2]
+    bf = torch.bfloat16
+    qb = qr.to(bf).contiguous()
+    kb = ext_k.to(bf).contiguous()
+    vb = ext_v.to(bf)
+    if vb.stride(-1) != 1:
+        vb = vb.contiguous()
+    ns = 0 if sink_k is None else sink_k.shape[2]
+    skb = None if sink_k is None else sink_k.to(bf).contiguous()
+    svb = None if sink_v is None else sink_v.to(bf).contiguous()
+    o = torch.empty(B, Tq, H, D, device=qr.device, dtype=torch.float32)
+    lse = torch.empty(B, H, Tq, device=qr.device, dtype=torch.float32) if with_lse else None
+    nws = _lib.size("bf_window_workspace", B, G, Tk, D)
+    ws = _ws(nws, qr.device)
+    _lib.call("bf_window_attn_fwd", ptr(qb), ptr(kb), ptr(vb), vb.stride(0), vb.stride(1), vb.stride(2), ptr(skb),
+              ptr(svb), ns, int(qpos0), int(kpos0), int(klo), B, H, G, Tq, Tk, D, int(window), ptr(o), ptr(lse),
+              ptr(ws), nws, stream_handle())
+    return o, lse

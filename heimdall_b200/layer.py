@@ -103,7 +103,60 @@ class BifrostLayer:
         t = x.shape[1]
         if cache is not None and t == 1 and "ring_k" in cache:
             return self._decode(x, q, k, v, qr, kr, int(start), cache, memory)
-        raise NotImplementedError("prefill path not built yet")
+        return self._prefill(x, q, k, v, qr, kr, int(start), cache, memory)
+
+    def _prefill(self, x, q, k, v, qr, kr, start, cache, memory, lse_out=None):
+        B, t = x.shape[:2]
+        H, G, D, W, S = self.H, self.G, self.D, self.window, self.sinks
+        dev = x.device
+        bf = torch.bfloat16
+        xb, qb, kb, vb = (z.to(bf).contiguous() for z in (x, q, k, v))
+        qrb, krb = qr.to(bf).contiguous(), kr.to(bf).contiguous()
+        st = cache if cache is not None else {}
+        # sinks: the first S positions, extended with this call's tokens below S (hibrit.py:369-373)
+        sk, sv = st.get("sink_k"), st.get("sink_v")
+        n_new = max(0, min(t, S - start))
+        if n_new:
+            nk, nv = krb[:, :, :n_new], vb[:, :n_new].transpose(1, 2)
+            sk = nk if sk is None else torch.cat((sk.to(bf), nk), 2)
+            sv = nv if sv is None else torch.cat((sv.to(bf), nv), 2)
+        if sk is not None:
+            sk, sv = sk.to(bf).contiguous(), sv.to(bf).contiguous()
+        ns = 0 if sk is None else sk.shape[2]
+        use_mem = bool(memory) and start + t > W
+        rc = None
+        if cache is not None:
+            if "ring_k" not in cache:
+                cache.update(ring_k=torch.zeros(B, G, W, D, device=dev, dtype=bf),
+                             ring_v=torch.zeros(B, G, W, D, device=dev, dtype=bf),
+                             ring_km=torch.zeros(B, W, G, D, device=dev, dtype=torch.float32),
+                             ring_g=torch.zeros(B, W, G, device=dev, dtype=torch.float32),
+                             ring_beta=torch.zeros(B, W, G, device=dev, dtype=torch.float32),
+                             ring_pos=torch.full((W,), -1, device=dev, dtype=torch.int64))
+            for key, dt in (("ring_k", bf), ("ring_v", bf), ("ring_km", torch.float32), ("ring_g", torch.float32),
+                            ("ring_beta", torch.float32), ("ring_pos", torch.int64)):
+                tns = cache[key]
+                if tns.dtype != dt or not tns.is_contiguous() or tns.device != dev:
+                    cache[key] = tns.to(device=dev, dtype=dt).contiguous()
+            if use_mem:
+                s0 = cache.get("S")
+                if s0 is None:
+                    cache["S"] = torch.zeros(B, G, D, D, device=dev, dtype=torch.float32)
+                elif s0.dtype != torch.float32 or not s0.is_contiguous() or s0.device != dev:
+                    cache["S"] = s0.to(device=dev, dtype=torch.float32).contiguous()
+            Sst = cache["S"] if use_mem else _dummy_state(dev)
+            rc = BfRingCache(ptr(cache["ring_k"]), ptr(cache["ring_v"]), ptr(cache["ring_km"]), ptr(cache["ring_g"]),
+                             ptr(cache["ring_beta"]), ptr(cache["ring_pos"]), 0, 0, 0, 0, ptr(Sst))
+        o = torch.empty(B, t, H, D, device=dev, dtype=torch.float32)
+        ring_case = cache is not None and start > 0
+        nws = _lib.size("bf_layer_prefill_workspace", B, t, H, G, D, W, 1 if ring_case else 0)
+        ws = torch.empty(nws, dtype=torch.uint8, device=dev)
+        _lib.call("bf_bifrost_layer_prefill", ctypes_ref(self._struct), ptr(xb), ptr(qb), ptr(kb), ptr(vb), ptr(qrb),
+                  ptr(krb), start, B, t, 0 if rc is None else ctypes_ref(rc), ptr(sk), ptr(sv), ns,
+                  1 if memory else 0, ptr(o), ptr(lse_out), ptr(ws), nws, stream_handle())
+        if cache is not None:
+            cache["sink_k"], cache["sink_v"] = sk, sv
+        return o
 
     def _decode(self, x, q, k, v, qr, kr, start, cache, memory):
         B = x.shape[0]

@@ -135,6 +135,54 @@ int bf_bifrost_layer_decode(const bf_layer* L, const void* x, const void* q, con
                             const void* qr, const void* kr, const int64_t* pos, int B, bf_ring_cache* cache,
                             int memory, float* o, float* lse, void* ws, size_t ws_bytes, bf_stream_t stream);
 
+/* ------------------------------------------------------------------------------------------
+ * Chunked gated delta rule, forward (prefill), GQA-native.
+ * Replaces heimdall/kernels.py:94-129 (delta_rule_reference, reached through delta_rule at
+ * heimdall/kernels.py:152-155) and heimdall/motor.py:70-102 (delta_rule_gqa).
+ * q [B,T,G*R,D] (q_dtype), k [B,T,G,D] (k_dtype), v [B,T,G,D] (v_dtype): BF_F32 or BF_BF16;
+ * g, beta [B,T,G] fp32; s0 [B,G,D,D] fp32 or NULL (zero state); o [B,T,G*R,D] fp32;
+ * s_out [B,G,D,D] fp32 (may alias s0).  D must be 256.  The GPU scan uses 128-token chunks and
+ * fp16 tensor-core operands with fp32 accumulation and an fp32 state.
+ */
+size_t bf_gdn_chunk_workspace(int B, int T, int G, int R, int D);
+int bf_gdn_chunk_fwd(const void* q, int q_dtype, const void* k, int k_dtype, const void* v, int v_dtype,
+                     const float* g, const float* beta, const float* s0, float* o, float* s_out, int B, int T,
+                     int G, int R, int D, void* ws, size_t ws_bytes, bf_stream_t stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Sliding-window + sink attention with log-sum-exp (fp32 softmax), replacing
+ * heimdall/hibrit.py:336-361 (_window / _window_fp32).
+ * qr [B,H,Tq,D] bf16, query i at position qpos0 + i.  k_ext [B,G,Tk,D] bf16, key j at position
+ * kpos0 + j; v_ext bf16 addressed as v_ext[b*vb + g*vg + j*vj + d] (element strides).  Keys with
+ * position < klo are not window keys (the reference's kp >= sinks rule, and empty ring slots).
+ * sink_k/sink_v [B,G,ns,D] bf16 contiguous, positions 0..ns-1 (ns <= 8), or NULL.
+ * A query at p sees window keys p-window < kp <= p and sinks kp <= p.
+ * o [B,Tq,H,D] fp32; lse [B,H,Tq] fp32 or NULL.  D must be 256.
+ */
+size_t bf_window_workspace(int B, int G, int Tk, int D);
+int bf_window_attn_fwd(const void* qr, const void* k_ext, const void* v_ext, long long vb, long long vg,
+                       long long vj, const void* sink_k, const void* sink_v, int ns, long long qpos0,
+                       long long kpos0, long long klo, int B, int H, int G, int Tq, int Tk, int D, int window,
+                       float* o, float* lse, void* ws, size_t ws_bytes, bf_stream_t stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Fused layer prefill of T new tokens at positions start .. start+T-1, replacing
+ * HybridAttention._student for any t (heimdall/hibrit.py:363-424): memory inputs, the delayed
+ * memory write stream (token j is written at step j + W; earlier steps come from the ring),
+ * the chunked delta rule, the window + sink attention, the LSE gate and mix, and (with a cache)
+ * the ring write of the last min(T, W) tokens and the in-place state update.
+ * x [B,T,d], q [B,T,H,D], k/v [B,T,G,D], qr [B,H,T,D], kr [B,G,T,D]: bf16.
+ * cache: NULL (no cache) or the ring cache (ring_pos shared by the batch, ring_pos_bstride 0; S
+ * must point at a zero state when the cache holds none yet).  The sinks (positions 0..ns-1,
+ * including any of this call's tokens) are passed separately, contiguous [B,G,ns,D] bf16.
+ * memory = 0 is the reference's "window" mode.  o [B,T,H,D] fp32; lse [B,H,T] fp32 or NULL.
+ */
+size_t bf_layer_prefill_workspace(int B, int T, int H, int G, int D, int window, int with_ring);
+int bf_bifrost_layer_prefill(const bf_layer* L, const void* x, const void* q, const void* k, const void* v,
+                             const void* qr, const void* kr, long long start, int B, int T, bf_ring_cache* cache,
+                             const void* sink_k, const void* sink_v, int ns, int memory, float* o, float* lse,
+                             void* ws, size_t ws_bytes, bf_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
