@@ -22,6 +22,7 @@ SIGNATURES = {
     "bf_strerror": [_I],
     "bf_abi_version": [],
     "bf_device_error": [ctypes.POINTER(ctypes.c_uint), _P],
+    "bf_stage_events": [_P, _I],
     "bf_gdn_decode_step": [_P, _P, _P, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
     "bf_layer_weights_bytes": [_I, _I, _I, _I],
     "bf_prepare_layer_weights": [_P, _P, _P, _P, _I, _I, _I, _I, _P, _Z, _P],

@@ -41,6 +41,14 @@ int device_state(DeviceState* st) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// optional per-stage CUDA events (bf_stage_events): recorded on the launching stream around each stage
+static cudaEvent_t g_stage_ev[2 * BF_MAX_STAGES];
+static int g_stage_n = 0;
+
+void stage_mark(int stage, int end, cudaStream_t stream) {
+  if (stage < g_stage_n && g_stage_ev[2 * stage + end]) cudaEventRecord(g_stage_ev[2 * stage + end], stream);
+}
+
 }  // namespace bfb
 
 using namespace bfb;
@@ -76,6 +84,14 @@ int bf_device_error(unsigned int* word, bf_stream_t stream) {
     const unsigned int zero = 0;
     if (cudaMemcpy(st.err, &zero, sizeof(zero), cudaMemcpyHostToDevice) != cudaSuccess) return BF_ERR_CUDA;
   }
+  return BF_OK;
+}
+
+int bf_stage_events(void* const* events, int n_stages) {
+  if (n_stages < 0 || n_stages > BF_MAX_STAGES || (n_stages > 0 && !events)) return BF_ERR_INVALID_ARGUMENT;
+  for (int i = 0; i < 2 * BF_MAX_STAGES; ++i)
+    g_stage_ev[i] = (i < 2 * n_stages) ? static_cast<cudaEvent_t>(events[i]) : nullptr;
+  g_stage_n = n_stages;
   return BF_OK;
 }
 

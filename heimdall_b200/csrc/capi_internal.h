@@ -4,6 +4,7 @@
 #include <stdint.h>
 
 #define BF_ABI_VERSION 1
+#define BF_MAX_STAGES 10
 
 namespace bfb {
 
@@ -14,6 +15,11 @@ struct DeviceState {
 };
 
 int device_state(DeviceState* st);
+
+// per-stage timing hooks (no-ops unless bf_stage_events installed events)
+void stage_mark(int stage, int end, cudaStream_t stream);
+enum Stage { ST_XPROJ = 0, ST_HEADPROJ, ST_GDN_P1, ST_GDN_P2, ST_GDN_P3, ST_WIN_PREP, ST_WIN, ST_CACHE, ST_DEC_STATE,
+             ST_DEC_WIN };
 bool aligned16(const void* p);
 
 int launch_gdn_decode(const float* q, const float* k, const void* v, int v_bf16, const float* g,

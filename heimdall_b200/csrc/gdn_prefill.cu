@@ -197,7 +197,7 @@ __global__ void __launch_bounds__(kP1_Threads, 1) gdn_p1_kernel(GdnStreams s) {
       const int col = t;
       for (int ii = 0; ii < 16; ++ii) {
         const int i = r0 + ii;
-        if (col > i) break;
+        if (col > i) continue;  // rows above this column's diagonal stay zero
         if (col == i) {
           Tm[i * kAS + col] = 1.f;
           continue;
@@ -694,15 +694,19 @@ int launch_gdn_prefill(GdnStreams s, cudaStream_t stream) {
       return BF_ERR_CUDA;
     g_p_attr[0] = true;
   }
+  stage_mark(ST_GDN_P1, 0, stream);
   gdn_p1_kernel<<<dim3(s.n_chunks, s.B * s.G), kP1_Threads, kP1_Smem, stream>>>(s);
   if (cudaGetLastError() != cudaSuccess) return BF_ERR_CUDA;
+  stage_mark(ST_GDN_P1, 1, stream);
   CUtensorMap wmap, ktmap;
   int rc = make_tmap_kmajor(&wmap, s.w, BF_F16, (uint64_t)s.B * s.G * s.n_pad, kGD, kGD, kGC, 4);
   if (rc) return rc;
   rc = make_tmap_kmajor(&ktmap, s.ktT, BF_F16, (uint64_t)s.B * s.G * s.n_chunks * kGD, kGC, kGC, kGD, 2);
   if (rc) return rc;
+  stage_mark(ST_GDN_P2, 0, stream);
   gdn_p2_kernel<<<dim3(kGD / kP2_NB, s.B * s.G), kP2_Threads, kP2_Smem, stream>>>(wmap, ktmap, s);
   if (cudaGetLastError() != cudaSuccess) return BF_ERR_CUDA;
+  stage_mark(ST_GDN_P2, 1, stream);
   // P3 maps: q [B,T,H,D] fp16 as (d, token, atom, head); k/kw; S^T; v'^T
   CUtensorMap qmap, kmap, smap, vmap;
   {
@@ -718,7 +722,9 @@ int launch_gdn_prefill(GdnStreams s, cudaStream_t stream) {
   if (rc) return rc;
   rc = make_tmap_kmajor(&vmap, s.VT, BF_F16, (uint64_t)s.B * s.G * s.n_chunks * kGD, kGC, kGC, 128, 2);
   if (rc) return rc;
+  stage_mark(ST_GDN_P3, 0, stream);
   gdn_p3_kernel<<<dim3(s.n_chunks, H, s.B), kP3_Threads, kP3_Smem, stream>>>(qmap, kmap, smap, vmap, s);
+  stage_mark(ST_GDN_P3, 1, stream);
   return cudaGetLastError() == cudaSuccess ? BF_OK : BF_ERR_CUDA;
 }
 

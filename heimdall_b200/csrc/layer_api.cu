@@ -45,12 +45,17 @@ int check_layer(const bf_layer* L) {
 int mem_inputs_impl(const DeviceState& st, const bf_layer* L, const void* x, const void* q, const void* k,
                     const int64_t* pos, long long pos0, int B, int T, float* qm, float* km, float* g, float* beta,
                     float* mixx, cudaStream_t stream, __half* qm16) {
+  stage_mark(ST_XPROJ, 0, stream);
   int rc = launch_x_proj(static_cast<const __nv_bfloat16*>(x), weights_x(L->wbuf, L->H, L->G, L->D), L->ab_b,
                          L->mix_b, L->A_log, L->dt_bias, L->decay_mask, g, beta, mixx, pos, pos0, B * T, T, L->d,
                          L->G, L->H, L->sinks, st.err, stream);
   if (rc) return rc;
-  return launch_head_proj(static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
-                          weights_heads(L->wbuf), qm, qm16, km, B, T, L->H, L->G, st.sm_count, st.err, stream);
+  stage_mark(ST_XPROJ, 1, stream);
+  stage_mark(ST_HEADPROJ, 0, stream);
+  rc = launch_head_proj(static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
+                        weights_heads(L->wbuf), qm, qm16, km, B, T, L->H, L->G, st.sm_count, st.err, stream);
+  stage_mark(ST_HEADPROJ, 1, stream);
+  return rc;
 }
 
 }  // namespace bfb
@@ -159,8 +164,10 @@ int bf_bifrost_layer_decode(const bf_layer* L, const void* x, const void* q, con
     rc = launch_gather_evicted(C->ring_km, static_cast<const __nv_bfloat16*>(C->ring_v), C->ring_g, C->ring_beta,
                                C->ring_pos, C->ring_pos_bstride, pos, B, G, W, D, k_e, v_e, g_e, b_e, stream);
     if (rc) return rc;
+    stage_mark(ST_DEC_STATE, 0, stream);
     rc = launch_gdn_decode(qm, k_e, v_e, 0, g_e, b_e, C->S, C->S, o_mem, B, G, R, D, stream);
     if (rc) return rc;
+    stage_mark(ST_DEC_STATE, 1, stream);
   }
   WinDecArgs a{};
   a.qr = static_cast<const __nv_bfloat16*>(qr);
@@ -196,7 +203,10 @@ int bf_bifrost_layer_decode(const bf_layer* L, const void* x, const void* q, con
   a.ring_g = C->ring_g;
   a.ring_beta = C->ring_beta;
   a.ring_pos_w = C->ring_pos;
-  return launch_win_dec(a, stream);
+  stage_mark(ST_DEC_WIN, 0, stream);
+  rc = launch_win_dec(a, stream);
+  stage_mark(ST_DEC_WIN, 1, stream);
+  return rc;
 }
 
 }  // extern "C"

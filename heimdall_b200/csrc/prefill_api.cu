@@ -280,6 +280,7 @@ int bf_bifrost_layer_prefill(const bf_layer* L, const void* x, const void* q, co
   }
   // 3. window attention over the extended keys, with the gate and mix fused into its epilogue
   const void* kx = kr;
+  stage_mark(ST_WIN_PREP, 0, stream);
   if (ring_case) {
     rc = launch_kext_prep(static_cast<const __nv_bfloat16*>(kr), static_cast<const __nv_bfloat16*>(C->ring_k), W,
                           start - W, W, B, T, G, kext, stream);
@@ -290,17 +291,22 @@ int bf_bifrost_layer_prefill(const bf_layer* L, const void* x, const void* q, co
                       ring_case ? static_cast<const __nv_bfloat16*>(C->ring_v) : nullptr, ring_case ? W : 0,
                       start - W, W, B, G, Tk, Tkp, vt, stream);
   if (rc) return rc;
+  stage_mark(ST_WIN_PREP, 1, stream);
+  stage_mark(ST_WIN, 0, stream);
   rc = window_common(qr, kx, vt, sink_k, sink_v, ns, start, ring_case ? start - W : start, L->sinks, B, H, G, T, Tk, W,
                      o, lse, use_mem ? o_mem : nullptr, mixx, L->mix_lse, L->mem_scale, st.err, stream);
   if (rc) return rc;
+  stage_mark(ST_WIN, 1, stream);
   // 4. cache: the last min(T, W) tokens go to their ring slots (the state was updated in place)
   if (C) {
+    stage_mark(ST_CACHE, 0, stream);
     const int m = T < W ? T : W;
     ring_write_kernel<<<dim3(m, B * G), 32, 0, stream>>>(
         static_cast<const __nv_bfloat16*>(kr), static_cast<const __nv_bfloat16*>(v), km, g, beta, start, T, m, G, W,
         static_cast<__nv_bfloat16*>(C->ring_k), static_cast<__nv_bfloat16*>(C->ring_v), C->ring_km, C->ring_g,
         C->ring_beta, C->ring_pos);
     if (cudaGetLastError() != cudaSuccess) return BF_ERR_CUDA;
+    stage_mark(ST_CACHE, 1, stream);
   }
   return BF_OK;
 }

@@ -49,6 +49,31 @@ class BifrostLayer:
         self.refresh()
 
     @classmethod
+    def converted(cls, H: int, G: int, D: int, d: int, window: int, sinks: int, archival: int,
+                  mem_init: str = "long", generator=None, device=None) -> "BifrostLayer":
+        """Conversion-time parameters, as ``HybridAttention.convert`` creates them (heimdall/hibrit.py:211-240):
+        fq/fk identities, ab/mix zero with mix bias -2, mix_lse 0, dt log-uniform in [1e-3, 1e-1] with
+        dt_bias = softplus^-1(dt); "long": half-lives log-spaced from the window to 1e6 tokens and
+        mem_scale = sqrt(D); "mamba": A in U[1, 16] and mem_scale 1.  The first ``archival`` KV heads never decay."""
+        import math
+        gen = generator
+        dt = torch.exp(torch.empty(G).uniform_(math.log(1e-3), math.log(1e-1), generator=gen))
+        if mem_init == "mamba":
+            mem_scale = torch.ones(H)
+            A_log = torch.empty(G).uniform_(1.0, 16.0, generator=gen).log()
+        else:
+            mem_scale = torch.full((H,), float(D) ** 0.5)
+            life = torch.logspace(math.log10(max(window, 2)), 6.0, G)
+            A_log = (math.log(2.0) / (life * dt)).log()
+        mask = torch.ones(G)
+        mask[:archival] = 0.0
+        params = dict(fq=torch.eye(D).repeat(H, 1, 1), fk=torch.eye(D).repeat(G, 1, 1), ab_w=torch.zeros(2 * G, d),
+                      ab_b=torch.zeros(2 * G), mix_w=torch.zeros(H, d), mix_b=torch.full((H,), -2.0),
+                      mix_lse=torch.zeros(H), mem_scale=mem_scale, A_log=A_log,
+                      dt_bias=dt + torch.log(-torch.expm1(-dt)), decay_mask=mask)
+        return cls(params, window, sinks, device)
+
+    @classmethod
     def from_module(cls, attn, device=None) -> "BifrostLayer":
         """From a converted reference ``HybridAttention`` (its new parameters and decay_mask buffer)."""
         params = dict(fq=attn.fq, fk=attn.fk, ab_w=attn.ab.weight, ab_b=attn.ab.bias, mix_w=attn.mix.weight,

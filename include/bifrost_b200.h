@@ -55,6 +55,14 @@ int bf_abi_version(void);
  * kernel gave up a wait; otherwise (site << 8) | BF_ERR_TIMEOUT.  Returns BF_OK or BF_ERR_CUDA. */
 int bf_device_error(unsigned int* word, bf_stream_t stream);
 
+/* Per-stage timing: `events` holds 2*n_stages cudaEvent_t handles (begin/end per stage); each
+ * layer entry point records them on its stream around its stages (0 x-projection, 1 head
+ * projection, 2-4 delta-rule phases P1/P2/P3, 5 window key/value prep, 6 window attention,
+ * 7 cache write, 8 decode state update, 9 decode window).  n_stages = 0 turns this off.
+ * Process-wide; not for concurrent use from several threads.  No counterpart in the reference
+ * (its only timing is wall-clock logging, heimdall/motor.py:292-297). */
+int bf_stage_events(void* const* events, int n_stages);
+
 /* ------------------------------------------------------------------------------------------
  * Gated delta rule, recurrent decode step (one token), GQA-native.
  * Replaces heimdall/kernels.py:132-138 (delta_rule_step) and the inline decode update of
