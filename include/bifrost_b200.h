@@ -143,6 +143,19 @@ int bf_bifrost_layer_decode(const bf_layer* L, const void* x, const void* q, con
                             const void* qr, const void* kr, const int64_t* pos, int B, bf_ring_cache* cache,
                             int memory, float* o, float* lse, void* ws, size_t ws_bytes, bf_stream_t stream);
 
+/* The same decode step for callers that cannot allocate device memory (for instance a runtime whose
+ * memory manager has reserved nearly all of HBM for its own pools, or a host that binds only these C
+ * entry points and cannot own a device workspace).  No counterpart in the reference: Heimdall's
+ * decode allocates freely through PyTorch.  It allocates nothing: its scratch is a fixed 16 MiB array
+ * compiled into the library (one per GPU that loads it, held until the process exits), enough for
+ * bf_layer_decode_workspace() of up to 64 sequences of the Bifrost geometry; larger requests return
+ * BF_ERR_WORKSPACE before any launch.  The first call on each device looks the array's device address
+ * up (cudaGetSymbolAddress) and should come before any stream capture.  All calls on a device share
+ * the array, so calls that overlap on the GPU race; nothing in it needs to start at zero. */
+int bf_bifrost_layer_decode_noalloc(const bf_layer* L, const void* x, const void* q, const void* k,
+                                    const void* v, const void* qr, const void* kr, const int64_t* pos, int B,
+                                    bf_ring_cache* cache, int memory, float* o, float* lse, bf_stream_t stream);
+
 /* ------------------------------------------------------------------------------------------
  * Chunked gated delta rule, forward (prefill), GQA-native.
  * Replaces heimdall/kernels.py:94-129 (delta_rule_reference, reached through delta_rule at
