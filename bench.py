@@ -405,6 +405,9 @@ def main(argv=None):
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--T", type=int, default=32768)
     ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--decode-seqs", type=int, default=64)
+    ap.add_argument("--decode-layers", type=int, default=12)
+    ap.add_argument("--decode-steps", type=int, default=256)
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)
@@ -479,7 +482,7 @@ def run_ours(args, ctx):
                                "sample": "512 tokens at positions 30720.. with a full cache (steady-state cost of "
                                          f"the T=32768 prefill), {dt:.1f} s on {cores} threads"}
     if not args.no_decode:
-        out["decode"] = run_decode(dev)
+        out["decode"] = run_decode(dev, steps=args.decode_steps, nseq=args.decode_seqs, nlayers=args.decode_layers)
     print(json.dumps(out), flush=True)
 
 

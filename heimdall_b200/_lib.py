@@ -21,7 +21,7 @@ _L = ctypes.c_longlong
 SIGNATURES = {
     "bf_strerror": [_I],
     "bf_abi_version": [],
-    "bf_device_error": [ctypes.POINTER(ctypes.c_uint), _P],
+    "bf_device_error": [_P, _P],
     "bf_stage_events": [_P, _I],
     "bf_gdn_decode_step": [_P, _P, _P, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
     "bf_layer_weights_bytes": [_I, _I, _I, _I],
@@ -84,10 +84,11 @@ def call(name: str, *args) -> None:
         raise BifrostError(name, rc, strerror(rc))
 
 
-def device_error(stream: int = 0) -> int:
-    w = ctypes.c_uint(0)
-    call("bf_device_error", ctypes.byref(w), stream)
-    return w.value
+def device_error(stream: int = 0):
+    """(word, block_x, block_yz, thread) of the first device-side wait that gave up since the last read."""
+    w = (ctypes.c_uint * 4)()
+    call("bf_device_error", w, stream)
+    return tuple(int(x) for x in w)
 
 
 def declared_symbols() -> list:

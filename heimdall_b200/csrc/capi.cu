@@ -11,7 +11,7 @@
 namespace bfb {
 
 // device error word (one per device context); kernels receive its address as an argument
-__device__ unsigned int g_bf_error_word = 0;
+__device__ unsigned int g_bf_error_word[4] = {0u, 0u, 0u, 0u};
 
 static std::mutex g_dev_mu;
 static unsigned int* g_err_ptr[64] = {nullptr};
@@ -77,12 +77,12 @@ int bf_device_error(unsigned int* word, bf_stream_t stream) {
   int rc = device_state(&st);
   if (rc) return rc;
   if (cudaStreamSynchronize(stream) != cudaSuccess) return BF_ERR_CUDA;
-  unsigned int v = 0;
-  if (cudaMemcpy(&v, st.err, sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess) return BF_ERR_CUDA;
-  *word = v;
-  if (v) {
-    const unsigned int zero = 0;
-    if (cudaMemcpy(st.err, &zero, sizeof(zero), cudaMemcpyHostToDevice) != cudaSuccess) return BF_ERR_CUDA;
+  unsigned int v[4] = {0u, 0u, 0u, 0u};
+  if (cudaMemcpy(v, st.err, sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess) return BF_ERR_CUDA;
+  for (int i = 0; i < 4; ++i) word[i] = v[i];
+  if (v[0]) {
+    const unsigned int zero[4] = {0u, 0u, 0u, 0u};
+    if (cudaMemcpy(st.err, zero, sizeof(zero), cudaMemcpyHostToDevice) != cudaSuccess) return BF_ERR_CUDA;
   }
   return BF_OK;
 }

@@ -25,8 +25,14 @@ namespace bfb {
 // ----------------------------------------------------------------------------------------------
 // device error word: 0 = fine; otherwise (site << 8) | BF_ERR_TIMEOUT.  Set with atomicCAS so the
 // first failure wins; the host reads and clears it after a launch sequence (bf_check_device_error).
+// err points at 4 words: [0] = (site << 8) | BF_ERR_TIMEOUT of the first failure, [1] = blockIdx.x,
+// [2] = blockIdx.y | blockIdx.z << 16, [3] = threadIdx.x of the thread that gave up.
 __device__ __forceinline__ void record_error(unsigned int* err, unsigned int site) {
-  if (err) atomicCAS(err, 0u, (site << 8) | (unsigned)BF_ERR_TIMEOUT);
+  if (err && atomicCAS(err, 0u, (site << 8) | (unsigned)BF_ERR_TIMEOUT) == 0u) {
+    err[1] = blockIdx.x;
+    err[2] = blockIdx.y | (blockIdx.z << 16);
+    err[3] = threadIdx.x;
+  }
 }
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
@@ -35,8 +41,8 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
-// wait limit for any single mbarrier wait: ~1 s of wall time
-constexpr uint64_t kWaitLimitNs = 1000ull * 1000ull * 1000ull;
+// wait limit for any single mbarrier wait: 200 ms of wall time (legitimate waits last microseconds)
+constexpr uint64_t kWaitLimitNs = 200ull * 1000ull * 1000ull;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -86,6 +92,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
       }
     }
   }
+}
+
+// Warp-uniform wait for code that is followed by warp-collective (.sync.aligned) instructions: every lane
+// waits, then the warp agrees, so either all lanes go on or all lanes unwind together.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort, unsigned int* err,
+                                               unsigned int site) {
+  const bool ok = mbar_wait(bar, parity, abort, err, site);
+  return __all_sync(0xffffffffu, ok) != 0;
 }
 
 // ----------------------------------------------------------------------------------------------

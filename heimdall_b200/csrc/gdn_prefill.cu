@@ -76,8 +76,8 @@ constexpr int kP1_Threads = 256;
 constexpr int kP1_Reg0 = 0;                 // k tile (64 KB) -> T fp32 -> (beta v)^T (64 KB)
 constexpr int kP1_Reg1 = 69632;             // A fp32 (67.6 KB) -> (beta e^c k)^T (64 KB)
 constexpr int kP1_RegW = 69632 * 2;         // T fp16 (32 KB)
-constexpr int kP1_Small = kP1_RegW + 32768; // gc/g/beta (3 x 512 B) + barriers
-constexpr int kP1_Smem = kP1_Small + 2048 + 1024;
+constexpr int kP1_Small = kP1_RegW + 32768; // gc/g/beta (3 x 512 B) + barriers + row pointers (3 KB)
+constexpr int kP1_Smem = kP1_Small + 2048 + 3072 + 1024;
 constexpr int kAS = 132;                    // row stride (floats) of A and T in shared memory
 
 __global__ void __launch_bounds__(kP1_Threads, 1) gdn_p1_kernel(GdnStreams s) {
@@ -93,6 +93,9 @@ __global__ void __launch_bounds__(kP1_Threads, 1) gdn_p1_kernel(GdnStreams s) {
   uint64_t* bar_kk = bars + 0;
   uint64_t* bar_uw = bars + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2);
+  const float** s_kp = reinterpret_cast<const float**>(smem + kP1_Small + 2048);   // [128] key row (or null)
+  const __nv_bfloat16** s_vp = reinterpret_cast<const __nv_bfloat16**>(s_kp + 128);  // [128] bf16 value row
+  const float** s_vp32 = reinterpret_cast<const float**>(s_vp + 128);             // [128] fp32 value row
   float* A = reinterpret_cast<float*>(reg1);   // [128][kAS]
   float* Tm = reinterpret_cast<float*>(reg0);  // [128][kAS]
 
@@ -116,6 +119,9 @@ __global__ void __launch_bounds__(kP1_Threads, 1) gdn_p1_kernel(GdnStreams s) {
     if (hh == 0) {
       s_g[r] = src.zero ? 0.f : src.g;
       s_beta[r] = src.zero ? 0.f : src.beta;
+      s_kp[r] = src.zero ? nullptr : src.k;
+      s_vp[r] = src.zero ? nullptr : src.v;
+      s_vp32[r] = src.zero ? nullptr : src.v32;
     }
     __half* kwrow = s.kw + (rowbase + r) * kGD + hh * 128;
 #pragma unroll 4
@@ -162,7 +168,7 @@ __global__ void __launch_bounds__(kP1_Threads, 1) gdn_p1_kernel(GdnStreams s) {
   bool alive = true;
   if (warp < 4) {
     const int r = t;
-    alive = mbar_wait(bar_kk, 0, nullptr, s.err, 0x41);
+    alive = mbar_wait_warp(bar_kk, 0, nullptr, s.err, 0x41);
     tc_fence_after();
     const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
     const float br = s_beta[r], cr = s_gc[r];
@@ -219,41 +225,36 @@ __global__ void __launch_bounds__(kP1_Threads, 1) gdn_p1_kernel(GdnStreams s) {
   }
   __syncthreads();  // Tm (reg0) and A (reg1) are free now
   // ---- (d) B operands: (beta v)^T -> reg0, (beta e^c k)^T -> reg1 ([256 dims][128 tokens] K-major);
-  //      and k_tail^T = (e^{c_C - c} k)^T to global (P2's A operand)
+  //      and k_tail^T = (e^{c_C - c} k)^T to global (P2's A operand).  Thread t owns dimension t and builds
+  //      16-byte chunks of 8 tokens, so shared and global stores are vector-wide and loads coalesce over t.
   {
-    const int r = t >> 1, hh = t & 1;
-    const RowSrc src = write_row(s, b, gg, c * kGC + r);
-    const float br = s_beta[r], ec = __expf(s_gc[r]), et = __expf(gamma_last - s_gc[r]);
-    __half* ktT = s.ktT + ((size_t)bg * s.n_chunks + c) * kGD * kGC;
-    for (int d0 = hh * 128; d0 < hh * 128 + 128; d0 += 8) {
-      float kx[8], vx[8];
-      if (src.zero) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) kx[e] = vx[e] = 0.f;
-      } else {
-        const float4 a0 = *reinterpret_cast<const float4*>(src.k + d0);
-        const float4 a1 = *reinterpret_cast<const float4*>(src.k + d0 + 4);
-        kx[0] = a0.x; kx[1] = a0.y; kx[2] = a0.z; kx[3] = a0.w; kx[4] = a1.x; kx[5] = a1.y; kx[6] = a1.z; kx[7] = a1.w;
-        if (src.v32) {
-          const float4 b0 = *reinterpret_cast<const float4*>(src.v32 + d0);
-          const float4 b1 = *reinterpret_cast<const float4*>(src.v32 + d0 + 4);
-          vx[0] = b0.x; vx[1] = b0.y; vx[2] = b0.z; vx[3] = b0.w; vx[4] = b1.x; vx[5] = b1.y; vx[6] = b1.z; vx[7] = b1.w;
-        } else {
-          const uint4 vv = *reinterpret_cast<const uint4*>(src.v + d0);
-          const uint32_t vw[4] = {vv.x, vv.y, vv.z, vv.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            vx[2 * e] = __uint_as_float(vw[e] << 16);
-            vx[2 * e + 1] = __uint_as_float(vw[e] & 0xffff0000u);
-          }
-        }
-      }
+    const int d = t;
+    __half* ktT = s.ktT + ((size_t)bg * s.n_chunks + c) * kGD * kGC + (size_t)d * kGC;
+#pragma unroll 1
+    for (int r0 = 0; r0 < kGC; r0 += 8) {
+      float kv[8], vv[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        st_half_sw128(reg0, 256, d0 + e, r, br * vx[e]);
-        st_half_sw128(reg1, 256, d0 + e, r, br * ec * kx[e]);
-        ktT[(size_t)(d0 + e) * kGC + r] = __float2half_rn(kx[e] * et);
+        const int r = r0 + e;
+        const float* kp = s_kp[r];
+        kv[e] = kp ? kp[d] : 0.f;
+        if (s_vp32[r]) vv[e] = s_vp32[r][d];
+        else vv[e] = s_vp[r] ? __bfloat162float(s_vp[r][d]) : 0.f;
       }
+      uint32_t pv[4], pk[4], pt[4];
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        const int r = r0 + e;
+        const float b0 = s_beta[r], b1 = s_beta[r + 1];
+        const float g0 = s_gc[r], g1 = s_gc[r + 1];
+        pv[e / 2] = pack_half2(b0 * vv[e], b1 * vv[e + 1]);
+        pk[e / 2] = pack_half2(b0 * __expf(g0) * kv[e], b1 * __expf(g1) * kv[e + 1]);
+        pt[e / 2] = pack_half2(__expf(gamma_last - g0) * kv[e], __expf(gamma_last - g1) * kv[e + 1]);
+      }
+      const uint32_t off = (uint32_t)(r0 >> 6) * (256 * 128) + sw128_offset(d, r0 & 63);
+      *reinterpret_cast<uint4*>(reg0 + off) = make_uint4(pv[0], pv[1], pv[2], pv[3]);
+      *reinterpret_cast<uint4*>(reg1 + off) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      *reinterpret_cast<uint4*>(ktT + r0) = make_uint4(pt[0], pt[1], pt[2], pt[3]);
     }
   }
   fence_async_smem();
@@ -274,7 +275,7 @@ __global__ void __launch_bounds__(kP1_Threads, 1) gdn_p1_kernel(GdnStreams s) {
   // ---- (e) u, w rows -> fp16 global (warps 0-3)
   if (warp < 4) {
     const int r = t;
-    alive = mbar_wait(bar_uw, 0, nullptr, s.err, 0x42) && alive;
+    alive = mbar_wait_warp(bar_uw, 0, nullptr, s.err, 0x42) && alive;
     tc_fence_after();
     const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
     __half* urow = s.u + (rowbase + r) * kGD;
@@ -443,7 +444,7 @@ __global__ void __launch_bounds__(kP2_Threads, 1)
           uu[2 * e + 1] = f2.y;
         }
       }
-      if (!mbar_wait(bar_m1, c & 1, abort_flag, s.err, 0x59)) { alive = false; break; }
+      if (!mbar_wait_warp(bar_m1, c & 1, abort_flag, s.err, 0x59)) { alive = false; break; }
       tc_fence_after();
       float dv[kP2_NB];
       tmem_ld16_wait(trow, dv);
@@ -458,7 +459,7 @@ __global__ void __launch_bounds__(kP2_Threads, 1)
       tc_fence_before();
       mbar_arrive(bar_vt);
       const float decay = __expf(s.gc[(size_t)bg * s.n_pad + (size_t)c * kGC + kGC - 1]);
-      if (!mbar_wait(bar_m2, c & 1, abort_flag, s.err, 0x5a)) { alive = false; break; }
+      if (!mbar_wait_warp(bar_m2, c & 1, abort_flag, s.err, 0x5a)) { alive = false; break; }
       tc_fence_after();
       float d0[kP2_NB], d1[kP2_NB];
       tmem_ld16_wait(trow + kP2_NB, d0);
@@ -597,7 +598,7 @@ __global__ void __launch_bounds__(kP3_Threads, 1)
     const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
     const float* gcc = s.gc + (size_t)bg * s.n_pad + (size_t)c * kGC;
     const float ci = gcc[r];
-    bool alive = mbar_wait(bar_qkd, 0, abort_flag, s.err, 0x6b);
+    bool alive = mbar_wait_warp(bar_qkd, 0, abort_flag, s.err, 0x6b);
     if (alive) {
       tc_fence_after();
 #pragma unroll 1
@@ -626,7 +627,7 @@ __global__ void __launch_bounds__(kP3_Threads, 1)
     const float eci = __expf(ci);
     float* orow = s.o + (((size_t)b * s.T + s.qoff + step) * H + h) * kGD;
     for (int half = 0; half < 2 && alive; ++half) {
-      alive = mbar_wait(bar_o, half & 1, abort_flag, s.err, 0x6c);
+      alive = mbar_wait_warp(bar_o, half & 1, abort_flag, s.err, 0x6c);
       if (!alive) break;
       tc_fence_after();
 #pragma unroll 1

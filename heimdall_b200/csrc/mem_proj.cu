@@ -64,7 +64,8 @@ struct HeadProjArgs {
 };
 
 __global__ void __launch_bounds__(kHP_Threads, 1)
-    head_proj_kernel(const __grid_constant__ CUtensorMap wmap, HeadProjArgs a) {
+    head_proj_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap qmap,
+                     const __grid_constant__ CUtensorMap kmap, HeadProjArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -74,16 +75,17 @@ __global__ void __launch_bounds__(kHP_Threads, 1)
   uint64_t* bar_mma = bars + 1;    // MMA finished reading A
   uint64_t* bar_full = bars + 2;   // [2] accumulator ready
   uint64_t* bar_free = bars + 4;   // [2] accumulator drained (128 arrivals)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 6);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 7);
+  uint64_t* bar_a = bars + 6;      // A tile landed (TMA)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 7);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 8);
 
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tid = threadIdx.x, warp = tid >> 5;
   const int head = blockIdx.y;     // 0..H+G-1
   const int b = blockIdx.z;
   const bool is_q = head < a.H;
   const int nheads_src = is_q ? a.H : a.G;
   const int hsrc = is_q ? head : head - a.H;
-  const __nv_bfloat16* src = is_q ? a.q : a.k;
+  const CUtensorMap* amap = is_q ? &qmap : &kmap;
   float* dst = is_q ? a.qm : a.km;
   const float out_scale = is_q ? rsqrtf((float)kHP_D) : 1.f;
   const int ntiles = (a.T + kHP_M - 1) / kHP_M;
@@ -97,6 +99,7 @@ __global__ void __launch_bounds__(kHP_Threads, 1)
     mbar_init(&bar_full[1], 1);
     mbar_init(&bar_free[0], 128);
     mbar_init(&bar_free[1], 128);
+    mbar_init(bar_a, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -110,38 +113,32 @@ __global__ void __launch_bounds__(kHP_Threads, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp >= 4) {
-    // ---------------------------------------------------------------- staging + MMA issue
-    const int st = tid - 128;  // 0..127: one row each
+    // ---------------------------------------------------------------- A tiles (TMA, bf16 -> fp16 in place) + MMA issue
+    const int st = tid - 128;  // 0..127
     if (st == 0) {
       tma_prefetch(&wmap);
+      tma_prefetch(amap);
       mbar_expect_tx(bar_b, kHP_SmemB);
       tma_load_3d(sB, &wmap, bar_b, 0, head * kHP_D, 0);
+      if (tile0 < tile1) {
+        mbar_expect_tx(bar_a, kHP_SmemA);
+        tma_load_4d(sA, amap, bar_a, 0, b * a.T + tile0 * kHP_M, 0, hsrc);
+      }
     }
+    int loaded = tile0 < tile1 ? 1 : 0;
     for (int it = tile0; it < tile1; ++it) {
       const int i = it - tile0;
-      if (i > 0 && !mbar_wait(bar_mma, (i - 1) & 1, abort_flag, a.err, 0x11)) break;
-      // row st of this tile: 256 bf16 -> fp16, 16-byte chunks into the SW128 layout
-      const int t = it * kHP_M + st;
-      if (t < a.T) {
-        const uint4* rp = reinterpret_cast<const uint4*>(src + (((size_t)b * a.T + t) * nheads_src + hsrc) * kHP_D);
+      if (!mbar_wait(bar_a, i & 1, abort_flag, a.err, 0x11)) break;
+      // convert this thread's 4 x 128-byte slice of the tile in place (same swizzled positions)
 #pragma unroll 4
-        for (int c = 0; c < 32; ++c) {  // 32 chunks of 8 elements
-          uint4 u = rp[c];
-          uint32_t w[4] = {u.x, u.y, u.z, u.w};
+      for (int c = 0; c < 32; ++c) {
+        uint4* pch = reinterpret_cast<uint4*>(sA + (size_t)(c * 128 + st) * 16);
+        uint4 u = *pch;
+        uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float lo = __uint_as_float(w[j] << 16), hi = __uint_as_float(w[j] & 0xffff0000u);
-            w[j] = pack_half2(lo, hi);
-          }
-          const int atom = c >> 3, col = (c & 7) * 8;
-          *reinterpret_cast<uint4*>(sA + atom * (kHP_M * 128) + sw128_offset(st, col)) = make_uint4(w[0], w[1], w[2], w[3]);
-        }
-      } else {
-#pragma unroll 4
-        for (int c = 0; c < 32; ++c) {
-          const int atom = c >> 3, col = (c & 7) * 8;
-          *reinterpret_cast<uint4*>(sA + atom * (kHP_M * 128) + sw128_offset(st, col)) = make_uint4(0, 0, 0, 0);
-        }
+        for (int j = 0; j < 4; ++j)
+          w[j] = pack_half2(__uint_as_float(w[j] << 16), __uint_as_float(w[j] & 0xffff0000u));
+        *pch = make_uint4(w[0], w[1], w[2], w[3]);
       }
       fence_async_smem();
       asm volatile("bar.sync 1, 128;" ::: "memory");
@@ -161,17 +158,26 @@ __global__ void __launch_bounds__(kHP_Threads, 1)
             umma_f16_ss(d, sdesc_kstep(aB, kHP_M, ks), sdesc_kstep(bB, kHP_D, ks), idesc, ks > 0);
           umma_commit(bar_mma);
           umma_commit(&bar_full[buf]);
+          // the next A tile may land once the tensor core has read this one
+          if (it + 1 < tile1 && mbar_wait(bar_mma, i & 1, abort_flag, a.err, 0x16)) {
+            mbar_expect_tx(bar_a, kHP_SmemA);
+            tma_load_4d(sA, amap, bar_a, 0, b * a.T + (it + 1) * kHP_M, 0, hsrc);
+            ++loaded;
+          }
         }
       }
     }
-    // drain: the weights TMA must have landed before the CTA may exit
-    if (st == 0) mbar_wait(bar_b, 0, nullptr, a.err, 0x14);
+    // drain: every TMA issued must have landed before the CTA may exit
+    if (st == 0) {
+      mbar_wait(bar_b, 0, nullptr, a.err, 0x14);
+      if (loaded > 0) mbar_wait(bar_a, (loaded - 1) & 1, nullptr, a.err, 0x17);
+    }
   } else {
     // ---------------------------------------------------------------- epilogue: one row per thread
     const int row = tid;  // TMEM lane
     for (int it = tile0; it < tile1; ++it) {
       const int i = it - tile0, buf = i & 1;
-      if (!mbar_wait(&bar_full[buf], (i >> 1) & 1, abort_flag, a.err, 0x15)) break;
+      if (!mbar_wait_warp(&bar_full[buf], (i >> 1) & 1, abort_flag, a.err, 0x15)) break;
       tc_fence_after();
       const uint32_t base = tmem + ((uint32_t)(warp * 32) << 16) + buf * 256;
       float ss = 0.f;
@@ -321,7 +327,7 @@ __global__ void __launch_bounds__(192, 1)
     // epilogue warps 2..5 -> TMEM lane quarter (warp % 4)
     const int q4 = warp & 3;
     const int row = q4 * 32 + (tid & 31);
-    if (mbar_wait(done, 0, abort_flag, a.err, 0x24)) {
+    if (mbar_wait_warp(done, 0, abort_flag, a.err, 0x24)) {
       tc_fence_after();
       uint32_t ra[32], rb[32];  // columns 0..31: x*hi, 32..63: x*lo
       const uint32_t base = tmem + ((uint32_t)(q4 * 32) << 16);
@@ -368,9 +374,19 @@ int launch_prep_weights(const float* fq, const float* fk, const float* ab_w, con
 
 int launch_head_proj(const __nv_bfloat16* q, const __nv_bfloat16* k, const __half* w_heads, float* qm, __half* qm16,
                      float* km, int B, int T, int H, int G, int sm_count, unsigned int* err, cudaStream_t stream) {
-  CUtensorMap wmap;
+  CUtensorMap wmap, qmap, kmap;
   int rc = make_tmap_kmajor(&wmap, w_heads, BF_F16, (uint64_t)(H + G) * kHP_D, kHP_D, kHP_D, kHP_D, 4);
   if (rc) return rc;
+  // q [B,T,H,D] / k [B,T,G,D] bf16 as (d, token, atom, head): one 128-token x 256 tile of one head per TMA
+  for (int which = 0; which < 2; ++which) {
+    const int nh = which == 0 ? H : G;
+    const uint64_t dims[4] = {64, (uint64_t)B * T, 4, (uint64_t)nh};
+    const uint64_t strides[3] = {(uint64_t)nh * kHP_D * 2, 128, (uint64_t)kHP_D * 2};
+    const uint32_t box[4] = {64, (uint32_t)kHP_M, 4, 1};
+    rc = make_tmap(which == 0 ? &qmap : &kmap, which == 0 ? (const void*)q : (const void*)k, BF_BF16, 4, dims, strides,
+                   box, true);
+    if (rc) return rc;
+  }
   static bool attr = false;
   if (!attr) {
     if (cudaFuncSetAttribute(head_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kHP_Smem) != cudaSuccess)
@@ -384,7 +400,7 @@ int launch_head_proj(const __nv_bfloat16* q, const __nv_bfloat16* k, const __hal
   per = per < 1 ? 1 : (per > ntiles ? ntiles : per);
   HeadProjArgs a{q, k, qm, qm16, km, B, T, H, G, per, err};
   dim3 grid((ntiles + per - 1) / per, H + G, B);
-  head_proj_kernel<<<grid, kHP_Threads, kHP_Smem, stream>>>(wmap, a);
+  head_proj_kernel<<<grid, kHP_Threads, kHP_Smem, stream>>>(wmap, qmap, kmap, a);
   return cudaGetLastError() == cudaSuccess ? BF_OK : BF_ERR_CUDA;
 }
 

@@ -9,17 +9,19 @@
 // kpos0 + j; positions below `klo` are not valid window keys).  K is bf16 [B,G,Tk,D]; V is pre-transposed
 // to fp16 [B,G,D,Tkp] so that both MMA operands are K-major.
 //
-// CTA = (128-query tile, query head, batch).  Warp roles (224 threads):
-//   warp 0: TMA producer of Q and K tiles;   warp 6: TMA producer of V tiles;
-//   warp 1: MMA issuer (one elected thread): S = Q K^T (bf16, M128 N128 K256) into a double-buffered TMEM
-//           score tile, then O += P V (fp16, M128 N256 K128) into a TMEM accumulator;
-//   warps 2-5: softmax / epilogue, one thread per query row (= TMEM lane): online softmax with lazy
-//           rescaling (O is rescaled in TMEM only when the running max grows by more than e^8, so P stays
-//           within fp16 range), fp16 P written to shared memory in the 128-byte-swizzled K-major layout.
+// CTA = (128-query tile, query head, batch), key tiles of 64.  Warp roles (224 threads):
+//   warp 0: TMA producer of Q and K tiles (two K stages);  warp 6: TMA producer of V^T tiles (two stages);
+//   warp 1: MMA issuer (one thread): S_j = Q K_j^T (bf16, M128 N64 K256) into one of two TMEM score
+//           buffers, then O += P_j V_j (fp16, M128 N256 K64) into the TMEM accumulator; S_{j+1} is issued
+//           before O += P_j V_j so the tensor core works while the softmax warps work;
+//   warps 2-5: softmax / epilogue, one thread per query row (= TMEM lane), scores in the log2 domain
+//           (one FFMA + ex2 per score), tree reductions, fp16 P into one of two shared buffers.  O is
+//           rescaled in TMEM only when the running max grows by more than 2^8, so P stays within fp16 range
+//           and the softmax of tile j waits for the product of tile j-1 only in that rare case.
 //   Epilogue: the sink keys (<= 8) are folded in exactly in fp32 per row, then o / lse are written, or the
 //   gate and mix with the memory read are applied and the layer output is written.
-// TMEM: S buffers at columns 0 and 128, O at columns 256..511.
-// Shared memory: Q 64 KB, K 64 KB, V 64 KB, P 32 KB.
+// TMEM: score buffers at columns 0 and 64, O at columns 256..511.
+// Shared memory: Q 64 KB, K 2 x 32 KB, V^T 2 x 32 KB, P 2 x 16 KB.
 #include "capi_internal.h"
 #include "common.cuh"
 #include "tmap.h"
@@ -28,15 +30,23 @@
 namespace bfb {
 
 constexpr int kWP_M = 128;       // queries per tile
-constexpr int kWP_N = 128;       // keys per tile
+constexpr int kWP_N = 64;        // keys per tile
 constexpr int kWP_D = 256;
 constexpr int kWP_Threads = 224;
-constexpr int kWP_SmemQ = kWP_M * kWP_D * 2;
-constexpr int kWP_SmemK = kWP_N * kWP_D * 2;
-constexpr int kWP_SmemV = kWP_D * kWP_N * 2;
-constexpr int kWP_SmemP = kWP_M * kWP_N * 2;
-constexpr int kWP_Smem = kWP_SmemQ + kWP_SmemK + kWP_SmemV + kWP_SmemP + 1024 + 256;
-constexpr float kRescaleThresh = 8.0f;  // natural-log units
+constexpr int kWP_SmemQ = kWP_M * kWP_D * 2;      // 64 KB
+constexpr int kWP_SmemK = kWP_N * kWP_D * 2;      // 32 KB per stage
+constexpr int kWP_SmemV = kWP_D * kWP_N * 2;      // 32 KB per stage
+constexpr int kWP_SmemP = kWP_M * kWP_N * 2;      // 16 KB per stage
+constexpr int kWP_Smem = kWP_SmemQ + 2 * (kWP_SmemK + kWP_SmemV + kWP_SmemP) + 1024 + 256;
+constexpr float kRescaleLog2 = 8.0f;              // rescale O when the max grows by more than 2^8
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
@@ -55,20 +65,20 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
-  uint8_t* sK = sQ + kWP_SmemQ;
-  uint8_t* sV = sK + kWP_SmemK;
-  uint8_t* sP = sV + kWP_SmemV;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kWP_SmemP);
+  uint8_t* sK = sQ + kWP_SmemQ;            // [2]
+  uint8_t* sV = sK + 2 * kWP_SmemK;        // [2]
+  uint8_t* sP = sV + 2 * kWP_SmemV;        // [2]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kWP_SmemP);
   uint64_t* bar_q = bars + 0;
-  uint64_t* bar_k_full = bars + 1;
-  uint64_t* bar_k_empty = bars + 2;
-  uint64_t* bar_v_full = bars + 3;
-  uint64_t* bar_pv = bars + 4;       // PV_j finished (O stable, P and V buffers free)
-  uint64_t* bar_s_full = bars + 5;   // [2]
-  uint64_t* bar_s_free = bars + 7;   // [2] (128 arrivals)
-  uint64_t* bar_p_full = bars + 9;   // (128 arrivals)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 11);
+  uint64_t* k_full = bars + 1;     // [2]
+  uint64_t* k_empty = bars + 3;    // [2] S_j = Q K_j^T finished (K stage and nothing else)
+  uint64_t* v_full = bars + 5;     // [2]
+  uint64_t* v_empty = bars + 7;    // [2] O += P_j V_j finished (V stage and P buffer free, O stable)
+  uint64_t* s_full = bars + 9;     // [2]
+  uint64_t* s_free = bars + 11;    // [2] (128 arrivals)
+  uint64_t* p_full = bars + 13;    // [2] (128 arrivals)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 16);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int i0 = blockIdx.x * kWP_M;
@@ -87,7 +97,7 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
   }
 
   if (tid == 0) {
-    for (int i = 0; i < 10; ++i) mbar_init(bars + i, (i == 7 || i == 8 || i == 9) ? 128 : 1);
+    for (int i = 0; i < 15; ++i) mbar_init(bars + i, (i >= 11) ? 128 : 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -108,54 +118,59 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
       tma_load_3d(sQ, &qmap, bar_q, 0, (b * a.H + h) * a.Tq + i0, 0);
       int issued = 0;
       for (int j = 0; j < n; ++j) {
-        if (j >= 1 && !mbar_wait(bar_k_empty, (j - 1) & 1, abort_flag, a.err, 0x31)) break;
-        mbar_expect_tx(bar_k_full, kWP_SmemK);
-        tma_load_3d(sK, &kmap, bar_k_full, 0, (b * a.G + g) * a.Tk + (jt0 + j) * kWP_N, 0);
+        const int s = j & 1;
+        if (j >= 2 && !mbar_wait(&k_empty[s], ((j >> 1) - 1) & 1, abort_flag, a.err, 0x31)) break;
+        mbar_expect_tx(&k_full[s], kWP_SmemK);
+        tma_load_3d(sK + s * kWP_SmemK, &kmap, &k_full[s], 0, (b * a.G + g) * a.Tk + (jt0 + j) * kWP_N, 0);
         issued = j + 1;
       }
       // drain our copies before the CTA can exit
       mbar_wait(bar_q, 0, nullptr, a.err, 0x32);
-      if (issued > 0) mbar_wait(bar_k_full, (issued - 1) & 1, nullptr, a.err, 0x33);
+      for (int j = max(0, issued - 2); j < issued; ++j) mbar_wait(&k_full[j & 1], (j >> 1) & 1, nullptr, a.err, 0x33);
     }
   } else if (warp == 6) {
     if (lane == 0) {
       tma_prefetch(&vmap);
       int issued = 0;
       for (int j = 0; j < n; ++j) {
-        if (j >= 1 && !mbar_wait(bar_pv, (j - 1) & 1, abort_flag, a.err, 0x34)) break;
-        mbar_expect_tx(bar_v_full, kWP_SmemV);
-        tma_load_3d(sV, &vmap, bar_v_full, 0, (b * a.G + g) * kWP_D, ((jt0 + j) * kWP_N) / 64);
+        const int s = j & 1;
+        if (j >= 2 && !mbar_wait(&v_empty[s], ((j >> 1) - 1) & 1, abort_flag, a.err, 0x34)) break;
+        mbar_expect_tx(&v_full[s], kWP_SmemV);
+        tma_load_3d(sV + s * kWP_SmemV, &vmap, &v_full[s], 0, (b * a.G + g) * kWP_D, jt0 + j);
         issued = j + 1;
       }
-      if (issued > 0) mbar_wait(bar_v_full, (issued - 1) & 1, nullptr, a.err, 0x35);
+      for (int j = max(0, issued - 2); j < issued; ++j) mbar_wait(&v_full[j & 1], (j >> 1) & 1, nullptr, a.err, 0x35);
     }
   } else if (warp == 1) {
     if (lane == 0 && n > 0) {
       constexpr uint32_t idesc_qk = idesc_f16(kWP_M, kWP_N, 1);
       constexpr uint32_t idesc_pv = idesc_f16(kWP_M, kWP_D, 0);
-      const uint32_t aQ = smem_u32(sQ), bK = smem_u32(sK), aP = smem_u32(sP), bV = smem_u32(sV);
+      const uint32_t aQ = smem_u32(sQ), bK0 = smem_u32(sK), aP0 = smem_u32(sP), bV0 = smem_u32(sV);
       bool ok = mbar_wait(bar_q, 0, abort_flag, a.err, 0x36);
       auto issue_pv = [&](int jj) -> bool {
-        if (!mbar_wait(bar_p_full, jj & 1, abort_flag, a.err, 0x37)) return false;
-        if (!mbar_wait(bar_v_full, jj & 1, abort_flag, a.err, 0x38)) return false;
+        const int s = jj & 1;
+        if (!mbar_wait(&p_full[s], (jj >> 1) & 1, abort_flag, a.err, 0x37)) return false;
+        if (!mbar_wait(&v_full[s], (jj >> 1) & 1, abort_flag, a.err, 0x38)) return false;
         tc_fence_after();
+        const uint32_t aP = aP0 + s * kWP_SmemP, bV = bV0 + s * kWP_SmemV;
 #pragma unroll
         for (int ks = 0; ks < kWP_N / 16; ++ks)
-          umma_f16_ss(tmem + 256, sdesc_kstep(aP, kWP_M, ks), sdesc_kstep(bV, kWP_D, ks), idesc_pv, (jj | ks) > 0);
-        umma_commit(bar_pv);
+          umma_f16_ss(tmem + 256, sdesc_sw128(aP + ks * 32), sdesc_sw128(bV + ks * 32), idesc_pv, (jj | ks) > 0);
+        umma_commit(&v_empty[s]);
         return true;
       };
       for (int j = 0; j < n && ok; ++j) {
-        const int buf = j & 1;
-        ok = mbar_wait(bar_k_full, j & 1, abort_flag, a.err, 0x39);
-        if (ok && j >= 2) ok = mbar_wait(&bar_s_free[buf], ((j >> 1) - 1) & 1, abort_flag, a.err, 0x3a);
+        const int s = j & 1;
+        ok = mbar_wait(&k_full[s], (j >> 1) & 1, abort_flag, a.err, 0x39);
+        if (ok && j >= 2) ok = mbar_wait(&s_free[s], ((j >> 1) - 1) & 1, abort_flag, a.err, 0x3a);
         if (!ok) break;
         tc_fence_after();
+        const uint32_t bK = bK0 + s * kWP_SmemK;
 #pragma unroll
         for (int ks = 0; ks < kWP_D / 16; ++ks)
-          umma_f16_ss(tmem + buf * 128, sdesc_kstep(aQ, kWP_M, ks), sdesc_kstep(bK, kWP_N, ks), idesc_qk, ks > 0);
-        umma_commit(bar_k_empty);
-        umma_commit(&bar_s_full[buf]);
+          umma_f16_ss(tmem + s * kWP_N, sdesc_kstep(aQ, kWP_M, ks), sdesc_kstep(bK, kWP_N, ks), idesc_qk, ks > 0);
+        umma_commit(&k_empty[s]);
+        umma_commit(&s_full[s]);
         if (j >= 1) ok = issue_pv(j - 1);
       }
       if (ok) issue_pv(n - 1);
@@ -167,92 +182,108 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
     const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
     const long long p = P0 + r;                  // position of this query
     const float scale = rsqrtf((float)kWP_D);
-    float m_ref = -INFINITY, l = 0.f;
+    const float c2 = scale * kLog2e;             // score -> log2 domain
+    float m_ref = -INFINITY, l = 0.f;            // running max (log2 domain) and sum
     bool alive = true;
     for (int j = 0; j < n && alive; ++j) {
-      const int buf = j & 1;
-      if (!mbar_wait(&bar_s_full[buf], (j >> 1) & 1, abort_flag, a.err, 0x3b)) { alive = false; break; }
+      const int s = j & 1;
+      if (!mbar_wait_warp(&s_full[s], (j >> 1) & 1, abort_flag, a.err, 0x3b)) { alive = false; break; }
       tc_fence_after();
-      float s[kWP_N];
-#pragma unroll
-      for (int c = 0; c < kWP_N; c += 32) {
-        uint32_t u[32];
-        tmem_ld32(trow + buf * 128 + c, u);
+      float u[kWP_N];
+      {
+        uint32_t w0[32], w1[32];
+        tmem_ld32(trow + s * kWP_N, w0);
+        tmem_ld32(trow + s * kWP_N + 32, w1);
         tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 32; ++e) s[c + e] = __uint_as_float(u[e]) * scale;
-      }
-      tc_fence_before();
-      mbar_arrive(&bar_s_free[buf]);
-      // mask: key position kp = kpos0 + (jt0 + j) * 128 + c
-      const long long kt = a.kpos0 + (long long)(jt0 + j) * kWP_N;
-      const bool full = kt >= a.klo && kt + kWP_N - 1 <= P0 && (Plast - kt) < a.W;
-      float mt = -INFINITY;
-      if (full) {
-#pragma unroll
-        for (int c = 0; c < kWP_N; ++c) mt = fmaxf(mt, s[c]);
-      } else {
-#pragma unroll
-        for (int c = 0; c < kWP_N; ++c) {
-          const long long kp = kt + c;
-          const bool ok = kp >= a.klo && kp <= p && (p - kp) < a.W;
-          s[c] = ok ? s[c] : -INFINITY;
-          mt = fmaxf(mt, s[c]);
+        for (int e = 0; e < 32; ++e) {
+          u[e] = __uint_as_float(w0[e]);
+          u[32 + e] = __uint_as_float(w1[e]);
         }
       }
+      tc_fence_before();
+      mbar_arrive(&s_free[s]);
+      // mask: key position kt + c is a window key for this row when c_lo <= c <= c_hi
+      const long long kt = a.kpos0 + (long long)(jt0 + j) * kWP_N;
+      const bool full = kt >= a.klo && kt + kWP_N - 1 <= P0 && (Plast - kt) < a.W;
+      if (!full) {
+        const long long lo = max(max(a.klo - kt, p - a.W + 1 - kt), 0LL);
+        const long long hi = min(p - kt, (long long)kWP_N - 1);
+        const int c_lo = (int)min(lo, (long long)kWP_N), c_hi = (int)max(hi, -1LL);
+#pragma unroll
+        for (int c = 0; c < kWP_N; ++c) u[c] = (c >= c_lo && c <= c_hi) ? u[c] : -INFINITY;
+      }
+      float mx[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) mx[e] = u[e];
+#pragma unroll
+      for (int c = 8; c < kWP_N; c += 8)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) mx[e] = fmaxf(mx[e], u[c + e]);
+      const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                             fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * c2;
       float factor = 1.f;
       bool rescale = false;
       if (m_ref == -INFINITY) {
         m_ref = mt;  // O holds nothing yet (or only zeros)
-      } else if (mt > m_ref + kRescaleThresh) {
-        factor = __expf(m_ref - mt);
+      } else if (mt > m_ref + kRescaleLog2) {
+        factor = ex2_approx(m_ref - mt);
         rescale = true;
         m_ref = mt;
         l *= factor;
       }
-      // probabilities (fp32 sum, fp16 operand)
       uint32_t pk[kWP_N / 2];
       if (m_ref == -INFINITY) {
 #pragma unroll
         for (int c = 0; c < kWP_N / 2; ++c) pk[c] = 0u;
       } else {
+        float ls[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ls[e] = 0.f;
+        const float nm = -m_ref;
 #pragma unroll
         for (int c = 0; c < kWP_N; c += 2) {
-          const float e0 = __expf(s[c] - m_ref), e1 = __expf(s[c + 1] - m_ref);
-          l += e0 + e1;
+          const float e0 = ex2_approx(fmaf(u[c], c2, nm)), e1 = ex2_approx(fmaf(u[c + 1], c2, nm));
+          ls[(c >> 1) & 7] += e0 + e1;
           pk[c / 2] = pack_half2(e0, e1);
         }
+        l += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
       }
-      // the P buffer and O are free once PV_{j-1} has completed
-      if (j >= 1 && !mbar_wait(bar_pv, (j - 1) & 1, abort_flag, a.err, 0x3c)) { alive = false; break; }
-      tc_fence_after();
-      if (rescale) {
+      // P buffer s is free once O += P_{j-2} V_{j-2} finished; O itself only matters when rescaling
+      if (j >= 2 && !mbar_wait_warp(&v_empty[s], ((j >> 1) - 1) & 1, abort_flag, a.err, 0x3c)) { alive = false; break; }
+      // the TMEM load/store below is warp-collective: the warp rescales when any of its rows needs it
+      // (rows that do not need it use factor 1)
+      if (__any_sync(0xffffffffu, rescale)) {
+        if (j >= 1 && !mbar_wait_warp(&v_empty[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, a.err, 0x3e)) {
+          alive = false;
+          break;
+        }
+        tc_fence_after();
 #pragma unroll 1
         for (int c = 0; c < kWP_D; c += 32) {
-          uint32_t u[32];
-          tmem_ld32(trow + 256 + c, u);
+          uint32_t w[32];
+          tmem_ld32(trow + 256 + c, w);
           tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 32; ++e) u[e] = __float_as_uint(__uint_as_float(u[e]) * factor);
-          tmem_st32(trow + 256 + c, u);
+          for (int e = 0; e < 32; ++e) w[e] = __float_as_uint(__uint_as_float(w[e]) * factor);
+          tmem_st32(trow + 256 + c, w);
         }
         tmem_wait_st();
       }
+      uint8_t* pb = sP + s * kWP_SmemP;
 #pragma unroll
-      for (int ch = 0; ch < kWP_N / 8; ++ch) {  // 16 chunks of 8 fp16
-        const int atom = ch >> 3, col = (ch & 7) * 8;
-        *reinterpret_cast<uint4*>(sP + atom * (kWP_M * 128) + sw128_offset(r, col)) =
+      for (int ch = 0; ch < kWP_N / 8; ++ch)
+        *reinterpret_cast<uint4*>(pb + sw128_offset(r, ch * 8)) =
             make_uint4(pk[ch * 4], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
-      }
       fence_async_smem();
       tc_fence_before();
-      mbar_arrive(bar_p_full);
+      mbar_arrive(&p_full[s]);
     }
     // ------------------------------------------------------------------ epilogue
-    if (alive && n > 0) alive = mbar_wait(bar_pv, (n - 1) & 1, abort_flag, a.err, 0x3d);
+    if (alive && n > 0) alive = mbar_wait_warp(&v_empty[(n - 1) & 1], ((n - 1) >> 1) & 1, abort_flag, a.err, 0x3d);
     tc_fence_after();
     if (alive) {
-      // sink keys (positions 0..ns-1), exact in fp32
+      // sink keys (positions 0..ns-1), exact in fp32, scores in the log2 domain
       float se[8];
       int nsv = 0;
       for (int e = 0; e < a.ns; ++e) {
@@ -270,20 +301,20 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
             acc += __uint_as_float(qw[t2] & 0xffff0000u) * __uint_as_float(kw[t2] & 0xffff0000u);
           }
         }
-        se[e] = (e <= p) ? acc * scale : -INFINITY;
+        se[e] = (e <= p) ? acc * c2 : -INFINITY;
         nsv = e + 1;
       }
       float mf = m_ref;
       for (int e = 0; e < nsv; ++e) mf = fmaxf(mf, se[e]);
-      const float fo = (m_ref == -INFINITY) ? 0.f : __expf(m_ref - mf);
+      const float fo = (m_ref == -INFINITY) ? 0.f : ex2_approx(m_ref - mf);
       float lf = l * fo;
       float we[8];
       for (int e = 0; e < nsv; ++e) {
-        we[e] = (se[e] == -INFINITY) ? 0.f : __expf(se[e] - mf);
+        we[e] = (se[e] == -INFINITY) ? 0.f : ex2_approx(se[e] - mf);
         lf += we[e];
       }
       const float inv = lf > 0.f ? 1.f / lf : 0.f;
-      const float lse = lf > 0.f ? mf + logf(lf) : -INFINITY;
+      const float lse = lf > 0.f ? (mf + log2f(lf)) * kLn2 : -INFINITY;
       const int qi = i0 + r;
       const bool row_ok = qi < a.Tq;
       float gam = 0.f;
@@ -298,17 +329,17 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
       const float rho = a.o_mem ? a.mem_scale[h] : 0.f;
 #pragma unroll 1
       for (int c = 0; c < kWP_D; c += 32) {
-        uint32_t u[32];
+        uint32_t w[32];
         if (n > 0) {
-          tmem_ld32(trow + 256 + c, u);
+          tmem_ld32(trow + 256 + c, w);
           tmem_wait_ld();
         } else {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) u[e] = 0u;
+          for (int e = 0; e < 32; ++e) w[e] = 0u;
         }
         float ov[32];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) ov[e] = __uint_as_float(u[e]) * fo;
+        for (int e = 0; e < 32; ++e) ov[e] = __uint_as_float(w[e]) * fo;
         for (int e2 = 0; e2 < nsv; ++e2) {
           if (we[e2] == 0.f) continue;
           const __nv_bfloat16* vp = a.sink_v + (size_t)b * a.sv_b + (size_t)g * a.sv_h + (size_t)e2 * a.sv_k + c;
@@ -437,7 +468,7 @@ int launch_window_prefill(const void* qr, const void* kext, const __half* vt, Wi
   if (rc) return rc;
   rc = make_tmap_kmajor(&kmap, kext, BF_BF16, (uint64_t)a.B * a.G * a.Tk, kWP_D, kWP_D, kWP_N, 4);
   if (rc) return rc;
-  rc = make_tmap_kmajor(&vmap, vt, BF_F16, (uint64_t)a.B * a.G * kWP_D, a.Tkp, a.Tkp, kWP_D, 2);
+  rc = make_tmap_kmajor(&vmap, vt, BF_F16, (uint64_t)a.B * a.G * kWP_D, a.Tkp, a.Tkp, kWP_D, 1);
   if (rc) return rc;
   static bool attr = false;
   if (!attr) {

@@ -51,8 +51,10 @@ const char* bf_strerror(int code);
 /* ABI version of this library (bumped on any signature change). */
 int bf_abi_version(void);
 
-/* Synchronises `stream`, then reads and clears this device's error word.  *word = 0 when no
- * kernel gave up a wait; otherwise (site << 8) | BF_ERR_TIMEOUT.  Returns BF_OK or BF_ERR_CUDA. */
+/* Synchronises `stream`, then reads and clears this device's error record into word[0..3]:
+ * word[0] = 0 when no kernel gave up a wait, else (site << 8) | BF_ERR_TIMEOUT of the first one;
+ * word[1] = its blockIdx.x, word[2] = blockIdx.y | blockIdx.z << 16, word[3] = its threadIdx.x.
+ * Returns BF_OK or BF_ERR_CUDA. */
 int bf_device_error(unsigned int* word, bf_stream_t stream);
 
 /* Per-stage timing: `events` holds 2*n_stages cudaEvent_t handles (begin/end per stage); each

@@ -28,3 +28,17 @@ def golden_gdn():
 def golden_layer():
     import torch
     return torch.load(ROOT / "tests" / "golden" / "golden_layer.pt", weights_only=False)
+
+
+@pytest.fixture(autouse=True)
+def _no_device_timeouts(request):
+    """GPU tests must leave the device error record clean (no bounded wait gave up)."""
+    yield
+    if request.node.get_closest_marker("gpu") is None:
+        return
+    import torch
+    if not torch.cuda.is_available():
+        return
+    from heimdall_b200 import _lib
+    rec = _lib.device_error(torch.cuda.current_stream().cuda_stream)
+    assert rec[0] == 0, f"a device-side wait gave up: site 0x{rec[0] >> 8:x}, block ({rec[1]}, {rec[2]}), thread {rec[3]}"
