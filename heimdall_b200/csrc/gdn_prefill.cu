@@ -185,33 +185,39 @@ __global__ void __launch_bounds__(kP1_Threads, 1) gdn_p1_kernel(GdnStreams s) {
   }
   tc_fence_before();
   __syncthreads();  // A complete; the K tile (reg0) is free (K K^T finished)
-  // ---- (c) T = (I + A)^-1 by blocked forward substitution (16-row blocks)
+  // ---- (c) T = (I + A)^-1: invert the eight 16x16 diagonal blocks (one column chain per thread), then
+  //      double the solved block size 16 -> 32 -> 64 -> 128 with T21 = -T22 (A21 T11)
   for (int i = t; i < 128 * kAS; i += kP1_Threads) Tm[i] = 0.f;
   __syncthreads();
-  for (int I = 0; I < 8; ++I) {
-    const int r0 = I * 16;
-    // contribution of earlier blocks: T[i][col] = -sum_{j < r0} A[i][j] T[j][col], i in block, col < r0
-    for (int p = t; p < 16 * r0; p += kP1_Threads) {
-      const int i = r0 + p / r0, col = p % r0;
+  if (t < 128) {
+    const int r0 = (t >> 4) * 16, col = r0 + (t & 15);
+    Tm[col * kAS + col] = 1.f;
+    for (int i = col + 1; i < r0 + 16; ++i) {
       float acc = 0.f;
-      for (int j = col; j < r0; ++j) acc += A[i * kAS + j] * Tm[j * kAS + col];
+      for (int j = col; j < i; ++j) acc += A[i * kAS + j] * Tm[j * kAS + col];
       Tm[i * kAS + col] = -acc;
     }
+  }
+  __syncthreads();
+  float* X = reinterpret_cast<float*>(regW);  // scratch: A21 T11 for every block pair of a level (<= 16 KB)
+  for (int m = 16; m < 128; m *= 2) {
+    const int npair = 128 / (2 * m), per = m * m;
+    // X_k[i][c] = sum_{j >= c} A[r2 + i][r1 + j] T[r1 + j][r1 + c]
+    for (int q = t; q < npair * per; q += kP1_Threads) {
+      const int k = q / per, i = (q % per) / m, c = q % m;
+      const int r1 = k * 2 * m, r2 = r1 + m;
+      float acc = 0.f;
+      for (int j = c; j < m; ++j) acc += A[(r2 + i) * kAS + r1 + j] * Tm[(r1 + j) * kAS + r1 + c];
+      X[q] = acc;
+    }
     __syncthreads();
-    // inside the block: each column is a sequential chain owned by one thread
-    if (t < r0 + 16) {
-      const int col = t;
-      for (int ii = 0; ii < 16; ++ii) {
-        const int i = r0 + ii;
-        if (col > i) continue;  // rows above this column's diagonal stay zero
-        if (col == i) {
-          Tm[i * kAS + col] = 1.f;
-          continue;
-        }
-        float acc = Tm[i * kAS + col];
-        for (int j = max(r0, col); j < i; ++j) acc -= A[i * kAS + j] * Tm[j * kAS + col];
-        Tm[i * kAS + col] = acc;
-      }
+    // T21[i][c] = -sum_{j <= i} T[r2 + i][r2 + j] X_k[j][c]
+    for (int q = t; q < npair * per; q += kP1_Threads) {
+      const int k = q / per, i = (q % per) / m, c = q % m;
+      const int r1 = k * 2 * m, r2 = r1 + m;
+      float acc = 0.f;
+      for (int j = 0; j <= i; ++j) acc += Tm[(r2 + i) * kAS + r2 + j] * X[k * per + j * m + c];
+      Tm[(r2 + i) * kAS + r1 + c] = -acc;
     }
     __syncthreads();
   }
@@ -231,30 +237,35 @@ __global__ void __launch_bounds__(kP1_Threads, 1) gdn_p1_kernel(GdnStreams s) {
     const int d = t;
     __half* ktT = s.ktT + ((size_t)bg * s.n_chunks + c) * kGD * kGC + (size_t)d * kGC;
 #pragma unroll 1
-    for (int r0 = 0; r0 < kGC; r0 += 8) {
-      float kv[8], vv[8];
+    for (int rb = 0; rb < kGC; rb += 32) {
+      // 64 independent loads in flight per thread (32 tokens x {k, v}), then pack and store
+      float kv[32], vv[32];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const int r = r0 + e;
+      for (int e = 0; e < 32; ++e) {
+        const int r = rb + e;
         const float* kp = s_kp[r];
         kv[e] = kp ? kp[d] : 0.f;
         if (s_vp32[r]) vv[e] = s_vp32[r][d];
         else vv[e] = s_vp[r] ? __bfloat162float(s_vp[r][d]) : 0.f;
       }
-      uint32_t pv[4], pk[4], pt[4];
 #pragma unroll
-      for (int e = 0; e < 8; e += 2) {
-        const int r = r0 + e;
-        const float b0 = s_beta[r], b1 = s_beta[r + 1];
-        const float g0 = s_gc[r], g1 = s_gc[r + 1];
-        pv[e / 2] = pack_half2(b0 * vv[e], b1 * vv[e + 1]);
-        pk[e / 2] = pack_half2(b0 * __expf(g0) * kv[e], b1 * __expf(g1) * kv[e + 1]);
-        pt[e / 2] = pack_half2(__expf(gamma_last - g0) * kv[e], __expf(gamma_last - g1) * kv[e + 1]);
+      for (int q = 0; q < 32; q += 8) {
+        const int r0 = rb + q;
+        uint32_t pv[4], pk[4], pt[4];
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+          const int r = r0 + e;
+          const float b0 = s_beta[r], b1 = s_beta[r + 1];
+          const float g0 = s_gc[r], g1 = s_gc[r + 1];
+          pv[e / 2] = pack_half2(b0 * vv[q + e], b1 * vv[q + e + 1]);
+          pk[e / 2] = pack_half2(b0 * __expf(g0) * kv[q + e], b1 * __expf(g1) * kv[q + e + 1]);
+          pt[e / 2] = pack_half2(__expf(gamma_last - g0) * kv[q + e], __expf(gamma_last - g1) * kv[q + e + 1]);
+        }
+        const uint32_t off = (uint32_t)(r0 >> 6) * (256 * 128) + sw128_offset(d, r0 & 63);
+        *reinterpret_cast<uint4*>(reg0 + off) = make_uint4(pv[0], pv[1], pv[2], pv[3]);
+        *reinterpret_cast<uint4*>(reg1 + off) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        *reinterpret_cast<uint4*>(ktT + r0) = make_uint4(pt[0], pt[1], pt[2], pt[3]);
       }
-      const uint32_t off = (uint32_t)(r0 >> 6) * (256 * 128) + sw128_offset(d, r0 & 63);
-      *reinterpret_cast<uint4*>(reg0 + off) = make_uint4(pv[0], pv[1], pv[2], pv[3]);
-      *reinterpret_cast<uint4*>(reg1 + off) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-      *reinterpret_cast<uint4*>(ktT + r0) = make_uint4(pt[0], pt[1], pt[2], pt[3]);
     }
   }
   fence_async_smem();
