@@ -9,7 +9,8 @@
 // budget), accumulation and the state are fp32.
 //
 // P1 (parallel, CTA = chunk x (b, KV head)): K K^T on tcgen05, A masked/decayed in the epilogue, T by blocked
-//     forward substitution in shared memory (16-row blocks), u and w on tcgen05; also writes fp16 keys,
+//     inversion of the 16x16 diagonal blocks then recursive doubling of the block-triangular inverse in
+//     shared memory, u and w on tcgen05; also writes fp16 keys,
 //     (e^{c_C - c} k)^T and the cumulative decays.
 // P2 (sequential over chunks, CTA = (b, KV head, 16 state columns)): the state block lives in registers (fp32),
 //     v' = u - w S and dS = k_tail^T v' run on tcgen05 with fp16 copies of S^T / v'^T staged in shared memory;
