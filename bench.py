@@ -198,32 +198,34 @@ def ctypes_array(handles):
     return arr
 
 
-def run_e2e(L, T, steps, warmup, device):
-    """Same workload through the public API with host buffers: H2D of every input and D2H of the output per step."""
-    host = [t.cpu().pin_memory() for t in make_inputs(T, 1, device)]
-    dev_bufs = [torch.empty_like(h, device=device) for h in host]
+def run_e2e(L, T, steps, warmup, device, ctx):
+    """Same workload through the public host-buffer API (``BifrostLayer.student_host``): pinned host inputs in,
+    pinned host output back, every copy inside the timed region (the API overlaps them with the layer by
+    processing the sequence in chunks on three streams).  Max over ranks."""
+    host = [t.cpu().pin_memory() for t in make_inputs(T, 1 + ctx["rank"], device)]
     o_host = torch.empty(1, T, H, D, dtype=torch.float32).pin_memory()
     bi = sum(h.numel() * h.element_size() for h in host)
     bo = o_host.numel() * o_host.element_size()
 
     def step():
-        for d_, h_ in zip(dev_bufs, host):
-            d_.copy_(h_, non_blocking=True)
-        o = L.student(*dev_bufs, 0, None)
-        o_host.copy_(o, non_blocking=True)
+        L.student_host(*host, 0, None, out=o_host)
 
     for _ in range(max(1, warmup)):
         step()
     torch.cuda.synchronize()
+    barrier(ctx)
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     for _ in range(steps):
         step()
     b.record()
     torch.cuda.synchronize()
-    ms = a.elapsed_time(b) / steps
-    return {"value": T / (ms / 1e3), "unit": "tok/s", "ms_per_step": ms, "h2d_bytes_per_step": bi,
-            "d2h_bytes_per_step": bo}
+    t = torch.tensor([a.elapsed_time(b) / steps], device=device)
+    if ctx["world"] > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms = float(t.item())
+    return {"value": T * ctx["world"] / (ms / 1e3), "unit": "tok/s", "ms_per_step": ms, "h2d_bytes_per_step": bi,
+            "d2h_bytes_per_step": bo, "api": "BifrostLayer.student_host (chunks of 4096 tokens, 3 streams)"}
 
 
 def run_decode(device, steps=256, warmup=8, nseq=64, nlayers=12):
@@ -322,13 +324,14 @@ def run_decode(device, steps=256, warmup=8, nseq=64, nlayers=12):
 
 
 # ---------------------------------------------------------------------------------------------- CPU arms
-def cpu_sample_tokens_per_s(n_new=512, start=30720, seed=0, threads=None):
+def cpu_sample_tokens_per_s(n_new=2048, start=None, seed=0, threads=None):
     """The CPU oracle (a restatement of the reference's PyTorch path) on a bounded sample of the workload:
-    n_new tokens at positions start.. with a full synthetic cache (W ring entries, sinks, state), i.e. the
-    steady-state per-token cost of the T=32768 prefill."""
+    the last n_new tokens of the T=32768 prefill (positions start.. with a full synthetic cache: W ring
+    entries, sinks, state), i.e. its steady-state per-token cost."""
     import torch.nn.functional as F
     sys.path.insert(0, str(ROOT / "tests" / "golden"))
     from oracle import bifrost_oracle as ob
+    start = 32768 - n_new if start is None else start
     threads = threads or os.cpu_count() or 1
     torch.set_num_threads(threads)
     gen = torch.Generator().manual_seed(seed)
@@ -353,28 +356,49 @@ def cpu_sample_tokens_per_s(n_new=512, start=30720, seed=0, threads=None):
     return n_new / dt, threads, dt
 
 
+def cpu_baseline(min_seconds=10.0, n_new=2048):
+    """Repeats the bounded sample until at least ``min_seconds`` of CPU work ran; tokens / total time."""
+    tot_t, tot_n, reps = 0.0, 0, 0
+    cores = 1
+    while tot_t < min_seconds or reps < 2:
+        _, cores, dt = cpu_sample_tokens_per_s(n_new)
+        tot_t += dt
+        tot_n += n_new
+        reps += 1
+    return tot_n / tot_t, cores, tot_t, reps
+
+
+def arm_config(world):
+    return {"workload": "BASELINE config 1: single Bifrost layer prefill, T=32768, B=1 per GPU, 24q/4kv heads, D=256, "
+                        "W=2048, 4 sinks, d=5120, from an empty cache",
+            "global_batch": world, "seq_len": 32768,
+            "parallelism": f"dp{world} (one independent sequence per GPU)" if world > 1 else "single GPU",
+            "l2": "inputs larger than L2 (1.34 GB read per step), no flush"}
+
+
 def run_reference(args, dist_ctx):
-    rank = dist_ctx["rank"]
-    if rank != 0:
+    """The reference's CPU path (the oracle port; the reference is PyTorch, nothing compiles into oracle/_ref)
+    on all host threads: each step is a bounded sample of the config-1 workload (its last n_new tokens,
+    against a full cache), sized so the whole --steps/--warmup run stays within a few minutes."""
+    if dist_ctx["rank"] != 0:
         return
-    n_new = 512
+    n_new = 2048 if args.steps + args.warmup <= 300 else 512
     for _ in range(args.warmup):
         cpu_sample_tokens_per_s(n_new)
-    vals = []
-    t0 = time.perf_counter()
+    tot = 0.0
+    cores = 1
     for _ in range(args.steps):
-        tps, cores, _ = cpu_sample_tokens_per_s(n_new)
-        vals.append(tps)
-    wall = time.perf_counter() - t0
-    val = sum(vals) / len(vals)
-    sample = (f"{n_new} new tokens at positions 30720.. with a full cache (W=2048 ring, 4 sinks, state): the "
-              f"steady-state per-token cost of the T=32768 layer prefill")
+        _, cores, dt = cpu_sample_tokens_per_s(n_new)
+        tot += dt
+    val = n_new * args.steps / tot
+    sample = (f"{n_new} tokens per step: the last {n_new} tokens of the T=32768 prefill (positions {32768 - n_new}..) "
+              f"with a full cache (W=2048 ring, 4 sinks, state), i.e. its steady-state per-token cost")
+    cfg = arm_config(1)
+    cfg["sample"] = sample
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": val, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": wall / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, config-1 shapes)",
-        "config": {"workload": "BASELINE config 1: single Bifrost layer prefill, T=32768, B=1, 24q/4kv heads, D=256, "
-                               "W=2048, 4 sinks, d=5120", "sample": sample},
+        "warmup": args.warmup, "ms_per_step": tot / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, config-1 shapes)", "config": cfg,
         "cpu_baseline": {"value": val, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": val, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}), flush=True)
 
@@ -409,6 +433,7 @@ def main(argv=None):
     ap.add_argument("--decode-layers", type=int, default=12)
     ap.add_argument("--decode-steps", type=int, default=256)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)
     ctx = dist_setup()
@@ -436,6 +461,7 @@ def run_ours(args, ctx):
     if ctx["world"] > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     ms_max = float(t.item())
+    e2e = None if args.no_e2e else run_e2e(L, T, min(args.steps, 10), 1, dev, ctx)
     if ctx["rank"] != 0:
         return
     ms_step = ms_max / args.steps
@@ -466,22 +492,17 @@ def run_ours(args, ctx):
     out = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ctx["world"], "steps": args.steps,
            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded; config-1 shapes and distributions)",
-           "config": {"workload": "BASELINE config 1: single Bifrost layer prefill, T=32768, B=1 per GPU, 24q/4kv "
-                                  "heads, D=256, W=2048, 4 sinks, d=5120, from an empty cache",
-                      "global_batch": ctx["world"], "seq_len": T,
-                      "parallelism": f"dp{ctx['world']} (one independent sequence per GPU)" if ctx["world"] > 1
-                      else "single GPU",
-                      "l2": "inputs larger than L2 (1.34 GB read per step), no flush"},
+           "config": arm_config(ctx["world"]),
            "stage_ms": stage_ms, "roofline": roof, "layer_roofline": layer_roof, "clocks": clocks,
            "gpu_launches": 8 * args.steps}
-    if not args.no_cpu:
-        e2e = run_e2e(L, T, min(args.steps, 10), 1, dev)
+    if e2e is not None:
         out["e2e"] = e2e
-        tps, cores, dt = cpu_sample_tokens_per_s(512)
+    if not args.no_cpu and ctx["world"] == 1:
+        tps, cores, dt, reps = cpu_baseline()
         out["cpu_baseline"] = {"value": tps, "unit": "tok/s", "cores": cores, "kind": "port",
-                               "sample": "512 tokens at positions 30720.. with a full cache (steady-state cost of "
-                                         f"the T=32768 prefill), {dt:.1f} s on {cores} threads"}
-    if not args.no_decode:
+                               "sample": f"{reps} x the last 2048 tokens of the T=32768 prefill against a full cache "
+                                         f"(its steady-state per-token cost), {dt:.1f} s on {cores} threads"}
+    if not args.no_decode and ctx["world"] == 1:
         out["decode"] = run_decode(dev, steps=args.decode_steps, nseq=args.decode_seqs, nlayers=args.decode_layers)
     print(json.dumps(out), flush=True)
 

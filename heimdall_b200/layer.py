@@ -46,6 +46,7 @@ class BifrostLayer:
         self.R = self.H // self.G
         nbytes = _lib.size("bf_layer_weights_bytes", self.H, self.G, self.D, self.d)
         self.wbuf = _aligned_bytes(nbytes, device)
+        self._host_slots = None
         self.refresh()
 
     @classmethod
@@ -183,6 +184,94 @@ class BifrostLayer:
             cache["sink_k"], cache["sink_v"] = sk, sv
         return o
 
+    def student_host(self, x, q, k, v, qr, kr, start: int = 0, cache=None, memory: bool = True,
+                     chunk: int = 4096, out=None):
+        """``student`` for inputs in host memory: returns o [B,T,H,D] fp32 in pinned host memory.
+
+        The sequence is processed in chunks of ``chunk`` tokens (a prefill with a carried cache, which
+        gives the result of one pass over the whole sequence: the cache holds exactly what the next
+        tokens read), on three streams so that the host->device copy of chunk i+1, the layer on chunk i
+        and the device->host copy of chunk i-1 overlap.  Inputs should be pinned for the copies to run
+        asynchronously.  Layouts as ``student``: x [B,T,d], q [B,T,H,D], k/v [B,T,G,D], qr [B,H,T,D],
+        kr [B,G,T,D].  When ``cache`` is None a private cache carries the chunks and is dropped.
+        Returns after the output is in host memory."""
+        dev = self.device
+        B, T = x.shape[:2]
+        H, G, D = self.H, self.G, self.D
+        if T == 0:
+            return torch.empty(B, 0, H, D, dtype=torch.float32).pin_memory() if out is None else out
+        chunk = max(1, min(int(chunk), T))
+        if out is None:
+            out = torch.empty(B, T, H, D, dtype=torch.float32).pin_memory()
+        st = cache if cache is not None else {}
+        cur = torch.cuda.current_stream(dev)
+        # persistent streams and staging slots: the caching allocator reuses blocks per stream, so fresh
+        # streams on every call would make every call allocate (and free) device memory again
+        s_in, s_comp, s_out = _host_streams(dev)
+        for s_ in (s_in, s_comp, s_out):
+            s_.wait_stream(cur)
+        bf = torch.bfloat16
+        key = (B, chunk, x.shape[2])
+        if self._host_slots is None or self._host_slots[0] != key:
+            def alloc():
+                return (torch.empty(B, chunk, x.shape[2], device=dev, dtype=bf),
+                        torch.empty(B, chunk, H, D, device=dev, dtype=bf),
+                        torch.empty(B, chunk, G, D, device=dev, dtype=bf),
+                        torch.empty(B, chunk, G, D, device=dev, dtype=bf),
+                        torch.empty(B, H, chunk, D, device=dev, dtype=bf),
+                        torch.empty(B, G, chunk, D, device=dev, dtype=bf))
+            torch.cuda.synchronize(dev)
+            self._host_slots = (key, [alloc(), alloc()])
+        slots = self._host_slots[1]
+        freed = [None, None]          # event: the layer has finished reading a slot
+        outs = []
+        t0 = 0
+        for i, n in enumerate(_chunk_plan(T, chunk)):
+            t1 = t0 + n
+            sl = i % 2
+            bx, bq, bk, bv, bqr, bkr = slots[sl]
+            with torch.cuda.stream(s_in):
+                if freed[sl] is not None:
+                    s_in.wait_event(freed[sl])
+                bx[:, :n].copy_(x[:, t0:t1], non_blocking=True)
+                bq[:, :n].copy_(q[:, t0:t1], non_blocking=True)
+                bk[:, :n].copy_(k[:, t0:t1], non_blocking=True)
+                bv[:, :n].copy_(v[:, t0:t1], non_blocking=True)
+                for b in range(B):          # head-major inputs: one contiguous run per (b, head)
+                    for h in range(H):
+                        bqr[b, h, :n].copy_(qr[b, h, t0:t1], non_blocking=True)
+                    for g in range(G):
+                        bkr[b, g, :n].copy_(kr[b, g, t0:t1], non_blocking=True)
+                landed = torch.cuda.Event()
+                landed.record(s_in)
+            with torch.cuda.stream(s_comp):
+                s_comp.wait_event(landed)
+                if n == chunk:
+                    args = (bx, bq, bk, bv, bqr, bkr)
+                else:
+                    args = (bx[:, :n], bq[:, :n], bk[:, :n], bv[:, :n], bqr[:, :, :n].contiguous(),
+                            bkr[:, :, :n].contiguous())
+                o = self._prefill(*args, start + t0, st, memory)
+                freed[sl] = torch.cuda.Event()
+                freed[sl].record(s_comp)
+                done = torch.cuda.Event()
+                done.record(s_comp)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(done)
+                o.record_stream(s_out)
+                if B == 1:
+                    out[:, t0:t1].copy_(o, non_blocking=True)
+                else:
+                    for b in range(B):
+                        out[b, t0:t1].copy_(o[b], non_blocking=True)
+            outs.append(o)
+            t0 = t1
+        for s_ in (s_in, s_comp, s_out):
+            cur.wait_stream(s_)
+        s_out.synchronize()
+        s_comp.synchronize()          # the staging slots are free for the next call
+        return out
+
     def _decode(self, x, q, k, v, qr, kr, start, cache, memory):
         B = x.shape[0]
         H, G, D, W, S = self.H, self.G, self.D, self.window, self.sinks
@@ -232,6 +321,21 @@ class BifrostLayer:
 
 
 _DUMMY = {}
+_STREAMS = {}
+
+
+def _chunk_plan(T: int, chunk: int) -> list:
+    """Chunk lengths for the host-buffer prefill: equal chunks, the last one ragged (a ramp of smaller chunks
+    at both ends measured slower on B200: the per-chunk fixed costs outweigh the shorter fill and drain)."""
+    return [min(chunk, T - t0) for t0 in range(0, T, chunk)]
+
+
+def _host_streams(dev):
+    """Three streams per device for the host-buffer prefill: copies in, the layer, copies out."""
+    key = str(dev)
+    if key not in _STREAMS:
+        _STREAMS[key] = tuple(torch.cuda.Stream(dev) for _ in range(3))
+    return _STREAMS[key]
 
 
 def _dummy_state(dev):
