@@ -12,6 +12,8 @@ Public API (mirrors of the reference ``heimdall`` package):
   window_attention                   heimdall/hibrit.py:336-361 (the math of _window_fp32)
   BifrostLayer.student               heimdall/hibrit.py:363-424 (HybridAttention._student)
   BifrostLayer.mem_inputs            heimdall/hibrit.py:327-334
+  BifrostLayer.student_host          _student for host (pinned) inputs, copies overlapped with the layer
+  plugin.prepare / install           the kernels.prepare plug-in convention (heimdall/kernels.py:158-188)
 """
 from .functional import delta_rule, delta_rule_gqa, delta_rule_step, delta_rule_step_gqa, window_attention  # noqa: F401
 from .layer import BifrostLayer  # noqa: F401
