@@ -9,18 +9,19 @@
 // Ring layout is the reference cache layout: ring_k/ring_v [B,G,W,D] bf16 in slot order (slot = pos % W),
 // ring_km [B,W,G,D] fp32, ring_g/ring_beta [B,W,G] fp32, ring_pos [W] (or [B,W]) int64.
 //
-// Kernel 1 (split): CTA = (key split of 256 ring entries, sequence, KV head).  Thread t owns one key for
-// the scores (R query heads at once), then one 8-column slice of V for the weighted sum over the split's
-// keys; per-split (max, sum, acc) partials go to the workspace.  K/V are read once per (sequence, KV head).
+// Kernel 1 (split): persistent CTAs over (sequence, KV head, 256-slot split); TMA streams the ring K/V rows,
+// the scores run on the tensor core, the weighted sum of V in fp32 SIMT; per-split (max, sum, acc) partials
+// go to the workspace.  K/V are read once per (sequence, KV head).
 // Kernel 2 (combine): CTA = (sequence, KV head): merges the splits, adds the sinks and the new token, forms
 // lse, applies the gate and mix, and writes the new token into its ring slot.
 #include "capi_internal.h"
 #include "common.cuh"
+#include "tmap.h"
 #include "window_decode_args.h"
 
 namespace bfb {
 
-constexpr int kWD_Keys = 256;     // ring entries per split CTA
+constexpr int kWD_Keys = 512;     // ring slots per split (one work item of the split kernel)
 constexpr int kWD_Threads = 256;
 constexpr int kWD_MaxR = 8;
 
@@ -35,121 +36,313 @@ __device__ __forceinline__ void bf16x8_to_f32(const uint4& u, float (&f)[8]) {
   }
 }
 
-__global__ void __launch_bounds__(kWD_Threads) win_dec_split_kernel(WinDecArgs a) {
-  extern __shared__ float sm[];
-  const int D = a.D, R = a.R;
-  float* sq = sm;                          // [R][D]
-  float* sp = sq + kWD_MaxR * 256;         // [R][kWD_Keys] scores, then probabilities
-  float* red = sp + kWD_MaxR * kWD_Keys;   // [8][R][D] per-warp partial sums
-  __shared__ float s_m[kWD_MaxR], s_l[kWD_MaxR];
+// ------------------------------------------------------------------------------------------------ split kernel
+// Persistent CTA (one per SM) over items = (sequence, KV head, split of 512 ring slots), each split as four
+// tiles of 128 slots.  Per tile: TMA brings the K and V rows (K-major, 128-byte swizzle); the scores of the
+// R query heads are S^T = K_tile Q^T on the tensor core (M128 N16 K256, Q staged as a 16-row K-major
+// operand, rows >= R zero) into one of two 16-column TMEM buffers; the softmax warps (one thread per slot)
+// mask by the slot's ring position, keep a running max per head and write the probabilities; the PV warps
+// (a pair of value columns and one half of the tile's slots per thread) accumulate P V in fp32 from the
+// swizzled V tile.  The partial (sum of p v, max, sum of p) per (item, head) goes to the workspace in the
+// layout the combine kernel reads.  Slot j is a window key for the token at position p when its ring
+// position kp satisfies p - W < kp < p, kp >= S and j == kp mod W (the token at p - W leaves the window at
+// this step; the new token and the sinks are added by the combine kernel).
+constexpr int kWT_N = 128;                        // ring slots per tile
+constexpr int kWT_TilesPerItem = kWD_Keys / kWT_N;
+constexpr int kWT_Threads = 512;                  // warp 0 TMA, warp 1 MMA, warp 2 Q staging, warps 4-7 softmax, 8-15 PV
+constexpr int kWT_SmemK = kWT_N * 256 * 2;        // 64 KB
+constexpr int kWT_SmemV = kWT_N * 256 * 2;        // 64 KB, two buffers
+constexpr int kWT_SmemQ = 16 * 256 * 2;           // 8 KB, two buffers
+constexpr int kWT_SmemP = kWT_N * 8 * 4;          // 4 KB, two buffers
+constexpr int kWT_SmemRed = kWD_MaxR * 256 * 4;   // 8 KB
+constexpr int kWT_Tiles = kWT_SmemK + 2 * kWT_SmemV + 2 * kWT_SmemQ + 2 * kWT_SmemP + kWT_SmemRed;
+constexpr int kWT_Smem = kWT_Tiles + 1024 + 1024; // + barriers/statistics + alignment
 
-  const int split = blockIdx.x, bg = blockIdx.y;
-  const int b = bg / a.G, g = bg % a.G;
-  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-  const long long p = a.pos[b];
-  const float scale = rsqrtf((float)D);
+template <int R>
+__global__ void __launch_bounds__(kWT_Threads, 1)
+    win_dec_split_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                         WinDecArgs a, unsigned int* err) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem;
+  uint8_t* sV = sK + kWT_SmemK;                                   // [2][4 atoms][128 rows][128 B]
+  uint8_t* sQ = sV + 2 * kWT_SmemV;                               // [2][4 atoms][16 rows][128 B]
+  float* sP = reinterpret_cast<float*>(sQ + 2 * kWT_SmemQ);       // [2][128 slots][8 heads]
+  float* red = sP + 2 * kWT_N * 8;                                // [8 heads][256]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kWT_Tiles);
+  uint64_t* k_full = bars + 0;
+  uint64_t* k_empty = bars + 1;    // QK of the tile finished reading sK
+  uint64_t* v_full = bars + 2;     // [2]
+  uint64_t* pv_done = bars + 4;    // [2] PV of the tile finished (V buffer and P buffer free); 8 warps
+  uint64_t* q_full = bars + 6;     // [2] Q of an item staged (warp 2)
+  uint64_t* q_empty = bars + 8;    // [2] last QK of the item finished reading its Q buffer
+  uint64_t* s_full = bars + 10;    // [2]
+  uint64_t* s_empty = bars + 12;   // [2] softmax warps read the scores; 4 warps
+  uint64_t* p_full = bars + 14;    // [2] probabilities + rescale factors written; 4 warps
+  uint64_t* sync4 = bars + 16;     // softmax warps among themselves; 4 warps
+  uint64_t* sync8 = bars + 17;     // PV warps among themselves; 8 warps
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 19);
+  float* wmax = reinterpret_cast<float*>(bars + 20);             // [2][4 warps][8]
+  float* wsum = wmax + 64;                                       // [4 warps][8]
+  float* alpha = wsum + 32;                                      // [2][8]
 
-  for (int i = t; i < R * D; i += kWD_Threads) {
-    const int h = i / D, dd = i % D;
-    sq[h * 256 + dd] = __bfloat162float(a.qr[((size_t)b * a.G * R + g * R + h) * D + dd]) * scale;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int D = 256, W = a.W, G = a.G;
+  const int nitems = a.B * G * a.nsplit;
+
+  if (tid == 0) {
+    for (int i = 0; i < 18; ++i)
+      mbar_init(bars + i, (i == 4 || i == 5 || i == 17) ? 8 : (i >= 12 && i <= 16) ? 4 : 1);
+    *abort_flag = 0;
+    fence_barrier_init();
   }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 32);
+    tmem_relinquish();
+  }
+  tc_fence_before();
   __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
 
-  // ---- scores: thread t <-> ring time index j (position p - W + j)
-  const int j = split * kWD_Keys + t;
-  bool valid = false;
-  size_t rowoff = 0;
-  if (j < a.W && j > 0) {
-    const long long kp = p - a.W + j;
-    const int slot = (int)(((kp % a.W) + a.W) % a.W);
-    valid = kp >= a.S && a.ring_pos[(size_t)b * a.ring_pos_bstride + slot] == kp;
-    rowoff = (((size_t)b * a.G + g) * a.W + slot) * D;
-  }
-  float sc[kWD_MaxR];
-#pragma unroll
-  for (int h = 0; h < kWD_MaxR; ++h) sc[h] = 0.f;
-  if (valid) {
-    const uint4* kp4 = reinterpret_cast<const uint4*>(a.ring_k + rowoff);
-    for (int c = 0; c < D / 8; ++c) {
-      float kf[8];
-      bf16x8_to_f32(__ldg(kp4 + c), kf);
-#pragma unroll
-      for (int h = 0; h < kWD_MaxR; ++h) {
-        if (h < R) {
-          const float4 q0 = *reinterpret_cast<const float4*>(sq + h * 256 + c * 8);
-          const float4 q1 = *reinterpret_cast<const float4*>(sq + h * 256 + c * 8 + 4);
-          sc[h] += q0.x * kf[0] + q0.y * kf[1] + q0.z * kf[2] + q0.w * kf[3] + q1.x * kf[4] + q1.y * kf[5] +
-                   q1.z * kf[6] + q1.w * kf[7];
-        }
-      }
-    }
-  }
-  for (int h = 0; h < R; ++h) sp[h * kWD_Keys + t] = valid ? sc[h] : -INFINITY;
-  __syncthreads();
-  // ---- softmax statistics per head (warp h)
-  if (warp < R) {
-    float m = -INFINITY;
-    for (int i = lane; i < kWD_Keys; i += 32) m = fmaxf(m, sp[warp * kWD_Keys + i]);
-    m = warp_max(m);
-    float l = 0.f;
-    for (int i = lane; i < kWD_Keys; i += 32) {
-      const float s = sp[warp * kWD_Keys + i];
-      const float e = (m == -INFINITY) ? 0.f : __expf(s - m);
-      sp[warp * kWD_Keys + i] = e;
-      l += e;
-    }
-    l = warp_sum(l);
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
     if (lane == 0) {
-      s_m[warp] = m;
-      s_l[warp] = l;
+      tma_prefetch(&kmap);
+      tma_prefetch(&vmap);
+      int n = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x) {
+        const int bg = item / a.nsplit, split = item % a.nsplit;
+        for (int tt = 0; tt < kWT_TilesPerItem && ok; ++tt, ++n) {
+          const int row = bg * W + (split * kWT_TilesPerItem + tt) * kWT_N;
+          if (n >= 1 && !(ok = mbar_wait(k_empty, (n - 1) & 1, abort_flag, err, 0x51))) break;
+          mbar_expect_tx(k_full, kWT_SmemK);
+          tma_load_3d(sK, &kmap, k_full, 0, row, 0);
+          if (n >= 2 && !(ok = mbar_wait(&pv_done[n & 1], ((n - 2) >> 1) & 1, abort_flag, err, 0x52))) break;
+          mbar_expect_tx(&v_full[n & 1], kWT_SmemV);
+          tma_load_3d(sV + (n & 1) * kWT_SmemV, &vmap, &v_full[n & 1], 0, row, 0);
+        }
+      }
+      // drain: the last loads land before the CTA ends
+      if (ok && n >= 1) {
+        mbar_wait(k_full, (n - 1) & 1, nullptr, err, 0x53);
+        mbar_wait(&v_full[(n - 1) & 1], ((n - 1) >> 1) & 1, nullptr, err, 0x54);
+        if (n >= 2) mbar_wait(&v_full[n & 1], ((n - 2) >> 1) & 1, nullptr, err, 0x55);
+      }
     }
-  }
-  __syncthreads();
-  // ---- weighted V: warp w takes keys [32w, 32w+32) of the split, lane owns columns [8 lane, 8 lane + 8)
-  float acc[kWD_MaxR][8];
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16(kWT_N, 16, 1);
+      const uint32_t aK = smem_u32(sK), bQ = smem_u32(sQ);
+      int n = 0, it = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x, ++it) {
+        if (!(ok = mbar_wait(&q_full[it & 1], (it >> 1) & 1, abort_flag, err, 0x56))) break;
+        const uint32_t bQi = bQ + (uint32_t)((it & 1) * kWT_SmemQ);
+        for (int tt = 0; tt < kWT_TilesPerItem; ++tt, ++n) {
+          if (!(ok = mbar_wait(k_full, n & 1, abort_flag, err, 0x57))) break;
+          if (n >= 2 && !(ok = mbar_wait(&s_empty[n & 1], ((n - 2) >> 1) & 1, abort_flag, err, 0x58))) break;
+          tc_fence_after();
 #pragma unroll
-  for (int h = 0; h < kWD_MaxR; ++h)
-#pragma unroll
-    for (int c = 0; c < 8; ++c) acc[h][c] = 0.f;
-  const int c0 = lane * 8;
-  if (c0 < D) {
-    for (int kk = 0; kk < 32; ++kk) {
-      const int key = warp * 32 + kk;
-      const int jj = split * kWD_Keys + key;
-      if (jj >= a.W || jj == 0) continue;
-      bool any = false;
-      for (int h = 0; h < R; ++h) any |= sp[h * kWD_Keys + key] != 0.f;
-      if (!any) continue;
-      const long long kp = p - a.W + jj;
-      const int slot = (int)(((kp % a.W) + a.W) % a.W);
-      float vf[8];
-      bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(a.ring_v + (((size_t)b * a.G + g) * a.W + slot) * D + c0)), vf);
-#pragma unroll
-      for (int h = 0; h < kWD_MaxR; ++h) {
-        if (h < R) {
-          const float pr = sp[h * kWD_Keys + key];
-#pragma unroll
-          for (int c = 0; c < 8; ++c) acc[h][c] += pr * vf[c];
+          for (int ks = 0; ks < 16; ++ks)
+            umma_f16_ss(tmem + (n & 1) * 16, sdesc_kstep(aK, kWT_N, ks), sdesc_kstep(bQi, 16, ks), idesc, ks > 0);
+          umma_commit(k_empty);
+          umma_commit(&s_full[n & 1]);
+          if (tt == kWT_TilesPerItem - 1) umma_commit(&q_empty[it & 1]);
         }
       }
     }
-  }
-  for (int h = 0; h < R; ++h)
+  } else if (warp == 2) {
+    // ---------------------------------------------------------------- Q staging, one item ahead (rows R..15 zero)
+    int it = 0;
+    for (int item = blockIdx.x; item < nitems; item += gridDim.x, ++it) {
+      const int bg = item / a.nsplit;
+      const int b = bg / G, g = bg % G;
+      if (it >= 2 && !mbar_wait_warp(&q_empty[it & 1], ((it - 2) >> 1) & 1, abort_flag, err, 0x59)) break;
+      uint8_t* q = sQ + (it & 1) * kWT_SmemQ;
+      for (int i = lane; i < 16 * 32; i += 32) {
+        const int h = i >> 5, c = i & 31;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (h < R) v = __ldg(reinterpret_cast<const uint4*>(a.qr + ((size_t)b * G * R + g * R + h) * D) + c);
+        *reinterpret_cast<uint4*>(q + (c >> 3) * (16 * 128) + h * 128 + (((c & 7) ^ (h & 7)) << 4)) = v;
+      }
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&q_full[it & 1]);
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // ---------------------------------------------------------------- softmax warps: thread = slot of the tile
+    const int q4 = warp - 4;
+    const int r = q4 * 32 + lane;
+    const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
+    const float scale = rsqrtf((float)D);
+    uint32_t ph4 = 0;
+    auto sync_sm = [&](unsigned int site) -> bool {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(sync4);
+      const bool ok = mbar_wait_warp(sync4, ph4 & 1, abort_flag, err, site);
+      ++ph4;
+      return ok;
+    };
+    int n = 0, it = 0;
+    bool alive = true;
+    for (int item = blockIdx.x; item < nitems && alive; item += gridDim.x, ++it) {
+      const int bg = item / a.nsplit, split = item % a.nsplit;
+      const int b = bg / G, g = bg % G;
+      const long long p = a.pos[b];
+      const long long pm = ((p + 1) % W + W) % W;      // slot of position p - W + 1
+      float m[R], l[R];
 #pragma unroll
-    for (int c = 0; c < 8; ++c)
-      if (c0 + c < D) red[(warp * kWD_MaxR + h) * 256 + c0 + c] = acc[h][c];
+      for (int h = 0; h < R; ++h) {
+        m[h] = -INFINITY;
+        l[h] = 0.f;
+      }
+      for (int tt = 0; tt < kWT_TilesPerItem; ++tt, ++n) {
+        const int s = n & 1;
+        // the slot's ring position is loaded before the wait for the scores and tested after it
+        const int slot = (split * kWT_TilesPerItem + tt) * kWT_N + r;
+        const long long kp = slot < W ? __ldg(a.ring_pos + (size_t)b * a.ring_pos_bstride + slot) : -1;
+        if (!(alive = mbar_wait_warp(&s_full[s], (n >> 1) & 1, abort_flag, err, 0x5a))) break;
+        bool valid = false;
+        const long long off = kp - (p - W + 1);         // 0 .. W-2 for window keys
+        if (kp >= a.S && off >= 0 && off < W - 1) {
+          long long want = pm + off;
+          if (want >= W) want -= W;
+          valid = want == slot;
+        }
+        tc_fence_after();
+        uint32_t w[16];
+        tmem_ld16(trow + s * 16, w);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_empty[s]);
+        float sc[R];
+#pragma unroll
+        for (int h = 0; h < R; ++h) {
+          sc[h] = valid ? __uint_as_float(w[h]) * scale : -INFINITY;
+          const float mx = warp_max(sc[h]);
+          if (lane == 0) wmax[(s * 4 + q4) * 8 + h] = mx;
+        }
+        if (!(alive = sync_sm(0x5b))) break;
+        float pr[8], alh[R];
+#pragma unroll
+        for (int h = 0; h < 8; ++h) pr[h] = 0.f;
+#pragma unroll
+        for (int h = 0; h < R; ++h) {
+          const float mt = fmaxf(fmaxf(wmax[(s * 4 + 0) * 8 + h], wmax[(s * 4 + 1) * 8 + h]),
+                                 fmaxf(wmax[(s * 4 + 2) * 8 + h], wmax[(s * 4 + 3) * 8 + h]));
+          const float mn = fmaxf(m[h], mt);
+          const float al = (mn == -INFINITY) ? 1.f : __expf(m[h] - mn);
+          pr[h] = (sc[h] == -INFINITY) ? 0.f : __expf(sc[h] - mn);
+          l[h] = l[h] * al + pr[h];
+          m[h] = mn;
+          alh[h] = al;
+        }
+        // the P buffer and the rescale factors are free once the product of tile n - 2 is done
+        if (n >= 2 && !(alive = mbar_wait_warp(&pv_done[s], ((n - 2) >> 1) & 1, abort_flag, err, 0x5c))) break;
+        if (r == 0) {
+#pragma unroll
+          for (int h = 0; h < R; ++h) alpha[s * 8 + h] = alh[h];
+        }
+        float4* dst = reinterpret_cast<float4*>(sP + (s * kWT_N + r) * 8);
+        dst[0] = make_float4(pr[0], pr[1], pr[2], pr[3]);
+        dst[1] = make_float4(pr[4], pr[5], pr[6], pr[7]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[s]);
+      }
+      if (!alive) break;
+      // item end: sum of p per head over the 128 slot threads; one thread per head writes (max, sum)
+#pragma unroll
+      for (int h = 0; h < R; ++h) {
+        const float sum = warp_sum(l[h]);
+        if (lane == 0) wsum[q4 * 8 + h] = sum;
+      }
+      if (!(alive = sync_sm(0x5d))) break;
+      if (r < R) {
+        float* out = a.part + (((size_t)bg * a.nsplit + split) * R + r) * (D + 2);
+        out[D] = m[r];
+        out[D + 1] = wsum[r] + wsum[8 + r] + wsum[16 + r] + wsum[24 + r];
+      }
+      if (!(alive = sync_sm(0x5e))) break;     // wsum is rewritten at the next item end
+    }
+  } else if (warp >= 8) {
+    // ---------------------------------------------------------------- PV warps: value columns 2dp, 2dp+1 over half the slots
+    const int u = tid - 256;
+    const int dp = u & 127, kh = u >> 7;
+    const uint32_t voff = (uint32_t)(dp >> 5) * (kWT_N * 128) + (uint32_t)((dp & 3) * 4);
+    const uint32_t vchunk = (uint32_t)((dp & 31) >> 2);
+    uint32_t ph8 = 0;
+    auto sync_pv = [&](unsigned int site) -> bool {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(sync8);
+      const bool ok = mbar_wait_warp(sync8, ph8 & 1, abort_flag, err, site);
+      ++ph8;
+      return ok;
+    };
+    int n = 0;
+    bool alive = true;
+    for (int item = blockIdx.x; item < nitems && alive; item += gridDim.x) {
+      const int bg = item / a.nsplit, split = item % a.nsplit;
+      float acc[R][2];
+#pragma unroll
+      for (int h = 0; h < R; ++h) acc[h][0] = acc[h][1] = 0.f;
+      for (int tt = 0; tt < kWT_TilesPerItem; ++tt, ++n) {
+        const int s = n & 1;
+        if (!(alive = mbar_wait_warp(&p_full[s], (n >> 1) & 1, abort_flag, err, 0x60))) break;
+        if (!(alive = mbar_wait_warp(&v_full[s], (n >> 1) & 1, abort_flag, err, 0x61))) break;
+#pragma unroll
+        for (int h = 0; h < R; ++h) {
+          const float al = alpha[s * 8 + h];
+          acc[h][0] *= al;
+          acc[h][1] *= al;
+        }
+        const uint8_t* vb = sV + s * kWT_SmemV + voff;
+        const float* pb = sP + s * kWT_N * 8;
+#pragma unroll 4
+        for (int kk = 0; kk < kWT_N / 2; ++kk) {
+          const int key = kh * (kWT_N / 2) + kk;
+          const float4 p0 = *reinterpret_cast<const float4*>(pb + key * 8);
+          const float4 p1 = *reinterpret_cast<const float4*>(pb + key * 8 + 4);
+          const uint32_t vv = *reinterpret_cast<const uint32_t*>(vb + key * 128 + ((vchunk ^ (uint32_t)(key & 7)) << 4));
+          const float v0 = __uint_as_float(vv << 16), v1 = __uint_as_float(vv & 0xffff0000u);
+          const float pv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+#pragma unroll
+          for (int h = 0; h < R; ++h) {
+            acc[h][0] = fmaf(pv[h], v0, acc[h][0]);
+            acc[h][1] = fmaf(pv[h], v1, acc[h][1]);
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&pv_done[s]);
+      }
+      if (!alive) break;
+      // item end: add the two slot halves, write the partial sums
+      if (kh == 1) {
+#pragma unroll
+        for (int h = 0; h < R; ++h) *reinterpret_cast<float2*>(red + h * 256 + 2 * dp) = make_float2(acc[h][0], acc[h][1]);
+      }
+      if (!(alive = sync_pv(0x62))) break;
+      if (kh == 0) {
+        float* out = a.part + ((size_t)bg * a.nsplit + split) * R * (D + 2);
+#pragma unroll
+        for (int h = 0; h < R; ++h) {
+          const float2 o2 = *reinterpret_cast<const float2*>(red + h * 256 + 2 * dp);
+          out[h * (D + 2) + 2 * dp] = acc[h][0] + o2.x;
+          out[h * (D + 2) + 2 * dp + 1] = acc[h][1] + o2.y;
+        }
+      }
+      if (!(alive = sync_pv(0x63))) break;
+    }
+  }
+  tc_fence_before();
   __syncthreads();
-  float* out = a.part + ((size_t)bg * a.nsplit + split) * R * (D + 2);
-  for (int i = t; i < R * D; i += kWD_Threads) {
-    const int h = i / D, dd = i % D;
-    float s = 0.f;
-#pragma unroll
-    for (int w = 0; w < 8; ++w) s += red[(w * kWD_MaxR + h) * 256 + dd];
-    out[h * (D + 2) + dd] = s;
-  }
-  if (t < R) {
-    out[t * (D + 2) + D] = s_m[t];
-    out[t * (D + 2) + D + 1] = s_l[t];
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 32);
   }
 }
 
@@ -256,16 +449,45 @@ size_t win_dec_workspace(int B, int G, int R, int D, int W) {
   return (size_t)B * G * nsplit * R * (D + 2) * sizeof(float);
 }
 
-int launch_win_dec(WinDecArgs a, cudaStream_t stream) {
-  a.nsplit = (a.W + kWD_Keys - 1) / kWD_Keys;
-  const size_t smem = (size_t)(kWD_MaxR * 256 + kWD_MaxR * kWD_Keys + 8 * kWD_MaxR * 256) * sizeof(float);
+template <int R>
+static int launch_split(const CUtensorMap& kmap, const CUtensorMap& vmap, const WinDecArgs& a, int grid,
+                        unsigned int* err, cudaStream_t stream) {
   static bool attr = false;
   if (!attr) {
-    if (cudaFuncSetAttribute(win_dec_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    if (cudaFuncSetAttribute(win_dec_split_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, kWT_Smem) !=
+        cudaSuccess)
       return BF_ERR_CUDA;
     attr = true;
   }
-  win_dec_split_kernel<<<dim3(a.nsplit, a.B * a.G), kWD_Threads, smem, stream>>>(a);
+  win_dec_split_kernel<R><<<grid, kWT_Threads, kWT_Smem, stream>>>(kmap, vmap, a, err);
+  return BF_OK;
+}
+
+int launch_win_dec(WinDecArgs a, cudaStream_t stream) {
+  a.nsplit = (a.W + kWD_Keys - 1) / kWD_Keys;
+  if (a.D != 256 || a.R < 1 || a.R > kWD_MaxR) return BF_ERR_UNSUPPORTED;
+  DeviceState st;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  CUtensorMap kmap, vmap;
+  const uint64_t rows = (uint64_t)a.B * a.G * a.W;
+  rc = make_tmap_kmajor(&kmap, a.ring_k, BF_BF16, rows, 256, 256, kWT_N, 4);
+  if (rc) return rc;
+  rc = make_tmap_kmajor(&vmap, a.ring_v, BF_BF16, rows, 256, 256, kWT_N, 4);
+  if (rc) return rc;
+  const int nitems = a.B * a.G * a.nsplit;
+  const int grid = nitems < st.sm_count ? nitems : st.sm_count;
+  switch (a.R) {
+    case 1: rc = launch_split<1>(kmap, vmap, a, grid, st.err, stream); break;
+    case 2: rc = launch_split<2>(kmap, vmap, a, grid, st.err, stream); break;
+    case 3: rc = launch_split<3>(kmap, vmap, a, grid, st.err, stream); break;
+    case 4: rc = launch_split<4>(kmap, vmap, a, grid, st.err, stream); break;
+    case 5: rc = launch_split<5>(kmap, vmap, a, grid, st.err, stream); break;
+    case 6: rc = launch_split<6>(kmap, vmap, a, grid, st.err, stream); break;
+    case 7: rc = launch_split<7>(kmap, vmap, a, grid, st.err, stream); break;
+    default: rc = launch_split<8>(kmap, vmap, a, grid, st.err, stream); break;
+  }
+  if (rc) return rc;
   win_dec_combine_kernel<<<a.B * a.G, kWD_Threads, 0, stream>>>(a);
   return cudaGetLastError() == cudaSuccess ? BF_OK : BF_ERR_CUDA;
 }
