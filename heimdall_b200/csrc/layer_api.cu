@@ -52,8 +52,9 @@ int mem_inputs_impl(const DeviceState& st, const bf_layer* L, const void* x, con
   if (rc) return rc;
   stage_mark(ST_XPROJ, 1, stream);
   stage_mark(ST_HEADPROJ, 0, stream);
+  // the projection is per token and [B,T,heads,D] is token-contiguous: one flat run of B*T tokens
   rc = launch_head_proj(static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
-                        weights_heads(L->wbuf), qm, qm16, km, B, T, L->H, L->G, st.sm_count, st.err, stream);
+                        weights_heads(L->wbuf), qm, qm16, km, 1, B * T, L->H, L->G, st.sm_count, st.err, stream);
   stage_mark(ST_HEADPROJ, 1, stream);
   return rc;
 }

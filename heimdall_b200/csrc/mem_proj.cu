@@ -362,6 +362,62 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// x_proj for few rows (decode): one CTA per row, warp w forms outputs 4w..4w+3 as dot products of the row
+// with the same hi and lo bf16 weight rows the tensor-core path uses (x*hi + x*lo in fp32), then the same
+// epilogue.  A 128-row tensor-core tile would walk all d columns in one CTA for a handful of rows.
+constexpr int kXP_SmallRows = 256;
+
+__global__ void __launch_bounds__(256) x_proj_small_kernel(const __nv_bfloat16* __restrict__ x,
+                                                           const __nv_bfloat16* __restrict__ w_x, XProjArgs a) {
+  __shared__ float rs[32];
+  const int m = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)m * a.d);
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int c = lane; c < a.d / 8; c += 32) {
+    float xf[8];
+    {
+      const uint4 u = __ldg(xr + c);
+      const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        xf[2 * e] = __uint_as_float(w4[e] << 16);
+        xf[2 * e + 1] = __uint_as_float(w4[e] & 0xffff0000u);
+      }
+    }
+#pragma unroll
+    for (int o = 0; o < 4; ++o) {
+      const int j = warp * 4 + o;
+      const uint4 hi = __ldg(reinterpret_cast<const uint4*>(w_x + (size_t)j * a.d) + c);
+      const uint4 lo = __ldg(reinterpret_cast<const uint4*>(w_x + (size_t)(32 + j) * a.d) + c);
+      const uint32_t h4[4] = {hi.x, hi.y, hi.z, hi.w}, l4[4] = {lo.x, lo.y, lo.z, lo.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        acc[o] = fmaf(xf[2 * e], __uint_as_float(h4[e] << 16) + __uint_as_float(l4[e] << 16), acc[o]);
+        acc[o] = fmaf(xf[2 * e + 1], __uint_as_float(h4[e] & 0xffff0000u) + __uint_as_float(l4[e] & 0xffff0000u),
+                      acc[o]);
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 0; o < 4; ++o) {
+    const float v = warp_sum(acc[o]);
+    if (lane == 0) rs[warp * 4 + o] = v;
+  }
+  __syncthreads();
+  const int G = a.G, H = a.H, t = threadIdx.x;
+  if (t < G) {
+    const long long p = a.pos ? (long long)a.pos[m] : a.pos0 + (m % a.T);
+    const float av = rs[t] + a.ab_b[t];
+    const float bv = rs[G + t] + a.ab_b[G + t];
+    const float z = av + a.dt_bias[t];
+    const float sp = z > 20.f ? z : log1pf(__expf(z));
+    a.g[(size_t)m * G + t] = -__expf(a.A_log[t]) * sp * a.decay_mask[t];
+    a.beta[(size_t)m * G + t] = (p >= a.sinks) ? 1.f / (1.f + __expf(-bv)) : 0.f;
+  } else if (t < G + H) {
+    a.mixx[(size_t)m * H + (t - G)] = rs[2 * G + (t - G)] + a.mix_b[t - G];
+  }
+}
+
 // ============================================================================ launchers
 int launch_prep_weights(const float* fq, const float* fk, const float* ab_w, const float* mix_w, int H, int G,
                         int D, int d, __half* w_heads, __nv_bfloat16* w_x, cudaStream_t stream) {
@@ -408,6 +464,11 @@ int launch_x_proj(const __nv_bfloat16* x, const __nv_bfloat16* w_x, const float*
                   const float* A_log, const float* dt_bias, const float* decay_mask, float* g, float* beta,
                   float* mixx, const int64_t* pos, long long pos0, int M, int T, int d, int G, int H, int sinks,
                   unsigned int* err, cudaStream_t stream) {
+  if (M <= kXP_SmallRows && d % 8 == 0) {
+    XProjArgs a{ab_b, mix_b, A_log, dt_bias, decay_mask, nullptr, g, beta, mixx, pos, pos0, M, T, d, G, H, sinks, err};
+    x_proj_small_kernel<<<M, 256, 0, stream>>>(x, w_x, a);
+    return cudaGetLastError() == cudaSuccess ? BF_OK : BF_ERR_CUDA;
+  }
   CUtensorMap xmap, wmap;
   int rc = make_tmap_kmajor(&xmap, x, BF_BF16, (uint64_t)M, d, d, kXP_M, 1);
   if (rc) return rc;

@@ -42,14 +42,29 @@ __device__ __forceinline__ void bf16x8_to_f32(const uint4& u, float (&f)[8]) {
 // R query heads are S^T = K_tile Q^T on the tensor core (M128 N16 K256, Q staged as a 16-row K-major
 // operand, rows >= R zero) into one of two 16-column TMEM buffers; the softmax warps (one thread per slot)
 // mask by the slot's ring position, keep a running max per head and write the probabilities; the PV warps
-// (a pair of value columns and one half of the tile's slots per thread) accumulate P V in fp32 from the
-// swizzled V tile.  The partial (sum of p v, max, sum of p) per (item, head) goes to the workspace in the
+// (four value columns and a quarter of the tile's slots per thread) accumulate P V in fp32 from the
+// swizzled V tile with packed fp32 FMAs over head pairs.  The partial (sum of p v, max, sum of p) per (item, head) goes to the workspace in the
 // layout the combine kernel reads.  Slot j is a window key for the token at position p when its ring
 // position kp satisfies p - W < kp < p, kp >= S and j == kp mod W (the token at p - W leaves the window at
 // this step; the new token and the sinks are added by the combine kernel).
+// packed fp32 pair helpers (fma.rn.f32x2 updates two accumulators per instruction)
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t dup2(uint32_t x) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %1};" : "=l"(d) : "r"(x));
+  return d;
+}
+__device__ __forceinline__ float lo_hi(uint64_t x, int hi) {
+  return __uint_as_float(hi ? (uint32_t)(x >> 32) : (uint32_t)x);
+}
+
 constexpr int kWT_N = 128;                        // ring slots per tile
 constexpr int kWT_TilesPerItem = kWD_Keys / kWT_N;
-constexpr int kWT_Threads = 512;                  // warp 0 TMA, warp 1 MMA, warp 2 Q staging, warps 4-7 softmax, 8-15 PV
+constexpr int kWT_Threads = 512;  // warp 0 K TMA, warp 1 MMA, warp 2 Q staging, warp 3 V TMA, 4-7 softmax, 8-15 PV
 constexpr int kWT_SmemK = kWT_N * 256 * 2;        // 64 KB
 constexpr int kWT_SmemV = kWT_N * 256 * 2;        // 64 KB, two buffers
 constexpr int kWT_SmemQ = 16 * 256 * 2;           // 8 KB, two buffers
@@ -70,8 +85,6 @@ __global__ void __launch_bounds__(kWT_Threads, 1)
   float* sP = reinterpret_cast<float*>(sQ + 2 * kWT_SmemQ);       // [2][128 slots][8 heads]
   float* red = sP + 2 * kWT_N * 8;                                // [8 heads][256]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kWT_Tiles);
-  uint64_t* k_full = bars + 0;
-  uint64_t* k_empty = bars + 1;    // QK of the tile finished reading sK
   uint64_t* v_full = bars + 2;     // [2]
   uint64_t* pv_done = bars + 4;    // [2] PV of the tile finished (V buffer and P buffer free); 8 warps
   uint64_t* q_full = bars + 6;     // [2] Q of an item staged (warp 2)
@@ -81,9 +94,11 @@ __global__ void __launch_bounds__(kWT_Threads, 1)
   uint64_t* p_full = bars + 14;    // [2] probabilities + rescale factors written; 4 warps
   uint64_t* sync4 = bars + 16;     // softmax warps among themselves; 4 warps
   uint64_t* sync8 = bars + 17;     // PV warps among themselves; 8 warps
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 19);
-  float* wmax = reinterpret_cast<float*>(bars + 20);             // [2][4 warps][8]
+  uint64_t* k_full = bars + 18;    // [4] one per 64-column atom of the K tile
+  uint64_t* k_empty = bars + 22;   // [4] the four k-steps of an atom finished reading it
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 26);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 27);
+  float* wmax = reinterpret_cast<float*>(bars + 28);             // [2][4 warps][8]
   float* wsum = wmax + 64;                                       // [4 warps][8]
   float* alpha = wsum + 32;                                      // [2][8]
 
@@ -92,7 +107,7 @@ __global__ void __launch_bounds__(kWT_Threads, 1)
   const int nitems = a.B * G * a.nsplit;
 
   if (tid == 0) {
-    for (int i = 0; i < 18; ++i)
+    for (int i = 0; i < 26; ++i)
       mbar_init(bars + i, (i == 4 || i == 5 || i == 17) ? 8 : (i >= 12 && i <= 16) ? 4 : 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -107,9 +122,29 @@ __global__ void __launch_bounds__(kWT_Threads, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ---------------------------------------------------------------- TMA producer
+    // ---------------------------------------------------------------- K producer: the four 64-column atoms of a
+    // tile load separately, each as soon as the product of the previous tile has read that atom
     if (lane == 0) {
       tma_prefetch(&kmap);
+      int n = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x) {
+        const int bg = item / a.nsplit, split = item % a.nsplit;
+        for (int tt = 0; tt < kWT_TilesPerItem && ok; ++tt, ++n) {
+          const int row = bg * W + (split * kWT_TilesPerItem + tt) * kWT_N;
+          for (int at = 0; at < 4; ++at) {
+            if (n >= 1 && !(ok = mbar_wait(&k_empty[at], (n - 1) & 1, abort_flag, err, 0x51))) break;
+            mbar_expect_tx(&k_full[at], kWT_SmemK / 4);
+            tma_load_3d(sK + at * (kWT_SmemK / 4), &kmap, &k_full[at], 0, row, at);
+          }
+        }
+      }
+      if (ok && n >= 1)
+        for (int at = 0; at < 4; ++at) mbar_wait(&k_full[at], (n - 1) & 1, nullptr, err, 0x53);
+    }
+  } else if (warp == 3) {
+    // ---------------------------------------------------------------- V producer (two tile buffers)
+    if (lane == 0) {
       tma_prefetch(&vmap);
       int n = 0;
       bool ok = true;
@@ -117,9 +152,6 @@ __global__ void __launch_bounds__(kWT_Threads, 1)
         const int bg = item / a.nsplit, split = item % a.nsplit;
         for (int tt = 0; tt < kWT_TilesPerItem && ok; ++tt, ++n) {
           const int row = bg * W + (split * kWT_TilesPerItem + tt) * kWT_N;
-          if (n >= 1 && !(ok = mbar_wait(k_empty, (n - 1) & 1, abort_flag, err, 0x51))) break;
-          mbar_expect_tx(k_full, kWT_SmemK);
-          tma_load_3d(sK, &kmap, k_full, 0, row, 0);
           if (n >= 2 && !(ok = mbar_wait(&pv_done[n & 1], ((n - 2) >> 1) & 1, abort_flag, err, 0x52))) break;
           mbar_expect_tx(&v_full[n & 1], kWT_SmemV);
           tma_load_3d(sV + (n & 1) * kWT_SmemV, &vmap, &v_full[n & 1], 0, row, 0);
@@ -127,7 +159,6 @@ __global__ void __launch_bounds__(kWT_Threads, 1)
       }
       // drain: the last loads land before the CTA ends
       if (ok && n >= 1) {
-        mbar_wait(k_full, (n - 1) & 1, nullptr, err, 0x53);
         mbar_wait(&v_full[(n - 1) & 1], ((n - 1) >> 1) & 1, nullptr, err, 0x54);
         if (n >= 2) mbar_wait(&v_full[n & 1], ((n - 2) >> 1) & 1, nullptr, err, 0x55);
       }
@@ -142,14 +173,19 @@ __global__ void __launch_bounds__(kWT_Threads, 1)
       for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x, ++it) {
         if (!(ok = mbar_wait(&q_full[it & 1], (it >> 1) & 1, abort_flag, err, 0x56))) break;
         const uint32_t bQi = bQ + (uint32_t)((it & 1) * kWT_SmemQ);
-        for (int tt = 0; tt < kWT_TilesPerItem; ++tt, ++n) {
-          if (!(ok = mbar_wait(k_full, n & 1, abort_flag, err, 0x57))) break;
+        for (int tt = 0; tt < kWT_TilesPerItem && ok; ++tt, ++n) {
           if (n >= 2 && !(ok = mbar_wait(&s_empty[n & 1], ((n - 2) >> 1) & 1, abort_flag, err, 0x58))) break;
-          tc_fence_after();
+          for (int at = 0; at < 4; ++at) {
+            if (!(ok = mbar_wait(&k_full[at], n & 1, abort_flag, err, 0x57))) break;
+            tc_fence_after();
 #pragma unroll
-          for (int ks = 0; ks < 16; ++ks)
-            umma_f16_ss(tmem + (n & 1) * 16, sdesc_kstep(aK, kWT_N, ks), sdesc_kstep(bQi, 16, ks), idesc, ks > 0);
-          umma_commit(k_empty);
+            for (int k4 = 0; k4 < 4; ++k4) {
+              const int ks = at * 4 + k4;
+              umma_f16_ss(tmem + (n & 1) * 16, sdesc_kstep(aK, kWT_N, ks), sdesc_kstep(bQi, 16, ks), idesc, ks > 0);
+            }
+            umma_commit(&k_empty[at]);
+          }
+          if (!ok) break;
           umma_commit(&s_full[n & 1]);
           if (tt == kWT_TilesPerItem - 1) umma_commit(&q_empty[it & 1]);
         }
@@ -270,11 +306,13 @@ __global__ void __launch_bounds__(kWT_Threads, 1)
       if (!(alive = sync_sm(0x5e))) break;     // wsum is rewritten at the next item end
     }
   } else if (warp >= 8) {
-    // ---------------------------------------------------------------- PV warps: value columns 2dp, 2dp+1 over half the slots
+    // ---------------------------------------------------------------- PV warps: value columns 4dq..4dq+3 over a
+    // quarter of the slots; accumulators are (head 2i, head 2i+1) pairs updated with packed fp32 FMAs
+    constexpr int HP = (R + 1) / 2;
     const int u = tid - 256;
-    const int dp = u & 127, kh = u >> 7;
-    const uint32_t voff = (uint32_t)(dp >> 5) * (kWT_N * 128) + (uint32_t)((dp & 3) * 4);
-    const uint32_t vchunk = (uint32_t)((dp & 31) >> 2);
+    const int dq = u & 63, kq = u >> 6;
+    const uint32_t voff = (uint32_t)(dq >> 4) * (kWT_N * 128) + (uint32_t)((dq & 1) * 8);
+    const uint32_t vchunk = (uint32_t)((dq & 15) >> 1);
     uint32_t ph8 = 0;
     auto sync_pv = [&](unsigned int site) -> bool {
       __syncwarp();
@@ -287,55 +325,72 @@ __global__ void __launch_bounds__(kWT_Threads, 1)
     bool alive = true;
     for (int item = blockIdx.x; item < nitems && alive; item += gridDim.x) {
       const int bg = item / a.nsplit, split = item % a.nsplit;
-      float acc[R][2];
+      uint64_t acc[HP][4];
 #pragma unroll
-      for (int h = 0; h < R; ++h) acc[h][0] = acc[h][1] = 0.f;
+      for (int h = 0; h < HP; ++h)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[h][c] = 0ull;
       for (int tt = 0; tt < kWT_TilesPerItem; ++tt, ++n) {
         const int s = n & 1;
         if (!(alive = mbar_wait_warp(&p_full[s], (n >> 1) & 1, abort_flag, err, 0x60))) break;
         if (!(alive = mbar_wait_warp(&v_full[s], (n >> 1) & 1, abort_flag, err, 0x61))) break;
+        {
+          const uint64_t* al2 = reinterpret_cast<const uint64_t*>(alpha + s * 8);
 #pragma unroll
-        for (int h = 0; h < R; ++h) {
-          const float al = alpha[s * 8 + h];
-          acc[h][0] *= al;
-          acc[h][1] *= al;
+          for (int h = 0; h < HP; ++h) {
+            const uint64_t al = al2[h];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) acc[h][c] = fma2(al, acc[h][c], 0ull);
+          }
         }
         const uint8_t* vb = sV + s * kWT_SmemV + voff;
         const float* pb = sP + s * kWT_N * 8;
 #pragma unroll 4
-        for (int kk = 0; kk < kWT_N / 2; ++kk) {
-          const int key = kh * (kWT_N / 2) + kk;
-          const float4 p0 = *reinterpret_cast<const float4*>(pb + key * 8);
-          const float4 p1 = *reinterpret_cast<const float4*>(pb + key * 8 + 4);
-          const uint32_t vv = *reinterpret_cast<const uint32_t*>(vb + key * 128 + ((vchunk ^ (uint32_t)(key & 7)) << 4));
-          const float v0 = __uint_as_float(vv << 16), v1 = __uint_as_float(vv & 0xffff0000u);
-          const float pv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+        for (int kk = 0; kk < kWT_N / 4; ++kk) {
+          const int key = kq * (kWT_N / 4) + kk;
+          const ulonglong2 p01 = *reinterpret_cast<const ulonglong2*>(pb + key * 8);
+          const ulonglong2 p23 = *reinterpret_cast<const ulonglong2*>(pb + key * 8 + 4);
+          const uint64_t pp[4] = {p01.x, p01.y, p23.x, p23.y};
+          const uint2 vv = *reinterpret_cast<const uint2*>(vb + key * 128 + ((vchunk ^ (uint32_t)(key & 7)) << 4));
+          const uint64_t vd[4] = {dup2(vv.x << 16), dup2(vv.x & 0xffff0000u), dup2(vv.y << 16),
+                                  dup2(vv.y & 0xffff0000u)};
 #pragma unroll
-          for (int h = 0; h < R; ++h) {
-            acc[h][0] = fmaf(pv[h], v0, acc[h][0]);
-            acc[h][1] = fmaf(pv[h], v1, acc[h][1]);
-          }
+          for (int h = 0; h < HP; ++h)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) acc[h][c] = fma2(pp[h], vd[c], acc[h][c]);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&pv_done[s]);
       }
       if (!alive) break;
-      // item end: add the two slot halves, write the partial sums
-      if (kh == 1) {
+      // item end: the four slot quarters are summed through `red` ([head][256] fp32), quarter 0 writes out
+      float* rp = red + 4 * dq;
+      for (int step = 3; step >= 0 && alive; --step) {
+        if (kq == step) {
 #pragma unroll
-        for (int h = 0; h < R; ++h) *reinterpret_cast<float2*>(red + h * 256 + 2 * dp) = make_float2(acc[h][0], acc[h][1]);
-      }
-      if (!(alive = sync_pv(0x62))) break;
-      if (kh == 0) {
-        float* out = a.part + ((size_t)bg * a.nsplit + split) * R * (D + 2);
+          for (int h = 0; h < HP; ++h) {
 #pragma unroll
-        for (int h = 0; h < R; ++h) {
-          const float2 o2 = *reinterpret_cast<const float2*>(red + h * 256 + 2 * dp);
-          out[h * (D + 2) + 2 * dp] = acc[h][0] + o2.x;
-          out[h * (D + 2) + 2 * dp + 1] = acc[h][1] + o2.y;
+            for (int e = 0; e < 2; ++e) {
+              const int hh = 2 * h + e;
+              if (hh < R) {
+                float4 v = make_float4(lo_hi(acc[h][0], e), lo_hi(acc[h][1], e), lo_hi(acc[h][2], e),
+                                       lo_hi(acc[h][3], e));
+                if (step < 3) {
+                  const float4 o = *reinterpret_cast<const float4*>(rp + hh * 256);
+                  v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
+                }
+                if (step > 0) {
+                  *reinterpret_cast<float4*>(rp + hh * 256) = v;
+                } else {
+                  float* out = a.part + (((size_t)bg * a.nsplit + split) * R + hh) * (D + 2) + 4 * dq;
+                  out[0] = v.x; out[1] = v.y; out[2] = v.z; out[3] = v.w;
+                }
+              }
+            }
+          }
         }
+        alive = sync_pv(0x62 + step);
       }
-      if (!(alive = sync_pv(0x63))) break;
     }
   }
   tc_fence_before();
@@ -471,7 +526,7 @@ int launch_win_dec(WinDecArgs a, cudaStream_t stream) {
   if (rc) return rc;
   CUtensorMap kmap, vmap;
   const uint64_t rows = (uint64_t)a.B * a.G * a.W;
-  rc = make_tmap_kmajor(&kmap, a.ring_k, BF_BF16, rows, 256, 256, kWT_N, 4);
+  rc = make_tmap_kmajor(&kmap, a.ring_k, BF_BF16, rows, 256, 256, kWT_N, 1);   // one 64-column atom per load
   if (rc) return rc;
   rc = make_tmap_kmajor(&vmap, a.ring_v, BF_BF16, rows, 256, 256, kWT_N, 4);
   if (rc) return rc;
