@@ -4,139 +4,220 @@
 // heimdall/hibrit.py:398-403:
 //   S <- a S (a = e^g);  delta = (v - S^T k) beta;  S <- S + k delta^T;  o_r = S^T q_r.
 // Because o_r = (aS)^T q_r + delta (k . q_r), the state is read once and written once:
-// one pass computes (aS)^T k and (aS)^T q_r together, the rank-1 update is applied in registers and
-// the new state is stored.  HBM traffic per (sequence, KV head) = 2 * D*D*4 bytes (+ vectors).
+// one pass computes (aS)^T k and (aS)^T q_r together, the rank-1 update follows, and the new state is
+// stored.  HBM traffic per (sequence, KV head) = 2 * D*D*4 bytes (+ vectors).
 //
-// Work split: columns of S (the Dv axis) are independent, so a CTA owns a 32-column block of one
-// (sequence, KV head) state; 256 threads = 8 column quads x 32 row groups; each thread keeps
-// D/32 rows x 4 columns of S in registers.  Loads/stores are float4 and each warp touches 4 full
-// 128-byte row segments per instruction.
+// Work split: columns of S (the Dv axis) are independent.  An item is one 32-column block of one
+// (sequence, KV head) state, a [D rows][32] fp32 tile.  Persistent CTAs (one per SM) stream items
+// through a ring of shared-memory stages: warp 8 issues one TMA per tile plus bulk copies of the item's
+// q_r and k vectors (and stages v and the gates), so several tiles are in flight per SM; compute warp w
+// owns column quad w over all rows (lane = rows lane + 32 i, so every column sum reduces inside the warp
+// with shuffles), writes the updated tile back over the stage, and warp 9 stores it with one TMA.
+#include "capi_internal.h"
 #include "common.cuh"
+#include "tmap.h"
 
 namespace bfb {
 
-constexpr int kDecCols = 32;     // columns of S per CTA
-constexpr int kDecThreads = 256;
+constexpr int kDecCols = 32;          // columns of S per item
 constexpr int kDecMaxR = 8;
+constexpr int kDecStages = 4;
+constexpr int kDecThreads = 320;      // warps 0-7 compute (one column quad each), warp 8 loads, warp 9 stores
+constexpr int kDecTile = 256 * kDecCols * 4;           // 32 KB (D = 256), 128-byte swizzled rows
+constexpr int kDecVec = (kDecMaxR + 1) * 256 * 4;      // q_r rows + k: 9 KB
+constexpr int kDecAux = 1024;                          // v slice (32 floats), g, beta
+constexpr int kDecStage = kDecTile + kDecVec + kDecAux;  // 42 KB, a multiple of 1024
+constexpr int kDecSmem = kDecStages * kDecStage + 256 + 1024;
 
-__global__ void __launch_bounds__(kDecThreads) gdn_decode_kernel(
-    const float* __restrict__ q, const float* __restrict__ k, const void* __restrict__ v, int v_bf16,
-    const float* __restrict__ g, const float* __restrict__ beta, const float* s_in, float* s_out,
-    float* __restrict__ o, int G, int R, int D) {
-  const int bg = blockIdx.y;             // (sequence, KV head)
-  const int col0 = blockIdx.x * kDecCols;
-  const int t = threadIdx.x;
-  const int cq = t & 7;                  // column quad within the block
-  const int rg = t >> 3;                 // row group 0..31
-  const int lane = t & 31, warp = t >> 5;
-  const int nrow = D >> 5;               // rows per thread
+// Warp reduce-scatter by recursive halving: 32 per-lane partial values in, lane l holds the warp total of
+// quantity l (31 shuffles instead of 32 butterflies of 5).
+__device__ __forceinline__ float reduce_scatter32(float (&v)[32], int lane) {
+#pragma unroll
+  for (int lvl = 16; lvl >= 1; lvl >>= 1) {
+    const bool up = (lane & lvl) != 0;
+#pragma unroll
+    for (int i = 0; i < lvl; ++i) {
+      const float send = up ? v[i] : v[i + lvl];
+      const float keep = up ? v[i + lvl] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, lvl);
+    }
+  }
+  return v[0];
+}
+// 16 quantities: lane l holds the total of quantity l >> 1
+__device__ __forceinline__ float reduce_scatter16(float (&v)[16], int lane) {
+#pragma unroll
+  for (int lvl = 16; lvl >= 2; lvl >>= 1) {
+    const bool up = (lane & lvl) != 0;
+    const int h = lvl >> 1;
+#pragma unroll
+    for (int i = 0; i < h; ++i) {
+      const float send = up ? v[i] : v[i + h];
+      const float keep = up ? v[i + h] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, lvl);
+    }
+  }
+  return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
+}
 
-  __shared__ float sk[256];
-  __shared__ float sq[kDecMaxR][256];
-  __shared__ float red[8][kDecMaxR + 1][kDecCols];   // per-warp partial column sums
-  __shared__ float kq[kDecMaxR];
-  __shared__ float delta_s[kDecCols];
+__global__ void __launch_bounds__(kDecThreads, 1) gdn_decode_kernel(
+    const __grid_constant__ CUtensorMap smap, const __grid_constant__ CUtensorMap omap, const float* __restrict__ q,
+    const float* __restrict__ k, const void* __restrict__ v, int v_bf16, const float* __restrict__ g,
+    const float* __restrict__ beta, float* __restrict__ o, int BG, int R, int D, unsigned int* err) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kDecStages * kDecStage);
+  uint64_t* full = bars;                       // [stages] TMA bytes + the loader warp's arrival
+  uint64_t* done = bars + kDecStages;          // [stages] 8 compute warps wrote the updated tile
+  uint64_t* empty = bars + 2 * kDecStages;     // [stages] the store of the stage has read it
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 3 * kDecStages);
 
-  const float* kp = k + (size_t)bg * D;
-  const float* qp = q + (size_t)bg * R * D;
-  for (int i = t; i < D; i += kDecThreads) sk[i] = kp[i];
-  for (int i = t; i < R * D; i += kDecThreads) sq[i / D][i % D] = qp[i];
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int ncb = D / kDecCols, nitems = BG * ncb;
+  const uint32_t tile_bytes = (uint32_t)D * kDecCols * 4;
+  if (t == 0) {
+    for (int i = 0; i < kDecStages; ++i) {
+      mbar_init(&full[i], 2);
+      mbar_init(&done[i], 8);
+      mbar_init(&empty[i], 1);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
   __syncthreads();
 
-  const float a = __expf(g[bg]);
-  const float bt = beta[bg];
-  const float* S = s_in + (size_t)bg * D * D;
-  float* So = s_out + (size_t)bg * D * D;
-
-  float4 s[8];
-  float pk[4] = {0.f, 0.f, 0.f, 0.f};
-  float pq[kDecMaxR][4];
+  if (warp == 8) {
+    // ------------------------------------------------------------------ loads: tile + q_r + k by TMA / bulk copy,
+    // the v slice and the gates with plain loads (all into the stage)
+    if (lane == 0) {
+      tma_prefetch(&smap);
+    }
+    int n = 0;
+    for (int item = blockIdx.x; item < nitems; item += gridDim.x, ++n) {
+      const int s = n % kDecStages;
+      if (n >= kDecStages && !mbar_wait_warp(&empty[s], ((n / kDecStages) - 1) & 1, abort_flag, err, 0x71)) break;
+      const int bg = item / ncb, col0 = (item % ncb) * kDecCols;
+      uint8_t* st = smem + s * kDecStage;
+      if (lane == 0) {
+        mbar_expect_tx(&full[s], tile_bytes + (uint32_t)(R + 1) * D * 4);
+        tma_load_2d(st, &smap, &full[s], col0, bg * D);
+        bulk_load_1d(st + kDecTile, q + (size_t)bg * R * D, (uint32_t)R * D * 4, &full[s]);
+        bulk_load_1d(st + kDecTile + kDecMaxR * 256 * 4, k + (size_t)bg * D, (uint32_t)D * 4, &full[s]);
+      }
+      float* aux = reinterpret_cast<float*>(st + kDecTile + kDecVec);
+      aux[lane] = v_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(v)[(size_t)bg * D + col0 + lane])
+                         : reinterpret_cast<const float*>(v)[(size_t)bg * D + col0 + lane];
+      if (lane == 0) {
+        aux[32] = __expf(g[bg]);
+        aux[33] = beta[bg];
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full[s]);
+    }
+    // drain: the last TMA loads land before the CTA ends
+    if (lane == 0) {
+      const int last = n - 1;
+      for (int j = last; j >= 0 && j > last - kDecStages; --j)
+        mbar_wait(&full[j % kDecStages], (j / kDecStages) & 1, nullptr, err, 0x72);
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------------ stores: the updated tile by TMA
+    if (lane == 0) {
+      tma_prefetch(&omap);
+      int n = 0;
+      for (int item = blockIdx.x; item < nitems; item += gridDim.x, ++n) {
+        const int s = n % kDecStages;
+        if (!mbar_wait(&done[s], (n / kDecStages) & 1, abort_flag, err, 0x76)) break;
+        const int bg = item / ncb, col0 = (item % ncb) * kDecCols;
+        tma_store_2d(&omap, smem + s * kDecStage, col0, bg * D);
+        tma_store_commit();
+        tma_store_wait_read();
+        mbar_arrive(&empty[s]);
+      }
+      tma_store_wait_all();
+    }
+  } else {
+    // ------------------------------------------------------------------ compute: warp w = column quad w,
+    // lane = rows lane + 32 i; column sums reduce inside the warp
+    const int nrow = D >> 5;
+    int n = 0;
+    for (int item = blockIdx.x; item < nitems; item += gridDim.x, ++n) {
+      const int s = n % kDecStages;
+      if (!mbar_wait_warp(&full[s], (n / kDecStages) & 1, abort_flag, err, 0x73)) break;
+      const int bg = item / ncb, col0 = (item % ncb) * kDecCols;
+      uint8_t* tile = smem + s * kDecStage;
+      const float* sq = reinterpret_cast<const float*>(tile + kDecTile);      // [R][D]
+      const float* sk = sq + kDecMaxR * 256;                                   // [D]
+      const float* aux = reinterpret_cast<const float*>(tile + kDecTile + kDecVec);
+      const float a = aux[32], bt = aux[33];
+      float4 x[8];
+      float kr[8];
+      float pk[4] = {0.f, 0.f, 0.f, 0.f};
+      float pq[kDecMaxR][4];
 #pragma unroll
-  for (int r = 0; r < kDecMaxR; ++r) pq[r][0] = pq[r][1] = pq[r][2] = pq[r][3] = 0.f;
-
+      for (int r = 0; r < kDecMaxR; ++r) pq[r][0] = pq[r][1] = pq[r][2] = pq[r][3] = 0.f;
+      float kq[kDecMaxR];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    if (i < nrow) {
-      const int row = rg + 32 * i;
-      float4 x = *reinterpret_cast<const float4*>(S + (size_t)row * D + col0 + cq * 4);
-      x.x *= a; x.y *= a; x.z *= a; x.w *= a;
-      s[i] = x;
-      const float kr = sk[row];
-      pk[0] += kr * x.x; pk[1] += kr * x.y; pk[2] += kr * x.z; pk[3] += kr * x.w;
+      for (int r = 0; r < kDecMaxR; ++r) kq[r] = 0.f;
 #pragma unroll
-      for (int r = 0; r < kDecMaxR; ++r) {
-        if (r < R) {
-          const float qr = sq[r][row];
-          pq[r][0] += qr * x.x; pq[r][1] += qr * x.y; pq[r][2] += qr * x.z; pq[r][3] += qr * x.w;
+      for (int i = 0; i < 8; ++i) {
+        if (i < nrow) {
+          const int row = lane + 32 * i;
+          float4 y = *reinterpret_cast<const float4*>(tile + row * 128 + ((warp ^ (row & 7)) << 4));
+          y.x *= a; y.y *= a; y.z *= a; y.w *= a;
+          x[i] = y;
+          kr[i] = sk[row];
+          pk[0] += kr[i] * y.x; pk[1] += kr[i] * y.y; pk[2] += kr[i] * y.z; pk[3] += kr[i] * y.w;
+#pragma unroll
+          for (int r = 0; r < kDecMaxR; ++r) {
+            if (r < R) {
+              const float qv = sq[r * D + row];
+              pq[r][0] += qv * y.x; pq[r][1] += qv * y.y; pq[r][2] += qv * y.z; pq[r][3] += qv * y.w;
+              kq[r] += qv * kr[i];
+            }
+          }
         }
       }
-    }
-  }
-  // reduce over the 4 row groups sharing this column quad inside the warp (lanes l, l^8, l^16, l^24)
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    pk[c] += __shfl_xor_sync(0xffffffffu, pk[c], 8);
-    pk[c] += __shfl_xor_sync(0xffffffffu, pk[c], 16);
-#pragma unroll
-    for (int r = 0; r < kDecMaxR; ++r) {
-      pq[r][c] += __shfl_xor_sync(0xffffffffu, pq[r][c], 8);
-      pq[r][c] += __shfl_xor_sync(0xffffffffu, pq[r][c], 16);
-    }
-  }
-  if (lane < 8) {
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      red[warp][0][cq * 4 + c] = pk[c];
+      // column totals: A = q_r . (aS)[:, c] (quantity 4r + c), B = k . (aS)[:, c] (quantity c) and k . q_r (4 + r)
+      float va[32], vb[16];
 #pragma unroll
       for (int r = 0; r < kDecMaxR; ++r)
-        if (r < R) red[warp][r + 1][cq * 4 + c] = pq[r][c];
-    }
-  }
-  // k . q_r (same for every column block; warp r computes head r)
-  if (warp < R) {
-    float acc = 0.f;
-    for (int i = lane; i < D; i += 32) acc += sk[i] * sq[warp][i];
-    acc = warp_sum(acc);
-    if (lane == 0) kq[warp] = acc;
-  }
-  __syncthreads();
-  // finish the column sums: thread (quantity j, column c) over the 8 warps
-  for (int idx = t; idx < (R + 1) * kDecCols; idx += kDecThreads) {
-    const int j = idx / kDecCols, c = idx % kDecCols;
-    float acc = 0.f;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) acc += red[w][j][c];
-    red[0][j][c] = acc;
-  }
-  __syncthreads();
-  if (t < kDecCols) {
-    const int col = col0 + t;
-    float vv;
-    if (v_bf16) {
-      vv = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(v)[(size_t)bg * D + col]);
-    } else {
-      vv = reinterpret_cast<const float*>(v)[(size_t)bg * D + col];
-    }
-    delta_s[t] = (vv - red[0][0][t]) * bt;
-  }
-  __syncthreads();
-  // outputs o_r[col] = (aS)^T q_r + delta * (k . q_r)
-  for (int idx = t; idx < R * kDecCols; idx += kDecThreads) {
-    const int r = idx / kDecCols, c = idx % kDecCols;
-    o[((size_t)bg * R + r) * D + col0 + c] = red[0][r + 1][c] + delta_s[c] * kq[r];
-  }
-  // rank-1 update in registers and store
-  float d4[4];
+        for (int c = 0; c < 4; ++c) va[4 * r + c] = pq[r][c];
 #pragma unroll
-  for (int c = 0; c < 4; ++c) d4[c] = delta_s[cq * 4 + c];
+      for (int c = 0; c < 4; ++c) vb[c] = pk[c];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    if (i < nrow) {
-      const int row = rg + 32 * i;
-      const float kr = sk[row];
-      float4 x = s[i];
-      x.x += kr * d4[0]; x.y += kr * d4[1]; x.z += kr * d4[2]; x.w += kr * d4[3];
-      *reinterpret_cast<float4*>(So + (size_t)row * D + col0 + cq * 4) = x;
+      for (int r = 0; r < kDecMaxR; ++r) vb[4 + r] = kq[r];
+#pragma unroll
+      for (int i = 12; i < 16; ++i) vb[i] = 0.f;
+      const float ta = reduce_scatter32(va, lane);
+      const float tb = reduce_scatter16(vb, lane);
+      float d4[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) d4[c] = (aux[warp * 4 + c] - __shfl_sync(0xffffffffu, tb, 2 * c)) * bt;
+      // outputs o_r[col] = (aS)^T q_r + delta * (k . q_r): lane 4r + c holds head r, column 4w + c
+      {
+        const int r = lane >> 2, c = lane & 3;
+        const float kqr = __shfl_sync(0xffffffffu, tb, 2 * (4 + r));
+        const float dc = (c == 0) ? d4[0] : (c == 1) ? d4[1] : (c == 2) ? d4[2] : d4[3];
+        if (r < R) o[((size_t)bg * R + r) * D + col0 + warp * 4 + c] = ta + dc * kqr;
+      }
+      // rank-1 update written back over the tile (the store warp copies it out)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (i < nrow) {
+          const int row = lane + 32 * i;
+          float4 y = x[i];
+          y.x = fmaf(kr[i], d4[0], y.x);
+          y.y = fmaf(kr[i], d4[1], y.y);
+          y.z = fmaf(kr[i], d4[2], y.z);
+          y.w = fmaf(kr[i], d4[3], y.w);
+          *reinterpret_cast<float4*>(tile + row * 128 + ((warp ^ (row & 7)) << 4)) = y;
+        }
+      }
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&done[s]);
     }
   }
 }
@@ -144,8 +225,30 @@ __global__ void __launch_bounds__(kDecThreads) gdn_decode_kernel(
 int launch_gdn_decode(const float* q, const float* k, const void* v, int v_bf16, const float* g,
                       const float* beta, const float* s_in, float* s_out, float* o, int B, int G, int R, int D,
                       cudaStream_t stream) {
-  dim3 grid(D / kDecCols, B * G);
-  gdn_decode_kernel<<<grid, kDecThreads, 0, stream>>>(q, k, v, v_bf16, g, beta, s_in, s_out, o, G, R, D);
+  if (D % kDecCols || D > 256 || R < 1 || R > kDecMaxR) return BF_ERR_UNSUPPORTED;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(s_in) || !aligned16(s_out)) return BF_ERR_ALIGNMENT;
+  DeviceState st;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  // S as [B*G*D rows][D] fp32; an item is a [D][32] box (128-byte rows, 128-byte swizzle)
+  CUtensorMap smap, omap;
+  const uint64_t dims[2] = {(uint64_t)D, (uint64_t)B * G * D};
+  const uint64_t strides[1] = {(uint64_t)D * 4};
+  const uint32_t box[2] = {(uint32_t)kDecCols, (uint32_t)D};
+  rc = make_tmap(&smap, s_in, BF_F32, 2, dims, strides, box, true);
+  if (rc) return rc;
+  rc = make_tmap(&omap, s_out, BF_F32, 2, dims, strides, box, true);
+  if (rc) return rc;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(gdn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDecSmem) != cudaSuccess)
+      return BF_ERR_CUDA;
+    attr = true;
+  }
+  const int nitems = B * G * (D / kDecCols);
+  const int grid = nitems < st.sm_count ? nitems : st.sm_count;
+  gdn_decode_kernel<<<grid, kDecThreads, kDecSmem, stream>>>(smap, omap, q, k, v, v_bf16, g, beta, o, B * G, R, D,
+                                                            st.err);
   return cudaGetLastError() == cudaSuccess ? BF_OK : BF_ERR_CUDA;
 }
 
