@@ -12,7 +12,7 @@ int launch_head_proj(const __nv_bfloat16* q, const __nv_bfloat16* k, const __hal
 int launch_x_proj(const __nv_bfloat16* x, const __nv_bfloat16* w_x, const float* ab_b, const float* mix_b,
                   const float* A_log, const float* dt_bias, const float* decay_mask, float* g, float* beta,
                   float* mixx, const int64_t* pos, long long pos0, int M, int T, int d, int G, int H, int sinks,
-                  unsigned int* err, cudaStream_t stream);
+                  float* scratch, size_t scratch_bytes, unsigned int* err, cudaStream_t stream);
 
 size_t win_dec_workspace(int B, int G, int R, int D, int W);
 int launch_gather_evicted(const float* ring_km, const __nv_bfloat16* ring_v, const float* ring_g,
@@ -42,13 +42,14 @@ int check_layer(const bf_layer* L) {
   return BF_OK;
 }
 
+// `scratch` (nullable): device memory the small-row x projection may use for its split-K partials
 int mem_inputs_impl(const DeviceState& st, const bf_layer* L, const void* x, const void* q, const void* k,
                     const int64_t* pos, long long pos0, int B, int T, float* qm, float* km, float* g, float* beta,
-                    float* mixx, cudaStream_t stream, __half* qm16) {
+                    float* mixx, cudaStream_t stream, __half* qm16, float* scratch, size_t scratch_bytes) {
   stage_mark(ST_XPROJ, 0, stream);
   int rc = launch_x_proj(static_cast<const __nv_bfloat16*>(x), weights_x(L->wbuf, L->H, L->G, L->D), L->ab_b,
                          L->mix_b, L->A_log, L->dt_bias, L->decay_mask, g, beta, mixx, pos, pos0, B * T, T, L->d,
-                         L->G, L->H, L->sinks, st.err, stream);
+                         L->G, L->H, L->sinks, scratch, scratch_bytes, st.err, stream);
   if (rc) return rc;
   stage_mark(ST_XPROJ, 1, stream);
   stage_mark(ST_HEADPROJ, 0, stream);
@@ -102,7 +103,7 @@ int bf_mem_inputs(const bf_layer* L, const void* x, const void* q, const void* k
   DeviceState st;
   rc = device_state(&st);
   if (rc) return rc;
-  return mem_inputs_impl(st, L, x, q, k, pos, pos0, B, T, qm, km, g, beta, mixx, stream, nullptr);
+  return mem_inputs_impl(st, L, x, q, k, pos, pos0, B, T, qm, km, g, beta, mixx, stream, nullptr, nullptr, 0);
 }
 
 size_t bf_layer_decode_workspace(int B, int H, int G, int D, int window) {
@@ -158,7 +159,9 @@ int bf_bifrost_layer_decode(const bf_layer* L, const void* x, const void* q, con
   float* part = reinterpret_cast<float*>(take(win_dec_workspace(B, G, R, D, W)));
 
   // memory inputs of the new tokens (T = 1 per sequence, per-sequence positions)
-  rc = mem_inputs_impl(st, L, x, q, k, pos, 0, B, 1, qm, km, g, beta, mixx, stream, nullptr);
+  // o_mem is first written by the state update, after the projections: it is their split-K scratch
+  rc = mem_inputs_impl(st, L, x, q, k, pos, 0, B, 1, qm, km, g, beta, mixx, stream, nullptr, o_mem,
+                       (size_t)B * H * D * 4);
   if (rc) return rc;
   if (memory) {
     // the token leaving the window (position p - W) is written into memory before the read

@@ -362,60 +362,96 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
-// x_proj for few rows (decode): one CTA per row, warp w forms outputs 4w..4w+3 as dot products of the row
-// with the same hi and lo bf16 weight rows the tensor-core path uses (x*hi + x*lo in fp32), then the same
-// epilogue.  A 128-row tensor-core tile would walk all d columns in one CTA for a handful of rows.
-constexpr int kXP_SmallRows = 256;
+// x_proj for few rows (decode) as split-K: CTA = (slice of 128 columns of d, block of 32 rows).  The x and
+// weight slices are staged in shared memory as fp32 (weights = hi + lo, the same values the tensor-core path
+// multiplies), each thread forms 4 outputs of one row over the slice, and the partial sums go to a scratch
+// array [slice][row][32]; x_proj_finish_kernel adds the slices and applies the epilogue.  A 128-row
+// tensor-core tile would instead walk all d columns in one CTA for a handful of rows.
+constexpr int kXS_C = 128;           // columns per slice
+constexpr int kXS_Rows = 32;         // rows per CTA
+constexpr int kXS_MaxRows = 256;     // the split-K path serves up to this many rows
 
-__global__ void __launch_bounds__(256) x_proj_small_kernel(const __nv_bfloat16* __restrict__ x,
-                                                           const __nv_bfloat16* __restrict__ w_x, XProjArgs a) {
-  __shared__ float rs[32];
-  const int m = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)m * a.d);
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int c = lane; c < a.d / 8; c += 32) {
-    float xf[8];
-    {
-      const uint4 u = __ldg(xr + c);
-      const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+__global__ void __launch_bounds__(256) x_proj_split_kernel(const __nv_bfloat16* __restrict__ x,
+                                                           const __nv_bfloat16* __restrict__ w_x, int M, int d,
+                                                           float* __restrict__ part) {
+  __shared__ __align__(16) float xs[kXS_Rows][kXS_C + 4];   // padded rows: conflict-free 16-byte reads
+  __shared__ __align__(16) float ws[32][kXS_C + 4];
+  const int t = threadIdx.x;
+  const int c0 = blockIdx.x * kXS_C, m0 = blockIdx.y * kXS_Rows;
+  const int nc = min(kXS_C, d - c0);
+  // stage x (bf16 -> fp32) and w = hi + lo: 8 columns per 16-byte load
+  for (int i = t; i < kXS_Rows * (kXS_C / 8); i += 256) {
+    const int r = i / (kXS_C / 8), c8 = (i % (kXS_C / 8)) * 8;
+    uint4 u = make_uint4(0u, 0u, 0u, 0u);
+    if (m0 + r < M && c8 < nc) u = __ldg(reinterpret_cast<const uint4*>(x + (size_t)(m0 + r) * d + c0 + c8));
+    const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        xf[2 * e] = __uint_as_float(w4[e] << 16);
-        xf[2 * e + 1] = __uint_as_float(w4[e] & 0xffff0000u);
-      }
-    }
-#pragma unroll
-    for (int o = 0; o < 4; ++o) {
-      const int j = warp * 4 + o;
-      const uint4 hi = __ldg(reinterpret_cast<const uint4*>(w_x + (size_t)j * a.d) + c);
-      const uint4 lo = __ldg(reinterpret_cast<const uint4*>(w_x + (size_t)(32 + j) * a.d) + c);
-      const uint32_t h4[4] = {hi.x, hi.y, hi.z, hi.w}, l4[4] = {lo.x, lo.y, lo.z, lo.w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        acc[o] = fmaf(xf[2 * e], __uint_as_float(h4[e] << 16) + __uint_as_float(l4[e] << 16), acc[o]);
-        acc[o] = fmaf(xf[2 * e + 1], __uint_as_float(h4[e] & 0xffff0000u) + __uint_as_float(l4[e] & 0xffff0000u),
-                      acc[o]);
-      }
+    for (int e = 0; e < 4; ++e) {
+      xs[r][c8 + 2 * e] = __uint_as_float(w4[e] << 16);
+      xs[r][c8 + 2 * e + 1] = __uint_as_float(w4[e] & 0xffff0000u);
     }
   }
+  for (int i = t; i < 32 * (kXS_C / 8); i += 256) {
+    const int j = i / (kXS_C / 8), c8 = (i % (kXS_C / 8)) * 8;
+    uint4 hi = make_uint4(0u, 0u, 0u, 0u), lo = hi;
+    if (c8 < nc) {
+      hi = __ldg(reinterpret_cast<const uint4*>(w_x + (size_t)j * d + c0 + c8));
+      lo = __ldg(reinterpret_cast<const uint4*>(w_x + (size_t)(32 + j) * d + c0 + c8));
+    }
+    const uint32_t h4[4] = {hi.x, hi.y, hi.z, hi.w}, l4[4] = {lo.x, lo.y, lo.z, lo.w};
 #pragma unroll
-  for (int o = 0; o < 4; ++o) {
-    const float v = warp_sum(acc[o]);
-    if (lane == 0) rs[warp * 4 + o] = v;
+    for (int e = 0; e < 4; ++e) {
+      ws[j][c8 + 2 * e] = __uint_as_float(h4[e] << 16) + __uint_as_float(l4[e] << 16);
+      ws[j][c8 + 2 * e + 1] = __uint_as_float(h4[e] & 0xffff0000u) + __uint_as_float(l4[e] & 0xffff0000u);
+    }
   }
   __syncthreads();
-  const int G = a.G, H = a.H, t = threadIdx.x;
-  if (t < G) {
-    const long long p = a.pos ? (long long)a.pos[m] : a.pos0 + (m % a.T);
-    const float av = rs[t] + a.ab_b[t];
-    const float bv = rs[G + t] + a.ab_b[G + t];
-    const float z = av + a.dt_bias[t];
-    const float sp = z > 20.f ? z : log1pf(__expf(z));
-    a.g[(size_t)m * G + t] = -__expf(a.A_log[t]) * sp * a.decay_mask[t];
-    a.beta[(size_t)m * G + t] = (p >= a.sinks) ? 1.f / (1.f + __expf(-bv)) : 0.f;
-  } else if (t < G + H) {
-    a.mixx[(size_t)m * H + (t - G)] = rs[2 * G + (t - G)] + a.mix_b[t - G];
+  // thread = (row t / 8, outputs 4 (t % 8) .. + 3)
+  const int r = t >> 3, j0 = (t & 7) * 4;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+  for (int c = 0; c < kXS_C; c += 4) {
+    const float4 xv = *reinterpret_cast<const float4*>(&xs[r][c]);
+#pragma unroll
+    for (int o = 0; o < 4; ++o) {
+      const float4 wv = *reinterpret_cast<const float4*>(&ws[j0 + o][c]);
+      acc[o] = fmaf(xv.x, wv.x, fmaf(xv.y, wv.y, fmaf(xv.z, wv.z, fmaf(xv.w, wv.w, acc[o]))));
+    }
   }
+  if (m0 + r < M)
+    *reinterpret_cast<float4*>(part + ((size_t)blockIdx.x * M + m0 + r) * 32 + j0) =
+        make_float4(acc[0], acc[1], acc[2], acc[3]);
+}
+
+// sums the slices of x_proj_split_kernel and applies the x_proj epilogue; 8 rows per CTA, thread = (row, output)
+__global__ void __launch_bounds__(256) x_proj_finish_kernel(const float* __restrict__ part, int nslices, XProjArgs a) {
+  __shared__ float rs[8][33];
+  const int t = threadIdx.x, rl = t >> 5, j = t & 31;
+  const int m = blockIdx.x * 8 + rl;
+  if (m < a.M) {
+    float acc = 0.f;
+#pragma unroll 8
+    for (int sl = 0; sl < nslices; ++sl) acc += part[((size_t)sl * a.M + m) * 32 + j];
+    rs[rl][j] = acc;
+  }
+  __syncwarp();
+  if (m >= a.M) return;
+  const int G = a.G, H = a.H;
+  if (j < G) {
+    const long long p = a.pos ? (long long)a.pos[m] : a.pos0 + (m % a.T);
+    const float av = rs[rl][j] + a.ab_b[j];
+    const float bv = rs[rl][G + j] + a.ab_b[G + j];
+    const float z = av + a.dt_bias[j];
+    const float sp = z > 20.f ? z : log1pf(__expf(z));
+    a.g[(size_t)m * G + j] = -__expf(a.A_log[j]) * sp * a.decay_mask[j];
+    a.beta[(size_t)m * G + j] = (p >= a.sinks) ? 1.f / (1.f + __expf(-bv)) : 0.f;
+  } else if (j < G + H) {
+    a.mixx[(size_t)m * H + (j - G)] = rs[rl][2 * G + (j - G)] + a.mix_b[j - G];
+  }
+}
+
+size_t x_proj_scratch_bytes(int M, int d) {
+  return M <= kXS_MaxRows ? (size_t)((d + kXS_C - 1) / kXS_C) * M * 32 * sizeof(float) : 0;
 }
 
 // ============================================================================ launchers
@@ -463,10 +499,13 @@ int launch_head_proj(const __nv_bfloat16* q, const __nv_bfloat16* k, const __hal
 int launch_x_proj(const __nv_bfloat16* x, const __nv_bfloat16* w_x, const float* ab_b, const float* mix_b,
                   const float* A_log, const float* dt_bias, const float* decay_mask, float* g, float* beta,
                   float* mixx, const int64_t* pos, long long pos0, int M, int T, int d, int G, int H, int sinks,
-                  unsigned int* err, cudaStream_t stream) {
-  if (M <= kXP_SmallRows && d % 8 == 0) {
+                  float* scratch, size_t scratch_bytes, unsigned int* err, cudaStream_t stream) {
+  const size_t need = x_proj_scratch_bytes(M, d);
+  if (need && scratch && scratch_bytes >= need && d % 8 == 0) {
+    const int nslices = (d + kXS_C - 1) / kXS_C;
+    x_proj_split_kernel<<<dim3(nslices, (M + kXS_Rows - 1) / kXS_Rows), 256, 0, stream>>>(x, w_x, M, d, scratch);
     XProjArgs a{ab_b, mix_b, A_log, dt_bias, decay_mask, nullptr, g, beta, mixx, pos, pos0, M, T, d, G, H, sinks, err};
-    x_proj_small_kernel<<<M, 256, 0, stream>>>(x, w_x, a);
+    x_proj_finish_kernel<<<(M + 7) / 8, 256, 0, stream>>>(scratch, nslices, a);
     return cudaGetLastError() == cudaSuccess ? BF_OK : BF_ERR_CUDA;
   }
   CUtensorMap xmap, wmap;

@@ -11,7 +11,7 @@ int launch_head_proj(const __nv_bfloat16* q, const __nv_bfloat16* k, const __hal
                      float* km, int B, int T, int H, int G, int sm_count, unsigned int* err, cudaStream_t stream);
 int mem_inputs_impl(const DeviceState& st, const bf_layer* L, const void* x, const void* q, const void* k,
                     const int64_t* pos, long long pos0, int B, int T, float* qm, float* km, float* g, float* beta,
-                    float* mixx, cudaStream_t stream, __half* qm16);
+                    float* mixx, cudaStream_t stream, __half* qm16, float* scratch, size_t scratch_bytes);
 int check_layer(const bf_layer* L);
 size_t gdn_prefill_workspace(int B, int G, int T_steps);
 int gdn_prefill_carve(GdnStreams& s, void* ws);
@@ -247,7 +247,7 @@ int bf_bifrost_layer_prefill(const bf_layer* L, const void* x, const void* q, co
 
   // 1. memory inputs (projections on tcgen05)
   if (use_mem || C) {
-    rc = mem_inputs_impl(st, L, x, q, k, nullptr, start, B, T, nullptr, km, g, beta, mixx, stream, qm16);
+    rc = mem_inputs_impl(st, L, x, q, k, nullptr, start, B, T, nullptr, km, g, beta, mixx, stream, qm16, nullptr, 0);
     if (rc) return rc;
   }
   // 2. memory: the write stream is delayed by W (token i enters memory when it leaves the window)

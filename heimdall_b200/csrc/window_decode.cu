@@ -401,76 +401,97 @@ __global__ void __launch_bounds__(kWT_Threads, 1)
   }
 }
 
+// Combine: CTA = (sequence, KV head, query head), thread = value column (D = 256).  Every load is issued before
+// the arithmetic that needs it: the split statistics and the extra-key scores first, then the split partial
+// sums, the extra keys' values and the memory read of the mix, so a CTA costs about two DRAM round trips.
+constexpr int kWD_MaxSplits = 16;
+constexpr int kWD_MaxExtra = 8;
+
 __global__ void __launch_bounds__(kWD_Threads) win_dec_combine_kernel(WinDecArgs a) {
-  const int bg = blockIdx.x;
+  const int bg = blockIdx.x, h = blockIdx.y;
   const int b = bg / a.G, g = bg % a.G;
-  const int D = a.D, R = a.R;
+  const int D = a.D, R = a.R, ns = a.nsplit;
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const long long p = a.pos[b];
-  const float scale = rsqrtf((float)D);
-  __shared__ float s_extra[kWD_MaxR][8];   // scores of the extra keys: sinks (<= 4..7) + the new token
-  __shared__ float s_stat[kWD_MaxR][2];
-  const int nx = a.ns + (p >= a.S ? 1 : 0);  // extra keys
-  // ---- scores of the extra keys: pair (h, key) per warp iteration
-  for (int pr = warp; pr < R * nx; pr += 8) {
-    const int h = pr / nx, e = pr % nx;
+  const int hh = g * R + h;
+  const size_t qrow = (size_t)b * a.G * R + hh;
+  __shared__ float s_ms[kWD_MaxSplits], s_ls[kWD_MaxSplits], s_extra[kWD_MaxExtra];
+  const int nx = a.ns + (p >= a.S ? 1 : 0);  // extra keys: the sinks and, once past them, the new token
+  const float* part = a.part + ((size_t)bg * ns * R + h) * (D + 2);   // split s at + s * R * (D + 2)
+  if (t < ns) {
+    s_ms[t] = part[(size_t)t * R * (D + 2) + D];
+    s_ls[t] = part[(size_t)t * R * (D + 2) + D + 1];
+  }
+  if (warp < nx) {   // extra key e = warp: one 16-byte load of q and k per lane
+    const int e = warp;
     const __nv_bfloat16* kp = (e < a.ns) ? a.sink_k + (((size_t)b * a.G + g) * a.ns + e) * D
                                          : a.kr + ((size_t)b * a.G + g) * D;
-    const __nv_bfloat16* qp = a.qr + ((size_t)b * a.G * R + g * R + h) * D;
-    float s = 0.f;
-    for (int dd = lane; dd < D; dd += 32) s += __bfloat162float(qp[dd]) * __bfloat162float(kp[dd]);
-    s = warp_sum(s) * scale;
-    if (lane == 0) s_extra[h][e] = s;
+    const uint4 qv = __ldg(reinterpret_cast<const uint4*>(a.qr + qrow * D) + lane);
+    const uint4 kv = __ldg(reinterpret_cast<const uint4*>(kp) + lane);
+    const uint32_t q4[4] = {qv.x, qv.y, qv.z, qv.w}, k4[4] = {kv.x, kv.y, kv.z, kv.w};
+    float sdot = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      sdot = fmaf(__uint_as_float(q4[i] << 16), __uint_as_float(k4[i] << 16), sdot);
+      sdot = fmaf(__uint_as_float(q4[i] & 0xffff0000u), __uint_as_float(k4[i] & 0xffff0000u), sdot);
+    }
+    sdot = warp_sum(sdot) * rsqrtf((float)D);
+    if (lane == 0) s_extra[e] = sdot;
   }
+  // this column's loads, all in flight together
+  float pv[kWD_MaxSplits], ev[kWD_MaxExtra];
+#pragma unroll
+  for (int s2 = 0; s2 < kWD_MaxSplits; ++s2) pv[s2] = s2 < ns ? part[(size_t)s2 * R * (D + 2) + t] : 0.f;
+#pragma unroll
+  for (int e = 0; e < kWD_MaxExtra; ++e) {
+    ev[e] = 0.f;
+    if (e < nx) {
+      const __nv_bfloat16* vp = (e < a.ns) ? a.sink_v + (((size_t)b * a.G + g) * a.ns + e) * D
+                                           : a.v + ((size_t)b * a.G + g) * D;
+      ev[e] = __bfloat162float(vp[t]);
+    }
+  }
+  const bool gate_on = a.o_mem && p >= a.W;
+  const float om = gate_on ? a.o_mem[qrow * D + t] : 0.f;
+  const float mx = gate_on ? a.mixx[qrow] : 0.f;
   __syncthreads();
-  // ---- merge split partials + extra keys (thread t = column)
-  const float* part = a.part + (size_t)bg * a.nsplit * R * (D + 2);
-  for (int h = 0; h < R; ++h) {
-    float m = -INFINITY;
-    for (int s = 0; s < a.nsplit; ++s) m = fmaxf(m, part[(s * R + h) * (D + 2) + D]);
-    for (int e = 0; e < nx; ++e) m = fmaxf(m, s_extra[h][e]);
-    float l = 0.f, acc = 0.f;
-    for (int s = 0; s < a.nsplit; ++s) {
-      const float* ps = part + (s * R + h) * (D + 2);
-      const float ms = ps[D];
-      if (ms == -INFINITY) continue;
-      const float f = __expf(ms - m);
-      l += ps[D + 1] * f;
-      if (t < D) acc += ps[t] * f;
+  float m = -INFINITY;
+  for (int s2 = 0; s2 < ns; ++s2) m = fmaxf(m, s_ms[s2]);
+  for (int e = 0; e < nx; ++e) m = fmaxf(m, s_extra[e]);
+  float l = 0.f, acc = 0.f;
+#pragma unroll
+  for (int s2 = 0; s2 < kWD_MaxSplits; ++s2) {
+    if (s2 < ns && s_ms[s2] != -INFINITY) {
+      const float f = __expf(s_ms[s2] - m);
+      l = fmaf(s_ls[s2], f, l);
+      acc = fmaf(pv[s2], f, acc);
     }
-    for (int e = 0; e < nx; ++e) {
-      const float f = __expf(s_extra[h][e] - m);
-      l += f;
-      if (t < D) {
-        const __nv_bfloat16* vp = (e < a.ns) ? a.sink_v + (((size_t)b * a.G + g) * a.ns + e) * D
-                                             : a.v + ((size_t)b * a.G + g) * D;
-        acc += f * __bfloat162float(vp[t]);
-      }
-    }
-    const int hh = g * R + h;
-    const float lse = m + logf(l);
-    if (t < D) {
-      const float ow = acc / l;
-      float res = ow;
-      if (a.o_mem && p >= a.W) {
-        const float z = a.mixx[(size_t)b * a.G * R + hh] + a.mix_lse[hh] * (lse - logf((float)a.W));
-        const float gam = 1.f / (1.f + __expf(-z));
-        res = ow + gam * (a.mem_scale[hh] * a.o_mem[((size_t)b * a.G * R + hh) * D + t] - ow);
-      }
-      a.o[((size_t)b * a.G * R + hh) * D + t] = res;
-    }
-    if (t == 0 && a.lse_out) a.lse_out[(size_t)b * a.G * R + hh] = lse;
-    (void)s_stat;
   }
-  // ---- ring write of the new token
-  if (a.ring_km) {
+#pragma unroll
+  for (int e = 0; e < kWD_MaxExtra; ++e) {
+    if (e < nx) {
+      const float f = __expf(s_extra[e] - m);
+      l += f;
+      acc = fmaf(f, ev[e], acc);
+    }
+  }
+  const float lse = m + logf(l);
+  const float ow = acc / l;
+  float res = ow;
+  if (gate_on) {
+    const float z = mx + a.mix_lse[hh] * (lse - logf((float)a.W));
+    const float gam = 1.f / (1.f + __expf(-z));
+    res = ow + gam * (a.mem_scale[hh] * om - ow);
+  }
+  a.o[qrow * D + t] = res;
+  if (t == 0 && a.lse_out) a.lse_out[qrow] = lse;
+  // ring write of the new token (once per sequence and KV head)
+  if (a.ring_km && h == 0) {
     const int slot = (int)(p % a.W);
     const size_t kv = (((size_t)b * a.G + g) * a.W + slot) * D;
-    for (int dd = t; dd < D; dd += kWD_Threads) {
-      a.ring_k_w[kv + dd] = a.kr[((size_t)b * a.G + g) * D + dd];
-      a.ring_v_w[kv + dd] = a.v[((size_t)b * a.G + g) * D + dd];
-      a.ring_km[(((size_t)b * a.W + slot) * a.G + g) * D + dd] = a.km[((size_t)b * a.G + g) * D + dd];
-    }
+    a.ring_k_w[kv + t] = a.kr[((size_t)b * a.G + g) * D + t];
+    a.ring_v_w[kv + t] = a.v[((size_t)b * a.G + g) * D + t];
+    a.ring_km[(((size_t)b * a.W + slot) * a.G + g) * D + t] = a.km[((size_t)b * a.G + g) * D + t];
     if (t == 0) {
       a.ring_g[((size_t)b * a.W + slot) * a.G + g] = a.g_new[(size_t)b * a.G + g];
       a.ring_beta[((size_t)b * a.W + slot) * a.G + g] = a.beta_new[(size_t)b * a.G + g];
@@ -520,7 +541,9 @@ static int launch_split(const CUtensorMap& kmap, const CUtensorMap& vmap, const 
 
 int launch_win_dec(WinDecArgs a, cudaStream_t stream) {
   a.nsplit = (a.W + kWD_Keys - 1) / kWD_Keys;
-  if (a.D != 256 || a.R < 1 || a.R > kWD_MaxR) return BF_ERR_UNSUPPORTED;
+  if (a.D != 256 || a.R < 1 || a.R > kWD_MaxR || a.nsplit > kWD_MaxSplits || a.ns + 1 > kWD_MaxExtra)
+    return BF_ERR_UNSUPPORTED;
+  if (!aligned16(a.qr) || !aligned16(a.kr) || (a.ns && !aligned16(a.sink_k))) return BF_ERR_ALIGNMENT;
   DeviceState st;
   int rc = device_state(&st);
   if (rc) return rc;
@@ -543,7 +566,7 @@ int launch_win_dec(WinDecArgs a, cudaStream_t stream) {
     default: rc = launch_split<8>(kmap, vmap, a, grid, st.err, stream); break;
   }
   if (rc) return rc;
-  win_dec_combine_kernel<<<a.B * a.G, kWD_Threads, 0, stream>>>(a);
+  win_dec_combine_kernel<<<dim3(a.B * a.G, a.R), kWD_Threads, 0, stream>>>(a);
   return cudaGetLastError() == cudaSuccess ? BF_OK : BF_ERR_CUDA;
 }
 
