@@ -3,7 +3,7 @@
 // * status codes shared with the C ABI (include/bifrost_b200.h)
 // * bounded mbarrier waits: every wait gives up after a time limit, records where it gave up in a
 //   device-side error word and lets the kernel unwind (no trap, no endless spin)
-// * thin inline-PTX wrappers for TMA (cp.async.bulk.tensor, no multicast anywhere) and the
+// * thin inline-PTX wrappers for TMA (cp.async.bulk.tensor; every CTA loads only its own tiles) and the
 //   5th-generation tensor core (tcgen05.alloc / mma / commit / ld / st)
 // * UMMA shared-memory and instruction descriptors for K-major, 128-byte-swizzled operands
 #pragma once
@@ -109,7 +109,7 @@ __device__ __forceinline__ void fence_async_smem() {
 }
 
 // ----------------------------------------------------------------------------------------------
-// TMA loads (tiled, no multicast).  `tmap` is the generic address of a __grid_constant__ CUtensorMap.
+// TMA loads (tiled, one CTA per load).  `tmap` is the generic address of a __grid_constant__ CUtensorMap.
 __device__ __forceinline__ void tma_prefetch(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }

@@ -342,8 +342,11 @@ __global__ void __launch_bounds__(kP2_Threads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 6);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 7);
 
-  const int blk = blockIdx.x, bg = blockIdx.y;
-  const int col0 = blk * kP2_NB;
+  const int bg = blockIdx.y;
+  // column blocks beyond the state's (transform mode only) run the map path: start at the identity, no inputs
+  const bool mpath = blockIdx.x >= kGD / kP2_NB;
+  const int col0 = (mpath ? blockIdx.x - kGD / kP2_NB : blockIdx.x) * kP2_NB;
+  const bool keep = s.m_out == nullptr;   // chunk-start states and v' are kept for P3
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int nch = s.n_chunks;
   if (t == 0) {
@@ -414,7 +417,13 @@ __global__ void __launch_bounds__(kP2_Threads, 1)
     const int r = t;
     const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
     float S0[kP2_NB], S1[kP2_NB];
-    if (s.s0) {
+    if (mpath) {
+#pragma unroll
+      for (int e = 0; e < kP2_NB; ++e) {
+        S0[e] = (r == col0 + e) ? 1.f : 0.f;
+        S1[e] = (r + 128 == col0 + e) ? 1.f : 0.f;
+      }
+    } else if (s.s0) {
       const float* sp = s.s0 + (size_t)bg * kGD * kGD;
 #pragma unroll
       for (int e = 0; e < kP2_NB; e += 4) {
@@ -428,15 +437,21 @@ __global__ void __launch_bounds__(kP2_Threads, 1)
       for (int e = 0; e < kP2_NB; ++e) S0[e] = S1[e] = 0.f;
     }
     bool alive = true;
+    float lsum = 0.f;   // map path: log of the cumulative decay
     for (int c = 0; c < nch && alive; ++c) {
       // stage S^T (fp16) as the B operand of v' = u - w S, and store it for P3
-      __half* stg = s.ST + (((size_t)bg * nch + c) * kGD + col0) * kGD;
 #pragma unroll
       for (int e = 0; e < kP2_NB; ++e) {
         st_half_sw128(sST, kP2_NB, e, r, S0[e]);
         st_half_sw128(sST, kP2_NB, e, r + 128, S1[e]);
-        stg[(size_t)e * kGD + r] = __float2half_rn(S0[e]);
-        stg[(size_t)e * kGD + r + 128] = __float2half_rn(S1[e]);
+      }
+      if (keep) {
+        __half* stg = s.ST + (((size_t)bg * nch + c) * kGD + col0) * kGD;
+#pragma unroll
+        for (int e = 0; e < kP2_NB; ++e) {
+          stg[(size_t)e * kGD + r] = __float2half_rn(S0[e]);
+          stg[(size_t)e * kGD + r + 128] = __float2half_rn(S1[e]);
+        }
       }
       fence_async_smem();
       tc_fence_before();
@@ -444,7 +459,10 @@ __global__ void __launch_bounds__(kP2_Threads, 1)
       // u row r (this chunk), columns col0..+15
       const __half* up = s.u + ((size_t)bg * s.n_pad + (size_t)c * kGC + r) * kGD + col0;
       float uu[kP2_NB];
-      {
+      if (mpath) {
+#pragma unroll
+        for (int e = 0; e < kP2_NB; ++e) uu[e] = 0.f;
+      } else {
         const uint4 a0 = *reinterpret_cast<const uint4*>(up);
         const uint4 a1 = *reinterpret_cast<const uint4*>(up + 8);
         const uint32_t w[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
@@ -460,31 +478,52 @@ __global__ void __launch_bounds__(kP2_Threads, 1)
       tc_fence_after();
       float dv[kP2_NB];
       tmem_ld16_wait(trow, dv);
-      __half* vtg = s.VT + (((size_t)bg * nch + c) * kGD + col0) * kGC;
 #pragma unroll
-      for (int e = 0; e < kP2_NB; ++e) {
-        const float vn = uu[e] - dv[e];
-        st_half_sw128(sVT, kP2_NB, e, r, vn);
-        vtg[(size_t)e * kGC + r] = __float2half_rn(vn);
+      for (int e = 0; e < kP2_NB; ++e) st_half_sw128(sVT, kP2_NB, e, r, uu[e] - dv[e]);
+      if (keep) {
+        __half* vtg = s.VT + (((size_t)bg * nch + c) * kGD + col0) * kGC;
+#pragma unroll
+        for (int e = 0; e < kP2_NB; ++e) vtg[(size_t)e * kGC + r] = __float2half_rn(uu[e] - dv[e]);
       }
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(bar_vt);
-      const float decay = __expf(s.gc[(size_t)bg * s.n_pad + (size_t)c * kGC + kGC - 1]);
+      const float lgc = s.gc[(size_t)bg * s.n_pad + (size_t)c * kGC + kGC - 1];
+      const float decay = __expf(lgc);
       if (!mbar_wait_warp(bar_m2, c & 1, abort_flag, s.err, 0x5a)) { alive = false; break; }
       tc_fence_after();
       float d0[kP2_NB], d1[kP2_NB];
       tmem_ld16_wait(trow + kP2_NB, d0);
       tmem_ld16_wait(trow + 2 * kP2_NB, d1);
+      if (mpath) {
+        // the map path keeps its state divided by the cumulative decay (the recurrence is homogeneous), so the
+        // fp16 operand copies stay in range however far the segment decays; the factor is applied at the end
+        const float inv = __expf(-lgc);
+        lsum += lgc;
 #pragma unroll
-      for (int e = 0; e < kP2_NB; ++e) {
-        S0[e] = decay * S0[e] + d0[e];
-        S1[e] = decay * S1[e] + d1[e];
+        for (int e = 0; e < kP2_NB; ++e) {
+          S0[e] = fmaf(d0[e], inv, S0[e]);
+          S1[e] = fmaf(d1[e], inv, S1[e]);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < kP2_NB; ++e) {
+          S0[e] = decay * S0[e] + d0[e];
+          S1[e] = decay * S1[e] + d1[e];
+        }
       }
       tc_fence_before();
     }
+    if (alive && mpath) {
+      const float f = __expf(lsum);
+#pragma unroll
+      for (int e = 0; e < kP2_NB; ++e) {
+        S0[e] *= f;
+        S1[e] *= f;
+      }
+    }
     if (alive) {
-      float* so = s.s_out + (size_t)bg * kGD * kGD;
+      float* so = (mpath ? s.m_out : s.s_out) + (size_t)bg * kGD * kGD;
 #pragma unroll
       for (int e = 0; e < kP2_NB; e += 4) {
         *reinterpret_cast<float4*>(so + (size_t)r * kGD + col0 + e) = make_float4(S0[e], S0[e + 1], S0[e + 2], S0[e + 3]);
@@ -668,7 +707,7 @@ __global__ void __launch_bounds__(kP3_Threads, 1)
 }
 
 // ============================================================================================ launch
-size_t gdn_prefill_workspace(int B, int G, int T_steps) {
+size_t gdn_prefill_workspace(int B, int G, int T_steps, bool transform) {
   const size_t n_pad = (size_t)((T_steps + kGC - 1) / kGC) * kGC;
   const size_t nch = n_pad / kGC;
   auto al = [](size_t x) { return (x + 1023) & ~size_t(1023); };
@@ -676,6 +715,7 @@ size_t gdn_prefill_workspace(int B, int G, int T_steps) {
   n += al((size_t)B * G * n_pad * kGD * 2) * 3;       // kw, w, u
   n += al((size_t)B * G * nch * kGD * kGC * 2);       // ktT
   n += al((size_t)B * G * n_pad * 4);                 // gc
+  if (transform) return n;                            // no P3: the chunk states are not kept
   n += al((size_t)B * G * nch * kGD * kGD * 2);       // ST
   n += al((size_t)B * G * nch * kGD * kGC * 2);       // VT
   return n;
@@ -690,6 +730,10 @@ int gdn_prefill_carve(GdnStreams& s, void* ws) {
   s.u = reinterpret_cast<__half*>(p); p += al((size_t)s.B * s.G * n_pad * kGD * 2);
   s.ktT = reinterpret_cast<__half*>(p); p += al((size_t)s.B * s.G * nch * kGD * kGC * 2);
   s.gc = reinterpret_cast<float*>(p); p += al((size_t)s.B * s.G * n_pad * 4);
+  if (s.m_out) {
+    s.ST = s.VT = nullptr;
+    return BF_OK;
+  }
   s.ST = reinterpret_cast<__half*>(p); p += al((size_t)s.B * s.G * nch * kGD * kGD * 2);
   s.VT = reinterpret_cast<__half*>(p); p += al((size_t)s.B * s.G * nch * kGD * kGC * 2);
   return BF_OK;
@@ -717,9 +761,10 @@ int launch_gdn_prefill(GdnStreams s, cudaStream_t stream) {
   rc = make_tmap_kmajor(&ktmap, s.ktT, BF_F16, (uint64_t)s.B * s.G * s.n_chunks * kGD, kGC, kGC, kGD, 2);
   if (rc) return rc;
   stage_mark(ST_GDN_P2, 0, stream);
-  gdn_p2_kernel<<<dim3(kGD / kP2_NB, s.B * s.G), kP2_Threads, kP2_Smem, stream>>>(wmap, ktmap, s);
+  gdn_p2_kernel<<<dim3((s.m_out ? 2 : 1) * (kGD / kP2_NB), s.B * s.G), kP2_Threads, kP2_Smem, stream>>>(wmap, ktmap, s);
   if (cudaGetLastError() != cudaSuccess) return BF_ERR_CUDA;
   stage_mark(ST_GDN_P2, 1, stream);
+  if (s.m_out) return BF_OK;   // segment transform: no reads
   // P3 maps: q [B,T,H,D] fp16 as (d, token, atom, head); k/kw; S^T; v'^T
   CUtensorMap qmap, kmap, smap, vmap;
   {

@@ -40,6 +40,9 @@ struct GdnStreams {
   float* s_out;                // [B,G,D,D]
   const __half* qm;            // [B,T,H,D] fp16 (read queries, unit-norm * D^-1/2)
   float* o;                    // [B,T,H,D] memory read of query u + qoff
+  // segment-transform mode (m_out != null): no reads; P2 also runs the recurrence from the identity with
+  // zero inputs, whose final value is the segment's state map M (S_out = M S_in + N), and writes it here
+  float* m_out;                // [B,G,D,D]
   unsigned int* err;
 };
 

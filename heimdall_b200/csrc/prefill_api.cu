@@ -13,7 +13,7 @@ int mem_inputs_impl(const DeviceState& st, const bf_layer* L, const void* x, con
                     const int64_t* pos, long long pos0, int B, int T, float* qm, float* km, float* g, float* beta,
                     float* mixx, cudaStream_t stream, __half* qm16, float* scratch, size_t scratch_bytes);
 int check_layer(const bf_layer* L);
-size_t gdn_prefill_workspace(int B, int G, int T_steps);
+size_t gdn_prefill_workspace(int B, int G, int T_steps, bool transform);
 int gdn_prefill_carve(GdnStreams& s, void* ws);
 int launch_gdn_prefill(GdnStreams s, cudaStream_t stream);
 int launch_vt_prep(const __nv_bfloat16* v, long long vb, long long vg, long long vj, const __nv_bfloat16* ring_v,
@@ -84,7 +84,7 @@ extern "C" {
 // ================================================================================ delta rule op
 size_t bf_gdn_chunk_workspace(int B, int T, int G, int R, int D) {
   if (B <= 0 || T <= 0 || G <= 0 || R <= 0 || D != 256) return 0;
-  return al1k((size_t)B * T * G * R * D * 2) + al1k((size_t)B * T * G * D * 4) + gdn_prefill_workspace(B, G, T);
+  return al1k((size_t)B * T * G * R * D * 2) + al1k((size_t)B * T * G * D * 4) + gdn_prefill_workspace(B, G, T, false);
 }
 
 int bf_gdn_chunk_fwd(const void* q, int q_dtype, const void* k, int k_dtype, const void* v, int v_dtype,
@@ -199,7 +199,7 @@ size_t bf_layer_prefill_workspace(int B, int T, int H, int G, int D, int window,
   n += al1k((size_t)B * G * D * D * 4);     // state when there is no cache
   n += al1k((size_t)B * G * D * Tkp * 2);   // V^T
   if (with_ring) n += al1k((size_t)B * G * Tk * D * 2);  // K of the extended sequence
-  n += gdn_prefill_workspace(B, G, steps);
+  n += gdn_prefill_workspace(B, G, steps, false);
   return n;
 }
 

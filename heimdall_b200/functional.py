@@ -147,3 +147,40 @@ def window_attention(qr, ext_k, ext_v, qpos0: int, kpos0: int, klo: int, window:
               ptr(svb), ns, int(qpos0), int(kpos0), int(klo), B, H, G, Tq, Tk, D, int(window), ptr(o), ptr(lse),
               ptr(ws), nws, stream_handle())
     return o, lse
+
+
+def segment_transform(k, v, g, beta, s0=None):
+    """State map of one segment of the write stream, for sequence parallelism of the delta rule.
+
+    k, v [B,T,G,D] (fp32 or bf16), g, beta [B,T,G], s0 [B,G,D,D] or None.  Returns (M, N), both
+    [B,G,D,D] fp32: N is the final state of ``delta_rule_gqa`` over the segment from s0 (zero state when
+    None), and for any other initial state S the final state is M (S - s0) + N.  The reference runs the
+    same recurrence as one sequential scan (heimdall/kernels.py:118-129).
+    """
+    check_cuda(k, v, g, beta, s0)
+    B, T, G, D = k.shape
+    if D != 256 or v.shape[-1] != D:
+        raise NotImplementedError("the tensor-core delta rule is built for head dim 256")
+    dev = k.device
+    kk, vv = _as_kernel_dtype(k), _as_kernel_dtype(v)
+    gg, bb = g.float().contiguous(), beta.float().contiguous()
+    s0c = None if s0 is None else s0.float().contiguous()
+    M = torch.empty(B, G, D, D, device=dev, dtype=torch.float32)
+    N = torch.empty(B, G, D, D, device=dev, dtype=torch.float32)
+    nws = _lib.size("bf_gdn_segment_workspace", B, T, G, D)
+    ws = _ws(nws, dev)
+    _lib.call("bf_gdn_segment_transform", ptr(kk), _dt(kk), ptr(vv), _dt(vv), ptr(gg), ptr(bb), ptr(s0c), ptr(M),
+              ptr(N), B, T, G, D, ptr(ws), nws, stream_handle())
+    return M, N
+
+
+def apply_prefix(M, N, s0=None):
+    """Incoming states of consecutive segments: M, N [n,B,G,D,D] (segments in order), s0 [B,G,D,D] or None.
+    Returns S [n+1,B,G,D,D] fp32 with S[0] = s0 (zero state when None) and S[j+1] = M[j] S[j] + N[j]."""
+    check_cuda(M, N, s0)
+    n, B, G, D = M.shape[0], M.shape[1], M.shape[2], M.shape[3]
+    Mc, Nc = M.float().contiguous(), N.float().contiguous()
+    s0c = None if s0 is None else s0.float().contiguous()
+    S = torch.empty(n + 1, B, G, D, D, device=M.device, dtype=torch.float32)
+    _lib.call("bf_gdn_apply_prefix", ptr(Mc), ptr(Nc), n, ptr(s0c), ptr(S), B, G, D, stream_handle())
+    return S

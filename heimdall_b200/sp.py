@@ -1,0 +1,145 @@
+"""Sequence-parallel prefill of one Bifrost layer: a long sequence split into consecutive segments, one per
+rank (one GPU per rank, ``torch.distributed`` over NCCL).
+
+The layer is ``HybridAttention._student`` (heimdall/hibrit.py:363-424) run over the whole sequence from an
+empty cache.  Rank j holds tokens [j T, (j+1) T) and returns their outputs.  Two things cross segments:
+
+* the window: a token sees the previous W tokens and the S sinks, so rank j needs the last W tokens of
+  rank j-1 (a halo: x, k, v, kr) and the first S tokens of rank 0;
+* the memory: the delta-rule state after all earlier tokens.  Memory writes lag the window by W
+  (hibrit.py:391-396), so rank j's write stream is the W halo tokens followed by its first T - W tokens.
+  Each rank computes the state map of its write stream, (M_j, N_j) with S_out = M_j S_in + N_j
+  (``functional.segment_transform``), the maps are all-gathered, and each rank folds the earlier ones
+  into its incoming state (``functional.apply_prefix``).
+
+Rank j then runs the ordinary layer prefill of its tokens with a cache built from the halo: the ring holds
+the halo tokens (slot = position mod W), the sinks are rank 0's first tokens and S is the incoming state.
+A prefill from such a cache is exactly the continuation of the sequence (the reference's mixed-parts
+property, tests/test_hibrit.py:78-90), so the outputs equal one pass over the whole sequence.
+
+Traffic per rank and layer: the halo (W tokens of x, k, v, kr: 33 MB at W = 2048, d = 5120) from the left
+neighbour, the sink rows from rank 0, and an all-gather of (M, N) (2 MB per rank at G = 4, D = 256).
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from . import functional as F_
+
+
+def _peer(group, r: int) -> int:
+    return dist.get_global_rank(group, r) if group is not None else r
+
+
+def _p2p_shift(tensors, rank: int, world: int, group):
+    """Send ``tensors`` to rank+1 and receive the same shapes from rank-1 (None on rank 0)."""
+    reqs, recv = [], None
+    send = [t.contiguous() for t in tensors]          # held until the sends completed
+    if rank > 0:
+        recv = [torch.empty_like(t) for t in send]
+        reqs += [dist.irecv(r, src=_peer(group, rank - 1), group=group) for r in recv]
+    if rank < world - 1:
+        reqs += [dist.isend(t, dst=_peer(group, rank + 1), group=group) for t in send]
+    for r in reqs:
+        r.wait()
+    return recv
+
+
+def write_stream(km_h, g_h, b_h, v_h, km, g, beta, v, T: int, W: int, first: bool):
+    """The segment's memory write stream: write step u uses the token W positions back, i.e. halo token u
+    for u < W, then this rank's token u - W.  Rank 0 has no halo and T - W steps."""
+    n_own = max(0, T - W)
+    own = (km[:, :n_own], g[:, :n_own], beta[:, :n_own], v[:, :n_own])
+    if first:
+        return own
+    return tuple(torch.cat((h, o), 1) for h, o in zip((km_h, g_h, b_h, v_h), own))
+
+
+def halo_cache(kr_h, v_h, km_h, g_h, b_h, sink_k, sink_v, S_in, start: int, W: int):
+    """The reference cache (hibrit.py:414-423) a rank starts from: ring = the W tokens before ``start`` in
+    slot order (slot = position mod W), the sinks, and the incoming state."""
+    dev = kr_h.device
+    pos = torch.arange(start - W, start, device=dev, dtype=torch.int64)
+    slot = pos % W
+    B, G, _, D = kr_h.shape
+    ring_k = torch.empty_like(kr_h)
+    ring_k[:, :, slot] = kr_h
+    ring_v = torch.empty(B, G, W, D, device=dev, dtype=v_h.dtype)
+    ring_v[:, :, slot] = v_h.transpose(1, 2)
+    ring_km = torch.empty_like(km_h)
+    ring_km[:, slot] = km_h
+    ring_g = torch.empty_like(g_h)
+    ring_g[:, slot] = g_h
+    ring_beta = torch.empty_like(b_h)
+    ring_beta[:, slot] = b_h
+    ring_pos = torch.empty(W, device=dev, dtype=torch.int64)
+    ring_pos[slot] = pos
+    return dict(ring_k=ring_k, ring_v=ring_v, ring_km=ring_km, ring_g=ring_g, ring_beta=ring_beta,
+                ring_pos=ring_pos, sink_k=sink_k, sink_v=sink_v, S=S_in)
+
+
+def student_sp(L, x, q, k, v, qr, kr, group=None, memory: bool = True):
+    """One layer prefill of a sequence split over the ranks of ``group`` in rank order, from an empty cache.
+
+    Every rank passes its own T consecutive tokens (the same T on every rank, T >= W) in the layouts of
+    ``BifrostLayer.student``: x [B,T,d], q [B,T,H,D], k/v [B,T,G,D], qr [B,H,T,D], kr [B,G,T,D] (bf16, on
+    this rank's GPU).  Returns (o, cache): this rank's outputs [B,T,H,D] fp32 and its cache after the call
+    (on the last rank that is the cache of the whole sequence).  Every rank must call it (collectives).
+    """
+    rank = dist.get_rank(group)
+    world = dist.get_world_size(group)
+    B, T = x.shape[:2]
+    W, S = L.window, L.sinks
+    if T < W or T < S:
+        raise NotImplementedError("sequence parallelism needs at least one window (and the sinks) per rank")
+    start = rank * T
+    bf = torch.bfloat16
+    x, q, k, v, qr, kr = (z.to(bf).contiguous() for z in (x, q, k, v, qr, kr))
+    # sinks: rank 0's first S tokens
+    sink_k = kr[:, :, :S].contiguous()
+    sink_v = v[:, :S].transpose(1, 2).contiguous()
+    if world > 1 and S > 0:
+        dist.broadcast(sink_k, src=_peer(group, 0), group=group)
+        dist.broadcast(sink_v, src=_peer(group, 0), group=group)
+    # halo: the last W tokens of the previous rank, and their memory inputs
+    halo = _p2p_shift([x[:, -W:], k[:, -W:], v[:, -W:], kr[:, :, -W:]], rank, world, group)
+    first = rank == 0
+    if not first:
+        km_h, g_h, b_h = _halo_inputs(L, halo, start, W, q)
+    G, D = k.shape[2], k.shape[3]
+    zero = torch.zeros(B, G, D, D, device=x.device, dtype=torch.float32)
+    S_in = zero
+    if memory:
+        _, km, g, beta, _ = L.mem_inputs(x, q, k, pos0=start)
+        kw, gw, bw, vw = write_stream(None if first else km_h, None if first else g_h, None if first else b_h,
+                                      None if first else halo[2], km, g, beta, v, T, W, first)
+        if kw.shape[1] > 0:
+            M, N = F_.segment_transform(kw, vw, gw, bw)
+        else:   # no memory writes in this segment: identity map
+            M = torch.eye(D, device=x.device, dtype=torch.float32).expand(B, G, D, D).contiguous()
+            N = zero.clone()
+        if world > 1:
+            Ml = [torch.empty_like(M) for _ in range(world)]
+            Nl = [torch.empty_like(N) for _ in range(world)]
+            dist.all_gather(Ml, M.contiguous(), group=group)
+            dist.all_gather(Nl, N.contiguous(), group=group)
+            Ms, Ns = torch.stack(Ml), torch.stack(Nl)
+        else:
+            Ms, Ns = M[None], N[None]
+        S_in = F_.apply_prefix(Ms[:rank], Ns[:rank])[rank].contiguous()
+    if first:
+        cache = {"S": S_in}
+    else:
+        cache = halo_cache(halo[3], halo[2], km_h, g_h, b_h, sink_k, sink_v, S_in, start, W)
+    o = L.student(x, q, k, v, qr, kr, start, cache, memory=memory)
+    return o, cache
+
+
+def _halo_inputs(L, halo, start: int, W: int, q):
+    """Memory inputs (km, g, beta) of the halo tokens, at their positions start - W .. start - 1.
+    Their query projections are not needed (those tokens' outputs belong to the previous rank)."""
+    x_h, k_h = halo[0], halo[1]
+    q_h = torch.zeros(q.shape[0], W, *q.shape[2:], device=q.device, dtype=q.dtype)
+    _, km_h, g_h, b_h, _ = L.mem_inputs(x_h, q_h, k_h, pos0=start - W)
+    return km_h, g_h, b_h

@@ -206,6 +206,26 @@ int bf_bifrost_layer_prefill(const bf_layer* L, const void* x, const void* q, co
                              const void* sink_k, const void* sink_v, int ns, int memory, float* o, float* lse,
                              void* ws, size_t ws_bytes, bf_stream_t stream);
 
+/* ---------------------------------------------------------------------------------------------
+ * Sequence parallelism of the delta rule (a long sequence split into consecutive segments, one per
+ * GPU).  A segment of the write stream maps any incoming state S to S_out = M (S - s0) + N, where N
+ * is the final state from s0 (zero state when s0 is NULL).  These two entry points replace the
+ * reference's single sequential scan over chunks (heimdall/kernels.py:118-129, the loop of
+ * delta_rule_reference) when the chunks are spread over several devices.
+ *
+ * bf_gdn_segment_transform: k, v [B,T,G,D] (fp32 or bf16), g, beta [B,T,G] fp32, s0 [B,G,D,D] or
+ * NULL -> m_out, n_out [B,G,D,D] fp32.  D = 256.
+ * bf_gdn_apply_prefix: M, N [n_seg][B,G,D,D] (segments in order; NULL allowed when n_seg = 0), s0
+ * [B,G,D,D] or NULL ->
+ * s_in [n_seg + 1][B,G,D,D]: s_in[0] = s0, s_in[j+1] = M[j] s_in[j] + N[j] (fp32).
+ */
+size_t bf_gdn_segment_workspace(int B, int T, int G, int D);
+int bf_gdn_segment_transform(const void* k, int k_dtype, const void* v, int v_dtype, const float* g,
+                             const float* beta, const float* s0, float* m_out, float* n_out, int B, int T, int G,
+                             int D, void* ws, size_t ws_bytes, bf_stream_t stream);
+int bf_gdn_apply_prefix(const float* M, const float* N, int n_seg, const float* s0, float* s_in, int B, int G,
+                        int D, bf_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
