@@ -14,6 +14,7 @@ Extra keys: ``roofline`` (window-attention kernel, the dominant one, timed live 
 stream), ``layer_roofline`` (all algorithmic FLOPs of the step), ``cpu_baseline`` (the CPU oracle port on
 a bounded sample), ``e2e`` (host buffers in, host output back, copies inside the timed region),
 ``decode`` (64 sequences x 12 layers, one token per sequence per step),
+``sp`` (one 131072-token sequence split over the N GPUs, sequence-parallel prefill),
 ``clocks`` (nvidia-smi samples during the timed region) and ``gpu_launches``.
 """
 from __future__ import annotations
@@ -228,6 +229,38 @@ def run_e2e(L, T, steps, warmup, device, ctx):
             "d2h_bytes_per_step": bo, "api": "BifrostLayer.student_host (chunks of 4096 tokens, 3 streams)"}
 
 
+def run_sp(L, device, ctx, T_total=131072, steps=5, warmup=2):
+    """one sequence of T_total tokens split over the ranks (heimdall_b200.sp.student_sp:
+    halo exchange, segment state maps, all-gather, prefix fold, then each rank's prefill).  At N=1 the
+    same sequence is one ordinary prefill.  Max over ranks of the device time."""
+    from heimdall_b200 import sp
+    world, rank = ctx["world"], ctx["rank"]
+    T = T_total // world
+    ins = make_inputs(T, seed=11 + rank, device=device)
+    if world > 1:
+        step = lambda: sp.student_sp(L, *ins)
+    else:
+        step = lambda: L.student(*ins, 0, {})
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(ctx)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        step()
+    b.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([a.elapsed_time(b) / steps], device=device)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms = float(t.item())
+    del ins
+    return {"workload": f"BASELINE config 3: one sequence of {T_total} tokens split over {world} GPU(s) "
+                        f"({T} per GPU), from an empty cache", "T_total": T_total, "ms_per_step": ms,
+            "value": T_total / (ms / 1e3), "unit": "tok/s", "steps": steps, "warmup": warmup}
+
+
 def run_decode(device, steps=256, warmup=8, nseq=64, nlayers=12):
     """64 sequences at positions U[4K, 128K], 12 stacked layers, one token per sequence per
     step; the whole 12-layer step is captured in a CUDA graph and replayed."""
@@ -434,6 +467,7 @@ def main(argv=None):
     ap.add_argument("--decode-steps", type=int, default=256)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-sp", action="store_true")
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)
     ctx = dist_setup()
@@ -462,6 +496,8 @@ def run_ours(args, ctx):
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     ms_max = float(t.item())
     e2e = None if args.no_e2e else run_e2e(L, T, min(args.steps, 10), 1, dev, ctx)
+    del inputs
+    sp_res = None if args.no_sp else run_sp(L, dev, ctx)
     if ctx["rank"] != 0:
         return
     ms_step = ms_max / args.steps
@@ -497,6 +533,8 @@ def run_ours(args, ctx):
            "gpu_launches": 8 * args.steps}
     if e2e is not None:
         out["e2e"] = e2e
+    if sp_res is not None:
+        out["sp"] = sp_res
     if not args.no_cpu and ctx["world"] == 1:
         tps, cores, dt, reps = cpu_baseline()
         out["cpu_baseline"] = {"value": tps, "unit": "tok/s", "cores": cores, "kind": "port",

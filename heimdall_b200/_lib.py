@@ -40,6 +40,8 @@ SIGNATURES = {
     "bf_gdn_segment_workspace": [_I, _I, _I, _I],
     "bf_gdn_segment_transform": [_P, _I, _P, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _Z, _P],
     "bf_gdn_apply_prefix": [_P, _P, _I, _P, _P, _I, _I, _I, _P],
+    "bf_bifrost_layer_prefill_sp": [_P, _P, _P, _P, _P, _P, _P, _L, _I, _I, _P, _P, _P, _I, _I, _P, _P, _P, _P, _P,
+                                    _Z, _P],
 }
 _RESTYPE = {"bf_strerror": ctypes.c_char_p, "bf_layer_weights_bytes": _Z, "bf_layer_decode_workspace": _Z,
             "bf_gdn_chunk_workspace": _Z, "bf_window_workspace": _Z, "bf_layer_prefill_workspace": _Z,

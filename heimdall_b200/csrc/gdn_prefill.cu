@@ -741,7 +741,7 @@ int gdn_prefill_carve(GdnStreams& s, void* ws) {
 
 static bool g_p_attr[3] = {false, false, false};
 
-int launch_gdn_prefill(GdnStreams s, cudaStream_t stream) {
+int launch_gdn_prefill(GdnStreams s, cudaStream_t stream, int parts) {
   if (s.n_steps <= 0) return BF_OK;
   const int H = s.G * s.R;
   if (!g_p_attr[0]) {
@@ -751,10 +751,13 @@ int launch_gdn_prefill(GdnStreams s, cudaStream_t stream) {
       return BF_ERR_CUDA;
     g_p_attr[0] = true;
   }
-  stage_mark(ST_GDN_P1, 0, stream);
-  gdn_p1_kernel<<<dim3(s.n_chunks, s.B * s.G), kP1_Threads, kP1_Smem, stream>>>(s);
-  if (cudaGetLastError() != cudaSuccess) return BF_ERR_CUDA;
-  stage_mark(ST_GDN_P1, 1, stream);
+  if (parts & kGdnP1) {
+    stage_mark(ST_GDN_P1, 0, stream);
+    gdn_p1_kernel<<<dim3(s.n_chunks, s.B * s.G), kP1_Threads, kP1_Smem, stream>>>(s);
+    if (cudaGetLastError() != cudaSuccess) return BF_ERR_CUDA;
+    stage_mark(ST_GDN_P1, 1, stream);
+  }
+  if (!(parts & kGdnP23)) return BF_OK;
   CUtensorMap wmap, ktmap;
   int rc = make_tmap_kmajor(&wmap, s.w, BF_F16, (uint64_t)s.B * s.G * s.n_pad, kGD, kGD, kGC, 4);
   if (rc) return rc;

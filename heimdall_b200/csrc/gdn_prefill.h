@@ -7,6 +7,8 @@
 namespace bfb {
 
 constexpr int kGC = 128;   // chunk length of the GPU scan (tokens)
+// parts of launch_gdn_prefill: P1 (per-chunk products) and P2 (+ P3 unless in transform mode)
+constexpr int kGdnP1 = 1, kGdnP23 = 2, kGdnAll = 3;
 constexpr int kGD = 256;   // head dim (Dk == Dv)
 
 // The write stream (step u writes one key/value into memory) and the read stream (step u reads with

@@ -15,7 +15,7 @@ int mem_inputs_impl(const DeviceState& st, const bf_layer* L, const void* x, con
 int check_layer(const bf_layer* L);
 size_t gdn_prefill_workspace(int B, int G, int T_steps, bool transform);
 int gdn_prefill_carve(GdnStreams& s, void* ws);
-int launch_gdn_prefill(GdnStreams s, cudaStream_t stream);
+int launch_gdn_prefill(GdnStreams s, cudaStream_t stream, int parts);
 int launch_vt_prep(const __nv_bfloat16* v, long long vb, long long vg, long long vj, const __nv_bfloat16* ring_v,
                    int nring, long long ring_pos0, int W, int B, int G, int Tk, int Tkp, __half* vt,
                    cudaStream_t stream);
@@ -131,7 +131,7 @@ int bf_gdn_chunk_fwd(const void* q, int q_dtype, const void* k, int k_dtype, con
   s.qm = q16; s.o = o;
   s.err = st.err;
   gdn_prefill_carve(s, p);
-  return launch_gdn_prefill(s, stream);
+  return launch_gdn_prefill(s, stream, kGdnAll);
 }
 
 // ================================================================================ window op
@@ -203,10 +203,24 @@ size_t bf_layer_prefill_workspace(int B, int T, int H, int G, int D, int window,
   return n;
 }
 
-int bf_bifrost_layer_prefill(const bf_layer* L, const void* x, const void* q, const void* k, const void* v,
-                             const void* qr, const void* kr, long long start, int B, int T, bf_ring_cache* C,
-                             const void* sink_k, const void* sink_v, int ns, int memory, float* o, float* lse,
-                             void* ws, size_t ws_bytes, bf_stream_t stream) {
+// phase: kPhaseAll (the whole layer), kPhaseBegin (memory inputs, P1 and the segment state map -> m_out, n_out),
+// kPhaseFinish (the rest, from C->S, reusing the workspace of the begin phase)
+constexpr int kPhaseAll = 0, kPhaseBegin = 1, kPhaseFinish = 2;
+
+__global__ void identity_maps_kernel(float* m, float* n, int BG, int D) {
+  const size_t total = (size_t)BG * D * D;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t e = i % ((size_t)D * D);
+    m[i] = (e / D == e % D) ? 1.f : 0.f;
+    n[i] = 0.f;
+  }
+}
+
+static int layer_prefill_impl(const bf_layer* L, const void* x, const void* q, const void* k, const void* v,
+                              const void* qr, const void* kr, long long start, int B, int T, bf_ring_cache* C,
+                              const void* sink_k, const void* sink_v, int ns, int memory, float* o, float* lse,
+                              void* ws, size_t ws_bytes, cudaStream_t stream, int phase, float* m_out,
+                              float* n_out) {
   int rc = check_layer(L);
   if (rc) return rc;
   if (!x || !q || !k || !v || !qr || !kr || !o || !ws || B <= 0 || T <= 0 || start < 0) return BF_ERR_INVALID_ARGUMENT;
@@ -246,7 +260,7 @@ int bf_bifrost_layer_prefill(const bf_layer* L, const void* x, const void* q, co
   void* gws = p;
 
   // 1. memory inputs (projections on tcgen05)
-  if (use_mem || C) {
+  if ((use_mem || C) && phase != kPhaseFinish) {
     rc = mem_inputs_impl(st, L, x, q, k, nullptr, start, B, T, nullptr, km, g, beta, mixx, stream, qm16, nullptr, 0);
     if (rc) return rc;
   }
@@ -272,12 +286,24 @@ int bf_bifrost_layer_prefill(const bf_layer* L, const void* x, const void* q, co
     s.km = km; s.v = static_cast<const __nv_bfloat16*>(v); s.g = g; s.beta = beta;
     s.s_out = C ? C->S : s_tmp;
     s.qm = qm16; s.o = o_mem; s.err = st.err;
+    if (phase == kPhaseBegin) {   // the state map of this segment's write stream, from a zero state
+      s.s0 = nullptr;
+      s.s_out = n_out;
+      s.m_out = m_out;
+    }
     if (s.n_steps > 0) {
       gdn_prefill_carve(s, gws);
-      rc = launch_gdn_prefill(s, stream);
+      rc = launch_gdn_prefill(s, stream, phase == kPhaseFinish ? kGdnP23 : kGdnAll);
       if (rc) return rc;
+    } else if (phase == kPhaseBegin) {
+      identity_maps_kernel<<<grid_for((size_t)B * G * D * D), 256, 0, stream>>>(m_out, n_out, B * G, D);
+      if (cudaGetLastError() != cudaSuccess) return BF_ERR_CUDA;
     }
+  } else if (phase == kPhaseBegin) {
+    identity_maps_kernel<<<grid_for((size_t)B * G * D * D), 256, 0, stream>>>(m_out, n_out, B * G, D);
+    if (cudaGetLastError() != cudaSuccess) return BF_ERR_CUDA;
   }
+  if (phase == kPhaseBegin) return BF_OK;
   // 3. window attention over the extended keys, with the gate and mix fused into its epilogue
   const void* kx = kr;
   stage_mark(ST_WIN_PREP, 0, stream);
@@ -309,6 +335,25 @@ int bf_bifrost_layer_prefill(const bf_layer* L, const void* x, const void* q, co
     stage_mark(ST_CACHE, 1, stream);
   }
   return BF_OK;
+}
+
+int bf_bifrost_layer_prefill(const bf_layer* L, const void* x, const void* q, const void* k, const void* v,
+                             const void* qr, const void* kr, long long start, int B, int T, bf_ring_cache* C,
+                             const void* sink_k, const void* sink_v, int ns, int memory, float* o, float* lse,
+                             void* ws, size_t ws_bytes, bf_stream_t stream) {
+  return layer_prefill_impl(L, x, q, k, v, qr, kr, start, B, T, C, sink_k, sink_v, ns, memory, o, lse, ws, ws_bytes,
+                            stream, kPhaseAll, nullptr, nullptr);
+}
+
+int bf_bifrost_layer_prefill_sp(const bf_layer* L, const void* x, const void* q, const void* k, const void* v,
+                                const void* qr, const void* kr, long long start, int B, int T, bf_ring_cache* C,
+                                const void* sink_k, const void* sink_v, int ns, int phase, float* m_out,
+                                float* n_out, float* o, float* lse, void* ws, size_t ws_bytes, bf_stream_t stream) {
+  if (phase != 0 && phase != 1) return BF_ERR_INVALID_ARGUMENT;
+  if (phase == 0 && (!m_out || !n_out || !aligned16(m_out) || !aligned16(n_out))) return BF_ERR_INVALID_ARGUMENT;
+  if (start > 0 && !C) return BF_ERR_INVALID_ARGUMENT;
+  return layer_prefill_impl(L, x, q, k, v, qr, kr, start, B, T, C, sink_k, sink_v, ns, 1, o, lse, ws, ws_bytes,
+                            stream, phase == 0 ? kPhaseBegin : kPhaseFinish, m_out, n_out);
 }
 
 }  // extern "C"

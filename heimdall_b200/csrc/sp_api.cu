@@ -19,7 +19,7 @@
 namespace bfb {
 size_t gdn_prefill_workspace(int B, int G, int T_steps, bool transform);
 int gdn_prefill_carve(GdnStreams& s, void* ws);
-int launch_gdn_prefill(GdnStreams s, cudaStream_t stream);
+int launch_gdn_prefill(GdnStreams s, cudaStream_t stream, int parts);
 
 static size_t al1k_sp(size_t x) { return (x + 1023) & ~size_t(1023); }
 
@@ -123,7 +123,7 @@ int bf_gdn_segment_transform(const void* k, int k_dtype, const void* v, int v_dt
   s.s0 = s0; s.s_out = n_out; s.m_out = m_out;
   s.err = st.err;
   gdn_prefill_carve(s, p);
-  return launch_gdn_prefill(s, stream);
+  return launch_gdn_prefill(s, stream, kGdnAll);
 }
 
 int bf_gdn_apply_prefix(const float* M, const float* N, int n_seg, const float* s0, float* s_in, int B, int G, int D,

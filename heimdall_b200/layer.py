@@ -131,7 +131,8 @@ class BifrostLayer:
             return self._decode(x, q, k, v, qr, kr, int(start), cache, memory)
         return self._prefill(x, q, k, v, qr, kr, int(start), cache, memory)
 
-    def _prefill(self, x, q, k, v, qr, kr, start, cache, memory, lse_out=None):
+    def _prefill_setup(self, x, q, k, v, qr, kr, start, cache, memory):
+        """Operands of one layer prefill: bf16 inputs, sinks, the cache in device layout, output, workspace."""
         B, t = x.shape[:2]
         H, G, D, W, S = self.H, self.G, self.D, self.window, self.sinks
         dev = x.device
@@ -177,12 +178,52 @@ class BifrostLayer:
         ring_case = cache is not None and start > 0
         nws = _lib.size("bf_layer_prefill_workspace", B, t, H, G, D, W, 1 if ring_case else 0)
         ws = torch.empty(nws, dtype=torch.uint8, device=dev)
+        return dict(args=(xb, qb, kb, vb, qrb, krb), B=B, t=t, start=start, rc=rc, sk=sk, sv=sv, ns=ns, o=o, ws=ws,
+                    nws=nws, cache=cache)
+
+    def _finish_cache(self, c):
+        if c["cache"] is not None:
+            c["cache"]["sink_k"], c["cache"]["sink_v"] = c["sk"], c["sv"]
+
+    def _prefill(self, x, q, k, v, qr, kr, start, cache, memory, lse_out=None):
+        c = self._prefill_setup(x, q, k, v, qr, kr, start, cache, memory)
+        xb, qb, kb, vb, qrb, krb = c["args"]
         _lib.call("bf_bifrost_layer_prefill", ctypes_ref(self._struct), ptr(xb), ptr(qb), ptr(kb), ptr(vb), ptr(qrb),
-                  ptr(krb), start, B, t, 0 if rc is None else ctypes_ref(rc), ptr(sk), ptr(sv), ns,
-                  1 if memory else 0, ptr(o), ptr(lse_out), ptr(ws), nws, stream_handle())
-        if cache is not None:
-            cache["sink_k"], cache["sink_v"] = sk, sv
-        return o
+                  ptr(krb), start, c["B"], c["t"], 0 if c["rc"] is None else ctypes_ref(c["rc"]), ptr(c["sk"]),
+                  ptr(c["sv"]), c["ns"], 1 if memory else 0, ptr(c["o"]), ptr(lse_out), ptr(c["ws"]), c["nws"],
+                  stream_handle())
+        self._finish_cache(c)
+        return c["o"]
+
+    def prefill_sp_begin(self, x, q, k, v, qr, kr, start: int, cache: dict):
+        """First phase of a sequence-parallel layer prefill of this rank's tokens (``heimdall_b200.sp``):
+        the memory inputs, the per-chunk products and this segment's state map.  ``cache`` holds the ring
+        (the W tokens before ``start``) and the sinks; its "S" is replaced by the incoming state before
+        ``prefill_sp_finish``.  Returns (M, N, handle): S_out = M S_in + N for the segment's write stream."""
+        check_cuda(x, q, k, v, qr, kr)
+        c = self._prefill_setup(x, q, k, v, qr, kr, int(start), cache, True)
+        B, G, D = c["B"], self.G, self.D
+        M = torch.empty(B, G, D, D, device=x.device, dtype=torch.float32)
+        N = torch.empty_like(M)
+        self._prefill_sp_call(c, 0, M, N)
+        return M, N, c
+
+    def prefill_sp_finish(self, handle):
+        """Second phase: the rest of the prefill from the incoming state now in ``cache["S"]``; returns o."""
+        c = handle
+        cache = c["cache"]
+        if c["rc"] is not None and "S" in cache:
+            c["rc"].S = ptr(cache["S"])
+        self._prefill_sp_call(c, 1, None, None)
+        self._finish_cache(c)
+        return c["o"]
+
+    def _prefill_sp_call(self, c, phase, M, N):
+        xb, qb, kb, vb, qrb, krb = c["args"]
+        _lib.call("bf_bifrost_layer_prefill_sp", ctypes_ref(self._struct), ptr(xb), ptr(qb), ptr(kb), ptr(vb),
+                  ptr(qrb), ptr(krb), c["start"], c["B"], c["t"], 0 if c["rc"] is None else ctypes_ref(c["rc"]),
+                  ptr(c["sk"]), ptr(c["sv"]), c["ns"], phase, ptr(M), ptr(N), ptr(c["o"]), None, ptr(c["ws"]),
+                  c["nws"], stream_handle())
 
     def student_host(self, x, q, k, v, qr, kr, start: int = 0, cache=None, memory: bool = True,
                      chunk: int = 4096, out=None):

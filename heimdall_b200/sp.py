@@ -8,14 +8,17 @@ empty cache.  Rank j holds tokens [j T, (j+1) T) and returns their outputs.  Two
   rank j-1 (a halo: x, k, v, kr) and the first S tokens of rank 0;
 * the memory: the delta-rule state after all earlier tokens.  Memory writes lag the window by W
   (hibrit.py:391-396), so rank j's write stream is the W halo tokens followed by its first T - W tokens.
-  Each rank computes the state map of its write stream, (M_j, N_j) with S_out = M_j S_in + N_j
-  (``functional.segment_transform``), the maps are all-gathered, and each rank folds the earlier ones
-  into its incoming state (``functional.apply_prefix``).
+  Each rank computes the state map of its write stream, (M_j, N_j) with S_out = M_j S_in + N_j, the maps
+  are all-gathered, and each rank folds the earlier ones into its incoming state
+  (``functional.apply_prefix``).
 
-Rank j then runs the ordinary layer prefill of its tokens with a cache built from the halo: the ring holds
-the halo tokens (slot = position mod W), the sinks are rank 0's first tokens and S is the incoming state.
-A prefill from such a cache is exactly the continuation of the sequence (the reference's mixed-parts
-property, tests/test_hibrit.py:78-90), so the outputs equal one pass over the whole sequence.
+Rank j runs the layer prefill of its tokens from a cache built from the halo: the ring holds the halo
+tokens (slot = position mod W), the sinks are rank 0's first tokens and S is the incoming state.  A
+prefill from such a cache is exactly the continuation of the sequence (the reference's mixed-parts
+property, tests/test_hibrit.py:78-90), so the outputs equal one pass over the whole sequence.  The
+prefill runs in two phases on one workspace (``BifrostLayer.prefill_sp_begin`` / ``prefill_sp_finish``):
+the first computes the memory inputs, the per-chunk products and the state map, the second everything
+that depends on the incoming state, so nothing is computed twice.
 
 Traffic per rank and layer: the halo (W tokens of x, k, v, kr: 33 MB at W = 2048, d = 5120) from the left
 neighbour, the sink rows from rank 0, and an all-gather of (M, N) (2 MB per rank at G = 4, D = 256).
@@ -33,16 +36,18 @@ def _peer(group, r: int) -> int:
 
 
 def _p2p_shift(tensors, rank: int, world: int, group):
-    """Send ``tensors`` to rank+1 and receive the same shapes from rank-1 (None on rank 0)."""
-    reqs, recv = [], None
+    """Send ``tensors`` to rank+1 and receive the same shapes from rank-1 (None on rank 0), as one batch
+    of point-to-point operations."""
+    ops, recv = [], None
     send = [t.contiguous() for t in tensors]          # held until the sends completed
     if rank > 0:
         recv = [torch.empty_like(t) for t in send]
-        reqs += [dist.irecv(r, src=_peer(group, rank - 1), group=group) for r in recv]
+        ops += [dist.P2POp(dist.irecv, r, _peer(group, rank - 1), group) for r in recv]
     if rank < world - 1:
-        reqs += [dist.isend(t, dst=_peer(group, rank + 1), group=group) for t in send]
-    for r in reqs:
-        r.wait()
+        ops += [dist.P2POp(dist.isend, t, _peer(group, rank + 1), group) for t in send]
+    if ops:
+        for r in dist.batch_isend_irecv(ops):
+            r.wait()
     return recv
 
 
@@ -75,8 +80,11 @@ def halo_cache(kr_h, v_h, km_h, g_h, b_h, sink_k, sink_v, S_in, start: int, W: i
     ring_beta[:, slot] = b_h
     ring_pos = torch.empty(W, device=dev, dtype=torch.int64)
     ring_pos[slot] = pos
-    return dict(ring_k=ring_k, ring_v=ring_v, ring_km=ring_km, ring_g=ring_g, ring_beta=ring_beta,
-                ring_pos=ring_pos, sink_k=sink_k, sink_v=sink_v, S=S_in)
+    cache = dict(ring_k=ring_k, ring_v=ring_v, ring_km=ring_km, ring_g=ring_g, ring_beta=ring_beta,
+                 ring_pos=ring_pos, sink_k=sink_k, sink_v=sink_v)
+    if S_in is not None:
+        cache["S"] = S_in
+    return cache
 
 
 def student_sp(L, x, q, k, v, qr, kr, group=None, memory: bool = True):
@@ -105,34 +113,30 @@ def student_sp(L, x, q, k, v, qr, kr, group=None, memory: bool = True):
     # halo: the last W tokens of the previous rank, and their memory inputs
     halo = _p2p_shift([x[:, -W:], k[:, -W:], v[:, -W:], kr[:, :, -W:]], rank, world, group)
     first = rank == 0
+    cache = {}
     if not first:
         km_h, g_h, b_h = _halo_inputs(L, halo, start, W, q)
-    G, D = k.shape[2], k.shape[3]
-    zero = torch.zeros(B, G, D, D, device=x.device, dtype=torch.float32)
-    S_in = zero
-    if memory:
-        _, km, g, beta, _ = L.mem_inputs(x, q, k, pos0=start)
-        kw, gw, bw, vw = write_stream(None if first else km_h, None if first else g_h, None if first else b_h,
-                                      None if first else halo[2], km, g, beta, v, T, W, first)
-        if kw.shape[1] > 0:
-            M, N = F_.segment_transform(kw, vw, gw, bw)
-        else:   # no memory writes in this segment: identity map
-            M = torch.eye(D, device=x.device, dtype=torch.float32).expand(B, G, D, D).contiguous()
-            N = zero.clone()
-        if world > 1:
-            Ml = [torch.empty_like(M) for _ in range(world)]
-            Nl = [torch.empty_like(N) for _ in range(world)]
-            dist.all_gather(Ml, M.contiguous(), group=group)
-            dist.all_gather(Nl, N.contiguous(), group=group)
-            Ms, Ns = torch.stack(Ml), torch.stack(Nl)
-        else:
-            Ms, Ns = M[None], N[None]
-        S_in = F_.apply_prefix(Ms[:rank], Ns[:rank])[rank].contiguous()
-    if first:
-        cache = {"S": S_in}
+        cache = halo_cache(halo[3], halo[2], km_h, g_h, b_h, sink_k, sink_v, None, start, W)
+    if not memory:
+        o = L.student(x, q, k, v, qr, kr, start, cache, memory=False)
+        return o, cache
+    # phase 1: this segment's state map (memory inputs and per-chunk products are kept for phase 2)
+    M, N, handle = L.prefill_sp_begin(x, q, k, v, qr, kr, start, cache)
+    if world > 1:
+        Ml = [torch.empty_like(M) for _ in range(world)]
+        Nl = [torch.empty_like(N) for _ in range(world)]
+        dist.all_gather(Ml, M.contiguous(), group=group)
+        dist.all_gather(Nl, N.contiguous(), group=group)
+        Ms, Ns = torch.stack(Ml), torch.stack(Nl)
     else:
-        cache = halo_cache(halo[3], halo[2], km_h, g_h, b_h, sink_k, sink_v, S_in, start, W)
-    o = L.student(x, q, k, v, qr, kr, start, cache, memory=memory)
+        Ms, Ns = M[None], N[None]
+    S_in = F_.apply_prefix(Ms[:rank], Ns[:rank])[rank]
+    if cache.get("S") is not None:
+        cache["S"].copy_(S_in)
+    else:
+        cache["S"] = S_in.contiguous()
+    # phase 2: the rest of the layer from the incoming state
+    o = L.prefill_sp_finish(handle)
     return o, cache
 
 

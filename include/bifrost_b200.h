@@ -226,6 +226,19 @@ int bf_gdn_segment_transform(const void* k, int k_dtype, const void* v, int v_dt
 int bf_gdn_apply_prefix(const float* M, const float* N, int n_seg, const float* s0, float* s_in, int B, int G,
                         int D, bf_stream_t stream);
 
+/*
+ * The fused layer prefill in two phases for sequence parallelism (same arguments and workspace for both):
+ * phase 0 computes the memory inputs, the per-chunk products and the state map of this segment's
+ * write stream (m_out, n_out [B,G,D,D] fp32: S_out = M S_in + N, N from a zero state); phase 1 runs
+ * the rest from the incoming state cache->S (the state recurrence, the memory reads, the window, the
+ * gate and mix, and the cache write) without recomputing phase 0's work.  memory is on; o/lse as in
+ * bf_bifrost_layer_prefill (written by phase 1).
+ */
+int bf_bifrost_layer_prefill_sp(const bf_layer* L, const void* x, const void* q, const void* k, const void* v,
+                                const void* qr, const void* kr, long long start, int B, int T, bf_ring_cache* cache,
+                                const void* sink_k, const void* sink_v, int ns, int phase, float* m_out,
+                                float* n_out, float* o, float* lse, void* ws, size_t ws_bytes, bf_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

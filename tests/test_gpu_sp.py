@@ -176,3 +176,38 @@ def test_student_sp_two_gpus(tmp_path):
     parts = [torch.load(f"{out}.{r}") for r in range(2)]
     assert ob.rel_l2(torch.cat([pt["o"] for pt in parts], 1), o_ref.cpu()) < O_TOL
     assert ob.rel_l2(parts[1]["S"], cache["S"].cpu()) < S_TOL
+
+
+def test_two_phase_prefill_matches_one_call():
+    """prefill_sp_begin + prefill_sp_finish == one prefill from the same cache, and the begin phase's state
+    map equals segment_transform of the segment's write stream (halo tokens, then this rank's tokens)."""
+    dev = _dev()
+    from heimdall_b200 import BifrostLayer, sp
+    from heimdall_b200.functional import segment_transform
+    H, G, D, d, W, S, T = 24, 4, 256, 128, 256, 4, 700
+    p = layer_params(H, G, D, d, window=W, sinks=S, archival=1, seed=12)
+    L = BifrostLayer.from_params(p, dev)
+    x, q, k, v, qr, kr = (z.to(dev) for z in _layer_inputs(H, G, D, d, 2 * T, seed=13))
+    start = T
+    prev = (x[:, :T], k[:, :T], v[:, :T], kr[:, :, :T])
+    halo = [prev[0][:, -W:].contiguous(), prev[1][:, -W:].contiguous(), prev[2][:, -W:].contiguous(),
+            prev[3][:, :, -W:].contiguous()]
+    mine = [x[:, T:].contiguous(), q[:, T:].contiguous(), k[:, T:].contiguous(), v[:, T:].contiguous(),
+            qr[:, :, T:].contiguous(), kr[:, :, T:].contiguous()]
+    km_h, g_h, b_h = sp._halo_inputs(L, halo, start, W, mine[1])
+    sink_k, sink_v = kr[:, :, :S].contiguous(), v[:, :S].transpose(1, 2).contiguous()
+    S_in = torch.randn(1, G, D, D, generator=torch.Generator().manual_seed(3)).to(dev) * 0.05
+    c1 = sp.halo_cache(halo[3], halo[2], km_h, g_h, b_h, sink_k, sink_v, S_in.clone(), start, W)
+    o1 = L.student(*mine, start, c1)
+    c2 = sp.halo_cache(halo[3], halo[2], km_h, g_h, b_h, sink_k, sink_v, None, start, W)
+    M, N, h = L.prefill_sp_begin(*mine, start, c2)
+    c2["S"].copy_(S_in)
+    o2 = L.prefill_sp_finish(h)
+    torch.cuda.synchronize()
+    assert ob.rel_l2(o2.cpu(), o1.cpu()) < 1e-6
+    assert ob.rel_l2(c2["S"].cpu(), c1["S"].cpu()) < 1e-6
+    _, km, g, beta, _ = L.mem_inputs(mine[0], mine[1], mine[2], pos0=start)
+    kw, gw, bw, vw = sp.write_stream(km_h, g_h, b_h, halo[2], km, g, beta, mine[3], T, W, False)
+    M2, N2 = segment_transform(kw, vw, gw, bw)
+    torch.cuda.synchronize()
+    assert ob.rel_l2(M.cpu(), M2.cpu()) < 1e-5 and ob.rel_l2(N.cpu(), N2.cpu()) < 1e-5

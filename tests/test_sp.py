@@ -33,6 +33,24 @@ class OracleLayer:
         return ob.student(self.p, x.double(), q.double(), k.double(), v.double(), qr.double(), kr.double(), start,
                           cache, memory=memory, dtype=torch.float64)
 
+    def prefill_sp_begin(self, x, q, k, v, qr, kr, start, cache):
+        from heimdall_b200 import sp
+        t, W = x.shape[1], self.window
+        _, km, g, beta, _ = self.mem_inputs(x, q, k, pos0=start)
+        if start == 0:
+            kw, gw, bw, vw = sp.write_stream(None, None, None, None, km, g, beta, v, t, W, True)
+        else:   # the halo in time order, read back from the ring (slot = position mod W)
+            idx = torch.arange(start - W, start) % W
+            kw, gw, bw, vw = sp.write_stream(cache["ring_km"][:, idx], cache["ring_g"][:, idx],
+                                             cache["ring_beta"][:, idx], cache["ring_v"][:, :, idx].transpose(1, 2),
+                                             km, g, beta, v, t, W, False)
+        M, N = oracle_segment_transform(kw, vw, gw, bw)
+        return M, N, (x, q, k, v, qr, kr, start, cache)
+
+    def prefill_sp_finish(self, h):
+        x, q, k, v, qr, kr, start, cache = h
+        return self.student(x, q, k, v, qr, kr, start, cache, True)
+
 
 def oracle_segment_transform(k, v, g, beta, s0=None):
     B, n, Gh, Dd = k.shape
@@ -66,7 +84,6 @@ def _rank_main(rank, world, port, memory, out_path):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         from heimdall_b200 import sp
-        sp.F_.segment_transform = oracle_segment_transform
         sp.F_.apply_prefix = oracle_apply_prefix
         p = layer_params(H, G, D, DM, window=W, sinks=S, archival=1, seed=5)
         x, q, k, v, qr, kr = _inputs()
