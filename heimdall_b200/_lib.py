@@ -30,8 +30,8 @@ SIGNATURES = {
     "bf_layer_decode_workspace": [_I, _I, _I, _I, _I],
     "bf_bifrost_layer_decode": [_P, _P, _P, _P, _P, _P, _P, _P, _I, _P, _I, _P, _P, _P, _Z, _P],
     "bf_bifrost_layer_decode_noalloc": [_P, _P, _P, _P, _P, _P, _P, _P, _I, _P, _I, _P, _P, _P],
-    "bf_gdn_chunk_workspace": [_I, _I, _I, _I, _I],
-    "bf_gdn_chunk_fwd": [_P, _I, _P, _I, _P, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _Z, _P],
+    "bf_gdn_chunk_workspace": [_I, _I, _I, _I, _I, _I],
+    "bf_gdn_chunk_fwd": [_P, _I, _P, _I, _P, _I, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _Z, _P],
     "bf_window_workspace": [_I, _I, _I, _I],
     "bf_window_attn_fwd": [_P, _P, _P, _L, _L, _L, _P, _P, _I, _L, _L, _L, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P,
                            _Z, _P],

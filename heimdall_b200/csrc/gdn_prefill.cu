@@ -35,6 +35,18 @@ struct RowSrc {
 
 __device__ __forceinline__ RowSrc write_row(const GdnStreams& s, int b, int gg, int u) {
   RowSrc r{nullptr, nullptr, nullptr, 0.f, 0.f, true};
+  if (s.chunk_tok0) {   // packed sequences: row u % kGC of global chunk u / kGC
+    const int c = u / kGC, rr = u % kGC;
+    if (rr >= s.chunk_len[c]) return r;
+    const size_t tok = (size_t)s.chunk_tok0[c] + rr;
+    r.k = s.km + (tok * s.G + gg) * kGD;
+    if (s.v32) r.v32 = s.v32 + (tok * s.G + gg) * kGD;
+    else r.v = s.v + (tok * s.G + gg) * kGD;
+    r.g = s.g[tok * s.G + gg];
+    r.beta = s.beta[tok * s.G + gg];
+    r.zero = false;
+    return r;
+  }
   if (u >= s.n_steps) return r;
   if (u < s.nring) {
     const long long kp = s.ring_pos0 + u;
@@ -103,6 +115,7 @@ __global__ void __launch_bounds__(kP1_Threads, 1) gdn_p1_kernel(GdnStreams s) {
   const int c = blockIdx.x, bg = blockIdx.y, b = bg / s.G, gg = bg % s.G;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const size_t rowbase = (size_t)bg * s.n_pad + (size_t)c * kGC;
+  if (s.chunk_tok0 && c >= s.seq_chunk0[s.n_seq]) return;   // grid sized for the most chunks possible
 
   if (t == 0) {
     mbar_init(bar_kk, 1);
@@ -342,7 +355,16 @@ __global__ void __launch_bounds__(kP2_Threads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 6);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 7);
 
-  const int bg = blockIdx.y;
+  // per-chunk arrays are indexed by bg = (batch, KV head); with packed sequences (B = 1) bg is the KV head and
+  // this CTA walks the chunks of sequence blockIdx.y / G; the states are per (sequence or batch, KV head)
+  int bg = blockIdx.y, sidx = blockIdx.y, c_begin = 0, c_end = s.n_chunks;
+  if (s.chunk_tok0) {
+    const int i = blockIdx.y / s.G;
+    bg = blockIdx.y % s.G;
+    c_begin = s.seq_chunk0[i];
+    c_end = s.seq_chunk0[i + 1];
+  }
+  const int ncl = c_end - c_begin;          // chunks of this CTA; barrier phases count from its first
   // column blocks beyond the state's (transform mode only) run the map path: start at the identity, no inputs
   const bool mpath = blockIdx.x >= kGD / kP2_NB;
   const int col0 = (mpath ? blockIdx.x - kGD / kP2_NB : blockIdx.x) * kP2_NB;
@@ -373,15 +395,16 @@ __global__ void __launch_bounds__(kP2_Threads, 1)
       tma_prefetch(&wmap);
       tma_prefetch(&ktmap);
       int iw = 0, ik = 0;
-      for (int c = 0; c < nch; ++c) {
-        if (c >= 1 && !mbar_wait(bar_m1, (c - 1) & 1, abort_flag, s.err, 0x51)) break;
+      for (int j = 0; j < ncl; ++j) {
+        const int c = c_begin + j;
+        if (j >= 1 && !mbar_wait(bar_m1, (j - 1) & 1, abort_flag, s.err, 0x51)) break;
         mbar_expect_tx(bar_w, kP2_SmemW);
         tma_load_3d(sW, &wmap, bar_w, 0, bg * s.n_pad + c * kGC, 0);
-        iw = c + 1;
-        if (c >= 1 && !mbar_wait(bar_m2, (c - 1) & 1, abort_flag, s.err, 0x52)) break;
+        iw = j + 1;
+        if (j >= 1 && !mbar_wait(bar_m2, (j - 1) & 1, abort_flag, s.err, 0x52)) break;
         mbar_expect_tx(bar_kt, kP2_SmemKT);
         tma_load_3d(sKT, &ktmap, bar_kt, 0, (bg * nch + c) * kGD, 0);
-        ik = c + 1;
+        ik = j + 1;
       }
       if (iw > 0) mbar_wait(bar_w, (iw - 1) & 1, nullptr, s.err, 0x53);
       if (ik > 0) mbar_wait(bar_kt, (ik - 1) & 1, nullptr, s.err, 0x54);
@@ -390,16 +413,16 @@ __global__ void __launch_bounds__(kP2_Threads, 1)
     if (lane == 0) {
       constexpr uint32_t id1 = idesc_f16(128, kP2_NB, 0);
       const uint32_t aW = smem_u32(sW), bST = smem_u32(sST), aKT = smem_u32(sKT), bVT = smem_u32(sVT);
-      for (int c = 0; c < nch; ++c) {
-        if (!mbar_wait(bar_w, c & 1, abort_flag, s.err, 0x55)) break;
-        if (!mbar_wait(bar_st, c & 1, abort_flag, s.err, 0x56)) break;
+      for (int j = 0; j < ncl; ++j) {
+        if (!mbar_wait(bar_w, j & 1, abort_flag, s.err, 0x55)) break;
+        if (!mbar_wait(bar_st, j & 1, abort_flag, s.err, 0x56)) break;
         tc_fence_after();
 #pragma unroll
         for (int ks = 0; ks < kGD / 16; ++ks)
           umma_f16_ss(tmem, sdesc_kstep(aW, 128, ks), sdesc_kstep(bST, kP2_NB, ks), id1, ks > 0);
         umma_commit(bar_m1);
-        if (!mbar_wait(bar_kt, c & 1, abort_flag, s.err, 0x57)) break;
-        if (!mbar_wait(bar_vt, c & 1, abort_flag, s.err, 0x58)) break;
+        if (!mbar_wait(bar_kt, j & 1, abort_flag, s.err, 0x57)) break;
+        if (!mbar_wait(bar_vt, j & 1, abort_flag, s.err, 0x58)) break;
         tc_fence_after();
 #pragma unroll
         for (int mt = 0; mt < 2; ++mt) {
@@ -424,7 +447,7 @@ __global__ void __launch_bounds__(kP2_Threads, 1)
         S1[e] = (r + 128 == col0 + e) ? 1.f : 0.f;
       }
     } else if (s.s0) {
-      const float* sp = s.s0 + (size_t)bg * kGD * kGD;
+      const float* sp = s.s0 + (size_t)sidx * kGD * kGD;
 #pragma unroll
       for (int e = 0; e < kP2_NB; e += 4) {
         const float4 x0 = *reinterpret_cast<const float4*>(sp + (size_t)r * kGD + col0 + e);
@@ -438,7 +461,8 @@ __global__ void __launch_bounds__(kP2_Threads, 1)
     }
     bool alive = true;
     float lsum = 0.f;   // map path: log of the cumulative decay
-    for (int c = 0; c < nch && alive; ++c) {
+    for (int j = 0; j < ncl && alive; ++j) {
+      const int c = c_begin + j;
       // stage S^T (fp16) as the B operand of v' = u - w S, and store it for P3
 #pragma unroll
       for (int e = 0; e < kP2_NB; ++e) {
@@ -474,7 +498,7 @@ __global__ void __launch_bounds__(kP2_Threads, 1)
           uu[2 * e + 1] = f2.y;
         }
       }
-      if (!mbar_wait_warp(bar_m1, c & 1, abort_flag, s.err, 0x59)) { alive = false; break; }
+      if (!mbar_wait_warp(bar_m1, j & 1, abort_flag, s.err, 0x59)) { alive = false; break; }
       tc_fence_after();
       float dv[kP2_NB];
       tmem_ld16_wait(trow, dv);
@@ -490,7 +514,7 @@ __global__ void __launch_bounds__(kP2_Threads, 1)
       mbar_arrive(bar_vt);
       const float lgc = s.gc[(size_t)bg * s.n_pad + (size_t)c * kGC + kGC - 1];
       const float decay = __expf(lgc);
-      if (!mbar_wait_warp(bar_m2, c & 1, abort_flag, s.err, 0x5a)) { alive = false; break; }
+      if (!mbar_wait_warp(bar_m2, j & 1, abort_flag, s.err, 0x5a)) { alive = false; break; }
       tc_fence_after();
       float d0[kP2_NB], d1[kP2_NB];
       tmem_ld16_wait(trow + kP2_NB, d0);
@@ -523,7 +547,7 @@ __global__ void __launch_bounds__(kP2_Threads, 1)
       }
     }
     if (alive) {
-      float* so = (mpath ? s.m_out : s.s_out) + (size_t)bg * kGD * kGD;
+      float* so = (mpath ? s.m_out : s.s_out) + (size_t)sidx * kGD * kGD;
 #pragma unroll
       for (int e = 0; e < kP2_NB; e += 4) {
         *reinterpret_cast<float4*>(so + (size_t)r * kGD + col0 + e) = make_float4(S0[e], S0[e + 1], S0[e + 2], S0[e + 3]);
@@ -573,6 +597,10 @@ __global__ void __launch_bounds__(kP3_Threads, 1)
   const int bg = b * G + gg;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int nch = s.n_chunks;
+  if (s.chunk_tok0 && c >= s.seq_chunk0[s.n_seq]) return;   // grid sized for the most chunks possible
+  // query/output row of chunk row 0 and the number of valid rows of this chunk
+  const long long qrow0 = s.chunk_tok0 ? (long long)s.chunk_tok0[c] : (long long)b * s.T + s.qoff + (long long)c * kGC;
+  const int nvalid = s.chunk_tok0 ? s.chunk_len[c] : s.n_steps - c * kGC;
   if (t == 0) {
     for (int i = 0; i < 7; ++i) mbar_init(bars + i, (i == 4 || i == 6) ? 128 : 1);
     *abort_flag = 0;
@@ -596,7 +624,7 @@ __global__ void __launch_bounds__(kP3_Threads, 1)
       tma_prefetch(&vmap);
       // read rows c*128.. of query stream -> query token qoff + c*128 + i (4-D map: d, token, atom, head)
       mbar_expect_tx(bar_qk, kP3_SmemQ + kGC * kGD * 2);
-      tma_load_4d(sQ, &qmap, bar_qk, 0, b * s.T + s.qoff + c * kGC, 0, h);
+      tma_load_4d(sQ, &qmap, bar_qk, 0, (int)qrow0, 0, h);
       tma_load_3d(sKS, &kmap, bar_qk, 0, bg * s.n_pad + c * kGC, 0);
       int ns_ = 0, nv_ = 0;
       bool ok = mbar_wait(bar_qkd, 0, abort_flag, s.err, 0x61);
@@ -673,10 +701,9 @@ __global__ void __launch_bounds__(kP3_Threads, 1)
       tc_fence_before();
       mbar_arrive(bar_p);
     }
-    const int step = c * kGC + r;
-    const bool row_ok = step < s.n_steps;
+    const bool row_ok = r < nvalid;
     const float eci = __expf(ci);
-    float* orow = s.o + (((size_t)b * s.T + s.qoff + step) * H + h) * kGD;
+    float* orow = s.o + (((size_t)qrow0 + r) * H + h) * kGD;
     for (int half = 0; half < 2 && alive; ++half) {
       alive = mbar_wait_warp(bar_o, half & 1, abort_flag, s.err, 0x6c);
       if (!alive) break;
@@ -707,6 +734,48 @@ __global__ void __launch_bounds__(kP3_Threads, 1)
 }
 
 // ============================================================================================ launch
+// chunk table of packed sequences (one CTA): sequence i has ceil(len_i / kGC) chunks, the last one partial
+__global__ void __launch_bounds__(1024) build_chunk_table_kernel(const int* __restrict__ cu_seqlens, int n_seq,
+                                                                 int max_chunks, int* __restrict__ seq_chunk0,
+                                                                 int* __restrict__ chunk_tok0,
+                                                                 int* __restrict__ chunk_len, unsigned int* err) {
+  __shared__ int total;
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    seq_chunk0[0] = 0;
+    for (int i = 0; i < n_seq; ++i) {
+      const int len = cu_seqlens[i + 1] - cu_seqlens[i];
+      acc += len > 0 ? (len + kGC - 1) / kGC : 0;
+      seq_chunk0[i + 1] = acc;
+    }
+    if (acc > max_chunks) {   // cu_seqlens inconsistent with T: no chunks at all rather than out-of-range work
+      record_error(err, 0x4f);
+      for (int i = 0; i <= n_seq; ++i) seq_chunk0[i] = 0;
+      acc = 0;
+    }
+    total = acc;
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < total; c += blockDim.x) {
+    int lo = 0, hi = n_seq - 1;          // the sequence i with seq_chunk0[i] <= c < seq_chunk0[i + 1]
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (seq_chunk0[mid] <= c) lo = mid;
+      else hi = mid - 1;
+    }
+    const int tok0 = cu_seqlens[lo] + (c - seq_chunk0[lo]) * kGC;
+    chunk_tok0[c] = tok0;
+    chunk_len[c] = min(kGC, cu_seqlens[lo + 1] - tok0);
+  }
+}
+
+int launch_chunk_table(const int* cu_seqlens, int n_seq, int max_chunks, int* seq_chunk0, int* chunk_tok0,
+                       int* chunk_len, unsigned int* err, cudaStream_t stream) {
+  build_chunk_table_kernel<<<1, 1024, 0, stream>>>(cu_seqlens, n_seq, max_chunks, seq_chunk0, chunk_tok0, chunk_len,
+                                                   err);
+  return cudaGetLastError() == cudaSuccess ? BF_OK : BF_ERR_CUDA;
+}
+
 size_t gdn_prefill_workspace(int B, int G, int T_steps, bool transform) {
   const size_t n_pad = (size_t)((T_steps + kGC - 1) / kGC) * kGC;
   const size_t nch = n_pad / kGC;
@@ -764,7 +833,8 @@ int launch_gdn_prefill(GdnStreams s, cudaStream_t stream, int parts) {
   rc = make_tmap_kmajor(&ktmap, s.ktT, BF_F16, (uint64_t)s.B * s.G * s.n_chunks * kGD, kGC, kGC, kGD, 2);
   if (rc) return rc;
   stage_mark(ST_GDN_P2, 0, stream);
-  gdn_p2_kernel<<<dim3((s.m_out ? 2 : 1) * (kGD / kP2_NB), s.B * s.G), kP2_Threads, kP2_Smem, stream>>>(wmap, ktmap, s);
+  gdn_p2_kernel<<<dim3((s.m_out ? 2 : 1) * (kGD / kP2_NB), s.chunk_tok0 ? s.G * s.n_seq : s.B * s.G), kP2_Threads,
+                  kP2_Smem, stream>>>(wmap, ktmap, s);
   if (cudaGetLastError() != cudaSuccess) return BF_ERR_CUDA;
   stage_mark(ST_GDN_P2, 1, stream);
   if (s.m_out) return BF_OK;   // segment transform: no reads

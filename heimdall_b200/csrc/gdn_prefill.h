@@ -45,6 +45,13 @@ struct GdnStreams {
   // segment-transform mode (m_out != null): no reads; P2 also runs the recurrence from the identity with
   // zero inputs, whose final value is the segment's state map M (S_out = M S_in + N), and writes it here
   float* m_out;                // [B,G,D,D]
+  // packed variable-length sequences (chunk_tok0 != null; B = 1, no ring, qoff = 0): global chunk c holds
+  // packed tokens chunk_tok0[c] .. + chunk_len[c] - 1 of one sequence; sequence i owns chunks
+  // seq_chunk0[i] .. seq_chunk0[i+1] - 1 (seq_chunk0[n_seq] = number of chunks); states are per sequence
+  const int* chunk_tok0;
+  const int* chunk_len;
+  const int* seq_chunk0;
+  int n_seq;
   unsigned int* err;
 };
 

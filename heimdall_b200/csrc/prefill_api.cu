@@ -16,6 +16,8 @@ int check_layer(const bf_layer* L);
 size_t gdn_prefill_workspace(int B, int G, int T_steps, bool transform);
 int gdn_prefill_carve(GdnStreams& s, void* ws);
 int launch_gdn_prefill(GdnStreams s, cudaStream_t stream, int parts);
+int launch_chunk_table(const int* cu_seqlens, int n_seq, int max_chunks, int* seq_chunk0, int* chunk_tok0,
+                       int* chunk_len, unsigned int* err, cudaStream_t stream);
 int launch_vt_prep(const __nv_bfloat16* v, long long vb, long long vg, long long vj, const __nv_bfloat16* ring_v,
                    int nring, long long ring_pos0, int W, int B, int G, int Tk, int Tkp, __half* vt,
                    cudaStream_t stream);
@@ -82,24 +84,36 @@ using namespace bfb;
 extern "C" {
 
 // ================================================================================ delta rule op
-size_t bf_gdn_chunk_workspace(int B, int T, int G, int R, int D) {
-  if (B <= 0 || T <= 0 || G <= 0 || R <= 0 || D != 256) return 0;
-  return al1k((size_t)B * T * G * R * D * 2) + al1k((size_t)B * T * G * D * 4) + gdn_prefill_workspace(B, G, T, false);
+// packed sequences: at most T / kGC + n_seq chunks (each sequence adds at most one partial chunk)
+static int max_chunks_for(int T, int n_seq) { return (T + kGC - 1) / kGC + n_seq; }
+
+size_t bf_gdn_chunk_workspace(int B, int T, int G, int R, int D, int n_seq) {
+  if (B <= 0 || T <= 0 || G <= 0 || R <= 0 || D != 256 || n_seq < 0) return 0;
+  size_t n = al1k((size_t)B * T * G * R * D * 2) + al1k((size_t)B * T * G * D * 4);
+  if (n_seq > 0) {
+    const int mc = max_chunks_for(T, n_seq);
+    n += al1k((size_t)(n_seq + 1) * 4) + 2 * al1k((size_t)mc * 4);
+    return n + gdn_prefill_workspace(1, G, mc * kGC, false);
+  }
+  return n + gdn_prefill_workspace(B, G, T, false);
 }
 
 int bf_gdn_chunk_fwd(const void* q, int q_dtype, const void* k, int k_dtype, const void* v, int v_dtype,
-                     const float* g, const float* beta, const float* s0, float* o, float* s_out, int B, int T, int G,
-                     int R, int D, void* ws, size_t ws_bytes, bf_stream_t stream) {
+                     const float* g, const float* beta, const float* s0, float* o, float* s_out,
+                     const int* cu_seqlens, int n_seq, int B, int T, int G, int R, int D, void* ws, size_t ws_bytes,
+                     bf_stream_t stream) {
   if (!q || !k || !v || !g || !beta || !o || !s_out || !ws) return BF_ERR_INVALID_ARGUMENT;
   if (B <= 0 || T <= 0 || G <= 0 || R <= 0 || R > 8) return BF_ERR_INVALID_ARGUMENT;
+  if (cu_seqlens ? (n_seq <= 0 || B != 1) : n_seq != 0) return BF_ERR_INVALID_ARGUMENT;
   if (D != 256) return BF_ERR_UNSUPPORTED;
   for (int dt : {q_dtype, k_dtype, v_dtype})
     if (dt != BF_F32 && dt != BF_BF16) return BF_ERR_INVALID_ARGUMENT;
-  if (ws_bytes < bf_gdn_chunk_workspace(B, T, G, R, D)) return BF_ERR_WORKSPACE;
+  if (ws_bytes < bf_gdn_chunk_workspace(B, T, G, R, D, n_seq)) return BF_ERR_WORKSPACE;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || !aligned16(s_out) || !aligned16(ws) ||
       (s0 && !aligned16(s0)))
     return BF_ERR_ALIGNMENT;
-  if ((long long)B * G > 65535 || (long long)B * T * G * R > (1LL << 40)) return BF_ERR_UNSUPPORTED;
+  if ((long long)B * G > 65535 || (long long)G * n_seq > 65535 || (long long)B * T * G * R > (1LL << 40))
+    return BF_ERR_UNSUPPORTED;
   DeviceState st;
   int rc = device_state(&st);
   if (rc) return rc;
@@ -121,6 +135,22 @@ int bf_gdn_chunk_fwd(const void* q, int q_dtype, const void* k, int k_dtype, con
   s.B = B; s.G = G; s.R = R; s.T = T;
   s.n_steps = T;
   s.n_chunks = (T + kGC - 1) / kGC;
+  if (cu_seqlens) {
+    const int mc = max_chunks_for(T, n_seq);
+    int* seq_chunk0 = reinterpret_cast<int*>(p);
+    p += al1k((size_t)(n_seq + 1) * 4);
+    int* chunk_tok0 = reinterpret_cast<int*>(p);
+    p += al1k((size_t)mc * 4);
+    int* chunk_len = reinterpret_cast<int*>(p);
+    p += al1k((size_t)mc * 4);
+    rc = launch_chunk_table(cu_seqlens, n_seq, mc, seq_chunk0, chunk_tok0, chunk_len, st.err, stream);
+    if (rc) return rc;
+    s.n_chunks = mc;
+    s.chunk_tok0 = chunk_tok0;
+    s.chunk_len = chunk_len;
+    s.seq_chunk0 = seq_chunk0;
+    s.n_seq = n_seq;
+  }
   s.n_pad = s.n_chunks * kGC;
   s.nring = 0; s.W = 1; s.qoff = 0; s.ring_pos0 = 0;
   s.km = kf;

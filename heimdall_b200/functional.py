@@ -80,42 +80,54 @@ def _as_kernel_dtype(t):
     return t.contiguous() if t.dtype == torch.bfloat16 else t.float().contiguous()
 
 
-def delta_rule_gqa(q, k, v, g, beta, chunk: int = 64, state=None):
+def delta_rule_gqa(q, k, v, g, beta, chunk: int = 64, state=None, cu_seqlens=None):
     """GQA-native chunked gated delta rule (mirror of ``heimdall.motor.delta_rule_gqa``, motor.py:70-102).
 
     q [B,T,G,R,Dk]; k [B,T,G,Dk]; v [B,T,G,Dv]; g, beta [B,T,G]; state [B,G,Dk,Dv] or None.
     Returns o [B,T,G,R,Dv] and the final state [B,G,Dk,Dv], both fp32.  ``chunk`` is accepted for signature
     compatibility: the GPU scan always uses 128-token chunks (the recurrence, hence the result, does not
     depend on the chunk length).
+    ``cu_seqlens`` (int tensor [n+1], cumulative lengths, B = 1): the T tokens are n packed sequences, each
+    with its own recurrence; state and the returned final states are then [n,G,Dk,Dv].
     """
-    check_cuda(q, k, v, g, beta, state)
+    check_cuda(q, k, v, g, beta, state, cu_seqlens)
     B, T, G, R, D = q.shape
     if k.shape[-1] != D or v.shape[-1] != D:
         raise NotImplementedError("heimdall_b200 implements square states (Dk == Dv)")
     if D != 256:
         raise NotImplementedError("the tensor-core delta rule is built for head dim 256")
+    n_seq = 0
+    cu = None
+    if cu_seqlens is not None:
+        if B != 1:
+            raise ValueError("packed sequences (cu_seqlens) need batch size 1")
+        cu = cu_seqlens.to(device=q.device, dtype=torch.int32).contiguous()
+        n_seq = cu.numel() - 1
+        if n_seq <= 0:
+            raise ValueError("cu_seqlens needs at least two entries")
     dev = q.device
     qq, kk, vv = _as_kernel_dtype(q), _as_kernel_dtype(k), _as_kernel_dtype(v)
     gg, bb = g.float().contiguous(), beta.float().contiguous()
     s0 = None if state is None else state.float().contiguous()
     o = torch.empty(B, T, G, R, D, device=dev, dtype=torch.float32)
-    s_out = torch.empty(B, G, D, D, device=dev, dtype=torch.float32)
-    nws = _lib.size("bf_gdn_chunk_workspace", B, T, G, R, D)
+    s_out = torch.empty(n_seq if n_seq else B, G, D, D, device=dev, dtype=torch.float32)
+    nws = _lib.size("bf_gdn_chunk_workspace", B, T, G, R, D, n_seq)
     ws = _ws(nws, dev)
     _lib.call("bf_gdn_chunk_fwd", ptr(qq), _dt(qq), ptr(kk), _dt(kk), ptr(vv), _dt(vv), ptr(gg), ptr(bb), ptr(s0),
-              ptr(o), ptr(s_out), B, T, G, R, D, ptr(ws), nws, stream_handle())
+              ptr(o), ptr(s_out), ptr(cu), n_seq, B, T, G, R, D, ptr(ws), nws, stream_handle())
     return o, s_out
 
 
-def delta_rule(q, k, v, g, beta, chunk_size: int = 64, initial_state=None, backend: str = "auto"):
+def delta_rule(q, k, v, g, beta, chunk_size: int = 64, initial_state=None, backend: str = "auto", cu_seqlens=None):
     """Chunked gated delta rule (mirror of ``heimdall.kernels.delta_rule``, kernels.py:94-129 / 152-155).
 
     q, k: [B,T,H,Dk]; v: [B,T,H,Dv]; g, beta: [B,T,H]; initial_state [B,H,Dk,Dv] or None.
     Returns o [B,T,H,Dv] and the final state [B,H,Dk,Dv] (fp32).  ``backend`` is accepted for signature
     compatibility; this implementation always runs the CUDA kernels (there is no CPU path).
+    ``cu_seqlens``: packed sequences as in ``delta_rule_gqa`` (states [n,H,Dk,Dv]).
     """
     B, T, H, D = q.shape
-    o, s = delta_rule_gqa(q.reshape(B, T, H, 1, D), k, v, g, beta, chunk_size, initial_state)
+    o, s = delta_rule_gqa(q.reshape(B, T, H, 1, D), k, v, g, beta, chunk_size, initial_state, cu_seqlens)
     return o.reshape(B, T, H, D), s
 
 

@@ -166,11 +166,16 @@ int bf_bifrost_layer_decode_noalloc(const bf_layer* L, const void* x, const void
  * g, beta [B,T,G] fp32; s0 [B,G,D,D] fp32 or NULL (zero state); o [B,T,G*R,D] fp32;
  * s_out [B,G,D,D] fp32 (may alias s0).  D must be 256.  The GPU scan uses 128-token chunks and
  * fp16 tensor-core operands with fp32 accumulation and an fp32 state.
+ * Packed variable-length sequences: cu_seqlens (device int32 [n_seq + 1], cu_seqlens[0] = 0,
+ * non-decreasing, cu_seqlens[n_seq] = T) with B = 1; sequence i is tokens cu_seqlens[i] ..
+ * cu_seqlens[i+1] - 1, runs its own recurrence, and s0 / s_out are [n_seq,G,D,D].  cu_seqlens NULL
+ * and n_seq = 0: B sequences of T tokens.
  */
-size_t bf_gdn_chunk_workspace(int B, int T, int G, int R, int D);
+size_t bf_gdn_chunk_workspace(int B, int T, int G, int R, int D, int n_seq);
 int bf_gdn_chunk_fwd(const void* q, int q_dtype, const void* k, int k_dtype, const void* v, int v_dtype,
-                     const float* g, const float* beta, const float* s0, float* o, float* s_out, int B, int T,
-                     int G, int R, int D, void* ws, size_t ws_bytes, bf_stream_t stream);
+                     const float* g, const float* beta, const float* s0, float* o, float* s_out,
+                     const int* cu_seqlens, int n_seq, int B, int T, int G, int R, int D, void* ws, size_t ws_bytes,
+                     bf_stream_t stream);
 
 /* ------------------------------------------------------------------------------------------
  * Sliding-window + sink attention with log-sum-exp (fp32 softmax), replacing

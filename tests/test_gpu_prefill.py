@@ -3,6 +3,8 @@
 CUDA results are compared with the reference's own outputs (golden fixtures) and with the CPU oracle on
 seeded bf16-valued inputs.  Tolerances (north star): outputs rel-L2 <= 2e-3, states rel-L2 <= 1e-3.
 """
+import math
+
 import pytest
 import torch
 import torch.nn.functional as F
@@ -222,3 +224,56 @@ def test_student_host_matches_oracle(B, T, chunk):
     torch.cuda.synchronize()
     for key in ("ring_k", "ring_v", "ring_pos", "sink_k", "sink_v"):
         assert torch.equal(cache_h[key].cpu(), cache_d[key].cpu()), key
+
+
+def _varlen_inputs(lens, G, R, D, seed):
+    gen = torch.Generator().manual_seed(seed)
+    T = sum(lens)
+    q = F.normalize(torch.randn(1, T, G, R, D, generator=gen), dim=-1) * D ** -0.5
+    k = F.normalize(torch.randn(1, T, G, D, generator=gen), dim=-1)
+    v = torch.randn(1, T, G, D, generator=gen)
+    g = -torch.rand(1, T, G, generator=gen) * 0.05
+    beta = torch.rand(1, T, G, generator=gen)
+    s0 = torch.randn(len(lens), G, D, D, generator=gen) * 0.05
+    cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32)
+    return q, k, v, g, beta, s0, cu
+
+
+def test_varlen_matches_per_sequence_oracle():
+    """Packed sequences (cu_seqlens): each sequence runs its own recurrence from its own state, including
+    empty, one-token and chunk-boundary lengths."""
+    dev = _dev()
+    from heimdall_b200.functional import delta_rule_gqa
+    lens = [1, 127, 0, 128, 129, 300, 5, 700]
+    G, R, D = 4, 2, 256
+    q, k, v, g, beta, s0, cu = _varlen_inputs(lens, G, R, D, seed=31)
+    o, s = delta_rule_gqa(*(z.to(dev) for z in (q, k, v, g, beta)), 64, s0.to(dev), cu_seqlens=cu.to(dev))
+    torch.cuda.synchronize()
+    for i, n in enumerate(lens):
+        a, b = int(cu[i]), int(cu[i + 1])
+        if n == 0:
+            assert ob.rel_l2(s[i].cpu(), s0[i]) < 1e-6
+            continue
+        o_ref, s_ref = ob.gdn_gqa(q[:, a:b], k[:, a:b], v[:, a:b], g[:, a:b], beta[:, a:b], 64, s0[i:i + 1],
+                                  dtype=torch.float64)
+        assert ob.rel_l2(o[:, a:b].cpu(), o_ref) < O_TOL, i
+        assert ob.rel_l2(s[i:i + 1].cpu(), s_ref) < S_TOL, i
+
+
+def test_varlen_config4_matches_separate_calls():
+    """BASELINE config 4 shapes: 8 sequences, lengths round(exp U[ln 2048, ln 65536]) (seed 0), packed;
+    the packed call equals one call per sequence (same chunking per sequence, so up to rounding)."""
+    dev = _dev()
+    from heimdall_b200.functional import delta_rule_gqa
+    gen = torch.Generator().manual_seed(0)
+    lens = torch.exp(torch.empty(8).uniform_(math.log(2048), math.log(65536), generator=gen)).round().long().tolist()
+    G, R, D = 4, 2, 256
+    q, k, v, g, beta, s0, cu = _varlen_inputs(lens, G, R, D, seed=0)
+    to = lambda z: z.to(dev)
+    o, s = delta_rule_gqa(to(q), to(k), to(v.to(torch.bfloat16)), to(g), to(beta), 64, to(s0), cu_seqlens=to(cu))
+    for i in range(8):
+        a, b = int(cu[i]), int(cu[i + 1])
+        o1, s1 = delta_rule_gqa(to(q[:, a:b]), to(k[:, a:b]), to(v[:, a:b].to(torch.bfloat16)), to(g[:, a:b]),
+                                to(beta[:, a:b]), 64, to(s0[i:i + 1]))
+        assert ob.rel_l2(o[:, a:b].cpu(), o1.cpu()) < 1e-5, i
+        assert ob.rel_l2(s[i:i + 1].cpu(), s1.cpu()) < 1e-5, i
