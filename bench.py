@@ -15,6 +15,7 @@ stream), ``layer_roofline`` (all algorithmic FLOPs of the step), ``cpu_baseline`
 a bounded sample), ``e2e`` (host buffers in, host output back, copies inside the timed region),
 ``decode`` (64 sequences x 12 layers, one token per sequence per step),
 ``sp`` (one 131072-token sequence split over the N GPUs, sequence-parallel prefill),
+``delta_rule`` (BASELINE configs 0 and 4: the chunked delta-rule op alone, and on packed sequences),
 ``clocks`` (nvidia-smi samples during the timed region) and ``gpu_launches``.
 """
 from __future__ import annotations
@@ -261,6 +262,62 @@ def run_sp(L, device, ctx, T_total=131072, steps=5, warmup=2):
             "value": T_total / (ms / 1e3), "unit": "tok/s", "steps": steps, "warmup": warmup}
 
 
+def _time_device(fn, steps, warmup):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / steps
+
+
+def run_delta_configs(device, steps=10, warmup=3):
+    """BASELINE configs 0 and 4 (the chunked delta-rule op alone, ``delta_rule`` / ``delta_rule_gqa``):
+    config 0 = B=1, 4 heads, T=4096, D=256, fp32 inputs (q, k unit-norm, v ~ N(0,1), beta = sigmoid(N(0,1)),
+    g = -e^{A_log} softplus(a) with A_log ~ U(-4,0), a ~ N(0,1)); config 4 = 8 packed sequences of
+    round(exp U[ln 2048, ln 65536]) tokens (seed 0) with cu_seqlens, 4 KV heads x 6 query heads, fixed-rate
+    decays (half-lives logspace(log10 2048, 6, 4), the last head archival)."""
+    import torch.nn.functional as F
+    from heimdall_b200.functional import delta_rule, delta_rule_gqa
+    out = {}
+    torch.manual_seed(0)
+    Hc, Tc = 4, 4096
+    q = F.normalize(torch.randn(1, Tc, Hc, D), dim=-1)
+    k = F.normalize(torch.randn(1, Tc, Hc, D), dim=-1)
+    v = torch.randn(1, Tc, Hc, D)
+    beta = torch.sigmoid(torch.randn(1, Tc, Hc))
+    A_log = torch.empty(Hc).uniform_(-4, 0)
+    g = -A_log.exp() * F.softplus(torch.randn(1, Tc, Hc))
+    args = [z.to(device) for z in (q, k, v, g, beta)]
+    ms = _time_device(lambda: delta_rule(*args, 64, None), steps, warmup)
+    out["config0"] = {"workload": "BASELINE config 0: delta rule, B=1, H=4, T=4096, D=256, fp32 inputs",
+                      "value": Tc / (ms / 1e3), "unit": "tok/s", "ms_per_step": ms}
+    gen = torch.Generator().manual_seed(0)
+    lens = torch.exp(torch.empty(8).uniform_(math.log(2048), math.log(65536), generator=gen)).round().long()
+    T4 = int(lens.sum())
+    cu = torch.cat((torch.zeros(1, dtype=torch.long), lens.cumsum(0))).to(torch.int32)
+    Gc, Rc = 4, 6
+    life = torch.logspace(math.log10(2048), 6.0, Gc)
+    gfix = -(math.log(2.0) / life)
+    gfix[-1] = 0.0
+    q4 = F.normalize(torch.randn(1, T4, Gc, Rc, D, generator=gen), dim=-1) * D ** -0.5
+    k4 = F.normalize(torch.randn(1, T4, Gc, D, generator=gen), dim=-1)
+    v4 = torch.randn(1, T4, Gc, D, generator=gen).to(torch.bfloat16)
+    b4 = torch.sigmoid(torch.randn(1, T4, Gc, generator=gen))
+    g4 = gfix.expand(1, T4, Gc).contiguous()
+    args4 = [z.to(device) for z in (q4, k4, v4, g4, b4)]
+    cud = cu.to(device)
+    ms4 = _time_device(lambda: delta_rule_gqa(*args4, 64, None, cu_seqlens=cud), steps, warmup)
+    out["config4"] = {"workload": f"BASELINE config 4: 8 packed sequences ({lens.tolist()} tokens, {T4} total) "
+                                  f"with cu_seqlens, 4 KV x 6 query heads, D=256",
+                      "value": T4 / (ms4 / 1e3), "unit": "tok/s", "ms_per_step": ms4}
+    return out
+
+
 def run_decode(device, steps=256, warmup=8, nseq=64, nlayers=12):
     """64 sequences at positions U[4K, 128K], 12 stacked layers, one token per sequence per
     step; the whole 12-layer step is captured in a CUDA graph and replayed."""
@@ -468,6 +525,7 @@ def main(argv=None):
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-sp", action="store_true")
+    ap.add_argument("--no-delta", action="store_true")
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)
     ctx = dist_setup()
@@ -540,6 +598,8 @@ def run_ours(args, ctx):
         out["cpu_baseline"] = {"value": tps, "unit": "tok/s", "cores": cores, "kind": "port",
                                "sample": f"{reps} x the last 2048 tokens of the T=32768 prefill against a full cache "
                                          f"(its steady-state per-token cost), {dt:.1f} s on {cores} threads"}
+    if ctx["world"] == 1 and not args.no_delta:
+        out["delta_rule"] = run_delta_configs(dev)
     if not args.no_decode and ctx["world"] == 1:
         out["decode"] = run_decode(dev, steps=args.decode_steps, nseq=args.decode_seqs, nlayers=args.decode_layers)
     print(json.dumps(out), flush=True)
