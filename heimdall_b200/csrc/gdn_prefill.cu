@@ -89,9 +89,63 @@ constexpr int kP1_Threads = 256;
 constexpr int kP1_Reg0 = 0;                 // k tile (64 KB) -> T fp32 -> (beta v)^T (64 KB)
 constexpr int kP1_Reg1 = 69632;             // A fp32 (67.6 KB) -> (beta e^c k)^T (64 KB)
 constexpr int kP1_RegW = 69632 * 2;         // T fp16 (32 KB)
-constexpr int kP1_Small = kP1_RegW + 32768; // gc/g/beta (3 x 512 B) + barriers + row pointers (3 KB)
-constexpr int kP1_Smem = kP1_Small + 2048 + 3072 + 1024;
+constexpr int kP1_Small = kP1_RegW + 32768; // gc/g/beta (3 x 512 B) + barriers + row pointers (3 KB) + factors (1 KB)
+constexpr int kP1_Smem = kP1_Small + 2048 + 3072 + 1024 + 1024;
 constexpr int kAS = 132;                    // row stride (floats) of A and T in shared memory
+
+// rows of zeros that invalid write steps point at, so P1's staging loads need no branches
+__device__ __align__(16) float g_zero_row[kGD];
+
+// O = (NEG ? -1 : 1) * L R for M x M blocks of row-major fp32 matrices in shared memory (leading dims in
+// floats, multiples of 4), block b of nb; thread tile TR x TC, the reduction read four columns of L at a time.
+template <int M, int TR, int TC, bool NEG>
+__device__ __forceinline__ void block_mm(const float* L, int ldl, const float* R, int ldr, float* O, int ldo,
+                                         int tt) {
+  constexpr int NTC = M / TC, NT = (M / TR) * NTC;
+  if (tt >= NT) return;
+  const int i0 = (tt / NTC) * TR, c0 = (tt % NTC) * TC;
+  float acc[TR][TC];
+#pragma unroll
+  for (int a = 0; a < TR; ++a)
+#pragma unroll
+    for (int b = 0; b < TC; ++b) acc[a][b] = 0.f;
+#pragma unroll 2
+  for (int j = 0; j < M; j += 4) {
+    float4 av[TR];
+#pragma unroll
+    for (int a = 0; a < TR; ++a) av[a] = *reinterpret_cast<const float4*>(L + (i0 + a) * ldl + j);
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {
+      float bv[TC];
+#pragma unroll
+      for (int b = 0; b < TC; ++b) bv[b] = R[(j + jj) * ldr + c0 + b];
+#pragma unroll
+      for (int a = 0; a < TR; ++a) {
+        const float x = jj == 0 ? av[a].x : jj == 1 ? av[a].y : jj == 2 ? av[a].z : av[a].w;
+#pragma unroll
+        for (int b = 0; b < TC; ++b) acc[a][b] = fmaf(x, bv[b], acc[a][b]);
+      }
+    }
+  }
+#pragma unroll
+  for (int a = 0; a < TR; ++a)
+#pragma unroll
+    for (int b = 0; b < TC; ++b) O[(i0 + a) * ldo + c0 + b] = NEG ? -acc[a][b] : acc[a][b];
+}
+
+// one doubling level of the block-triangular inverse: for each block pair (rows r1.., r2 = r1 + M)
+// T21 = -T22 (A21 T11), with X (the products A21 T11) in scratch; `tt` = thread index, threads split by pair
+template <int M, int TR, int TC>
+__device__ __forceinline__ void inverse_doubling_level(const float* A, float* Tm, float* X, int tt) {
+  constexpr int NT = (M / TR) * (M / TC), NPAIR = 128 / (2 * M);
+  static_assert(NT * NPAIR <= kP1_Threads, "one tile per thread");
+  const int k = tt / NT, lt = tt % NT;
+  const int r1 = k * 2 * M, r2 = r1 + M;
+  if (k < NPAIR) block_mm<M, TR, TC, false>(A + r2 * kAS + r1, kAS, Tm + r1 * kAS + r1, kAS, X + k * M * M, M, lt);
+  __syncthreads();
+  if (k < NPAIR) block_mm<M, TR, TC, true>(Tm + r2 * kAS + r2, kAS, X + k * M * M, M, Tm + r2 * kAS + r1, kAS, lt);
+  __syncthreads();
+}
 
 __global__ void __launch_bounds__(kP1_Threads, 1) gdn_p1_kernel(GdnStreams s) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -130,12 +184,12 @@ __global__ void __launch_bounds__(kP1_Threads, 1) gdn_p1_kernel(GdnStreams s) {
   {
     const int r = t >> 1, hh = t & 1;
     const RowSrc src = write_row(s, b, gg, c * kGC + r);
-    if (hh == 0) {
+    if (hh == 0) {   // invalid steps read a zero row (their beta is 0, so they contribute nothing)
       s_g[r] = src.zero ? 0.f : src.g;
       s_beta[r] = src.zero ? 0.f : src.beta;
-      s_kp[r] = src.zero ? nullptr : src.k;
-      s_vp[r] = src.zero ? nullptr : src.v;
-      s_vp32[r] = src.zero ? nullptr : src.v32;
+      s_kp[r] = src.zero ? g_zero_row : src.k;
+      s_vp[r] = src.zero ? reinterpret_cast<const __nv_bfloat16*>(g_zero_row) : src.v;
+      s_vp32[r] = src.zero ? g_zero_row : src.v32;
     }
     __half* kwrow = s.kw + (rowbase + r) * kGD + hh * 128;
 #pragma unroll 4
@@ -178,6 +232,13 @@ __global__ void __launch_bounds__(kP1_Threads, 1) gdn_p1_kernel(GdnStreams s) {
   }
   __syncthreads();
   const float gamma_last = s_gc[127];
+  // per-step factors of the B operands: beta e^{c} and e^{c_C - c} (both <= 1)
+  float* s_bec = reinterpret_cast<float*>(smem + kP1_Small + 2048 + 3072);   // [128], after the row pointers
+  float* s_ect = s_bec + 128;                                                // [128]
+  if (t < 128) {
+    s_bec[t] = s_beta[t] * __expf(s_gc[t]);
+    s_ect[t] = __expf(gamma_last - s_gc[t]);
+  }
   // ---- (b) A = strict_lower(beta_i e^{c_i - c_j} (k_i . k_j)) from TMEM (warps 0-3, row = lane)
   bool alive = true;
   if (warp < 4) {
@@ -213,28 +274,12 @@ __global__ void __launch_bounds__(kP1_Threads, 1) gdn_p1_kernel(GdnStreams s) {
     }
   }
   __syncthreads();
-  float* X = reinterpret_cast<float*>(regW);  // scratch: A21 T11 for every block pair of a level (<= 16 KB)
-  for (int m = 16; m < 128; m *= 2) {
-    const int npair = 128 / (2 * m), per = m * m;
-    // X_k[i][c] = sum_{j >= c} A[r2 + i][r1 + j] T[r1 + j][r1 + c]
-    for (int q = t; q < npair * per; q += kP1_Threads) {
-      const int k = q / per, i = (q % per) / m, c = q % m;
-      const int r1 = k * 2 * m, r2 = r1 + m;
-      float acc = 0.f;
-      for (int j = c; j < m; ++j) acc += A[(r2 + i) * kAS + r1 + j] * Tm[(r1 + j) * kAS + r1 + c];
-      X[q] = acc;
-    }
-    __syncthreads();
-    // T21[i][c] = -sum_{j <= i} T[r2 + i][r2 + j] X_k[j][c]
-    for (int q = t; q < npair * per; q += kP1_Threads) {
-      const int k = q / per, i = (q % per) / m, c = q % m;
-      const int r1 = k * 2 * m, r2 = r1 + m;
-      float acc = 0.f;
-      for (int j = 0; j <= i; ++j) acc += Tm[(r2 + i) * kAS + r2 + j] * X[k * per + j * m + c];
-      Tm[(r2 + i) * kAS + r1 + c] = -acc;
-    }
-    __syncthreads();
-  }
+  // (T stays zero above its diagonal and T11, T22 are lower triangular, so both products are plain block
+  // products: X = A21 T11, T21 = -T22 X)
+  float* X = reinterpret_cast<float*>(regW);  // scratch: A21 T11 for every block pair of a level (16 KB)
+  inverse_doubling_level<16, 2, 2>(A, Tm, X, t);
+  inverse_doubling_level<32, 4, 2>(A, Tm, X, t);
+  inverse_doubling_level<64, 4, 4>(A, Tm, X, t);
   // ---- T -> fp16 SW128 tile (rows i, K = j) in regW
   for (int p = t; p < 128 * 16; p += kP1_Threads) {
     const int i = p >> 4, ch = p & 15;  // chunk of 8 columns
@@ -250,17 +295,19 @@ __global__ void __launch_bounds__(kP1_Threads, 1) gdn_p1_kernel(GdnStreams s) {
   {
     const int d = t;
     __half* ktT = s.ktT + ((size_t)bg * s.n_chunks + c) * kGD * kGC + (size_t)d * kGC;
+    const bool v32 = s.v32 != nullptr;   // uniform for the launch
 #pragma unroll 1
     for (int rb = 0; rb < kGC; rb += 32) {
-      // 64 independent loads in flight per thread (32 tokens x {k, v}), then pack and store
+      // 64 independent, unconditional loads in flight per thread (32 tokens x {k, v}), then pack and store
       float kv[32], vv[32];
 #pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        const int r = rb + e;
-        const float* kp = s_kp[r];
-        kv[e] = kp ? kp[d] : 0.f;
-        if (s_vp32[r]) vv[e] = s_vp32[r][d];
-        else vv[e] = s_vp[r] ? __bfloat162float(s_vp[r][d]) : 0.f;
+      for (int e = 0; e < 32; ++e) kv[e] = s_kp[rb + e][d];
+      if (v32) {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) vv[e] = s_vp32[rb + e][d];
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) vv[e] = __bfloat162float(s_vp[rb + e][d]);
       }
 #pragma unroll
       for (int q = 0; q < 32; q += 8) {
@@ -269,11 +316,9 @@ __global__ void __launch_bounds__(kP1_Threads, 1) gdn_p1_kernel(GdnStreams s) {
 #pragma unroll
         for (int e = 0; e < 8; e += 2) {
           const int r = r0 + e;
-          const float b0 = s_beta[r], b1 = s_beta[r + 1];
-          const float g0 = s_gc[r], g1 = s_gc[r + 1];
-          pv[e / 2] = pack_half2(b0 * vv[q + e], b1 * vv[q + e + 1]);
-          pk[e / 2] = pack_half2(b0 * __expf(g0) * kv[q + e], b1 * __expf(g1) * kv[q + e + 1]);
-          pt[e / 2] = pack_half2(__expf(gamma_last - g0) * kv[q + e], __expf(gamma_last - g1) * kv[q + e + 1]);
+          pv[e / 2] = pack_half2(s_beta[r] * vv[q + e], s_beta[r + 1] * vv[q + e + 1]);
+          pk[e / 2] = pack_half2(s_bec[r] * kv[q + e], s_bec[r + 1] * kv[q + e + 1]);
+          pt[e / 2] = pack_half2(s_ect[r] * kv[q + e], s_ect[r + 1] * kv[q + e + 1]);
         }
         const uint32_t off = (uint32_t)(r0 >> 6) * (256 * 128) + sw128_offset(d, r0 & 63);
         *reinterpret_cast<uint4*>(reg0 + off) = make_uint4(pv[0], pv[1], pv[2], pv[3]);
