@@ -588,7 +588,7 @@ def run_ours(args, ctx):
            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded; config-1 shapes and distributions)",
            "config": arm_config(ctx["world"]),
            "stage_ms": stage_ms, "roofline": roof, "layer_roofline": layer_roof, "clocks": clocks,
-           "gpu_launches": 8 * args.steps}
+           "gpu_launches": 7 * args.steps}
     if e2e is not None:
         out["e2e"] = e2e
     if sp_res is not None:

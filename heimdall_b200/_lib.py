@@ -20,6 +20,7 @@ _L = ctypes.c_longlong
 # name -> (argtypes); every entry point returns int (status) unless listed in _RESTYPE
 SIGNATURES = {
     "bf_strerror": [_I],
+    "bf_last_cuda_error": [],
     "bf_abi_version": [],
     "bf_device_error": [_P, _P],
     "bf_stage_events": [_P, _I],
@@ -43,7 +44,7 @@ SIGNATURES = {
     "bf_bifrost_layer_prefill_sp": [_P, _P, _P, _P, _P, _P, _P, _L, _I, _I, _P, _P, _P, _I, _I, _P, _P, _P, _P, _P,
                                     _Z, _P],
 }
-_RESTYPE = {"bf_strerror": ctypes.c_char_p, "bf_layer_weights_bytes": _Z, "bf_layer_decode_workspace": _Z,
+_RESTYPE = {"bf_strerror": ctypes.c_char_p, "bf_last_cuda_error": ctypes.c_char_p, "bf_layer_weights_bytes": _Z, "bf_layer_decode_workspace": _Z,
             "bf_gdn_chunk_workspace": _Z, "bf_window_workspace": _Z, "bf_layer_prefill_workspace": _Z,
             "bf_gdn_segment_workspace": _Z}
 
@@ -87,7 +88,10 @@ def size(name: str, *args) -> int:
 def call(name: str, *args) -> None:
     rc = getattr(load(), name)(*args)
     if rc != 0:
-        raise BifrostError(name, rc, strerror(rc))
+        msg = strerror(rc)
+        if rc == 5:   # BF_ERR_CUDA: add the CUDA error behind it
+            msg += ": " + load().bf_last_cuda_error().decode()
+        raise BifrostError(name, rc, msg)
 
 
 def device_error(stream: int = 0):

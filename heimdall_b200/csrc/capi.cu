@@ -24,10 +24,10 @@ int device_state(DeviceState* st) {
   std::lock_guard<std::mutex> lk(g_dev_mu);
   if (!g_err_ptr[dev]) {
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_bf_error_word) != cudaSuccess) return BF_ERR_CUDA;
+    if (cudaGetSymbolAddress(&p, g_bf_error_word) != cudaSuccess) return cuda_fail();
     int sms = 0, major = 0;
-    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return BF_ERR_CUDA;
-    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return BF_ERR_CUDA;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return cuda_fail();
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return cuda_fail();
     g_err_ptr[dev] = static_cast<unsigned int*>(p);
     g_sm_count[dev] = sms;
     g_cc_major[dev] = major;
@@ -40,6 +40,26 @@ int device_state(DeviceState* st) {
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+static thread_local int g_last_cuda_error = 0;
+
+int cuda_fail(cudaError_t e) {
+  if (e == cudaSuccess) e = cudaGetLastError();
+  g_last_cuda_error = (int)e;
+  return BF_ERR_CUDA;
+}
+
+static cudaStream_t g_side[64] = {nullptr};
+
+cudaStream_t side_stream(const DeviceState& st) {
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (!g_side[st.device]) {
+    cudaStream_t s = nullptr;
+    if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess) return nullptr;
+    g_side[st.device] = s;
+  }
+  return g_side[st.device];
+}
 
 // optional per-stage CUDA events (bf_stage_events): recorded on the launching stream around each stage
 static cudaEvent_t g_stage_ev[2 * BF_MAX_STAGES];
@@ -54,6 +74,10 @@ void stage_mark(int stage, int end, cudaStream_t stream) {
 using namespace bfb;
 
 extern "C" {
+
+const char* bf_last_cuda_error(void) {
+  return g_last_cuda_error ? cudaGetErrorString((cudaError_t)g_last_cuda_error) : "no CUDA error recorded";
+}
 
 const char* bf_strerror(int code) {
   switch (code) {
@@ -76,13 +100,13 @@ int bf_device_error(unsigned int* word, bf_stream_t stream) {
   DeviceState st;
   int rc = device_state(&st);
   if (rc) return rc;
-  if (cudaStreamSynchronize(stream) != cudaSuccess) return BF_ERR_CUDA;
+  if (cudaStreamSynchronize(stream) != cudaSuccess) return cuda_fail();
   unsigned int v[4] = {0u, 0u, 0u, 0u};
-  if (cudaMemcpy(v, st.err, sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess) return BF_ERR_CUDA;
+  if (cudaMemcpy(v, st.err, sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess) return cuda_fail();
   for (int i = 0; i < 4; ++i) word[i] = v[i];
   if (v[0]) {
     const unsigned int zero[4] = {0u, 0u, 0u, 0u};
-    if (cudaMemcpy(st.err, zero, sizeof(zero), cudaMemcpyHostToDevice) != cudaSuccess) return BF_ERR_CUDA;
+    if (cudaMemcpy(st.err, zero, sizeof(zero), cudaMemcpyHostToDevice) != cudaSuccess) return cuda_fail();
   }
   return BF_OK;
 }

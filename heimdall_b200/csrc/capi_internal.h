@@ -15,12 +15,22 @@ struct DeviceState {
 };
 
 int device_state(DeviceState* st);
+// a non-blocking side stream per device (created on first use, kept for the process) for work that runs
+// concurrently with the caller's stream inside one call; joined back with events before the call returns
+cudaStream_t side_stream(const DeviceState& st);
 
 // per-stage timing hooks (no-ops unless bf_stage_events installed events)
 void stage_mark(int stage, int end, cudaStream_t stream);
 enum Stage { ST_XPROJ = 0, ST_HEADPROJ, ST_GDN_P1, ST_GDN_P2, ST_GDN_P3, ST_WIN_PREP, ST_WIN, ST_CACHE, ST_DEC_STATE,
              ST_DEC_WIN };
 bool aligned16(const void* p);
+// BF_ERR_CUDA with the CUDA error recorded for bf_last_cuda_error (e: a failed call's result, or the pending
+// launch error when e is cudaSuccess); launch_status() is BF_OK or that
+int cuda_fail(cudaError_t e = cudaSuccess);
+inline int launch_status() {
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : cuda_fail(e);
+}
 
 int launch_gdn_decode(const float* q, const float* k, const void* v, int v_bf16, const float* g,
                       const float* beta, const float* s_in, float* s_out, float* o, int B, int G, int R, int D,

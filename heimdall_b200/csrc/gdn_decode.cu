@@ -242,14 +242,14 @@ int launch_gdn_decode(const float* q, const float* k, const void* v, int v_bf16,
   static bool attr = false;
   if (!attr) {
     if (cudaFuncSetAttribute(gdn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDecSmem) != cudaSuccess)
-      return BF_ERR_CUDA;
+      return cuda_fail();
     attr = true;
   }
   const int nitems = B * G * (D / kDecCols);
   const int grid = nitems < st.sm_count ? nitems : st.sm_count;
   gdn_decode_kernel<<<grid, kDecThreads, kDecSmem, stream>>>(smap, omap, q, k, v, v_bf16, g, beta, o, B * G, R, D,
                                                             st.err);
-  return cudaGetLastError() == cudaSuccess ? BF_OK : BF_ERR_CUDA;
+  return launch_status();
 }
 
 }  // namespace bfb

@@ -749,21 +749,65 @@ __global__ void __launch_bounds__(kP3_Threads, 1)
     const bool row_ok = r < nvalid;
     const float eci = __expf(ci);
     float* orow = s.o + (((size_t)qrow0 + r) * H + h) * kGD;
+    // fused mix: gate of this query (position pos0 + token)
+    bool gate_on = false;
+    float gam = 0.f, rho = 0.f;
+    if (s.mix && row_ok) {
+      const long long tq = qrow0 + r - (long long)b * s.T;   // token index within its sequence
+      gate_on = s.pos0 + tq >= s.W;
+      if (gate_on) {
+        const float lse = s.lse[((size_t)b * H + h) * s.T + tq];
+        const float z = s.mixx[((size_t)b * s.T + tq) * H + h] + s.mix_lse[h] * (lse - logf((float)s.W));
+        gam = 1.f / (1.f + __expf(-z));
+        rho = s.mem_scale[h];
+      }
+    }
     for (int half = 0; half < 2 && alive; ++half) {
+      // fused mix: the window result of this row's 32-column batch b is read one batch ahead (the first batch
+      // before the wait for the products), so its latency overlaps the TMEM reads and the arithmetic
+      float4 cur[8], nxt[8];
+      if (gate_on) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) cur[e] = *reinterpret_cast<const float4*>(orow + half * 128 + 4 * e);
+      }
       alive = mbar_wait_warp(bar_o, half & 1, abort_flag, s.err, 0x6c);
       if (!alive) break;
       tc_fence_after();
 #pragma unroll 1
-      for (int c0 = 0; c0 < 128; c0 += 16) {
-        float fi[16], fa[16];
-        tmem_ld16_wait(trow + 128 + c0, fi);
-        tmem_ld16_wait(trow + 256 + c0, fa);
-        if (row_ok) {
+      for (int bb = 0; bb < 4; ++bb) {
+        if (gate_on && bb < 3) {
 #pragma unroll
-          for (int e = 0; e < 16; e += 4)
-            *reinterpret_cast<float4*>(orow + half * 128 + c0 + e) =
-                make_float4(eci * fi[e] + fa[e], eci * fi[e + 1] + fa[e + 1], eci * fi[e + 2] + fa[e + 2],
-                            eci * fi[e + 3] + fa[e + 3]);
+          for (int e = 0; e < 8; ++e)
+            nxt[e] = *reinterpret_cast<const float4*>(orow + half * 128 + (bb + 1) * 32 + 4 * e);
+        }
+#pragma unroll
+        for (int sub = 0; sub < 2; ++sub) {
+          const int c0 = bb * 32 + sub * 16;
+          float fi[16], fa[16];
+          tmem_ld16_wait(trow + 128 + c0, fi);
+          tmem_ld16_wait(trow + 256 + c0, fa);
+          if (row_ok && !s.mix) {
+#pragma unroll
+            for (int e = 0; e < 16; e += 4)
+              *reinterpret_cast<float4*>(orow + half * 128 + c0 + e) =
+                  make_float4(eci * fi[e] + fa[e], eci * fi[e + 1] + fa[e + 1], eci * fi[e + 2] + fa[e + 2],
+                              eci * fi[e + 3] + fa[e + 3]);
+          } else if (gate_on) {
+#pragma unroll
+            for (int e = 0; e < 16; e += 4) {
+              const float4 ow = cur[sub * 4 + e / 4];
+              float4 res;
+              res.x = ow.x + gam * (rho * (eci * fi[e] + fa[e]) - ow.x);
+              res.y = ow.y + gam * (rho * (eci * fi[e + 1] + fa[e + 1]) - ow.y);
+              res.z = ow.z + gam * (rho * (eci * fi[e + 2] + fa[e + 2]) - ow.z);
+              res.w = ow.w + gam * (rho * (eci * fi[e + 3] + fa[e + 3]) - ow.w);
+              *reinterpret_cast<float4*>(orow + half * 128 + c0 + e) = res;
+            }
+          }
+        }
+        if (gate_on) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) cur[e] = nxt[e];
         }
       }
       tc_fence_before();
@@ -818,7 +862,7 @@ int launch_chunk_table(const int* cu_seqlens, int n_seq, int max_chunks, int* se
                        int* chunk_len, unsigned int* err, cudaStream_t stream) {
   build_chunk_table_kernel<<<1, 1024, 0, stream>>>(cu_seqlens, n_seq, max_chunks, seq_chunk0, chunk_tok0, chunk_len,
                                                    err);
-  return cudaGetLastError() == cudaSuccess ? BF_OK : BF_ERR_CUDA;
+  return launch_status();
 }
 
 size_t gdn_prefill_workspace(int B, int G, int T_steps, bool transform) {
@@ -862,27 +906,29 @@ int launch_gdn_prefill(GdnStreams s, cudaStream_t stream, int parts) {
     if (cudaFuncSetAttribute(gdn_p1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kP1_Smem) != cudaSuccess ||
         cudaFuncSetAttribute(gdn_p2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kP2_Smem) != cudaSuccess ||
         cudaFuncSetAttribute(gdn_p3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kP3_Smem) != cudaSuccess)
-      return BF_ERR_CUDA;
+      return cuda_fail();
     g_p_attr[0] = true;
   }
   if (parts & kGdnP1) {
     stage_mark(ST_GDN_P1, 0, stream);
     gdn_p1_kernel<<<dim3(s.n_chunks, s.B * s.G), kP1_Threads, kP1_Smem, stream>>>(s);
-    if (cudaGetLastError() != cudaSuccess) return BF_ERR_CUDA;
+    if (int e_ = launch_status()) return e_;
     stage_mark(ST_GDN_P1, 1, stream);
   }
-  if (!(parts & kGdnP23)) return BF_OK;
+  if (!(parts & (kGdnP2 | kGdnP3))) return BF_OK;
   CUtensorMap wmap, ktmap;
   int rc = make_tmap_kmajor(&wmap, s.w, BF_F16, (uint64_t)s.B * s.G * s.n_pad, kGD, kGD, kGC, 4);
   if (rc) return rc;
   rc = make_tmap_kmajor(&ktmap, s.ktT, BF_F16, (uint64_t)s.B * s.G * s.n_chunks * kGD, kGC, kGC, kGD, 2);
   if (rc) return rc;
+  if (parts & kGdnP2) {
   stage_mark(ST_GDN_P2, 0, stream);
   gdn_p2_kernel<<<dim3((s.m_out ? 2 : 1) * (kGD / kP2_NB), s.chunk_tok0 ? s.G * s.n_seq : s.B * s.G), kP2_Threads,
                   kP2_Smem, stream>>>(wmap, ktmap, s);
-  if (cudaGetLastError() != cudaSuccess) return BF_ERR_CUDA;
+  if (int e_ = launch_status()) return e_;
   stage_mark(ST_GDN_P2, 1, stream);
-  if (s.m_out) return BF_OK;   // segment transform: no reads
+  }
+  if (s.m_out || !(parts & kGdnP3)) return BF_OK;   // segment transform: no reads
   // P3 maps: q [B,T,H,D] fp16 as (d, token, atom, head); k/kw; S^T; v'^T
   CUtensorMap qmap, kmap, smap, vmap;
   {
@@ -901,7 +947,7 @@ int launch_gdn_prefill(GdnStreams s, cudaStream_t stream, int parts) {
   stage_mark(ST_GDN_P3, 0, stream);
   gdn_p3_kernel<<<dim3(s.n_chunks, H, s.B), kP3_Threads, kP3_Smem, stream>>>(qmap, kmap, smap, vmap, s);
   stage_mark(ST_GDN_P3, 1, stream);
-  return cudaGetLastError() == cudaSuccess ? BF_OK : BF_ERR_CUDA;
+  return launch_status();
 }
 
 }  // namespace bfb

@@ -7,8 +7,8 @@
 namespace bfb {
 
 constexpr int kGC = 128;   // chunk length of the GPU scan (tokens)
-// parts of launch_gdn_prefill: P1 (per-chunk products) and P2 (+ P3 unless in transform mode)
-constexpr int kGdnP1 = 1, kGdnP23 = 2, kGdnAll = 3;
+// parts of launch_gdn_prefill: P1 (per-chunk products), P2 (the recurrence), P3 (the reads; not in transform mode)
+constexpr int kGdnP1 = 1, kGdnP2 = 2, kGdnP3 = 4, kGdnAll = 7;
 constexpr int kGD = 256;   // head dim (Dk == Dv)
 
 // The write stream (step u writes one key/value into memory) and the read stream (step u reads with
@@ -52,6 +52,15 @@ struct GdnStreams {
   const int* chunk_len;
   const int* seq_chunk0;
   int n_seq;
+  // fused gate and mix (mix != 0; then o is the layer output holding the window result o_win): the memory
+  // read of a query at position p >= W becomes o = o_win + gamma (mem_scale o_mem - o_win) in place, with
+  // gamma = sigmoid(mixx + mix_lse (lse - ln W)); rows below W keep o_win
+  int mix;
+  long long pos0;              // position of token 0 of each sequence
+  const float* lse;            // [B,H,T] window log-sum-exp
+  const float* mixx;           // [B,T,H]
+  const float* mix_lse;        // [H]
+  const float* mem_scale;      // [H]
   unsigned int* err;
 };
 

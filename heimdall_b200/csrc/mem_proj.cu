@@ -461,7 +461,7 @@ int launch_prep_weights(const float* fq, const float* fk, const float* ab_w, con
   prep_head_weights_kernel<<<dim3(D / 32, D / 32, H), blk, 0, stream>>>(fq, w_heads, D);
   prep_head_weights_kernel<<<dim3(D / 32, D / 32, G), blk, 0, stream>>>(fk, w_heads + (size_t)H * D * D, D);
   prep_x_weights_kernel<<<dim3((d + 255) / 256, 32), 256, 0, stream>>>(ab_w, mix_w, 2 * G, H, d, w_x);
-  return cudaGetLastError() == cudaSuccess ? BF_OK : BF_ERR_CUDA;
+  return launch_status();
 }
 
 int launch_head_proj(const __nv_bfloat16* q, const __nv_bfloat16* k, const __half* w_heads, float* qm, __half* qm16,
@@ -482,7 +482,7 @@ int launch_head_proj(const __nv_bfloat16* q, const __nv_bfloat16* k, const __hal
   static bool attr = false;
   if (!attr) {
     if (cudaFuncSetAttribute(head_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kHP_Smem) != cudaSuccess)
-      return BF_ERR_CUDA;
+      return cuda_fail();
     attr = true;
   }
   const int ntiles = (T + kHP_M - 1) / kHP_M;
@@ -493,7 +493,7 @@ int launch_head_proj(const __nv_bfloat16* q, const __nv_bfloat16* k, const __hal
   HeadProjArgs a{q, k, qm, qm16, km, B, T, H, G, per, err};
   dim3 grid((ntiles + per - 1) / per, H + G, B);
   head_proj_kernel<<<grid, kHP_Threads, kHP_Smem, stream>>>(wmap, qmap, kmap, a);
-  return cudaGetLastError() == cudaSuccess ? BF_OK : BF_ERR_CUDA;
+  return launch_status();
 }
 
 int launch_x_proj(const __nv_bfloat16* x, const __nv_bfloat16* w_x, const float* ab_b, const float* mix_b,
@@ -506,7 +506,7 @@ int launch_x_proj(const __nv_bfloat16* x, const __nv_bfloat16* w_x, const float*
     x_proj_split_kernel<<<dim3(nslices, (M + kXS_Rows - 1) / kXS_Rows), 256, 0, stream>>>(x, w_x, M, d, scratch);
     XProjArgs a{ab_b, mix_b, A_log, dt_bias, decay_mask, nullptr, g, beta, mixx, pos, pos0, M, T, d, G, H, sinks, err};
     x_proj_finish_kernel<<<(M + 7) / 8, 256, 0, stream>>>(scratch, nslices, a);
-    return cudaGetLastError() == cudaSuccess ? BF_OK : BF_ERR_CUDA;
+    return launch_status();
   }
   CUtensorMap xmap, wmap;
   int rc = make_tmap_kmajor(&xmap, x, BF_BF16, (uint64_t)M, d, d, kXP_M, 1);
@@ -516,12 +516,12 @@ int launch_x_proj(const __nv_bfloat16* x, const __nv_bfloat16* w_x, const float*
   static bool attr = false;
   if (!attr) {
     if (cudaFuncSetAttribute(x_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kXP_Smem) != cudaSuccess)
-      return BF_ERR_CUDA;
+      return cuda_fail();
     attr = true;
   }
   XProjArgs a{ab_b, mix_b, A_log, dt_bias, decay_mask, nullptr, g, beta, mixx, pos, pos0, M, T, d, G, H, sinks, err};
   x_proj_kernel<<<(M + kXP_M - 1) / kXP_M, 192, kXP_Smem, stream>>>(xmap, wmap, a);
-  return cudaGetLastError() == cudaSuccess ? BF_OK : BF_ERR_CUDA;
+  return launch_status();
 }
 
 }  // namespace bfb

@@ -37,7 +37,7 @@ static int noalloc_scratch(void** out) {
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
   if (!g_noalloc_ptr[dev]) {
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return BF_ERR_CUDA;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return cuda_fail();
     g_noalloc_ptr[dev] = p;
   }
   *out = g_noalloc_ptr[dev];

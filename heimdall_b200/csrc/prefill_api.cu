@@ -40,13 +40,6 @@ __global__ void bf16_to_f32_kernel(const __nv_bfloat16* __restrict__ src, float*
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
     dst[i] = __bfloat162float(src[i]);
 }
-__global__ void zero_rows_kernel(float* __restrict__ o, int T, int rows, size_t row_elems) {
-  // o [B,T,row_elems]: zero rows 0..rows-1 of every batch
-  const int b = blockIdx.y;
-  const size_t n = (size_t)rows * row_elems;
-  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
-    o[(size_t)b * T * row_elems + i] = 0.f;
-}
 // write the last m new tokens into their ring slots (heimdall/hibrit.py:414-422)
 __global__ void ring_write_kernel(const __nv_bfloat16* __restrict__ kr, const __nv_bfloat16* __restrict__ v,
                                   const float* __restrict__ km, const float* __restrict__ g, const float* __restrict__ beta,
@@ -130,7 +123,7 @@ int bf_gdn_chunk_fwd(const void* q, int q_dtype, const void* k, int k_dtype, con
     bf16_to_f32_kernel<<<grid_for(nk), 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(k), k32, nk);
     kf = k32;
   }
-  if (cudaGetLastError() != cudaSuccess) return BF_ERR_CUDA;
+  if (int e_ = launch_status()) return e_;
   GdnStreams s{};
   s.B = B; s.G = G; s.R = R; s.T = T;
   s.n_steps = T;
@@ -225,7 +218,7 @@ size_t bf_layer_prefill_workspace(int B, int T, int H, int G, int D, int window,
   n += al1k((size_t)B * T * G * D * 4);     // km
   n += al1k((size_t)B * T * G * 4) * 2;     // g, beta
   n += al1k((size_t)B * T * H * 4);         // mixx
-  n += al1k((size_t)B * T * H * D * 4);     // o_mem
+  n += al1k((size_t)B * H * T * 4);         // window lse (for the gate) when the caller does not keep it
   n += al1k((size_t)B * G * D * D * 4);     // state when there is no cache
   n += al1k((size_t)B * G * D * Tkp * 2);   // V^T
   if (with_ring) n += al1k((size_t)B * G * Tk * D * 2);  // K of the extended sequence
@@ -283,20 +276,36 @@ static int layer_prefill_impl(const bf_layer* L, const void* x, const void* q, c
   float* g = reinterpret_cast<float*>(take((size_t)B * T * G * 4));
   float* beta = reinterpret_cast<float*>(take((size_t)B * T * G * 4));
   float* mixx = reinterpret_cast<float*>(take((size_t)B * T * H * 4));
-  float* o_mem = reinterpret_cast<float*>(take((size_t)B * T * H * D * 4));
+  float* lse_ws = reinterpret_cast<float*>(take((size_t)B * H * T * 4));
   float* s_tmp = reinterpret_cast<float*>(take((size_t)B * G * D * D * 4));
   __half* vt = reinterpret_cast<__half*>(take((size_t)B * G * D * Tkp * 2));
   __nv_bfloat16* kext = ring_case ? reinterpret_cast<__nv_bfloat16*>(take((size_t)B * G * Tk * D * 2)) : nullptr;
   void* gws = p;
+  float* lse_w = lse ? lse : lse_ws;   // the window's lse, needed by the gate
 
+  // the window (step 3) depends only on the inputs: when there are memory reads to overlap with, it runs on a
+  // side stream forked here, before the memory work is enqueued, and joins before the reads mix into o
+  const bool will_read = use_mem && phase != kPhaseBegin && (ring_case ? T : T - W) > 0;
+  cudaStream_t ws2 = stream;   // (a null handle is the legacy default stream, a valid stream)
+  cudaEvent_t ev_fork = nullptr, ev_win = nullptr;
+  if (will_read) {
+    ws2 = side_stream(st);
+    if (!ws2) return cuda_fail();
+    if (cudaEventCreateWithFlags(&ev_fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ev_win, cudaEventDisableTiming) != cudaSuccess)
+      return cuda_fail();
+    if (cudaEventRecord(ev_fork, stream) != cudaSuccess || cudaStreamWaitEvent(ws2, ev_fork, 0) != cudaSuccess)
+      return cuda_fail();
+  }
   // 1. memory inputs (projections on tcgen05)
   if ((use_mem || C) && phase != kPhaseFinish) {
     rc = mem_inputs_impl(st, L, x, q, k, nullptr, start, B, T, nullptr, km, g, beta, mixx, stream, qm16, nullptr, 0);
     if (rc) return rc;
   }
   // 2. memory: the write stream is delayed by W (token i enters memory when it leaves the window)
+  GdnStreams s{};
+  bool reads = false;
   if (use_mem) {
-    GdnStreams s{};
     s.B = B; s.G = G; s.R = R; s.T = T; s.W = W;
     if (ring_case) {
       s.nring = W; s.qoff = 0; s.n_steps = T; s.ring_pos0 = start - W;
@@ -305,17 +314,19 @@ static int layer_prefill_impl(const bf_layer* L, const void* x, const void* q, c
       s.ring_g = C->ring_g; s.ring_beta = C->ring_beta; s.ring_pos = C->ring_pos;
       s.s0 = C->S;
     } else {
-      // no history: the first W write steps are no-ops, so queries before W read the zero state
+      // no history: the first W write steps are no-ops, so queries before W read the zero state (their gate
+      // is off: they keep the window result)
       s.nring = 0; s.qoff = W; s.n_steps = T - W; s.ring_pos0 = 0;
       s.s0 = nullptr;
-      const int zr = T < W ? T : W;
-      zero_rows_kernel<<<dim3(grid_for((size_t)zr * H * D), B), 256, 0, stream>>>(o_mem, T, zr, (size_t)H * D);
     }
     s.n_chunks = (s.n_steps + kGC - 1) / kGC;
     s.n_pad = s.n_chunks * kGC;
     s.km = km; s.v = static_cast<const __nv_bfloat16*>(v); s.g = g; s.beta = beta;
     s.s_out = C ? C->S : s_tmp;
-    s.qm = qm16; s.o = o_mem; s.err = st.err;
+    s.qm = qm16; s.err = st.err;
+    // the memory reads go straight into the layer output, mixed with the window result there
+    s.o = o; s.mix = 1; s.pos0 = start; s.lse = lse_w; s.mixx = mixx; s.mix_lse = L->mix_lse;
+    s.mem_scale = L->mem_scale;
     if (phase == kPhaseBegin) {   // the state map of this segment's write stream, from a zero state
       s.s0 = nullptr;
       s.s_out = n_out;
@@ -323,37 +334,50 @@ static int layer_prefill_impl(const bf_layer* L, const void* x, const void* q, c
     }
     if (s.n_steps > 0) {
       gdn_prefill_carve(s, gws);
-      rc = launch_gdn_prefill(s, stream, phase == kPhaseFinish ? kGdnP23 : kGdnAll);
+      reads = phase != kPhaseBegin;
+      const int parts = phase == kPhaseBegin ? (kGdnP1 | kGdnP2) : phase == kPhaseFinish ? kGdnP2 : (kGdnP1 | kGdnP2);
+      rc = launch_gdn_prefill(s, stream, parts);
       if (rc) return rc;
     } else if (phase == kPhaseBegin) {
       identity_maps_kernel<<<grid_for((size_t)B * G * D * D), 256, 0, stream>>>(m_out, n_out, B * G, D);
-      if (cudaGetLastError() != cudaSuccess) return BF_ERR_CUDA;
+      if (int e_ = launch_status()) return e_;
     }
   } else if (phase == kPhaseBegin) {
     identity_maps_kernel<<<grid_for((size_t)B * G * D * D), 256, 0, stream>>>(m_out, n_out, B * G, D);
-    if (cudaGetLastError() != cudaSuccess) return BF_ERR_CUDA;
+    if (int e_ = launch_status()) return e_;
   }
   if (phase == kPhaseBegin) return BF_OK;
-  // 3. window attention over the extended keys, with the gate and mix fused into its epilogue
+  // 3. window attention over the extended keys (o = window result, lse), on the side stream when forked
   const void* kx = kr;
-  stage_mark(ST_WIN_PREP, 0, stream);
+  stage_mark(ST_WIN_PREP, 0, ws2);
   if (ring_case) {
     rc = launch_kext_prep(static_cast<const __nv_bfloat16*>(kr), static_cast<const __nv_bfloat16*>(C->ring_k), W,
-                          start - W, W, B, T, G, kext, stream);
+                          start - W, W, B, T, G, kext, ws2);
     if (rc) return rc;
     kx = kext;
   }
   rc = launch_vt_prep(static_cast<const __nv_bfloat16*>(v), (long long)T * G * D, D, (long long)G * D,
                       ring_case ? static_cast<const __nv_bfloat16*>(C->ring_v) : nullptr, ring_case ? W : 0,
-                      start - W, W, B, G, Tk, Tkp, vt, stream);
+                      start - W, W, B, G, Tk, Tkp, vt, ws2);
   if (rc) return rc;
-  stage_mark(ST_WIN_PREP, 1, stream);
-  stage_mark(ST_WIN, 0, stream);
+  stage_mark(ST_WIN_PREP, 1, ws2);
+  stage_mark(ST_WIN, 0, ws2);
   rc = window_common(qr, kx, vt, sink_k, sink_v, ns, start, ring_case ? start - W : start, L->sinks, B, H, G, T, Tk, W,
-                     o, lse, use_mem ? o_mem : nullptr, mixx, L->mix_lse, L->mem_scale, st.err, stream);
+                     o, lse_w, nullptr, nullptr, nullptr, nullptr, st.err, ws2);
   if (rc) return rc;
-  stage_mark(ST_WIN, 1, stream);
-  // 4. cache: the last min(T, W) tokens go to their ring slots (the state was updated in place)
+  stage_mark(ST_WIN, 1, ws2);
+  if (will_read) {
+    if (cudaEventRecord(ev_win, ws2) != cudaSuccess || cudaStreamWaitEvent(stream, ev_win, 0) != cudaSuccess)
+      return cuda_fail();
+    cudaEventDestroy(ev_fork);
+    cudaEventDestroy(ev_win);
+  }
+  // 4. memory reads, mixed into o by the gate
+  if (reads) {
+    rc = launch_gdn_prefill(s, stream, kGdnP3);
+    if (rc) return rc;
+  }
+  // 5. cache: the last min(T, W) tokens go to their ring slots (the state was updated in place)
   if (C) {
     stage_mark(ST_CACHE, 0, stream);
     const int m = T < W ? T : W;
@@ -361,7 +385,7 @@ static int layer_prefill_impl(const bf_layer* L, const void* x, const void* q, c
         static_cast<const __nv_bfloat16*>(kr), static_cast<const __nv_bfloat16*>(v), km, g, beta, start, T, m, G, W,
         static_cast<__nv_bfloat16*>(C->ring_k), static_cast<__nv_bfloat16*>(C->ring_v), C->ring_km, C->ring_g,
         C->ring_beta, C->ring_pos);
-    if (cudaGetLastError() != cudaSuccess) return BF_ERR_CUDA;
+    if (int e_ = launch_status()) return e_;
     stage_mark(ST_CACHE, 1, stream);
   }
   return BF_OK;

@@ -106,7 +106,7 @@ int bf_gdn_segment_transform(const void* k, int k_dtype, const void* v, int v_dt
     float* k32 = reinterpret_cast<float*>(p);
     const size_t nk = (size_t)B * T * G * D;
     sp_bf16_to_f32_kernel<<<1184, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(k), k32, nk);
-    if (cudaGetLastError() != cudaSuccess) return BF_ERR_CUDA;
+    if (int e_ = launch_status()) return e_;
     kf = k32;
   }
   p += al1k_sp((size_t)B * T * G * D * 4);
@@ -135,14 +135,14 @@ int bf_gdn_apply_prefix(const float* M, const float* N, int n_seg, const float* 
   if ((long long)B * G > 65535) return BF_ERR_UNSUPPORTED;
   const size_t mat = (size_t)B * G * D * D;
   if (s0) {
-    if (cudaMemcpyAsync(s_in, s0, mat * 4, cudaMemcpyDeviceToDevice, stream) != cudaSuccess) return BF_ERR_CUDA;
+    if (cudaMemcpyAsync(s_in, s0, mat * 4, cudaMemcpyDeviceToDevice, stream) != cudaSuccess) return cuda_fail();
   } else {
-    if (cudaMemsetAsync(s_in, 0, mat * 4, stream) != cudaSuccess) return BF_ERR_CUDA;
+    if (cudaMemsetAsync(s_in, 0, mat * 4, stream) != cudaSuccess) return cuda_fail();
   }
   for (int j = 0; j < n_seg; ++j)
     state_map_kernel<<<dim3(D / kSM_T, D / kSM_T, B * G), 256, 0, stream>>>(M + j * mat, s_in + j * mat, N + j * mat,
                                                                           s_in + (j + 1) * mat, D);
-  return cudaGetLastError() == cudaSuccess ? BF_OK : BF_ERR_CUDA;
+  return launch_status();
 }
 
 }  // extern "C"

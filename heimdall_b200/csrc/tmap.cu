@@ -4,6 +4,7 @@
 
 #include <mutex>
 
+#include "capi_internal.h"
 #include "common.cuh"
 #include "tmap.h"
 
@@ -28,7 +29,7 @@ static PFN_cuTensorMapEncodeTiled_v12000 encoder() {
 int make_tmap(CUtensorMap* map, const void* base, int dtype, int rank, const uint64_t* dims,
               const uint64_t* strides_bytes, const uint32_t* box, bool swizzle128) {
   auto enc = encoder();
-  if (!enc) return BF_ERR_CUDA;
+  if (!enc) return cuda_fail(cudaErrorNotSupported);   // no driver entry point for tensor maps
   if (reinterpret_cast<uintptr_t>(base) & 15u) return BF_ERR_ALIGNMENT;
   for (int i = 0; i < rank - 1; ++i)
     if (strides_bytes[i] & 15u) return BF_ERR_ALIGNMENT;
@@ -47,7 +48,7 @@ int make_tmap(CUtensorMap* map, const void* base, int dtype, int rank, const uin
   CUresult r = enc(map, t, (cuuint32_t)rank, const_cast<void*>(base), d, s, b, e, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? BF_OK : BF_ERR_CUDA;
+  return r == CUDA_SUCCESS ? BF_OK : cuda_fail(cudaErrorInvalidValue);   // the encoder rejected the operand
 }
 
 // K-major operand matrix [rows][K] of 16-bit elements with row stride `ld` elements, loaded as boxes of

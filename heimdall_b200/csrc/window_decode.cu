@@ -532,7 +532,7 @@ static int launch_split(const CUtensorMap& kmap, const CUtensorMap& vmap, const 
   if (!attr) {
     if (cudaFuncSetAttribute(win_dec_split_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, kWT_Smem) !=
         cudaSuccess)
-      return BF_ERR_CUDA;
+      return cuda_fail();
     attr = true;
   }
   win_dec_split_kernel<R><<<grid, kWT_Threads, kWT_Smem, stream>>>(kmap, vmap, a, err);
@@ -567,7 +567,7 @@ int launch_win_dec(WinDecArgs a, cudaStream_t stream) {
   }
   if (rc) return rc;
   win_dec_combine_kernel<<<dim3(a.B * a.G, a.R), kWD_Threads, 0, stream>>>(a);
-  return cudaGetLastError() == cudaSuccess ? BF_OK : BF_ERR_CUDA;
+  return launch_status();
 }
 
 int launch_gather_evicted(const float* ring_km, const __nv_bfloat16* ring_v, const float* ring_g,
@@ -576,7 +576,7 @@ int launch_gather_evicted(const float* ring_km, const __nv_bfloat16* ring_v, con
                           float* b_e, cudaStream_t stream) {
   decode_gather_evicted_kernel<<<B * G, 256, 0, stream>>>(ring_km, ring_v, ring_g, ring_beta, ring_pos,
                                                           ring_pos_bstride, pos, G, W, D, k_e, v_e, g_e, b_e);
-  return cudaGetLastError() == cudaSuccess ? BF_OK : BF_ERR_CUDA;
+  return launch_status();
 }
 
 }  // namespace bfb

@@ -529,13 +529,13 @@ int launch_vt_prep(const __nv_bfloat16* v, long long vb, long long vg, long long
                    int nring, long long ring_pos0, int W, int B, int G, int Tk, int Tkp, __half* vt,
                    cudaStream_t stream) {
   vt_prep_kernel<<<dim3(Tkp / 64, B * G), 256, 0, stream>>>(v, vb, vg, vj, ring_v, nring, ring_pos0, W, G, Tk, Tkp, vt);
-  return cudaGetLastError() == cudaSuccess ? BF_OK : BF_ERR_CUDA;
+  return launch_status();
 }
 
 int launch_kext_prep(const __nv_bfloat16* kr, const __nv_bfloat16* ring_k, int nring, long long ring_pos0, int W, int B,
                      int T, int G, __nv_bfloat16* kext, cudaStream_t stream) {
   kext_prep_kernel<<<dim3(nring + T, B * G), 32, 0, stream>>>(kr, ring_k, nring, ring_pos0, W, T, G, kext);
-  return cudaGetLastError() == cudaSuccess ? BF_OK : BF_ERR_CUDA;
+  return launch_status();
 }
 
 int launch_window_prefill(const void* qr, const void* kext, const __half* vt, WinPreArgs a, cudaStream_t stream) {
@@ -560,12 +560,12 @@ int launch_window_prefill(const void* qr, const void* kext, const __half* vt, Wi
   if (!attr) {
     if (cudaFuncSetAttribute(window_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kWP_Smem) !=
         cudaSuccess)
-      return BF_ERR_CUDA;
+      return cuda_fail();
     attr = true;
   }
   dim3 grid((a.Tq + kWP_M - 1) / kWP_M, a.H, a.B);
   window_prefill_kernel<<<grid, kWP_Threads, kWP_Smem, stream>>>(qmap, kmap, vmap, omap, mmap, a);
-  return cudaGetLastError() == cudaSuccess ? BF_OK : BF_ERR_CUDA;
+  return launch_status();
 }
 
 }  // namespace bfb

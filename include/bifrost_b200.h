@@ -47,6 +47,8 @@ enum { BF_F32 = 0, BF_BF16 = 1, BF_F16 = 2 };
 
 /* Human-readable name of a status code. */
 const char* bf_strerror(int code);
+/* Text of the CUDA error behind the calling thread's last BF_ERR_CUDA status. */
+const char* bf_last_cuda_error(void);
 
 /* ABI version of this library (bumped on any signature change). */
 int bf_abi_version(void);
