@@ -49,16 +49,21 @@ int cuda_fail(cudaError_t e) {
   return BF_ERR_CUDA;
 }
 
-static cudaStream_t g_side[64] = {nullptr};
+static cudaStream_t g_side[2][64] = {{nullptr}};
 
-cudaStream_t side_stream(const DeviceState& st) {
+// which = 0: the device's least priority (the window, which fills whatever SMs the memory chain leaves);
+// which = 1: its greatest priority (the memory chain, whose CTAs are dispatched first as SMs free up)
+cudaStream_t side_stream(const DeviceState& st, int which) {
   std::lock_guard<std::mutex> lk(g_dev_mu);
-  if (!g_side[st.device]) {
+  if (!g_side[which][st.device]) {
+    int least = 0, greatest = 0;
+    if (cudaDeviceGetStreamPriorityRange(&least, &greatest) != cudaSuccess) return nullptr;
     cudaStream_t s = nullptr;
-    if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess) return nullptr;
-    g_side[st.device] = s;
+    if (cudaStreamCreateWithPriority(&s, cudaStreamNonBlocking, which ? greatest : least) != cudaSuccess)
+      return nullptr;
+    g_side[which][st.device] = s;
   }
-  return g_side[st.device];
+  return g_side[which][st.device];
 }
 
 // optional per-stage CUDA events (bf_stage_events): recorded on the launching stream around each stage

@@ -610,44 +610,126 @@ __global__ void __launch_bounds__(kP2_Threads, 1)
 }
 
 // ============================================================================================ P3
-constexpr int kP3_Threads = 192;   // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
-constexpr int kP3_SmemQ = kGC * kGD * 2;      // 64 KB
-constexpr int kP3_SmemKS = kGD * kGD;         // 64 KB: k tile, then S^T half (128 x 256 fp16)
-constexpr int kP3_SmemVN = 128 * kGC * 2;     // 32 KB: v'^T half
-constexpr int kP3_SmemP = kGC * kGC * 2;      // 32 KB
-constexpr int kP3_Smem = kP3_SmemQ + kP3_SmemKS + kP3_SmemVN + kP3_SmemP + 1024 + 256;
+// Persistent: a CTA walks work items (b, chunk, KV head g, value half vh) round-robin and, per item, the R
+// query heads of g.  The chunk's keys K, the state half S_vh^T and v'_vh^T stay in shared memory for the
+// item; each head's queries Q (fp16) stream through one buffer.  Per head:
+//   A = Q K^T (TMEM, one of two buffers) -> P = decayed causal A, fp16, written by the epilogue warps over
+//   the first half of their own A columns (the TMEM A operand of the next product) ->
+//   inter = Q S_vh^T, intra = P v'_vh (TMEM) -> o[:, vh half] = e^c inter + intra (+ gate and mix).
+// TMEM holds one A / P buffer and three output buffers X: inter is computed into X, the epilogue scales each
+// row by e^{c} in place while it stages P, and intra accumulates on top, so X = o_mem when the head's
+// products are done.  While the epilogue mixes and stores head m-1 from its X, the tensor core computes
+// intra of head m and Q K^T / inter of head m+1 into the other buffers; the stores stream HBM continuously.
+constexpr int kP3_Threads = 320;   // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue (two per TMEM lane quarter)
+constexpr int kP3_Epi = 256;       // epilogue threads: row (warp & 3) * 32 + lane, columns ((warp - 2) >> 2) * 64 .. + 63
+constexpr int kP3_SmemK = kGC * kGD * 2;      // 64 KB: k tile [128 tokens][256]
+constexpr int kP3_SmemS = 128 * kGD * 2;      // 64 KB: S^T half [128 dv][256 dk]
+constexpr int kP3_SmemV = 128 * kGC * 2;      // 32 KB: v'^T half [128 dv][128 tokens]
+constexpr int kP3_SmemQ = kGC * kGD * 2;      // 64 KB: queries of one head [128][256]
+constexpr int kP3_Smem = kP3_SmemK + kP3_SmemS + kP3_SmemV + kP3_SmemQ + 1024 + 256;
+constexpr uint32_t kP3_TA = 0;     // A / P
+constexpr uint32_t kP3_TX = 128;   // output buffers at 128, 256, 384 (head index mod 3)
+
+struct P3Item {
+  int b, c, g, vh;
+};
+__device__ __forceinline__ P3Item p3_item(const GdnStreams& s, long long u) {
+  P3Item it;
+  it.vh = (int)(u & 1);
+  const long long t = u >> 1;
+  it.g = (int)(t % s.G);
+  const long long bc = t / s.G;
+  it.c = (int)(bc % s.n_chunks);
+  it.b = (int)(bc / s.n_chunks);
+  return it;
+}
+__device__ __forceinline__ long long p3_qrow0(const GdnStreams& s, const P3Item& it) {
+  return s.chunk_tok0 ? (long long)s.chunk_tok0[it.c] : (long long)it.b * s.T + s.qoff + (long long)it.c * kGC;
+}
+
+// per (head, row) epilogue context of one epilogue thread
+struct P3Ctx {
+  float* orow;       // output row, this thread's 64 columns
+  const float* owp;  // its window result: float4 e at owp + e * owstride
+  const float* gcc;  // cumulative log-decay of the chunk
+  float ci, eci, gam, rho;
+  int owstride;
+  bool row_ok, gate_on, need_ow;   // need_ow: the output is the window result (mixed when gate_on)
+};
+__device__ __forceinline__ P3Ctx p3_ctx(const GdnStreams& s, const P3Item& it, int rh, int r, int cb) {
+  const int H = s.G * s.R, h = it.g * s.R + rh, bg = it.b * s.G + it.g;
+  const long long qrow0 = p3_qrow0(s, it);
+  const int nvalid = s.chunk_tok0 ? s.chunk_len[it.c] : s.n_steps - it.c * kGC;
+  P3Ctx x;
+  x.gcc = s.gc + (size_t)bg * s.n_pad + (size_t)it.c * kGC;
+  x.ci = x.gcc[r];
+  x.eci = __expf(x.ci);
+  x.row_ok = r < nvalid;
+  x.orow = s.o + (((size_t)qrow0 + r) * H + h) * kGD + it.vh * 128 + cb * 64;
+  if (s.owin) {   // tile order [value half][column block][row group][float4 e][row in group][4]
+    x.owp = s.owin + (((size_t)it.b * s.n_chunks + it.c) * H + h) * (size_t)(kGC * kGD) +
+            ((size_t)(((it.vh * 2 + cb) * 4 + (r >> 5)) * 16) * 32 + (r & 31)) * 4;
+    x.owstride = 128;
+  } else {
+    x.owp = x.orow;
+    x.owstride = 4;
+  }
+  x.need_ow = s.mix && x.row_ok && s.owin != nullptr;
+  x.gate_on = false;
+  x.gam = x.rho = 0.f;
+  if (s.mix && x.row_ok) {
+    const long long tq = qrow0 + r - (long long)it.b * s.T;   // token index within its sequence
+    x.gate_on = s.pos0 + tq >= s.W;
+    x.need_ow = x.need_ow || x.gate_on;
+    if (x.gate_on) {
+      const float lse = s.lse[((size_t)it.b * H + h) * s.T + tq];
+      const float z = s.mixx[((size_t)it.b * s.T + tq) * H + h] + s.mix_lse[h] * (lse - logf((float)s.W));
+      x.gam = 1.f / (1.f + __expf(-z));
+      x.rho = s.mem_scale[h];
+    }
+  }
+  return x;
+}
+
+// TMEM column of the fp16 P operand for key step ks (16 keys): the epilogue thread of column block cb writes
+// the probabilities of keys cb*64 .. cb*64+63 into the first 32 columns of its own 64 A columns
+__device__ __forceinline__ uint32_t p3_pcol(int ks) { return (uint32_t)((ks >> 2) * 64 + (ks & 3) * 8); }
 
 __global__ void __launch_bounds__(kP3_Threads, 1)
     gdn_p3_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                   const __grid_constant__ CUtensorMap smap, const __grid_constant__ CUtensorMap vmap, GdnStreams s) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sKS = sQ + kP3_SmemQ;
-  uint8_t* sVN = sKS + kP3_SmemKS;
-  uint8_t* sP = sVN + kP3_SmemVN;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kP3_SmemP);
-  uint64_t* bar_qk = bars + 0;     // q and k landed
-  uint64_t* bar_qkd = bars + 1;    // Q K^T done (k buffer free)
-  uint64_t* bar_s = bars + 2;      // S^T half landed
-  uint64_t* bar_vn = bars + 3;     // v'^T half landed
-  uint64_t* bar_p = bars + 4;      // P staged (128)
-  uint64_t* bar_o = bars + 5;      // half products done
-  uint64_t* bar_of = bars + 6;     // accumulators drained (128)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 7);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 8);
+  uint8_t* sK = smem;
+  uint8_t* sS = sK + kP3_SmemK;
+  uint8_t* sV = sS + kP3_SmemS;
+  uint8_t* sQ = sV + kP3_SmemV;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sQ + kP3_SmemQ);
+  uint64_t* bar_k = bars + 0;      // K landed (per item)
+  uint64_t* bar_s = bars + 1;      // S^T half landed (per item)
+  uint64_t* bar_v = bars + 2;      // v'^T half landed (per item)
+  uint64_t* bar_kf = bars + 3;     // the item's last Q K^T done: K buffer free
+  uint64_t* bar_sf = bars + 4;     // the item's last inter done: S buffer free
+  uint64_t* bar_vf = bars + 5;     // the item's last intra done: v' buffer free
+  uint64_t* bar_q = bars + 6;      // Q landed (per head)
+  uint64_t* bar_qf = bars + 7;     // inter done: Q buffer free (per head)
+  uint64_t* bar_a = bars + 8;      // A ready (per head)
+  uint64_t* bar_i = bars + 9;      // inter done: X readable for the scaling (per head)
+  uint64_t* bar_p = bars + 10;     // P staged and X scaled (kP3_Epi arrivals, per head)
+  uint64_t* bar_paf = bars + 11;   // intra done: A / P buffer free (per head)
+  uint64_t* bar_o = bars + 12;     // intra done: X = o_mem (per head)
+  uint64_t* bar_xf = bars + 13;    // [3] X buffer drained (kP3_Epi arrivals; buffer = head mod 3)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 17);
 
-  const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int R = s.R, G = s.G, H = G * R, gg = h / R;
-  const int bg = b * G + gg;
+  const int R = s.R, G = s.G, H = G * R;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int nch = s.n_chunks;
-  if (s.chunk_tok0 && c >= s.seq_chunk0[s.n_seq]) return;   // grid sized for the most chunks possible
-  // query/output row of chunk row 0 and the number of valid rows of this chunk
-  const long long qrow0 = s.chunk_tok0 ? (long long)s.chunk_tok0[c] : (long long)b * s.T + s.qoff + (long long)c * kGC;
-  const int nvalid = s.chunk_tok0 ? s.chunk_len[c] : s.n_steps - c * kGC;
+  // packed sequences: chunks beyond the last sequence's are not work (B = 1, so they are the trailing items)
+  const long long nitems = 2LL * G * (s.chunk_tok0 ? (long long)s.seq_chunk0[s.n_seq] : (long long)s.B * nch);
   if (t == 0) {
-    for (int i = 0; i < 7; ++i) mbar_init(bars + i, (i == 4 || i == 6) ? 128 : 1);
+    for (int i = 0; i < 16; ++i)
+      mbar_init(bars + i, (i == 10 || i >= 13) ? kP3_Epi : 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -659,7 +741,6 @@ __global__ void __launch_bounds__(kP3_Threads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // TMEM: QK^T cols 0..127, inter 128..255, intra 256..383
 
   if (warp == 0) {
     if (lane == 0) {
@@ -667,151 +748,196 @@ __global__ void __launch_bounds__(kP3_Threads, 1)
       tma_prefetch(&kmap);
       tma_prefetch(&smap);
       tma_prefetch(&vmap);
-      // read rows c*128.. of query stream -> query token qoff + c*128 + i (4-D map: d, token, atom, head)
-      mbar_expect_tx(bar_qk, kP3_SmemQ + kGC * kGD * 2);
-      tma_load_4d(sQ, &qmap, bar_qk, 0, (int)qrow0, 0, h);
-      tma_load_3d(sKS, &kmap, bar_qk, 0, bg * s.n_pad + c * kGC, 0);
-      int ns_ = 0, nv_ = 0;
-      bool ok = mbar_wait(bar_qkd, 0, abort_flag, s.err, 0x61);
-      for (int half = 0; half < 2 && ok; ++half) {
-        if (half == 1) ok = mbar_wait(bar_o, 0, abort_flag, s.err, 0x62);
+      int n = 0, m = 0;
+      bool ok = true;
+      for (long long u = blockIdx.x; u < nitems && ok; u += gridDim.x, ++n) {
+        const P3Item it = p3_item(s, u);
+        const int bg = it.b * G + it.g;
+        const long long qrow0 = p3_qrow0(s, it);
+        const int row_st = (bg * nch + it.c) * kGD + it.vh * 128;
+        if (n > 0) ok = mbar_wait(bar_kf, (n - 1) & 1, abort_flag, s.err, 0x61);
         if (!ok) break;
-        mbar_expect_tx(bar_s, 128 * kGD * 2);
-        tma_load_3d(sKS, &smap, bar_s, 0, ((bg * nch + c) * kGD) + half * 128, 0);
-        ns_ = half + 1;
-        mbar_expect_tx(bar_vn, kP3_SmemVN);
-        tma_load_3d(sVN, &vmap, bar_vn, 0, ((bg * nch + c) * kGD) + half * 128, 0);
-        nv_ = half + 1;
+        mbar_expect_tx(bar_k, kP3_SmemK);
+        tma_load_3d(sK, &kmap, bar_k, 0, bg * s.n_pad + it.c * kGC, 0);
+        for (int rh = 0; rh < R && ok; ++rh, ++m) {
+          if (m > 0) ok = mbar_wait(bar_qf, (m - 1) & 1, abort_flag, s.err, 0x62);
+          if (!ok) break;
+          mbar_expect_tx(bar_q, kP3_SmemQ);
+          tma_load_4d(sQ, &qmap, bar_q, 0, (int)qrow0, 0, it.g * R + rh);
+          if (rh == 0) {
+            if (n > 0) ok = mbar_wait(bar_sf, (n - 1) & 1, abort_flag, s.err, 0x63);
+            if (!ok) break;
+            mbar_expect_tx(bar_s, kP3_SmemS);
+            tma_load_3d(sS, &smap, bar_s, 0, row_st, 0);
+            if (n > 0) ok = mbar_wait(bar_vf, (n - 1) & 1, abort_flag, s.err, 0x64);
+            if (!ok) break;
+            mbar_expect_tx(bar_v, kP3_SmemV);
+            tma_load_3d(sV, &vmap, bar_v, 0, row_st, 0);
+          }
+        }
       }
-      mbar_wait(bar_qk, 0, nullptr, s.err, 0x63);
-      if (ns_ > 0) mbar_wait(bar_s, (ns_ - 1) & 1, nullptr, s.err, 0x64);
-      if (nv_ > 0) mbar_wait(bar_vn, (nv_ - 1) & 1, nullptr, s.err, 0x65);
+      // drain: every TMA issued has landed before the CTA may exit
+      if (n > 0) {
+        mbar_wait(bar_k, (n - 1) & 1, nullptr, s.err, 0x65);
+        mbar_wait(bar_s, (n - 1) & 1, nullptr, s.err, 0x65);
+        mbar_wait(bar_v, (n - 1) & 1, nullptr, s.err, 0x65);
+      }
+      if (m > 0) mbar_wait(bar_q, (m - 1) & 1, nullptr, s.err, 0x60);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t id128 = idesc_f16(128, 128, 0);
-      const uint32_t aQ = smem_u32(sQ), bKS = smem_u32(sKS), aP = smem_u32(sP), bVN = smem_u32(sVN);
-      bool ok = mbar_wait(bar_qk, 0, abort_flag, s.err, 0x66);
-      if (ok) {
-        tc_fence_after();
+      const uint32_t aQ = smem_u32(sQ), bK = smem_u32(sK), bS = smem_u32(sS), bV = smem_u32(sV);
+      int n = 0, m = 0;
+      bool ok = true;
+      for (long long u = blockIdx.x; u < nitems && ok; u += gridDim.x, ++n) {
+        for (int rh = 0; rh < R; ++rh, ++m) {
+          const int xb = m % 3;
+          const uint32_t X = tmem + kP3_TX + 128u * (uint32_t)xb;
+          // A = Q K^T (the A / P buffer is free once intra of head m-1 has read its P)
+          ok = mbar_wait(bar_q, m & 1, abort_flag, s.err, 0x66) &&
+               (rh > 0 || mbar_wait(bar_k, n & 1, abort_flag, s.err, 0x67)) &&
+               (m < 1 || mbar_wait(bar_paf, (m - 1) & 1, abort_flag, s.err, 0x68));
+          if (!ok) break;
+          tc_fence_after();
 #pragma unroll
-        for (int ks = 0; ks < kGD / 16; ++ks)
-          umma_f16_ss(tmem, sdesc_kstep(aQ, 128, ks), sdesc_kstep(bKS, 128, ks), id128, ks > 0);
-        umma_commit(bar_qkd);
-      }
-      for (int half = 0; half < 2 && ok; ++half) {
-        ok = mbar_wait(bar_s, half & 1, abort_flag, s.err, 0x67);
-        if (ok && half == 1) ok = mbar_wait(bar_of, 0, abort_flag, s.err, 0x68);
-        if (!ok) break;
-        tc_fence_after();
+          for (int ks = 0; ks < kGD / 16; ++ks)
+            umma_f16_ss(tmem + kP3_TA, sdesc_kstep(aQ, 128, ks), sdesc_kstep(bK, 128, ks), id128, ks > 0);
+          umma_commit(bar_a);
+          if (rh == R - 1) umma_commit(bar_kf);
+          // inter = Q S^T into X (free once head m-3's output has been stored)
+          ok = (m < 3 || mbar_wait(&bar_xf[xb], ((m / 3) - 1) & 1, abort_flag, s.err, 0x69)) &&
+               (rh > 0 || mbar_wait(bar_s, n & 1, abort_flag, s.err, 0x6a));
+          if (!ok) break;
+          tc_fence_after();
 #pragma unroll
-        for (int ks = 0; ks < kGD / 16; ++ks)
-          umma_f16_ss(tmem + 128, sdesc_kstep(aQ, 128, ks), sdesc_kstep(bKS, 128, ks), id128, ks > 0);
-        ok = mbar_wait(bar_p, 0, abort_flag, s.err, 0x69) && mbar_wait(bar_vn, half & 1, abort_flag, s.err, 0x6a);
-        if (!ok) break;
-        tc_fence_after();
+          for (int ks = 0; ks < kGD / 16; ++ks)
+            umma_f16_ss(X, sdesc_kstep(aQ, 128, ks), sdesc_kstep(bS, 128, ks), id128, ks > 0);
+          umma_commit(bar_i);
+          umma_commit(bar_qf);
+          if (rh == R - 1) umma_commit(bar_sf);
+          // X (scaled by e^c) += P v' with P from TMEM
+          ok = mbar_wait(bar_p, m & 1, abort_flag, s.err, 0x6d) &&
+               (rh > 0 || mbar_wait(bar_v, n & 1, abort_flag, s.err, 0x6e));
+          if (!ok) break;
+          tc_fence_after();
 #pragma unroll
-        for (int ks = 0; ks < kGC / 16; ++ks)
-          umma_f16_ss(tmem + 256, sdesc_kstep(aP, 128, ks), sdesc_kstep(bVN, 128, ks), id128, ks > 0);
-        umma_commit(bar_o);
+          for (int ks = 0; ks < kGC / 16; ++ks)
+            umma_f16_ts(X, tmem + kP3_TA + p3_pcol(ks), sdesc_kstep(bV, 128, ks), id128, 1u);
+          umma_commit(bar_o);
+          umma_commit(bar_paf);
+          if (rh == R - 1) umma_commit(bar_vf);
+        }
       }
     }
   } else {
     const int q4 = warp & 3;
-    const int r = q4 * 32 + lane;  // row i of the chunk (query step c*128 + r)
+    const int cb = (warp - 2) >> 2;   // column block (64 keys of A, 64 value columns of the half)
+    const int r = q4 * 32 + lane;     // row of the chunk
     const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
-    const float* gcc = s.gc + (size_t)bg * s.n_pad + (size_t)c * kGC;
-    const float ci = gcc[r];
-    bool alive = mbar_wait_warp(bar_qkd, 0, abort_flag, s.err, 0x6b);
-    if (alive) {
-      tc_fence_after();
+    float4 ow[16];     // window result of the head whose output is written next
+    P3Ctx pc{};
+    bool have_prev = false, alive = true;
+    long long u = blockIdx.x;
+    int rh = 0, m = 0;
+    P3Item it{};
+    if (u < nitems) it = p3_item(s, u);
+    for (;;) {
+      const bool has_cur = u < nitems;
+      P3Ctx cc{};
+      if (has_cur) cc = p3_ctx(s, it, rh, r, cb);
+      if (m == 0 && cc.need_ow) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) ow[e] = *reinterpret_cast<const float4*>(cc.owp + e * cc.owstride);
+      }
+      if (has_cur) {
+        // 1. P of this head over the first half of this thread's A columns
+        const uint32_t pa = trow + kP3_TA + cb * 64;
+        alive = mbar_wait_warp(bar_a, m & 1, abort_flag, s.err, 0x6c);
+        if (!alive) break;
+        tc_fence_after();
 #pragma unroll 1
-      for (int c0 = 0; c0 < kGC; c0 += 16) {
-        float f[16];
-        tmem_ld16_wait(trow + c0, f);
-        uint32_t pk[8];
+        for (int q = 0; q < 4; ++q) {   // 16 keys per step: A columns q*16.., P columns q*8..
+          const int c0 = cb * 64 + q * 16;
+          float f[16];
+          tmem_ld16_wait(pa + q * 16, f);
+          uint32_t pk[8];
 #pragma unroll
-        for (int e = 0; e < 16; e += 2) {
-          const int j = c0 + e;
-          const float p0 = (j <= r) ? f[e] * __expf(ci - gcc[j]) : 0.f;
-          const float p1 = (j + 1 <= r) ? f[e + 1] * __expf(ci - gcc[j + 1]) : 0.f;
-          pk[e / 2] = pack_half2(p0, p1);
+          for (int e = 0; e < 16; e += 2) {
+            const int j = c0 + e;
+            const float p0 = (j <= r) ? f[e] * __expf(cc.ci - cc.gcc[j]) : 0.f;
+            const float p1 = (j + 1 <= r) ? f[e + 1] * __expf(cc.ci - cc.gcc[j + 1]) : 0.f;
+            pk[e / 2] = pack_half2(p0, p1);
+          }
+          tmem_st8(pa + q * 8, pk);
         }
-        const int atom = c0 >> 6, col = c0 & 63;
-        *reinterpret_cast<uint4*>(sP + atom * (128 * 128) + sw128_offset(r, col)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-        *reinterpret_cast<uint4*>(sP + atom * (128 * 128) + sw128_offset(r, col + 8)) =
-            make_uint4(pk[4], pk[5], pk[6], pk[7]);
-      }
-      fence_async_smem();
-      tc_fence_before();
-      mbar_arrive(bar_p);
-    }
-    const bool row_ok = r < nvalid;
-    const float eci = __expf(ci);
-    float* orow = s.o + (((size_t)qrow0 + r) * H + h) * kGD;
-    // fused mix: gate of this query (position pos0 + token)
-    bool gate_on = false;
-    float gam = 0.f, rho = 0.f;
-    if (s.mix && row_ok) {
-      const long long tq = qrow0 + r - (long long)b * s.T;   // token index within its sequence
-      gate_on = s.pos0 + tq >= s.W;
-      if (gate_on) {
-        const float lse = s.lse[((size_t)b * H + h) * s.T + tq];
-        const float z = s.mixx[((size_t)b * s.T + tq) * H + h] + s.mix_lse[h] * (lse - logf((float)s.W));
-        gam = 1.f / (1.f + __expf(-z));
-        rho = s.mem_scale[h];
-      }
-    }
-    for (int half = 0; half < 2 && alive; ++half) {
-      // fused mix: the window result of this row's 32-column batch b is read one batch ahead (the first batch
-      // before the wait for the products), so its latency overlaps the TMEM reads and the arithmetic
-      float4 cur[8], nxt[8];
-      if (gate_on) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) cur[e] = *reinterpret_cast<const float4*>(orow + half * 128 + 4 * e);
-      }
-      alive = mbar_wait_warp(bar_o, half & 1, abort_flag, s.err, 0x6c);
-      if (!alive) break;
-      tc_fence_after();
+        // 2. inter * e^c in place (intra accumulates on top)
+        alive = mbar_wait_warp(bar_i, m & 1, abort_flag, s.err, 0x5e);
+        if (!alive) break;
+        tc_fence_after();
+        const uint32_t xr = trow + kP3_TX + 128u * (uint32_t)(m % 3) + cb * 64;
 #pragma unroll 1
-      for (int bb = 0; bb < 4; ++bb) {
-        if (gate_on && bb < 3) {
+        for (int q = 0; q < 4; ++q) {
+          uint32_t w[16];
+          tmem_ld16(xr + q * 16, w);
+          tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 8; ++e)
-            nxt[e] = *reinterpret_cast<const float4*>(orow + half * 128 + (bb + 1) * 32 + 4 * e);
+          for (int e = 0; e < 16; ++e) w[e] = __float_as_uint(__uint_as_float(w[e]) * cc.eci);
+          tmem_st16(xr + q * 16, w);
         }
+        tmem_wait_st();
+      }
+      // the previous head's products are complete before this head's intra may start (keeps bar_o one phase
+      // ahead at most)
+      if (have_prev) {
+        alive = mbar_wait_warp(bar_o, (m - 1) & 1, abort_flag, s.err, 0x6b);
+        if (!alive) break;
+      }
+      if (has_cur) {
+        tc_fence_before();
+        mbar_arrive(bar_p);
+      }
+      // 3. the previous head's output from its X; this head's window result is read into the registers used
+      if (have_prev) {
+        tc_fence_after();
+        const bool refill = has_cur && cc.need_ow;
+        const uint32_t xr = trow + kP3_TX + 128u * (uint32_t)((m - 1) % 3) + cb * 64;
 #pragma unroll
-        for (int sub = 0; sub < 2; ++sub) {
-          const int c0 = bb * 32 + sub * 16;
-          float fi[16], fa[16];
-          tmem_ld16_wait(trow + 128 + c0, fi);
-          tmem_ld16_wait(trow + 256 + c0, fa);
-          if (row_ok && !s.mix) {
+        for (int sub = 0; sub < 4; ++sub) {
+          float om[16];
+          tmem_ld16_wait(xr + sub * 16, om);
 #pragma unroll
-            for (int e = 0; e < 16; e += 4)
-              *reinterpret_cast<float4*>(orow + half * 128 + c0 + e) =
-                  make_float4(eci * fi[e] + fa[e], eci * fi[e + 1] + fa[e + 1], eci * fi[e + 2] + fa[e + 2],
-                              eci * fi[e + 3] + fa[e + 3]);
-          } else if (gate_on) {
-#pragma unroll
-            for (int e = 0; e < 16; e += 4) {
-              const float4 ow = cur[sub * 4 + e / 4];
+          for (int e4 = 0; e4 < 4; ++e4) {
+            const int e = sub * 4 + e4;
+            float* out = pc.orow + 4 * e;
+            if (pc.gate_on) {
+              const float4 w = ow[e];
               float4 res;
-              res.x = ow.x + gam * (rho * (eci * fi[e] + fa[e]) - ow.x);
-              res.y = ow.y + gam * (rho * (eci * fi[e + 1] + fa[e + 1]) - ow.y);
-              res.z = ow.z + gam * (rho * (eci * fi[e + 2] + fa[e + 2]) - ow.z);
-              res.w = ow.w + gam * (rho * (eci * fi[e + 3] + fa[e + 3]) - ow.w);
-              *reinterpret_cast<float4*>(orow + half * 128 + c0 + e) = res;
+              res.x = w.x + pc.gam * (pc.rho * om[4 * e4] - w.x);
+              res.y = w.y + pc.gam * (pc.rho * om[4 * e4 + 1] - w.y);
+              res.z = w.z + pc.gam * (pc.rho * om[4 * e4 + 2] - w.z);
+              res.w = w.w + pc.gam * (pc.rho * om[4 * e4 + 3] - w.w);
+              *reinterpret_cast<float4*>(out) = res;
+            } else if (pc.need_ow) {   // rows below the window: the window result as it is
+              *reinterpret_cast<float4*>(out) = ow[e];
+            } else if (pc.row_ok && !s.mix) {
+              *reinterpret_cast<float4*>(out) = make_float4(om[4 * e4], om[4 * e4 + 1], om[4 * e4 + 2], om[4 * e4 + 3]);
             }
+            if (refill) ow[e] = *reinterpret_cast<const float4*>(cc.owp + e * cc.owstride);
           }
         }
-        if (gate_on) {
-#pragma unroll
-          for (int e = 0; e < 8; ++e) cur[e] = nxt[e];
-        }
+        tc_fence_before();
+        mbar_arrive(&bar_xf[(m - 1) % 3]);
       }
-      tc_fence_before();
-      if (half == 0) mbar_arrive(bar_of);
+      if (!has_cur) break;
+      pc = cc;
+      have_prev = true;
+      ++m;
+      if (++rh == R) {
+        rh = 0;
+        u += gridDim.x;
+        if (u < nitems) it = p3_item(s, u);
+      }
     }
   }
   tc_fence_before();
@@ -944,8 +1070,13 @@ int launch_gdn_prefill(GdnStreams s, cudaStream_t stream, int parts) {
   if (rc) return rc;
   rc = make_tmap_kmajor(&vmap, s.VT, BF_F16, (uint64_t)s.B * s.G * s.n_chunks * kGD, kGC, kGC, 128, 2);
   if (rc) return rc;
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return cuda_fail();
+  const long long nitems = 2LL * s.B * s.G * s.n_chunks;   // (b, chunk, KV head, value half)
+  (void)H;
   stage_mark(ST_GDN_P3, 0, stream);
-  gdn_p3_kernel<<<dim3(s.n_chunks, H, s.B), kP3_Threads, kP3_Smem, stream>>>(qmap, kmap, smap, vmap, s);
+  gdn_p3_kernel<<<(unsigned)(nitems < sms ? nitems : sms), kP3_Threads, kP3_Smem, stream>>>(qmap, kmap, smap, vmap, s);
   stage_mark(ST_GDN_P3, 1, stream);
   return launch_status();
 }

@@ -45,12 +45,18 @@ __global__ void prep_x_weights_kernel(const float* __restrict__ ab_w, const floa
 }
 
 // ============================================================================ head projection
+// Work items are (b, head, 128-token tile), ordered head-major; a persistent CTA walks one contiguous run of
+// items, so its weights (the B operand, 128 KB) change at most once or twice.  The A operand streams through
+// a ring of 64-column K atoms: the loader warp keeps up to kHP_Slots atoms in flight, four converter warps
+// turn each landed atom from bf16 to fp16 in place, the MMA warp issues the atom's four K steps, and the
+// epilogue warps drain one of two TMEM accumulators while the tensor core fills the other.
 constexpr int kHP_M = 128;                  // tokens per tile
 constexpr int kHP_D = 256;                  // head dim (K and N)
-constexpr int kHP_Threads = 256;            // warps 0-3 epilogue, warps 4-7 staging + MMA issue
-constexpr int kHP_SmemA = kHP_M * kHP_D * 2;        // 64 KB
+constexpr int kHP_Threads = 320;            // warps 0-3 epilogue, 4-7 convert, 8 loads, 9 MMA issue
+constexpr int kHP_Slots = 6;                // A atoms in flight
+constexpr int kHP_Atom = kHP_M * 64 * 2;            // 16 KB: 128 rows x 64 K (bf16 or fp16), SW128
 constexpr int kHP_SmemB = kHP_D * kHP_D * 2;        // 128 KB
-constexpr int kHP_Smem = kHP_SmemA + kHP_SmemB + 1024 + 256;
+constexpr int kHP_Smem = kHP_SmemB + kHP_Slots * kHP_Atom + 1024 + 256;
 
 struct HeadProjArgs {
   const __nv_bfloat16* q;  // [B,T,H,D]
@@ -59,47 +65,58 @@ struct HeadProjArgs {
   __half* qm16;            // [B,T,H,D] fp16 (optional)
   float* km;               // [B,T,G,D]
   int B, T, H, G;
-  int tiles_per_cta;       // token tiles walked by one CTA
+  int ntiles;              // token tiles per (b, head)
+  long long nitems;        // B * (H + G) * ntiles
   unsigned int* err;
 };
+
+struct HPItem {
+  int b, head, tile;
+};
+__device__ __forceinline__ HPItem hp_item(const HeadProjArgs& a, long long u) {
+  HPItem it;
+  it.tile = (int)(u % a.ntiles);
+  const long long bh = u / a.ntiles;
+  it.head = (int)(bh % (a.H + a.G));
+  it.b = (int)(bh / (a.H + a.G));
+  return it;
+}
 
 __global__ void __launch_bounds__(kHP_Threads, 1)
     head_proj_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap qmap,
                      const __grid_constant__ CUtensorMap kmap, HeadProjArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sA = smem;
-  uint8_t* sB = smem + kHP_SmemA;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + kHP_SmemB);
-  uint64_t* bar_b = bars + 0;      // weights landed (TMA)
-  uint64_t* bar_mma = bars + 1;    // MMA finished reading A
-  uint64_t* bar_full = bars + 2;   // [2] accumulator ready
-  uint64_t* bar_free = bars + 4;   // [2] accumulator drained (128 arrivals)
-  uint64_t* bar_a = bars + 6;      // A tile landed (TMA)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 7);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 8);
+  uint8_t* sB = smem;
+  uint8_t* sA = smem + kHP_SmemB;                     // kHP_Slots atoms
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sA + kHP_Slots * kHP_Atom);
+  uint64_t* bar_b = bars + 0;                // weights landed (TMA)
+  uint64_t* bar_bfree = bars + 1;            // MMAs on the previous weights finished
+  uint64_t* full = bars + 2;                 // [kHP_Slots] atom landed (TMA)
+  uint64_t* conv = full + kHP_Slots;         // [kHP_Slots] atom converted (128 arrivals)
+  uint64_t* empty = conv + kHP_Slots;        // [kHP_Slots] MMA finished reading the atom
+  uint64_t* acc_full = empty + kHP_Slots;    // [2] accumulator ready
+  uint64_t* acc_free = acc_full + 2;         // [2] accumulator drained (128 arrivals)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_free + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(acc_free + 3);
 
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int head = blockIdx.y;     // 0..H+G-1
-  const int b = blockIdx.z;
-  const bool is_q = head < a.H;
-  const int nheads_src = is_q ? a.H : a.G;
-  const int hsrc = is_q ? head : head - a.H;
-  const CUtensorMap* amap = is_q ? &qmap : &kmap;
-  float* dst = is_q ? a.qm : a.km;
-  const float out_scale = is_q ? rsqrtf((float)kHP_D) : 1.f;
-  const int ntiles = (a.T + kHP_M - 1) / kHP_M;
-  const int tile0 = blockIdx.x * a.tiles_per_cta;
-  const int tile1 = min(ntiles, tile0 + a.tiles_per_cta);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const long long u0 = (long long)blockIdx.x * a.nitems / gridDim.x;
+  const long long u1 = (long long)(blockIdx.x + 1) * a.nitems / gridDim.x;
+  const int nloc = (int)(u1 - u0);
 
   if (tid == 0) {
     mbar_init(bar_b, 1);
-    mbar_init(bar_mma, 1);
-    mbar_init(&bar_full[0], 1);
-    mbar_init(&bar_full[1], 1);
-    mbar_init(&bar_free[0], 128);
-    mbar_init(&bar_free[1], 128);
-    mbar_init(bar_a, 1);
+    mbar_init(bar_bfree, 1);
+    for (int i = 0; i < kHP_Slots; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&conv[i], 128);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_free[i], 128);
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -112,73 +129,106 @@ __global__ void __launch_bounds__(kHP_Threads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp >= 4) {
-    // ---------------------------------------------------------------- A tiles (TMA, bf16 -> fp16 in place) + MMA issue
-    const int st = tid - 128;  // 0..127
-    if (st == 0) {
+  if (warp == 8) {
+    // ---------------------------------------------------------------- loads: weights per head, A atoms
+    if (lane == 0) {
       tma_prefetch(&wmap);
-      tma_prefetch(amap);
-      mbar_expect_tx(bar_b, kHP_SmemB);
-      tma_load_3d(sB, &wmap, bar_b, 0, head * kHP_D, 0);
-      if (tile0 < tile1) {
-        mbar_expect_tx(bar_a, kHP_SmemA);
-        tma_load_4d(sA, amap, bar_a, 0, b * a.T + tile0 * kHP_M, 0, hsrc);
-      }
-    }
-    int loaded = tile0 < tile1 ? 1 : 0;
-    for (int it = tile0; it < tile1; ++it) {
-      const int i = it - tile0;
-      if (!mbar_wait(bar_a, i & 1, abort_flag, a.err, 0x11)) break;
-      // convert this thread's 4 x 128-byte slice of the tile in place (same swizzled positions)
-#pragma unroll 4
-      for (int c = 0; c < 32; ++c) {
-        uint4* pch = reinterpret_cast<uint4*>(sA + (size_t)(c * 128 + st) * 16);
-        uint4 u = *pch;
-        uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          w[j] = pack_half2(__uint_as_float(w[j] << 16), __uint_as_float(w[j] & 0xffff0000u));
-        *pch = make_uint4(w[0], w[1], w[2], w[3]);
-      }
-      fence_async_smem();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (*abort_flag) break;
-      if (st == 0) {
-        bool ok = true;
-        if (i == 0) ok = mbar_wait(bar_b, 0, abort_flag, a.err, 0x12);
-        const int buf = i & 1;
-        if (ok && i >= 2) ok = mbar_wait(&bar_free[buf], ((i >> 1) - 1) & 1, abort_flag, a.err, 0x13);
-        if (ok) {
-          tc_fence_after();
-          const uint32_t d = tmem + buf * 256;
-          const uint32_t aB = smem_u32(sA), bB = smem_u32(sB);
-          constexpr uint32_t idesc = idesc_f16(kHP_M, kHP_D, 0);
-#pragma unroll
-          for (int ks = 0; ks < kHP_D / 16; ++ks)
-            umma_f16_ss(d, sdesc_kstep(aB, kHP_M, ks), sdesc_kstep(bB, kHP_D, ks), idesc, ks > 0);
-          umma_commit(bar_mma);
-          umma_commit(&bar_full[buf]);
-          // the next A tile may land once the tensor core has read this one
-          if (it + 1 < tile1 && mbar_wait(bar_mma, i & 1, abort_flag, a.err, 0x16)) {
-            mbar_expect_tx(bar_a, kHP_SmemA);
-            tma_load_4d(sA, amap, bar_a, 0, b * a.T + (it + 1) * kHP_M, 0, hsrc);
-            ++loaded;
-          }
+      tma_prefetch(&qmap);
+      tma_prefetch(&kmap);
+      int cur_head = -1, nb = 0, issued = 0;
+      bool ok = true;
+      for (int li = 0; li < nloc && ok; ++li) {
+        const HPItem it = hp_item(a, u0 + li);
+        if (it.head != cur_head) {
+          if (nb > 0) ok = mbar_wait(bar_bfree, (nb - 1) & 1, abort_flag, a.err, 0x18);
+          if (!ok) break;
+          mbar_expect_tx(bar_b, kHP_SmemB);
+          tma_load_3d(sB, &wmap, bar_b, 0, it.head * kHP_D, 0);
+          ++nb;
+          cur_head = it.head;
+        }
+        const bool is_q = it.head < a.H;
+        const int hsrc = is_q ? it.head : it.head - a.H;
+        for (int at = 0; at < 4; ++at) {
+          const int n = li * 4 + at, slot = n % kHP_Slots;
+          if (n >= kHP_Slots) ok = mbar_wait(&empty[slot], ((n / kHP_Slots) - 1) & 1, abort_flag, a.err, 0x11);
+          if (!ok) break;
+          mbar_expect_tx(&full[slot], kHP_Atom);
+          tma_load_4d(sA + slot * kHP_Atom, is_q ? (const void*)&qmap : (const void*)&kmap, &full[slot], 0,
+                      it.b * a.T + it.tile * kHP_M, at, hsrc);
+          issued = n + 1;
         }
       }
+      // drain: every TMA issued must have landed before the CTA may exit
+      if (nb > 0) mbar_wait(bar_b, (nb - 1) & 1, nullptr, a.err, 0x14);
+      for (int n = issued - 1; n >= 0 && n >= issued - kHP_Slots; --n)
+        mbar_wait(&full[n % kHP_Slots], (n / kHP_Slots) & 1, nullptr, a.err, 0x17);
     }
-    // drain: every TMA issued must have landed before the CTA may exit
-    if (st == 0) {
-      mbar_wait(bar_b, 0, nullptr, a.err, 0x14);
-      if (loaded > 0) mbar_wait(bar_a, (loaded - 1) & 1, nullptr, a.err, 0x17);
+  } else if (warp == 9) {
+    // ---------------------------------------------------------------- MMA issue
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16(kHP_M, kHP_D, 0);
+      const uint32_t bB = smem_u32(sB);
+      int cur_head = -1, nb = 0;
+      bool ok = true;
+      for (int li = 0; li < nloc && ok; ++li) {
+        const HPItem it = hp_item(a, u0 + li);
+        if (it.head != cur_head) {
+          ok = mbar_wait(bar_b, nb & 1, abort_flag, a.err, 0x12);
+          ++nb;
+          cur_head = it.head;
+        }
+        const int buf = li & 1;
+        if (ok && li >= 2) ok = mbar_wait(&acc_free[buf], ((li >> 1) - 1) & 1, abort_flag, a.err, 0x13);
+        const uint32_t d = tmem + buf * 256;
+        for (int at = 0; at < 4 && ok; ++at) {
+          const int n = li * 4 + at, slot = n % kHP_Slots;
+          ok = mbar_wait(&conv[slot], (n / kHP_Slots) & 1, abort_flag, a.err, 0x16);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t aA = smem_u32(sA + slot * kHP_Atom);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_f16_ss(d, sdesc_kstep(aA, kHP_M, kk), sdesc_kstep(bB, kHP_D, at * 4 + kk), idesc, (at | kk) > 0);
+          umma_commit(&empty[slot]);
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[buf]);
+        if (li + 1 < nloc && hp_item(a, u0 + li + 1).head != cur_head) umma_commit(bar_bfree);
+      }
+    }
+  } else if (warp >= 4) {
+    // ---------------------------------------------------------------- bf16 -> fp16, in place, per atom
+    const int st = tid - 128;  // 0..127
+    for (int n = 0; n < nloc * 4; ++n) {
+      const int slot = n % kHP_Slots;
+      if (!mbar_wait(&full[slot], (n / kHP_Slots) & 1, abort_flag, a.err, 0x19)) break;
+      uint4* atom = reinterpret_cast<uint4*>(sA + slot * kHP_Atom);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        uint4 v = atom[st + 128 * j];
+        uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          w[e] = pack_half2(__uint_as_float(w[e] << 16), __uint_as_float(w[e] & 0xffff0000u));
+        atom[st + 128 * j] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      fence_async_smem();
+      mbar_arrive(&conv[slot]);
     }
   } else {
     // ---------------------------------------------------------------- epilogue: one row per thread
     const int row = tid;  // TMEM lane
-    for (int it = tile0; it < tile1; ++it) {
-      const int i = it - tile0, buf = i & 1;
-      if (!mbar_wait_warp(&bar_full[buf], (i >> 1) & 1, abort_flag, a.err, 0x15)) break;
+    for (int li = 0; li < nloc; ++li) {
+      const int buf = li & 1;
+      if (!mbar_wait_warp(&acc_full[buf], (li >> 1) & 1, abort_flag, a.err, 0x15)) break;
       tc_fence_after();
+      const HPItem it = hp_item(a, u0 + li);
+      const bool is_q = it.head < a.H;
+      const int nheads_src = is_q ? a.H : a.G;
+      const int hsrc = is_q ? it.head : it.head - a.H;
+      float* dst = is_q ? a.qm : a.km;
+      const float out_scale = is_q ? rsqrtf((float)kHP_D) : 1.f;
       const uint32_t base = tmem + ((uint32_t)(warp * 32) << 16) + buf * 256;
       float ss = 0.f;
 #pragma unroll 1
@@ -193,8 +243,8 @@ __global__ void __launch_bounds__(kHP_Threads, 1)
         }
       }
       const float inv = out_scale / fmaxf(sqrtf(ss), 1e-12f);
-      const int t = it * kHP_M + row;
-      const size_t ooff = (((size_t)b * a.T + t) * nheads_src + hsrc) * kHP_D;
+      const int t = it.tile * kHP_M + row;
+      const size_t ooff = (((size_t)it.b * a.T + t) * nheads_src + hsrc) * kHP_D;
       const bool half_out = is_q && a.qm16 != nullptr;
 #pragma unroll 1
       for (int c = 0; c < kHP_D; c += 32) {
@@ -221,7 +271,7 @@ __global__ void __launch_bounds__(kHP_Threads, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(&bar_free[buf]);
+      mbar_arrive(&acc_free[buf]);
     }
   }
   tc_fence_before();
@@ -469,12 +519,12 @@ int launch_head_proj(const __nv_bfloat16* q, const __nv_bfloat16* k, const __hal
   CUtensorMap wmap, qmap, kmap;
   int rc = make_tmap_kmajor(&wmap, w_heads, BF_F16, (uint64_t)(H + G) * kHP_D, kHP_D, kHP_D, kHP_D, 4);
   if (rc) return rc;
-  // q [B,T,H,D] / k [B,T,G,D] bf16 as (d, token, atom, head): one 128-token x 256 tile of one head per TMA
+  // q [B,T,H,D] / k [B,T,G,D] bf16 as (d, token, atom, head): one 128-token x 64 atom of one head per TMA
   for (int which = 0; which < 2; ++which) {
     const int nh = which == 0 ? H : G;
     const uint64_t dims[4] = {64, (uint64_t)B * T, 4, (uint64_t)nh};
     const uint64_t strides[3] = {(uint64_t)nh * kHP_D * 2, 128, (uint64_t)kHP_D * 2};
-    const uint32_t box[4] = {64, (uint32_t)kHP_M, 4, 1};
+    const uint32_t box[4] = {64, (uint32_t)kHP_M, 1, 1};
     rc = make_tmap(which == 0 ? &qmap : &kmap, which == 0 ? (const void*)q : (const void*)k, BF_BF16, 4, dims, strides,
                    box, true);
     if (rc) return rc;
@@ -486,12 +536,11 @@ int launch_head_proj(const __nv_bfloat16* q, const __nv_bfloat16* k, const __hal
     attr = true;
   }
   const int ntiles = (T + kHP_M - 1) / kHP_M;
-  // enough CTAs to fill the GPU once, each walking a run of token tiles with its weights resident
-  const long long units = (long long)(H + G) * B;
-  int per = (int)((ntiles * units + sm_count - 1) / sm_count);
-  per = per < 1 ? 1 : (per > ntiles ? ntiles : per);
-  HeadProjArgs a{q, k, qm, qm16, km, B, T, H, G, per, err};
-  dim3 grid((ntiles + per - 1) / per, H + G, B);
+  const long long nitems = (long long)B * (H + G) * ntiles;
+  if (nitems == 0) return BF_OK;
+  // one persistent CTA per SM, each walking a contiguous run of (b, head, tile) items
+  const int grid = (int)(nitems < sm_count ? nitems : sm_count);
+  HeadProjArgs a{q, k, qm, qm16, km, B, T, H, G, ntiles, nitems, err};
   head_proj_kernel<<<grid, kHP_Threads, kHP_Smem, stream>>>(wmap, qmap, kmap, a);
   return launch_status();
 }

@@ -167,7 +167,9 @@ size_t bf_window_workspace(int B, int G, int Tk, int D) {
 static int window_common(const void* qr, const void* k_ext, const __half* vt, const void* sink_k, const void* sink_v,
                          int ns, long long qpos0, long long kpos0, long long klo, int B, int H, int G, int Tq, int Tk,
                          int window, float* o, float* lse, const float* o_mem, const float* mixx, const float* mix_lse,
-                         const float* mem_scale, unsigned int* err, cudaStream_t stream) {
+                         const float* mem_scale, unsigned int* err, cudaStream_t stream, float* o_perm = nullptr,
+                         int perm_tile0 = 0, int perm_nch = 0) {
+  if (o_perm && o_mem) return BF_ERR_INVALID_ARGUMENT;   // the permuted tiles are not mixed by the window
   WinPreArgs a{};
   a.B = B; a.H = H; a.G = G; a.Tq = Tq; a.Tk = Tk; a.Tkp = ((Tk + 63) / 64) * 64; a.W = window;
   a.qpos0 = qpos0; a.kpos0 = kpos0; a.klo = klo;
@@ -178,6 +180,7 @@ static int window_common(const void* qr, const void* k_ext, const __half* vt, co
   a.sv_b = a.sk_b; a.sv_h = a.sk_h; a.sv_k = 256;
   a.o = o; a.lse = lse;
   a.o_mem = o_mem; a.mixx = mixx; a.mix_lse = mix_lse; a.mem_scale = mem_scale;
+  a.o_perm = o_perm; a.perm_tile0 = perm_tile0; a.perm_nch = perm_nch;
   a.err = err;
   return launch_window_prefill(qr, k_ext, vt, a, stream);
 }
@@ -223,6 +226,7 @@ size_t bf_layer_prefill_workspace(int B, int T, int H, int G, int D, int window,
   n += al1k((size_t)B * G * D * Tkp * 2);   // V^T
   if (with_ring) n += al1k((size_t)B * G * Tk * D * 2);  // K of the extended sequence
   n += gdn_prefill_workspace(B, G, steps, false);
+  n += al1k((size_t)B * ((steps + 127) / 128) * H * 128 * D * 4);   // window results of the mixed rows, tile order
   return n;
 }
 
@@ -283,23 +287,29 @@ static int layer_prefill_impl(const bf_layer* L, const void* x, const void* q, c
   void* gws = p;
   float* lse_w = lse ? lse : lse_ws;   // the window's lse, needed by the gate
 
-  // the window (step 3) depends only on the inputs: when there are memory reads to overlap with, it runs on a
-  // side stream forked here, before the memory work is enqueued, and joins before the reads mix into o
+  // the window (step 3) depends only on the inputs: when there are memory reads to overlap with, the window
+  // and the memory chain (steps 1-2) run on two side streams forked here and joined before the reads mix
+  // into o.  The chain's stream has the greater priority, so its CTAs (the sequential scan among them, which
+  // fills only part of the GPU) are dispatched first and the window's CTAs fill the remaining SMs.
   const bool will_read = use_mem && phase != kPhaseBegin && (ring_case ? T : T - W) > 0;
   cudaStream_t ws2 = stream;   // (a null handle is the legacy default stream, a valid stream)
-  cudaEvent_t ev_fork = nullptr, ev_win = nullptr;
+  cudaStream_t wsm = stream;   // the memory chain
+  cudaEvent_t ev_fork = nullptr, ev_win = nullptr, ev_mem = nullptr;
   if (will_read) {
-    ws2 = side_stream(st);
-    if (!ws2) return cuda_fail();
+    ws2 = side_stream(st, 0);
+    wsm = side_stream(st, 1);
+    if (!ws2 || !wsm) return cuda_fail();
     if (cudaEventCreateWithFlags(&ev_fork, cudaEventDisableTiming) != cudaSuccess ||
-        cudaEventCreateWithFlags(&ev_win, cudaEventDisableTiming) != cudaSuccess)
+        cudaEventCreateWithFlags(&ev_win, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ev_mem, cudaEventDisableTiming) != cudaSuccess)
       return cuda_fail();
-    if (cudaEventRecord(ev_fork, stream) != cudaSuccess || cudaStreamWaitEvent(ws2, ev_fork, 0) != cudaSuccess)
+    if (cudaEventRecord(ev_fork, stream) != cudaSuccess || cudaStreamWaitEvent(wsm, ev_fork, 0) != cudaSuccess ||
+        cudaStreamWaitEvent(ws2, ev_fork, 0) != cudaSuccess)
       return cuda_fail();
   }
   // 1. memory inputs (projections on tcgen05)
   if ((use_mem || C) && phase != kPhaseFinish) {
-    rc = mem_inputs_impl(st, L, x, q, k, nullptr, start, B, T, nullptr, km, g, beta, mixx, stream, qm16, nullptr, 0);
+    rc = mem_inputs_impl(st, L, x, q, k, nullptr, start, B, T, nullptr, km, g, beta, mixx, wsm, qm16, nullptr, 0);
     if (rc) return rc;
   }
   // 2. memory: the write stream is delayed by W (token i enters memory when it leaves the window)
@@ -334,9 +344,13 @@ static int layer_prefill_impl(const bf_layer* L, const void* x, const void* q, c
     }
     if (s.n_steps > 0) {
       gdn_prefill_carve(s, gws);
+      // the window writes the rows the reads cover in tile order when its query tiles line up with the chunks
+      if (s.qoff % kGC == 0 && phase != kPhaseBegin) {
+        s.owin = reinterpret_cast<float*>(static_cast<uint8_t*>(gws) + al1k(gdn_prefill_workspace(B, G, s.n_steps, false)));
+      }
       reads = phase != kPhaseBegin;
       const int parts = phase == kPhaseBegin ? (kGdnP1 | kGdnP2) : phase == kPhaseFinish ? kGdnP2 : (kGdnP1 | kGdnP2);
-      rc = launch_gdn_prefill(s, stream, parts);
+      rc = launch_gdn_prefill(s, wsm, parts);
       if (rc) return rc;
     } else if (phase == kPhaseBegin) {
       identity_maps_kernel<<<grid_for((size_t)B * G * D * D), 256, 0, stream>>>(m_out, n_out, B * G, D);
@@ -363,14 +377,17 @@ static int layer_prefill_impl(const bf_layer* L, const void* x, const void* q, c
   stage_mark(ST_WIN_PREP, 1, ws2);
   stage_mark(ST_WIN, 0, ws2);
   rc = window_common(qr, kx, vt, sink_k, sink_v, ns, start, ring_case ? start - W : start, L->sinks, B, H, G, T, Tk, W,
-                     o, lse_w, nullptr, nullptr, nullptr, nullptr, st.err, ws2);
+                     o, lse_w, nullptr, nullptr, nullptr, nullptr, st.err, ws2, reads ? const_cast<float*>(s.owin) : nullptr,
+                     s.qoff / kGC, s.n_chunks);
   if (rc) return rc;
   stage_mark(ST_WIN, 1, ws2);
   if (will_read) {
-    if (cudaEventRecord(ev_win, ws2) != cudaSuccess || cudaStreamWaitEvent(stream, ev_win, 0) != cudaSuccess)
+    if (cudaEventRecord(ev_win, ws2) != cudaSuccess || cudaEventRecord(ev_mem, wsm) != cudaSuccess ||
+        cudaStreamWaitEvent(stream, ev_win, 0) != cudaSuccess || cudaStreamWaitEvent(stream, ev_mem, 0) != cudaSuccess)
       return cuda_fail();
     cudaEventDestroy(ev_fork);
     cudaEventDestroy(ev_win);
+    cudaEventDestroy(ev_mem);
   }
   // 4. memory reads, mixed into o by the gate
   if (reads) {

@@ -71,6 +71,13 @@ __device__ __forceinline__ uint32_t stage_off(uint32_t row, uint32_t col) {
   return (col >> 5) * (128u * 128u) + row * 128u + ((((col & 31u) >> 2) ^ (row & 7u)) << 4) + (col & 3u) * 4u;
 }
 
+// byte offset of (row, col) of a 128 x 256 fp32 output tile in the memory-read epilogue's order: warp (row group
+// row / 32, column block) loads float4 e of its 32 rows as 512 contiguous bytes
+__device__ __forceinline__ uint32_t perm_off(uint32_t row, uint32_t col) {
+  return (((((col >> 7) * 2 + ((col >> 6) & 1)) * 4 + (row >> 5)) * 16 + ((col & 63) >> 2)) * 32 + (row & 31)) * 16 +
+         (col & 3) * 4;
+}
+
 // TMEM column of the fp16 P operand for key-step ks (16 keys) of an S buffer: each softmax half writes the
 // probabilities of its 64 keys into the first 32 columns of its own 64 score columns.
 __device__ __forceinline__ uint32_t p_col(int ks) { return (uint32_t)((ks >> 2) * 64 + (ks & 3) * 8); }
@@ -122,6 +129,10 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
   }
   const int ns = a.ns;
   const bool mixing = a.o_mem != nullptr;
+  const int pc = blockIdx.x - a.perm_tile0;   // chunk of the memory reads this tile belongs to
+  float* const perm_dst = (a.o_perm && pc >= 0 && pc < a.perm_nch)
+                              ? a.o_perm + (((size_t)b * a.perm_nch + pc) * a.H + h) * (size_t)(kWP_M * kWP_D)
+                              : nullptr;
 
   if (tid == 0) {
     for (int i = 0; i < 13; ++i) mbar_init(bars + i, (i == 7 || i == 8 || i == 10 || i == 11) ? 8 : 1);
@@ -427,7 +438,7 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
         }
 #pragma unroll
         for (int e = 0; e < 32; e += 4) {
-          float4* sp4 = reinterpret_cast<float4*>(sO + stage_off(r, c + e));
+          float4* sp4 = reinterpret_cast<float4*>(sO + (perm_dst ? perm_off(r, c + e) : stage_off(r, c + e)));
           float4 res = make_float4(ov[e] * inv, ov[e + 1] * inv, ov[e + 2] * inv, ov[e + 3] * inv);
           if (gate_on) {
             const float4 mv = *sp4;
@@ -446,7 +457,11 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
     if (lane == 0) mbar_arrive(bar_st);
     if (st == 0) {
       if (alive && mbar_wait(bar_st, 0, abort_flag, a.err, 0x42)) {
-        for (int c = 0; c < 8; ++c) tma_store_4d(&omap, sO + c * (kWP_M * 128), c * 32, h, i0, b);
+        if (perm_dst) {
+          for (int c = 0; c < 8; ++c) bulk_store_1d(perm_dst + c * (kWP_M * 32), sO + c * (kWP_M * 128), kWP_M * 128);
+        } else {
+          for (int c = 0; c < 8; ++c) tma_store_4d(&omap, sO + c * (kWP_M * 128), c * 32, h, i0, b);
+        }
         tma_store_commit();
         tma_store_wait_read();
       }

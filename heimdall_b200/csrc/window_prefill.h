@@ -28,6 +28,11 @@ struct WinPreArgs {
   const float* mixx;    // [B,Tq,H]
   const float* mix_lse; // [H]
   const float* mem_scale;
+  // query tiles that the memory reads will mix (tile perm_tile0 + c, 0 <= c < perm_nch) go to o_perm instead of o:
+  // tile (b, c, h) at o_perm + ((b * perm_nch + c) * H + h) * 128 * 256 floats, in the order the memory-read
+  // epilogue loads it: [value half][64-column block][32-row group][float4 index][row in group][4]
+  float* o_perm;
+  int perm_tile0, perm_nch;
   unsigned int* err;
 };
 
