@@ -897,33 +897,62 @@ __global__ void __launch_bounds__(kP3_Threads, 1)
         tc_fence_before();
         mbar_arrive(bar_p);
       }
-      // 3. the previous head's output from its X; this head's window result is read into the registers used
+      // 3. the previous head's output: mixed in row order (thread = row) and written back over its X, then
+      //    stored from X in 16-row blocks, four threads per 32 contiguous bytes of a row (full sectors); this
+      //    head's window result is read into the registers as they are used
       if (have_prev) {
         tc_fence_after();
         const bool refill = has_cur && cc.need_ow;
-        const uint32_t xr = trow + kP3_TX + 128u * (uint32_t)((m - 1) % 3) + cb * 64;
+        const uint32_t xcol = kP3_TX + 128u * (uint32_t)((m - 1) % 3) + cb * 64;
+        const uint32_t xr = trow + xcol;
 #pragma unroll
         for (int sub = 0; sub < 4; ++sub) {
           float om[16];
           tmem_ld16_wait(xr + sub * 16, om);
+          uint32_t w[16];
 #pragma unroll
           for (int e4 = 0; e4 < 4; ++e4) {
             const int e = sub * 4 + e4;
-            float* out = pc.orow + 4 * e;
+            float4 res;
             if (pc.gate_on) {
-              const float4 w = ow[e];
-              float4 res;
-              res.x = w.x + pc.gam * (pc.rho * om[4 * e4] - w.x);
-              res.y = w.y + pc.gam * (pc.rho * om[4 * e4 + 1] - w.y);
-              res.z = w.z + pc.gam * (pc.rho * om[4 * e4 + 2] - w.z);
-              res.w = w.w + pc.gam * (pc.rho * om[4 * e4 + 3] - w.w);
-              *reinterpret_cast<float4*>(out) = res;
+              const float4 v = ow[e];
+              res.x = v.x + pc.gam * (pc.rho * om[4 * e4] - v.x);
+              res.y = v.y + pc.gam * (pc.rho * om[4 * e4 + 1] - v.y);
+              res.z = v.z + pc.gam * (pc.rho * om[4 * e4 + 2] - v.z);
+              res.w = v.w + pc.gam * (pc.rho * om[4 * e4 + 3] - v.w);
             } else if (pc.need_ow) {   // rows below the window: the window result as it is
-              *reinterpret_cast<float4*>(out) = ow[e];
-            } else if (pc.row_ok && !s.mix) {
-              *reinterpret_cast<float4*>(out) = make_float4(om[4 * e4], om[4 * e4 + 1], om[4 * e4 + 2], om[4 * e4 + 3]);
+              res = ow[e];
+            } else {
+              res = make_float4(om[4 * e4], om[4 * e4 + 1], om[4 * e4 + 2], om[4 * e4 + 3]);
             }
+            w[4 * e4] = __float_as_uint(res.x);
+            w[4 * e4 + 1] = __float_as_uint(res.y);
+            w[4 * e4 + 2] = __float_as_uint(res.z);
+            w[4 * e4 + 3] = __float_as_uint(res.w);
             if (refill) ow[e] = *reinterpret_cast<const float4*>(cc.owp + e * cc.owstride);
+          }
+          tmem_st16(xr + sub * 16, w);
+        }
+        tmem_wait_st();
+        __syncwarp();
+        const bool wr = pc.gate_on || pc.need_ow || (pc.row_ok && !s.mix);
+        const size_t rstride = (size_t)H * kGD;
+#pragma unroll
+        for (int sg = 0; sg < 2; ++sg) {
+          uint32_t v[32];
+          tmem_ld_16x256b_x8(tmem + ((uint32_t)(q4 * 32 + sg * 16) << 16) + xcol, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+            const int rl = sg * 16 + hf * 8 + (lane >> 2);   // row (within this warp's 32) of this half block
+            const bool wrow = __shfl_sync(0xffffffffu, wr, rl) != 0;
+            float* op = pc.orow + (long long)(rl - lane) * (long long)rstride + 2 * (lane & 3);
+            if (wrow) {
+#pragma unroll
+              for (int k = 0; k < 8; ++k)
+                *reinterpret_cast<float2*>(op + 8 * k) =
+                    make_float2(__uint_as_float(v[4 * k + 2 * hf]), __uint_as_float(v[4 * k + 2 * hf + 1]));
+            }
           }
         }
         tc_fence_before();
