@@ -12,7 +12,7 @@
 //     inversion of the 16x16 diagonal blocks then recursive doubling of the block-triangular inverse in
 //     shared memory, u and w on tcgen05; also writes fp16 keys,
 //     (e^{c_C - c} k)^T and the cumulative decays.
-// P2 (sequential over chunks, CTA = (b, KV head, 16 state columns)): the state block lives in registers (fp32),
+// P2 (sequential over chunks, CTA = (b, KV head, kP2_NB state columns)): the state block lives in registers (fp32),
 //     v' = u - w S and dS = k_tail^T v' run on tcgen05 with fp16 copies of S^T / v'^T staged in shared memory;
 //     the state at each chunk start and v' are written (fp16, transposed) for P3.
 // P3 (parallel, CTA = chunk x (b, query head)): Q K^T (-> decayed causal P in fp16), then per half of the value
@@ -374,13 +374,14 @@ __global__ void __launch_bounds__(kP1_Threads, 1) gdn_p1_kernel(GdnStreams s) {
 }
 
 // ============================================================================================ P2
-constexpr int kP2_NB = 16;               // state columns per CTA
+constexpr int kP2_NB = 32;               // state columns per CTA
 constexpr int kP2_Threads = 192;         // warps 0-3 state/epilogue, warp 4 TMA, warp 5 MMA
 constexpr int kP2_SmemW = kGC * kGD * 2;          // 64 KB
 constexpr int kP2_SmemKT = kGD * kGC * 2;         // 64 KB
 constexpr int kP2_SmemST = kP2_NB * kGD * 2;      // 8 KB
 constexpr int kP2_SmemVT = kP2_NB * kGC * 2;      // 4 KB
 constexpr int kP2_Smem = kP2_SmemW + kP2_SmemKT + kP2_SmemST + kP2_SmemVT + 1024 + 256;
+constexpr int kP2_Tmem = 3 * kP2_NB <= 64 ? 64 : 128;   // v' product, then the two halves of the state product
 
 __global__ void __launch_bounds__(kP2_Threads, 1)
     gdn_p2_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap ktmap, GdnStreams s) {
@@ -427,7 +428,7 @@ __global__ void __launch_bounds__(kP2_Threads, 1)
     fence_barrier_init();
   }
   if (warp == 0) {
-    tmem_alloc(tmem_slot, 64);
+    tmem_alloc(tmem_slot, kP2_Tmem);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -481,7 +482,7 @@ __global__ void __launch_bounds__(kP2_Threads, 1)
       }
     }
   } else {
-    // warps 0-3: thread r owns state rows r and r + 128 (columns col0 .. col0+15) and token row r
+    // warps 0-3: thread r owns state rows r and r + 128 (columns col0 .. col0 + kP2_NB - 1) and token row r
     const int r = t;
     const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
     float S0[kP2_NB], S1[kP2_NB];
@@ -525,28 +526,30 @@ __global__ void __launch_bounds__(kP2_Threads, 1)
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(bar_st);
-      // u row r (this chunk), columns col0..+15
+      // u row r (this chunk), columns col0 .. col0 + kP2_NB - 1
       const __half* up = s.u + ((size_t)bg * s.n_pad + (size_t)c * kGC + r) * kGD + col0;
       float uu[kP2_NB];
       if (mpath) {
 #pragma unroll
         for (int e = 0; e < kP2_NB; ++e) uu[e] = 0.f;
       } else {
-        const uint4 a0 = *reinterpret_cast<const uint4*>(up);
-        const uint4 a1 = *reinterpret_cast<const uint4*>(up + 8);
-        const uint32_t w[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const __half2 h2 = *reinterpret_cast<const __half2*>(&w[e]);
-          const float2 f2 = __half22float2(h2);
-          uu[2 * e] = f2.x;
-          uu[2 * e + 1] = f2.y;
+        for (int h8 = 0; h8 < kP2_NB / 8; ++h8) {
+          const uint4 a0 = *reinterpret_cast<const uint4*>(up + 8 * h8);
+          const uint32_t w[4] = {a0.x, a0.y, a0.z, a0.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f2 = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
+            uu[8 * h8 + 2 * e] = f2.x;
+            uu[8 * h8 + 2 * e + 1] = f2.y;
+          }
         }
       }
       if (!mbar_wait_warp(bar_m1, j & 1, abort_flag, s.err, 0x59)) { alive = false; break; }
       tc_fence_after();
       float dv[kP2_NB];
-      tmem_ld16_wait(trow, dv);
+#pragma unroll
+      for (int q = 0; q < kP2_NB; q += 16) tmem_ld16_wait(trow + q, *reinterpret_cast<float(*)[16]>(dv + q));
 #pragma unroll
       for (int e = 0; e < kP2_NB; ++e) st_half_sw128(sVT, kP2_NB, e, r, uu[e] - dv[e]);
       if (keep) {
@@ -562,8 +565,11 @@ __global__ void __launch_bounds__(kP2_Threads, 1)
       if (!mbar_wait_warp(bar_m2, j & 1, abort_flag, s.err, 0x5a)) { alive = false; break; }
       tc_fence_after();
       float d0[kP2_NB], d1[kP2_NB];
-      tmem_ld16_wait(trow + kP2_NB, d0);
-      tmem_ld16_wait(trow + 2 * kP2_NB, d1);
+#pragma unroll
+      for (int q = 0; q < kP2_NB; q += 16) {
+        tmem_ld16_wait(trow + kP2_NB + q, *reinterpret_cast<float(*)[16]>(d0 + q));
+        tmem_ld16_wait(trow + 2 * kP2_NB + q, *reinterpret_cast<float(*)[16]>(d1 + q));
+      }
       if (mpath) {
         // the map path keeps its state divided by the cumulative decay (the recurrence is homogeneous), so the
         // fp16 operand copies stay in range however far the segment decays; the factor is applied at the end
@@ -605,7 +611,7 @@ __global__ void __launch_bounds__(kP2_Threads, 1)
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(tmem, 64);
+    tmem_dealloc(tmem, kP2_Tmem);
   }
 }
 

@@ -243,30 +243,72 @@ __global__ void __launch_bounds__(kHP_Threads, 1)
         }
       }
       const float inv = out_scale / fmaxf(sqrtf(ss), 1e-12f);
-      const int t = it.tile * kHP_M + row;
-      const size_t ooff = (((size_t)it.b * a.T + t) * nheads_src + hsrc) * kHP_D;
+      const bool row_ok = it.tile * kHP_M + row < a.T;
       const bool half_out = is_q && a.qm16 != nullptr;
+      // scaled (and for fp16 output packed into the first 16 columns of each 32) in place, then stored from TMEM
+      // in 16-row blocks: four threads write 32 contiguous bytes of a row
 #pragma unroll 1
       for (int c = 0; c < kHP_D; c += 32) {
         uint32_t r[32];
         tmem_ld32(base + c, r);
         tmem_wait_ld();
-        if (t < a.T) {
-          if (half_out) {
+        if (half_out) {
+          uint32_t pk[16];
 #pragma unroll
-            for (int j = 0; j < 32; j += 8)
-              *reinterpret_cast<uint4*>(a.qm16 + ooff + c + j) = make_uint4(
-                  pack_half2(__uint_as_float(r[j]) * inv, __uint_as_float(r[j + 1]) * inv),
-                  pack_half2(__uint_as_float(r[j + 2]) * inv, __uint_as_float(r[j + 3]) * inv),
-                  pack_half2(__uint_as_float(r[j + 4]) * inv, __uint_as_float(r[j + 5]) * inv),
-                  pack_half2(__uint_as_float(r[j + 6]) * inv, __uint_as_float(r[j + 7]) * inv));
-          } else {
-            float* op = dst + ooff;
+          for (int j = 0; j < 16; ++j) pk[j] = pack_half2(__uint_as_float(r[2 * j]) * inv, __uint_as_float(r[2 * j + 1]) * inv);
+          tmem_st16(base + c, pk);
+        } else {
 #pragma unroll
-            for (int j = 0; j < 32; j += 4)
-              *reinterpret_cast<float4*>(op + c + j) =
-                  make_float4(__uint_as_float(r[j]) * inv, __uint_as_float(r[j + 1]) * inv,
-                              __uint_as_float(r[j + 2]) * inv, __uint_as_float(r[j + 3]) * inv);
+          for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * inv);
+          tmem_st32(base + c, r);
+        }
+      }
+      tmem_wait_st();
+      __syncwarp();
+      const size_t row0 = ((size_t)it.b * a.T + (size_t)it.tile * kHP_M + warp * 32) * nheads_src + hsrc;   // row 0 of the warp
+      const int q = lane & 3;
+#pragma unroll 1
+      for (int sg = 0; sg < 2; ++sg) {
+        const uint32_t lb = tmem + ((uint32_t)(warp * 32 + sg * 16) << 16) + buf * 256;
+        bool ok[2];
+        size_t off[2];
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          const int rl = sg * 16 + hf * 8 + (lane >> 2);
+          ok[hf] = __shfl_sync(0xffffffffu, row_ok, rl) != 0;
+          off[hf] = (row0 + (size_t)rl * nheads_src) * kHP_D;
+        }
+        if (half_out) {
+#pragma unroll 1
+          for (int c = 0; c < kHP_D; c += 32) {   // 32 fp16 of a row = 16 packed columns at c
+            uint32_t v[8];
+            tmem_ld_16x256b_x2(lb + c, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+              if (ok[hf]) {
+                __half* op = a.qm16 + off[hf] + c + 4 * q;
+                *reinterpret_cast<uint2*>(op) = make_uint2(v[2 * hf], v[2 * hf + 1]);
+                *reinterpret_cast<uint2*>(op + 16) = make_uint2(v[4 + 2 * hf], v[5 + 2 * hf]);
+              }
+            }
+          }
+        } else {
+#pragma unroll 1
+          for (int c = 0; c < kHP_D; c += 64) {
+            uint32_t v[32];
+            tmem_ld_16x256b_x8(lb + c, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+              if (ok[hf]) {
+                float* op = dst + off[hf] + c + 2 * q;
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                  *reinterpret_cast<float2*>(op + 8 * k) =
+                      make_float2(__uint_as_float(v[4 * k + 2 * hf]), __uint_as_float(v[4 * k + 2 * hf + 1]));
+              }
+            }
           }
         }
       }
