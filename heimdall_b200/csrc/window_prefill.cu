@@ -107,8 +107,10 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
   uint64_t* bar_sk = bars + 11;    // sink keys staged (one arrival per softmax warp)
   uint64_t* bar_sink = bars + 12;  // sink scores in TMEM
   uint64_t* pair = bars + 13;      // [4] sync of the two softmax warps on a lane quarter (one arrival per warp)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 18);
+  uint64_t* o_fin = bars + 17;     // the last O += P V finished (once per CTA; a parity wait on v_empty could
+                                   // alias: nothing orders the next-to-last product before the last softmax)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 19);
   // row exchange: [2 tile parities][2 halves][128] running maxima, then [2 halves][128] final sums
   float* xch = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);
 
@@ -137,6 +139,7 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
   if (tid == 0) {
     for (int i = 0; i < 13; ++i) mbar_init(bars + i, (i == 7 || i == 8 || i == 10 || i == 11) ? 8 : 1);
     for (int i = 0; i < 4; ++i) mbar_init(pair + i, 2);
+    mbar_init(o_fin, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -205,6 +208,7 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
         for (int ks = 0; ks < kWP_N / 16; ++ks)
           umma_f16_ts(tmem + kTmO, tmem + s * kWP_N + p_col(ks), sdesc_kstep(bV, kWP_D, ks), idesc_pv, (jj | ks) > 0);
         umma_commit(v_empty);
+        if (jj == n - 1) umma_commit(o_fin);
         return true;
       };
       for (int j = 0; j < n && ok; ++j) {
@@ -371,7 +375,7 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
       if (lane == 0) mbar_arrive(&p_full[s]);
     }
     // ------------------------------------------------------------------ epilogue
-    if (alive && n > 0) alive = mbar_wait_warp(v_empty, (n - 1) & 1, abort_flag, a.err, 0x3d);
+    if (alive && n > 0) alive = mbar_wait_warp(o_fin, 0, abort_flag, a.err, 0x3d);
     tc_fence_after();
     // the memory read of the fused mix lands in the staging buffer (K/V are free once the last product ended)
     if (mixing && st == 0 && alive) {
