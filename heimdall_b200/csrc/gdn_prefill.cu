@@ -655,13 +655,26 @@ __device__ __forceinline__ long long p3_qrow0(const GdnStreams& s, const P3Item&
 
 // per (head, row) epilogue context of one epilogue thread
 struct P3Ctx {
-  float* orow;       // output row, this thread's 64 columns
-  const float* owp;  // its window result: float4 e at owp + e * owstride
-  const float* gcc;  // cumulative log-decay of the chunk
+  float* orow;        // output row, this thread's 64 columns
+  const __half* owp;  // its window result in the workspace: 8 fp16 of column group e8 at owp + e8 * 256
+  const float* gcc;   // cumulative log-decay of the chunk
   float ci, eci, gam, rho;
-  int owstride;
   bool row_ok, gate_on, need_ow;   // need_ow: the output is the window result (mixed when gate_on)
 };
+// the window result of this thread's 8-column group e8 (fp16): from the workspace, or from o itself
+__device__ __forceinline__ uint4 p3_load_ow(const P3Ctx& x, int e8) {
+  if (x.owp) return *reinterpret_cast<const uint4*>(x.owp + e8 * 256);
+  const float4 lo = *reinterpret_cast<const float4*>(x.orow + 8 * e8);
+  const float4 hi = *reinterpret_cast<const float4*>(x.orow + 8 * e8 + 4);
+  return make_uint4(pack_half2(lo.x, lo.y), pack_half2(lo.z, lo.w), pack_half2(hi.x, hi.y), pack_half2(hi.z, hi.w));
+}
+__device__ __forceinline__ float4 p3_ow4(const uint4& u, int half) {   // columns 4 half .. 4 half + 3 of a group
+  const uint32_t a = half ? u.z : u.x, b = half ? u.w : u.y;
+  const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&a));
+  const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&b));
+  return make_float4(f0.x, f0.y, f1.x, f1.y);
+}
+
 __device__ __forceinline__ P3Ctx p3_ctx(const GdnStreams& s, const P3Item& it, int rh, int r, int cb) {
   const int H = s.G * s.R, h = it.g * s.R + rh, bg = it.b * s.G + it.g;
   const long long qrow0 = p3_qrow0(s, it);
@@ -672,14 +685,10 @@ __device__ __forceinline__ P3Ctx p3_ctx(const GdnStreams& s, const P3Item& it, i
   x.eci = __expf(x.ci);
   x.row_ok = r < nvalid;
   x.orow = s.o + (((size_t)qrow0 + r) * H + h) * kGD + it.vh * 128 + cb * 64;
-  if (s.owin) {   // tile order [value half][column block][row group][float4 e][row in group][4]
-    x.owp = s.owin + (((size_t)it.b * s.n_chunks + it.c) * H + h) * (size_t)(kGC * kGD) +
-            ((size_t)(((it.vh * 2 + cb) * 4 + (r >> 5)) * 16) * 32 + (r & 31)) * 4;
-    x.owstride = 128;
-  } else {
-    x.owp = x.orow;
-    x.owstride = 4;
-  }
+  // tile order [value half][column block][row group][8-column group][row in group][8]
+  x.owp = s.owin ? s.owin + (((size_t)it.b * s.n_chunks + it.c) * H + h) * (size_t)(kGC * kGD) +
+                       ((size_t)(((it.vh * 2 + cb) * 4 + (r >> 5)) * 8) * 32 + (r & 31)) * 8
+                 : nullptr;
   x.need_ow = s.mix && x.row_ok && s.owin != nullptr;
   x.gate_on = false;
   x.gam = x.rho = 0.f;
@@ -841,7 +850,7 @@ __global__ void __launch_bounds__(kP3_Threads, 1)
     const int cb = (warp - 2) >> 2;   // column block (64 keys of A, 64 value columns of the half)
     const int r = q4 * 32 + lane;     // row of the chunk
     const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
-    float4 ow[16];     // window result of the head whose output is written next
+    uint4 ow[8];       // window result (fp16) of the head whose output is written next
     P3Ctx pc{};
     bool have_prev = false, alive = true;
     long long u = blockIdx.x;
@@ -854,7 +863,7 @@ __global__ void __launch_bounds__(kP3_Threads, 1)
       if (has_cur) cc = p3_ctx(s, it, rh, r, cb);
       if (m == 0 && cc.need_ow) {
 #pragma unroll
-        for (int e = 0; e < 16; ++e) ow[e] = *reinterpret_cast<const float4*>(cc.owp + e * cc.owstride);
+        for (int e8 = 0; e8 < 8; ++e8) ow[e8] = p3_load_ow(cc, e8);
       }
       if (has_cur) {
         // 1. P of this head over the first half of this thread's A columns
@@ -921,13 +930,13 @@ __global__ void __launch_bounds__(kP3_Threads, 1)
             const int e = sub * 4 + e4;
             float4 res;
             if (pc.gate_on) {
-              const float4 v = ow[e];
+              const float4 v = p3_ow4(ow[e >> 1], e & 1);
               res.x = v.x + pc.gam * (pc.rho * om[4 * e4] - v.x);
               res.y = v.y + pc.gam * (pc.rho * om[4 * e4 + 1] - v.y);
               res.z = v.z + pc.gam * (pc.rho * om[4 * e4 + 2] - v.z);
               res.w = v.w + pc.gam * (pc.rho * om[4 * e4 + 3] - v.w);
             } else if (pc.need_ow) {   // rows below the window: the window result as it is
-              res = ow[e];
+              res = p3_ow4(ow[e >> 1], e & 1);
             } else {
               res = make_float4(om[4 * e4], om[4 * e4 + 1], om[4 * e4 + 2], om[4 * e4 + 3]);
             }
@@ -935,7 +944,7 @@ __global__ void __launch_bounds__(kP3_Threads, 1)
             w[4 * e4 + 1] = __float_as_uint(res.y);
             w[4 * e4 + 2] = __float_as_uint(res.z);
             w[4 * e4 + 3] = __float_as_uint(res.w);
-            if (refill) ow[e] = *reinterpret_cast<const float4*>(cc.owp + e * cc.owstride);
+            if (refill && (e & 1)) ow[e >> 1] = p3_load_ow(cc, e >> 1);
           }
           tmem_st16(xr + sub * 16, w);
         }

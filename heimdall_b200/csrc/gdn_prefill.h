@@ -61,9 +61,9 @@ struct GdnStreams {
   const float* mixx;           // [B,T,H]
   const float* mix_lse;        // [H]
   const float* mem_scale;      // [H]
-  // with mix: the window result of the rows this kernel reads, per (b, chunk, head) tile of 128 x 256 fp32 in
+  // with mix: the window result of the rows this kernel reads, per (b, chunk, head) tile of 128 x 256 fp16 in
   // the order of the epilogue's loads (null: the window result is read from o itself)
-  const float* owin;
+  const __half* owin;
   unsigned int* err;
 };
 

@@ -166,10 +166,8 @@ size_t bf_window_workspace(int B, int G, int Tk, int D) {
 
 static int window_common(const void* qr, const void* k_ext, const __half* vt, const void* sink_k, const void* sink_v,
                          int ns, long long qpos0, long long kpos0, long long klo, int B, int H, int G, int Tq, int Tk,
-                         int window, float* o, float* lse, const float* o_mem, const float* mixx, const float* mix_lse,
-                         const float* mem_scale, unsigned int* err, cudaStream_t stream, float* o_perm = nullptr,
-                         int perm_tile0 = 0, int perm_nch = 0) {
-  if (o_perm && o_mem) return BF_ERR_INVALID_ARGUMENT;   // the permuted tiles are not mixed by the window
+                         int window, float* o, float* lse, unsigned int* err, cudaStream_t stream,
+                         __half* o_perm = nullptr, int perm_tile0 = 0, int perm_nch = 0, int persistent = 1) {
   WinPreArgs a{};
   a.B = B; a.H = H; a.G = G; a.Tq = Tq; a.Tk = Tk; a.Tkp = ((Tk + 63) / 64) * 64; a.W = window;
   a.qpos0 = qpos0; a.kpos0 = kpos0; a.klo = klo;
@@ -179,8 +177,7 @@ static int window_common(const void* qr, const void* k_ext, const __half* vt, co
   a.sk_b = (long long)G * ns * 256; a.sk_h = (long long)ns * 256; a.sk_k = 256;
   a.sv_b = a.sk_b; a.sv_h = a.sk_h; a.sv_k = 256;
   a.o = o; a.lse = lse;
-  a.o_mem = o_mem; a.mixx = mixx; a.mix_lse = mix_lse; a.mem_scale = mem_scale;
-  a.o_perm = o_perm; a.perm_tile0 = perm_tile0; a.perm_nch = perm_nch;
+  a.o_perm = o_perm; a.perm_tile0 = perm_tile0; a.perm_nch = perm_nch; a.persistent = persistent;
   a.err = err;
   return launch_window_prefill(qr, k_ext, vt, a, stream);
 }
@@ -206,8 +203,8 @@ int bf_window_attn_fwd(const void* qr, const void* k_ext, const void* v_ext, lon
   __half* vt = static_cast<__half*>(ws);
   rc = launch_vt_prep(static_cast<const __nv_bfloat16*>(v_ext), vb, vg, vj, nullptr, 0, 0, 1, B, G, Tk, Tkp, vt, stream);
   if (rc) return rc;
-  return window_common(qr, k_ext, vt, sink_k, sink_v, ns, qpos0, kpos0, klo, B, H, G, Tq, Tk, window, o, lse, nullptr,
-                       nullptr, nullptr, nullptr, st.err, stream);
+  return window_common(qr, k_ext, vt, sink_k, sink_v, ns, qpos0, kpos0, klo, B, H, G, Tq, Tk, window, o, lse, st.err,
+                       stream);
 }
 
 // ================================================================================ fused layer prefill
@@ -226,7 +223,7 @@ size_t bf_layer_prefill_workspace(int B, int T, int H, int G, int D, int window,
   n += al1k((size_t)B * G * D * Tkp * 2);   // V^T
   if (with_ring) n += al1k((size_t)B * G * Tk * D * 2);  // K of the extended sequence
   n += gdn_prefill_workspace(B, G, steps, false);
-  n += al1k((size_t)B * ((steps + 127) / 128) * H * 128 * D * 4);   // window results of the mixed rows, tile order
+  n += al1k((size_t)B * ((steps + 127) / 128) * H * 128 * D * 2);   // window results of the mixed rows (fp16), tile order
   return n;
 }
 
@@ -346,7 +343,7 @@ static int layer_prefill_impl(const bf_layer* L, const void* x, const void* q, c
       gdn_prefill_carve(s, gws);
       // the window writes the rows the reads cover in tile order when its query tiles line up with the chunks
       if (s.qoff % kGC == 0 && phase != kPhaseBegin) {
-        s.owin = reinterpret_cast<float*>(static_cast<uint8_t*>(gws) + al1k(gdn_prefill_workspace(B, G, s.n_steps, false)));
+        s.owin = reinterpret_cast<__half*>(static_cast<uint8_t*>(gws) + al1k(gdn_prefill_workspace(B, G, s.n_steps, false)));
       }
       reads = phase != kPhaseBegin;
       const int parts = phase == kPhaseBegin ? (kGdnP1 | kGdnP2) : phase == kPhaseFinish ? kGdnP2 : (kGdnP1 | kGdnP2);
@@ -377,8 +374,8 @@ static int layer_prefill_impl(const bf_layer* L, const void* x, const void* q, c
   stage_mark(ST_WIN_PREP, 1, ws2);
   stage_mark(ST_WIN, 0, ws2);
   rc = window_common(qr, kx, vt, sink_k, sink_v, ns, start, ring_case ? start - W : start, L->sinks, B, H, G, T, Tk, W,
-                     o, lse_w, nullptr, nullptr, nullptr, nullptr, st.err, ws2, reads ? const_cast<float*>(s.owin) : nullptr,
-                     s.qoff / kGC, s.n_chunks);
+                     o, lse_w, st.err, ws2, reads ? const_cast<__half*>(s.owin) : nullptr, s.qoff / kGC, s.n_chunks,
+                     will_read ? 0 : 1);
   if (rc) return rc;
   stage_mark(ST_WIN, 1, ws2);
   if (will_read) {

@@ -23,16 +23,14 @@ struct WinPreArgs {
   // outputs
   float* o;             // [B,Tq,H,D]
   float* lse;           // [B,H,Tq] or null
-  // fused gate + mix (o_mem null: plain window output)
-  const float* o_mem;   // [B,Tq,H,D]
-  const float* mixx;    // [B,Tq,H]
-  const float* mix_lse; // [H]
-  const float* mem_scale;
-  // query tiles that the memory reads will mix (tile perm_tile0 + c, 0 <= c < perm_nch) go to o_perm instead of o:
-  // tile (b, c, h) at o_perm + ((b * perm_nch + c) * H + h) * 128 * 256 floats, in the order the memory-read
-  // epilogue loads it: [value half][64-column block][32-row group][float4 index][row in group][4]
-  float* o_perm;
+  // query tiles that the memory reads will mix (tile perm_tile0 + c, 0 <= c < perm_nch) go to o_perm instead of o,
+  // in fp16: tile (b, c, h) at o_perm + ((b * perm_nch + c) * H + h) * 128 * 256 halves, in the order the
+  // memory-read epilogue loads it: [value half][64-column block][32-row group][8-column group][row in group][8]
+  __half* o_perm;
   int perm_tile0, perm_nch;
+  // launch: one CTA per SM walking the items (fastest alone), or one CTA per item (lets concurrent kernels on
+  // other streams take SMs as CTAs finish: the layer prefill, where the memory chain runs beside the window)
+  int persistent;
   unsigned int* err;
 };
 
