@@ -10,9 +10,11 @@
 // Work split: columns of S (the Dv axis) are independent.  An item is one 32-column block of one
 // (sequence, KV head) state, a [D rows][32] fp32 tile.  Persistent CTAs (one per SM) stream items
 // through a ring of shared-memory stages: warp 8 issues one TMA per tile plus bulk copies of the item's
-// q_r and k vectors (and stages v and the gates), so several tiles are in flight per SM; compute warp w
-// owns column quad w over all rows (lane = rows lane + 32 i, so every column sum reduces inside the warp
-// with shuffles), writes the updated tile back over the stage, and warp 9 stores it with one TMA.
+// q_r and k vectors (and stages v and the gates), warp 10 computes the item's k . q_r dot products from the
+// copied vectors, so several tiles are in flight per SM; compute warp w owns column quad w over
+// all rows (lane = rows lane + 32 i, so every column sum reduces inside the warp with one reduce-scatter
+// of the R x 4 query sums and the 4 key sums), writes the updated tile back over the stage, and warp 9
+// stores it with one TMA.
 #include "capi_internal.h"
 #include "common.cuh"
 #include "tmap.h"
@@ -21,13 +23,13 @@ namespace bfb {
 
 constexpr int kDecCols = 32;          // columns of S per item
 constexpr int kDecMaxR = 8;
-constexpr int kDecStages = 4;
-constexpr int kDecThreads = 320;      // warps 0-7 compute (one column quad each), warp 8 loads, warp 9 stores
+constexpr int kDecStages = 5;
+constexpr int kDecThreads = 352;      // warps 0-7 compute (one column quad each), 8 loads, 9 stores, 10 k . q_r
 constexpr int kDecTile = 256 * kDecCols * 4;           // 32 KB (D = 256), 128-byte swizzled rows
 constexpr int kDecVec = (kDecMaxR + 1) * 256 * 4;      // q_r rows + k: 9 KB
-constexpr int kDecAux = 1024;                          // v slice (32 floats), g, beta
+constexpr int kDecAux = 1024;                          // v slice (32 floats), a, beta, k . q_r (at 40)
 constexpr int kDecStage = kDecTile + kDecVec + kDecAux;  // 42 KB, a multiple of 1024
-constexpr int kDecSmem = kDecStages * kDecStage + 256 + 1024;
+constexpr int kDecSmem = kDecStages * kDecStage + 256 + 1024;   // + barriers (4 per stage, abort flag)
 
 // Warp reduce-scatter by recursive halving: 32 per-lane partial values in, lane l holds the warp total of
 // quantity l (31 shuffles instead of 32 butterflies of 5).
@@ -60,6 +62,8 @@ __device__ __forceinline__ float reduce_scatter16(float (&v)[16], int lane) {
   return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
 }
 
+// RT > 0: R == RT and D == 256 at compile time (the Bifrost geometry); RT == 0: R and D from the arguments
+template <int RT>
 __global__ void __launch_bounds__(kDecThreads, 1) gdn_decode_kernel(
     const __grid_constant__ CUtensorMap smap, const __grid_constant__ CUtensorMap omap, const float* __restrict__ q,
     const float* __restrict__ k, const void* __restrict__ v, int v_bf16, const float* __restrict__ g,
@@ -70,16 +74,18 @@ __global__ void __launch_bounds__(kDecThreads, 1) gdn_decode_kernel(
   uint64_t* full = bars;                       // [stages] TMA bytes + the loader warp's arrival
   uint64_t* done = bars + kDecStages;          // [stages] 8 compute warps wrote the updated tile
   uint64_t* empty = bars + 2 * kDecStages;     // [stages] the store of the stage has read it
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 3 * kDecStages);
+  uint64_t* vec = bars + 3 * kDecStages;       // [stages] the q_r and k copies landed
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 4 * kDecStages);
 
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int ncb = D / kDecCols, nitems = BG * ncb;
   const uint32_t tile_bytes = (uint32_t)D * kDecCols * 4;
   if (t == 0) {
     for (int i = 0; i < kDecStages; ++i) {
-      mbar_init(&full[i], 2);
+      mbar_init(&full[i], 3);
       mbar_init(&done[i], 8);
       mbar_init(&empty[i], 1);
+      mbar_init(&vec[i], 1);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -99,10 +105,11 @@ __global__ void __launch_bounds__(kDecThreads, 1) gdn_decode_kernel(
       const int bg = item / ncb, col0 = (item % ncb) * kDecCols;
       uint8_t* st = smem + s * kDecStage;
       if (lane == 0) {
-        mbar_expect_tx(&full[s], tile_bytes + (uint32_t)(R + 1) * D * 4);
+        mbar_expect_tx(&vec[s], (uint32_t)(R + 1) * D * 4);
+        bulk_load_1d(st + kDecTile, q + (size_t)bg * R * D, (uint32_t)R * D * 4, &vec[s]);
+        bulk_load_1d(st + kDecTile + kDecMaxR * 256 * 4, k + (size_t)bg * D, (uint32_t)D * 4, &vec[s]);
+        mbar_expect_tx(&full[s], tile_bytes);
         tma_load_2d(st, &smap, &full[s], col0, bg * D);
-        bulk_load_1d(st + kDecTile, q + (size_t)bg * R * D, (uint32_t)R * D * 4, &full[s]);
-        bulk_load_1d(st + kDecTile + kDecMaxR * 256 * 4, k + (size_t)bg * D, (uint32_t)D * 4, &full[s]);
       }
       float* aux = reinterpret_cast<float*>(st + kDecTile + kDecVec);
       aux[lane] = v_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(v)[(size_t)bg * D + col0 + lane])
@@ -117,8 +124,49 @@ __global__ void __launch_bounds__(kDecThreads, 1) gdn_decode_kernel(
     // drain: the last TMA loads land before the CTA ends
     if (lane == 0) {
       const int last = n - 1;
-      for (int j = last; j >= 0 && j > last - kDecStages; --j)
+      for (int j = last; j >= 0 && j > last - kDecStages; --j) {
+        mbar_wait(&vec[j % kDecStages], (j / kDecStages) & 1, nullptr, err, 0x72);
         mbar_wait(&full[j % kDecStages], (j / kDecStages) & 1, nullptr, err, 0x72);
+      }
+    }
+  } else if (warp == 10) {
+    // ------------------------------------------------------------------ k . q_r of the item (the same for every
+    // column block of a state) from the stage's vector copies, into the stage's aux area
+    const int Rr = RT > 0 ? RT : R;
+    const int Dd = RT > 0 ? 256 : D;
+    int n = 0;
+    for (int item = blockIdx.x; item < nitems; item += gridDim.x, ++n) {
+      const int s = n % kDecStages;
+      if (!mbar_wait_warp(&vec[s], (n / kDecStages) & 1, abort_flag, err, 0x77)) break;
+      const uint8_t* st = smem + s * kDecStage;
+      const float* sq = reinterpret_cast<const float*>(st + kDecTile);
+      const float* sk = sq + kDecMaxR * 256;
+      float kv[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) kv[i] = (lane + 32 * i < Dd) ? sk[lane + 32 * i] : 0.f;
+      float acc[kDecMaxR];
+#pragma unroll
+      for (int r = 0; r < kDecMaxR; ++r) {
+        acc[r] = 0.f;
+        if (r < Rr) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            if (lane + 32 * i < Dd) acc[r] = fmaf(sq[r * Dd + lane + 32 * i], kv[i], acc[r]);
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < kDecMaxR; ++r)
+#pragma unroll
+        for (int o2 = 16; o2 >= 1; o2 >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o2);
+      float* aux = reinterpret_cast<float*>(smem + s * kDecStage + kDecTile + kDecVec);
+      if (lane < kDecMaxR) {
+        float val = acc[0];
+#pragma unroll
+        for (int r = 1; r < kDecMaxR; ++r) val = (lane == r) ? acc[r] : val;
+        aux[40 + lane] = val;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full[s]);
     }
   } else if (warp == 9) {
     // ------------------------------------------------------------------ stores: the updated tile by TMA
@@ -139,11 +187,17 @@ __global__ void __launch_bounds__(kDecThreads, 1) gdn_decode_kernel(
   } else {
     // ------------------------------------------------------------------ compute: warp w = column quad w,
     // lane = rows lane + 32 i; column sums reduce inside the warp
-    const int nrow = D >> 5;
+    const int Rr = RT > 0 ? RT : R;
+    const int Dd = RT > 0 ? 256 : D;
+    const int nrow = Dd >> 5;
     int n = 0;
     for (int item = blockIdx.x; item < nitems; item += gridDim.x, ++n) {
       const int s = n % kDecStages;
-      if (!mbar_wait_warp(&full[s], (n / kDecStages) & 1, abort_flag, err, 0x73)) break;
+      // (the vector copies completed before the k . q_r warp's arrival on full; their own barrier is
+      // observed here too, so the copies are visible to this warp directly)
+      if (!mbar_wait_warp(&full[s], (n / kDecStages) & 1, abort_flag, err, 0x73) ||
+          !mbar_wait_warp(&vec[s], (n / kDecStages) & 1, abort_flag, err, 0x78))
+        break;
       const int bg = item / ncb, col0 = (item % ncb) * kDecCols;
       uint8_t* tile = smem + s * kDecStage;
       const float* sq = reinterpret_cast<const float*>(tile + kDecTile);      // [R][D]
@@ -156,9 +210,6 @@ __global__ void __launch_bounds__(kDecThreads, 1) gdn_decode_kernel(
       float pq[kDecMaxR][4];
 #pragma unroll
       for (int r = 0; r < kDecMaxR; ++r) pq[r][0] = pq[r][1] = pq[r][2] = pq[r][3] = 0.f;
-      float kq[kDecMaxR];
-#pragma unroll
-      for (int r = 0; r < kDecMaxR; ++r) kq[r] = 0.f;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         if (i < nrow) {
@@ -167,40 +218,52 @@ __global__ void __launch_bounds__(kDecThreads, 1) gdn_decode_kernel(
           y.x *= a; y.y *= a; y.z *= a; y.w *= a;
           x[i] = y;
           kr[i] = sk[row];
-          pk[0] += kr[i] * y.x; pk[1] += kr[i] * y.y; pk[2] += kr[i] * y.z; pk[3] += kr[i] * y.w;
+          pk[0] = fmaf(kr[i], y.x, pk[0]); pk[1] = fmaf(kr[i], y.y, pk[1]);
+          pk[2] = fmaf(kr[i], y.z, pk[2]); pk[3] = fmaf(kr[i], y.w, pk[3]);
 #pragma unroll
           for (int r = 0; r < kDecMaxR; ++r) {
-            if (r < R) {
-              const float qv = sq[r * D + row];
-              pq[r][0] += qv * y.x; pq[r][1] += qv * y.y; pq[r][2] += qv * y.z; pq[r][3] += qv * y.w;
-              kq[r] += qv * kr[i];
+            if (r < Rr) {
+              const float qv = sq[r * Dd + row];
+              pq[r][0] = fmaf(qv, y.x, pq[r][0]); pq[r][1] = fmaf(qv, y.y, pq[r][1]);
+              pq[r][2] = fmaf(qv, y.z, pq[r][2]); pq[r][3] = fmaf(qv, y.w, pq[r][3]);
             }
           }
         }
       }
-      // column totals: A = q_r . (aS)[:, c] (quantity 4r + c), B = k . (aS)[:, c] (quantity c) and k . q_r (4 + r)
-      float va[32], vb[16];
+      // column totals by one reduce-scatter: quantity 4r + c = q_r . (aS)[:, c]; with R <= 7 the key sums
+      // k . (aS)[:, c] ride in quantities 28 + c, with R = 8 they take a second, 16-quantity pass
+      float va[32];
 #pragma unroll
       for (int r = 0; r < kDecMaxR; ++r)
 #pragma unroll
         for (int c = 0; c < 4; ++c) va[4 * r + c] = pq[r][c];
+      if (Rr <= 7) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c) vb[c] = pk[c];
-#pragma unroll
-      for (int r = 0; r < kDecMaxR; ++r) vb[4 + r] = kq[r];
-#pragma unroll
-      for (int i = 12; i < 16; ++i) vb[i] = 0.f;
+        for (int c = 0; c < 4; ++c) va[28 + c] = pk[c];
+      }
       const float ta = reduce_scatter32(va, lane);
-      const float tb = reduce_scatter16(vb, lane);
+      float ks4[4];
+      if (Rr <= 7) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) ks4[c] = __shfl_sync(0xffffffffu, ta, 28 + c);
+      } else {
+        float vb[16];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) vb[c] = pk[c];
+#pragma unroll
+        for (int i = 4; i < 16; ++i) vb[i] = 0.f;
+        const float tb = reduce_scatter16(vb, lane);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) ks4[c] = __shfl_sync(0xffffffffu, tb, 2 * c);
+      }
       float d4[4];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) d4[c] = (aux[warp * 4 + c] - __shfl_sync(0xffffffffu, tb, 2 * c)) * bt;
+      for (int c = 0; c < 4; ++c) d4[c] = (aux[warp * 4 + c] - ks4[c]) * bt;
       // outputs o_r[col] = (aS)^T q_r + delta * (k . q_r): lane 4r + c holds head r, column 4w + c
       {
         const int r = lane >> 2, c = lane & 3;
-        const float kqr = __shfl_sync(0xffffffffu, tb, 2 * (4 + r));
         const float dc = (c == 0) ? d4[0] : (c == 1) ? d4[1] : (c == 2) ? d4[2] : d4[3];
-        if (r < R) o[((size_t)bg * R + r) * D + col0 + warp * 4 + c] = ta + dc * kqr;
+        if (r < Rr) o[((size_t)bg * Rr + r) * Dd + col0 + warp * 4 + c] = ta + dc * aux[40 + r];
       }
       // rank-1 update written back over the tile (the store warp copies it out)
 #pragma unroll
@@ -241,14 +304,20 @@ int launch_gdn_decode(const float* q, const float* k, const void* v, int v_bf16,
   if (rc) return rc;
   static bool attr = false;
   if (!attr) {
-    if (cudaFuncSetAttribute(gdn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDecSmem) != cudaSuccess)
+    if (cudaFuncSetAttribute(gdn_decode_kernel<6>, cudaFuncAttributeMaxDynamicSharedMemorySize, kDecSmem) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(gdn_decode_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kDecSmem) != cudaSuccess)
       return cuda_fail();
     attr = true;
   }
   const int nitems = B * G * (D / kDecCols);
   const int grid = nitems < st.sm_count ? nitems : st.sm_count;
-  gdn_decode_kernel<<<grid, kDecThreads, kDecSmem, stream>>>(smap, omap, q, k, v, v_bf16, g, beta, o, B * G, R, D,
-                                                            st.err);
+  if (R == 6 && D == 256)
+    gdn_decode_kernel<6><<<grid, kDecThreads, kDecSmem, stream>>>(smap, omap, q, k, v, v_bf16, g, beta, o, B * G, R, D,
+                                                                 st.err);
+  else
+    gdn_decode_kernel<0><<<grid, kDecThreads, kDecSmem, stream>>>(smap, omap, q, k, v, v_bf16, g, beta, o, B * G, R, D,
+                                                                 st.err);
   return launch_status();
 }
 
