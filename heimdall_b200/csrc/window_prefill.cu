@@ -43,7 +43,7 @@ constexpr int kWP_SmemQ = kWP_M * kWP_D * 2;      // 64 KB
 constexpr int kWP_SmemK = kWP_N * kWP_D * 2;      // 64 KB
 constexpr int kWP_SmemV = kWP_D * kWP_N * 2;      // 64 KB
 constexpr int kWP_SmemSK = kWP_SinkRows * kWP_D * 2;      // 8 KB: sink keys, K-major 128-byte swizzle
-constexpr int kWP_SmemSV = 2 * kWP_MaxSinks * kWP_D * 4;  // 16 KB: sink values in fp32, two items
+constexpr int kWP_SmemSV = kWP_D * kWP_SinkRows * 2;     // 8 KB: sink values^T fp16 [256][16], no swizzle
 constexpr int kWP_Tiles = kWP_SmemQ + kWP_SmemK + kWP_SmemV + kWP_SmemSK + kWP_SmemSV;
 constexpr int kWP_Smem = kWP_Tiles + 256 + 4096 + 1024;   // + barriers + row exchanges (3 KB) + alignment
 constexpr float kRescaleLog2 = 8.0f;              // rescale O when the max grows by more than 2^8
@@ -72,6 +72,21 @@ __device__ __forceinline__ uint32_t cvt_half2(float lo, float hi) {
 // TMEM column of the fp16 P operand for key-step ks (16 keys) of an S buffer: each softmax half writes the
 // probabilities of its 64 keys into the first 32 columns of its own 64 score columns.
 __device__ __forceinline__ uint32_t p_col(int ks) { return (uint32_t)((ks >> 2) * 64 + (ks & 3) * 8); }
+
+// The sink values^T as the B operand of one K = 16 product: K-major without swizzle, core matrices of 8 rows x
+// 16 bytes; element (d, e) at (d / 8) * 256 + (e / 8) * 128 + (d % 8) * 16 + (e % 8) * 2 (8-row groups 256 B
+// apart, the two 8-key halves 128 B apart)
+__device__ __forceinline__ uint32_t sv_off(uint32_t d, uint32_t e) {
+  return (d >> 3) * 256u + (e >> 3) * 128u + (d & 7u) * 16u + (e & 7u) * 2u;
+}
+__device__ __forceinline__ uint64_t sdesc_sinkv(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr & 0x3FFFFu) >> 4);  // start address
+  d |= (uint64_t)(128 >> 4) << 16;               // leading byte offset: between the two 8-key core matrices
+  d |= (uint64_t)(256 >> 4) << 32;               // stride byte offset: between 8-row groups
+  d |= (uint64_t)1 << 46;                        // descriptor version (sm_100); swizzle mode 0 (none)
+  return d;
+}
 
 // one work item of the persistent kernel
 struct WItem {
@@ -116,7 +131,7 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
   uint8_t* sK = sQ + kWP_SmemQ;
   uint8_t* sV = sK + kWP_SmemK;
   uint8_t* sSK = sV + kWP_SmemV;           // [4 atoms][16 rows][128 B]
-  float* sSVb = reinterpret_cast<float*>(sSK + kWP_SmemSK);                  // [2 items][8][256]
+  uint8_t* sSV = sSK + kWP_SmemSK;         // sink values^T, fp16 (sv_off layout)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kWP_Tiles);
   uint64_t* bar_q = bars + 0;      // Q landed (per item)
   uint64_t* q_free = bars + 1;     // the item's last product reading Q finished (per item)
@@ -127,13 +142,14 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
   uint64_t* s_full = bars + 6;     // [2]
   uint64_t* p_full = bars + 8;     // [2] P_t in TMEM (one arrival per softmax warp)
   uint64_t* bar_sk = bars + 10;    // sink keys staged (one arrival per softmax warp, per item)
-  uint64_t* bar_sink = bars + 11;  // O free (previous item drained) and the item's sink scores in TMEM (per item)
-  uint64_t* o_fin = bars + 12;     // the item's last O += P V finished (per item with key tiles)
+  uint64_t* bar_sink = bars + 11;  // the item's sink scores in TMEM (per item, with sinks)
+  uint64_t* o_fin = bars + 12;     // the item's O is complete (per item)
   uint64_t* o_free = bars + 13;    // O drained by the epilogue (one arrival per softmax warp, per item)
-  uint64_t* ssync = bars + 14;     // the softmax warps read the sink scores (one arrival per warp, per item)
-  uint64_t* pair = bars + 15;      // [4] sync of the two softmax warps on a lane quarter (one arrival per warp)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 20);
+  uint64_t* psink = bars + 14;     // sink scores read and P_sink staged (one arrival per softmax warp, per item)
+  uint64_t* osink = bars + 15;     // O = P_sink V_sink finished (per item, with sinks)
+  uint64_t* pair = bars + 16;      // [4] sync of the two softmax warps on a lane quarter (one arrival per warp)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 21);
   // row exchange: [2 tile parities][2 halves][128] running maxima, then [2 halves][128] final sums
   float* xch = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);
 
@@ -143,7 +159,7 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
   const int ns = a.ns;
 
   if (tid == 0) {
-    for (int i = 0; i < 15; ++i) mbar_init(bars + i, (i == 8 || i == 9 || i == 10 || i == 13 || i == 14) ? 8 : 1);
+    for (int i = 0; i < 16; ++i) mbar_init(bars + i, (i == 8 || i == 9 || i == 10 || i == 13 || i == 14) ? 8 : 1);
     for (int i = 0; i < 4; ++i) mbar_init(pair + i, 2);
     *abort_flag = 0;
     fence_barrier_init();
@@ -203,25 +219,34 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
       constexpr uint32_t idesc_sk = idesc_f16(kWP_M, kWP_SinkRows, 1);
       constexpr uint32_t idesc_pv = idesc_f16(kWP_M, kWP_D, 0);
       const uint32_t aQ = smem_u32(sQ), bK = smem_u32(sK), bV = smem_u32(sV), bSK = smem_u32(sSK);
+      const uint64_t dSV = sdesc_sinkv(smem_u32(sSV));
       int it = 0, t = 0;
       bool ok = true;
       for (long long u = blockIdx.x; u < nitems && ok; u += gridDim.x, ++it) {
         const WItem w = win_item(a, u, ntq);
         ok = mbar_wait(bar_q, it & 1, abort_flag, a.err, 0x36);
         if (!ok) break;
-        // O is free once the previous item is drained; then the sink scores Q . sink_k go into O's columns
-        // (read by the softmax warps before this item's first O += P V)
-        auto sink_step = [&]() -> bool {
+        // the S buffer of the item's second tile holds the sink scores (columns 0..15) and P_sink (16..23) until
+        // that tile's product; its previous P was read by a product issued before this item's
+        const uint32_t sb = tmem + (uint32_t)((t + 1) & 1) * kWP_N;
+        auto sink_scores = [&]() -> bool {
+          if (ns == 0) return true;
           if (!mbar_wait(bar_sk, it & 1, abort_flag, a.err, 0x3c)) return false;
-          if (it >= 1 && !mbar_wait(o_free, (it - 1) & 1, abort_flag, a.err, 0x3f)) return false;
           tc_fence_after();
-          if (ns > 0) {
 #pragma unroll
-            for (int ks = 0; ks < kWP_D / 16; ++ks)
-              umma_f16_ss(tmem + kTmO, sdesc_kstep(aQ, kWP_M, ks), sdesc_kstep(bSK, kWP_SinkRows, ks), idesc_sk,
-                          ks > 0);
-          }
+          for (int ks = 0; ks < kWP_D / 16; ++ks)
+            umma_f16_ss(sb, sdesc_kstep(aQ, kWP_M, ks), sdesc_kstep(bSK, kWP_SinkRows, ks), idesc_sk, ks > 0);
           umma_commit(bar_sink);
+          return true;
+        };
+        // O is free once the previous item is drained; with sinks it starts as P_sink V_sink
+        auto sink_pv = [&]() -> bool {
+          if (it >= 1 && !mbar_wait(o_free, (it - 1) & 1, abort_flag, a.err, 0x3f)) return false;
+          if (ns == 0) return true;
+          if (!mbar_wait(psink, it & 1, abort_flag, a.err, 0x44)) return false;
+          tc_fence_after();
+          umma_f16_ts(tmem + kTmO, sb + 16, dSV, idesc_pv, 0u);
+          umma_commit(osink);
           return true;
         };
         auto issue_pv = [&](int jj, int tt) -> bool {
@@ -232,14 +257,17 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
 #pragma unroll
           for (int ks = 0; ks < kWP_N / 16; ++ks)
             umma_f16_ts(tmem + kTmO, tmem + s * kWP_N + p_col(ks), sdesc_kstep(bV, kWP_D, ks), idesc_pv,
-                        (jj | ks) > 0);
+                        (ns > 0 || (jj | ks) > 0) ? 1u : 0u);
           umma_commit(v_empty);
           if (jj == w.n - 1) umma_commit(o_fin);
           return true;
         };
-        if (w.n == 0) {
-          ok = sink_step();
-          if (ok) umma_commit(q_free);
+        if (w.n == 0) {   // no key tiles: O is P_sink V_sink (or zero); o_fin still marks the item once
+          ok = sink_scores() && sink_pv();
+          if (ok) {
+            umma_commit(q_free);
+            umma_commit(o_fin);
+          }
         }
         for (int j = 0; j < w.n && ok; ++j) {
           const int tt = t + j, s = tt & 1;
@@ -251,7 +279,7 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
             umma_f16_ss(tmem + s * kWP_N, sdesc_kstep(aQ, kWP_M, ks), sdesc_kstep(bK, kWP_N, ks), idesc_qk, ks > 0);
           umma_commit(k_empty);
           umma_commit(&s_full[s]);
-          if (j == 0) ok = sink_step();
+          if (j == 0) ok = sink_scores() && sink_pv();
           if (ok && j == w.n - 1) umma_commit(q_free);
           if (ok && j >= 1) ok = issue_pv(j - 1, tt - 1);
         }
@@ -277,14 +305,13 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
       return ok;
     };
     bool alive = true;
-    int it = 0, t = 0, nfin = 0;
+    int it = 0, t = 0;
     for (long long u = blockIdx.x; u < nitems && alive; u += gridDim.x, ++it) {
       const WItem w = win_item(a, u, ntq);
       const long long p = w.P0 + r;              // position of this query
-      float* sSV = sSVb + (it & 1) * (kWP_MaxSinks * kWP_D);
-      // sink keys -> K-major swizzled B operand (rows >= ns zero); sink values -> fp32.  The sink keys of the
-      // previous item were read by its sink product (finished: its scores were read); its sink values are in
-      // the other buffer
+      const uint32_t sbc = (uint32_t)((t + 1) & 1) * kWP_N;   // S buffer of the sink scores and P_sink
+      // sink keys -> K-major swizzled B operand (rows >= ns zero); sink values^T -> fp16 B operand (keys >= ns
+      // zero).  The previous item's sink products finished before its O was complete
       for (int i = st; i < kWP_SinkRows * (kWP_D / 8); i += 256) {
         const int e = i / (kWP_D / 8), c = i % (kWP_D / 8);
         uint4 v = make_uint4(0u, 0u, 0u, 0u);
@@ -293,40 +320,57 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
                                                    (size_t)e * a.sk_k) + c);
         *reinterpret_cast<uint4*>(sSK + (c >> 3) * (kWP_SinkRows * 128) + e * 128 + (((c & 7) ^ (e & 7)) << 4)) = v;
       }
-      for (int i = st; i < ns * (kWP_D / 8); i += 256) {
-        const int e = i / (kWP_D / 8), c = i % (kWP_D / 8);
-        const uint4 v = __ldg(reinterpret_cast<const uint4*>(a.sink_v + (size_t)w.b * a.sv_b + (size_t)w.g * a.sv_h +
-                                                             (size_t)e * a.sv_k) + c);
-        float4* d = reinterpret_cast<float4*>(sSV + e * kWP_D + c * 8);
-        d[0] = make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xffff0000u), __uint_as_float(v.y << 16),
-                           __uint_as_float(v.y & 0xffff0000u));
-        d[1] = make_float4(__uint_as_float(v.z << 16), __uint_as_float(v.z & 0xffff0000u), __uint_as_float(v.w << 16),
-                           __uint_as_float(v.w & 0xffff0000u));
+      if (ns > 0) {
+        const int d = st;   // one value column per thread, the 16 sink keys of it
+        uint32_t hv[8];
+#pragma unroll
+        for (int e2 = 0; e2 < 8; ++e2) {
+          float f0 = 0.f, f1 = 0.f;
+          if (2 * e2 < ns)
+            f0 = __bfloat162float(a.sink_v[(size_t)w.b * a.sv_b + (size_t)w.g * a.sv_h + (size_t)(2 * e2) * a.sv_k + d]);
+          if (2 * e2 + 1 < ns)
+            f1 = __bfloat162float(
+                a.sink_v[(size_t)w.b * a.sv_b + (size_t)w.g * a.sv_h + (size_t)(2 * e2 + 1) * a.sv_k + d]);
+          hv[e2] = pack_half2(f0, f1);
+        }
+        *reinterpret_cast<uint4*>(sSV + sv_off(d, 0)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+        *reinterpret_cast<uint4*>(sSV + sv_off(d, 8)) = make_uint4(hv[4], hv[5], hv[6], hv[7]);
       }
       fence_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_sk);
-      float se[kWP_MaxSinks];   // sink scores in the log2 domain (-inf: not visible from this row)
-#pragma unroll
-      for (int e = 0; e < kWP_MaxSinks; ++e) se[e] = -INFINITY;
-      if (!(alive = mbar_wait_warp(bar_sink, it & 1, abort_flag, a.err, 0x3a))) break;
-      tc_fence_after();
-      if (ns > 0) {
-        uint32_t sw[16];
-        tmem_ld16(trow + kTmO, sw);
-        tmem_wait_ld();
-#pragma unroll
-        for (int e = 0; e < kWP_MaxSinks; ++e)
-          se[e] = (e < ns && e <= p) ? __uint_as_float(sw[e]) * c2 : -INFINITY;
-      }
-      // every softmax warp has read the sink scores before any P of this item is published (the first
-      // product overwrites O's columns)
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(ssync);
-      if (!(alive = mbar_wait_warp(ssync, it & 1, abort_flag, a.err, 0x44))) break;
-
+      // sinks start the online softmax: m_ref = the row's largest visible sink score, l (half 0) = the sum of
+      // their weights, O = P_sink V_sink; half 0 stages P_sink beside the scores it read them from
       float m_ref = -INFINITY, l = 0.f;            // running max (log2 domain) and this half's sum
+      if (ns > 0) {
+        if (!(alive = mbar_wait_warp(bar_sink, it & 1, abort_flag, a.err, 0x3a))) break;
+        tc_fence_after();
+        uint32_t sw[16];
+        tmem_ld16(trow + sbc, sw);
+        tmem_wait_ld();
+        float se[kWP_SinkRows];
+#pragma unroll
+        for (int e = 0; e < kWP_SinkRows; ++e) {
+          se[e] = (e < ns && e <= p) ? __uint_as_float(sw[e]) * c2 : -INFINITY;
+          m_ref = fmaxf(m_ref, se[e]);
+        }
+        if (hh == 0) {
+          uint32_t pk8[8];
+#pragma unroll
+          for (int e = 0; e < kWP_SinkRows; e += 2) {
+            const float w0 = (se[e] == -INFINITY) ? 0.f : ex2_approx(se[e] - m_ref);
+            const float w1 = (se[e + 1] == -INFINITY) ? 0.f : ex2_approx(se[e + 1] - m_ref);
+            l += w0 + w1;
+            pk8[e / 2] = cvt_half2(w0, w1);
+          }
+          tmem_st8(trow + sbc + 16, pk8);
+          tmem_wait_st();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(psink);
+      }
+
       for (int j = 0; j < w.n && alive; ++j) {
         const int tt = t + j, s = tt & 1;
         if (!mbar_wait_warp(&s_full[s], (tt >> 1) & 1, abort_flag, a.err, 0x3b)) { alive = false; break; }
@@ -395,7 +439,9 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
         // O rescale (warp-collective): after O += P_{t-1} V_{t-1} has finished (O += P_{t-2} V_{t-2} was
         // issued before S_t, so this parity wait cannot pass early)
         if (__any_sync(0xffffffffu, rescale)) {
-          if (j >= 1 && !mbar_wait_warp(v_empty, (tt - 1) & 1, abort_flag, a.err, 0x3e)) {
+          // O += P_{t-1} V_{t-1} (or, at the item's first tile, O = P_sink V_sink) has finished
+          if (j >= 1 ? !mbar_wait_warp(v_empty, (tt - 1) & 1, abort_flag, a.err, 0x3e)
+                     : (ns > 0 && !mbar_wait_warp(osink, it & 1, abort_flag, a.err, 0x45))) {
             alive = false;
             break;
           }
@@ -420,27 +466,14 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
       if (!alive) break;
       t += w.n;
       // ---------------------------------------------------------------- epilogue
-      if (w.n > 0) {
-        if (!(alive = mbar_wait_warp(o_fin, nfin & 1, abort_flag, a.err, 0x3d))) break;
-        ++nfin;
-      }
+      const bool has_o = w.n > 0 || ns > 0;
+      if (!(alive = mbar_wait_warp(o_fin, it & 1, abort_flag, a.err, 0x3d))) break;
       tc_fence_after();
       xch[512 + hh * 128 + r] = l;
       if (!(alive = pair_sync(0x43))) break;
       l += xch[512 + (1 - hh) * 128 + r];
-      float mf = m_ref;
-#pragma unroll
-      for (int e = 0; e < kWP_MaxSinks; ++e) mf = fmaxf(mf, se[e]);
-      const float fo = (m_ref == -INFINITY) ? 0.f : ex2_approx(m_ref - mf);
-      float lf = l * fo;
-      float we[kWP_MaxSinks];
-#pragma unroll
-      for (int e = 0; e < kWP_MaxSinks; ++e) {
-        we[e] = (se[e] == -INFINITY) ? 0.f : ex2_approx(se[e] - mf);
-        lf += we[e];
-      }
-      const float inv = lf > 0.f ? 1.f / lf : 0.f;
-      const float lse = lf > 0.f ? (mf + log2f(lf)) * kLn2 : -INFINITY;
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const float lse = l > 0.f ? (m_ref + log2f(l)) * kLn2 : -INFINITY;
       const int qi = w.i0 + r;
       if (qi < a.Tq && a.lse && hh == 0) a.lse[((size_t)w.b * a.H + w.h) * a.Tq + qi] = lse;
       // rows that the memory reads mix go to the workspace tile in their load order
@@ -452,7 +485,7 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
       for (int c4 = 0; c4 < 4; ++c4) {
         const int c = hh * 128 + c4 * 32;
         uint32_t ow[32];
-        if (w.n > 0) {
+        if (has_o) {
           tmem_ld32(trow + kTmO + c, ow);
           tmem_wait_ld();
         } else {
@@ -461,21 +494,7 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
         }
         float ov[32];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) ov[e] = __uint_as_float(ow[e]) * fo;
-#pragma unroll
-        for (int e2 = 0; e2 < kWP_MaxSinks; ++e2) {
-          if (e2 < ns) {   // (uniform: we[e2] is 0 where the sink is not visible)
-            const float4* vw = reinterpret_cast<const float4*>(sSV + e2 * kWP_D + c);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const float4 vv = vw[e];
-              ov[4 * e] = fmaf(we[e2], vv.x, ov[4 * e]);
-              ov[4 * e + 1] = fmaf(we[e2], vv.y, ov[4 * e + 1]);
-              ov[4 * e + 2] = fmaf(we[e2], vv.z, ov[4 * e + 2]);
-              ov[4 * e + 3] = fmaf(we[e2], vv.w, ov[4 * e + 3]);
-            }
-          }
-        }
+        for (int e = 0; e < 32; ++e) ov[e] = __uint_as_float(ow[e]);
         if (perm_dst) {
           // 8-column group e8 of column block cb = c4 / 2 as fp16: [half][cb][row group][e8][row in group][8],
           // 512 contiguous bytes per warp store
