@@ -192,19 +192,16 @@ __global__ void __launch_bounds__(kP1_Threads, 1) gdn_p1_kernel(GdnStreams s) {
       s_vp32[r] = src.zero ? g_zero_row : src.v32;
     }
     __half* kwrow = s.kw + (rowbase + r) * kGD + hh * 128;
-#pragma unroll 4
-    for (int ch = 0; ch < 16; ++ch) {  // 16 chunks of 8 elements = 128 columns
-      float x[8];
-      if (src.zero) {
+    // all 32 loads of this thread's half row in flight at once (invalid steps read the zero row)
+    const float* kp = src.zero ? g_zero_row : src.k;
+    float4 kx[32];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) x[e] = 0.f;
-      } else {
-        const float4 a0 = *reinterpret_cast<const float4*>(src.k + hh * 128 + ch * 8);
-        const float4 a1 = *reinterpret_cast<const float4*>(src.k + hh * 128 + ch * 8 + 4);
-        x[0] = a0.x; x[1] = a0.y; x[2] = a0.z; x[3] = a0.w; x[4] = a1.x; x[5] = a1.y; x[6] = a1.z; x[7] = a1.w;
-      }
-      const uint4 pk = make_uint4(pack_half2(x[0], x[1]), pack_half2(x[2], x[3]), pack_half2(x[4], x[5]),
-                                  pack_half2(x[6], x[7]));
+    for (int i = 0; i < 32; ++i) kx[i] = *reinterpret_cast<const float4*>(kp + hh * 128 + i * 4);
+#pragma unroll
+    for (int ch = 0; ch < 16; ++ch) {  // 16 chunks of 8 elements = 128 columns
+      const float4 a0 = kx[2 * ch], a1 = kx[2 * ch + 1];
+      const uint4 pk = make_uint4(pack_half2(a0.x, a0.y), pack_half2(a0.z, a0.w), pack_half2(a1.x, a1.y),
+                                  pack_half2(a1.z, a1.w));
       const int col = hh * 128 + ch * 8;
       *reinterpret_cast<uint4*>(reg0 + (col >> 6) * (128 * 128) + sw128_offset(r, col & 63)) = pk;
       *reinterpret_cast<uint4*>(kwrow + ch * 8) = pk;
@@ -239,16 +236,18 @@ __global__ void __launch_bounds__(kP1_Threads, 1) gdn_p1_kernel(GdnStreams s) {
     s_bec[t] = s_beta[t] * __expf(s_gc[t]);
     s_ect[t] = __expf(gamma_last - s_gc[t]);
   }
-  // ---- (b) A = strict_lower(beta_i e^{c_i - c_j} (k_i . k_j)) from TMEM (warps 0-3, row = lane)
+  // ---- (b) A = strict_lower(beta_i e^{c_i - c_j} (k_i . k_j)) from TMEM (all warps: row = lane quarter of
+  //      the warp, columns 64 * (warp / 4) .. + 63)
   bool alive = true;
-  if (warp < 4) {
-    const int r = t;
+  {
+    const int r = (warp & 3) * 32 + lane;
+    const int cbase = (warp >> 2) * 64;
     alive = mbar_wait_warp(bar_kk, 0, nullptr, s.err, 0x41);
     tc_fence_after();
-    const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+    const uint32_t trow = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     const float br = s_beta[r], cr = s_gc[r];
 #pragma unroll 1
-    for (int c0 = 0; c0 < 128; c0 += 16) {
+    for (int c0 = cbase; c0 < cbase + 64; c0 += 16) {
       float f[16];
       tmem_ld16_wait(trow + c0, f);
 #pragma unroll
@@ -297,20 +296,20 @@ __global__ void __launch_bounds__(kP1_Threads, 1) gdn_p1_kernel(GdnStreams s) {
     __half* ktT = s.ktT + ((size_t)bg * s.n_chunks + c) * kGD * kGC + (size_t)d * kGC;
     const bool v32 = s.v32 != nullptr;   // uniform for the launch
 #pragma unroll 1
-    for (int rb = 0; rb < kGC; rb += 32) {
-      // 64 independent, unconditional loads in flight per thread (32 tokens x {k, v}), then pack and store
-      float kv[32], vv[32];
+    for (int rb = 0; rb < kGC; rb += 64) {
+      // 128 independent, unconditional loads in flight per thread (64 tokens x {k, v}), then pack and store
+      float kv[64], vv[64];
 #pragma unroll
-      for (int e = 0; e < 32; ++e) kv[e] = s_kp[rb + e][d];
+      for (int e = 0; e < 64; ++e) kv[e] = s_kp[rb + e][d];
       if (v32) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) vv[e] = s_vp32[rb + e][d];
+        for (int e = 0; e < 64; ++e) vv[e] = s_vp32[rb + e][d];
       } else {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) vv[e] = __bfloat162float(s_vp[rb + e][d]);
+        for (int e = 0; e < 64; ++e) vv[e] = __bfloat162float(s_vp[rb + e][d]);
       }
 #pragma unroll
-      for (int q = 0; q < 32; q += 8) {
+      for (int q = 0; q < 64; q += 8) {
         const int r0 = rb + q;
         uint32_t pv[4], pk[4], pt[4];
 #pragma unroll
@@ -342,26 +341,21 @@ __global__ void __launch_bounds__(kP1_Threads, 1) gdn_p1_kernel(GdnStreams s) {
       umma_f16_ss(tmem + 256, sdesc_kstep(aT, 128, ks), sdesc_kstep(bK, 256, ks), idesc, ks > 0);
     umma_commit(bar_uw);
   }
-  // ---- (e) u, w rows -> fp16 global (warps 0-3)
-  if (warp < 4) {
-    const int r = t;
+  // ---- (e) u rows (warps 0-3) and w rows (warps 4-7) -> fp16 global
+  {
+    const int r = (warp & 3) * 32 + lane;
+    const bool is_w = warp >= 4;
     alive = mbar_wait_warp(bar_uw, 0, nullptr, s.err, 0x42) && alive;
     tc_fence_after();
-    const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
-    __half* urow = s.u + (rowbase + r) * kGD;
-    __half* wrow = s.w + (rowbase + r) * kGD;
+    const uint32_t trow = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (is_w ? 256u : 0u);
+    __half* orow = (is_w ? s.w : s.u) + (rowbase + r) * kGD;
 #pragma unroll 1
     for (int c0 = 0; c0 < 256; c0 += 16) {
       float f[16];
       tmem_ld16_wait(trow + c0, f);
-      uint4* up = reinterpret_cast<uint4*>(urow + c0);
-      up[0] = make_uint4(pack_half2(f[0], f[1]), pack_half2(f[2], f[3]), pack_half2(f[4], f[5]), pack_half2(f[6], f[7]));
-      up[1] = make_uint4(pack_half2(f[8], f[9]), pack_half2(f[10], f[11]), pack_half2(f[12], f[13]),
-                         pack_half2(f[14], f[15]));
-      tmem_ld16_wait(trow + 256 + c0, f);
-      uint4* wp = reinterpret_cast<uint4*>(wrow + c0);
-      wp[0] = make_uint4(pack_half2(f[0], f[1]), pack_half2(f[2], f[3]), pack_half2(f[4], f[5]), pack_half2(f[6], f[7]));
-      wp[1] = make_uint4(pack_half2(f[8], f[9]), pack_half2(f[10], f[11]), pack_half2(f[12], f[13]),
+      uint4* op = reinterpret_cast<uint4*>(orow + c0);
+      op[0] = make_uint4(pack_half2(f[0], f[1]), pack_half2(f[2], f[3]), pack_half2(f[4], f[5]), pack_half2(f[6], f[7]));
+      op[1] = make_uint4(pack_half2(f[8], f[9]), pack_half2(f[10], f[11]), pack_half2(f[12], f[13]),
                          pack_half2(f[14], f[15]));
     }
   }
