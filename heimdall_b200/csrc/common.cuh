@@ -103,6 +103,27 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, v
 }
 
 // ----------------------------------------------------------------------------------------------
+// packed fp32 pairs (fma.rn.f32x2 updates two values per instruction); the low word is the first value
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t dup2(uint32_t x) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %1};" : "=l"(d) : "r"(x));
+  return d;
+}
+__device__ __forceinline__ uint64_t pair2(float lo, float hi) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "r"(__float_as_uint(lo)), "r"(__float_as_uint(hi)));
+  return d;
+}
+__device__ __forceinline__ float lo_hi(uint64_t x, int hi) {
+  return __uint_as_float(hi ? (uint32_t)(x >> 32) : (uint32_t)x);
+}
+
+// ----------------------------------------------------------------------------------------------
 // proxy fences: make generic-proxy shared-memory writes visible to the async proxy (TMA, tcgen05)
 __device__ __forceinline__ void fence_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

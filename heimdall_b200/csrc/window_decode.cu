@@ -47,20 +47,6 @@ __device__ __forceinline__ void bf16x8_to_f32(const uint4& u, float (&f)[8]) {
 // layout the combine kernel reads.  Slot j is a window key for the token at position p when its ring
 // position kp satisfies p - W < kp < p, kp >= S and j == kp mod W (the token at p - W leaves the window at
 // this step; the new token and the sinks are added by the combine kernel).
-// packed fp32 pair helpers (fma.rn.f32x2 updates two accumulators per instruction)
-__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
-__device__ __forceinline__ uint64_t dup2(uint32_t x) {
-  uint64_t d;
-  asm("mov.b64 %0, {%1, %1};" : "=l"(d) : "r"(x));
-  return d;
-}
-__device__ __forceinline__ float lo_hi(uint64_t x, int hi) {
-  return __uint_as_float(hi ? (uint32_t)(x >> 32) : (uint32_t)x);
-}
 
 constexpr int kWT_N = 128;                        // ring slots per tile
 constexpr int kWT_TilesPerItem = kWD_Keys / kWT_N;
