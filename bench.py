@@ -528,8 +528,11 @@ def dist_setup():
     if world > 1:
         import datetime
         torch.cuda.set_device(local)
+        # the sequence-parallel exchange runs beside the window kernel's queued CTAs: a high-priority NCCL
+        # stream gets its CTAs dispatched first
+        opts = torch.distributed.ProcessGroupNCCL.Options(is_high_priority_stream=True)
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                             device_id=torch.device("cuda", local))
+                                             device_id=torch.device("cuda", local), pg_options=opts)
     return {"world": world, "rank": rank, "local": local}
 
 

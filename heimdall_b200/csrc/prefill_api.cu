@@ -288,10 +288,24 @@ static int layer_prefill_impl(const bf_layer* L, const void* x, const void* q, c
   // and the memory chain (steps 1-2) run on two side streams forked here and joined before the reads mix
   // into o.  The chain's stream has the greater priority, so its CTAs (the sequential scan among them, which
   // fills only part of the GPU) are dispatched first and the window's CTAs fill the remaining SMs.
-  const bool will_read = use_mem && phase != kPhaseBegin && (ring_case ? T : T - W) > 0;
+  // Sequence-parallel phases: the window is launched in the first phase and left running on its side stream
+  // (it overlaps the state-map scan and the caller's exchange of the maps); the second phase joins it before
+  // the reads.  The buffers it uses are the caller's inputs, output and workspace, held until that phase.
+  const bool reads_later = use_mem && (ring_case ? T : T - W) > 0;
+  const bool will_read = reads_later && phase != kPhaseFinish;   // fork the window and the chain here
+  const bool win_here = phase == kPhaseAll || (phase == kPhaseBegin) == reads_later;
   cudaStream_t ws2 = stream;   // (a null handle is the legacy default stream, a valid stream)
   cudaStream_t wsm = stream;   // the memory chain
   cudaEvent_t ev_fork = nullptr, ev_win = nullptr, ev_mem = nullptr;
+  if (reads_later && phase == kPhaseFinish) {
+    // the scan from the incoming state goes on the high-priority stream too, ahead of the window's CTAs
+    // still waiting for SMs; it is joined before the reads
+    wsm = side_stream(st, 1);
+    if (!wsm || cudaEventCreateWithFlags(&ev_fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ev_mem, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventRecord(ev_fork, stream) != cudaSuccess || cudaStreamWaitEvent(wsm, ev_fork, 0) != cudaSuccess)
+      return cuda_fail();
+  }
   if (will_read) {
     ws2 = side_stream(st, 0);
     wsm = side_stream(st, 1);
@@ -342,7 +356,7 @@ static int layer_prefill_impl(const bf_layer* L, const void* x, const void* q, c
     if (s.n_steps > 0) {
       gdn_prefill_carve(s, gws);
       // the window writes the rows the reads cover in tile order when its query tiles line up with the chunks
-      if (s.qoff % kGC == 0 && phase != kPhaseBegin) {
+      if (s.qoff % kGC == 0 && reads_later) {
         s.owin = reinterpret_cast<__half*>(static_cast<uint8_t*>(gws) + al1k(gdn_prefill_workspace(B, G, s.n_steps, false)));
       }
       reads = phase != kPhaseBegin;
@@ -357,9 +371,32 @@ static int layer_prefill_impl(const bf_layer* L, const void* x, const void* q, c
     identity_maps_kernel<<<grid_for((size_t)B * G * D * D), 256, 0, stream>>>(m_out, n_out, B * G, D);
     if (int e_ = launch_status()) return e_;
   }
-  if (phase == kPhaseBegin) return BF_OK;
+  if (phase == kPhaseBegin && will_read) {   // the maps are complete when this call returns, the window not
+    if (cudaEventRecord(ev_mem, wsm) != cudaSuccess || cudaStreamWaitEvent(stream, ev_mem, 0) != cudaSuccess)
+      return cuda_fail();
+  }
+  if (!win_here) {
+    if (phase == kPhaseFinish && reads_later) {   // join the scan and the window launched by the first phase
+      cudaStream_t wsw = side_stream(st, 0);
+      if (!wsw || cudaEventCreateWithFlags(&ev_win, cudaEventDisableTiming) != cudaSuccess ||
+          cudaEventRecord(ev_win, wsw) != cudaSuccess || cudaStreamWaitEvent(stream, ev_win, 0) != cudaSuccess ||
+          cudaEventRecord(ev_mem, wsm) != cudaSuccess || cudaStreamWaitEvent(stream, ev_mem, 0) != cudaSuccess)
+        return cuda_fail();
+      cudaEventDestroy(ev_win);
+      cudaEventDestroy(ev_mem);
+      cudaEventDestroy(ev_fork);
+      ev_win = ev_mem = ev_fork = nullptr;
+    }
+    if (phase == kPhaseBegin) {
+      if (ev_fork) cudaEventDestroy(ev_fork);
+      if (ev_win) cudaEventDestroy(ev_win);
+      if (ev_mem) cudaEventDestroy(ev_mem);
+      return BF_OK;
+    }
+  }
   // 3. window attention over the extended keys (o = window result, lse), on the side stream when forked
   const void* kx = kr;
+  if (win_here) {
   stage_mark(ST_WIN_PREP, 0, ws2);
   if (ring_case) {
     rc = launch_kext_prep(static_cast<const __nv_bfloat16*>(kr), static_cast<const __nv_bfloat16*>(C->ring_k), W,
@@ -374,10 +411,17 @@ static int layer_prefill_impl(const bf_layer* L, const void* x, const void* q, c
   stage_mark(ST_WIN_PREP, 1, ws2);
   stage_mark(ST_WIN, 0, ws2);
   rc = window_common(qr, kx, vt, sink_k, sink_v, ns, start, ring_case ? start - W : start, L->sinks, B, H, G, T, Tk, W,
-                     o, lse_w, st.err, ws2, reads ? const_cast<__half*>(s.owin) : nullptr, s.qoff / kGC, s.n_chunks,
-                     will_read ? 0 : 1);
+                     o, lse_w, st.err, ws2, reads_later ? const_cast<__half*>(s.owin) : nullptr, s.qoff / kGC,
+                     s.n_chunks, will_read ? 0 : 1);
   if (rc) return rc;
   stage_mark(ST_WIN, 1, ws2);
+  }
+  if (phase == kPhaseBegin) {   // the window stays on its stream until the second phase
+    cudaEventDestroy(ev_fork);
+    cudaEventDestroy(ev_win);
+    cudaEventDestroy(ev_mem);
+    return BF_OK;
+  }
   if (will_read) {
     if (cudaEventRecord(ev_win, ws2) != cudaSuccess || cudaEventRecord(ev_mem, wsm) != cudaSuccess ||
         cudaStreamWaitEvent(stream, ev_win, 0) != cudaSuccess || cudaStreamWaitEvent(stream, ev_mem, 0) != cudaSuccess)

@@ -18,7 +18,11 @@ prefill from such a cache is exactly the continuation of the sequence (the refer
 property, tests/test_hibrit.py:78-90), so the outputs equal one pass over the whole sequence.  The
 prefill runs in two phases on one workspace (``BifrostLayer.prefill_sp_begin`` / ``prefill_sp_finish``):
 the first computes the memory inputs, the per-chunk products and the state map, the second everything
-that depends on the incoming state, so nothing is computed twice.
+that depends on the incoming state, so nothing is computed twice.  The window attention depends on no state:
+the first phase launches it on a low-priority side stream and returns while it runs, so that it fills the SMs
+the two sequential scans leave free; the second phase joins it before the memory reads.  The rest of the call
+runs on a high-priority stream, and the exchange should run on a high-priority NCCL stream too (a process group made with
+``ProcessGroupNCCL.Options(is_high_priority_stream=True)``), or its kernels wait behind the window's CTAs.
 
 Traffic per rank and layer: the halo (W tokens of x, k, v, kr: 33 MB at W = 2048, d = 5120) from the left
 neighbour, the sink rows from rank 0, and an all-gather of (M, N) (2 MB per rank at G = 4, D = 256).
@@ -95,12 +99,40 @@ def student_sp(L, x, q, k, v, qr, kr, group=None, memory: bool = True):
     this rank's GPU).  Returns (o, cache): this rank's outputs [B,T,H,D] fp32 and its cache after the call
     (on the last rank that is the cache of the whole sequence).  Every rank must call it (collectives).
     """
+    T = x.shape[1]
+    if T < L.window or T < L.sinks:
+        raise NotImplementedError("sequence parallelism needs at least one window (and the sinks) per rank")
+    # The call runs on a high-priority stream: the window kernel, launched by the first phase on the
+    # lowest-priority stream and left running, then yields the SMs to everything else of the call (the
+    # exchange, the fold of the maps, the second scan) instead of holding them back until it ends.
+    if x.device.type != "cuda":   # the host logic on CPU tensors (a CPU restatement of the layer)
+        return _student_sp(L, x, q, k, v, qr, kr, group, memory)
+    cur = torch.cuda.current_stream(x.device)
+    hp = _priority_stream(x.device)
+    hp.wait_stream(cur)
+    with torch.cuda.stream(hp):
+        o, cache = _student_sp(L, x, q, k, v, qr, kr, group, memory)
+    cur.wait_stream(hp)   # later work on the caller's stream (reuse of the inputs' memory included) waits
+    for t in [o, *(z for z in cache.values() if isinstance(z, torch.Tensor))]:
+        t.record_stream(cur)   # allocated on the priority stream, used on the caller's
+    return o, cache
+
+
+_PRIORITY_STREAMS = {}
+
+
+def _priority_stream(device):
+    key = torch.device(device).index
+    if key not in _PRIORITY_STREAMS:
+        _PRIORITY_STREAMS[key] = torch.cuda.Stream(device=device, priority=-5)   # clamped to the greatest
+    return _PRIORITY_STREAMS[key]
+
+
+def _student_sp(L, x, q, k, v, qr, kr, group, memory):
     rank = dist.get_rank(group)
     world = dist.get_world_size(group)
     B, T = x.shape[:2]
     W, S = L.window, L.sinks
-    if T < W or T < S:
-        raise NotImplementedError("sequence parallelism needs at least one window (and the sinks) per rank")
     start = rank * T
     bf = torch.bfloat16
     x, q, k, v, qr, kr = (z.to(bf).contiguous() for z in (x, q, k, v, qr, kr))
