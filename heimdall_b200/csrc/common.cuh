@@ -173,6 +173,10 @@ __device__ __forceinline__ void tma_store_4d(const void* tmap, const void* src, 
       "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
 }
+__device__ __forceinline__ void tma_store_3d(const void* tmap, const void* src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2) : "memory");
+}
 __device__ __forceinline__ void tma_store_2d(const void* tmap, const void* src, int c0, int c1) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
                    reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(src)), "r"(c0), "r"(c1) : "memory");
@@ -310,6 +314,16 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t smem_addr) {
   d |= (uint64_t)(1024 >> 4) << 32;              // stride byte offset: 8 rows x 128 B
   d |= (uint64_t)1 << 46;                        // descriptor version (sm_100)
   d |= (uint64_t)2 << 61;                        // SWIZZLE_128B
+  return d;
+}
+// K-major tile without swizzle: 8-row x 16-byte core matrices of 128 contiguous bytes, `lbo` bytes between
+// core matrices adjacent in K and `sbo` bytes between adjacent 8-row groups
+__device__ __forceinline__ uint64_t sdesc_nosw(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr & 0x3FFFFu) >> 4);  // start address
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;   // leading byte offset
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;   // stride byte offset
+  d |= (uint64_t)1 << 46;                        // descriptor version (sm_100); swizzle mode 0 (none)
   return d;
 }
 // descriptor for k-step `ks` (16 elements of 16 bits) of a K-major SW128 tile with `rows` rows

@@ -97,7 +97,8 @@ constexpr int kAS = 132;                    // row stride (floats) of A and T in
 __device__ __align__(16) float g_zero_row[kGD];
 
 // O = (NEG ? -1 : 1) * L R for M x M blocks of row-major fp32 matrices in shared memory (leading dims in
-// floats, multiples of 4), block b of nb; thread tile TR x TC, the reduction read four columns of L at a time.
+// floats, multiples of 4; block origins 16-byte aligned), block b of nb; thread tile TR x TC, the reduction
+// reads four columns of L and TC-wide rows of R at a time.
 template <int M, int TR, int TC, bool NEG>
 __device__ __forceinline__ void block_mm(const float* L, int ldl, const float* R, int ldr, float* O, int ldo,
                                          int tt) {
@@ -117,8 +118,16 @@ __device__ __forceinline__ void block_mm(const float* L, int ldl, const float* R
 #pragma unroll
     for (int jj = 0; jj < 4; ++jj) {
       float bv[TC];
+      if constexpr (TC == 4) {
+        const float4 r4 = *reinterpret_cast<const float4*>(R + (j + jj) * ldr + c0);
+        bv[0] = r4.x; bv[1] = r4.y; bv[2] = r4.z; bv[3] = r4.w;
+      } else if constexpr (TC == 2) {
+        const float2 r2 = *reinterpret_cast<const float2*>(R + (j + jj) * ldr + c0);
+        bv[0] = r2.x; bv[1] = r2.y;
+      } else {
 #pragma unroll
-      for (int b = 0; b < TC; ++b) bv[b] = R[(j + jj) * ldr + c0 + b];
+        for (int b = 0; b < TC; ++b) bv[b] = R[(j + jj) * ldr + c0 + b];
+      }
 #pragma unroll
       for (int a = 0; a < TR; ++a) {
         const float x = jj == 0 ? av[a].x : jj == 1 ? av[a].y : jj == 2 ? av[a].z : av[a].w;
@@ -147,7 +156,11 @@ __device__ __forceinline__ void inverse_doubling_level(const float* A, float* Tm
   __syncthreads();
 }
 
-__global__ void __launch_bounds__(kP1_Threads, 1) gdn_p1_kernel(GdnStreams s) {
+// The fp16 keys, u and w leave through TMA stores of their K-major SW128 tiles (kwmap / umap / wmap: 3-D maps
+// (64, rows, 4 atoms) over [B*G*n_pad][256], one 128-row box per chunk).
+__global__ void __launch_bounds__(kP1_Threads, 1)
+    gdn_p1_kernel(const __grid_constant__ CUtensorMap kwmap, const __grid_constant__ CUtensorMap umap,
+                  const __grid_constant__ CUtensorMap wmap, GdnStreams s) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* reg0 = smem + kP1_Reg0;
@@ -180,7 +193,7 @@ __global__ void __launch_bounds__(kP1_Threads, 1) gdn_p1_kernel(GdnStreams s) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
-  // ---- (a) key rows -> fp16 K tile (SW128, 4 atoms) and the fp16 write keys in global memory
+  // ---- (a) key rows -> fp16 K tile (SW128, 4 atoms), which is also the chunk's tile of fp16 write keys
   {
     const int r = t >> 1, hh = t & 1;
     const RowSrc src = write_row(s, b, gg, c * kGC + r);
@@ -191,7 +204,6 @@ __global__ void __launch_bounds__(kP1_Threads, 1) gdn_p1_kernel(GdnStreams s) {
       s_vp[r] = src.zero ? reinterpret_cast<const __nv_bfloat16*>(g_zero_row) : src.v;
       s_vp32[r] = src.zero ? g_zero_row : src.v32;
     }
-    __half* kwrow = s.kw + (rowbase + r) * kGD + hh * 128;
     // all 32 loads of this thread's half row in flight at once (invalid steps read the zero row)
     const float* kp = src.zero ? g_zero_row : src.k;
     float4 kx[32];
@@ -204,7 +216,6 @@ __global__ void __launch_bounds__(kP1_Threads, 1) gdn_p1_kernel(GdnStreams s) {
                                   pack_half2(a1.z, a1.w));
       const int col = hh * 128 + ch * 8;
       *reinterpret_cast<uint4*>(reg0 + (col >> 6) * (128 * 128) + sw128_offset(r, col & 63)) = pk;
-      *reinterpret_cast<uint4*>(kwrow + ch * 8) = pk;
     }
   }
   fence_async_smem();
@@ -213,6 +224,10 @@ __global__ void __launch_bounds__(kP1_Threads, 1) gdn_p1_kernel(GdnStreams s) {
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   if (t == 0) {
+    tma_prefetch(&umap);
+    tma_prefetch(&wmap);
+    tma_store_3d(&kwmap, reg0, 0, (int)rowbase, 0);   // the write keys (fp16)
+    tma_store_commit();
     const uint32_t aK = smem_u32(reg0);
     constexpr uint32_t idesc = idesc_f16(128, 128, 0);
 #pragma unroll
@@ -220,12 +235,24 @@ __global__ void __launch_bounds__(kP1_Threads, 1) gdn_p1_kernel(GdnStreams s) {
       umma_f16_ss(tmem, sdesc_kstep(aK, 128, ks), sdesc_kstep(aK, 128, ks), idesc, ks > 0);
     umma_commit(bar_kk);
   }
-  // cumulative decay inside the chunk (thread r < 128)
+  // cumulative decay inside the chunk (thread r < 128): inclusive scans of the four warps, then the totals of
+  // the warps before
+  float* s_wsum = reinterpret_cast<float*>(smem + kP1_Small + 1600);   // [4], after the barriers
+  float gacc = 0.f;
   if (t < 128) {
-    float acc = 0.f;
-    for (int j = 0; j <= t; ++j) acc += s_g[j];
-    s_gc[t] = acc;
-    s.gc[rowbase + t] = acc;
+    gacc = s_g[t];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, gacc, o);
+      if (lane >= o) gacc += y;
+    }
+    if (lane == 31) s_wsum[warp] = gacc;
+  }
+  __syncthreads();
+  if (t < 128) {
+    for (int w2 = 0; w2 < warp; ++w2) gacc += s_wsum[w2];
+    s_gc[t] = gacc;
+    s.gc[rowbase + t] = gacc;
   }
   __syncthreads();
   const float gamma_last = s_gc[127];
@@ -253,24 +280,41 @@ __global__ void __launch_bounds__(kP1_Threads, 1) gdn_p1_kernel(GdnStreams s) {
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
         const int j = c0 + e;
-        A[r * kAS + j] = (j < r && alive) ? br * __expf(cr - s_gc[j]) * f[e] : 0.f;
+        f[e] = (j < r && alive) ? br * __expf(cr - s_gc[j]) * f[e] : 0.f;
       }
+#pragma unroll
+      for (int e = 0; e < 16; e += 4)   // rows 528 bytes apart: the 16-byte stores of 8 lanes hit 8 bank groups
+        *reinterpret_cast<float4*>(A + r * kAS + c0 + e) = make_float4(f[e], f[e + 1], f[e + 2], f[e + 3]);
     }
   }
+  if (t == 0) tma_store_wait_read();   // the key tile has been read out
   tc_fence_before();
-  __syncthreads();  // A complete; the K tile (reg0) is free (K K^T finished)
+  __syncthreads();  // A complete; the K tile (reg0) is free (K K^T finished, keys stored)
   // ---- (c) T = (I + A)^-1: invert the eight 16x16 diagonal blocks (one column chain per thread), then
   //      double the solved block size 16 -> 32 -> 64 -> 128 with T21 = -T22 (A21 T11)
   for (int i = t; i < 128 * kAS; i += kP1_Threads) Tm[i] = 0.f;
   __syncthreads();
   if (t < 128) {
-    const int r0 = (t >> 4) * 16, col = r0 + (t & 15);
-    Tm[col * kAS + col] = 1.f;
-    for (int i = col + 1; i < r0 + 16; ++i) {
+    // column cl of the inverse of diagonal block r0: x_m = -sum_{j<m} A[m][j] x_j below the unit diagonal;
+    // the entries above it are zero, so the sums run over all j < m (rows of A read four at a time)
+    const int r0 = (t >> 4) * 16, cl = t & 15;
+    float x[16];
+#pragma unroll
+    for (int m = 0; m < 16; ++m) {
       float acc = 0.f;
-      for (int j = col; j < i; ++j) acc += A[i * kAS + j] * Tm[j * kAS + col];
-      Tm[i * kAS + col] = -acc;
+      const float* ar = A + (r0 + m) * kAS + r0;
+#pragma unroll
+      for (int j4 = 0; j4 < m; j4 += 4) {
+        const float4 a4 = *reinterpret_cast<const float4*>(ar + j4);
+        acc = fmaf(a4.x, x[j4], acc);
+        if (j4 + 1 < m) acc = fmaf(a4.y, x[j4 + 1], acc);
+        if (j4 + 2 < m) acc = fmaf(a4.z, x[j4 + 2], acc);
+        if (j4 + 3 < m) acc = fmaf(a4.w, x[j4 + 3], acc);
+      }
+      x[m] = m < cl ? 0.f : m == cl ? 1.f : -acc;
     }
+#pragma unroll
+    for (int m = 0; m < 16; ++m) Tm[(r0 + m) * kAS + r0 + cl] = x[m];
   }
   __syncthreads();
   // (T stays zero above its diagonal and T11, T22 are lower triangular, so both products are plain block
@@ -293,7 +337,9 @@ __global__ void __launch_bounds__(kP1_Threads, 1) gdn_p1_kernel(GdnStreams s) {
   //      16-byte chunks of 8 tokens, so shared and global stores are vector-wide and loads coalesce over t.
   {
     const int d = t;
-    __half* ktT = s.ktT + ((size_t)bg * s.n_chunks + c) * kGD * kGC + (size_t)d * kGC;
+    // k_tail^T in core-matrix order [token group of 8][dimension][8 tokens]: the stores of a warp are 512
+    // contiguous bytes, and the tile is P2's operand as it lies in memory
+    __half* ktT = s.ktT + ((size_t)bg * s.n_chunks + c) * kGD * kGC + (size_t)d * 8;
     const bool v32 = s.v32 != nullptr;   // uniform for the launch
 #pragma unroll 1
     for (int rb = 0; rb < kGC; rb += 64) {
@@ -322,7 +368,7 @@ __global__ void __launch_bounds__(kP1_Threads, 1) gdn_p1_kernel(GdnStreams s) {
         const uint32_t off = (uint32_t)(r0 >> 6) * (256 * 128) + sw128_offset(d, r0 & 63);
         *reinterpret_cast<uint4*>(reg0 + off) = make_uint4(pv[0], pv[1], pv[2], pv[3]);
         *reinterpret_cast<uint4*>(reg1 + off) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-        *reinterpret_cast<uint4*>(ktT + r0) = make_uint4(pt[0], pt[1], pt[2], pt[3]);
+        *reinterpret_cast<uint4*>(ktT + (size_t)(r0 >> 3) * (kGD * 8)) = make_uint4(pt[0], pt[1], pt[2], pt[3]);
       }
     }
   }
@@ -341,26 +387,37 @@ __global__ void __launch_bounds__(kP1_Threads, 1) gdn_p1_kernel(GdnStreams s) {
       umma_f16_ss(tmem + 256, sdesc_kstep(aT, 128, ks), sdesc_kstep(bK, 256, ks), idesc, ks > 0);
     umma_commit(bar_uw);
   }
-  // ---- (e) u rows (warps 0-3) and w rows (warps 4-7) -> fp16 global
+  // ---- (e) u rows (warps 0-3) and w rows (warps 4-7) -> fp16 SW128 tiles over the operands the products
+  //      have consumed (u in reg0, w in reg1; the 16-byte stores of 8 consecutive rows hit distinct bank
+  //      groups), then one TMA store each
   {
     const int r = (warp & 3) * 32 + lane;
     const bool is_w = warp >= 4;
     alive = mbar_wait_warp(bar_uw, 0, nullptr, s.err, 0x42) && alive;
     tc_fence_after();
     const uint32_t trow = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (is_w ? 256u : 0u);
-    __half* orow = (is_w ? s.w : s.u) + (rowbase + r) * kGD;
+    uint8_t* tile = is_w ? reg1 : reg0;
 #pragma unroll 1
     for (int c0 = 0; c0 < 256; c0 += 16) {
       float f[16];
       tmem_ld16_wait(trow + c0, f);
-      uint4* op = reinterpret_cast<uint4*>(orow + c0);
-      op[0] = make_uint4(pack_half2(f[0], f[1]), pack_half2(f[2], f[3]), pack_half2(f[4], f[5]), pack_half2(f[6], f[7]));
-      op[1] = make_uint4(pack_half2(f[8], f[9]), pack_half2(f[10], f[11]), pack_half2(f[12], f[13]),
-                         pack_half2(f[14], f[15]));
+      uint8_t* at = tile + (c0 >> 6) * (128 * 128);
+      *reinterpret_cast<uint4*>(at + sw128_offset(r, c0 & 63)) =
+          make_uint4(pack_half2(f[0], f[1]), pack_half2(f[2], f[3]), pack_half2(f[4], f[5]), pack_half2(f[6], f[7]));
+      *reinterpret_cast<uint4*>(at + sw128_offset(r, (c0 & 63) + 8)) =
+          make_uint4(pack_half2(f[8], f[9]), pack_half2(f[10], f[11]), pack_half2(f[12], f[13]),
+                     pack_half2(f[14], f[15]));
     }
   }
+  fence_async_smem();
   tc_fence_before();
   __syncthreads();
+  if (t == 0) {
+    tma_store_3d(&umap, reg0, 0, (int)rowbase, 0);
+    tma_store_3d(&wmap, reg1, 0, (int)rowbase, 0);
+    tma_store_commit();
+    tma_store_wait_all();
+  }
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
@@ -378,7 +435,7 @@ constexpr int kP2_Smem = kP2_SmemW + kP2_SmemKT + kP2_SmemST + kP2_SmemVT + 1024
 constexpr int kP2_Tmem = 3 * kP2_NB <= 64 ? 64 : 128;   // v' product, then the two halves of the state product
 
 __global__ void __launch_bounds__(kP2_Threads, 1)
-    gdn_p2_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap ktmap, GdnStreams s) {
+    gdn_p2_kernel(const __grid_constant__ CUtensorMap wmap, GdnStreams s) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sW = smem;
@@ -433,7 +490,6 @@ __global__ void __launch_bounds__(kP2_Threads, 1)
   if (warp == 4) {
     if (lane == 0) {
       tma_prefetch(&wmap);
-      tma_prefetch(&ktmap);
       int iw = 0, ik = 0;
       for (int j = 0; j < ncl; ++j) {
         const int c = c_begin + j;
@@ -443,7 +499,7 @@ __global__ void __launch_bounds__(kP2_Threads, 1)
         iw = j + 1;
         if (j >= 1 && !mbar_wait(bar_m2, (j - 1) & 1, abort_flag, s.err, 0x52)) break;
         mbar_expect_tx(bar_kt, kP2_SmemKT);
-        tma_load_3d(sKT, &ktmap, bar_kt, 0, (bg * nch + c) * kGD, 0);
+        bulk_load_1d(sKT, s.ktT + ((size_t)bg * nch + c) * kGD * kGC, kP2_SmemKT, bar_kt);
         ik = j + 1;
       }
       if (iw > 0) mbar_wait(bar_w, (iw - 1) & 1, nullptr, s.err, 0x53);
@@ -468,8 +524,10 @@ __global__ void __launch_bounds__(kP2_Threads, 1)
         for (int mt = 0; mt < 2; ++mt) {
 #pragma unroll
           for (int ks = 0; ks < kGC / 16; ++ks) {
-            const uint32_t a = aKT + (ks >> 2) * (kGD * 128) + mt * (128 * 128) + (ks & 3) * 32;
-            umma_f16_ss(tmem + kP2_NB * (1 + mt), sdesc_sw128(a), sdesc_kstep(bVT, kP2_NB, ks), id1, ks > 0);
+            // k_tail^T core matrices: 16 tokens = two token groups (kGD * 16 bytes apart), rows mt * 128 ..
+            const uint32_t a = aKT + (uint32_t)ks * (2 * kGD * 16) + (uint32_t)mt * (128 * 16);
+            umma_f16_ss(tmem + kP2_NB * (1 + mt), sdesc_nosw(a, kGD * 16, 128), sdesc_kstep(bVT, kP2_NB, ks), id1,
+                        ks > 0);
           }
         }
         umma_commit(bar_m2);
@@ -1074,21 +1132,25 @@ int launch_gdn_prefill(GdnStreams s, cudaStream_t stream, int parts) {
     g_p_attr[0] = true;
   }
   if (parts & kGdnP1) {
+    CUtensorMap kwmap, umap, wmap1;
+    const uint64_t nrows = (uint64_t)s.B * s.G * s.n_pad;
+    int rc1 = make_tmap_kmajor(&kwmap, s.kw, BF_F16, nrows, kGD, kGD, kGC, 4);
+    if (!rc1) rc1 = make_tmap_kmajor(&umap, s.u, BF_F16, nrows, kGD, kGD, kGC, 4);
+    if (!rc1) rc1 = make_tmap_kmajor(&wmap1, s.w, BF_F16, nrows, kGD, kGD, kGC, 4);
+    if (rc1) return rc1;
     stage_mark(ST_GDN_P1, 0, stream);
-    gdn_p1_kernel<<<dim3(s.n_chunks, s.B * s.G), kP1_Threads, kP1_Smem, stream>>>(s);
+    gdn_p1_kernel<<<dim3(s.n_chunks, s.B * s.G), kP1_Threads, kP1_Smem, stream>>>(kwmap, umap, wmap1, s);
     if (int e_ = launch_status()) return e_;
     stage_mark(ST_GDN_P1, 1, stream);
   }
   if (!(parts & (kGdnP2 | kGdnP3))) return BF_OK;
-  CUtensorMap wmap, ktmap;
+  CUtensorMap wmap;
   int rc = make_tmap_kmajor(&wmap, s.w, BF_F16, (uint64_t)s.B * s.G * s.n_pad, kGD, kGD, kGC, 4);
-  if (rc) return rc;
-  rc = make_tmap_kmajor(&ktmap, s.ktT, BF_F16, (uint64_t)s.B * s.G * s.n_chunks * kGD, kGC, kGC, kGD, 2);
   if (rc) return rc;
   if (parts & kGdnP2) {
   stage_mark(ST_GDN_P2, 0, stream);
   gdn_p2_kernel<<<dim3((s.m_out ? 2 : 1) * (kGD / kP2_NB), s.chunk_tok0 ? s.G * s.n_seq : s.B * s.G), kP2_Threads,
-                  kP2_Smem, stream>>>(wmap, ktmap, s);
+                  kP2_Smem, stream>>>(wmap, s);
   if (int e_ = launch_status()) return e_;
   stage_mark(ST_GDN_P2, 1, stream);
   }
