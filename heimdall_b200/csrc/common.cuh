@@ -131,6 +131,9 @@ __device__ __forceinline__ void fence_async_smem() {
 
 // ----------------------------------------------------------------------------------------------
 // TMA loads (tiled, one CTA per load).  `tmap` is the generic address of a __grid_constant__ CUtensorMap.
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(p)));
+}
 __device__ __forceinline__ void tma_prefetch(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }
@@ -316,14 +319,15 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t smem_addr) {
   d |= (uint64_t)2 << 61;                        // SWIZZLE_128B
   return d;
 }
-// K-major tile without swizzle: 8-row x 16-byte core matrices of 128 contiguous bytes, `lbo` bytes between
-// core matrices adjacent in K and `sbo` bytes between adjacent 8-row groups
-__device__ __forceinline__ uint64_t sdesc_nosw(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
+// MN-major tile with the 128-byte swizzle: rows of 128 bytes hold 64 consecutive M/N elements, one row per K
+// index, 8-row (8 K) groups 1024 bytes apart (SBO) and 64-element M/N blocks `mn_stride` bytes apart (LBO)
+__device__ __forceinline__ uint64_t sdesc_sw128_mn(uint32_t smem_addr, uint32_t mn_stride) {
   uint64_t d = 0;
-  d |= (uint64_t)((smem_addr & 0x3FFFFu) >> 4);  // start address
-  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;   // leading byte offset
-  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;   // stride byte offset
-  d |= (uint64_t)1 << 46;                        // descriptor version (sm_100); swizzle mode 0 (none)
+  d |= (uint64_t)((smem_addr & 0x3FFFFu) >> 4);       // start address
+  d |= (uint64_t)((mn_stride >> 4) & 0x3FFFu) << 16;  // leading byte offset: next 64 M/N elements
+  d |= (uint64_t)(1024 >> 4) << 32;                   // stride byte offset: next 8 K rows
+  d |= (uint64_t)1 << 46;                             // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;                             // SWIZZLE_128B
   return d;
 }
 // descriptor for k-step `ks` (16 elements of 16 bits) of a K-major SW128 tile with `rows` rows
@@ -337,6 +341,8 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, int ab_bf16) {
   return (1u << 4) | ((uint32_t)ab_bf16 << 7) | ((uint32_t)ab_bf16 << 10) | ((uint32_t)(N >> 3) << 17) |
          ((uint32_t)(M >> 4) << 24);
 }
+constexpr uint32_t kIdescAMn = 1u << 15;   // A is MN-major (M contiguous)
+constexpr uint32_t kIdescBMn = 1u << 16;   // B is MN-major (N contiguous)
 
 // byte offset of element (row, col) (col in 16-bit elements, < 64) inside one SW128 atom column
 __device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t col16) {

@@ -10,10 +10,11 @@
 //
 // P1 (parallel, CTA = chunk x (b, KV head)): K K^T on tcgen05, A masked/decayed in the epilogue, T by blocked
 //     inversion of the 16x16 diagonal blocks then recursive doubling of the block-triangular inverse in
-//     shared memory, u and w on tcgen05; also writes fp16 keys,
-//     (e^{c_C - c} k)^T and the cumulative decays.
+//     shared memory, u = (T diag beta) V and w = (T diag(beta e^c)) K on tcgen05 with the value and key tiles
+//     in token-row order; also writes the fp16 keys and the cumulative decays.
 // P2 (sequential over chunks, CTA = (b, KV head, kP2_NB state columns)): the state block lives in registers (fp32),
-//     v' = u - w S and dS = k_tail^T v' run on tcgen05 with fp16 copies of S^T / v'^T staged in shared memory;
+//     v' = u - w S and dS = K^T (e^{c_C - c} v') run on tcgen05 with fp16 copies of S^T / v'^T staged in shared
+//     memory and the fp16 key tile as P1 wrote it;
 //     the state at each chunk start and v' are written (fp16, transposed) for P3.
 // P3 (parallel, CTA = chunk x (b, query head)): Q K^T (-> decayed causal P in fp16), then per half of the value
 //     columns o = e^{c} (Q S_chunk) + P v' with the two products in separate TMEM accumulators.
@@ -86,10 +87,11 @@ __device__ __forceinline__ void tmem_ld16_wait(uint32_t taddr, float (&f)[16]) {
 
 // ============================================================================================ P1
 constexpr int kP1_Threads = 256;
-constexpr int kP1_Reg0 = 0;                 // k tile (64 KB) -> T fp32 -> (beta v)^T (64 KB)
-constexpr int kP1_Reg1 = 69632;             // A fp32 (67.6 KB) -> (beta e^c k)^T (64 KB)
-constexpr int kP1_RegW = 69632 * 2;         // T fp16 (32 KB)
-constexpr int kP1_Small = kP1_RegW + 32768; // gc/g/beta (3 x 512 B) + barriers + row pointers (3 KB) + factors (1 KB)
+constexpr int kP1_RegK = 0;                   // fp16 key tile [128 tokens][256] (64 KB) -> w staging
+constexpr int kP1_RegA = 65536;               // A fp32 [128][kAS] (67.6 KB) -> T_u, T_w fp16 (2 x 32 KB)
+constexpr int kP1_RegT = kP1_RegA + 69632;    // T fp32 [128][kAS] -> fp16 value tile [128 tokens][256] -> u staging
+constexpr int kP1_RegX = kP1_RegT + 69632;    // doubling scratch (17 KB)
+constexpr int kP1_Small = kP1_RegX + 17408;   // gc/g/beta (3 x 512 B) + barriers + row pointers (3 KB) + factors (1 KB)
 constexpr int kP1_Smem = kP1_Small + 2048 + 3072 + 1024 + 1024;
 constexpr int kAS = 132;                    // row stride (floats) of A and T in shared memory
 
@@ -97,24 +99,41 @@ constexpr int kAS = 132;                    // row stride (floats) of A and T in
 __device__ __align__(16) float g_zero_row[kGD];
 
 // O = (NEG ? -1 : 1) * L R for M x M blocks of row-major fp32 matrices in shared memory (leading dims in
-// floats, multiples of 4; block origins 16-byte aligned), block b of nb; thread tile TR x TC, the reduction
-// reads four columns of L and TC-wide rows of R at a time.
-template <int M, int TR, int TC, bool NEG>
+// floats, multiples of 4; block origins 16-byte aligned); thread tile TR rows x TC columns, the reduction
+// reads four columns of L and TC-wide rows of R at a time.  TRI says which factor is lower triangular, so
+// that the reduction skips its zero part:
+//   TRI = 1: R (O[i][c] needs j >= c).  Threads of a warp share their columns and take rows g + a * M / TR
+//            (rows 16 bytes apart in the bank map for a leading dimension of 4 mod 32), so the sum starts
+//            at the warp's first column;
+//   TRI = 2: L (O[i][c] needs j <= i).  Threads of a warp share their rows, so the sum ends after the
+//            warp's last row.
+template <int M, int TR, int TC, bool NEG, int TRI>
 __device__ __forceinline__ void block_mm(const float* L, int ldl, const float* R, int ldr, float* O, int ldo,
                                          int tt) {
-  constexpr int NTC = M / TC, NT = (M / TR) * NTC;
+  constexpr int NTC = M / TC, NTR = M / TR, NT = NTR * NTC;
   if (tt >= NT) return;
-  const int i0 = (tt / NTC) * TR, c0 = (tt % NTC) * TC;
+  int rows[TR], c0;
+  if constexpr (TRI == 1) {
+    c0 = (tt / NTR) * TC;
+#pragma unroll
+    for (int a = 0; a < TR; ++a) rows[a] = tt % NTR + a * NTR;
+  } else {
+    c0 = (tt % NTC) * TC;
+#pragma unroll
+    for (int a = 0; a < TR; ++a) rows[a] = (tt / NTC) * TR + a;
+  }
+  const int j0 = TRI == 1 ? (c0 & ~3) : 0;
+  const int j1 = TRI == 2 ? ((rows[TR - 1] + 4) & ~3) : M;
   float acc[TR][TC];
 #pragma unroll
   for (int a = 0; a < TR; ++a)
 #pragma unroll
     for (int b = 0; b < TC; ++b) acc[a][b] = 0.f;
 #pragma unroll 2
-  for (int j = 0; j < M; j += 4) {
+  for (int j = j0; j < j1; j += 4) {
     float4 av[TR];
 #pragma unroll
-    for (int a = 0; a < TR; ++a) av[a] = *reinterpret_cast<const float4*>(L + (i0 + a) * ldl + j);
+    for (int a = 0; a < TR; ++a) av[a] = *reinterpret_cast<const float4*>(L + rows[a] * ldl + j);
 #pragma unroll
     for (int jj = 0; jj < 4; ++jj) {
       float bv[TC];
@@ -137,35 +156,46 @@ __device__ __forceinline__ void block_mm(const float* L, int ldl, const float* R
     }
   }
 #pragma unroll
-  for (int a = 0; a < TR; ++a)
+  for (int a = 0; a < TR; ++a) {
+    float* o = O + rows[a] * ldo + c0;
+    const float sg = NEG ? -1.f : 1.f;
+    if constexpr (TC == 4) {
+      *reinterpret_cast<float4*>(o) = make_float4(sg * acc[a][0], sg * acc[a][1], sg * acc[a][2], sg * acc[a][3]);
+    } else if constexpr (TC == 2) {
+      *reinterpret_cast<float2*>(o) = make_float2(sg * acc[a][0], sg * acc[a][1]);
+    } else {
 #pragma unroll
-    for (int b = 0; b < TC; ++b) O[(i0 + a) * ldo + c0 + b] = NEG ? -acc[a][b] : acc[a][b];
+      for (int b = 0; b < TC; ++b) o[b] = sg * acc[a][b];
+    }
+  }
 }
 
 // one doubling level of the block-triangular inverse: for each block pair (rows r1.., r2 = r1 + M)
-// T21 = -T22 (A21 T11), with X (the products A21 T11) in scratch; `tt` = thread index, threads split by pair
-template <int M, int TR, int TC>
+// T21 = -T22 (A21 T11), with X (the products A21 T11) in scratch; `tt` = thread index, threads split by pair.
+// T11 and T22 are lower triangular: the first product skips T11's upper part, the second T22's.
+template <int M, int TR, int TC, int TRI1, int TRI2>
 __device__ __forceinline__ void inverse_doubling_level(const float* A, float* Tm, float* X, int tt) {
   constexpr int NT = (M / TR) * (M / TC), NPAIR = 128 / (2 * M);
   static_assert(NT * NPAIR <= kP1_Threads, "one tile per thread");
+  constexpr int LDX = M + 4;   // X rows 16 bytes apart in the bank map
   const int k = tt / NT, lt = tt % NT;
   const int r1 = k * 2 * M, r2 = r1 + M;
-  if (k < NPAIR) block_mm<M, TR, TC, false>(A + r2 * kAS + r1, kAS, Tm + r1 * kAS + r1, kAS, X + k * M * M, M, lt);
+  if (k < NPAIR)
+    block_mm<M, TR, TC, false, TRI1>(A + r2 * kAS + r1, kAS, Tm + r1 * kAS + r1, kAS, X + k * M * LDX, LDX, lt);
   __syncthreads();
-  if (k < NPAIR) block_mm<M, TR, TC, true>(Tm + r2 * kAS + r2, kAS, X + k * M * M, M, Tm + r2 * kAS + r1, kAS, lt);
+  if (k < NPAIR)
+    block_mm<M, TR, TC, true, TRI2>(Tm + r2 * kAS + r2, kAS, X + k * M * LDX, LDX, Tm + r2 * kAS + r1, kAS, lt);
   __syncthreads();
 }
 
-// The fp16 keys, u and w leave through TMA stores of their K-major SW128 tiles (kwmap / umap / wmap: 3-D maps
-// (64, rows, 4 atoms) over [B*G*n_pad][256], one 128-row box per chunk).
 __global__ void __launch_bounds__(kP1_Threads, 1)
     gdn_p1_kernel(const __grid_constant__ CUtensorMap kwmap, const __grid_constant__ CUtensorMap umap,
                   const __grid_constant__ CUtensorMap wmap, GdnStreams s) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* reg0 = smem + kP1_Reg0;
-  uint8_t* reg1 = smem + kP1_Reg1;
-  uint8_t* regW = smem + kP1_RegW;
+  uint8_t* regK = smem + kP1_RegK;
+  uint8_t* regA = smem + kP1_RegA;
+  uint8_t* regT = smem + kP1_RegT;
   float* s_gc = reinterpret_cast<float*>(smem + kP1_Small);
   float* s_g = s_gc + 128;
   float* s_beta = s_g + 128;
@@ -176,8 +206,8 @@ __global__ void __launch_bounds__(kP1_Threads, 1)
   const float** s_kp = reinterpret_cast<const float**>(smem + kP1_Small + 2048);   // [128] key row (or null)
   const __nv_bfloat16** s_vp = reinterpret_cast<const __nv_bfloat16**>(s_kp + 128);  // [128] bf16 value row
   const float** s_vp32 = reinterpret_cast<const float**>(s_vp + 128);             // [128] fp32 value row
-  float* A = reinterpret_cast<float*>(reg1);   // [128][kAS]
-  float* Tm = reinterpret_cast<float*>(reg0);  // [128][kAS]
+  float* A = reinterpret_cast<float*>(regA);   // [128][kAS]
+  float* Tm = reinterpret_cast<float*>(regT);  // [128][kAS]
 
   const int c = blockIdx.x, bg = blockIdx.y, b = bg / s.G, gg = bg % s.G;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
@@ -193,29 +223,38 @@ __global__ void __launch_bounds__(kP1_Threads, 1)
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
-  // ---- (a) key rows -> fp16 K tile (SW128, 4 atoms), which is also the chunk's tile of fp16 write keys
+  // ---- (a) the chunk's write steps: gates and row pointers (thread r < 128; invalid steps point at a zero
+  //      row and have beta = 0, so they contribute nothing)
+  if (t < 128) {
+    const RowSrc src = write_row(s, b, gg, c * kGC + t);
+    s_g[t] = src.zero ? 0.f : src.g;
+    s_beta[t] = src.zero ? 0.f : src.beta;
+    s_kp[t] = src.zero ? g_zero_row : src.k;
+    s_vp[t] = src.zero ? reinterpret_cast<const __nv_bfloat16*>(g_zero_row) : src.v;
+    s_vp32[t] = src.zero ? g_zero_row : src.v32;
+  }
+  __syncthreads();
+  //      key rows -> fp16 K tile (SW128, 4 atoms), which is also the chunk's tile of fp16 write keys.  Warp w
+  //      takes rows w + 8 i; each load covers 512 contiguous bytes of a row (lane l: columns 4 l .. 4 l + 3 of
+  //      each half), all 32 in flight at once
   {
-    const int r = t >> 1, hh = t & 1;
-    const RowSrc src = write_row(s, b, gg, c * kGC + r);
-    if (hh == 0) {   // invalid steps read a zero row (their beta is 0, so they contribute nothing)
-      s_g[r] = src.zero ? 0.f : src.g;
-      s_beta[r] = src.zero ? 0.f : src.beta;
-      s_kp[r] = src.zero ? g_zero_row : src.k;
-      s_vp[r] = src.zero ? reinterpret_cast<const __nv_bfloat16*>(g_zero_row) : src.v;
-      s_vp32[r] = src.zero ? g_zero_row : src.v32;
-    }
-    // all 32 loads of this thread's half row in flight at once (invalid steps read the zero row)
-    const float* kp = src.zero ? g_zero_row : src.k;
     float4 kx[32];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) kx[i] = *reinterpret_cast<const float4*>(kp + hh * 128 + i * 4);
+    for (int i = 0; i < 16; ++i) {
+      const float* kp = s_kp[warp + 8 * i] + 4 * lane;
+      kx[2 * i] = *reinterpret_cast<const float4*>(kp);
+      kx[2 * i + 1] = *reinterpret_cast<const float4*>(kp + 128);
+    }
 #pragma unroll
-    for (int ch = 0; ch < 16; ++ch) {  // 16 chunks of 8 elements = 128 columns
-      const float4 a0 = kx[2 * ch], a1 = kx[2 * ch + 1];
-      const uint4 pk = make_uint4(pack_half2(a0.x, a0.y), pack_half2(a0.z, a0.w), pack_half2(a1.x, a1.y),
-                                  pack_half2(a1.z, a1.w));
-      const int col = hh * 128 + ch * 8;
-      *reinterpret_cast<uint4*>(reg0 + (col >> 6) * (128 * 128) + sw128_offset(r, col & 63)) = pk;
+    for (int i = 0; i < 16; ++i) {
+      const int r = warp + 8 * i;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const float4 x = kx[2 * i + hh];
+        const int col = hh * 128 + 4 * lane;
+        *reinterpret_cast<uint2*>(regK + (col >> 6) * (128 * 128) + sw128_offset(r, col & 63)) =
+            make_uint2(pack_half2(x.x, x.y), pack_half2(x.z, x.w));
+      }
     }
   }
   fence_async_smem();
@@ -226,9 +265,9 @@ __global__ void __launch_bounds__(kP1_Threads, 1)
   if (t == 0) {
     tma_prefetch(&umap);
     tma_prefetch(&wmap);
-    tma_store_3d(&kwmap, reg0, 0, (int)rowbase, 0);   // the write keys (fp16)
+    tma_store_3d(&kwmap, regK, 0, (int)rowbase, 0);   // the write keys (fp16)
     tma_store_commit();
-    const uint32_t aK = smem_u32(reg0);
+    const uint32_t aK = smem_u32(regK);
     constexpr uint32_t idesc = idesc_f16(128, 128, 0);
 #pragma unroll
     for (int ks = 0; ks < kGD / 16; ++ks)
@@ -255,14 +294,9 @@ __global__ void __launch_bounds__(kP1_Threads, 1)
     s.gc[rowbase + t] = gacc;
   }
   __syncthreads();
-  const float gamma_last = s_gc[127];
-  // per-step factors of the B operands: beta e^{c} and e^{c_C - c} (both <= 1)
+  // per-step factor of w's operand: beta e^{c} (<= 1)
   float* s_bec = reinterpret_cast<float*>(smem + kP1_Small + 2048 + 3072);   // [128], after the row pointers
-  float* s_ect = s_bec + 128;                                                // [128]
-  if (t < 128) {
-    s_bec[t] = s_beta[t] * __expf(s_gc[t]);
-    s_ect[t] = __expf(gamma_last - s_gc[t]);
-  }
+  if (t < 128) s_bec[t] = s_beta[t] * __expf(s_gc[t]);
   // ---- (b) A = strict_lower(beta_i e^{c_i - c_j} (k_i . k_j)) from TMEM (all warps: row = lane quarter of
   //      the warp, columns 64 * (warp / 4) .. + 63)
   bool alive = true;
@@ -287,9 +321,19 @@ __global__ void __launch_bounds__(kP1_Threads, 1)
         *reinterpret_cast<float4*>(A + r * kAS + c0 + e) = make_float4(f[e], f[e + 1], f[e + 2], f[e + 3]);
     }
   }
-  if (t == 0) tma_store_wait_read();   // the key tile has been read out
   tc_fence_before();
-  __syncthreads();  // A complete; the K tile (reg0) is free (K K^T finished, keys stored)
+  __syncthreads();  // A complete
+  {   // the value rows are read after the inverse: bring them into L2 while it runs
+    const int r = t & 127, part = t >> 7;
+    const uint8_t* vb = s.v32 ? reinterpret_cast<const uint8_t*>(s_vp32[r]) + part * 512
+                              : reinterpret_cast<const uint8_t*>(s_vp[r]) + part * 256;
+    prefetch_l2(vb);
+    prefetch_l2(vb + 128);
+    if (s.v32) {
+      prefetch_l2(vb + 256);
+      prefetch_l2(vb + 384);
+    }
+  }
   // ---- (c) T = (I + A)^-1: invert the eight 16x16 diagonal blocks (one column chain per thread), then
   //      double the solved block size 16 -> 32 -> 64 -> 128 with T21 = -T22 (A21 T11)
   for (int i = t; i < 128 * kAS; i += kP1_Threads) Tm[i] = 0.f;
@@ -319,84 +363,94 @@ __global__ void __launch_bounds__(kP1_Threads, 1)
   __syncthreads();
   // (T stays zero above its diagonal and T11, T22 are lower triangular, so both products are plain block
   // products: X = A21 T11, T21 = -T22 X)
-  float* X = reinterpret_cast<float*>(regW);  // scratch: A21 T11 for every block pair of a level (16 KB)
-  inverse_doubling_level<16, 2, 2>(A, Tm, X, t);
-  inverse_doubling_level<32, 4, 2>(A, Tm, X, t);
-  inverse_doubling_level<64, 4, 4>(A, Tm, X, t);
-  // ---- T -> fp16 SW128 tile (rows i, K = j) in regW
+  float* X = reinterpret_cast<float*>(smem + kP1_RegX);  // scratch: A21 T11 for every block pair of a level
+  inverse_doubling_level<16, 2, 2, 0, 0>(A, Tm, X, t);
+  inverse_doubling_level<32, 4, 2, 1, 2>(A, Tm, X, t);
+  inverse_doubling_level<64, 4, 4, 1, 2>(A, Tm, X, t);
+  // ---- T -> T_u = T diag(beta) and T_w = T diag(beta e^c), fp16 SW128 tiles (rows i, K = j) over A: then
+  //      u = T_u V and w = T_w K take the value and key tiles as they lie (token rows, MN-major B operands)
   for (int p = t; p < 128 * 16; p += kP1_Threads) {
     const int i = p >> 4, ch = p & 15;  // chunk of 8 columns
-    const float* tr = Tm + i * kAS + ch * 8;
-    const uint4 pk = make_uint4(pack_half2(tr[0], tr[1]), pack_half2(tr[2], tr[3]), pack_half2(tr[4], tr[5]),
-                                pack_half2(tr[6], tr[7]));
-    *reinterpret_cast<uint4*>(regW + (ch >> 3) * (128 * 128) + sw128_offset(i, (ch & 7) * 8)) = pk;
+    const float4* tr = reinterpret_cast<const float4*>(Tm + i * kAS + ch * 8);
+    const float4* bj = reinterpret_cast<const float4*>(s_beta + ch * 8);
+    const float4* ej = reinterpret_cast<const float4*>(s_bec + ch * 8);
+    const float4 t0 = tr[0], t1 = tr[1], b0 = bj[0], b1 = bj[1], e0 = ej[0], e1 = ej[1];
+    const uint32_t pu[4] = {pack_half2(t0.x * b0.x, t0.y * b0.y), pack_half2(t0.z * b0.z, t0.w * b0.w),
+                            pack_half2(t1.x * b1.x, t1.y * b1.y), pack_half2(t1.z * b1.z, t1.w * b1.w)};
+    const uint32_t pw[4] = {pack_half2(t0.x * e0.x, t0.y * e0.y), pack_half2(t0.z * e0.z, t0.w * e0.w),
+                            pack_half2(t1.x * e1.x, t1.y * e1.y), pack_half2(t1.z * e1.z, t1.w * e1.w)};
+    const uint32_t off = (uint32_t)(ch >> 3) * (128 * 128) + sw128_offset(i, (ch & 7) * 8);
+    *reinterpret_cast<uint4*>(regA + off) = make_uint4(pu[0], pu[1], pu[2], pu[3]);
+    *reinterpret_cast<uint4*>(regA + 32768 + off) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
   }
-  __syncthreads();  // Tm (reg0) and A (reg1) are free now
-  // ---- (d) B operands: (beta v)^T -> reg0, (beta e^c k)^T -> reg1 ([256 dims][128 tokens] K-major);
-  //      and k_tail^T = (e^{c_C - c} k)^T to global (P2's A operand).  Thread t owns dimension t and builds
-  //      16-byte chunks of 8 tokens, so shared and global stores are vector-wide and loads coalesce over t.
-  {
-    const int d = t;
-    // k_tail^T in core-matrix order [token group of 8][dimension][8 tokens]: the stores of a warp are 512
-    // contiguous bytes, and the tile is P2's operand as it lies in memory
-    __half* ktT = s.ktT + ((size_t)bg * s.n_chunks + c) * kGD * kGC + (size_t)d * 8;
-    const bool v32 = s.v32 != nullptr;   // uniform for the launch
-#pragma unroll 1
-    for (int rb = 0; rb < kGC; rb += 64) {
-      // 128 independent, unconditional loads in flight per thread (64 tokens x {k, v}), then pack and store
-      float kv[64], vv[64];
+  __syncthreads();  // T (fp32) is free: the value tile goes there
+  // ---- (d) value rows -> fp16 value tile [128 tokens][256] (SW128 atoms of 64 columns): warp w takes rows
+  //      w + 8 i, each load covering 512 contiguous bytes of a row
+  if (s.v32) {   // uniform for the launch
+    float4 x[32];
 #pragma unroll
-      for (int e = 0; e < 64; ++e) kv[e] = s_kp[rb + e][d];
-      if (v32) {
+    for (int i = 0; i < 16; ++i) {
+      const float* vp = s_vp32[warp + 8 * i] + 4 * lane;
+      x[2 * i] = *reinterpret_cast<const float4*>(vp);
+      x[2 * i + 1] = *reinterpret_cast<const float4*>(vp + 128);
+    }
 #pragma unroll
-        for (int e = 0; e < 64; ++e) vv[e] = s_vp32[rb + e][d];
-      } else {
+    for (int i = 0; i < 16; ++i) {
+      const int r = warp + 8 * i;
 #pragma unroll
-        for (int e = 0; e < 64; ++e) vv[e] = __bfloat162float(s_vp[rb + e][d]);
-      }
-#pragma unroll
-      for (int q = 0; q < 64; q += 8) {
-        const int r0 = rb + q;
-        uint32_t pv[4], pk[4], pt[4];
-#pragma unroll
-        for (int e = 0; e < 8; e += 2) {
-          const int r = r0 + e;
-          pv[e / 2] = pack_half2(s_beta[r] * vv[q + e], s_beta[r + 1] * vv[q + e + 1]);
-          pk[e / 2] = pack_half2(s_bec[r] * kv[q + e], s_bec[r + 1] * kv[q + e + 1]);
-          pt[e / 2] = pack_half2(s_ect[r] * kv[q + e], s_ect[r + 1] * kv[q + e + 1]);
-        }
-        const uint32_t off = (uint32_t)(r0 >> 6) * (256 * 128) + sw128_offset(d, r0 & 63);
-        *reinterpret_cast<uint4*>(reg0 + off) = make_uint4(pv[0], pv[1], pv[2], pv[3]);
-        *reinterpret_cast<uint4*>(reg1 + off) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-        *reinterpret_cast<uint4*>(ktT + (size_t)(r0 >> 3) * (kGD * 8)) = make_uint4(pt[0], pt[1], pt[2], pt[3]);
+      for (int hh = 0; hh < 2; ++hh) {
+        const float4 y = x[2 * i + hh];
+        const int col = hh * 128 + 4 * lane;
+        *reinterpret_cast<uint2*>(regT + (col >> 6) * (128 * 128) + sw128_offset(r, col & 63)) =
+            make_uint2(pack_half2(y.x, y.y), pack_half2(y.z, y.w));
       }
     }
+  } else {
+    uint4 x[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) x[i] = *reinterpret_cast<const uint4*>(s_vp[warp + 8 * i] + 8 * lane);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int r = warp + 8 * i;
+      const uint32_t w4[4] = {x[i].x, x[i].y, x[i].z, x[i].w};
+      uint32_t o4[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w4[e]));
+        o4[e] = pack_half2(f.x, f.y);
+      }
+      *reinterpret_cast<uint4*>(regT + (lane >> 3) * (128 * 128) + sw128_offset(r, (lane & 7) * 8)) =
+          make_uint4(o4[0], o4[1], o4[2], o4[3]);
+    }
   }
+  if (t == 0) tma_store_wait_read();   // the key tile has been stored (w is staged over it at the end)
   fence_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   if (t == 0) {
-    constexpr uint32_t idesc = idesc_f16(128, 256, 0);
-    const uint32_t aT = smem_u32(regW), bV = smem_u32(reg0), bK = smem_u32(reg1);
+    constexpr uint32_t idesc = idesc_f16(128, 256, 0) | kIdescBMn;
+    const uint32_t aTu = smem_u32(regA), aTw = smem_u32(regA + 32768), bV = smem_u32(regT), bK = smem_u32(regK);
+    // B operands: K index = token (8-token groups 1024 bytes apart), N = the 256 columns in four 64-column
+    // atoms 16 KB apart; one K step of 16 tokens = two groups
 #pragma unroll
     for (int ks = 0; ks < kGC / 16; ++ks)
-      umma_f16_ss(tmem, sdesc_kstep(aT, 128, ks), sdesc_kstep(bV, 256, ks), idesc, ks > 0);
+      umma_f16_ss(tmem, sdesc_kstep(aTu, 128, ks), sdesc_sw128_mn(bV + ks * 2048, 128 * 128), idesc, ks > 0);
 #pragma unroll
     for (int ks = 0; ks < kGC / 16; ++ks)
-      umma_f16_ss(tmem + 256, sdesc_kstep(aT, 128, ks), sdesc_kstep(bK, 256, ks), idesc, ks > 0);
+      umma_f16_ss(tmem + 256, sdesc_kstep(aTw, 128, ks), sdesc_sw128_mn(bK + ks * 2048, 128 * 128), idesc, ks > 0);
     umma_commit(bar_uw);
   }
   // ---- (e) u rows (warps 0-3) and w rows (warps 4-7) -> fp16 SW128 tiles over the operands the products
-  //      have consumed (u in reg0, w in reg1; the 16-byte stores of 8 consecutive rows hit distinct bank
-  //      groups), then one TMA store each
+  //      have consumed (u over the value tile, w over the key tile; the 16-byte stores of 8 consecutive rows
+  //      hit distinct bank groups), then one TMA store each
   {
     const int r = (warp & 3) * 32 + lane;
     const bool is_w = warp >= 4;
     alive = mbar_wait_warp(bar_uw, 0, nullptr, s.err, 0x42) && alive;
     tc_fence_after();
     const uint32_t trow = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (is_w ? 256u : 0u);
-    uint8_t* tile = is_w ? reg1 : reg0;
+    uint8_t* tile = is_w ? regK : regT;
 #pragma unroll 1
     for (int c0 = 0; c0 < 256; c0 += 16) {
       float f[16];
@@ -413,10 +467,10 @@ __global__ void __launch_bounds__(kP1_Threads, 1)
   tc_fence_before();
   __syncthreads();
   if (t == 0) {
-    tma_store_3d(&umap, reg0, 0, (int)rowbase, 0);
-    tma_store_3d(&wmap, reg1, 0, (int)rowbase, 0);
+    tma_store_3d(&umap, regT, 0, (int)rowbase, 0);
+    tma_store_3d(&wmap, regK, 0, (int)rowbase, 0);
     tma_store_commit();
-    tma_store_wait_all();
+    tma_store_wait_read();   // shared memory may be released once the stores have read it
   }
   if (warp == 0) {
     tc_fence_after();
@@ -435,7 +489,7 @@ constexpr int kP2_Smem = kP2_SmemW + kP2_SmemKT + kP2_SmemST + kP2_SmemVT + 1024
 constexpr int kP2_Tmem = 3 * kP2_NB <= 64 ? 64 : 128;   // v' product, then the two halves of the state product
 
 __global__ void __launch_bounds__(kP2_Threads, 1)
-    gdn_p2_kernel(const __grid_constant__ CUtensorMap wmap, GdnStreams s) {
+    gdn_p2_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap kmap, GdnStreams s) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sW = smem;
@@ -490,6 +544,7 @@ __global__ void __launch_bounds__(kP2_Threads, 1)
   if (warp == 4) {
     if (lane == 0) {
       tma_prefetch(&wmap);
+      tma_prefetch(&kmap);
       int iw = 0, ik = 0;
       for (int j = 0; j < ncl; ++j) {
         const int c = c_begin + j;
@@ -499,7 +554,7 @@ __global__ void __launch_bounds__(kP2_Threads, 1)
         iw = j + 1;
         if (j >= 1 && !mbar_wait(bar_m2, (j - 1) & 1, abort_flag, s.err, 0x52)) break;
         mbar_expect_tx(bar_kt, kP2_SmemKT);
-        bulk_load_1d(sKT, s.ktT + ((size_t)bg * nch + c) * kGD * kGC, kP2_SmemKT, bar_kt);
+        tma_load_3d(sKT, &kmap, bar_kt, 0, bg * s.n_pad + c * kGC, 0);   // the chunk's fp16 keys
         ik = j + 1;
       }
       if (iw > 0) mbar_wait(bar_w, (iw - 1) & 1, nullptr, s.err, 0x53);
@@ -520,14 +575,15 @@ __global__ void __launch_bounds__(kP2_Threads, 1)
         if (!mbar_wait(bar_kt, j & 1, abort_flag, s.err, 0x57)) break;
         if (!mbar_wait(bar_vt, j & 1, abort_flag, s.err, 0x58)) break;
         tc_fence_after();
+        // dS = K^T (e^{c_C - c} v'): A = the key tile as it lies (token rows: M = dimensions in 64-column
+        // atoms 16 KB apart, MN-major), rows mt * 128 .. of the state in atoms 2 mt, 2 mt + 1
 #pragma unroll
         for (int mt = 0; mt < 2; ++mt) {
 #pragma unroll
           for (int ks = 0; ks < kGC / 16; ++ks) {
-            // k_tail^T core matrices: 16 tokens = two token groups (kGD * 16 bytes apart), rows mt * 128 ..
-            const uint32_t a = aKT + (uint32_t)ks * (2 * kGD * 16) + (uint32_t)mt * (128 * 16);
-            umma_f16_ss(tmem + kP2_NB * (1 + mt), sdesc_nosw(a, kGD * 16, 128), sdesc_kstep(bVT, kP2_NB, ks), id1,
-                        ks > 0);
+            const uint32_t a = aKT + (uint32_t)mt * (2 * 128 * 128) + (uint32_t)ks * 2048u;
+            umma_f16_ss(tmem + kP2_NB * (1 + mt), sdesc_sw128_mn(a, 128 * 128), sdesc_kstep(bVT, kP2_NB, ks),
+                        id1 | kIdescAMn, ks > 0);
           }
         }
         umma_commit(bar_m2);
@@ -602,8 +658,11 @@ __global__ void __launch_bounds__(kP2_Threads, 1)
       float dv[kP2_NB];
 #pragma unroll
       for (int q = 0; q < kP2_NB; q += 16) tmem_ld16_wait(trow + q, *reinterpret_cast<float(*)[16]>(dv + q));
+      // the state update's B operand carries the decay to the chunk end: (e^{c_C - c_r} v'_r)^T
+      const float* gcc = s.gc + (size_t)bg * s.n_pad + (size_t)c * kGC;
+      const float ect = __expf(gcc[kGC - 1] - gcc[r]);
 #pragma unroll
-      for (int e = 0; e < kP2_NB; ++e) st_half_sw128(sVT, kP2_NB, e, r, uu[e] - dv[e]);
+      for (int e = 0; e < kP2_NB; ++e) st_half_sw128(sVT, kP2_NB, e, r, (uu[e] - dv[e]) * ect);
       if (keep) {
         __half* vtg = s.VT + (((size_t)bg * nch + c) * kGD + col0) * kGC;
 #pragma unroll
@@ -1093,7 +1152,6 @@ size_t gdn_prefill_workspace(int B, int G, int T_steps, bool transform) {
   auto al = [](size_t x) { return (x + 1023) & ~size_t(1023); };
   size_t n = 0;
   n += al((size_t)B * G * n_pad * kGD * 2) * 3;       // kw, w, u
-  n += al((size_t)B * G * nch * kGD * kGC * 2);       // ktT
   n += al((size_t)B * G * n_pad * 4);                 // gc
   if (transform) return n;                            // no P3: the chunk states are not kept
   n += al((size_t)B * G * nch * kGD * kGD * 2);       // ST
@@ -1108,7 +1166,6 @@ int gdn_prefill_carve(GdnStreams& s, void* ws) {
   s.kw = reinterpret_cast<__half*>(p); p += al((size_t)s.B * s.G * n_pad * kGD * 2);
   s.w = reinterpret_cast<__half*>(p); p += al((size_t)s.B * s.G * n_pad * kGD * 2);
   s.u = reinterpret_cast<__half*>(p); p += al((size_t)s.B * s.G * n_pad * kGD * 2);
-  s.ktT = reinterpret_cast<__half*>(p); p += al((size_t)s.B * s.G * nch * kGD * kGC * 2);
   s.gc = reinterpret_cast<float*>(p); p += al((size_t)s.B * s.G * n_pad * 4);
   if (s.m_out) {
     s.ST = s.VT = nullptr;
@@ -1144,19 +1201,20 @@ int launch_gdn_prefill(GdnStreams s, cudaStream_t stream, int parts) {
     stage_mark(ST_GDN_P1, 1, stream);
   }
   if (!(parts & (kGdnP2 | kGdnP3))) return BF_OK;
-  CUtensorMap wmap;
+  CUtensorMap wmap, kmap;
   int rc = make_tmap_kmajor(&wmap, s.w, BF_F16, (uint64_t)s.B * s.G * s.n_pad, kGD, kGD, kGC, 4);
+  if (!rc) rc = make_tmap_kmajor(&kmap, s.kw, BF_F16, (uint64_t)s.B * s.G * s.n_pad, kGD, kGD, kGC, 4);
   if (rc) return rc;
   if (parts & kGdnP2) {
   stage_mark(ST_GDN_P2, 0, stream);
   gdn_p2_kernel<<<dim3((s.m_out ? 2 : 1) * (kGD / kP2_NB), s.chunk_tok0 ? s.G * s.n_seq : s.B * s.G), kP2_Threads,
-                  kP2_Smem, stream>>>(wmap, s);
+                  kP2_Smem, stream>>>(wmap, kmap, s);
   if (int e_ = launch_status()) return e_;
   stage_mark(ST_GDN_P2, 1, stream);
   }
   if (s.m_out || !(parts & kGdnP3)) return BF_OK;   // segment transform: no reads
   // P3 maps: q [B,T,H,D] fp16 as (d, token, atom, head); k/kw; S^T; v'^T
-  CUtensorMap qmap, kmap, smap, vmap;
+  CUtensorMap qmap, smap, vmap;   // (and kmap, the keys)
   {
     const uint64_t dims[4] = {64, (uint64_t)s.B * s.T, 4, (uint64_t)H};
     const uint64_t strides[3] = {(uint64_t)H * kGD * 2, 128, (uint64_t)kGD * 2};
@@ -1164,8 +1222,6 @@ int launch_gdn_prefill(GdnStreams s, cudaStream_t stream, int parts) {
     rc = make_tmap(&qmap, s.qm, BF_F16, 4, dims, strides, box, true);
     if (rc) return rc;
   }
-  rc = make_tmap_kmajor(&kmap, s.kw, BF_F16, (uint64_t)s.B * s.G * s.n_pad, kGD, kGD, kGC, 4);
-  if (rc) return rc;
   rc = make_tmap_kmajor(&smap, s.ST, BF_F16, (uint64_t)s.B * s.G * s.n_chunks * kGD, kGD, kGD, 128, 4);
   if (rc) return rc;
   rc = make_tmap_kmajor(&vmap, s.VT, BF_F16, (uint64_t)s.B * s.G * s.n_chunks * kGD, kGC, kGC, 128, 2);

@@ -34,7 +34,6 @@ struct GdnStreams {
   __half* kw;                  // [B,G,n_pad,D]   write keys (fp16)
   __half* w;                   // [B,G,n_pad,D]   T (beta e^gc k)
   __half* u;                   // [B,G,n_pad,D]   T (beta v)
-  __half* ktT;                 // [B,G,n_chunks,kGC/8,D,8]  (e^{gc_last - gc} k)^T in core-matrix order
   float* gc;                   // [B,G,n_pad]     cumulative log-decay inside the chunk
   __half* ST;                  // [B,G,n_chunks,D(dv),D(dk)]  state at chunk start, transposed
   __half* VT;                  // [B,G,n_chunks,D(dv),kGC]    v_new, transposed
