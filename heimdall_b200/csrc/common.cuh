@@ -352,6 +352,14 @@ __device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t col16) {
 
 // ----------------------------------------------------------------------------------------------
 // small numeric helpers
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+__device__ __forceinline__ float ex2_approx(float x) {   // 2^x (the ex2.approx instruction; 0 for -inf)
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -977,25 +977,55 @@ __global__ void __launch_bounds__(kP3_Threads, 1)
         for (int e8 = 0; e8 < 8; ++e8) ow[e8] = p3_load_ow(cc, e8);
       }
       if (has_cur) {
-        // 1. P of this head over the first half of this thread's A columns
+        // 1. P of this head over the first half of this thread's A columns: the 64 scores in one TMEM read, the
+        //    decays of the keys (the same for every lane: broadcast loads) 16 at a time
         const uint32_t pa = trow + kP3_TA + cb * 64;
+        const float4* g4 = reinterpret_cast<const float4*>(cc.gcc + cb * 64);
+        const float ci2 = cc.ci * kLog2e;
         alive = mbar_wait_warp(bar_a, m & 1, abort_flag, s.err, 0x6c);
         if (!alive) break;
         tc_fence_after();
 #pragma unroll 1
-        for (int q = 0; q < 4; ++q) {   // 16 keys per step: A columns q*16.., P columns q*8..
-          const int c0 = cb * 64 + q * 16;
-          float f[16];
-          tmem_ld16_wait(pa + q * 16, f);
-          uint32_t pk[8];
+        for (int h2 = 0; h2 < 2; ++h2) {   // 32 keys per TMEM read (P of a half lands behind its reads)
+          uint32_t av[32];
+          tmem_ld32(pa + h2 * 32, av);
+          tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 16; e += 2) {
-            const int j = c0 + e;
-            const float p0 = (j <= r) ? f[e] * __expf(cc.ci - cc.gcc[j]) : 0.f;
-            const float p1 = (j + 1 <= r) ? f[e + 1] * __expf(cc.ci - cc.gcc[j + 1]) : 0.f;
-            pk[e / 2] = pack_half2(p0, p1);
+          for (int q2 = 0; q2 < 2; ++q2) {   // 16 keys per step: A columns q*16.., P columns q*8..
+            const int q = h2 * 2 + q2, j0 = cb * 64 + q * 16;
+            uint32_t pk[8];
+            if (j0 > q4 * 32 + 31) {   // every key after every row of this warp (warp-uniform)
+#pragma unroll
+              for (int e = 0; e < 8; ++e) pk[e] = 0u;
+            } else if (q4 * 32 >= j0 + 15) {
+              // every row of the warp at or after every key: with l = j0 + 15, e^{c_i - c_j} = e^{c_i - c_l} e^{c_l - c_j},
+              // both factors <= 1; lane l's column factor is that of key j0 + (l & 15), passed round by shuffles
+              const float cl = cc.gcc[j0 + 15];
+              const float rowf = ex2_approx((cc.ci - cl) * kLog2e);
+              const float colf = ex2_approx((cl - cc.gcc[j0 + (lane & 15)]) * kLog2e);
+#pragma unroll
+              for (int e = 0; e < 16; e += 2) {
+                const int jj = q2 * 16 + e;
+                const float f0 = __shfl_sync(0xffffffffu, colf, e), f1 = __shfl_sync(0xffffffffu, colf, e + 1);
+                pk[e / 2] = pack_half2(__uint_as_float(av[jj]) * rowf * f0, __uint_as_float(av[jj + 1]) * rowf * f1);
+              }
+            } else {   // the keys around the diagonal: one exponential per element, masked causally
+              float4 gk[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) gk[i] = g4[q * 4 + i];
+#pragma unroll
+              for (int e = 0; e < 16; e += 2) {
+                const int jj = q2 * 16 + e, j = j0 + e;
+                const float4 g = gk[e >> 2];
+                const float g0 = (e & 2) ? g.z : g.x, g1 = (e & 2) ? g.w : g.y;
+                const float p0 = (j <= r) ? __uint_as_float(av[jj]) * ex2_approx(fmaf(-g0, kLog2e, ci2)) : 0.f;
+                const float p1 =
+                    (j + 1 <= r) ? __uint_as_float(av[jj + 1]) * ex2_approx(fmaf(-g1, kLog2e, ci2)) : 0.f;
+                pk[e / 2] = pack_half2(p0, p1);
+              }
+            }
+            tmem_st8(pa + q * 8, pk);
           }
-          tmem_st8(pa + q * 8, pk);
         }
         // 2. inter * e^c in place (intra accumulates on top)
         alive = mbar_wait_warp(bar_i, m & 1, abort_flag, s.err, 0x5e);
@@ -1032,9 +1062,14 @@ __global__ void __launch_bounds__(kP3_Threads, 1)
         const uint32_t xcol = kP3_TX + 128u * (uint32_t)((m - 1) % 3) + cb * 64;
         const uint32_t xr = trow + xcol;
 #pragma unroll
-        for (int sub = 0; sub < 4; ++sub) {
-          float om[16];
-          tmem_ld16_wait(xr + sub * 16, om);
+        for (int sub2 = 0; sub2 < 2; ++sub2) {
+          uint32_t o32[32];
+          tmem_ld32(xr + sub2 * 32, o32);
+          tmem_wait_ld();
+#pragma unroll
+          for (int sh = 0; sh < 2; ++sh) {
+          const int sub = sub2 * 2 + sh;
+          const float* om = reinterpret_cast<const float*>(o32) + sh * 16;
           uint32_t w[16];
 #pragma unroll
           for (int e4 = 0; e4 < 4; ++e4) {
@@ -1058,6 +1093,7 @@ __global__ void __launch_bounds__(kP3_Threads, 1)
             if (refill && (e & 1)) ow[e >> 1] = p3_load_ow(cc, e >> 1);
           }
           tmem_st16(xr + sub * 16, w);
+          }
         }
         tmem_wait_st();
         __syncwarp();

@@ -47,15 +47,7 @@ constexpr int kWP_SmemSV = kWP_D * kWP_SinkRows * 2;     // 8 KB: sink values^T 
 constexpr int kWP_Tiles = kWP_SmemQ + kWP_SmemK + kWP_SmemV + kWP_SmemSK + kWP_SmemSV;
 constexpr int kWP_Smem = kWP_Tiles + 256 + 4096 + 1024;   // + barriers + row exchanges (3 KB) + alignment
 constexpr float kRescaleLog2 = 8.0f;              // rescale O when the max grows by more than 2^8
-constexpr float kLog2e = 1.4426950408889634f;
-constexpr float kLn2 = 0.6931471805599453f;
 constexpr uint32_t kTmO = 256;                    // TMEM column of O
-
-__device__ __forceinline__ float ex2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
 
 __device__ __forceinline__ float max3f(float x, float y, float z) {
   float r;
