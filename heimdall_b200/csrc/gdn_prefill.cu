@@ -369,8 +369,10 @@ __global__ void __launch_bounds__(kP1_Threads, 1)
   inverse_doubling_level<64, 4, 4, 1, 2>(A, Tm, X, t);
   // ---- T -> T_u = T diag(beta) and T_w = T diag(beta e^c), fp16 SW128 tiles (rows i, K = j) over A: then
   //      u = T_u V and w = T_w K take the value and key tiles as they lie (token rows, MN-major B operands)
-  for (int p = t; p < 128 * 16; p += kP1_Threads) {
-    const int i = p >> 4, ch = p & 15;  // chunk of 8 columns
+#pragma unroll 2
+  for (int ch = t >> 7; ch < 16; ch += kP1_Threads / 128) {   // chunk of 8 columns
+    // thread = row i: rows 528 bytes apart read distinct banks, the factors of the chunk are broadcasts
+    const int i = t & 127;
     const float4* tr = reinterpret_cast<const float4*>(Tm + i * kAS + ch * 8);
     const float4* bj = reinterpret_cast<const float4*>(s_beta + ch * 8);
     const float4* ej = reinterpret_cast<const float4*>(s_bec + ch * 8);
