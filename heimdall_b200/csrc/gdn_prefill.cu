@@ -308,17 +308,18 @@ __global__ void __launch_bounds__(kP1_Threads, 1)
     const uint32_t trow = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     const float br = s_beta[r], cr = s_gc[r];
 #pragma unroll 1
-    for (int c0 = cbase; c0 < cbase + 64; c0 += 16) {
-      float f[16];
-      tmem_ld16_wait(trow + c0, f);
+    for (int c1 = cbase; c1 < cbase + 64; c1 += 32) {   // 32 columns per TMEM read
+      uint32_t fa[32];
+      tmem_ld32(trow + c1, fa);
+      tmem_wait_ld();
 #pragma unroll
-      for (int e = 0; e < 16; ++e) {
-        const int j = c0 + e;
-        f[e] = (j < r && alive) ? br * __expf(cr - s_gc[j]) * f[e] : 0.f;
+      for (int e = 0; e < 32; ++e) {
+        const int j = c1 + e;
+        fa[e] = __float_as_uint((j < r && alive) ? br * __expf(cr - s_gc[j]) * __uint_as_float(fa[e]) : 0.f);
       }
 #pragma unroll
-      for (int e = 0; e < 16; e += 4)   // rows 528 bytes apart: the 16-byte stores of 8 lanes hit 8 bank groups
-        *reinterpret_cast<float4*>(A + r * kAS + c0 + e) = make_float4(f[e], f[e + 1], f[e + 2], f[e + 3]);
+      for (int e = 0; e < 32; e += 4)   // rows 528 bytes apart: the 16-byte stores of 8 lanes hit 8 bank groups
+        *reinterpret_cast<uint4*>(A + r * kAS + c1 + e) = make_uint4(fa[e], fa[e + 1], fa[e + 2], fa[e + 3]);
     }
   }
   tc_fence_before();
@@ -454,15 +455,21 @@ __global__ void __launch_bounds__(kP1_Threads, 1)
     const uint32_t trow = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (is_w ? 256u : 0u);
     uint8_t* tile = is_w ? regK : regT;
 #pragma unroll 1
-    for (int c0 = 0; c0 < 256; c0 += 16) {
-      float f[16];
-      tmem_ld16_wait(trow + c0, f);
-      uint8_t* at = tile + (c0 >> 6) * (128 * 128);
-      *reinterpret_cast<uint4*>(at + sw128_offset(r, c0 & 63)) =
-          make_uint4(pack_half2(f[0], f[1]), pack_half2(f[2], f[3]), pack_half2(f[4], f[5]), pack_half2(f[6], f[7]));
-      *reinterpret_cast<uint4*>(at + sw128_offset(r, (c0 & 63) + 8)) =
-          make_uint4(pack_half2(f[8], f[9]), pack_half2(f[10], f[11]), pack_half2(f[12], f[13]),
-                     pack_half2(f[14], f[15]));
+    for (int c1 = 0; c1 < 256; c1 += 64) {   // 64 columns (one atom) per TMEM wait
+      uint32_t fa[64];
+      tmem_ld32(trow + c1, *reinterpret_cast<uint32_t(*)[32]>(fa));
+      tmem_ld32(trow + c1 + 32, *reinterpret_cast<uint32_t(*)[32]>(fa + 32));
+      tmem_wait_ld();
+      uint8_t* at = tile + (c1 >> 6) * (128 * 128);
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        const uint32_t* f = fa + ch * 8;
+        *reinterpret_cast<uint4*>(at + sw128_offset(r, ch * 8)) =
+            make_uint4(pack_half2(__uint_as_float(f[0]), __uint_as_float(f[1])),
+                       pack_half2(__uint_as_float(f[2]), __uint_as_float(f[3])),
+                       pack_half2(__uint_as_float(f[4]), __uint_as_float(f[5])),
+                       pack_half2(__uint_as_float(f[6]), __uint_as_float(f[7])));
+      }
     }
   }
   fence_async_smem();
