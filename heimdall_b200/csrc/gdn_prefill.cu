@@ -626,6 +626,9 @@ __global__ void __launch_bounds__(kP2_Threads, 1)
     float lsum = 0.f;   // map path: log of the cumulative decay
     for (int j = 0; j < ncl && alive; ++j) {
       const int c = c_begin + j;
+      // the chunk's decays, read first so that they are in registers when the products need them
+      const float* gcc = s.gc + (size_t)bg * s.n_pad + (size_t)c * kGC;
+      const float lgc = gcc[kGC - 1], gcr = gcc[r];
       // stage S^T (fp16) as the B operand of v' = u - w S, and store it for P3
 #pragma unroll
       for (int e = 0; e < kP2_NB; ++e) {
@@ -662,14 +665,13 @@ __global__ void __launch_bounds__(kP2_Threads, 1)
           }
         }
       }
+      // the state update's B operand carries the decay to the chunk end: (e^{c_C - c_r} v'_r)^T
+      const float ect = __expf(lgc - gcr);
       if (!mbar_wait_warp(bar_m1, j & 1, abort_flag, s.err, 0x59)) { alive = false; break; }
       tc_fence_after();
       float dv[kP2_NB];
 #pragma unroll
       for (int q = 0; q < kP2_NB; q += 16) tmem_ld16_wait(trow + q, *reinterpret_cast<float(*)[16]>(dv + q));
-      // the state update's B operand carries the decay to the chunk end: (e^{c_C - c_r} v'_r)^T
-      const float* gcc = s.gc + (size_t)bg * s.n_pad + (size_t)c * kGC;
-      const float ect = __expf(gcc[kGC - 1] - gcc[r]);
 #pragma unroll
       for (int e = 0; e < kP2_NB; ++e) st_half_sw128(sVT, kP2_NB, e, r, (uu[e] - dv[e]) * ect);
       if (keep) {
@@ -680,7 +682,6 @@ __global__ void __launch_bounds__(kP2_Threads, 1)
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(bar_vt);
-      const float lgc = s.gc[(size_t)bg * s.n_pad + (size_t)c * kGC + kGC - 1];
       const float decay = __expf(lgc);
       if (!mbar_wait_warp(bar_m2, j & 1, abort_flag, s.err, 0x5a)) { alive = false; break; }
       tc_fence_after();
