@@ -491,7 +491,7 @@ __global__ void __launch_bounds__(kP1_Threads, 1)
 constexpr int kP2_NB = 32;               // state columns per CTA
 constexpr int kP2_Threads = 192;         // warps 0-3 state/epilogue, warp 4 TMA, warp 5 MMA
 constexpr int kP2_SmemW = kGC * kGD * 2;          // 64 KB
-constexpr int kP2_SmemKT = kGD * kGC * 2;         // 64 KB
+constexpr int kP2_SmemKT = kGD * kGC * 2;         // 64 KB: the chunk's fp16 key tile [128 tokens][256]
 constexpr int kP2_SmemST = kP2_NB * kGD * 2;      // 8 KB
 constexpr int kP2_SmemVT = kP2_NB * kGC * 2;      // 4 KB
 constexpr int kP2_Smem = kP2_SmemW + kP2_SmemKT + kP2_SmemST + kP2_SmemVT + 1024 + 256;
@@ -507,7 +507,7 @@ __global__ void __launch_bounds__(kP2_Threads, 1)
   uint8_t* sVT = sST + kP2_SmemST;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sVT + kP2_SmemVT);
   uint64_t* bar_w = bars + 0;      // w tile landed
-  uint64_t* bar_kt = bars + 1;     // k_tail^T tile landed
+  uint64_t* bar_kt = bars + 1;     // key tile landed
   uint64_t* bar_st = bars + 2;     // S^T staged (128)
   uint64_t* bar_vt = bars + 3;     // v'^T staged (128)
   uint64_t* bar_m1 = bars + 4;     // v' product done
