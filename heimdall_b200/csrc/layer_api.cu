@@ -15,6 +15,7 @@ int launch_x_proj(const __nv_bfloat16* x, const __nv_bfloat16* w_x, const float*
                   float* scratch, size_t scratch_bytes, unsigned int* err, cudaStream_t stream);
 
 size_t win_dec_workspace(int B, int G, int R, int D, int W);
+size_t x_proj_scratch_bytes(int M, int d);
 int launch_gather_evicted(const float* ring_km, const __nv_bfloat16* ring_v, const float* ring_g,
                           const float* ring_beta, const int64_t* ring_pos, long long ring_pos_bstride,
                           const int64_t* pos, int B, int G, int W, int D, float* k_e, float* v_e, float* g_e,
@@ -158,10 +159,36 @@ int bf_bifrost_layer_decode(const bf_layer* L, const void* x, const void* q, con
   float* o_mem = reinterpret_cast<float*>(take((size_t)B * H * D * 4));
   float* part = reinterpret_cast<float*>(take(win_dec_workspace(B, G, R, D, W)));
 
-  // memory inputs of the new tokens (T = 1 per sequence, per-sequence positions)
-  // o_mem is first written by the state update, after the projections: it is their split-K scratch
-  rc = mem_inputs_impl(st, L, x, q, k, pos, 0, B, 1, qm, km, g, beta, mixx, stream, nullptr, o_mem,
-                       (size_t)B * H * D * 4);
+  // memory inputs of the new tokens (T = 1 per sequence, per-sequence positions).  The gate projections (g, beta
+  // and the mix logit of the new tokens) feed only the window kernels' last step, so when the window's split
+  // partials (written by its first kernel, after the state update) can hold their split-K partials, they run
+  // on the greatest-priority side stream beside the head projections, the evicted-entry gather and the state
+  // update, and are joined before the window.  Otherwise they run in line with o_mem (written first by the
+  // state update) as their scratch.
+  const size_t part_bytes = win_dec_workspace(B, G, R, D, W);
+  const size_t xs_need = x_proj_scratch_bytes(B, L->d);
+  cudaStream_t sx = (xs_need > 0 && xs_need <= part_bytes) ? side_stream(st, 1) : nullptr;
+  cudaEvent_t ev_fork = nullptr, ev_x = nullptr;
+  if (sx) {
+    if (cudaEventCreateWithFlags(&ev_fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ev_x, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventRecord(ev_fork, stream) != cudaSuccess || cudaStreamWaitEvent(sx, ev_fork, 0) != cudaSuccess)
+      return cuda_fail();
+    stage_mark(ST_XPROJ, 0, sx);
+    rc = launch_x_proj(static_cast<const __nv_bfloat16*>(x), weights_x(L->wbuf, L->H, L->G, L->D), L->ab_b,
+                       L->mix_b, L->A_log, L->dt_bias, L->decay_mask, g, beta, mixx, pos, 0, B, 1, L->d, L->G, L->H,
+                       L->sinks, part, part_bytes, st.err, sx);
+    if (rc) return rc;
+    stage_mark(ST_XPROJ, 1, sx);
+    if (cudaEventRecord(ev_x, sx) != cudaSuccess) return cuda_fail();
+    stage_mark(ST_HEADPROJ, 0, stream);
+    rc = launch_head_proj(static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
+                          weights_heads(L->wbuf), qm, nullptr, km, 1, B, L->H, L->G, st.sm_count, st.err, stream);
+    stage_mark(ST_HEADPROJ, 1, stream);
+  } else {
+    rc = mem_inputs_impl(st, L, x, q, k, pos, 0, B, 1, qm, km, g, beta, mixx, stream, nullptr, o_mem,
+                         (size_t)B * H * D * 4);
+  }
   if (rc) return rc;
   if (memory) {
     // the token leaving the window (position p - W) is written into memory before the read
@@ -207,6 +234,11 @@ int bf_bifrost_layer_decode(const bf_layer* L, const void* x, const void* q, con
   a.ring_g = C->ring_g;
   a.ring_beta = C->ring_beta;
   a.ring_pos_w = C->ring_pos;
+  if (sx) {   // join the gate projections: the window's partials were their scratch
+    if (cudaStreamWaitEvent(stream, ev_x, 0) != cudaSuccess) return cuda_fail();
+    cudaEventDestroy(ev_fork);
+    cudaEventDestroy(ev_x);
+  }
   stage_mark(ST_DEC_WIN, 0, stream);
   rc = launch_win_dec(a, stream);
   stage_mark(ST_DEC_WIN, 1, stream);
