@@ -261,6 +261,10 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
             umma_commit(o_fin);
           }
         }
+        // the sink scores need only the queries and the staged sink keys: issued before the first key tile has
+        // landed, so the softmax warps form P_sink while it loads (the S buffer they use was last read by a
+        // product issued before this point)
+        if (w.n > 0) ok = sink_scores();
         for (int j = 0; j < w.n && ok; ++j) {
           const int tt = t + j, s = tt & 1;
           ok = mbar_wait(k_full, tt & 1, abort_flag, a.err, 0x39);
@@ -271,7 +275,7 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
             umma_f16_ss(tmem + s * kWP_N, sdesc_kstep(aQ, kWP_M, ks), sdesc_kstep(bK, kWP_N, ks), idesc_qk, ks > 0);
           umma_commit(k_empty);
           umma_commit(&s_full[s]);
-          if (j == 0) ok = sink_scores() && sink_pv();
+          if (j == 0) ok = sink_pv();
           if (ok && j == w.n - 1) umma_commit(q_free);
           if (ok && j >= 1) ok = issue_pv(j - 1, tt - 1);
         }
