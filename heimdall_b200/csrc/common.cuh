@@ -131,6 +131,11 @@ __device__ __forceinline__ void fence_async_smem() {
 
 // ----------------------------------------------------------------------------------------------
 // TMA loads (tiled, one CTA per load).  `tmap` is the generic address of a __grid_constant__ CUtensorMap.
+// L2 prefetch of a tensor-map tile (no shared memory, no completion to wait for)
+__device__ __forceinline__ void tma_prefetch_tile_3d(const void* tmap, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2) : "memory");
+}
 __device__ __forceinline__ void prefetch_l2(const void* p) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(p)));
 }

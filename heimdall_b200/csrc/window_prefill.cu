@@ -182,6 +182,14 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
           if (t >= 1 && !(ok = mbar_wait(k_empty, (t - 1) & 1, abort_flag, a.err, 0x31))) break;
           mbar_expect_tx(k_full, kWP_SmemK);
           tma_load_3d(sK, &kmap, k_full, 0, (w.b * a.G + w.g) * a.Tk + (w.jt0 + j) * kWP_N, 0);
+          // one item per CTA: behind this item's first loads, the item about one wave of CTAs later
+          // (pf_stride = the SM count) gets its queries and first key tile into L2, so that they arrive from L2
+          // when its CTA starts
+          if (j == 0 && a.pf_stride && u + a.pf_stride < nitems) {
+            const WItem wn = win_item(a, u + a.pf_stride, ntq);
+            tma_prefetch_tile_3d(&qmap, 0, (wn.b * a.H + wn.h) * a.Tq + wn.i0, 0);
+            if (wn.n > 0) tma_prefetch_tile_3d(&kmap, 0, (wn.b * a.G + wn.g) * a.Tk + wn.jt0 * kWP_N, 0);
+          }
         }
       }
       // drain: every load issued has landed before the CTA may exit
@@ -645,6 +653,7 @@ int launch_window_prefill(const void* qr, const void* kext, const __half* vt, Wi
   const long long nitems = (long long)a.B * ((a.Tq + kWP_M - 1) / kWP_M) * a.H;
   if (nitems == 0) return BF_OK;
   const long long grid = a.persistent ? (nitems < sms ? nitems : sms) : nitems;
+  a.pf_stride = a.persistent ? 0 : sms;
   window_prefill_kernel<<<(unsigned)grid, kWP_Threads, kWP_Smem, stream>>>(qmap, kmap, vmap, a);
   return launch_status();
 }

@@ -31,6 +31,7 @@ struct WinPreArgs {
   // launch: one CTA per SM walking the items (fastest alone), or one CTA per item (lets concurrent kernels on
   // other streams take SMs as CTAs finish: the layer prefill, where the memory chain runs beside the window)
   int persistent;
+  int pf_stride;        // set by the launcher: one item per CTA prefetches item + pf_stride into L2 (0: none)
   unsigned int* err;
 };
 
