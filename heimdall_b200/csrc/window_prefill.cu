@@ -315,30 +315,34 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
       const long long p = w.P0 + r;              // position of this query
       const uint32_t sbc = (uint32_t)((t + 1) & 1) * kWP_N;   // S buffer of the sink scores and P_sink
       // sink keys -> K-major swizzled B operand (rows >= ns zero); sink values^T -> fp16 B operand (keys >= ns
-      // zero).  The previous item's sink products finished before its O was complete
-      for (int i = st; i < kWP_SinkRows * (kWP_D / 8); i += 256) {
-        const int e = i / (kWP_D / 8), c = i % (kWP_D / 8);
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      // zero).  The previous item's sink products finished before its O was complete.  Every load is issued
+      // before the first store, so the staging costs one round trip to L2
+      static_assert(kWP_SinkRows * (kWP_D / 8) == 2 * 256, "two 16-byte sink-key chunks per thread");
+      uint4 skc[2];
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int i = st + q * 256, e = i / (kWP_D / 8), c = i % (kWP_D / 8);
+        skc[q] = make_uint4(0u, 0u, 0u, 0u);
         if (e < ns)
-          v = __ldg(reinterpret_cast<const uint4*>(a.sink_k + (size_t)w.b * a.sk_b + (size_t)w.g * a.sk_h +
-                                                   (size_t)e * a.sk_k) + c);
-        *reinterpret_cast<uint4*>(sSK + (c >> 3) * (kWP_SinkRows * 128) + e * 128 + (((c & 7) ^ (e & 7)) << 4)) = v;
+          skc[q] = __ldg(reinterpret_cast<const uint4*>(a.sink_k + (size_t)w.b * a.sk_b + (size_t)w.g * a.sk_h +
+                                                        (size_t)e * a.sk_k) + c);
+      }
+      float svl[kWP_SinkRows];   // the sink values of value column st
+#pragma unroll
+      for (int e = 0; e < kWP_SinkRows; ++e)
+        svl[e] = (e < ns) ? __bfloat162float(a.sink_v[(size_t)w.b * a.sv_b + (size_t)w.g * a.sv_h + (size_t)e * a.sv_k + st])
+                          : 0.f;
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int i = st + q * 256, e = i / (kWP_D / 8), c = i % (kWP_D / 8);
+        *reinterpret_cast<uint4*>(sSK + (c >> 3) * (kWP_SinkRows * 128) + e * 128 + (((c & 7) ^ (e & 7)) << 4)) = skc[q];
       }
       if (ns > 0) {
-        const int d = st;   // one value column per thread, the 16 sink keys of it
         uint32_t hv[8];
 #pragma unroll
-        for (int e2 = 0; e2 < 8; ++e2) {
-          float f0 = 0.f, f1 = 0.f;
-          if (2 * e2 < ns)
-            f0 = __bfloat162float(a.sink_v[(size_t)w.b * a.sv_b + (size_t)w.g * a.sv_h + (size_t)(2 * e2) * a.sv_k + d]);
-          if (2 * e2 + 1 < ns)
-            f1 = __bfloat162float(
-                a.sink_v[(size_t)w.b * a.sv_b + (size_t)w.g * a.sv_h + (size_t)(2 * e2 + 1) * a.sv_k + d]);
-          hv[e2] = pack_half2(f0, f1);
-        }
-        *reinterpret_cast<uint4*>(sSV + sv_off(d, 0)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-        *reinterpret_cast<uint4*>(sSV + sv_off(d, 8)) = make_uint4(hv[4], hv[5], hv[6], hv[7]);
+        for (int e2 = 0; e2 < 8; ++e2) hv[e2] = pack_half2(svl[2 * e2], svl[2 * e2 + 1]);
+        *reinterpret_cast<uint4*>(sSV + sv_off(st, 0)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+        *reinterpret_cast<uint4*>(sSV + sv_off(st, 8)) = make_uint4(hv[4], hv[5], hv[6], hv[7]);
       }
       fence_async_smem();
       __syncwarp();
