@@ -9,6 +9,8 @@ sees the same constant footprint.
 """
 from __future__ import annotations
 
+import weakref
+
 import torch
 
 from . import _lib
@@ -199,13 +201,20 @@ class BifrostLayer:
         """First phase of a sequence-parallel layer prefill of this rank's tokens (``heimdall_b200.sp``):
         the memory inputs, the per-chunk products and this segment's state map.  ``cache`` holds the ring
         (the W tokens before ``start``) and the sinks; its "S" is replaced by the incoming state before
-        ``prefill_sp_finish``.  Returns (M, N, handle): S_out = M S_in + N for the segment's write stream."""
+        ``prefill_sp_finish``.  Returns (M, N, handle): S_out = M S_in + N for the segment's write stream.
+
+        The window attention of the segment is still running when this returns (it is joined by
+        ``prefill_sp_finish``) and uses buffers that the handle holds; a handle dropped without
+        ``prefill_sp_finish`` waits for the device before those buffers are released."""
         check_cuda(x, q, k, v, qr, kr)
-        c = self._prefill_setup(x, q, k, v, qr, kr, int(start), cache, True)
+        c = _SpHandle(self._prefill_setup(x, q, k, v, qr, kr, int(start), cache, True))
         B, G, D = c["B"], self.G, self.D
         M = torch.empty(B, G, D, D, device=x.device, dtype=torch.float32)
         N = torch.empty_like(M)
         self._prefill_sp_call(c, 0, M, N)
+        done = [False]
+        c["_joined"] = done
+        weakref.finalize(c, _sp_abandoned, x.device, done)
         return M, N, c
 
     def prefill_sp_finish(self, handle):
@@ -215,6 +224,7 @@ class BifrostLayer:
         if c["rc"] is not None and "S" in cache:
             c["rc"].S = ptr(cache["S"])
         self._prefill_sp_call(c, 1, None, None)
+        c["_joined"][0] = True
         self._finish_cache(c)
         return c["o"]
 
@@ -391,3 +401,13 @@ def ctypes_ref(s):
     """Address of a ctypes struct, for the c_void_p struct-pointer arguments (the struct outlives the call)."""
     import ctypes
     return ctypes.addressof(s)
+
+
+class _SpHandle(dict):
+    """The state of a sequence-parallel prefill between its two phases (a dict that can carry a finalizer)."""
+
+
+def _sp_abandoned(device, done):
+    # a first phase whose second never ran: its window kernel may still use the handle's buffers
+    if not done[0]:
+        torch.cuda.synchronize(device)

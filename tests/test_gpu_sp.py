@@ -211,3 +211,36 @@ def test_two_phase_prefill_matches_one_call():
     M2, N2 = segment_transform(kw, vw, gw, bw)
     torch.cuda.synchronize()
     assert ob.rel_l2(M.cpu(), M2.cpu()) < 1e-5 and ob.rel_l2(N.cpu(), N2.cpu()) < 1e-5
+
+
+def test_abandoned_first_phase_is_safe():
+    """A first phase whose handle is dropped without the second phase: its window kernel (still running on a
+    side stream when prefill_sp_begin returns) is waited for before the handle's buffers are released, so a
+    prefill that reuses the memory right after is unaffected."""
+    import gc
+    dev = _dev()
+    from heimdall_b200 import BifrostLayer, sp
+    H, G, D, d, W, S, T = 24, 4, 256, 128, 256, 4, 700
+    p = layer_params(H, G, D, d, window=W, sinks=S, archival=1, seed=12)
+    L = BifrostLayer.from_params(p, dev)
+    x, q, k, v, qr, kr = (z.to(dev) for z in _layer_inputs(H, G, D, d, 2 * T, seed=13))
+    start = T
+    halo = [x[:, T - W:T].contiguous(), k[:, T - W:T].contiguous(), v[:, T - W:T].contiguous(),
+            kr[:, :, T - W:T].contiguous()]
+    mine = [x[:, T:].contiguous(), q[:, T:].contiguous(), k[:, T:].contiguous(), v[:, T:].contiguous(),
+            qr[:, :, T:].contiguous(), kr[:, :, T:].contiguous()]
+    km_h, g_h, b_h = sp._halo_inputs(L, halo, start, W, mine[1])
+    sink_k, sink_v = kr[:, :, :S].contiguous(), v[:, :S].transpose(1, 2).contiguous()
+    S_in = torch.randn(1, G, D, D, generator=torch.Generator().manual_seed(3)).to(dev) * 0.05
+    c0 = sp.halo_cache(halo[3], halo[2], km_h, g_h, b_h, sink_k, sink_v, None, start, W)
+    _, _, h = L.prefill_sp_begin(*mine, start, c0)
+    del h
+    gc.collect()
+    c1 = sp.halo_cache(halo[3], halo[2], km_h, g_h, b_h, sink_k, sink_v, S_in.clone(), start, W)
+    o1 = L.student(*mine, start, c1)
+    c2 = sp.halo_cache(halo[3], halo[2], km_h, g_h, b_h, sink_k, sink_v, None, start, W)
+    _, _, h2 = L.prefill_sp_begin(*mine, start, c2)
+    c2["S"].copy_(S_in)
+    o2 = L.prefill_sp_finish(h2)
+    torch.cuda.synchronize()
+    assert ob.rel_l2(o2.cpu(), o1.cpu()) < 1e-6
