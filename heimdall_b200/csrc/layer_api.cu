@@ -169,18 +169,29 @@ int bf_bifrost_layer_decode(const bf_layer* L, const void* x, const void* q, con
   const size_t xs_need = x_proj_scratch_bytes(B, L->d);
   cudaStream_t sx = (xs_need > 0 && xs_need <= part_bytes) ? side_stream(st, 1) : nullptr;
   cudaEvent_t ev_fork = nullptr, ev_x = nullptr;
+  auto drop_events = [&]() {
+    if (ev_fork) cudaEventDestroy(ev_fork);
+    if (ev_x) cudaEventDestroy(ev_x);
+    ev_fork = ev_x = nullptr;
+  };
   if (sx) {
     if (cudaEventCreateWithFlags(&ev_fork, cudaEventDisableTiming) != cudaSuccess ||
         cudaEventCreateWithFlags(&ev_x, cudaEventDisableTiming) != cudaSuccess ||
-        cudaEventRecord(ev_fork, stream) != cudaSuccess || cudaStreamWaitEvent(sx, ev_fork, 0) != cudaSuccess)
-      return cuda_fail();
+        cudaEventRecord(ev_fork, stream) != cudaSuccess || cudaStreamWaitEvent(sx, ev_fork, 0) != cudaSuccess) {
+      rc = cuda_fail();
+      drop_events();
+      return rc;
+    }
     stage_mark(ST_XPROJ, 0, sx);
     rc = launch_x_proj(static_cast<const __nv_bfloat16*>(x), weights_x(L->wbuf, L->H, L->G, L->D), L->ab_b,
                        L->mix_b, L->A_log, L->dt_bias, L->decay_mask, g, beta, mixx, pos, 0, B, 1, L->d, L->G, L->H,
                        L->sinks, part, part_bytes, st.err, sx);
-    if (rc) return rc;
+    if (!rc && cudaEventRecord(ev_x, sx) != cudaSuccess) rc = cuda_fail();
+    if (rc) {
+      drop_events();
+      return rc;
+    }
     stage_mark(ST_XPROJ, 1, sx);
-    if (cudaEventRecord(ev_x, sx) != cudaSuccess) return cuda_fail();
     stage_mark(ST_HEADPROJ, 0, stream);
     rc = launch_head_proj(static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
                           weights_heads(L->wbuf), qm, nullptr, km, 1, B, L->H, L->G, st.sm_count, st.err, stream);
@@ -189,15 +200,24 @@ int bf_bifrost_layer_decode(const bf_layer* L, const void* x, const void* q, con
     rc = mem_inputs_impl(st, L, x, q, k, pos, 0, B, 1, qm, km, g, beta, mixx, stream, nullptr, o_mem,
                          (size_t)B * H * D * 4);
   }
-  if (rc) return rc;
+  if (rc) {
+    drop_events();
+    return rc;
+  }
   if (memory) {
     // the token leaving the window (position p - W) is written into memory before the read
     rc = launch_gather_evicted(C->ring_km, static_cast<const __nv_bfloat16*>(C->ring_v), C->ring_g, C->ring_beta,
                                C->ring_pos, C->ring_pos_bstride, pos, B, G, W, D, k_e, v_e, g_e, b_e, stream);
-    if (rc) return rc;
+    if (rc) {
+      drop_events();
+      return rc;
+    }
     stage_mark(ST_DEC_STATE, 0, stream);
     rc = launch_gdn_decode(qm, k_e, v_e, 0, g_e, b_e, C->S, C->S, o_mem, B, G, R, D, stream);
-    if (rc) return rc;
+    if (rc) {
+      drop_events();
+      return rc;
+    }
     stage_mark(ST_DEC_STATE, 1, stream);
   }
   WinDecArgs a{};
@@ -235,9 +255,9 @@ int bf_bifrost_layer_decode(const bf_layer* L, const void* x, const void* q, con
   a.ring_beta = C->ring_beta;
   a.ring_pos_w = C->ring_pos;
   if (sx) {   // join the gate projections: the window's partials were their scratch
-    if (cudaStreamWaitEvent(stream, ev_x, 0) != cudaSuccess) return cuda_fail();
-    cudaEventDestroy(ev_fork);
-    cudaEventDestroy(ev_x);
+    rc = cudaStreamWaitEvent(stream, ev_x, 0) != cudaSuccess ? cuda_fail() : BF_OK;
+    drop_events();
+    if (rc) return rc;
   }
   stage_mark(ST_DEC_WIN, 0, stream);
   rc = launch_win_dec(a, stream);
