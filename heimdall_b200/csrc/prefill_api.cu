@@ -296,7 +296,18 @@ static int layer_prefill_impl(const bf_layer* L, const void* x, const void* q, c
   const bool win_here = phase == kPhaseAll || (phase == kPhaseBegin) == reads_later;
   cudaStream_t ws2 = stream;   // (a null handle is the legacy default stream, a valid stream)
   cudaStream_t wsm = stream;   // the memory chain
-  cudaEvent_t ev_fork = nullptr, ev_win = nullptr, ev_mem = nullptr;
+  // the fork/join events are released when the call returns, on every path (an event recorded for work still
+  // in flight may be destroyed: the release is deferred until that work completes)
+  struct Events {
+    cudaEvent_t fork = nullptr, win = nullptr, mem = nullptr;
+    ~Events() {
+      for (cudaEvent_t e : {fork, win, mem})
+        if (e) cudaEventDestroy(e);
+    }
+  } evs;
+  cudaEvent_t& ev_fork = evs.fork;
+  cudaEvent_t& ev_win = evs.win;
+  cudaEvent_t& ev_mem = evs.mem;
   if (reads_later && phase == kPhaseFinish) {
     // the scan from the incoming state goes on the high-priority stream too, ahead of the window's CTAs
     // still waiting for SMs; it is joined before the reads
@@ -382,53 +393,36 @@ static int layer_prefill_impl(const bf_layer* L, const void* x, const void* q, c
           cudaEventRecord(ev_win, wsw) != cudaSuccess || cudaStreamWaitEvent(stream, ev_win, 0) != cudaSuccess ||
           cudaEventRecord(ev_mem, wsm) != cudaSuccess || cudaStreamWaitEvent(stream, ev_mem, 0) != cudaSuccess)
         return cuda_fail();
-      cudaEventDestroy(ev_win);
-      cudaEventDestroy(ev_mem);
-      cudaEventDestroy(ev_fork);
-      ev_win = ev_mem = ev_fork = nullptr;
     }
-    if (phase == kPhaseBegin) {
-      if (ev_fork) cudaEventDestroy(ev_fork);
-      if (ev_win) cudaEventDestroy(ev_win);
-      if (ev_mem) cudaEventDestroy(ev_mem);
-      return BF_OK;
-    }
+    if (phase == kPhaseBegin) return BF_OK;
   }
   // 3. window attention over the extended keys (o = window result, lse), on the side stream when forked
   const void* kx = kr;
   if (win_here) {
-  stage_mark(ST_WIN_PREP, 0, ws2);
-  if (ring_case) {
-    rc = launch_kext_prep(static_cast<const __nv_bfloat16*>(kr), static_cast<const __nv_bfloat16*>(C->ring_k), W,
-                          start - W, W, B, T, G, kext, ws2);
+    stage_mark(ST_WIN_PREP, 0, ws2);
+    if (ring_case) {
+      rc = launch_kext_prep(static_cast<const __nv_bfloat16*>(kr), static_cast<const __nv_bfloat16*>(C->ring_k), W,
+                            start - W, W, B, T, G, kext, ws2);
+      if (rc) return rc;
+      kx = kext;
+    }
+    rc = launch_vt_prep(static_cast<const __nv_bfloat16*>(v), (long long)T * G * D, D, (long long)G * D,
+                        ring_case ? static_cast<const __nv_bfloat16*>(C->ring_v) : nullptr, ring_case ? W : 0,
+                        start - W, W, B, G, Tk, Tkp, vt, ws2);
     if (rc) return rc;
-    kx = kext;
+    stage_mark(ST_WIN_PREP, 1, ws2);
+    stage_mark(ST_WIN, 0, ws2);
+    rc = window_common(qr, kx, vt, sink_k, sink_v, ns, start, ring_case ? start - W : start, L->sinks, B, H, G, T,
+                       Tk, W, o, lse_w, st.err, ws2, reads_later ? const_cast<__half*>(s.owin) : nullptr,
+                       s.qoff / kGC, s.n_chunks, will_read ? 0 : 1);
+    if (rc) return rc;
+    stage_mark(ST_WIN, 1, ws2);
   }
-  rc = launch_vt_prep(static_cast<const __nv_bfloat16*>(v), (long long)T * G * D, D, (long long)G * D,
-                      ring_case ? static_cast<const __nv_bfloat16*>(C->ring_v) : nullptr, ring_case ? W : 0,
-                      start - W, W, B, G, Tk, Tkp, vt, ws2);
-  if (rc) return rc;
-  stage_mark(ST_WIN_PREP, 1, ws2);
-  stage_mark(ST_WIN, 0, ws2);
-  rc = window_common(qr, kx, vt, sink_k, sink_v, ns, start, ring_case ? start - W : start, L->sinks, B, H, G, T, Tk, W,
-                     o, lse_w, st.err, ws2, reads_later ? const_cast<__half*>(s.owin) : nullptr, s.qoff / kGC,
-                     s.n_chunks, will_read ? 0 : 1);
-  if (rc) return rc;
-  stage_mark(ST_WIN, 1, ws2);
-  }
-  if (phase == kPhaseBegin) {   // the window stays on its stream until the second phase
-    cudaEventDestroy(ev_fork);
-    cudaEventDestroy(ev_win);
-    cudaEventDestroy(ev_mem);
-    return BF_OK;
-  }
+  if (phase == kPhaseBegin) return BF_OK;   // the window stays on its stream until the second phase
   if (will_read) {
     if (cudaEventRecord(ev_win, ws2) != cudaSuccess || cudaEventRecord(ev_mem, wsm) != cudaSuccess ||
         cudaStreamWaitEvent(stream, ev_win, 0) != cudaSuccess || cudaStreamWaitEvent(stream, ev_mem, 0) != cudaSuccess)
       return cuda_fail();
-    cudaEventDestroy(ev_fork);
-    cudaEventDestroy(ev_win);
-    cudaEventDestroy(ev_mem);
   }
   // 4. memory reads, mixed into o by the gate
   if (reads) {
