@@ -170,3 +170,52 @@ def test_layer_decode_early_positions_sinks():
         assert ob.rel_l2(o.cpu(), o_ref) < O_TOL, i
     assert gcache["sink_k"].shape == cache["sink_k"].shape
     assert ob.rel_l2(gcache["S"].cpu(), cache["S"]) < S_TOL
+
+
+def test_layer_decode_graph_replay_matches_eager():
+    """The fused decode step captured in a CUDA graph (its gate projections run on a forked stream inside the
+    capture) leaves the same outputs and cache as the same step run eagerly."""
+    dev = _dev()
+    from heimdall_b200 import BifrostLayer, _lib
+    from heimdall_b200.functional import ptr
+    from heimdall_b200.layer import ctypes_ref
+    from heimdall_b200.structs import BfRingCache
+    H, G, D, d, W, S = 24, 4, 256, 128, 16, 4
+    p = layer_params(H, G, D, d, window=W, sinks=S, archival=1, seed=5)
+    T0, B = 40, 2
+    x, q, k, v, qr, kr = _layer_inputs(H, G, D, d, T0 + 1, seed=13, B=B)
+    f = lambda z: z.float()
+    cache = {}
+    ob.student(p, f(x[:, :T0]), f(q[:, :T0]), f(k[:, :T0]), f(v[:, :T0]), f(qr[:, :, :T0]), f(kr[:, :, :T0]), 0,
+               cache)
+    L = BifrostLayer.from_params(p, dev)
+    step = [z.to(dev).contiguous() for z in (x[:, T0], q[:, T0], k[:, T0], v[:, T0], qr[:, :, T0], kr[:, :, T0])]
+    pos = torch.full((B,), T0, dtype=torch.int64, device=dev)
+    nws = _lib.size("bf_layer_decode_workspace", B, H, G, D, W)
+
+    def make():
+        c = _cache_to(cache, dev)
+        st = BfRingCache(ptr(c["ring_k"]), ptr(c["ring_v"]), ptr(c["ring_km"]), ptr(c["ring_g"]), ptr(c["ring_beta"]),
+                         ptr(c["ring_pos"]), 0, ptr(c["sink_k"]), ptr(c["sink_v"]), S, ptr(c["S"]))
+        return c, st, torch.empty(B, H, D, device=dev), torch.empty(nws, dtype=torch.uint8, device=dev)
+
+    def call(st, o, ws, stream):
+        _lib.call("bf_bifrost_layer_decode", ctypes_ref(L.struct), *(ptr(z) for z in step), ptr(pos), B,
+                  ctypes_ref(st), 1, ptr(o), 0, ptr(ws), ws.numel(), stream)
+
+    ca, sta, oa, wsa = make()
+    call(sta, oa, wsa, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    cb, stb, ob_, wsb = make()
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        call(stb, ob_, wsb, s.cuda_stream)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert ob.rel_l2(ob_.cpu(), oa.cpu()) < 1e-6
+    for key in ("S", "ring_km", "ring_g", "ring_beta"):
+        assert ob.rel_l2(cb[key].cpu(), ca[key].cpu()) < 1e-6, key
+    assert torch.equal(cb["ring_k"].cpu(), ca["ring_k"].cpu()) and torch.equal(cb["ring_pos"].cpu(), ca["ring_pos"].cpu())
+    del graph
