@@ -232,12 +232,13 @@ __global__ void __launch_bounds__(kHP_Threads, 1)
       const uint32_t base = tmem + ((uint32_t)(warp * 32) << 16) + buf * 256;
       float ss = 0.f;
 #pragma unroll 1
-      for (int c = 0; c < kHP_D; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(base + c, r);
+      for (int c = 0; c < kHP_D; c += 64) {   // 64 columns per TMEM wait
+        uint32_t r[64];
+        tmem_ld32(base + c, *reinterpret_cast<uint32_t(*)[32]>(r));
+        tmem_ld32(base + c + 32, *reinterpret_cast<uint32_t(*)[32]>(r + 32));
         tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
+        for (int j = 0; j < 64; ++j) {
           const float x = __uint_as_float(r[j]);
           ss += x * x;
         }
@@ -245,22 +246,25 @@ __global__ void __launch_bounds__(kHP_Threads, 1)
       const float inv = out_scale / fmaxf(sqrtf(ss), 1e-12f);
       const bool row_ok = it.tile * kHP_M + row < a.T;
       const bool half_out = is_q && a.qm16 != nullptr;
-      // scaled (and for fp16 output packed into the first 16 columns of each 32) in place, then stored from TMEM
-      // in 16-row blocks: four threads write 32 contiguous bytes of a row
+      // scaled in place (for fp16 output packed two per column into columns 0..127: the 64 columns read at c
+      // land at c / 2, which the earlier reads have consumed), then stored from TMEM in 16-row blocks: four
+      // threads write 32 contiguous bytes of a row
 #pragma unroll 1
-      for (int c = 0; c < kHP_D; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(base + c, r);
+      for (int c = 0; c < kHP_D; c += 64) {
+        uint32_t r[64];
+        tmem_ld32(base + c, *reinterpret_cast<uint32_t(*)[32]>(r));
+        tmem_ld32(base + c + 32, *reinterpret_cast<uint32_t(*)[32]>(r + 32));
         tmem_wait_ld();
         if (half_out) {
-          uint32_t pk[16];
+          uint32_t pk[32];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) pk[j] = pack_half2(__uint_as_float(r[2 * j]) * inv, __uint_as_float(r[2 * j + 1]) * inv);
-          tmem_st16(base + c, pk);
+          for (int j = 0; j < 32; ++j) pk[j] = pack_half2(__uint_as_float(r[2 * j]) * inv, __uint_as_float(r[2 * j + 1]) * inv);
+          tmem_st32(base + c / 2, pk);
         } else {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * inv);
-          tmem_st32(base + c, r);
+          for (int j = 0; j < 64; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * inv);
+          tmem_st32(base + c, *reinterpret_cast<uint32_t(*)[32]>(r));
+          tmem_st32(base + c + 32, *reinterpret_cast<uint32_t(*)[32]>(r + 32));
         }
       }
       tmem_wait_st();
@@ -280,16 +284,17 @@ __global__ void __launch_bounds__(kHP_Threads, 1)
         }
         if (half_out) {
 #pragma unroll 1
-          for (int c = 0; c < kHP_D; c += 32) {   // 32 fp16 of a row = 16 packed columns at c
-            uint32_t v[8];
-            tmem_ld_16x256b_x2(lb + c, v);
+          for (int cc = 0; cc < kHP_D / 2; cc += 64) {   // packed column j holds fp16 elements 2j, 2j + 1
+            uint32_t v[32];
+            tmem_ld_16x256b_x8(lb + cc, v);
             tmem_wait_ld();
 #pragma unroll
             for (int hf = 0; hf < 2; ++hf) {
               if (ok[hf]) {
-                __half* op = a.qm16 + off[hf] + c + 4 * q;
-                *reinterpret_cast<uint2*>(op) = make_uint2(v[2 * hf], v[2 * hf + 1]);
-                *reinterpret_cast<uint2*>(op + 16) = make_uint2(v[4 + 2 * hf], v[5 + 2 * hf]);
+                __half* op = a.qm16 + off[hf] + 2 * cc + 4 * q;
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                  *reinterpret_cast<uint2*>(op + 16 * k) = make_uint2(v[4 * k + 2 * hf], v[4 * k + 2 * hf + 1]);
               }
             }
           }
