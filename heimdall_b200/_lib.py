@@ -23,6 +23,7 @@ SIGNATURES = {
     "bf_last_cuda_error": [],
     "bf_abi_version": [],
     "bf_device_error": [_P, _P],
+    "bf_selftest_wait_timeout": [ctypes.c_uint, _P],
     "bf_stage_events": [_P, _I],
     "bf_gdn_decode_step": [_P, _P, _P, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
     "bf_layer_weights_bytes": [_I, _I, _I, _I],

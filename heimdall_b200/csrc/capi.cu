@@ -4,6 +4,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <unordered_map>
 
 #include "common.cuh"
 #include "capi_internal.h"
@@ -47,6 +48,21 @@ int cuda_fail(cudaError_t e) {
   if (e == cudaSuccess) e = cudaGetLastError();
   g_last_cuda_error = (int)e;
   return BF_ERR_CUDA;
+}
+
+// per kernel: bit d set = the shared-memory opt-in was applied on device d
+static std::unordered_map<const void*, uint64_t> g_smem_attr;
+
+int ensure_smem_attr(const void* fn, int bytes) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return BF_ERR_NO_DEVICE;
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  uint64_t& done = g_smem_attr[fn];
+  if (done & (1ull << dev)) return BF_OK;
+  const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return cuda_fail(e);
+  done |= 1ull << dev;
+  return BF_OK;
 }
 
 static cudaStream_t g_side[2][64] = {{nullptr}};

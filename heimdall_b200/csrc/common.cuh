@@ -74,10 +74,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait.  Returns false (and records `site`) when the phase did not complete in time, or
-// when another thread of the CTA already gave up (*abort set): the caller then unwinds.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                          unsigned int* err, unsigned int site) {
+// Bounded wait with an explicit limit.  Returns false (and records `site`) when the phase did not complete
+// within `limit_ns`, or when another thread of the CTA already gave up (*abort set): the caller then unwinds.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                              unsigned int* err, unsigned int site, uint64_t limit_ns) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
@@ -85,13 +85,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     if (mbar_try_wait(a, parity)) return true;
     if ((i & 63u) == 0u) {
       if (abort && *abort) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (globaltimer_ns() - t0 > limit_ns) {
         if (abort) *abort = 1;
         record_error(err, site);
         return false;
       }
     }
   }
+}
+
+// The wait every kernel uses: the same, with the 200 ms limit.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                          unsigned int* err, unsigned int site) {
+  return mbar_wait_for(bar, parity, abort, err, site, kWaitLimitNs);
 }
 
 // Warp-uniform wait for code that is followed by warp-collective (.sync.aligned) instructions: every lane

@@ -302,14 +302,8 @@ int launch_gdn_decode(const float* q, const float* k, const void* v, int v_bf16,
   if (rc) return rc;
   rc = make_tmap(&omap, s_out, BF_F32, 2, dims, strides, box, true);
   if (rc) return rc;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(gdn_decode_kernel<6>, cudaFuncAttributeMaxDynamicSharedMemorySize, kDecSmem) !=
-            cudaSuccess ||
-        cudaFuncSetAttribute(gdn_decode_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kDecSmem) != cudaSuccess)
-      return cuda_fail();
-    attr = true;
-  }
+  if ((rc = ensure_smem_attr((const void*)gdn_decode_kernel<6>, kDecSmem)) != BF_OK) return rc;
+  if ((rc = ensure_smem_attr((const void*)gdn_decode_kernel<0>, kDecSmem)) != BF_OK) return rc;
   const int nitems = B * G * (D / kDecCols);
   const int grid = nitems < st.sm_count ? nitems : st.sm_count;
   if (R == 6 && D == 256)

@@ -1222,17 +1222,14 @@ int gdn_prefill_carve(GdnStreams& s, void* ws) {
   return BF_OK;
 }
 
-static bool g_p_attr[3] = {false, false, false};
-
 int launch_gdn_prefill(GdnStreams s, cudaStream_t stream, int parts) {
   if (s.n_steps <= 0) return BF_OK;
   const int H = s.G * s.R;
-  if (!g_p_attr[0]) {
-    if (cudaFuncSetAttribute(gdn_p1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kP1_Smem) != cudaSuccess ||
-        cudaFuncSetAttribute(gdn_p2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kP2_Smem) != cudaSuccess ||
-        cudaFuncSetAttribute(gdn_p3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kP3_Smem) != cudaSuccess)
-      return cuda_fail();
-    g_p_attr[0] = true;
+  {
+    int rc0 = ensure_smem_attr((const void*)gdn_p1_kernel, kP1_Smem);
+    if (!rc0) rc0 = ensure_smem_attr((const void*)gdn_p2_kernel, kP2_Smem);
+    if (!rc0) rc0 = ensure_smem_attr((const void*)gdn_p3_kernel, kP3_Smem);
+    if (rc0) return rc0;
   }
   if (parts & kGdnP1) {
     CUtensorMap kwmap, umap, wmap1;

@@ -576,12 +576,7 @@ int launch_head_proj(const __nv_bfloat16* q, const __nv_bfloat16* k, const __hal
                    box, true);
     if (rc) return rc;
   }
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(head_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kHP_Smem) != cudaSuccess)
-      return cuda_fail();
-    attr = true;
-  }
+  if ((rc = ensure_smem_attr((const void*)head_proj_kernel, kHP_Smem)) != BF_OK) return rc;
   const int ntiles = (T + kHP_M - 1) / kHP_M;
   const long long nitems = (long long)B * (H + G) * ntiles;
   if (nitems == 0) return BF_OK;
@@ -609,12 +604,7 @@ int launch_x_proj(const __nv_bfloat16* x, const __nv_bfloat16* w_x, const float*
   if (rc) return rc;
   rc = make_tmap_kmajor(&wmap, w_x, BF_BF16, 64, d, d, kXP_N, 1);
   if (rc) return rc;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(x_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kXP_Smem) != cudaSuccess)
-      return cuda_fail();
-    attr = true;
-  }
+  if ((rc = ensure_smem_attr((const void*)x_proj_kernel, kXP_Smem)) != BF_OK) return rc;
   XProjArgs a{ab_b, mix_b, A_log, dt_bias, decay_mask, nullptr, g, beta, mixx, pos, pos0, M, T, d, G, H, sinks, err};
   x_proj_kernel<<<(M + kXP_M - 1) / kXP_M, 192, kXP_Smem, stream>>>(xmap, wmap, a);
   return launch_status();

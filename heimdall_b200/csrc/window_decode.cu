@@ -514,13 +514,8 @@ size_t win_dec_workspace(int B, int G, int R, int D, int W) {
 template <int R>
 static int launch_split(const CUtensorMap& kmap, const CUtensorMap& vmap, const WinDecArgs& a, int grid,
                         unsigned int* err, cudaStream_t stream) {
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(win_dec_split_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, kWT_Smem) !=
-        cudaSuccess)
-      return cuda_fail();
-    attr = true;
-  }
+  const int rc = ensure_smem_attr((const void*)win_dec_split_kernel<R>, kWT_Smem);
+  if (rc) return rc;
   win_dec_split_kernel<R><<<grid, kWT_Threads, kWT_Smem, stream>>>(kmap, vmap, a, err);
   return BF_OK;
 }

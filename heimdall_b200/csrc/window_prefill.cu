@@ -20,12 +20,14 @@
 // warpgroups: half hh owns keys [64 hh, 64 hh + 64) of every tile and O columns [128 hh, 128 hh + 128) of
 // every row; both halves scan the whole score row for the max (identical decisions), scores in the log2
 // domain (FFMA + ex2), O rescaled only when the row max grows by more than 2^8 (P stays in fp16 range).
-// The sink keys (<= 8) are exact in fp32: their scores are one M128 N16 MMA into O's columns, read before
-// the item's first product; their values join in the epilogue.  In the persistent launch items overlap: the
-// next item's queries and first key tile load under this item's last products, and its first score tiles are
-// computed while the epilogue drains O.  The epilogue stores straight from registers: rows that the memory
-// reads mix go to a workspace in the reads' load order as fp16, others leave through a 16-lane TMEM read as
-// 32-byte row segments.
+// The sink keys (<= 8) start the online softmax: their scores are one M128 N16 MMA into the item's second
+// score buffer, issued as soon as the queries land; they give each row its initial max and weights, and one
+// softmax half stages P_sink (fp16) so that O = P_sink V_sink is a single M128 N256 K16 MMA (sink values in
+// an 8 KB non-swizzled K-major tile) ahead of the first window tile.  In the persistent launch the next item's
+// queries and first key tile load under this item's last products; its sink products and first softmax
+// still wait for this item's epilogue (items do not otherwise overlap).  The epilogue scales O by 1/l and
+// stores: rows that the memory reads mix go to a workspace in the reads' load order as fp16, others leave
+// through a 16-lane TMEM read as 32-byte row segments.
 #include "capi_internal.h"
 #include "common.cuh"
 #include "tmap.h"
@@ -644,13 +646,7 @@ int launch_window_prefill(const void* qr, const void* kext, const __half* vt, Wi
   if (rc) return rc;
   rc = make_tmap_kmajor(&vmap, vt, BF_F16, (uint64_t)a.B * a.G * kWP_D, a.Tkp, a.Tkp, kWP_D, 2);
   if (rc) return rc;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(window_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kWP_Smem) !=
-        cudaSuccess)
-      return cuda_fail();
-    attr = true;
-  }
+  if ((rc = ensure_smem_attr((const void*)window_prefill_kernel, kWP_Smem)) != BF_OK) return rc;
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
     return cuda_fail();

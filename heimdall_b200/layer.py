@@ -370,6 +370,48 @@ class BifrostLayer:
                   stream_handle())
         return o.reshape(B, 1, H, D)
 
+    def decode_step(self, x, q, k, v, qr, kr, pos, cache: dict, memory: bool = True, lse=None, ws=None):
+        """One decode token per sequence where every sequence has its own position (serving: a batch of
+        sequences at different lengths).  The reference's ``_student`` with t == 1 (hibrit.py:363-424) is the
+        case of one shared position; this is that step run for each sequence at once.
+
+        x [B,d], q/qr [B,H,D], k/kr/v [B,G,D] (bf16 or castable); pos [B] int64 on the device (the new
+        tokens' positions, not changed here).  ``cache`` holds the reference's keys on the device in kernel
+        layout: ring_k/ring_v [B,G,W,D] bf16, ring_km [B,W,G,D], ring_g/ring_beta [B,W,G], ring_pos [B,W]
+        (one ring position row per sequence; [W] when all sequences share it), sink_k/sink_v [B,G,ns,D] bf16
+        with every sequence past its sinks (ns == sinks), and S [B,G,D,D]; it is updated in place.  ``lse``
+        [B,H] fp32 receives the window log-sum-exp when given; ``ws`` is an optional reusable workspace of
+        at least ``bf_layer_decode_workspace`` bytes.  Returns o [B,H,D] fp32."""
+        check_cuda(x, q, k, v, qr, kr, pos)
+        B = x.shape[0]
+        H, G, D, W = self.H, self.G, self.D, self.window
+        dev = x.device
+        bf = torch.bfloat16
+        args = [z.reshape(B, -1).to(bf).contiguous() for z in (x, q, k, v, qr, kr)]
+        for key, dt in (("ring_k", bf), ("ring_v", bf), ("ring_km", torch.float32), ("ring_g", torch.float32),
+                        ("ring_beta", torch.float32), ("ring_pos", torch.int64), ("S", torch.float32)):
+            tns = cache[key]
+            if tns.dtype != dt or not tns.is_contiguous() or tns.device != dev:
+                raise ValueError(f"decode_step: cache[{key!r}] must be a contiguous {dt} tensor on {dev}")
+        rp = cache["ring_pos"]
+        if rp.dim() == 2 and tuple(rp.shape) != (B, W) or rp.dim() == 1 and rp.numel() != W:
+            raise ValueError("decode_step: ring_pos must be [W] or [B, W]")
+        sk, sv = cache.get("sink_k"), cache.get("sink_v")
+        ns = 0 if sk is None else sk.shape[2]
+        if sk is not None and (sk.dtype != bf or sv.dtype != bf or not sk.is_contiguous() or not sv.is_contiguous()):
+            raise ValueError("decode_step: sinks must be contiguous bf16 [B,G,ns,D]")
+        p = pos.to(device=dev, dtype=torch.int64).contiguous()
+        rc = BfRingCache(ptr(cache["ring_k"]), ptr(cache["ring_v"]), ptr(cache["ring_km"]), ptr(cache["ring_g"]),
+                         ptr(cache["ring_beta"]), ptr(rp), W if rp.dim() == 2 else 0, ptr(sk), ptr(sv), ns,
+                         ptr(cache["S"]))
+        o = torch.empty(B, H, D, device=dev, dtype=torch.float32)
+        nws = _lib.size("bf_layer_decode_workspace", B, H, G, D, W)
+        if ws is None or ws.numel() < nws:
+            ws = torch.empty(nws, dtype=torch.uint8, device=dev)
+        _lib.call("bf_bifrost_layer_decode", ctypes_ref(self._struct), *(ptr(z) for z in args), ptr(p), B,
+                  ctypes_ref(rc), 1 if memory else 0, ptr(o), ptr(lse), ptr(ws), ws.numel(), stream_handle())
+        return o
+
 
 _DUMMY = {}
 _STREAMS = {}

@@ -2,16 +2,20 @@
 
 Heimdall picks its fast delta-rule kernel in ``heimdall.kernels.prepare(device, backend)``
 (heimdall/kernels.py:158-188): a candidate is self-tested against ``delta_rule_reference`` on seeded data
-and enabled only when the relative error (outputs and final state) is below 0.03.  ``hibrit`` and ``motor``
-import the op names by value (heimdall/hibrit.py:32, heimdall/motor.py:37), so the patch points are module
-attributes and the ``HybridAttention`` methods that implement the layer core:
+and enabled only when the relative error (outputs and final state) is below 0.03.  ``motor`` imports its op
+by value (heimdall/motor.py:37), so the patch points are that module attribute and the ``HybridAttention``
+methods that implement the converted (Bifrost) layer core:
 
-  heimdall.kernels.delta_rule, .delta_rule_step   (kernels.py:132-155)  -> functional.delta_rule, .delta_rule_step
-  heimdall.hibrit.delta_rule, .delta_rule_step    (by-value imports)    -> the same
   heimdall.motor.delta_rule_gqa                   (motor.py:70-102)     -> functional.delta_rule_gqa
   HybridAttention._student                        (hibrit.py:363-424)   -> BifrostLayer.student
   HybridAttention._window                         (hibrit.py:336-361)   -> functional.window_attention
   HybridAttention._mem_inputs                     (hibrit.py:327-334)   -> BifrostLayer.mem_inputs
+
+The module-level ``delta_rule`` / ``delta_rule_step`` of ``heimdall.kernels`` and their by-value copies in
+``heimdall.hibrit`` (hibrit.py:32) are deliberately left alone: the model's linear-attention layers (Qwen3.5
+Gated DeltaNet, hibrit.py:170-180) call them with their own head sizes, which these head-dim-256 kernels do
+not cover, and the Bifrost layer never reaches them once ``_student`` is replaced.  The wrappers
+``delta_rule`` and ``delta_rule_step`` below are still exported for callers that want the B200 ops by name.
 
 ``prepare(device, backend="b200")`` runs the reference's self-test shape (seeded q, k, v, g, beta and an
 initial state, head dim 256 because the kernels are built for it) against the host package's
@@ -29,6 +33,9 @@ from . import functional as F_
 from .layer import BifrostLayer
 
 _SAVED: list = []          # (owner, attribute name, original value) in patch order
+# what install() replaces: (module key, attribute path)
+PATCHED_NAMES = (("motor", "delta_rule_gqa"), ("hibrit", "HybridAttention._student"),
+                 ("hibrit", "HybridAttention._mem_inputs"), ("hibrit", "HybridAttention._window"))
 SELF_TEST_TOL = 0.03       # the reference's acceptance threshold (kernels.py:182)
 
 
@@ -130,16 +137,15 @@ def _window(self, qr, ext_k, ext_v, ext_pos, sink_k, sink_v, pos):
 
 # ---------------------------------------------------------------------------------------------- install
 def install(modules=None) -> None:
-    """Patch the reference package's path functions and HybridAttention methods (idempotent)."""
+    """Patch the reference package's Bifrost-path functions and HybridAttention methods (idempotent).
+
+    Only ``PATCHED_NAMES`` change; the linear-attention ops (``kernels.delta_rule``, ``delta_rule_step`` and
+    their copies in ``hibrit``) keep the reference's implementation."""
     if _SAVED:
         return
     m = _modules(modules)
-    kernels, hibrit, motor = m["kernels"], m["hibrit"], m["motor"]
+    hibrit, motor = m["hibrit"], m["motor"]
     try:
-        _patch(kernels, "delta_rule", delta_rule)
-        _patch(kernels, "delta_rule_step", delta_rule_step)
-        _patch(hibrit, "delta_rule", delta_rule)
-        _patch(hibrit, "delta_rule_step", delta_rule_step)
         _patch(motor, "delta_rule_gqa", delta_rule_gqa)
         cls = hibrit.HybridAttention
         _patch(cls, "_student", _student)

@@ -162,6 +162,7 @@ def _student_sp(L, x, q, k, v, qr, kr, group, memory):
         Ms, Ns = torch.stack(Ml), torch.stack(Nl)
     else:
         Ms, Ns = M[None], N[None]
+    finite = _maps_finite(Ms, Ns)
     S_in = F_.apply_prefix(Ms[:rank], Ns[:rank])[rank]
     if cache.get("S") is not None:
         cache["S"].copy_(S_in)
@@ -169,7 +170,34 @@ def _student_sp(L, x, q, k, v, qr, kr, group, memory):
         cache["S"] = S_in.contiguous()
     # phase 2: the rest of the layer from the incoming state
     o = L.prefill_sp_finish(handle)
+    _raise_if_corrupted(finite)
     return o, cache
+
+
+def _maps_finite(Ms, Ns):
+    """Per segment, whether its gathered state map is finite (a rank that sent NaN or inf).  On a GPU the
+    flags are computed on the device and copied to pinned host memory behind an event, so the check does not
+    hold back the second phase: ``_raise_if_corrupted`` waits for the flags only, after it is launched."""
+    fin = torch.isfinite(Ms).flatten(1).all(1) & torch.isfinite(Ns).flatten(1).all(1)
+    if not fin.is_cuda:
+        return fin, None
+    host = torch.empty(fin.shape, dtype=torch.bool, pin_memory=True)
+    host.copy_(fin, non_blocking=True)
+    ev = torch.cuda.Event()
+    ev.record()
+    return host, ev
+
+
+def _raise_if_corrupted(finite):
+    """Every rank sees the same gathered maps, so every rank raises the same error for a corrupted one (the
+    outputs and the cache of this call are then undefined)."""
+    flags, ev = finite
+    if ev is not None:
+        ev.synchronize()
+    bad = [j for j, ok in enumerate(flags.tolist()) if not ok]
+    if bad:
+        raise RuntimeError(f"sequence-parallel prefill: the state map of segment(s) {bad} is not finite "
+                           f"(the rank(s) holding them sent corrupted maps)")
 
 
 def _halo_inputs(L, halo, start: int, W: int, q):

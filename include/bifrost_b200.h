@@ -59,6 +59,15 @@ int bf_abi_version(void);
  * Returns BF_OK or BF_ERR_CUDA. */
 int bf_device_error(unsigned int* word, bf_stream_t stream);
 
+/* Self-test of the device-side failure path.  Launches one small kernel (tensor memory allocated as the
+ * production kernels do) whose bounded mbarrier wait can never complete and gives up after `limit_us`
+ * microseconds (1 .. 1000000): it records the timeout in this device's error record (site 0xF1), frees its
+ * tensor memory and returns; nothing faults, traps or hangs, and the context stays usable.  The next
+ * bf_device_error() on the device reports word[0] = (0xF1 << 8) | BF_ERR_TIMEOUT.  Follows the
+ * reference's self-test convention for candidate kernels (heimdall/kernels.py:168-188), applied to the
+ * error path rather than to the numerics. */
+int bf_selftest_wait_timeout(unsigned int limit_us, bf_stream_t stream);
+
 /* Per-stage timing: `events` holds 2*n_stages cudaEvent_t handles (begin/end per stage); each
  * layer entry point records them on its stream around its stages (0 x-projection, 1 head
  * projection, 2-4 delta-rule phases P1/P2/P3, 5 window key/value prep, 6 window attention,

@@ -3,6 +3,7 @@
 ``-m "not gpu"`` runs the oracle-vs-golden pins, host logic and library-load checks on the CPU;
 ``-m gpu`` runs the CUDA parity tests (they need a B200 and the built extension).
 """
+import os
 import sys
 from pathlib import Path
 
@@ -12,6 +13,18 @@ ROOT = Path(__file__).resolve().parents[1]
 for p in (ROOT, ROOT / "tests" / "golden"):
     if str(p) not in sys.path:
         sys.path.insert(0, str(p))
+
+
+def reference_project():
+    """The reference project directory (the one holding the ``heimdall`` package), from the environment
+    variable HEIMDALL_REFERENCE; None when it is unset or does not exist (tests that need it skip)."""
+    p = os.environ.get("HEIMDALL_REFERENCE")
+    if not p:
+        return None
+    path = Path(p)
+    if (path / "Heimdall" / "heimdall").is_dir():
+        path = path / "Heimdall"
+    return path if (path / "heimdall").is_dir() else None
 
 
 def pytest_configure(config):

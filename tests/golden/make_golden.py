@@ -1,8 +1,9 @@
 """Generate the golden fixtures in this folder by running the REFERENCE implementation.
 
-Run in a container where the reference project is mounted (default ``/root/reference``)::
+Run where the reference project is available, naming its directory (the one that holds ``Heimdall/``, or
+``Heimdall/`` itself) with ``--ref`` or the environment variable HEIMDALL_REFERENCE::
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    HEIMDALL_REFERENCE=<reference checkout> python tests/golden/make_golden.py
 
 It imports Heimdall's own ``heimdall.kernels``, ``heimdall.motor`` and ``heimdall.hibrit`` and runs
 them, unmodified, on seeded inputs.  Inputs and outputs are saved to ``golden_*.pt``.  Inputs that
@@ -14,6 +15,7 @@ from __future__ import annotations
 
 import argparse
 import math
+import os
 import sys
 from pathlib import Path
 
@@ -128,9 +130,12 @@ def layer_case(hb, name, H, G, D, d, window, sinks, archival, parts, seed, keep_
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("HEIMDALL_REFERENCE"))
     args = ap.parse_args()
-    sys.path.insert(0, str(Path(args.ref) / "Heimdall"))
+    if not args.ref:
+        ap.error("name the reference project with --ref or HEIMDALL_REFERENCE")
+    ref = Path(args.ref)
+    sys.path.insert(0, str(ref / "Heimdall" if (ref / "Heimdall" / "heimdall").is_dir() else ref))
     import heimdall.hibrit as hb
     import heimdall.kernels as hk
     import heimdall.motor as hm

@@ -33,3 +33,17 @@ def test_invalid_arguments_rejected_before_launch():
     assert e.value.code == 1
     with pytest.raises(_lib.BifrostError):
         _lib.call("bf_prepare_layer_weights", 0, 0, 0, 0, 24, 4, 256, 5120, 0, 0, 0)
+
+
+def test_selftest_rejects_bad_limits_without_a_device():
+    for bad in (0, 2_000_000):
+        with pytest.raises(_lib.BifrostError) as e:
+            _lib.call("bf_selftest_wait_timeout", bad, 0)
+        assert e.value.code == 1
+
+
+def test_noalloc_scratch_bound_pinned():
+    """The allocation-free decode entry point's fixed scratch (16 MiB) holds the Bifrost geometry's decode
+    workspace for 64 sequences at W = 2048 (the documented limit) and not for 128."""
+    assert _lib.size("bf_layer_decode_workspace", 64, 24, 4, 256, 2048) <= 16 << 20
+    assert _lib.size("bf_layer_decode_workspace", 128, 24, 4, 256, 2048) > 16 << 20

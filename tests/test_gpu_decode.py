@@ -219,3 +219,33 @@ def test_layer_decode_graph_replay_matches_eager():
         assert ob.rel_l2(cb[key].cpu(), ca[key].cpu()) < 1e-6, key
     assert torch.equal(cb["ring_k"].cpu(), ca["ring_k"].cpu()) and torch.equal(cb["ring_pos"].cpu(), ca["ring_pos"].cpu())
     del graph
+
+
+def test_two_devices_in_one_process():
+    """The kernels' shared-memory opt-ins and per-device state are per device: a decode state step and a
+    layer prefill on device 0, then the same on device 1 of the same process, both match the oracle."""
+    _dev()
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import heimdall_b200 as hb
+    from heimdall_b200 import BifrostLayer
+    H, G, D, d, W, S, T = 24, 4, 256, 128, 64, 4, 300
+    p = layer_params(H, G, D, d, window=W, sinks=S, archival=1, seed=23)
+    x, q, k, v, qr, kr = _layer_inputs(H, G, D, d, T, seed=29)
+    f = lambda z: z.float()
+    o_ref = ob.student(p, f(x), f(q), f(k), f(v), f(qr), f(kr), 0, None)
+    g_ = torch.Generator().manual_seed(5)
+    qs = F.normalize(torch.randn(2, G, D, generator=g_), dim=-1) * D ** -0.5
+    ks = F.normalize(torch.randn(2, G, D, generator=g_), dim=-1)
+    vs, gs, bs = torch.randn(2, G, D, generator=g_), -torch.rand(2, G, generator=g_), torch.rand(2, G, generator=g_)
+    s0 = torch.randn(2, G, D, D, generator=g_) * 0.1
+    os_ref, ss_ref = ob.gdn_step(qs, ks, vs, gs, bs, s0, dtype=torch.float64)
+    for i in (0, 1):
+        dev = torch.device("cuda", i)
+        with torch.cuda.device(dev):
+            o_s, s_s = hb.delta_rule_step(*(z.to(dev) for z in (qs, ks, vs, gs, bs, s0)))
+            L = BifrostLayer.from_params(p, dev)
+            o = L.student(*(z.to(dev) for z in (x, q, k, v, qr, kr)), 0, None)
+            torch.cuda.synchronize(dev)
+        assert ob.rel_l2(o_s.cpu(), os_ref) < 1e-5 and ob.rel_l2(s_s.cpu(), ss_ref) < 1e-5, i
+        assert ob.rel_l2(o.cpu(), o_ref) < O_TOL, i

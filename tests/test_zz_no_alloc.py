@@ -4,7 +4,8 @@
 decode step (a runtime whose memory manager already holds nearly all of HBM, or a host that binds only the
 C entry points and cannot own a device workspace); it takes its scratch from a fixed array inside the
 library instead of a caller workspace.  This test runs two decode steps in a row through both entry points
-on identical copies of a cache and requires the same outputs and the same cache updates.  The file name
+on identical copies of a cache and requires the same outputs and the same cache updates, with the memory on
+and in the window-only mode (memory = 0).  The file name
 makes pytest collect it last, so a run that stops at the first failure has run every other test already.
 """
 import ctypes
@@ -18,7 +19,8 @@ from params import layer_params
 pytestmark = pytest.mark.gpu
 
 
-def test_noalloc_decode_matches_workspace_decode():
+@pytest.mark.parametrize("memory", [1, 0])
+def test_noalloc_decode_matches_workspace_decode(memory):
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     dev = torch.device("cuda")
@@ -57,9 +59,9 @@ def test_noalloc_decode_matches_workspace_decode():
         lse_ref = torch.empty(B, H, device=dev)
         lse_new = torch.empty(B, H, device=dev)
         _lib.call("bf_bifrost_layer_decode", lay, ptr(x), ptr(q), ptr(k), ptr(v), ptr(qr), ptr(kr), ptr(pos), B,
-                  ctypes.addressof(structs[0]), 1, ptr(o_ref), ptr(lse_ref), ptr(ws), nws, stream)
+                  ctypes.addressof(structs[0]), memory, ptr(o_ref), ptr(lse_ref), ptr(ws), nws, stream)
         _lib.call("bf_bifrost_layer_decode_noalloc", lay, ptr(x), ptr(q), ptr(k), ptr(v), ptr(qr), ptr(kr), ptr(pos),
-                  B, ctypes.addressof(structs[1]), 1, ptr(o_new), ptr(lse_new), stream)
+                  B, ctypes.addressof(structs[1]), memory, ptr(o_new), ptr(lse_new), stream)
         torch.cuda.synchronize()
         assert ob.rel_l2(o_new.cpu(), o_ref.cpu()) < 1e-6, step
         assert ob.rel_l2(lse_new.cpu(), lse_ref.cpu()) < 1e-6, step
