@@ -1,21 +1,25 @@
 #!/usr/bin/env python
-"""Bifrost-layer benchmark on B200 (the reference's headline path, BASELINE config 1 at N=1).
+"""Bifrost-layer benchmark on B200 (the headline is config 3 at 128K).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-A step is one full prefill of one converted Bifrost layer over T = 32768 tokens (B=1, 24 query / 4 KV
-heads, head dim 256, window 2048 + 4 sinks, hidden size 5120, bf16 inputs, fp32 state and outputs),
-from an empty cache, through ``BifrostLayer.student`` -> the C ABI ``bf_bifrost_layer_prefill``.
-Inputs are synthetic (seeded, RMS-normalised q/k/v as in config 1) and larger than L2 (1.3 GB per step),
-so no L2 flush is needed between steps.  With N > 1 each rank runs its own sequence (weak scaling,
-no collective in the data path); rank 0 prints the JSON line with the max-over-ranks time.
+Headline (``value``): one converted Bifrost layer prefill of ONE 131072-token sequence (B=1, 24 query / 4 KV
+heads, head dim 256, window 2048 + 4 sinks, hidden size 5120, bf16 inputs, fp32 state and outputs, from an empty
+cache), split evenly over the N GPUs (sequence parallelism: halo exchange, per-segment state maps all-gathered
+and prefix-folded over NCCL, then each rank's prefill; ``heimdall_b200.sp.student_sp``).  N = 1 is one ordinary
+prefill (``BifrostLayer.student`` -> ``bf_bifrost_layer_prefill``).  The total work is fixed, so the scaling is
+strong and the driver's per-N values give the sequence-parallel efficiency.  Inputs are synthetic (seeded,
+RMS-normalised q/k/v) and larger than L2 (5.4 GB per step on one GPU), so no L2 flush is needed.  Timed with
+CUDA events over exactly --steps steps after --warmup, max over ranks; rank 0 prints one JSON line.
 
-Extra keys: ``roofline`` (window-attention kernel, the dominant one, timed live with CUDA events on its
-stream), ``layer_roofline`` (all algorithmic FLOPs of the step), ``cpu_baseline`` (the CPU oracle port on
-a bounded sample), ``e2e`` (host buffers in, host output back, copies inside the timed region),
-``decode`` (64 sequences x 12 layers, one token per sequence per step),
-``sp`` (one 131072-token sequence split over the N GPUs, sequence-parallel prefill),
-``delta_rule`` (BASELINE configs 0 and 4: the chunked delta-rule op alone, and on packed sequences),
+Extra keys: ``config1`` (T = 32768 on each GPU: stage times, the layer roofline) and
+``roofline`` (its dominant kernel, the window attention, timed live on its stream; peak = the measured burst
+bf16 figure when the timed clocks sat at max, else the sustained one), ``layer_roofline`` (all algorithmic
+FLOPs of the headline step), ``cpu_baseline`` (the CPU oracle port in the reference's own form on a bounded
+sample), ``e2e`` (the headline through the public API from pinned host buffers, copies inside the timed
+region), ``sp_131k`` (N > 1: a per-rank timeline of one step and an in-bench parity check against one prefill
+of the whole sequence on one GPU), ``sp_1m`` (config 3 at T = 1048576, same), ``decode`` (64
+sequences x 12 layers, sharded over the N GPUs), ``delta_rule`` (configs 0 and 4: the chunked delta-rule op),
 ``clocks`` (nvidia-smi samples during the timed region) and ``gpu_launches``.
 """
 from __future__ import annotations
@@ -222,48 +226,36 @@ def ctypes_array(handles):
     return arr
 
 
-def run_e2e(L, T, steps, warmup, device, ctx):
-    """Same workload through the public host-buffer API (``BifrostLayer.student_host``): pinned host inputs in,
-    pinned host output back, every copy inside the timed region (the API overlaps them with the layer by
-    processing the sequence in chunks on three streams).  Max over ranks."""
-    host = [t.cpu().pin_memory() for t in make_inputs(T, 1 + ctx["rank"], device)]
-    o_host = torch.empty(1, T, H, D, dtype=torch.float32).pin_memory()
-    bi = sum(h.numel() * h.element_size() for h in host)
-    bo = o_host.numel() * o_host.element_size()
-
-    def step():
-        L.student_host(*host, 0, None, out=o_host)
-
-    for _ in range(max(1, warmup)):
-        step()
-    torch.cuda.synchronize()
-    barrier(ctx)
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(steps):
-        step()
-    b.record()
-    torch.cuda.synchronize()
-    t = torch.tensor([a.elapsed_time(b) / steps], device=device)
-    if ctx["world"] > 1:
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    ms = float(t.item())
-    return {"value": T * ctx["world"] / (ms / 1e3), "unit": "tok/s", "ms_per_step": ms, "h2d_bytes_per_step": bi,
-            "d2h_bytes_per_step": bo, "api": "BifrostLayer.student_host (chunks of 4096 tokens, 3 streams)"}
+SP_STAGES = ["x_proj", "head_proj", "gdn_p1", "gdn_p2", "gdn_p3", "window_prep", "window", "cache"]
 
 
-def run_sp(L, device, ctx, T_total=131072, steps=5, warmup=2):
+def _sp_stage_hook(handles):
+    """phase_hook for student_sp: per-phase stage events (phase 0: memory inputs, P1, the state-map scan, the
+    window; phase 1: the scan from the incoming state, the memory reads)."""
+    from heimdall_b200 import _lib
+
+    def hook(phase):
+        _lib.call("bf_stage_events", handles[phase], len(SP_STAGES))
+    return hook
+
+
+def run_sp(L, device, ctx, T_total, steps=5, warmup=2):
     """one sequence of T_total tokens split over the ranks (heimdall_b200.sp.student_sp:
     halo exchange, segment state maps, all-gather, prefix fold, then each rank's prefill).  At N=1 the
-    same sequence is one ordinary prefill.  Max over ranks of the device time."""
-    from heimdall_b200 import sp
+    same sequence is one ordinary prefill.  Max over ranks of the device time.
+
+    At N > 1 it also reports each rank's timeline of one instrumented step (ms from the step's start: the
+    student_sp marks and the kernels' stage events of both phases) and checks parity in the bench: rank 0
+    runs the whole sequence as one prefill on its own GPU and compares the last rank's final state
+    (rel-L2 <= 1e-3) and its last 2048 outputs (rel-L2 <= 2e-3), both sent to rank 0."""
+    from heimdall_b200 import _lib, sp
     world, rank = ctx["world"], ctx["rank"]
     T = T_total // world
     ins = make_inputs(T, seed=11 + rank, device=device)
     if world > 1:
-        step = lambda: sp.student_sp(L, *ins)
+        step = lambda **kw: sp.student_sp(L, *ins, **kw)
     else:
-        step = lambda: L.student(*ins, 0, {})
+        step = lambda **kw: (L.student(*ins, 0, {}), None)
     for _ in range(warmup):
         step()
     torch.cuda.synchronize()
@@ -278,10 +270,81 @@ def run_sp(L, device, ctx, T_total=131072, steps=5, warmup=2):
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     ms = float(t.item())
-    del ins
-    return {"workload": f"BASELINE config 3: one sequence of {T_total} tokens split over {world} GPU(s) "
-                        f"({T} per GPU), from an empty cache", "T_total": T_total, "ms_per_step": ms,
-            "value": T_total / (ms / 1e3), "unit": "tok/s", "steps": steps, "warmup": warmup}
+    res = {"workload": f"BASELINE config 3: one sequence of {T_total} tokens split over {world} GPU(s) "
+                       f"({T} per GPU), from an empty cache", "T_total": T_total, "ms_per_step": ms,
+           "value": T_total / (ms / 1e3), "unit": "tok/s", "steps": steps, "warmup": warmup}
+    if world == 1:
+        del ins
+        return res
+    # one instrumented step: per-rank timeline
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2 * len(SP_STAGES))] for _ in range(2)]
+    for es in evs:
+        for e in es:
+            e.record()
+    torch.cuda.synchronize()
+    handles = [ctypes_array([e.cuda_event for e in es]) for es in evs]
+    timeline = []
+    barrier(ctx)
+    o, cache = step(timeline=timeline, phase_hook=_sp_stage_hook(handles))
+    torch.cuda.synchronize()
+    _lib.call("bf_stage_events", None, 0)
+    t0 = timeline[0][1]
+    marks = {lab: round(t0.elapsed_time(ev), 4) for lab, ev in timeline}
+    stages = {}
+    for ph, es in enumerate(evs):
+        for j, name in enumerate(SP_STAGES):
+            try:
+                stages[f"p{ph}.{name}"] = [round(t0.elapsed_time(es[2 * j]), 4), round(t0.elapsed_time(es[2 * j + 1]), 4)]
+            except RuntimeError:
+                pass
+    per_rank = [None] * world
+    torch.distributed.all_gather_object(per_rank, {"rank": rank, "marks_ms": marks, "stages_ms": stages})
+    res["timeline"] = per_rank
+    res["timeline_note"] = ("ms from the start of one instrumented step on each rank; marks are student_sp's steps "
+                            "on its stream, stages are [begin, end] of the kernels of phase 0 (memory inputs, P1, "
+                            "state-map scan, window) and phase 1 (scan from the incoming state, memory reads)")
+    # parity: the last rank's final state and last outputs against one pass over the whole sequence on rank 0
+    last = world - 1
+    n_cmp = 2048
+    if rank == last:
+        torch.distributed.send(cache["S"].contiguous(), 0)
+        torch.distributed.send(o[:, -n_cmp:].contiguous(), 0)
+    elif rank == 0:
+        S_last = torch.empty_like(cache["S"])
+        o_last = torch.empty(o.shape[0], n_cmp, *o.shape[2:], device=device, dtype=o.dtype)
+        torch.distributed.recv(S_last, last)
+        torch.distributed.recv(o_last, last)
+    del o, cache, ins
+    if rank == 0:
+        torch.cuda.empty_cache()
+        full = [torch.empty(1, T_total, *shape[2:], device=device, dtype=torch.bfloat16) if i < 4 else
+                torch.empty(1, shape[1], T_total, shape[3], device=device, dtype=torch.bfloat16)
+                for i, shape in enumerate(_input_shapes(T))]
+        for r in range(world):
+            part = make_inputs(T, seed=11 + r, device=device)
+            for i, z in enumerate(part):
+                if i < 4:
+                    full[i][:, r * T:(r + 1) * T] = z
+                else:
+                    full[i][:, :, r * T:(r + 1) * T] = z
+            del part
+        cache1 = {}
+        o1 = L.student(*full, 0, cache1)
+        torch.cuda.synchronize()
+        rel = lambda a_, b_: float((a_.double() - b_.double()).norm() / b_.double().norm())
+        es = rel(S_last, cache1["S"])
+        eo = rel(o_last, o1[:, -n_cmp:])
+        res["parity"] = {"against": "one prefill of the whole sequence on one GPU", "state_rel_l2": es,
+                         "state_tol": 1e-3, "last_outputs_rel_l2": eo, "outputs_tol": 2e-3,
+                         "outputs_compared": f"the last {n_cmp} tokens of rank {last}", "ok": es <= 1e-3 and eo <= 2e-3}
+        del full, o1, cache1
+        torch.cuda.empty_cache()
+    barrier(ctx)
+    return res
+
+
+def _input_shapes(T, B=1):
+    return [(B, T, DM), (B, T, H, D), (B, T, G, D), (B, T, G, D), (B, H, T, D), (B, G, T, D)]
 
 
 def _time_device(fn, steps, warmup):
@@ -340,14 +403,19 @@ def run_delta_configs(device, steps=10, warmup=3):
     return out
 
 
-def run_decode(device, steps=256, warmup=8, nseq=64, nlayers=12):
+def run_decode(device, ctx, steps=256, warmup=8, nseq=64, nlayers=12):
     """64 sequences at positions U[4K, 128K], 12 stacked layers, one token per sequence per
-    step; the whole 12-layer step is captured in a CUDA graph and replayed."""
+    step; the whole 12-layer step is captured in a CUDA graph and replayed.  With N ranks the sequences are
+    sharded (64 / N per GPU, no collective: sequences are independent); the step time is the max over ranks and
+    the per-token figures are for the whole batch."""
+    world, rank = ctx["world"], ctx["rank"]
+    nseq_total = nseq
+    nseq = max(1, nseq // world)
     from heimdall_b200 import _lib
     from heimdall_b200.layer import ctypes_ref
     from heimdall_b200.structs import BfRingCache
     from heimdall_b200.functional import ptr
-    gen = torch.Generator(device=device).manual_seed(2)
+    gen = torch.Generator(device=device).manual_seed(2 + 1000 * rank)
     bf = torch.bfloat16
     r = lambda *s: torch.randn(*s, generator=gen, device=device)
     layers, caches, ins, outs, wss = [], [], [], [], []
@@ -397,6 +465,7 @@ def run_decode(device, steps=256, warmup=8, nseq=64, nlayers=12):
     for e in ev:
         e.record()
     torch.cuda.synchronize()
+    barrier(ctx)
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
         a.record()
@@ -404,7 +473,10 @@ def run_decode(device, steps=256, warmup=8, nseq=64, nlayers=12):
             graph.replay()
         b.record()
     torch.cuda.synchronize()
-    us_step = a.elapsed_time(b) * 1e3 / steps
+    t_ = torch.tensor([a.elapsed_time(b) * 1e3 / steps], device=device)
+    if world > 1:
+        torch.distributed.all_reduce(t_, op=torch.distributed.ReduceOp.MAX)
+    us_step = float(t_.item())
     # live per-kernel timing of the state update and the window (eager step with stage events)
     handles = ctypes_array([e.cuda_event for e in ev])
     st_us, win_us = [], []
@@ -426,8 +498,10 @@ def run_decode(device, steps=256, warmup=8, nseq=64, nlayers=12):
     su = statistics.fmean(st_us)   # event ticks are about 1 us: the mean of the samples resolves below that
     wu = statistics.fmean(win_us)
     per_layer_bytes = state_bytes + win_bytes
-    return {"config": f"{nseq} sequences x {nlayers} layers, positions U[4096,131072), {steps} graph-replayed steps",
-            "us_per_step": us_step, "us_per_token": us_step / nseq,
+    return {"config": f"{nseq_total} sequences x {nlayers} layers ({nseq} per GPU on {world} GPU(s)), positions "
+                      f"U[4096,131072), {steps} graph-replayed steps",
+            "us_per_step": us_step, "us_per_token": us_step / nseq_total, "tokens_per_s": nseq_total / (us_step * 1e-6),
+            "per_gpu_note": "state_update / window / step_roofline are for one GPU's shard (rank 0)",
             "state_update": {"us": su, "bytes": state_bytes, "achieved_gbs": state_bytes / (su * 1e-6) / 1e9,
                              "peak_gbs": pk["hbm_gbs"], "frac": state_bytes / (su * 1e-6) / 1e9 / pk["hbm_gbs"]},
             "window": {"us": wu, "bytes": win_bytes, "achieved_gbs": win_bytes / (wu * 1e-6) / 1e9},
@@ -437,9 +511,10 @@ def run_decode(device, steps=256, warmup=8, nseq=64, nlayers=12):
 
 # ---------------------------------------------------------------------------------------------- CPU arms
 def cpu_sample_tokens_per_s(n_new=2048, start=None, seed=0, threads=None):
-    """The CPU oracle (a restatement of the reference's PyTorch path) on a bounded sample of the workload:
-    the last n_new tokens of the T=32768 prefill (positions start.. with a full synthetic cache: W ring
-    entries, sinks, state), i.e. its steady-state per-token cost."""
+    """The CPU oracle (a restatement of the reference's PyTorch path, in the reference's own form: the prefill
+    memory repeats the state for each query head, heimdall/hibrit.py:404-408) on a bounded sample of the
+    workload: the last n_new tokens of the T=32768 prefill (positions start.. with a full synthetic cache: W
+    ring entries, sinks, state), i.e. its steady-state per-token cost."""
     import torch.nn.functional as F
     sys.path.insert(0, str(ROOT / "tests" / "golden"))
     from oracle import bifrost_oracle as ob
@@ -463,7 +538,7 @@ def cpu_sample_tokens_per_s(n_new=2048, start=None, seed=0, threads=None):
     cache["ring_pos"][pp % W] = pp
     t0 = time.perf_counter()
     with torch.no_grad():
-        ob.student(p, x, q, k, v, qr, kr, start, cache)
+        ob.student(p, x, q, k, v, qr, kr, start, cache, gqa_native=False)
     dt = time.perf_counter() - t0
     return n_new / dt, threads, dt
 
@@ -480,21 +555,39 @@ def cpu_baseline(min_seconds=10.0, n_new=2048):
     return tot_n / tot_t, cores, tot_t, reps
 
 
+HEADLINE_T = 131072
+
+
 def arm_config(world):
-    return {"workload": "BASELINE config 1: single Bifrost layer prefill, T=32768, B=1 per GPU, 24q/4kv heads, D=256, "
-                        "W=2048, 4 sinks, d=5120, from an empty cache",
-            "global_batch": world, "seq_len": 32768,
-            "parallelism": f"dp{world} (one independent sequence per GPU)" if world > 1 else "single GPU",
-            "l2": "inputs larger than L2 (1.34 GB read per step), no flush"}
+    return {"workload": f"BASELINE config 3 at T={HEADLINE_T}: one Bifrost layer prefill of one {HEADLINE_T}-token "
+                        f"sequence (B=1, 24q/4kv heads, D=256, W=2048, 4 sinks, d=5120, from an empty cache) split "
+                        f"evenly over the {world} GPU(s) (sequence-parallel; one GPU: an ordinary prefill)",
+            "global_batch": 1, "seq_len": HEADLINE_T,
+            "parallelism": f"sequence-parallel sp{world}" if world > 1 else "single GPU",
+            "l2": "inputs larger than L2 (5.4 GB read per step on one GPU), no flush"}
 
 
-def run_reference(args, dist_ctx):
-    """The reference's CPU path (the oracle port; the reference is PyTorch, nothing compiles into oracle/_ref)
-    on all host threads: each step is a bounded sample of the config-1 workload (its last n_new tokens,
-    against a full cache), sized so the whole --steps/--warmup run stays within a few minutes."""
-    if dist_ctx["rank"] != 0:
+def cpu_model():
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def run_reference(args, rank):
+    """The reference's CPU path on the host cores: the oracle port in the reference's own form (the reference is
+    PyTorch, nothing compiles into oracle/_ref; the port repeats the prefill state for each query head as
+    heimdall/hibrit.py:404-408 does), all host threads, no GPU and no process group.  Each step is a bounded
+    sample of the workload: the last n_new tokens of a long prefill against a full cache (W ring entries, sinks,
+    state), whose per-token cost is the steady state of any prefill longer than 2W (32K and 128K alike); n_new
+    shrinks for long runs so the whole --steps/--warmup run stays within a few minutes.  Under torchrun only
+    rank 0 runs and prints."""
+    if rank != 0:
         return
-    n_new = 2048 if args.steps + args.warmup <= 300 else 512
+    n_new = 2048 if args.steps + args.warmup <= 150 else (1024 if args.steps + args.warmup <= 300 else 512)
     for _ in range(args.warmup):
         cpu_sample_tokens_per_s(n_new)
     tot = 0.0
@@ -503,15 +596,17 @@ def run_reference(args, dist_ctx):
         _, cores, dt = cpu_sample_tokens_per_s(n_new)
         tot += dt
     val = n_new * args.steps / tot
-    sample = (f"{n_new} tokens per step: the last {n_new} tokens of the T=32768 prefill (positions {32768 - n_new}..) "
-              f"with a full cache (W=2048 ring, 4 sinks, state), i.e. its steady-state per-token cost")
-    cfg = arm_config(1)
+    sample = (f"{n_new} tokens per step: the last {n_new} tokens of a long prefill (positions from 32768 - {n_new}) "
+              f"with a full cache (W=2048 ring, 4 sinks, state): the steady-state per-token cost of the prefill; "
+              f"{cores} threads on {cpu_model()}")
+    cfg = arm_config(args.gpus)
     cfg["sample"] = sample
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": val, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": tot / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, config-1 shapes)", "config": cfg,
-        "cpu_baseline": {"value": val, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
+        "warmup": args.warmup, "ms_per_step": tot / args.steps * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, config-1/3 shapes)", "config": cfg,
+        "cpu_baseline": {"value": val, "unit": "tok/s", "cores": cores, "cpu": cpu_model(), "kind": "port",
+                         "form": "reference (state repeated per query head, hibrit.py:404-408)", "sample": sample},
         "e2e": {"value": val, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}), flush=True)
 
 
@@ -539,56 +634,67 @@ def dist_setup():
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--T", type=int, default=32768)
+    ap.add_argument("--T", type=int, default=32768, help="config-1 sequence length")
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--decode-seqs", type=int, default=64)
     ap.add_argument("--decode-layers", type=int, default=12)
     ap.add_argument("--decode-steps", type=int, default=256)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--no-sp", action="store_true")
+    ap.add_argument("--no-sp", action="store_true", help="skip the 1M-token sequence-parallel leg")
     ap.add_argument("--no-delta", action="store_true")
+    ap.add_argument("--no-config1", action="store_true")
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)
+    if args.impl == "reference":
+        # the CPU arm touches no GPU and joins no process group: rank 0 runs, the others leave
+        run_reference(args, int(os.environ.get("RANK", "0")))
+        return
     ctx = dist_setup()
     try:
-        if args.impl == "reference":
-            run_reference(args, ctx)
-            return
         run_ours(args, ctx)
     finally:
         if ctx["world"] > 1 and torch.distributed.is_initialized():
             torch.distributed.destroy_process_group()
 
 
-def run_ours(args, ctx):
-    dev = torch.device("cuda", ctx["local"])
-    torch.cuda.set_device(dev)
+def pick_peak(pk, clocks):
+    """The bf16 peak that matches the timed region's clocks: the burst figure when the SMs ran at their maximum
+    clock (median within 5 %), the sustained (power-capped) one otherwise."""
+    med, mx = clocks.get("sm_mhz"), clocks.get("sm_max_mhz")
+    if med and mx and med >= 0.95 * mx:
+        return pk["bf16_tflops"], "burst"
+    return pk["bf16_tflops_sustained"], "sustained"
+
+
+def headline_flops(T_total):
+    win_f, delta_f, proj_f = layer_flops(T_total)
+    return win_f + delta_f + proj_f
+
+
+def run_config1(L, dev, ctx, args, pk, pk_kind):
+    """BASELINE config 1 on each GPU (a T=32768 layer prefill from an empty cache): stage times, the dominant
+    kernel's roofline (the window, timed live on its stream), the layer roofline against the peak matching the
+    clocks, and the window kernel alone."""
     T = args.T
-    L = make_layer(dev)
     inputs = make_inputs(T, seed=1 + ctx["rank"], device=dev)
     stage_names = ["x_proj", "head_proj", "gdn_p1", "gdn_p2", "gdn_p3", "window_prep", "window", "cache"]
+    steps = max(10, args.steps)
     with ClockSampler(ctx["local"]) as clk:
-        ms, stage_ms = run_prefill(L, inputs, args.steps, args.warmup, T, ctx, stage_names)
+        ms, stage_ms = run_prefill(L, inputs, steps, args.warmup, T, ctx, stage_names)
     clocks = clk.summary()
     win_alone_ms = window_standalone_ms(inputs)
+    del inputs
     t = torch.tensor([ms], device=dev)
     if ctx["world"] > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    ms_max = float(t.item())
-    e2e = None if args.no_e2e else run_e2e(L, T, min(args.steps, 10), 1, dev, ctx)
-    del inputs
-    sp_res = None if args.no_sp else run_sp(L, dev, ctx)
-    if ctx["rank"] != 0:
-        return
-    ms_step = ms_max / args.steps
-    value = T * ctx["world"] / (ms_step / 1e3)
-    pk, pk_kind = peaks()
+    ms_step = float(t.item()) / steps
+    peak, peak_kind = pick_peak(pk, clocks)
     win_f, delta_f, proj_f = layer_flops(T)
-    tflops_peak = pk["bf16_tflops_sustained"]
+    total_f = win_f + delta_f + proj_f
     win_ms = stage_ms.get("window")
     traffic = None
     tp = ROOT / "profiles" / "roofline_traffic.json"
@@ -601,37 +707,151 @@ def run_ours(args, ctx):
     if win_ms:
         ach = win_f / (win_ms * 1e-3) / 1e12
         alone = win_f / (win_alone_ms * 1e-3) / 1e12
-        roof = {"kernel": "window_prefill_kernel", "bound": "tensor", "achieved": ach, "peak": tflops_peak,
-                "unit": "TFLOP/s", "frac": ach / tflops_peak, "traffic": traffic,
-                "flops_per_launch": win_f, "ms_per_launch": win_ms,
-                "note": "ms_per_launch is the window's stage time inside the timed step, where it runs beside the "
-                        "memory chain on the same SMs; standalone is the same kernel alone (with its V^T staging)",
-                "standalone": {"ms_per_launch": win_alone_ms, "achieved": alone, "frac": alone / tflops_peak},
-                "peak_source": f"{pk_kind} bf16 sustained (MEASURED_PEAKS.json)" if pk_kind == "measured"
-                else "fallback 1.4 PFLOP/s sustained"}
-    total_f = win_f + delta_f + proj_f
-    layer_roof = {"flops_per_step": total_f, "achieved_tflops": total_f / (ms_step * 1e-3) / 1e12,
-                  "frac": total_f / (ms_step * 1e-3) / 1e12 / tflops_peak,
-                  "split_flops": {"window": win_f, "delta_rule": delta_f, "projections": proj_f}}
-    out = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ctx["world"], "steps": args.steps,
-           "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
-           "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded; config-1 shapes and distributions)",
-           "config": arm_config(ctx["world"]),
-           "stage_ms": stage_ms, "roofline": roof, "layer_roofline": layer_roof, "clocks": clocks,
-           "gpu_launches": 7 * args.steps}
+        roof = {"kernel": "window_prefill_kernel", "bound": "tensor", "achieved": ach, "peak": peak,
+                "unit": "TFLOP/s", "frac": ach / peak, "traffic": traffic, "flops_per_launch": win_f,
+                "ms_per_launch": win_ms,
+                "note": "ms_per_launch is the window's stage time inside the timed config-1 step, where it runs beside "
+                        "the memory chain on the same SMs; standalone is the same kernel alone (with its V^T staging)",
+                "standalone": {"ms_per_launch": win_alone_ms, "achieved": alone, "frac": alone / peak},
+                "peak_source": f"{pk_kind} bf16 {peak_kind} (MEASURED_PEAKS.json; clocks median "
+                               f"{clocks.get('sm_mhz')} of {clocks.get('sm_max_mhz')} MHz)",
+                "frac_vs_burst": ach / pk["bf16_tflops"], "frac_vs_sustained": ach / pk["bf16_tflops_sustained"]}
+    ach_layer = total_f / (ms_step * 1e-3) / 1e12
+    return {"workload": "BASELINE config 1: single Bifrost layer prefill, T=32768, B=1 per GPU, 24q/4kv heads, "
+                        "D=256, W=2048, 4 sinks, d=5120, from an empty cache",
+            "value": T * ctx["world"] / (ms_step / 1e3), "unit": "tok/s", "ms_per_step": ms_step, "steps": steps,
+            "stage_ms": stage_ms, "clocks": clocks, "roofline": roof,
+            "layer_roofline": {"flops_per_step": total_f, "achieved_tflops": ach_layer, "peak": peak,
+                               "peak_kind": peak_kind, "frac": ach_layer / peak,
+                               "frac_vs_burst": ach_layer / pk["bf16_tflops"],
+                               "frac_vs_sustained": ach_layer / pk["bf16_tflops_sustained"],
+                               "split_flops": {"window": win_f, "delta_rule": delta_f, "projections": proj_f}}}
+
+
+def run_headline(L, dev, ctx, args):
+    """The headline: one HEADLINE_T-token sequence, sequence-parallel over the N GPUs (N=1: one prefill), timed
+    with CUDA events over exactly --steps steps after --warmup, max over ranks, with clocks sampled."""
+    from heimdall_b200 import sp
+    world, rank = ctx["world"], ctx["rank"]
+    T = HEADLINE_T // world
+    ins = make_inputs(T, seed=11 + rank, device=dev)
+    if world > 1:
+        step = lambda: sp.student_sp(L, *ins)
+    else:
+        step = lambda: L.student(*ins, 0, {})
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(ctx)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(ctx["local"]) as clk:
+        torch.cuda.synchronize()
+        a.record()
+        for _ in range(args.steps):
+            step()
+        b.record()
+        torch.cuda.synchronize()
+    clocks = clk.summary()
+    t = torch.tensor([a.elapsed_time(b) / args.steps], device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    del ins
+    return float(t.item()), clocks
+
+
+def run_e2e(L, dev, ctx, steps):
+    """The headline workload through the public API from pinned host buffers, copies inside the timed region:
+    one GPU: ``BifrostLayer.student_host`` (4096-token chunks on three streams, copies overlapped with the
+    layer); N GPUs: each rank copies its segment in, runs ``sp.student_sp`` and copies its outputs back.  Max
+    over ranks."""
+    from heimdall_b200 import sp
+    world, rank = ctx["world"], ctx["rank"]
+    T = HEADLINE_T // world
+    host = [t.cpu().pin_memory() for t in make_inputs(T, 31 + rank, dev)]
+    o_host = torch.empty(1, T, H, D, dtype=torch.float32).pin_memory()
+    bi = sum(h.numel() * h.element_size() for h in host) * world
+    bo = o_host.numel() * o_host.element_size() * world
+    if world == 1:
+        def step():
+            L.student_host(*host, 0, None, out=o_host)
+        api = "BifrostLayer.student_host (4096-token chunks, copies overlapped on three streams)"
+    else:
+        dbuf = [torch.empty_like(h, device=dev) for h in host]
+
+        def step():
+            for d_, h_ in zip(dbuf, host):
+                d_.copy_(h_, non_blocking=True)
+            o, _ = sp.student_sp(L, *dbuf)
+            o_host.copy_(o, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+        api = "per rank: segment copied in, heimdall_b200.sp.student_sp, outputs copied back"
+    step()
+    torch.cuda.synchronize()
+    barrier(ctx)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        step()
+    b.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([a.elapsed_time(b) / steps], device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms = float(t.item())
+    return {"value": HEADLINE_T / (ms / 1e3), "unit": "tok/s", "ms_per_step": ms, "h2d_bytes_per_step": bi,
+            "d2h_bytes_per_step": bo, "api": api, "steps": steps}
+
+
+def run_ours(args, ctx):
+    dev = torch.device("cuda", ctx["local"])
+    torch.cuda.set_device(dev)
+    world, rank = ctx["world"], ctx["rank"]
+    L = make_layer(dev)
+    pk, pk_kind = peaks()
+    ms_step, clocks = run_headline(L, dev, ctx, args)
+    value = HEADLINE_T / (ms_step / 1e3)
+    c1 = None if args.no_config1 else run_config1(L, dev, ctx, args, pk, pk_kind)
+    e2e = None if args.no_e2e else run_e2e(L, dev, ctx, min(args.steps, 10))
+    sp_131k = run_sp(L, dev, ctx, HEADLINE_T) if world > 1 else None
+    sp_1m = None if args.no_sp else run_sp(L, dev, ctx, 1048576, steps=3, warmup=2)
+    decode = None if args.no_decode else run_decode(dev, ctx, steps=args.decode_steps, nseq=args.decode_seqs,
+                                                    nlayers=args.decode_layers)
+    if rank != 0:
+        return
+    peak, peak_kind = pick_peak(pk, clocks)
+    total_f = headline_flops(HEADLINE_T)
+    ach = total_f / (ms_step * 1e-3) / 1e12
+    # our kernels per step: x_proj, head_proj, P1, P2, V^T prep, window, P3 on one GPU; with N ranks the
+    # worst rank adds the halo's two projections, the extended-key prep, the prefix fold and the second scan
+    launches = 7 if world == 1 else 12
+    out = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
+           "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded; config-1/3 shapes and distributions)",
+           "config": arm_config(world), "clocks": clocks,
+           "layer_roofline": {"flops_per_step": total_f, "achieved_tflops": ach, "peak": peak, "peak_kind": peak_kind,
+                              "frac": ach / peak / world, "frac_vs_burst": ach / pk["bf16_tflops"] / world,
+                              "frac_vs_sustained": ach / pk["bf16_tflops_sustained"] / world,
+                              "note": "all algorithmic FLOPs of the step over N x the measured peak"},
+           "gpu_launches": launches * args.steps}
+    if c1 is not None:
+        out["roofline"] = c1["roofline"]
+        out["config1"] = c1
     if e2e is not None:
         out["e2e"] = e2e
-    if sp_res is not None:
-        out["sp"] = sp_res
-    if not args.no_cpu and ctx["world"] == 1:
+    if sp_131k is not None:
+        out["sp_131k"] = sp_131k
+    if sp_1m is not None:
+        out["sp_1m"] = sp_1m
+    if not args.no_cpu and world == 1:
         tps, cores, dt, reps = cpu_baseline()
-        out["cpu_baseline"] = {"value": tps, "unit": "tok/s", "cores": cores, "kind": "port",
-                               "sample": f"{reps} x the last 2048 tokens of the T=32768 prefill against a full cache "
+        out["cpu_baseline"] = {"value": tps, "unit": "tok/s", "cores": cores, "cpu": cpu_model(), "kind": "port",
+                               "form": "reference (state repeated per query head, hibrit.py:404-408)",
+                               "sample": f"{reps} x the last 2048 tokens of a long prefill against a full cache "
                                          f"(its steady-state per-token cost), {dt:.1f} s on {cores} threads"}
-    if ctx["world"] == 1 and not args.no_delta:
+    if world == 1 and not args.no_delta:
         out["delta_rule"] = run_delta_configs(dev)
-    if not args.no_decode and ctx["world"] == 1:
-        out["decode"] = run_decode(dev, steps=args.decode_steps, nseq=args.decode_seqs, nlayers=args.decode_layers)
+    if decode is not None:
+        out["decode"] = decode
     print(json.dumps(out), flush=True)
 
 

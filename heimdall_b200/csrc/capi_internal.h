@@ -37,8 +37,9 @@ inline int launch_status() {
   return e == cudaSuccess ? 0 : cuda_fail(e);
 }
 
+// max_ctas > 0 caps the persistent grid (to share the GPU with a concurrent kernel); 0 = one CTA per SM
 int launch_gdn_decode(const float* q, const float* k, const void* v, int v_bf16, const float* g,
                       const float* beta, const float* s_in, float* s_out, float* o, int B, int G, int R, int D,
-                      cudaStream_t stream);
+                      cudaStream_t stream, int max_ctas = 0);
 
 }  // namespace bfb

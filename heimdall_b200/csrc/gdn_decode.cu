@@ -287,7 +287,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) gdn_decode_kernel(
 
 int launch_gdn_decode(const float* q, const float* k, const void* v, int v_bf16, const float* g,
                       const float* beta, const float* s_in, float* s_out, float* o, int B, int G, int R, int D,
-                      cudaStream_t stream) {
+                      cudaStream_t stream, int max_ctas) {
   if (D % kDecCols || D > 256 || R < 1 || R > kDecMaxR) return BF_ERR_UNSUPPORTED;
   if (!aligned16(q) || !aligned16(k) || !aligned16(s_in) || !aligned16(s_out)) return BF_ERR_ALIGNMENT;
   DeviceState st;
@@ -305,7 +305,8 @@ int launch_gdn_decode(const float* q, const float* k, const void* v, int v_bf16,
   if ((rc = ensure_smem_attr((const void*)gdn_decode_kernel<6>, kDecSmem)) != BF_OK) return rc;
   if ((rc = ensure_smem_attr((const void*)gdn_decode_kernel<0>, kDecSmem)) != BF_OK) return rc;
   const int nitems = B * G * (D / kDecCols);
-  const int grid = nitems < st.sm_count ? nitems : st.sm_count;
+  const int cap = (max_ctas > 0 && max_ctas < st.sm_count) ? max_ctas : st.sm_count;
+  const int grid = nitems < cap ? nitems : cap;
   if (R == 6 && D == 256)
     gdn_decode_kernel<6><<<grid, kDecThreads, kDecSmem, stream>>>(smap, omap, q, k, v, v_bf16, g, beta, o, B * G, R, D,
                                                                  st.err);

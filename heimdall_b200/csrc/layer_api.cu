@@ -68,6 +68,10 @@ int mem_inputs_impl(const DeviceState& st, const bf_layer* L, const void* x, con
 
 namespace bfb {
 int launch_win_dec(WinDecArgs a, cudaStream_t stream);
+int launch_win_dec_split(WinDecArgs a, cudaStream_t stream, int max_ctas);
+int launch_win_dec_combine(WinDecArgs a, cudaStream_t stream);
+int win_dec_check(WinDecArgs& a);
+int win_dec_split_items(const WinDecArgs& a);
 }
 
 using namespace bfb;
@@ -118,6 +122,7 @@ size_t bf_layer_decode_workspace(int B, int H, int G, int D, int window) {
   n += align_up((size_t)B * G * 4, 256) * 2;      // g_e, b_e
   n += align_up((size_t)B * H * D * 4, 256);      // o_mem
   n += align_up(win_dec_workspace(B, G, R, D, window), 256);
+  n += align_up(x_proj_scratch_bytes(B, 1 << 14), 256);   // split-K partials of the gate projections (d <= 16384)
   return n;
 }
 
@@ -158,68 +163,9 @@ int bf_bifrost_layer_decode(const bf_layer* L, const void* x, const void* q, con
   float* b_e = reinterpret_cast<float*>(take((size_t)B * G * 4));
   float* o_mem = reinterpret_cast<float*>(take((size_t)B * H * D * 4));
   float* part = reinterpret_cast<float*>(take(win_dec_workspace(B, G, R, D, W)));
+  const size_t xs_bytes = x_proj_scratch_bytes(B, 1 << 14);
+  float* xs = reinterpret_cast<float*>(take(xs_bytes));
 
-  // memory inputs of the new tokens (T = 1 per sequence, per-sequence positions).  The gate projections (g, beta
-  // and the mix logit of the new tokens) feed only the window kernels' last step, so when the window's split
-  // partials (written by its first kernel, after the state update) can hold their split-K partials, they run
-  // on the greatest-priority side stream beside the head projections, the evicted-entry gather and the state
-  // update, and are joined before the window.  Otherwise they run in line with o_mem (written first by the
-  // state update) as their scratch.
-  const size_t part_bytes = win_dec_workspace(B, G, R, D, W);
-  const size_t xs_need = x_proj_scratch_bytes(B, L->d);
-  cudaStream_t sx = (xs_need > 0 && xs_need <= part_bytes) ? side_stream(st, 1) : nullptr;
-  cudaEvent_t ev_fork = nullptr, ev_x = nullptr;
-  auto drop_events = [&]() {
-    if (ev_fork) cudaEventDestroy(ev_fork);
-    if (ev_x) cudaEventDestroy(ev_x);
-    ev_fork = ev_x = nullptr;
-  };
-  if (sx) {
-    if (cudaEventCreateWithFlags(&ev_fork, cudaEventDisableTiming) != cudaSuccess ||
-        cudaEventCreateWithFlags(&ev_x, cudaEventDisableTiming) != cudaSuccess ||
-        cudaEventRecord(ev_fork, stream) != cudaSuccess || cudaStreamWaitEvent(sx, ev_fork, 0) != cudaSuccess) {
-      rc = cuda_fail();
-      drop_events();
-      return rc;
-    }
-    stage_mark(ST_XPROJ, 0, sx);
-    rc = launch_x_proj(static_cast<const __nv_bfloat16*>(x), weights_x(L->wbuf, L->H, L->G, L->D), L->ab_b,
-                       L->mix_b, L->A_log, L->dt_bias, L->decay_mask, g, beta, mixx, pos, 0, B, 1, L->d, L->G, L->H,
-                       L->sinks, part, part_bytes, st.err, sx);
-    if (!rc && cudaEventRecord(ev_x, sx) != cudaSuccess) rc = cuda_fail();
-    if (rc) {
-      drop_events();
-      return rc;
-    }
-    stage_mark(ST_XPROJ, 1, sx);
-    stage_mark(ST_HEADPROJ, 0, stream);
-    rc = launch_head_proj(static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
-                          weights_heads(L->wbuf), qm, nullptr, km, 1, B, L->H, L->G, st.sm_count, st.err, stream);
-    stage_mark(ST_HEADPROJ, 1, stream);
-  } else {
-    rc = mem_inputs_impl(st, L, x, q, k, pos, 0, B, 1, qm, km, g, beta, mixx, stream, nullptr, o_mem,
-                         (size_t)B * H * D * 4);
-  }
-  if (rc) {
-    drop_events();
-    return rc;
-  }
-  if (memory) {
-    // the token leaving the window (position p - W) is written into memory before the read
-    rc = launch_gather_evicted(C->ring_km, static_cast<const __nv_bfloat16*>(C->ring_v), C->ring_g, C->ring_beta,
-                               C->ring_pos, C->ring_pos_bstride, pos, B, G, W, D, k_e, v_e, g_e, b_e, stream);
-    if (rc) {
-      drop_events();
-      return rc;
-    }
-    stage_mark(ST_DEC_STATE, 0, stream);
-    rc = launch_gdn_decode(qm, k_e, v_e, 0, g_e, b_e, C->S, C->S, o_mem, B, G, R, D, stream);
-    if (rc) {
-      drop_events();
-      return rc;
-    }
-    stage_mark(ST_DEC_STATE, 1, stream);
-  }
   WinDecArgs a{};
   a.qr = static_cast<const __nv_bfloat16*>(qr);
   a.kr = static_cast<const __nv_bfloat16*>(kr);
@@ -254,15 +200,73 @@ int bf_bifrost_layer_decode(const bf_layer* L, const void* x, const void* q, con
   a.ring_g = C->ring_g;
   a.ring_beta = C->ring_beta;
   a.ring_pos_w = C->ring_pos;
-  if (sx) {   // join the gate projections: the window's partials were their scratch
-    rc = cudaStreamWaitEvent(stream, ev_x, 0) != cudaSuccess ? cuda_fail() : BF_OK;
-    drop_events();
-    if (rc) return rc;
+  if ((rc = win_dec_check(a)) != BF_OK) return rc;
+
+  // Three independent chains meet in the combine kernel:
+  //   caller's stream:          head projections (qm, km) -> evicted ring entry -> state update (o_mem, S)
+  //   greatest-priority stream: gate projections (g, beta, mix logit), split-K over their own scratch
+  //   least-priority stream:    window split over the ring (per-split partials)
+  // The state update and the window split are both HBM-bound and read disjoint data (the state; the ring's K
+  // and V), so they run at the same time on disjoint SM shares (persistent grids sized by their bytes) instead
+  // of one after the other.  The combine reads all three results and writes the new token into its ring slot,
+  // which is the slot of the evicted entry: it runs after the gather on the caller's stream.
+  cudaStream_t sx = side_stream(st, 1), sw = side_stream(st, 0);
+  if (!sx || !sw) return cuda_fail();
+  struct Events {
+    cudaEvent_t e[3] = {nullptr, nullptr, nullptr};
+    ~Events() {
+      for (cudaEvent_t x : e)
+        if (x) cudaEventDestroy(x);
+    }
+  } evs;
+  cudaEvent_t &ev_fork = evs.e[0], &ev_x = evs.e[1], &ev_w = evs.e[2];
+  for (cudaEvent_t* e : {&ev_fork, &ev_x, &ev_w})
+    if (cudaEventCreateWithFlags(e, cudaEventDisableTiming) != cudaSuccess) return cuda_fail();
+  if (cudaEventRecord(ev_fork, stream) != cudaSuccess || cudaStreamWaitEvent(sx, ev_fork, 0) != cudaSuccess ||
+      cudaStreamWaitEvent(sw, ev_fork, 0) != cudaSuccess)
+    return cuda_fail();
+  // SM shares: the state update moves 2 D^2 fp32 per (sequence, KV head), the window 2 W D bf16
+  const int sms = st.sm_count;
+  int n_state = 0, n_win = sms;
+  if (memory) {
+    const double sb = 2.0 * D * D * 4, wb = 2.0 * W * D * 2;
+    n_state = (int)(sms * sb / (sb + wb) + 0.5);
+    n_state = n_state < 1 ? 1 : (n_state > sms - 1 ? sms - 1 : n_state);
+    n_win = sms - n_state;
   }
-  stage_mark(ST_DEC_WIN, 0, stream);
-  rc = launch_win_dec(a, stream);
-  stage_mark(ST_DEC_WIN, 1, stream);
-  return rc;
+  // window split (least priority)
+  stage_mark(ST_DEC_WIN, 0, sw);
+  rc = launch_win_dec_split(a, sw, n_win);
+  if (rc) return rc;
+  stage_mark(ST_DEC_WIN, 1, sw);
+  if (cudaEventRecord(ev_w, sw) != cudaSuccess) return cuda_fail();
+  // gate projections (greatest priority)
+  stage_mark(ST_XPROJ, 0, sx);
+  rc = launch_x_proj(static_cast<const __nv_bfloat16*>(x), weights_x(L->wbuf, L->H, L->G, L->D), L->ab_b, L->mix_b,
+                     L->A_log, L->dt_bias, L->decay_mask, g, beta, mixx, pos, 0, B, 1, L->d, L->G, L->H, L->sinks, xs,
+                     xs_bytes, st.err, sx);
+  if (rc) return rc;
+  stage_mark(ST_XPROJ, 1, sx);
+  if (cudaEventRecord(ev_x, sx) != cudaSuccess) return cuda_fail();
+  // head projections, then (memory on) the evicted entry and the state update
+  stage_mark(ST_HEADPROJ, 0, stream);
+  rc = launch_head_proj(static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
+                        weights_heads(L->wbuf), qm, nullptr, km, 1, B, L->H, L->G, st.sm_count, st.err, stream);
+  if (rc) return rc;
+  stage_mark(ST_HEADPROJ, 1, stream);
+  if (memory) {
+    // the token leaving the window (position p - W) is written into memory before the read
+    rc = launch_gather_evicted(C->ring_km, static_cast<const __nv_bfloat16*>(C->ring_v), C->ring_g, C->ring_beta,
+                               C->ring_pos, C->ring_pos_bstride, pos, B, G, W, D, k_e, v_e, g_e, b_e, stream);
+    if (rc) return rc;
+    stage_mark(ST_DEC_STATE, 0, stream);
+    rc = launch_gdn_decode(qm, k_e, v_e, 0, g_e, b_e, C->S, C->S, o_mem, B, G, R, D, stream, n_state);
+    if (rc) return rc;
+    stage_mark(ST_DEC_STATE, 1, stream);
+  }
+  if (cudaStreamWaitEvent(stream, ev_x, 0) != cudaSuccess || cudaStreamWaitEvent(stream, ev_w, 0) != cudaSuccess)
+    return cuda_fail();
+  return launch_win_dec_combine(a, stream);
 }
 
 }  // extern "C"

@@ -520,13 +520,21 @@ static int launch_split(const CUtensorMap& kmap, const CUtensorMap& vmap, const 
   return BF_OK;
 }
 
-int launch_win_dec(WinDecArgs a, cudaStream_t stream) {
+int win_dec_check(WinDecArgs& a) {
   a.nsplit = (a.W + kWD_Keys - 1) / kWD_Keys;
   if (a.D != 256 || a.R < 1 || a.R > kWD_MaxR || a.nsplit > kWD_MaxSplits || a.ns + 1 > kWD_MaxExtra)
     return BF_ERR_UNSUPPORTED;
   if (!aligned16(a.qr) || !aligned16(a.kr) || (a.ns && !aligned16(a.sink_k))) return BF_ERR_ALIGNMENT;
+  return BF_OK;
+}
+
+int win_dec_split_items(const WinDecArgs& a) { return a.B * a.G * ((a.W + kWD_Keys - 1) / kWD_Keys); }
+
+int launch_win_dec_split(WinDecArgs a, cudaStream_t stream, int max_ctas) {
+  int rc = win_dec_check(a);
+  if (rc) return rc;
   DeviceState st;
-  int rc = device_state(&st);
+  rc = device_state(&st);
   if (rc) return rc;
   CUtensorMap kmap, vmap;
   const uint64_t rows = (uint64_t)a.B * a.G * a.W;
@@ -535,7 +543,8 @@ int launch_win_dec(WinDecArgs a, cudaStream_t stream) {
   rc = make_tmap_kmajor(&vmap, a.ring_v, BF_BF16, rows, 256, 256, kWT_N, 4);
   if (rc) return rc;
   const int nitems = a.B * a.G * a.nsplit;
-  const int grid = nitems < st.sm_count ? nitems : st.sm_count;
+  const int cap = (max_ctas > 0 && max_ctas < st.sm_count) ? max_ctas : st.sm_count;
+  const int grid = nitems < cap ? nitems : cap;
   switch (a.R) {
     case 1: rc = launch_split<1>(kmap, vmap, a, grid, st.err, stream); break;
     case 2: rc = launch_split<2>(kmap, vmap, a, grid, st.err, stream); break;
@@ -547,8 +556,20 @@ int launch_win_dec(WinDecArgs a, cudaStream_t stream) {
     default: rc = launch_split<8>(kmap, vmap, a, grid, st.err, stream); break;
   }
   if (rc) return rc;
+  return launch_status();
+}
+
+int launch_win_dec_combine(WinDecArgs a, cudaStream_t stream) {
+  int rc = win_dec_check(a);
+  if (rc) return rc;
   win_dec_combine_kernel<<<dim3(a.B * a.G, a.R), kWD_Threads, 0, stream>>>(a);
   return launch_status();
+}
+
+int launch_win_dec(WinDecArgs a, cudaStream_t stream) {
+  int rc = launch_win_dec_split(a, stream, 0);
+  if (rc) return rc;
+  return launch_win_dec_combine(a, stream);
 }
 
 int launch_gather_evicted(const float* ring_km, const __nv_bfloat16* ring_v, const float* ring_g,

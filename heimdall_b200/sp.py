@@ -91,13 +91,19 @@ def halo_cache(kr_h, v_h, km_h, g_h, b_h, sink_k, sink_v, S_in, start: int, W: i
     return cache
 
 
-def student_sp(L, x, q, k, v, qr, kr, group=None, memory: bool = True):
+def student_sp(L, x, q, k, v, qr, kr, group=None, memory: bool = True, timeline=None, phase_hook=None):
     """One layer prefill of a sequence split over the ranks of ``group`` in rank order, from an empty cache.
 
     Every rank passes its own T consecutive tokens (the same T on every rank, T >= W) in the layouts of
     ``BifrostLayer.student``: x [B,T,d], q [B,T,H,D], k/v [B,T,G,D], qr [B,H,T,D], kr [B,G,T,D] (bf16, on
     this rank's GPU).  Returns (o, cache): this rank's outputs [B,T,H,D] fp32 and its cache after the call
     (on the last rank that is the cache of the whole sequence).  Every rank must call it (collectives).
+
+    Instrumentation (optional, GPU only): ``timeline`` is a list that receives (label, CUDA event) pairs
+    recorded on the call's stream at the start and after each step (halo exchanged, halo memory inputs, state
+    map, maps gathered, incoming state folded, done); ``phase_hook(phase)`` is called right before each of the
+    two layer phases (0: memory inputs, per-chunk products, state map and the window launch; 1: the rest), e.g.
+    to install per-phase stage events with ``bf_stage_events``.
     """
     T = x.shape[1]
     if T < L.window or T < L.sinks:
@@ -106,12 +112,12 @@ def student_sp(L, x, q, k, v, qr, kr, group=None, memory: bool = True):
     # lowest-priority stream and left running, then yields the SMs to everything else of the call (the
     # exchange, the fold of the maps, the second scan) instead of holding them back until it ends.
     if x.device.type != "cuda":   # the host logic on CPU tensors (a CPU restatement of the layer)
-        return _student_sp(L, x, q, k, v, qr, kr, group, memory)
+        return _student_sp(L, x, q, k, v, qr, kr, group, memory, None, None)
     cur = torch.cuda.current_stream(x.device)
     hp = _priority_stream(x.device)
     hp.wait_stream(cur)
     with torch.cuda.stream(hp):
-        o, cache = _student_sp(L, x, q, k, v, qr, kr, group, memory)
+        o, cache = _student_sp(L, x, q, k, v, qr, kr, group, memory, timeline, phase_hook)
     cur.wait_stream(hp)   # later work on the caller's stream (reuse of the inputs' memory included) waits
     for t in [o, *(z for z in cache.values() if isinstance(z, torch.Tensor))]:
         t.record_stream(cur)   # allocated on the priority stream, used on the caller's
@@ -128,7 +134,18 @@ def _priority_stream(device):
     return _PRIORITY_STREAMS[key]
 
 
-def _student_sp(L, x, q, k, v, qr, kr, group, memory):
+def _student_sp(L, x, q, k, v, qr, kr, group, memory, timeline, phase_hook):
+    def mark(label):
+        if timeline is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            timeline.append((label, ev))
+
+    def hook(phase):
+        if phase_hook is not None:
+            phase_hook(phase)
+
+    mark("start")
     rank = dist.get_rank(group)
     world = dist.get_world_size(group)
     B, T = x.shape[:2]
@@ -144,16 +161,21 @@ def _student_sp(L, x, q, k, v, qr, kr, group, memory):
         dist.broadcast(sink_v, src=_peer(group, 0), group=group)
     # halo: the last W tokens of the previous rank, and their memory inputs
     halo = _p2p_shift([x[:, -W:], k[:, -W:], v[:, -W:], kr[:, :, -W:]], rank, world, group)
+    mark("halo_exchanged")
     first = rank == 0
     cache = {}
     if not first:
         km_h, g_h, b_h = _halo_inputs(L, halo, start, W, q)
         cache = halo_cache(halo[3], halo[2], km_h, g_h, b_h, sink_k, sink_v, None, start, W)
+    mark("halo_inputs")
     if not memory:
         o = L.student(x, q, k, v, qr, kr, start, cache, memory=False)
+        mark("done")
         return o, cache
     # phase 1: this segment's state map (memory inputs and per-chunk products are kept for phase 2)
+    hook(0)
     M, N, handle = L.prefill_sp_begin(x, q, k, v, qr, kr, start, cache)
+    mark("maps")
     if world > 1:
         Ml = [torch.empty_like(M) for _ in range(world)]
         Nl = [torch.empty_like(N) for _ in range(world)]
@@ -162,14 +184,18 @@ def _student_sp(L, x, q, k, v, qr, kr, group, memory):
         Ms, Ns = torch.stack(Ml), torch.stack(Nl)
     else:
         Ms, Ns = M[None], N[None]
+    mark("gathered")
     finite = _maps_finite(Ms, Ns)
     S_in = F_.apply_prefix(Ms[:rank], Ns[:rank])[rank]
     if cache.get("S") is not None:
         cache["S"].copy_(S_in)
     else:
         cache["S"] = S_in.contiguous()
+    mark("folded")
     # phase 2: the rest of the layer from the incoming state
+    hook(1)
     o = L.prefill_sp_finish(handle)
+    mark("done")
     _raise_if_corrupted(finite)
     return o, cache
 

@@ -326,7 +326,7 @@ def mix(p: LayerParams, o_win, o_mem, gamma, dtype=torch.float32):
 
 
 def student(p: LayerParams, x, q, k, v, qr, kr, start: int, cache: Optional[dict], memory: bool = True,
-            dtype=torch.float32):
+            dtype=torch.float32, gqa_native: bool = True):
     """The converted layer core, restating ``HybridAttention._student`` (``heimdall/hibrit.py:363-424``).
 
     x [B,t,d]; q [B,t,H,D] (pre-RoPE); k, v [B,t,G,D]; qr [B,H,t,D]; kr [B,G,t,D]; ``start`` is the
@@ -336,6 +336,14 @@ def student(p: LayerParams, x, q, k, v, qr, kr, start: int, cache: Optional[dict
     Memory writes are delayed by W: the write stream at step i is token i - W (from the ring for the
     first W rows, then the new tokens), so a token enters memory exactly when it leaves the window.
     Returns o [B,t,H,D] in ``dtype``.
+
+    ``gqa_native`` (default) runs the memory of a prefill with one state per KV head read by its R query heads
+    (``gdn_gqa``, the arithmetic of ``heimdall/motor.py:70-102``).  ``gqa_native=False`` follows the reference's
+    own ``_student`` statement for statement instead: for t > 1 the write stream and the state are repeated for
+    every query head and ``gdn_chunked`` runs over H heads, then every R-th state is kept
+    (``heimdall/hibrit.py:404-408``); for t == 1 the inline update (``:398-403``).  Both give the same
+    numbers (the reference's own check, ``tests/test_motor.py:28-39``); the second does the reference's amount
+    of work (R times the state traffic), which is what the timed CPU baseline runs.
     """
     B, t, _ = x.shape
     H, G, D = q.shape[2], k.shape[2], q.shape[3]
@@ -375,7 +383,13 @@ def student(p: LayerParams, x, q, k, v, qr, kr, start: int, cache: Optional[dict
         wg = torch.cat((rg.to(dtype) * vf, g), 1)[:, :t]
         wb = torch.cat((rb.to(dtype) * vf, beta), 1)[:, :t]
         s0 = st.get("S")
-        o_mem, Snew = gdn_gqa(qm.reshape(B, t, G, R, D), wk, wv, wg, wb, 64, s0, dtype)
+        if gqa_native or t == 1:
+            o_mem, Snew = gdn_gqa(qm.reshape(B, t, G, R, D), wk, wv, wg, wb, 64, s0, dtype)
+        else:
+            rep = lambda z: z.repeat_interleave(R, 2)
+            o_mem, Snew = gdn_chunked(qm, rep(wk), rep(wv), rep(wg), rep(wb), 64,
+                                      None if s0 is None else s0.repeat_interleave(R, 1), dtype)
+            Snew = Snew[:, ::R]
         o_mem = o_mem.reshape(B, t, H, D)
         gm = gate(p, x, lse, pos, dtype)
         o = mix(p, o_win, o_mem, gm, dtype)

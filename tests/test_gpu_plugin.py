@@ -79,11 +79,13 @@ def test_prepare_installs_and_routes_every_entry_point():
         bad[W + 5] = -1               # a hole inside the window: not the contiguous form
         with pytest.raises(NotImplementedError):
             cls._window(attn, cu(qr), cu(ext_k), cu(ext_v), cu(bad), cu(kr[:, :, :S]), cu(vt[:, :, :S]), cu(pos))
-        # the module-level op
+        # the B200 op by name (exported by the plugin; the module-level op of the host package is left to
+        # its linear-attention layers)
+        assert m["kernels"].delta_rule is not plugin.delta_rule
         g = -torch.rand(1, T, G, generator=gen) * 0.1
         beta = torch.rand(1, T, G, generator=gen)
         kn = torch.nn.functional.normalize(f(k), dim=-1)
-        o, s = m["kernels"].delta_rule(cu(kn), cu(kn), cu(f(v)), cu(g), cu(beta), 64, None)
+        o, s = plugin.delta_rule(cu(kn), cu(kn), cu(f(v)), cu(g), cu(beta), 64, None)
         o_r, s_r = ob.gdn_chunked(kn, kn, f(v), g, beta, 64, None)
         assert ob.rel_l2(o.cpu(), o_r) < O_TOL and ob.rel_l2(s.cpu(), s_r) < 1e-3
         # parameters updated in place -> the cached layer is rebuilt

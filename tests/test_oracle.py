@@ -148,3 +148,14 @@ def test_oracle_against_live_reference():
     o3, s3 = delta_rule_reference(q[:, :, :, 0], k, v, g, beta, 32, s0)
     o4, s4 = ob.gdn_chunked(q[:, :, :, 0], k, v, g, beta, 32, s0)
     assert (o3 - o4).abs().max() < 1e-5 and (s3 - s4).abs().max() < 1e-5
+
+
+def test_student_reference_form_equals_gqa_form(golden_layer):
+    """The oracle's statement-for-statement form of the reference's prefill memory (state repeated per query
+    head, hibrit.py:404-408) equals its GQA-native form (the reference's pin tests/test_motor.py:28-39), and
+    both match the reference's own outputs."""
+    c, p = _layer(golden_layer, "d256")
+    f = lambda k: c[k].float()
+    a = ob.student(p, f("x"), f("q"), f("k"), f("v"), f("qr"), f("kr"), 0, None)
+    b = ob.student(p, f("x"), f("q"), f("k"), f("v"), f("qr"), f("kr"), 0, None, gqa_native=False)
+    assert (a - b).abs().max() < 1e-5
