@@ -109,12 +109,22 @@ def make_layer(device, seed=0):
 
 
 def layer_flops(T):
-    """Algorithmic FLOPs of one layer prefill from an empty cache (counting rules of the survey, section 8d)."""
-    win = 0
-    for t in range(T):
-        lo = max(t - W + 1, S)
-        nwin = max(0, t - lo + 1)
-        win += nwin + min(S, t + 1)
+    """Algorithmic FLOPs of one layer prefill from an empty cache (counting rules of the survey, section 8d):
+    window 4 H D per (query, valid key) pair, delta rule G (6CD + 4D^2 + R(4CD + 2D^2)) per write step (C = 64),
+    projections 2D^2(H+G) + 2d(2G+H) per token."""
+    # valid keys of the query at position t: min(S, t+1) sinks plus the window keys max(S, t-W+1) .. t
+    def win_keys(t0, t1):    # sum over t in [t0, t1) of the window keys, for t >= S (lo = max(S, t-W+1))
+        total = 0
+        a = max(t0, S)
+        b1 = min(t1, S + W - 1)              # t - W + 1 <= S: lo = S, keys = t - S + 1
+        if b1 > a:
+            total += (b1 - a) * (a + b1 - 1) // 2 - (S - 1) * (b1 - a)
+        a2 = max(t0, S + W - 1, a)           # lo = t - W + 1: keys = W
+        if t1 > a2:
+            total += (t1 - a2) * W
+        return total
+    sinks = sum(min(S, t + 1) for t in range(min(T, S))) + S * max(0, T - S)
+    win = win_keys(0, T) + sinks
     win_flops = 4 * H * D * win
     C = 64
     delta_per_tok = G * (6 * C * D + 4 * D * D + R * (4 * C * D + 2 * D * D))
@@ -397,10 +407,42 @@ def run_delta_configs(device, steps=10, warmup=3):
     args4 = [z.to(device) for z in (q4, k4, v4, g4, b4)]
     cud = cu.to(device)
     ms4 = _time_device(lambda: delta_rule_gqa(*args4, 64, None, cu_seqlens=cud), steps, warmup)
-    out["config4"] = {"workload": f"BASELINE config 4: 8 packed sequences ({lens.tolist()} tokens, {T4} total) "
-                                  f"with cu_seqlens, 4 KV x 6 query heads, D=256",
+    out["config4"] = {"workload": f"BASELINE config 4, the delta-rule op alone: 8 packed sequences ({lens.tolist()} "
+                                  f"tokens, {T4} total) with cu_seqlens, 4 KV x 6 query heads, D=256",
                       "value": T4 / (ms4 / 1e3), "unit": "tok/s", "ms_per_step": ms4}
+    del args4
+    out["config4_layer"] = run_config4_layer(device, lens.tolist(), steps=max(3, steps // 2), warmup=2)
     return out
+
+
+def run_config4_layer(device, lens, steps=5, warmup=2):
+    """BASELINE config 4 as the full layer (window + memory + gate): the 8 packed sequences through
+    ``BifrostLayer.student_varlen``, each with its own positions, sinks, ring and a state reset at its start;
+    fixed-rate decays (the x-dependent decay input zeroed) with half-lives logspace(log10 2048, 6, 4) and the
+    last KV head archival; inputs as config 1."""
+    L = make_layer(device, seed=4)
+    life = torch.logspace(math.log10(2048), 6.0, G, device=device)
+    L.p["ab_w"][:G].zero_()
+    L.p["ab_b"][:G].zero_()
+    L.p["A_log"].copy_((math.log(2.0) / life / torch.nn.functional.softplus(L.p["dt_bias"])).log())
+    L.p["decay_mask"].fill_(1.0)
+    L.p["decay_mask"][-1] = 0.0
+    L.refresh()
+    T = sum(lens)
+    cu = [0]
+    for n in lens:
+        cu.append(cu[-1] + n)
+    ins = make_inputs(T, seed=41, device=device)
+    ms = _time_device(lambda: L.student_varlen(*ins, cu), steps, warmup)
+    win_f = sum(sum(layer_flops_split(n)) for n in lens)
+    del ins
+    return {"workload": f"BASELINE config 4, the full layer: 8 packed sequences ({lens} tokens, {T} total), "
+                        f"window + memory + gate, per-sequence state reset", "value": T / (ms / 1e3), "unit": "tok/s",
+            "ms_per_step": ms, "achieved_tflops": win_f / (ms * 1e-3) / 1e12}
+
+
+def layer_flops_split(T):
+    return layer_flops(T)
 
 
 def run_decode(device, ctx, steps=256, warmup=8, nseq=64, nlayers=12):
@@ -460,8 +502,9 @@ def run_decode(device, ctx, steps=256, warmup=8, nseq=64, nlayers=12):
     with torch.cuda.graph(graph, stream=stream):
         step()
     torch.cuda.synchronize()
-    # state-update kernel alone: time one layer's stage with events (eager, same stream)
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * 10)]
+    # per-kernel stage times of one layer (eager, same stream)
+    NST = 12
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * NST)]
     for e in ev:
         e.record()
     torch.cuda.synchronize()
@@ -479,18 +522,26 @@ def run_decode(device, ctx, steps=256, warmup=8, nseq=64, nlayers=12):
     us_step = float(t_.item())
     # live per-kernel timing of the state update and the window (eager step with stage events)
     handles = ctypes_array([e.cuda_event for e in ev])
-    st_us, win_us = [], []
+    names = {0: "x_proj", 1: "head_proj", 10: "gather", 8: "state_update", 9: "window_split", 11: "combine"}
+    samples = {n: [] for n in names.values()}
+    layer_us = []
     with torch.cuda.stream(stream):
         for _ in range(4):
             for L, c, i, o, ws in zip(layers, structs, ins, outs, wss):
-                _lib.call("bf_stage_events", handles, 10)
+                _lib.call("bf_stage_events", handles, NST)
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record()
                 _lib.call("bf_bifrost_layer_decode", ctypes_ref(L.struct), ptr(i["x"]), ptr(i["q"]), ptr(i["k"]),
                           ptr(i["v"]), ptr(i["qr"]), ptr(i["kr"]), ptr(pos), nseq, ctypes_ref(c), 1, ptr(o), 0,
                           ptr(ws), ws.numel(), stream.cuda_stream)
+                e1.record()
                 torch.cuda.synchronize()
-                st_us.append(ev[16].elapsed_time(ev[17]) * 1e3)
-                win_us.append(ev[18].elapsed_time(ev[19]) * 1e3)
+                layer_us.append(e0.elapsed_time(e1) * 1e3)
+                for j, n in names.items():
+                    samples[n].append(ev[2 * j].elapsed_time(ev[2 * j + 1]) * 1e3)
     _lib.call("bf_stage_events", None, 0)
+    st_us, win_us = samples["state_update"], samples["window_split"]
     del graph
     state_bytes = 2 * nseq * G * D * D * 4
     win_bytes = nseq * G * (W + S) * D * 2 * 2
@@ -504,7 +555,10 @@ def run_decode(device, ctx, steps=256, warmup=8, nseq=64, nlayers=12):
             "per_gpu_note": "state_update / window / step_roofline are for one GPU's shard (rank 0)",
             "state_update": {"us": su, "bytes": state_bytes, "achieved_gbs": state_bytes / (su * 1e-6) / 1e9,
                              "peak_gbs": pk["hbm_gbs"], "frac": state_bytes / (su * 1e-6) / 1e9 / pk["hbm_gbs"]},
-            "window": {"us": wu, "bytes": win_bytes, "achieved_gbs": win_bytes / (wu * 1e-6) / 1e9},
+            "window": {"us": wu, "bytes": win_bytes, "achieved_gbs": win_bytes / (wu * 1e-6) / 1e9,
+                       "frac": win_bytes / (wu * 1e-6) / 1e9 / pk["hbm_gbs"], "kernel": "window split (combine apart)"},
+            "stage_us": {n: statistics.fmean(v) for n, v in samples.items()},
+            "eager_layer_us": statistics.fmean(layer_us),
             "step_roofline": {"bytes": per_layer_bytes * nlayers,
                               "frac": per_layer_bytes * nlayers / (us_step * 1e-6) / 1e9 / pk["hbm_gbs"]}}
 

@@ -4,7 +4,7 @@
 #include <stdint.h>
 
 #define BF_ABI_VERSION 1
-#define BF_MAX_STAGES 10
+#define BF_MAX_STAGES 12
 
 namespace bfb {
 
@@ -23,7 +23,7 @@ cudaStream_t side_stream(const DeviceState& st, int which);
 // per-stage timing hooks (no-ops unless bf_stage_events installed events)
 void stage_mark(int stage, int end, cudaStream_t stream);
 enum Stage { ST_XPROJ = 0, ST_HEADPROJ, ST_GDN_P1, ST_GDN_P2, ST_GDN_P3, ST_WIN_PREP, ST_WIN, ST_CACHE, ST_DEC_STATE,
-             ST_DEC_WIN };
+             ST_DEC_WIN, ST_DEC_GATHER, ST_DEC_COMBINE };
 bool aligned16(const void* p);
 // Opts `fn` into `bytes` of dynamic shared memory on the current device.  cudaFuncSetAttribute applies to
 // the current device only, so this is done once per (kernel, device), under a lock; later calls only look

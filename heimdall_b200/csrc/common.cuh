@@ -205,6 +205,11 @@ __device__ __forceinline__ void tma_store_commit() { asm volatile("cp.async.bulk
 __device__ __forceinline__ void tma_store_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 // wait until the committed stores have finished reading shared memory
 __device__ __forceinline__ void tma_store_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// wait until at most N of this thread's committed bulk-store groups have not finished reading shared memory
+template <int N>
+__device__ __forceinline__ void tma_store_wait_read_pending() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
 
 // ----------------------------------------------------------------------------------------------
 // tcgen05 (Tensor Memory + 5th-gen MMA), cta_group::1 only

@@ -170,6 +170,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) gdn_decode_kernel(
     }
   } else if (warp == 9) {
     // ------------------------------------------------------------------ stores: the updated tile by TMA
+    // two stores in flight: after issuing item n's store, wait until item n-1's has read its stage, then free it
     if (lane == 0) {
       tma_prefetch(&omap);
       int n = 0;
@@ -179,9 +180,13 @@ __global__ void __launch_bounds__(kDecThreads, 1) gdn_decode_kernel(
         const int bg = item / ncb, col0 = (item % ncb) * kDecCols;
         tma_store_2d(&omap, smem + s * kDecStage, col0, bg * D);
         tma_store_commit();
-        tma_store_wait_read();
-        mbar_arrive(&empty[s]);
+        if (n >= 1) {
+          tma_store_wait_read_pending<1>();
+          mbar_arrive(&empty[(n - 1) % kDecStages]);
+        }
       }
+      tma_store_wait_read();
+      if (n >= 1) mbar_arrive(&empty[(n - 1) % kDecStages]);
       tma_store_wait_all();
     }
   } else {
@@ -289,7 +294,7 @@ int launch_gdn_decode(const float* q, const float* k, const void* v, int v_bf16,
                       const float* beta, const float* s_in, float* s_out, float* o, int B, int G, int R, int D,
                       cudaStream_t stream, int max_ctas) {
   if (D % kDecCols || D > 256 || R < 1 || R > kDecMaxR) return BF_ERR_UNSUPPORTED;
-  if (!aligned16(q) || !aligned16(k) || !aligned16(s_in) || !aligned16(s_out)) return BF_ERR_ALIGNMENT;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(s_in) || !aligned16(s_out)) return BF_ERR_ALIGNMENT;
   DeviceState st;
   int rc = device_state(&st);
   if (rc) return rc;

@@ -202,16 +202,16 @@ int bf_bifrost_layer_decode(const bf_layer* L, const void* x, const void* q, con
   a.ring_pos_w = C->ring_pos;
   if ((rc = win_dec_check(a)) != BF_OK) return rc;
 
-  // Three independent chains meet in the combine kernel:
-  //   caller's stream:          head projections (qm, km) -> evicted ring entry -> state update (o_mem, S)
-  //   greatest-priority stream: gate projections (g, beta, mix logit), split-K over their own scratch
-  //   least-priority stream:    window split over the ring (per-split partials)
-  // The state update and the window split are both HBM-bound and read disjoint data (the state; the ring's K
-  // and V), so they run at the same time on disjoint SM shares (persistent grids sized by their bytes) instead
-  // of one after the other.  The combine reads all three results and writes the new token into its ring slot,
-  // which is the slot of the evicted entry: it runs after the gather on the caller's stream.
-  cudaStream_t sx = side_stream(st, 1), sw = side_stream(st, 0);
-  if (!sx || !sw) return cuda_fail();
+  // The evicted ring entry (read only by the state update) and the gate projections (g, beta and the mix logit
+  // of the new tokens, read only by the combine kernel) run on the greatest-priority side stream, the gate
+  // projections over their own split-K scratch, beside the head projections.  On the caller's stream: the head
+  // projections (qm, km) and the state update (o_mem, S), then the window split over the ring and the combine,
+  // which also writes the new token into its ring slot (the slot of the evicted entry, read before by the
+  // gather).  The state update and the window
+  // split are both HBM-bound persistent kernels that each need the whole GPU to reach their bandwidth (a
+  // concurrent run on disjoint SM shares measured slower), so they run one after the other.
+  cudaStream_t sx = side_stream(st, 1);
+  if (!sx) return cuda_fail();
   struct Events {
     cudaEvent_t e[3] = {nullptr, nullptr, nullptr};
     ~Events() {
@@ -219,28 +219,21 @@ int bf_bifrost_layer_decode(const bf_layer* L, const void* x, const void* q, con
         if (x) cudaEventDestroy(x);
     }
   } evs;
-  cudaEvent_t &ev_fork = evs.e[0], &ev_x = evs.e[1], &ev_w = evs.e[2];
-  for (cudaEvent_t* e : {&ev_fork, &ev_x, &ev_w})
+  cudaEvent_t &ev_fork = evs.e[0], &ev_x = evs.e[1], &ev_g = evs.e[2];
+  for (cudaEvent_t* e : {&ev_fork, &ev_x, &ev_g})
     if (cudaEventCreateWithFlags(e, cudaEventDisableTiming) != cudaSuccess) return cuda_fail();
-  if (cudaEventRecord(ev_fork, stream) != cudaSuccess || cudaStreamWaitEvent(sx, ev_fork, 0) != cudaSuccess ||
-      cudaStreamWaitEvent(sw, ev_fork, 0) != cudaSuccess)
+  if (cudaEventRecord(ev_fork, stream) != cudaSuccess || cudaStreamWaitEvent(sx, ev_fork, 0) != cudaSuccess)
     return cuda_fail();
-  // SM shares: the state update moves 2 D^2 fp32 per (sequence, KV head), the window 2 W D bf16
-  const int sms = st.sm_count;
-  int n_state = 0, n_win = sms;
   if (memory) {
-    const double sb = 2.0 * D * D * 4, wb = 2.0 * W * D * 2;
-    n_state = (int)(sms * sb / (sb + wb) + 0.5);
-    n_state = n_state < 1 ? 1 : (n_state > sms - 1 ? sms - 1 : n_state);
-    n_win = sms - n_state;
+    // the token leaving the window (position p - W) is written into memory before the read; gathered on the
+    // side stream, beside the head projections
+    stage_mark(ST_DEC_GATHER, 0, sx);
+    rc = launch_gather_evicted(C->ring_km, static_cast<const __nv_bfloat16*>(C->ring_v), C->ring_g, C->ring_beta,
+                               C->ring_pos, C->ring_pos_bstride, pos, B, G, W, D, k_e, v_e, g_e, b_e, sx);
+    if (rc) return rc;
+    stage_mark(ST_DEC_GATHER, 1, sx);
+    if (cudaEventRecord(ev_g, sx) != cudaSuccess) return cuda_fail();
   }
-  // window split (least priority)
-  stage_mark(ST_DEC_WIN, 0, sw);
-  rc = launch_win_dec_split(a, sw, n_win);
-  if (rc) return rc;
-  stage_mark(ST_DEC_WIN, 1, sw);
-  if (cudaEventRecord(ev_w, sw) != cudaSuccess) return cuda_fail();
-  // gate projections (greatest priority)
   stage_mark(ST_XPROJ, 0, sx);
   rc = launch_x_proj(static_cast<const __nv_bfloat16*>(x), weights_x(L->wbuf, L->H, L->G, L->D), L->ab_b, L->mix_b,
                      L->A_log, L->dt_bias, L->decay_mask, g, beta, mixx, pos, 0, B, 1, L->d, L->G, L->H, L->sinks, xs,
@@ -248,25 +241,27 @@ int bf_bifrost_layer_decode(const bf_layer* L, const void* x, const void* q, con
   if (rc) return rc;
   stage_mark(ST_XPROJ, 1, sx);
   if (cudaEventRecord(ev_x, sx) != cudaSuccess) return cuda_fail();
-  // head projections, then (memory on) the evicted entry and the state update
   stage_mark(ST_HEADPROJ, 0, stream);
   rc = launch_head_proj(static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
                         weights_heads(L->wbuf), qm, nullptr, km, 1, B, L->H, L->G, st.sm_count, st.err, stream);
   if (rc) return rc;
   stage_mark(ST_HEADPROJ, 1, stream);
   if (memory) {
-    // the token leaving the window (position p - W) is written into memory before the read
-    rc = launch_gather_evicted(C->ring_km, static_cast<const __nv_bfloat16*>(C->ring_v), C->ring_g, C->ring_beta,
-                               C->ring_pos, C->ring_pos_bstride, pos, B, G, W, D, k_e, v_e, g_e, b_e, stream);
-    if (rc) return rc;
+    if (cudaStreamWaitEvent(stream, ev_g, 0) != cudaSuccess) return cuda_fail();
     stage_mark(ST_DEC_STATE, 0, stream);
-    rc = launch_gdn_decode(qm, k_e, v_e, 0, g_e, b_e, C->S, C->S, o_mem, B, G, R, D, stream, n_state);
+    rc = launch_gdn_decode(qm, k_e, v_e, 0, g_e, b_e, C->S, C->S, o_mem, B, G, R, D, stream);
     if (rc) return rc;
     stage_mark(ST_DEC_STATE, 1, stream);
   }
-  if (cudaStreamWaitEvent(stream, ev_x, 0) != cudaSuccess || cudaStreamWaitEvent(stream, ev_w, 0) != cudaSuccess)
-    return cuda_fail();
-  return launch_win_dec_combine(a, stream);
+  stage_mark(ST_DEC_WIN, 0, stream);
+  rc = launch_win_dec_split(a, stream, 0);
+  if (rc) return rc;
+  stage_mark(ST_DEC_WIN, 1, stream);
+  if (cudaStreamWaitEvent(stream, ev_x, 0) != cudaSuccess) return cuda_fail();
+  stage_mark(ST_DEC_COMBINE, 0, stream);
+  rc = launch_win_dec_combine(a, stream);
+  stage_mark(ST_DEC_COMBINE, 1, stream);
+  return rc;
 }
 
 }  // extern "C"

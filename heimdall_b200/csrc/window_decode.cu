@@ -486,6 +486,121 @@ __global__ void __launch_bounds__(kWD_Threads) win_dec_combine_kernel(WinDecArgs
   }
 }
 
+// Combine, one CTA per (sequence, KV head) for up to kWD_FastSplits splits: thread = value column, the R query
+// heads in turn.  Every load of the CTA is issued before the arithmetic: the split statistics and partial sums
+// of all R heads, the extra keys' values (shared by the heads of the KV group) and the memory reads; the R x nx
+// extra-key scores are warp dot products spread over the eight warps.  One wave of B*G CTAs instead of
+// B*G*R CTAs of the per-head kernel above.
+constexpr int kWD_FastSplits = 4;
+
+template <int R>
+__global__ void __launch_bounds__(kWD_Threads) win_dec_combine_bg_kernel(WinDecArgs a) {
+  const int bg = blockIdx.x;
+  const int b = bg / a.G, g = bg % a.G;
+  constexpr int D = 256;
+  const int ns = a.nsplit;
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const long long p = a.pos[b];
+  __shared__ float s_ms[R][kWD_FastSplits], s_ls[R][kWD_FastSplits], s_extra[R][kWD_MaxExtra];
+  const int nx = a.ns + (p >= a.S ? 1 : 0);   // extra keys: the sinks and, once past them, the new token
+  const float* part = a.part + (size_t)bg * ns * R * (D + 2);   // [split][head][D + 2]
+  if (t < ns * R) {
+    const int s2 = t / R, h = t % R;
+    s_ms[h][s2] = part[(size_t)(s2 * R + h) * (D + 2) + D];
+    s_ls[h][s2] = part[(size_t)(s2 * R + h) * (D + 2) + D + 1];
+  }
+  const size_t qrow0 = (size_t)b * a.G * R + (size_t)g * R;
+  for (int j = warp; j < R * nx; j += kWD_Threads / 32) {
+    const int h = j / nx, e = j % nx;
+    const __nv_bfloat16* kp = (e < a.ns) ? a.sink_k + (((size_t)b * a.G + g) * a.ns + e) * D
+                                         : a.kr + ((size_t)b * a.G + g) * D;
+    const uint4 qv = __ldg(reinterpret_cast<const uint4*>(a.qr + (qrow0 + h) * D) + lane);
+    const uint4 kv = __ldg(reinterpret_cast<const uint4*>(kp) + lane);
+    const uint32_t q4[4] = {qv.x, qv.y, qv.z, qv.w}, k4[4] = {kv.x, kv.y, kv.z, kv.w};
+    float sdot = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      sdot = fmaf(__uint_as_float(q4[i] << 16), __uint_as_float(k4[i] << 16), sdot);
+      sdot = fmaf(__uint_as_float(q4[i] & 0xffff0000u), __uint_as_float(k4[i] & 0xffff0000u), sdot);
+    }
+    sdot = warp_sum(sdot) * rsqrtf((float)D);
+    if (lane == 0) s_extra[h][e] = sdot;
+  }
+  float pv[R][kWD_FastSplits], ev[kWD_MaxExtra], om[R], mx[R];
+#pragma unroll
+  for (int h = 0; h < R; ++h)
+#pragma unroll
+    for (int s2 = 0; s2 < kWD_FastSplits; ++s2) pv[h][s2] = s2 < ns ? part[(size_t)(s2 * R + h) * (D + 2) + t] : 0.f;
+#pragma unroll
+  for (int e = 0; e < kWD_MaxExtra; ++e) {
+    ev[e] = 0.f;
+    if (e < nx) {
+      const __nv_bfloat16* vp = (e < a.ns) ? a.sink_v + (((size_t)b * a.G + g) * a.ns + e) * D
+                                           : a.v + ((size_t)b * a.G + g) * D;
+      ev[e] = __bfloat162float(vp[t]);
+    }
+  }
+  const bool gate_on = a.o_mem && p >= a.W;
+#pragma unroll
+  for (int h = 0; h < R; ++h) {
+    om[h] = gate_on ? a.o_mem[(qrow0 + h) * D + t] : 0.f;
+    mx[h] = gate_on ? a.mixx[qrow0 + h] : 0.f;
+  }
+  __syncthreads();
+  const float lnW = logf((float)a.W);
+#pragma unroll
+  for (int h = 0; h < R; ++h) {
+    float m = -INFINITY;
+#pragma unroll
+    for (int s2 = 0; s2 < kWD_FastSplits; ++s2)
+      if (s2 < ns) m = fmaxf(m, s_ms[h][s2]);
+#pragma unroll
+    for (int e = 0; e < kWD_MaxExtra; ++e)
+      if (e < nx) m = fmaxf(m, s_extra[h][e]);
+    float l = 0.f, acc = 0.f;
+#pragma unroll
+    for (int s2 = 0; s2 < kWD_FastSplits; ++s2) {
+      if (s2 < ns && s_ms[h][s2] != -INFINITY) {
+        const float f = __expf(s_ms[h][s2] - m);
+        l = fmaf(s_ls[h][s2], f, l);
+        acc = fmaf(pv[h][s2], f, acc);
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < kWD_MaxExtra; ++e) {
+      if (e < nx) {
+        const float f = __expf(s_extra[h][e] - m);
+        l += f;
+        acc = fmaf(f, ev[e], acc);
+      }
+    }
+    const float lse = m + logf(l);
+    const float ow = acc / l;
+    float res = ow;
+    const int hh = g * R + h;
+    if (gate_on) {
+      const float z = mx[h] + a.mix_lse[hh] * (lse - lnW);
+      const float gam = 1.f / (1.f + __expf(-z));
+      res = ow + gam * (a.mem_scale[hh] * om[h] - ow);
+    }
+    a.o[(qrow0 + h) * D + t] = res;
+    if (t == 0 && a.lse_out) a.lse_out[qrow0 + h] = lse;
+  }
+  // ring write of the new token
+  if (a.ring_km) {
+    const int slot = (int)(p % a.W);
+    const size_t kv = (((size_t)b * a.G + g) * a.W + slot) * D;
+    a.ring_k_w[kv + t] = a.kr[((size_t)b * a.G + g) * D + t];
+    a.ring_v_w[kv + t] = a.v[((size_t)b * a.G + g) * D + t];
+    a.ring_km[(((size_t)b * a.W + slot) * a.G + g) * D + t] = a.km[((size_t)b * a.G + g) * D + t];
+    if (t == 0) {
+      a.ring_g[((size_t)b * a.W + slot) * a.G + g] = a.g_new[(size_t)b * a.G + g];
+      a.ring_beta[((size_t)b * a.W + slot) * a.G + g] = a.beta_new[(size_t)b * a.G + g];
+      if (g == 0) a.ring_pos_w[(size_t)b * a.ring_pos_bstride + slot] = p;
+    }
+  }
+}
+
 // gather the evicted ring entry (position p - W) for the state update; invalid entries become no-ops
 __global__ void decode_gather_evicted_kernel(const float* __restrict__ ring_km, const __nv_bfloat16* __restrict__ ring_v,
                                              const float* __restrict__ ring_g, const float* __restrict__ ring_beta,
@@ -562,7 +677,21 @@ int launch_win_dec_split(WinDecArgs a, cudaStream_t stream, int max_ctas) {
 int launch_win_dec_combine(WinDecArgs a, cudaStream_t stream) {
   int rc = win_dec_check(a);
   if (rc) return rc;
-  win_dec_combine_kernel<<<dim3(a.B * a.G, a.R), kWD_Threads, 0, stream>>>(a);
+  if (a.nsplit <= kWD_FastSplits) {
+    const dim3 grid(a.B * a.G);
+    switch (a.R) {
+      case 1: win_dec_combine_bg_kernel<1><<<grid, kWD_Threads, 0, stream>>>(a); break;
+      case 2: win_dec_combine_bg_kernel<2><<<grid, kWD_Threads, 0, stream>>>(a); break;
+      case 3: win_dec_combine_bg_kernel<3><<<grid, kWD_Threads, 0, stream>>>(a); break;
+      case 4: win_dec_combine_bg_kernel<4><<<grid, kWD_Threads, 0, stream>>>(a); break;
+      case 5: win_dec_combine_bg_kernel<5><<<grid, kWD_Threads, 0, stream>>>(a); break;
+      case 6: win_dec_combine_bg_kernel<6><<<grid, kWD_Threads, 0, stream>>>(a); break;
+      case 7: win_dec_combine_bg_kernel<7><<<grid, kWD_Threads, 0, stream>>>(a); break;
+      default: win_dec_combine_bg_kernel<8><<<grid, kWD_Threads, 0, stream>>>(a); break;
+    }
+  } else {
+    win_dec_combine_kernel<<<dim3(a.B * a.G, a.R), kWD_Threads, 0, stream>>>(a);
+  }
   return launch_status();
 }
 

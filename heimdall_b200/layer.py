@@ -133,8 +133,9 @@ class BifrostLayer:
             return self._decode(x, q, k, v, qr, kr, int(start), cache, memory)
         return self._prefill(x, q, k, v, qr, kr, int(start), cache, memory)
 
-    def _prefill_setup(self, x, q, k, v, qr, kr, start, cache, memory):
-        """Operands of one layer prefill: bf16 inputs, sinks, the cache in device layout, output, workspace."""
+    def _prefill_setup(self, x, q, k, v, qr, kr, start, cache, memory, out=None):
+        """Operands of one layer prefill: bf16 inputs, sinks, the cache in device layout, output, workspace.
+        ``out`` (optional): a contiguous fp32 [B,t,H,D] tensor the layer writes its output into."""
         B, t = x.shape[:2]
         H, G, D, W, S = self.H, self.G, self.D, self.window, self.sinks
         dev = x.device
@@ -176,7 +177,12 @@ class BifrostLayer:
             Sst = cache["S"] if use_mem else _dummy_state(dev)
             rc = BfRingCache(ptr(cache["ring_k"]), ptr(cache["ring_v"]), ptr(cache["ring_km"]), ptr(cache["ring_g"]),
                              ptr(cache["ring_beta"]), ptr(cache["ring_pos"]), 0, 0, 0, 0, ptr(Sst))
-        o = torch.empty(B, t, H, D, device=dev, dtype=torch.float32)
+        if out is not None:
+            if tuple(out.shape) != (B, t, H, D) or out.dtype != torch.float32 or not out.is_contiguous():
+                raise ValueError("out must be a contiguous fp32 tensor [B, t, H, D]")
+            o = out
+        else:
+            o = torch.empty(B, t, H, D, device=dev, dtype=torch.float32)
         ring_case = cache is not None and start > 0
         nws = _lib.size("bf_layer_prefill_workspace", B, t, H, G, D, W, 1 if ring_case else 0)
         ws = torch.empty(nws, dtype=torch.uint8, device=dev)
@@ -187,8 +193,8 @@ class BifrostLayer:
         if c["cache"] is not None:
             c["cache"]["sink_k"], c["cache"]["sink_v"] = c["sk"], c["sv"]
 
-    def _prefill(self, x, q, k, v, qr, kr, start, cache, memory, lse_out=None):
-        c = self._prefill_setup(x, q, k, v, qr, kr, start, cache, memory)
+    def _prefill(self, x, q, k, v, qr, kr, start, cache, memory, lse_out=None, out=None):
+        c = self._prefill_setup(x, q, k, v, qr, kr, start, cache, memory, out)
         xb, qb, kb, vb, qrb, krb = c["args"]
         _lib.call("bf_bifrost_layer_prefill", ctypes_ref(self._struct), ptr(xb), ptr(qb), ptr(kb), ptr(vb), ptr(qrb),
                   ptr(krb), start, c["B"], c["t"], 0 if c["rc"] is None else ctypes_ref(c["rc"]), ptr(c["sk"]),
@@ -196,6 +202,53 @@ class BifrostLayer:
                   stream_handle())
         self._finish_cache(c)
         return c["o"]
+
+    def student_varlen(self, x, q, k, v, qr, kr, cu_seqlens, memory: bool = True, caches=None, streams: int = 4):
+        """The layer core over packed variable-length sequences: the T tokens of x [1,T,d],
+        q [1,T,H,D], k/v [1,T,G,D], qr [1,H,T,D], kr [1,G,T,D] are n sequences, sequence i being tokens
+        cu_seqlens[i] .. cu_seqlens[i+1] - 1.  Each sequence is its own prefill from an empty cache: its own
+        positions from 0, sinks, window and ring, and a memory state that starts at zero (the reference runs
+        ``_student`` once per sequence for this, heimdall/hibrit.py:363-424; it has no packed form).  Returns o
+        [1,T,H,D] fp32.  ``caches`` (optional list of n dicts) receives each sequence's cache, ready for decode.
+
+        ``cu_seqlens`` is read on the host (a list or tensor of n+1 cumulative lengths; a device tensor costs one
+        copy to the host).  The per-sequence fused prefills are issued on ``streams`` rotating streams: each one
+        forks its window and memory chain onto the device's two side streams, so one sequence's window runs
+        while the previous sequence's memory reads finish, and the outputs are written straight into the
+        packed result."""
+        check_cuda(x, q, k, v, qr, kr)
+        cu = [int(c) for c in (cu_seqlens.tolist() if isinstance(cu_seqlens, torch.Tensor) else cu_seqlens)]
+        if x.shape[0] != 1 or len(cu) < 2 or cu[0] != 0 or cu[-1] != x.shape[1] or \
+                any(b < a for a, b in zip(cu, cu[1:])):
+            raise ValueError("cu_seqlens must be non-decreasing from 0 to T (with batch size 1)")
+        if caches is not None and len(caches) != len(cu) - 1:
+            raise ValueError("caches needs one dict per sequence")
+        dev = x.device
+        T = x.shape[1]
+        out = torch.empty(1, T, self.H, self.D, device=dev, dtype=torch.float32)
+        cur = torch.cuda.current_stream(dev)
+        pool = _varlen_streams(dev, max(1, int(streams)))
+        for s_ in pool:
+            s_.wait_stream(cur)
+        for i, (a, b) in enumerate(zip(cu, cu[1:])):
+            if b == a:
+                if caches is not None:
+                    caches[i].clear()
+                continue
+            s_ = pool[i % len(pool)]
+            with torch.cuda.stream(s_):
+                args = (x[:, a:b], q[:, a:b], k[:, a:b], v[:, a:b], qr[:, :, a:b].contiguous(),
+                        kr[:, :, a:b].contiguous())
+                cache = caches[i] if caches is not None else None
+                if cache is not None:
+                    cache.clear()
+                self._prefill(*args, 0, cache, memory, out=out[:, a:b])
+        for s_ in pool:
+            cur.wait_stream(s_)
+        out.record_stream(cur)
+        for s_ in pool:
+            out.record_stream(s_)
+        return out
 
     def prefill_sp_begin(self, x, q, k, v, qr, kr, start: int, cache: dict):
         """First phase of a sequence-parallel layer prefill of this rank's tokens (``heimdall_b200.sp``):
@@ -421,6 +474,17 @@ def _chunk_plan(T: int, chunk: int) -> list:
     """Chunk lengths for the host-buffer prefill: equal chunks, the last one ragged (a ramp of smaller chunks
     at both ends measured slower on B200: the per-chunk fixed costs outweigh the shorter fill and drain)."""
     return [min(chunk, T - t0) for t0 in range(0, T, chunk)]
+
+
+_VARLEN_STREAMS = {}
+
+
+def _varlen_streams(dev, n: int):
+    """n caller streams per device for the packed-sequence prefill (kept for the process)."""
+    key = (str(dev), n)
+    if key not in _VARLEN_STREAMS:
+        _VARLEN_STREAMS[key] = tuple(torch.cuda.Stream(dev) for _ in range(n))
+    return _VARLEN_STREAMS[key]
 
 
 def _host_streams(dev):

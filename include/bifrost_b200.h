@@ -71,7 +71,8 @@ int bf_selftest_wait_timeout(unsigned int limit_us, bf_stream_t stream);
 /* Per-stage timing: `events` holds 2*n_stages cudaEvent_t handles (begin/end per stage); each
  * layer entry point records them on its stream around its stages (0 x-projection, 1 head
  * projection, 2-4 delta-rule phases P1/P2/P3, 5 window key/value prep, 6 window attention,
- * 7 cache write, 8 decode state update, 9 decode window).  n_stages = 0 turns this off.
+ * 7 cache write, 8 decode state update, 9 decode window split, 10 decode evicted-entry gather, 11 decode
+ * combine; at most 12).  n_stages = 0 turns this off.
  * Process-wide; not for concurrent use from several threads.  No counterpart in the reference
  * (its only timing is wall-clock logging, heimdall/motor.py:292-297). */
 int bf_stage_events(void* const* events, int n_stages);
