@@ -797,20 +797,25 @@ def run_headline(L, dev, ctx, args):
         step()
     torch.cuda.synchronize()
     barrier(ctx)
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     with ClockSampler(ctx["local"]) as clk:
         torch.cuda.synchronize()
-        a.record()
-        for _ in range(args.steps):
+        h0 = time.perf_counter()
+        evs[0].record()
+        for i in range(args.steps):
             step()
-        b.record()
+            evs[i + 1].record()
+        h1 = time.perf_counter()
         torch.cuda.synchronize()
     clocks = clk.summary()
-    t = torch.tensor([a.elapsed_time(b) / args.steps], device=dev)
+    per = [evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
+    t = torch.tensor([evs[0].elapsed_time(evs[-1]) / args.steps], device=dev)
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     del ins
-    return float(t.item()), clocks
+    diag = {"step_ms_min": min(per), "step_ms_median": statistics.median(per), "step_ms_max": max(per),
+            "host_enqueue_ms_per_step": (h1 - h0) * 1e3 / args.steps}
+    return float(t.item()), clocks, diag
 
 
 def run_e2e(L, dev, ctx, steps):
@@ -862,7 +867,7 @@ def run_ours(args, ctx):
     world, rank = ctx["world"], ctx["rank"]
     L = make_layer(dev)
     pk, pk_kind = peaks()
-    ms_step, clocks = run_headline(L, dev, ctx, args)
+    ms_step, clocks, diag = run_headline(L, dev, ctx, args)
     value = HEADLINE_T / (ms_step / 1e3)
     c1 = None if args.no_config1 else run_config1(L, dev, ctx, args, pk, pk_kind)
     e2e = None if args.no_e2e else run_e2e(L, dev, ctx, min(args.steps, 10))
@@ -881,7 +886,7 @@ def run_ours(args, ctx):
     out = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded; config-1/3 shapes and distributions)",
-           "config": arm_config(world), "clocks": clocks,
+           "config": arm_config(world), "clocks": clocks, "step_diag_rank0": diag,
            "layer_roofline": {"flops_per_step": total_f, "achieved_tflops": ach, "peak": peak, "peak_kind": peak_kind,
                               "frac": ach / peak / world, "frac_vs_burst": ach / pk["bf16_tflops"] / world,
                               "frac_vs_sustained": ach / pk["bf16_tflops_sustained"] / world,

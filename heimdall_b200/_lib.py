@@ -38,6 +38,7 @@ SIGNATURES = {
     "bf_window_attn_fwd": [_P, _P, _P, _L, _L, _L, _P, _P, _I, _L, _L, _L, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P,
                            _Z, _P],
     "bf_layer_prefill_workspace": [_I, _I, _I, _I, _I, _I, _I],
+    "bf_layer_prefill_sp_workspace": [_I, _I, _I, _I, _I, _I, _I],
     "bf_bifrost_layer_prefill": [_P, _P, _P, _P, _P, _P, _P, _L, _I, _I, _P, _P, _P, _I, _I, _P, _P, _P, _Z, _P],
     "bf_gdn_segment_workspace": [_I, _I, _I, _I],
     "bf_gdn_segment_transform": [_P, _I, _P, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _Z, _P],
@@ -47,6 +48,7 @@ SIGNATURES = {
 }
 _RESTYPE = {"bf_strerror": ctypes.c_char_p, "bf_last_cuda_error": ctypes.c_char_p, "bf_layer_weights_bytes": _Z, "bf_layer_decode_workspace": _Z,
             "bf_gdn_chunk_workspace": _Z, "bf_window_workspace": _Z, "bf_layer_prefill_workspace": _Z,
+            "bf_layer_prefill_sp_workspace": _Z,
             "bf_gdn_segment_workspace": _Z}
 
 _lock = threading.Lock()

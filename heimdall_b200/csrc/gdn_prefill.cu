@@ -528,7 +528,9 @@ __global__ void __launch_bounds__(kP2_Threads, 1)
   // column blocks beyond the state's (transform mode only) run the map path: start at the identity, no inputs
   const bool mpath = blockIdx.x >= kGD / kP2_NB;
   const int col0 = (mpath ? blockIdx.x - kGD / kP2_NB : blockIdx.x) * kP2_NB;
-  const bool keep = s.m_out == nullptr;   // chunk-start states and v' are kept for P3
+  // chunk-start states and v' are kept for P3 (also by the map pass of a fix-up run, on the path from zero)
+  const bool keep = (s.m_out == nullptr || s.MC != nullptr) && !mpath;
+  const bool keep_map = mpath && s.MC != nullptr;   // the transition path keeps its chunk-start maps
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int nch = s.n_chunks;
   if (t == 0) {
@@ -643,6 +645,19 @@ __global__ void __launch_bounds__(kP2_Threads, 1)
           stg[(size_t)e * kGD + r + 128] = __float2half_rn(S1[e]);
         }
       }
+      if (keep_map) {   // M_c, row-major fp16 at its true scale (the path keeps it divided by the decay so far)
+        const float f = __expf(lsum);
+        __half* mc = s.MC + (((size_t)bg * nch + c) * kGD + r) * kGD + col0;
+#pragma unroll
+        for (int e = 0; e < kP2_NB; e += 8) {
+          *reinterpret_cast<uint4*>(mc + e) =
+              make_uint4(pack_half2(S0[e] * f, S0[e + 1] * f), pack_half2(S0[e + 2] * f, S0[e + 3] * f),
+                         pack_half2(S0[e + 4] * f, S0[e + 5] * f), pack_half2(S0[e + 6] * f, S0[e + 7] * f));
+          *reinterpret_cast<uint4*>(mc + (size_t)128 * kGD + e) =
+              make_uint4(pack_half2(S1[e] * f, S1[e + 1] * f), pack_half2(S1[e + 2] * f, S1[e + 3] * f),
+                         pack_half2(S1[e + 4] * f, S1[e + 5] * f), pack_half2(S1[e + 6] * f, S1[e + 7] * f));
+        }
+      }
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(bar_st);
@@ -733,6 +748,179 @@ __global__ void __launch_bounds__(kP2_Threads, 1)
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, kP2_Tmem);
+  }
+}
+
+// ============================================================================================ SP fix-up
+// Sequence parallelism, second phase.  The map pass kept, per chunk c of this segment, the chunk-start state from a
+// zero incoming state (N_c^T in ST) with its corrected values (v'^N_c^T in VT), and the chunk-start transition
+// M_c (MC, fp16 row-major [k][j]).  From an incoming state S_in the chunk starts at S_c = M_c S_in + N_c, and its
+// corrected values are v'_c = u_c - w_c S_c = v'^N_c - w_c (M_c S_in).  With Z = M_c S_in on the tensor core,
+// one CTA per (batch x KV head, chunk, value half) rewrites in place
+//   ST <- N_c^T + Z^T              (128 value rows x 256 key columns, fp16)
+//   VT <- v'^N_c^T - Z^T w_c^T      (128 value rows x 128 tokens, fp16)
+// so the memory reads (P3) run unchanged.  All chunks at once: this replaces a second sequential scan.
+constexpr int kFX_Threads = 192;            // warps 0-3 epilogue (thread = value row), warp 4 TMA, warp 5 MMA
+constexpr int kFX_SmemA = 128 * kGD * 2;    // 64 KB: S_in^T half (A of Z^T), then Z^T (A of the value product)
+constexpr int kFX_SmemB = kGD * kGD * 2;    // 128 KB: M_c [k][j] (B of Z^T), then w_c [t][k] in its first half
+constexpr int kFX_Smem = kFX_SmemA + kFX_SmemB + 1024 + 256;
+
+// SinT[bg][v][j] = fp16(S[bg][j][v]) for the fix-up's A operand (32 x 32 tiles through shared memory)
+__global__ void sp_sin_transpose_kernel(const float* __restrict__ S, __half* __restrict__ SinT) {
+  __shared__ float tile[32][33];
+  const size_t off = (size_t)blockIdx.z * kGD * kGD;
+  const int j0 = blockIdx.y * 32, v0 = blockIdx.x * 32;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) tile[i][threadIdx.x] = S[off + (size_t)(j0 + i) * kGD + v0 + threadIdx.x];
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y)
+    SinT[off + (size_t)(v0 + i) * kGD + j0 + threadIdx.x] = __float2half_rn(tile[threadIdx.x][i]);
+}
+
+__global__ void __launch_bounds__(kFX_Threads, 1)
+    gdn_sp_fixup_kernel(const __grid_constant__ CUtensorMap sinmap, const __grid_constant__ CUtensorMap mcmap,
+                        const __grid_constant__ CUtensorMap wmap, GdnStreams s) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + kFX_SmemA;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + kFX_SmemB);
+  uint64_t* bar_a = bars + 0;    // S_in^T half landed
+  uint64_t* bar_b = bars + 1;    // M_c landed
+  uint64_t* bar_m1 = bars + 2;   // Z^T product done (A and B free)
+  uint64_t* bar_z = bars + 3;    // Z^T staged in fp16 (128 arrivals)
+  uint64_t* bar_w = bars + 4;    // w_c landed
+  uint64_t* bar_m2 = bars + 5;   // value product done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 6);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 7);
+  const int c = blockIdx.x, bg = blockIdx.y, vh = blockIdx.z;
+  const int nch = s.n_chunks;
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  if (t == 0) {
+    mbar_init(bar_a, 1);
+    mbar_init(bar_b, 1);
+    mbar_init(bar_m1, 1);
+    mbar_init(bar_z, 128);
+    mbar_init(bar_w, 1);
+    mbar_init(bar_m2, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 512);   // Z^T at columns 0..255, the value product at 256..383
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      tma_prefetch(&sinmap);
+      tma_prefetch(&mcmap);
+      tma_prefetch(&wmap);
+      mbar_expect_tx(bar_a, kFX_SmemA);
+      tma_load_3d(sA, &sinmap, bar_a, 0, bg * kGD + vh * 128, 0);
+      mbar_expect_tx(bar_b, kFX_SmemB);
+      tma_load_3d(sB, &mcmap, bar_b, 0, (bg * nch + c) * kGD, 0);
+      bool got_w = false;
+      if (mbar_wait(bar_m1, 0, abort_flag, s.err, 0xB1)) {   // M_c consumed: w_c goes over it
+        mbar_expect_tx(bar_w, kGC * kGD * 2);
+        tma_load_3d(sB, &wmap, bar_w, 0, bg * s.n_pad + c * kGC, 0);
+        got_w = true;
+      }
+      // the CTA ends only after its loads landed
+      mbar_wait(bar_a, 0, nullptr, s.err, 0xB2);
+      mbar_wait(bar_b, 0, nullptr, s.err, 0xB2);
+      if (got_w) mbar_wait(bar_w, 0, nullptr, s.err, 0xB2);
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      const uint32_t aA = smem_u32(sA), aB = smem_u32(sB);
+      if (mbar_wait(bar_a, 0, abort_flag, s.err, 0xB3) && mbar_wait(bar_b, 0, abort_flag, s.err, 0xB4)) {
+        tc_fence_after();
+        constexpr uint32_t id1 = idesc_f16(128, 256, 0);
+#pragma unroll
+        for (int ks = 0; ks < kGD / 16; ++ks)
+          umma_f16_ss(tmem, sdesc_kstep(aA, 128, ks), sdesc_kstep(aB, kGD, ks), id1, ks > 0);
+        umma_commit(bar_m1);
+        if (mbar_wait(bar_z, 0, abort_flag, s.err, 0xB5) && mbar_wait(bar_w, 0, abort_flag, s.err, 0xB6)) {
+          tc_fence_after();
+          constexpr uint32_t id2 = idesc_f16(128, kGC, 0);
+#pragma unroll
+          for (int ks = 0; ks < kGD / 16; ++ks)
+            umma_f16_ss(tmem + 256, sdesc_kstep(aA, 128, ks), sdesc_kstep(aB, kGC, ks), id2, ks > 0);
+          umma_commit(bar_m2);
+        }
+      }
+    }
+  } else {
+    // warps 0-3: thread r = value row vh * 128 + r
+    const int r = t;
+    const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+    const size_t vrow = ((size_t)bg * nch + c) * kGD + (size_t)vh * 128 + r;
+    __half* st = s.ST + vrow * kGD;     // [k] of this value row
+    __half* vt = s.VT + vrow * kGC;     // [t] of this value row
+    bool ok = mbar_wait_warp(bar_m1, 0, abort_flag, s.err, 0xB7);
+    if (ok) {
+      tc_fence_after();
+#pragma unroll 1
+      for (int c1 = 0; c1 < kGD; c1 += 32) {
+        uint32_t z[32];
+        tmem_ld32(trow + c1, z);
+        tmem_wait_ld();
+        // S_c^T row = N_c^T row + Z^T row (in place), and Z^T (fp16) staged as the next product's A operand
+        uint4* sp4 = reinterpret_cast<uint4*>(st + c1);
+        uint8_t* atom = sA + (c1 >> 6) * (128 * 128);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 nv = sp4[q];
+          const uint32_t nw[4] = {nv.x, nv.y, nv.z, nv.w};
+          uint32_t ow[4], zw[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float z0 = __uint_as_float(z[8 * q + 2 * e]), z1 = __uint_as_float(z[8 * q + 2 * e + 1]);
+            const float2 n2 = __half22float2(*reinterpret_cast<const __half2*>(&nw[e]));
+            ow[e] = pack_half2(n2.x + z0, n2.y + z1);
+            zw[e] = pack_half2(z0, z1);
+          }
+          sp4[q] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+          *reinterpret_cast<uint4*>(atom + sw128_offset(r, (c1 & 63) + 8 * q)) = make_uint4(zw[0], zw[1], zw[2], zw[3]);
+        }
+      }
+    }
+    fence_async_smem();
+    tc_fence_before();
+    mbar_arrive(bar_z);
+    ok = ok && mbar_wait_warp(bar_m2, 0, abort_flag, s.err, 0xB8);
+    if (ok) {
+      tc_fence_after();
+#pragma unroll 1
+      for (int c1 = 0; c1 < kGC; c1 += 32) {
+        uint32_t y[32];
+        tmem_ld32(trow + 256 + c1, y);
+        tmem_wait_ld();
+        uint4* vp4 = reinterpret_cast<uint4*>(vt + c1);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 vv = vp4[q];
+          const uint32_t vw[4] = {vv.x, vv.y, vv.z, vv.w};
+          uint32_t ow[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 v2 = __half22float2(*reinterpret_cast<const __half2*>(&vw[e]));
+            ow[e] = pack_half2(v2.x - __uint_as_float(y[8 * q + 2 * e]), v2.y - __uint_as_float(y[8 * q + 2 * e + 1]));
+          }
+          vp4[q] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -1205,6 +1393,20 @@ size_t gdn_prefill_workspace(int B, int G, int T_steps, bool transform) {
   return n;
 }
 
+// the fix-up phase's extra buffers: per-chunk transitions MC, the incoming state transposed (SinT)
+size_t gdn_prefill_fix_workspace(int B, int G, int T_steps) {
+  const size_t nch = (size_t)((T_steps + kGC - 1) / kGC);
+  auto al = [](size_t x) { return (x + 1023) & ~size_t(1023); };
+  return al((size_t)B * G * nch * kGD * kGD * 2) + al((size_t)B * G * kGD * kGD * 2);
+}
+
+void gdn_prefill_carve_fix(GdnStreams& s, void* ws) {
+  auto al = [](size_t x) { return (x + 1023) & ~size_t(1023); };
+  uint8_t* p = static_cast<uint8_t*>(ws);
+  s.MC = reinterpret_cast<__half*>(p); p += al((size_t)s.B * s.G * s.n_chunks * kGD * kGD * 2);
+  s.SinT = reinterpret_cast<__half*>(p);
+}
+
 int gdn_prefill_carve(GdnStreams& s, void* ws) {
   auto al = [](size_t x) { return (x + 1023) & ~size_t(1023); };
   uint8_t* p = static_cast<uint8_t*>(ws);
@@ -1213,7 +1415,7 @@ int gdn_prefill_carve(GdnStreams& s, void* ws) {
   s.w = reinterpret_cast<__half*>(p); p += al((size_t)s.B * s.G * n_pad * kGD * 2);
   s.u = reinterpret_cast<__half*>(p); p += al((size_t)s.B * s.G * n_pad * kGD * 2);
   s.gc = reinterpret_cast<float*>(p); p += al((size_t)s.B * s.G * n_pad * 4);
-  if (s.m_out) {
+  if (s.m_out && !s.MC) {
     s.ST = s.VT = nullptr;
     return BF_OK;
   }
@@ -1242,6 +1444,22 @@ int launch_gdn_prefill(GdnStreams s, cudaStream_t stream, int parts) {
     gdn_p1_kernel<<<dim3(s.n_chunks, s.B * s.G), kP1_Threads, kP1_Smem, stream>>>(kwmap, umap, wmap1, s);
     if (int e_ = launch_status()) return e_;
     stage_mark(ST_GDN_P1, 1, stream);
+  }
+  if (parts & kGdnFix) {
+    if (!s.MC || !s.SinT || !s.s0 || !s.ST || !s.VT) return BF_ERR_INVALID_ARGUMENT;
+    int rcf = ensure_smem_attr((const void*)gdn_sp_fixup_kernel, kFX_Smem);
+    if (rcf) return rcf;
+    sp_sin_transpose_kernel<<<dim3(kGD / 32, kGD / 32, s.B * s.G), dim3(32, 8), 0, stream>>>(s.s0, s.SinT);
+    if (int e_ = launch_status()) return e_;
+    CUtensorMap sinmap, mcmap, wmapf;
+    rcf = make_tmap_kmajor(&sinmap, s.SinT, BF_F16, (uint64_t)s.B * s.G * kGD, kGD, kGD, 128, 4);
+    if (!rcf) rcf = make_tmap_kmajor(&mcmap, s.MC, BF_F16, (uint64_t)s.B * s.G * s.n_chunks * kGD, kGD, kGD, kGD, 4);
+    if (!rcf) rcf = make_tmap_kmajor(&wmapf, s.w, BF_F16, (uint64_t)s.B * s.G * s.n_pad, kGD, kGD, kGC, 4);
+    if (rcf) return rcf;
+    stage_mark(ST_GDN_P2, 0, stream);
+    gdn_sp_fixup_kernel<<<dim3(s.n_chunks, s.B * s.G, 2), kFX_Threads, kFX_Smem, stream>>>(sinmap, mcmap, wmapf, s);
+    if (int e_ = launch_status()) return e_;
+    stage_mark(ST_GDN_P2, 1, stream);
   }
   if (!(parts & (kGdnP2 | kGdnP3))) return BF_OK;
   CUtensorMap wmap, kmap;

@@ -7,8 +7,10 @@
 namespace bfb {
 
 constexpr int kGC = 128;   // chunk length of the GPU scan (tokens)
-// parts of launch_gdn_prefill: P1 (per-chunk products), P2 (the recurrence), P3 (the reads; not in transform mode)
-constexpr int kGdnP1 = 1, kGdnP2 = 2, kGdnP3 = 4, kGdnAll = 7;
+// parts of launch_gdn_prefill: P1 (per-chunk products), P2 (the recurrence), P3 (the reads; not in transform mode),
+// FIX (sequence parallelism, second phase: the chunk-start states and corrected values from the incoming state,
+// all chunks at once, from what the map pass stored)
+constexpr int kGdnP1 = 1, kGdnP2 = 2, kGdnP3 = 4, kGdnAll = 7, kGdnFix = 8;
 constexpr int kGD = 256;   // head dim (Dk == Dv)
 
 // The write stream (step u writes one key/value into memory) and the read stream (step u reads with
@@ -44,6 +46,12 @@ struct GdnStreams {
   // segment-transform mode (m_out != null): no reads; P2 also runs the recurrence from the identity with
   // zero inputs, whose final value is the segment's state map M (S_out = M S_in + N), and writes it here
   float* m_out;                // [B,G,D,D]
+  // sequence parallelism with a fix-up phase (MC != null, with m_out in the map pass): the map pass also keeps,
+  // per chunk, the chunk-start state from a zero incoming state (ST) with its corrected values (VT), and the
+  // chunk-start transition M_c (state at chunk c = M_c S_in + N_c), fp16 row-major [k][j]; the fix-up (kGdnFix)
+  // reads them with the incoming state s0, transposed to fp16 in SinT, and rewrites ST and VT in place
+  __half* MC;                  // [B,G,n_chunks,D,D]
+  __half* SinT;                // [B,G,D(dv),D(dk)]
   // packed variable-length sequences (chunk_tok0 != null; B = 1, no ring, qoff = 0): global chunk c holds
   // packed tokens chunk_tok0[c] .. + chunk_len[c] - 1 of one sequence; sequence i owns chunks
   // seq_chunk0[i] .. seq_chunk0[i+1] - 1 (seq_chunk0[n_seq] = number of chunks); states are per sequence

@@ -6,6 +6,9 @@
 #include "window_prefill.h"
 
 namespace bfb {
+size_t gdn_prefill_fix_workspace(int B, int G, int T_steps);
+void gdn_prefill_carve_fix(GdnStreams& s, void* ws);
+int launch_state_map(const float* A, const float* S, const float* N, float* out, int BG, int D, cudaStream_t stream);
 
 int launch_head_proj(const __nv_bfloat16* q, const __nv_bfloat16* k, const __half* w_heads, float* qm, __half* qm16,
                      float* km, int B, int T, int H, int G, int sm_count, unsigned int* err, cudaStream_t stream);
@@ -227,6 +230,13 @@ size_t bf_layer_prefill_workspace(int B, int T, int H, int G, int D, int window,
   return n;
 }
 
+// the two-phase (sequence-parallel) prefill's extra workspace: the fix-up buffers and a state for the final
+// state M S_in + N
+static size_t sp_extra_bytes(int B, int T, int G, int D, int window, int with_ring) {
+  const int steps = with_ring ? T : (T > window ? T - window : 1);
+  return gdn_prefill_fix_workspace(B, G, steps) + al1k((size_t)B * G * D * D * 4);
+}
+
 // phase: kPhaseAll (the whole layer), kPhaseBegin (memory inputs, P1 and the segment state map -> m_out, n_out),
 // kPhaseFinish (the rest, from C->S, reusing the workspace of the begin phase)
 constexpr int kPhaseAll = 0, kPhaseBegin = 1, kPhaseFinish = 2;
@@ -254,7 +264,10 @@ static int layer_prefill_impl(const bf_layer* L, const void* x, const void* q, c
   if (C && (!C->ring_k || !C->ring_v || !C->ring_km || !C->ring_g || !C->ring_beta || !C->ring_pos || !C->S))
     return BF_ERR_INVALID_ARGUMENT;
   if (C && C->ring_pos_bstride != 0) return BF_ERR_UNSUPPORTED;
-  if (ws_bytes < bf_layer_prefill_workspace(B, T, H, G, D, W, ring_case ? 1 : 0)) return BF_ERR_WORKSPACE;
+  const size_t ws_base = bf_layer_prefill_workspace(B, T, H, G, D, W, ring_case ? 1 : 0);
+  const bool two_phase = phase != kPhaseAll;
+  if (ws_bytes < ws_base + (two_phase ? sp_extra_bytes(B, T, G, D, W, ring_case ? 1 : 0) : 0)) return BF_ERR_WORKSPACE;
+  if (phase == kPhaseFinish && (!m_out || !n_out)) return BF_ERR_INVALID_ARGUMENT;
   for (const void* pp : {x, q, k, v, qr, kr, (const void*)o, (const void*)ws})
     if (!aligned16(pp)) return BF_ERR_ALIGNMENT;
   if (ns && (!aligned16(sink_k) || !aligned16(sink_v))) return BF_ERR_ALIGNMENT;
@@ -365,15 +378,30 @@ static int layer_prefill_impl(const bf_layer* L, const void* x, const void* q, c
       s.m_out = m_out;
     }
     if (s.n_steps > 0) {
+      uint8_t* extra = static_cast<uint8_t*>(ws) + ws_base;   // the two-phase buffers follow the layer's workspace
+      if (two_phase) gdn_prefill_carve_fix(s, extra);
       gdn_prefill_carve(s, gws);
       // the window writes the rows the reads cover in tile order when its query tiles line up with the chunks
       if (s.qoff % kGC == 0 && reads_later) {
         s.owin = reinterpret_cast<__half*>(static_cast<uint8_t*>(gws) + al1k(gdn_prefill_workspace(B, G, s.n_steps, false)));
       }
       reads = phase != kPhaseBegin;
-      const int parts = phase == kPhaseBegin ? (kGdnP1 | kGdnP2) : phase == kPhaseFinish ? kGdnP2 : (kGdnP1 | kGdnP2);
+      // the second phase does not scan again: the fix-up turns the map pass's per-chunk states from a zero
+      // incoming state and per-chunk transitions into the states from C->S (all chunks at once), and the
+      // cache's final state is M S_in + N in fp32
+      // (without an incoming state, as on the first segment, the map pass's values are final already)
+      const int parts = phase == kPhaseBegin ? (kGdnP1 | kGdnP2)
+                        : phase == kPhaseFinish ? (s.s0 ? kGdnFix : 0)
+                                                : (kGdnP1 | kGdnP2);
       rc = launch_gdn_prefill(s, wsm, parts);
       if (rc) return rc;
+      if (phase == kPhaseFinish) {
+        float* s_fin = reinterpret_cast<float*>(extra + gdn_prefill_fix_workspace(B, G, s.n_steps));
+        rc = launch_state_map(m_out, C->S, n_out, s_fin, B * G, D, wsm);
+        if (!rc && cudaMemcpyAsync(C->S, s_fin, (size_t)B * G * D * D * 4, cudaMemcpyDeviceToDevice, wsm) != cudaSuccess)
+          rc = cuda_fail();
+        if (rc) return rc;
+      }
     } else if (phase == kPhaseBegin) {
       identity_maps_kernel<<<grid_for((size_t)B * G * D * D), 256, 0, stream>>>(m_out, n_out, B * G, D);
       if (int e_ = launch_status()) return e_;
@@ -449,6 +477,11 @@ int bf_bifrost_layer_prefill(const bf_layer* L, const void* x, const void* q, co
                              void* ws, size_t ws_bytes, bf_stream_t stream) {
   return layer_prefill_impl(L, x, q, k, v, qr, kr, start, B, T, C, sink_k, sink_v, ns, memory, o, lse, ws, ws_bytes,
                             stream, kPhaseAll, nullptr, nullptr);
+}
+
+size_t bf_layer_prefill_sp_workspace(int B, int T, int H, int G, int D, int window, int with_ring) {
+  const size_t base = bf_layer_prefill_workspace(B, T, H, G, D, window, with_ring);
+  return base ? base + sp_extra_bytes(B, T, G, D, window, with_ring) : 0;
 }
 
 int bf_bifrost_layer_prefill_sp(const bf_layer* L, const void* x, const void* q, const void* k, const void* v,

@@ -73,6 +73,12 @@ __global__ void __launch_bounds__(256) state_map_kernel(const float* __restrict_
   }
 }
 
+// out = A @ S + N per (b, g) matrix (fp32), out distinct from S
+int launch_state_map(const float* A, const float* S, const float* N, float* out, int BG, int D, cudaStream_t stream) {
+  state_map_kernel<<<dim3(D / kSM_T, D / kSM_T, BG), 256, 0, stream>>>(A, S, N, out, D);
+  return launch_status();
+}
+
 }  // namespace bfb
 
 using namespace bfb;

@@ -133,7 +133,7 @@ class BifrostLayer:
             return self._decode(x, q, k, v, qr, kr, int(start), cache, memory)
         return self._prefill(x, q, k, v, qr, kr, int(start), cache, memory)
 
-    def _prefill_setup(self, x, q, k, v, qr, kr, start, cache, memory, out=None):
+    def _prefill_setup(self, x, q, k, v, qr, kr, start, cache, memory, out=None, two_phase=False):
         """Operands of one layer prefill: bf16 inputs, sinks, the cache in device layout, output, workspace.
         ``out`` (optional): a contiguous fp32 [B,t,H,D] tensor the layer writes its output into."""
         B, t = x.shape[:2]
@@ -184,7 +184,8 @@ class BifrostLayer:
         else:
             o = torch.empty(B, t, H, D, device=dev, dtype=torch.float32)
         ring_case = cache is not None and start > 0
-        nws = _lib.size("bf_layer_prefill_workspace", B, t, H, G, D, W, 1 if ring_case else 0)
+        nws = _lib.size("bf_layer_prefill_sp_workspace" if two_phase else "bf_layer_prefill_workspace", B, t, H, G, D,
+                        W, 1 if ring_case else 0)
         ws = torch.empty(nws, dtype=torch.uint8, device=dev)
         return dict(args=(xb, qb, kb, vb, qrb, krb), B=B, t=t, start=start, rc=rc, sk=sk, sv=sv, ns=ns, o=o, ws=ws,
                     nws=nws, cache=cache)
@@ -260,23 +261,25 @@ class BifrostLayer:
         ``prefill_sp_finish``) and uses buffers that the handle holds; a handle dropped without
         ``prefill_sp_finish`` waits for the device before those buffers are released."""
         check_cuda(x, q, k, v, qr, kr)
-        c = _SpHandle(self._prefill_setup(x, q, k, v, qr, kr, int(start), cache, True))
+        c = _SpHandle(self._prefill_setup(x, q, k, v, qr, kr, int(start), cache, True, two_phase=True))
         B, G, D = c["B"], self.G, self.D
         M = torch.empty(B, G, D, D, device=x.device, dtype=torch.float32)
         N = torch.empty_like(M)
         self._prefill_sp_call(c, 0, M, N)
+        c["maps"] = (M, N)
         done = [False]
         c["_joined"] = done
         weakref.finalize(c, _sp_abandoned, x.device, done)
         return M, N, c
 
     def prefill_sp_finish(self, handle):
-        """Second phase: the rest of the prefill from the incoming state now in ``cache["S"]``; returns o."""
+        """Second phase: the rest of the prefill from the incoming state now in ``cache["S"]``; returns o and
+        leaves ``cache["S"]`` = M S_in + N, the state after the segment."""
         c = handle
         cache = c["cache"]
         if c["rc"] is not None and "S" in cache:
             c["rc"].S = ptr(cache["S"])
-        self._prefill_sp_call(c, 1, None, None)
+        self._prefill_sp_call(c, 1, *c["maps"])
         c["_joined"][0] = True
         self._finish_cache(c)
         return c["o"]

@@ -244,13 +244,17 @@ int bf_gdn_apply_prefix(const float* M, const float* N, int n_seg, const float* 
                         int D, bf_stream_t stream);
 
 /*
- * The fused layer prefill in two phases for sequence parallelism (same arguments and workspace for both):
- * phase 0 computes the memory inputs, the per-chunk products and the state map of this segment's
- * write stream (m_out, n_out [B,G,D,D] fp32: S_out = M S_in + N, N from a zero state); phase 1 runs
- * the rest from the incoming state cache->S (the state recurrence, the memory reads, the window, the
- * gate and mix, and the cache write) without recomputing phase 0's work.  memory is on; o/lse as in
- * bf_bifrost_layer_prefill (written by phase 1).
+ * The fused layer prefill in two phases for sequence parallelism (same arguments and workspace for both; the
+ * workspace is bf_layer_prefill_sp_workspace() bytes): phase 0 computes the memory inputs, the per-chunk
+ * products and the state map of this segment's write stream (m_out, n_out [B,G,D,D] fp32: S_out = M S_in + N,
+ * N from a zero state), keeping each chunk's start state from a zero state and its start transition; phase 1
+ * (given phase 0's m_out and n_out again) turns those into the chunk states from the incoming state cache->S
+ * all at once (no second sequential scan), runs the memory reads, the window, the gate and mix and the cache
+ * write, and leaves cache->S = M S_in + N (fp32).  memory is on; o/lse as in bf_bifrost_layer_prefill
+ * (written by phase 1).  Replaces the single scan over chunks of heimdall/kernels.py:118-129 for one layer
+ * prefill split over devices.
  */
+size_t bf_layer_prefill_sp_workspace(int B, int T, int H, int G, int D, int window, int with_ring);
 int bf_bifrost_layer_prefill_sp(const bf_layer* L, const void* x, const void* q, const void* k, const void* v,
                                 const void* qr, const void* kr, long long start, int B, int T, bf_ring_cache* cache,
                                 const void* sink_k, const void* sink_v, int ns, int phase, float* m_out,
