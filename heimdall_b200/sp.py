@@ -91,13 +91,20 @@ def halo_cache(kr_h, v_h, km_h, g_h, b_h, sink_k, sink_v, S_in, start: int, W: i
     return cache
 
 
-def student_sp(L, x, q, k, v, qr, kr, group=None, memory: bool = True, timeline=None, phase_hook=None):
+def student_sp(L, x, q, k, v, qr, kr, group=None, memory: bool = True, timeline=None, phase_hook=None,
+               validate: str = "deferred"):
     """One layer prefill of a sequence split over the ranks of ``group`` in rank order, from an empty cache.
 
     Every rank passes its own T consecutive tokens (the same T on every rank, T >= W) in the layouts of
     ``BifrostLayer.student``: x [B,T,d], q [B,T,H,D], k/v [B,T,G,D], qr [B,H,T,D], kr [B,G,T,D] (bf16, on
     this rank's GPU).  Returns (o, cache): this rank's outputs [B,T,H,D] fp32 and its cache after the call
     (on the last rank that is the cache of the whole sequence).  Every rank must call it (collectives).
+
+    Every rank checks that the gathered state maps are finite (a rank that sent NaN or inf) and raises the same
+    RuntimeError for a corrupted one.  ``validate``: "deferred" (default) checks on the device and raises at the
+    start of the next call on this device, or at ``check_maps()``, so the host never waits for the exchange and
+    keeps enqueueing ahead of the GPU; "sync" waits for the check and raises before returning; "off" skips it.
+    (On CPU tensors the check is always immediate.)
 
     Instrumentation (optional, GPU only): ``timeline`` is a list that receives (label, CUDA event) pairs
     recorded on the call's stream at the start and after each step (halo exchanged, halo memory inputs, state
@@ -111,17 +118,42 @@ def student_sp(L, x, q, k, v, qr, kr, group=None, memory: bool = True, timeline=
     # The call runs on a high-priority stream: the window kernel, launched by the first phase on the
     # lowest-priority stream and left running, then yields the SMs to everything else of the call (the
     # exchange, the fold of the maps, the second scan) instead of holding them back until it ends.
+    if validate not in ("deferred", "sync", "off"):
+        raise ValueError("validate must be 'deferred', 'sync' or 'off'")
     if x.device.type != "cuda":   # the host logic on CPU tensors (a CPU restatement of the layer)
-        return _student_sp(L, x, q, k, v, qr, kr, group, memory, None, None)
+        o, cache, finite = _student_sp(L, x, q, k, v, qr, kr, group, memory, None, None)
+        if finite is not None and validate != "off":
+            _raise_if_corrupted(finite)
+        return o, cache
+    check_maps(x.device)          # the previous call's maps on this device
     cur = torch.cuda.current_stream(x.device)
     hp = _priority_stream(x.device)
     hp.wait_stream(cur)
     with torch.cuda.stream(hp):
-        o, cache = _student_sp(L, x, q, k, v, qr, kr, group, memory, timeline, phase_hook)
+        o, cache, finite = _student_sp(L, x, q, k, v, qr, kr, group, memory, timeline, phase_hook)
     cur.wait_stream(hp)   # later work on the caller's stream (reuse of the inputs' memory included) waits
     for t in [o, *(z for z in cache.values() if isinstance(z, torch.Tensor))]:
         t.record_stream(cur)   # allocated on the priority stream, used on the caller's
+    if finite is not None:
+        if validate == "sync":
+            _raise_if_corrupted(finite)
+        elif validate == "deferred":
+            _PENDING[torch.device(x.device).index] = finite
     return o, cache
+
+
+_PENDING = {}   # device index -> (flags in pinned host memory, event) of the last call's gathered maps
+
+
+def check_maps(device=None) -> None:
+    """Raise the RuntimeError of a corrupted state map received by the last ``student_sp`` call on ``device``
+    (the current device when None) that deferred its check; waits for that check on the device if needed."""
+    key = torch.device(device if device is not None else torch.cuda.current_device()).index
+    if key is None:
+        key = torch.cuda.current_device()
+    pend = _PENDING.pop(key, None)
+    if pend is not None:
+        _raise_if_corrupted(pend)
 
 
 _PRIORITY_STREAMS = {}
@@ -171,7 +203,7 @@ def _student_sp(L, x, q, k, v, qr, kr, group, memory, timeline, phase_hook):
     if not memory:
         o = L.student(x, q, k, v, qr, kr, start, cache, memory=False)
         mark("done")
-        return o, cache
+        return o, cache, None
     # phase 1: this segment's state map (memory inputs and per-chunk products are kept for phase 2)
     hook(0)
     M, N, handle = L.prefill_sp_begin(x, q, k, v, qr, kr, start, cache)
@@ -196,8 +228,7 @@ def _student_sp(L, x, q, k, v, qr, kr, group, memory, timeline, phase_hook):
     hook(1)
     o = L.prefill_sp_finish(handle)
     mark("done")
-    _raise_if_corrupted(finite)
-    return o, cache
+    return o, cache, finite
 
 
 def _maps_finite(Ms, Ns):
