@@ -65,17 +65,19 @@ int ensure_smem_attr(const void* fn, int bytes) {
   return BF_OK;
 }
 
-static cudaStream_t g_side[2][64] = {{nullptr}};
+static cudaStream_t g_side[3][64] = {{nullptr}};
 
-// which = 0: the device's least priority (the window, which fills whatever SMs the memory chain leaves);
-// which = 1: its greatest priority (the memory chain, whose CTAs are dispatched first as SMs free up)
+// which = 0 and 2: the device's least priority (the window, which fills whatever SMs the memory chain leaves;
+// two streams so that consecutive window launches overlap); which = 1: its greatest priority (the memory chain,
+// whose CTAs are dispatched first as SMs free up)
 cudaStream_t side_stream(const DeviceState& st, int which) {
+  if (which < 0 || which > 2) return nullptr;
   std::lock_guard<std::mutex> lk(g_dev_mu);
   if (!g_side[which][st.device]) {
     int least = 0, greatest = 0;
     if (cudaDeviceGetStreamPriorityRange(&least, &greatest) != cudaSuccess) return nullptr;
     cudaStream_t s = nullptr;
-    if (cudaStreamCreateWithPriority(&s, cudaStreamNonBlocking, which ? greatest : least) != cudaSuccess)
+    if (cudaStreamCreateWithPriority(&s, cudaStreamNonBlocking, which == 1 ? greatest : least) != cudaSuccess)
       return nullptr;
     g_side[which][st.device] = s;
   }

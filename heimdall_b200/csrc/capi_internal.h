@@ -17,7 +17,7 @@ struct DeviceState {
 int device_state(DeviceState* st);
 // non-blocking side streams per device (created on first use, kept for the process) for work that runs
 // concurrently inside one call, forked from and joined back into the caller's stream with events before the
-// call returns: which = 0 has the device's least stream priority, which = 1 its greatest
+// call returns: which = 0 and 2 have the device's least stream priority, which = 1 its greatest
 cudaStream_t side_stream(const DeviceState& st, int which);
 
 // per-stage timing hooks (no-ops unless bf_stage_events installed events)

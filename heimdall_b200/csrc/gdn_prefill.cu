@@ -954,8 +954,10 @@ __device__ __forceinline__ P3Item p3_item(const GdnStreams& s, long long u) {
   const long long t = u >> 1;
   it.g = (int)(t % s.G);
   const long long bc = t / s.G;
-  it.c = (int)(bc % s.n_chunks);
-  it.b = (int)(bc / s.n_chunks);
+  const int c0 = s.p3_c1 > 0 ? s.p3_c0 : 0;
+  const int nr = s.p3_c1 > 0 ? s.p3_c1 - s.p3_c0 : s.n_chunks;
+  it.c = c0 + (int)(bc % nr);
+  it.b = (int)(bc / nr);
   return it;
 }
 __device__ __forceinline__ long long p3_qrow0(const GdnStreams& s, const P3Item& it) {
@@ -1050,7 +1052,8 @@ __global__ void __launch_bounds__(kP3_Threads, 1)
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int nch = s.n_chunks;
   // packed sequences: chunks beyond the last sequence's are not work (B = 1, so they are the trailing items)
-  const long long nitems = 2LL * G * (s.chunk_tok0 ? (long long)s.seq_chunk0[s.n_seq] : (long long)s.B * nch);
+  const long long nitems =
+      2LL * G * (s.chunk_tok0 ? (long long)s.seq_chunk0[s.n_seq] : (long long)s.B * (s.p3_c1 > 0 ? s.p3_c1 - s.p3_c0 : nch));
   if (t == 0) {
     for (int i = 0; i < 16; ++i)
       mbar_init(bars + i, (i == 10 || i >= 13) ? kP3_Epi : 1);
@@ -1490,7 +1493,8 @@ int launch_gdn_prefill(GdnStreams s, cudaStream_t stream, int parts) {
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
     return cuda_fail();
-  const long long nitems = 2LL * s.B * s.G * s.n_chunks;   // (b, chunk, KV head, value half)
+  const long long nitems = 2LL * s.B * s.G * (s.p3_c1 > 0 ? s.p3_c1 - s.p3_c0 : s.n_chunks);   // (b, chunk, KV head, value half)
+  if (nitems <= 0) return BF_OK;
   (void)H;
   stage_mark(ST_GDN_P3, 0, stream);
   gdn_p3_kernel<<<(unsigned)(nitems < sms ? nitems : sms), kP3_Threads, kP3_Smem, stream>>>(qmap, kmap, smap, vmap, s);

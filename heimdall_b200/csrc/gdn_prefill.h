@@ -71,6 +71,8 @@ struct GdnStreams {
   // with mix: the window result of the rows this kernel reads, per (b, chunk, head) tile of 128 x 256 fp16 in
   // the order of the epilogue's loads (null: the window result is read from o itself)
   const __half* owin;
+  // P3 over chunks p3_c0 .. p3_c1 - 1 only (p3_c1 = 0: all chunks; not with packed sequences)
+  int p3_c0, p3_c1;
   unsigned int* err;
 };
 

@@ -170,7 +170,8 @@ size_t bf_window_workspace(int B, int G, int Tk, int D) {
 static int window_common(const void* qr, const void* k_ext, const __half* vt, const void* sink_k, const void* sink_v,
                          int ns, long long qpos0, long long kpos0, long long klo, int B, int H, int G, int Tq, int Tk,
                          int window, float* o, float* lse, unsigned int* err, cudaStream_t stream,
-                         __half* o_perm = nullptr, int perm_tile0 = 0, int perm_nch = 0, int persistent = 1) {
+                         __half* o_perm = nullptr, int perm_tile0 = 0, int perm_nch = 0, int persistent = 1,
+                         int qt0 = 0, int nqt = 0) {
   WinPreArgs a{};
   a.B = B; a.H = H; a.G = G; a.Tq = Tq; a.Tk = Tk; a.Tkp = ((Tk + 63) / 64) * 64; a.W = window;
   a.qpos0 = qpos0; a.kpos0 = kpos0; a.klo = klo;
@@ -181,6 +182,7 @@ static int window_common(const void* qr, const void* k_ext, const __half* vt, co
   a.sv_b = a.sk_b; a.sv_h = a.sk_h; a.sv_k = 256;
   a.o = o; a.lse = lse;
   a.o_perm = o_perm; a.perm_tile0 = perm_tile0; a.perm_nch = perm_nch; a.persistent = persistent;
+  a.qt0 = qt0; a.nqt = nqt;
   a.err = err;
   return launch_window_prefill(qr, k_ext, vt, a, stream);
 }
@@ -236,6 +238,13 @@ static size_t sp_extra_bytes(int B, int T, int G, int D, int window, int with_ri
   const int steps = with_ring ? T : (T > window ? T - window : 1);
   return gdn_prefill_fix_workspace(B, G, steps) + al1k((size_t)B * G * D * D * 4);
 }
+
+// The window of a whole-layer prefill with memory reads runs as up to kWinPieces launches over consecutive ranges of
+// query tiles, alternating between two least-priority streams so that each launch's CTAs fill the previous one's
+// tail; the memory reads of the chunks a piece covers start as soon as that piece (and the state scan) is done,
+// beside the next pieces, so only the last piece's reads remain after the window.
+constexpr int kWinPieces = 4;
+constexpr int kWinPieceMinChunks = 16;   // fewer chunks per piece than this: fewer pieces
 
 // phase: kPhaseAll (the whole layer), kPhaseBegin (memory inputs, P1 and the segment state map -> m_out, n_out),
 // kPhaseFinish (the rest, from C->S, reusing the workspace of the begin phase)
@@ -312,9 +321,11 @@ static int layer_prefill_impl(const bf_layer* L, const void* x, const void* q, c
   // the fork/join events are released when the call returns, on every path (an event recorded for work still
   // in flight may be destroyed: the release is deferred until that work completes)
   struct Events {
-    cudaEvent_t fork = nullptr, win = nullptr, mem = nullptr;
+    cudaEvent_t fork = nullptr, win = nullptr, mem = nullptr, vt = nullptr, piece[kWinPieces] = {};
     ~Events() {
-      for (cudaEvent_t e : {fork, win, mem})
+      for (cudaEvent_t e : {fork, win, mem, vt})
+        if (e) cudaEventDestroy(e);
+      for (cudaEvent_t e : piece)
         if (e) cudaEventDestroy(e);
     }
   } evs;
@@ -426,6 +437,7 @@ static int layer_prefill_impl(const bf_layer* L, const void* x, const void* q, c
   }
   // 3. window attention over the extended keys (o = window result, lse), on the side stream when forked
   const void* kx = kr;
+  int n_pieces = 1, piece_c0[kWinPieces] = {}, piece_c1[kWinPieces] = {};
   if (win_here) {
     stage_mark(ST_WIN_PREP, 0, ws2);
     if (ring_case) {
@@ -440,20 +452,66 @@ static int layer_prefill_impl(const bf_layer* L, const void* x, const void* q, c
     if (rc) return rc;
     stage_mark(ST_WIN_PREP, 1, ws2);
     stage_mark(ST_WIN, 0, ws2);
-    rc = window_common(qr, kx, vt, sink_k, sink_v, ns, start, ring_case ? start - W : start, L->sinks, B, H, G, T,
-                       Tk, W, o, lse_w, st.err, ws2, reads_later ? const_cast<__half*>(s.owin) : nullptr,
-                       s.qoff / kGC, s.n_chunks, will_read ? 0 : 1);
-    if (rc) return rc;
+    const long long kpos0 = ring_case ? start - W : start;
+    __half* owp = reads_later ? const_cast<__half*>(s.owin) : nullptr;
+    const int ptile0 = s.qoff / kGC, ntq = (T + kGC - 1) / kGC;
+    n_pieces = (phase == kPhaseAll && will_read && owp) ? s.n_chunks / kWinPieceMinChunks : 1;
+    n_pieces = n_pieces < 1 ? 1 : (n_pieces > kWinPieces ? kWinPieces : n_pieces);
+    if (n_pieces == 1) {
+      rc = window_common(qr, kx, vt, sink_k, sink_v, ns, start, kpos0, L->sinks, B, H, G, T, Tk, W, o, lse_w, st.err,
+                         ws2, owp, ptile0, s.n_chunks, will_read ? 0 : 1);
+      if (rc) return rc;
+    } else {
+      // the second least-priority stream starts after the V^T staging on ws2
+      cudaStream_t ws3 = side_stream(st, 2);
+      if (!ws3) return cuda_fail();
+      if (cudaEventCreateWithFlags(&evs.vt, cudaEventDisableTiming) != cudaSuccess ||
+          cudaEventRecord(evs.vt, ws2) != cudaSuccess || cudaStreamWaitEvent(ws3, evs.vt, 0) != cudaSuccess)
+        return cuda_fail();
+      for (int k = 0; k < n_pieces; ++k) {
+        // piece k: the tiles of chunks [k n / K, (k+1) n / K) (the first also the tiles before the reads)
+        piece_c0[k] = (int)((long long)s.n_chunks * k / n_pieces);
+        piece_c1[k] = (int)((long long)s.n_chunks * (k + 1) / n_pieces);
+        const int tb = k == 0 ? 0 : ptile0 + piece_c0[k];
+        const int te = k == n_pieces - 1 ? ntq : ptile0 + piece_c1[k];
+        cudaStream_t sk = (k & 1) ? ws3 : ws2;
+        if (te > tb) {
+          rc = window_common(qr, kx, vt, sink_k, sink_v, ns, start, kpos0, L->sinks, B, H, G, T, Tk, W, o, lse_w,
+                             st.err, sk, owp, ptile0, s.n_chunks, 0, tb, te - tb);
+          if (rc) return rc;
+        }
+        if (cudaEventCreateWithFlags(&evs.piece[k], cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventRecord(evs.piece[k], sk) != cudaSuccess)
+          return cuda_fail();
+      }
+      // ws2 ends after every piece (the join below and the stage mark wait for all of them)
+      for (int k = 1; k < n_pieces; k += 2)
+        if (cudaStreamWaitEvent(ws2, evs.piece[k], 0) != cudaSuccess) return cuda_fail();
+    }
     stage_mark(ST_WIN, 1, ws2);
   }
   if (phase == kPhaseBegin) return BF_OK;   // the window stays on its stream until the second phase
   if (will_read) {
-    if (cudaEventRecord(ev_win, ws2) != cudaSuccess || cudaEventRecord(ev_mem, wsm) != cudaSuccess ||
-        cudaStreamWaitEvent(stream, ev_win, 0) != cudaSuccess || cudaStreamWaitEvent(stream, ev_mem, 0) != cudaSuccess)
+    // join the memory chain; the window is joined as a whole, or piece by piece by the reads below (their waits
+    // then cover every piece before anything else runs on the caller's stream)
+    if (cudaEventRecord(ev_mem, wsm) != cudaSuccess || cudaStreamWaitEvent(stream, ev_mem, 0) != cudaSuccess)
+      return cuda_fail();
+    if (n_pieces == 1 && (cudaEventRecord(ev_win, ws2) != cudaSuccess || cudaStreamWaitEvent(stream, ev_win, 0) != cudaSuccess))
       return cuda_fail();
   }
-  // 4. memory reads, mixed into o by the gate
-  if (reads) {
+  // 4. memory reads, mixed into o by the gate (per window piece when the window was split)
+  if (reads && n_pieces > 1) {
+    for (int k = 0; k < n_pieces; ++k) {
+      if (cudaStreamWaitEvent(stream, evs.piece[k], 0) != cudaSuccess) return cuda_fail();
+      GdnStreams sp3 = s;
+      sp3.p3_c0 = piece_c0[k];
+      sp3.p3_c1 = piece_c1[k];
+      if (sp3.p3_c1 > sp3.p3_c0) {
+        rc = launch_gdn_prefill(sp3, stream, kGdnP3);
+        if (rc) return rc;
+      }
+    }
+  } else if (reads) {
     rc = launch_gdn_prefill(s, stream, kGdnP3);
     if (rc) return rc;
   }

@@ -96,7 +96,7 @@ __device__ __forceinline__ WItem win_item(const WinPreArgs& a, long long u, int 
   long long t = u / R;
   it.g = (int)(t % a.G);
   t /= a.G;
-  it.qt = (int)(t % ntq);
+  it.qt = a.qt0 + (int)(t % ntq);
   it.b = (int)(t / ntq);
   it.h = it.g * R + rr;
   it.i0 = it.qt * kWP_M;
@@ -148,7 +148,7 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
   float* xch = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int ntq = (a.Tq + kWP_M - 1) / kWP_M;
+  const int ntq = a.nqt > 0 ? a.nqt : (a.Tq + kWP_M - 1) / kWP_M;   // query tiles of this launch
   const long long nitems = (long long)a.B * ntq * a.H;
   const int ns = a.ns;
 
@@ -650,7 +650,7 @@ int launch_window_prefill(const void* qr, const void* kext, const __half* vt, Wi
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
     return cuda_fail();
-  const long long nitems = (long long)a.B * ((a.Tq + kWP_M - 1) / kWP_M) * a.H;
+  const long long nitems = (long long)a.B * (a.nqt > 0 ? a.nqt : (a.Tq + kWP_M - 1) / kWP_M) * a.H;
   if (nitems == 0) return BF_OK;
   const long long grid = a.persistent ? (nitems < sms ? nitems : sms) : nitems;
   a.pf_stride = a.persistent ? 0 : sms;

@@ -30,6 +30,8 @@ struct WinPreArgs {
   int perm_tile0, perm_nch;
   // launch: one CTA per SM walking the items (fastest alone), or one CTA per item (lets concurrent kernels on
   // other streams take SMs as CTAs finish: the layer prefill, where the memory chain runs beside the window)
+  // query tiles qt0 .. qt0 + nqt - 1 only (nqt = 0: all tiles); items of other tiles are not this launch's
+  int qt0, nqt;
   int persistent;
   int pf_stride;        // set by the launcher: one item per CTA prefetches item + pf_stride into L2 (0: none)
   unsigned int* err;

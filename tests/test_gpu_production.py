@@ -263,3 +263,31 @@ def test_delta_rule_long_state_archival():
     assert ob.rel_l2(o, o_ref) < O_TOL
     # the last 4096 tokens alone (where the accumulated state error would show most)
     assert ob.rel_l2(o[:, -4096:], o_ref[:, -4096:]) < O_TOL
+
+
+def test_layer_prefill_split_window_pieces():
+    """Prefills long enough for the window to run as several launches with the memory reads of each finished
+    piece beside the next (4 pieces here: 9000 tokens from an empty cache, then 5000 more from the ring), against
+    the oracle; outputs, state and ring."""
+    dev = _dev()
+    _threads()
+    from heimdall_b200 import BifrostLayer
+    d, Wl = 128, 512
+    parts = (9000, 5000)
+    p = layer_params(H, G, D, d, window=Wl, sinks=S, archival=1, seed=71)
+    x, q, k, v, qr, kr = _layer_inputs(d, sum(parts), seed=72)
+    f = lambda z: z.float()
+    L = BifrostLayer.from_params(p, dev)
+    cache_r, cache, s = {}, {}, 0
+    for n in parts:
+        sl = slice(s, s + n)
+        with torch.no_grad():
+            o_ref = ob.student(p, f(x[:, sl]), f(q[:, sl]), f(k[:, sl]), f(v[:, sl]), f(qr[:, :, sl]),
+                               f(kr[:, :, sl]), s, cache_r)
+        o = L.student(x[:, sl].to(dev), q[:, sl].to(dev), k[:, sl].to(dev), v[:, sl].to(dev),
+                      qr[:, :, sl].contiguous().to(dev), kr[:, :, sl].contiguous().to(dev), s, cache)
+        torch.cuda.synchronize()
+        assert ob.rel_l2(o.cpu(), o_ref) < O_TOL, (s, n)
+        s += n
+    assert ob.rel_l2(cache["S"].cpu(), cache_r["S"]) < S_TOL
+    assert torch.equal(cache["ring_pos"].cpu(), cache_r["ring_pos"])
