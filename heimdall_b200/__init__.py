@@ -13,10 +13,16 @@ Public API (mirrors of the reference ``heimdall`` package):
   BifrostLayer.student               heimdall/hibrit.py:363-424 (HybridAttention._student)
   BifrostLayer.mem_inputs            heimdall/hibrit.py:327-334
   BifrostLayer.student_host          _student for host (pinned) inputs, copies overlapped with the layer
+  BifrostLayer.decode_step           _student with t == 1 at a position per sequence (serving batches)
+  BifrostLayer.student_varlen        _student over packed variable-length sequences (one prefill each)
+  BifrostAttention.forward           heimdall/hibrit.py:426-432 (HybridAttention.forward, converted layer:
+                                     projections, fused prologue / epilogue around the core)
+  sp.student_sp                      one layer prefill of a sequence split over GPUs (sequence parallelism)
   plugin.prepare / install           the kernels.prepare plug-in convention (heimdall/kernels.py:158-188)
 """
 from .functional import delta_rule, delta_rule_gqa, delta_rule_step, delta_rule_step_gqa, window_attention  # noqa: F401
 from .layer import BifrostLayer  # noqa: F401
+from .attention import BifrostAttention  # noqa: F401
 
 __all__ = ["delta_rule", "delta_rule_gqa", "delta_rule_step", "delta_rule_step_gqa", "window_attention",
-           "BifrostLayer"]
+           "BifrostLayer", "BifrostAttention"]

@@ -40,6 +40,8 @@ SIGNATURES = {
     "bf_layer_prefill_workspace": [_I, _I, _I, _I, _I, _I, _I],
     "bf_layer_prefill_sp_workspace": [_I, _I, _I, _I, _I, _I, _I],
     "bf_bifrost_layer_prefill": [_P, _P, _P, _P, _P, _P, _P, _L, _I, _I, _P, _P, _P, _I, _I, _P, _P, _P, _Z, _P],
+    "bf_attn_prologue": [_P, _P, _P, _P, _P, _I, ctypes.c_float, _L, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P],
+    "bf_attn_epilogue": [_P, _P, _I, _I, _I, _I, _I, _P, _P],
     "bf_gdn_segment_workspace": [_I, _I, _I, _I],
     "bf_gdn_segment_transform": [_P, _I, _P, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _Z, _P],
     "bf_gdn_apply_prefix": [_P, _P, _I, _P, _P, _I, _I, _I, _P],

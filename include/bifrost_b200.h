@@ -224,6 +224,28 @@ int bf_bifrost_layer_prefill(const bf_layer* L, const void* x, const void* q, co
                              void* ws, size_t ws_bytes, bf_stream_t stream);
 
 /* ---------------------------------------------------------------------------------------------
+ * The converted attention layer around the core: fused prologue and epilogue.  The plain projection GEMMs
+ * (q/gate, k, v, o) are left to the caller's GEMM library; these two passes replace the elementwise work
+ * between them.
+ *
+ * bf_attn_prologue replaces the per-head split, the ZNorm and the partial RoPE of HybridAttention._proj
+ * (heimdall/hibrit.py:254-268; rope heimdall/kernels.py:40-49) in one pass:
+ *   qg [B,T,H,(gated ? 2 : 1)*D] bf16 (query projection, the output gate interleaved per head), kl [B,T,G,D]
+ *   bf16 (key projection), q_norm_w / k_norm_w [D] fp32 (zero-centred ZNorm weights, eps), inv_freq [rot/2]
+ *   fp32 (1 / theta^(2i/rot), as the reference computes it), pos [B*T] int64 or NULL (then start + t)
+ *   -> q [B,T,H,D], k [B,T,G,D] (normalised, before RoPE), qr [B,H,T,D], kr [B,G,T,D] (half-rotation RoPE on
+ *   the first rot dimensions), all bf16.  D must be 256; rot a multiple of 16, at most D.
+ * bf_attn_epilogue replaces the gating of HybridAttention._out (heimdall/hibrit.py:270-272) ahead of o_proj:
+ *   o [B,T,H,D] fp32 (the layer core's output), qg as above -> y [B,T,H*D] bf16 = bf16(o) * sigmoid(gate)
+ *   (y = bf16(o) when gated = 0).
+ */
+int bf_attn_prologue(const void* qg, const void* kl, const float* q_norm_w, const float* k_norm_w,
+                     const float* inv_freq, int rot, float eps, long long start, const int64_t* pos, int B, int T, int H,
+                     int G, int D, int gated, void* q, void* k, void* qr, void* kr, bf_stream_t stream);
+int bf_attn_epilogue(const float* o, const void* qg, int gated, int B, int T, int H, int D, void* y,
+                     bf_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------------
  * Sequence parallelism of the delta rule (a long sequence split into consecutive segments, one per
  * GPU).  A segment of the write stream maps any incoming state S to S_out = M (S - s0) + N, where N
  * is the final state from s0 (zero state when s0 is NULL).  These two entry points replace the

@@ -24,6 +24,10 @@ layer (reference project ``Heimdall``, package ``heimdall``):
                        (``heimdall/hibrit.py:363-424``)
 * ``init_params``   -- the conversion-time parameter init
                        (``heimdall/hibrit.py:211-240``)
+* ``proj`` / ``out`` / ``attention_forward`` -- the layer around the core:
+                       projections, ZNorm and partial RoPE, the output gate and
+                       o_proj (``heimdall/hibrit.py:246-272, 426-432``;
+                       ``heimdall/kernels.py:40-49``)
 
 Parity of this restatement is pinned against the reference itself: the fixtures
 in ``tests/golden/`` were produced by importing the reference and running it on
@@ -409,6 +413,103 @@ def student(p: LayerParams, x, q, k, v, qr, kr, start: int, cache: Optional[dict
         cache["ring_pos"][slot] = pos[-m:]
         cache["sink_k"], cache["sink_v"] = sink_k, sink_v
     return o
+
+
+# --------------------------------------------------------------------------- the layer around the core
+@dataclass
+class ProjParams:
+    """The converted layer's frozen projections (``HybridAttention.__init__``, ``heimdall/hibrit.py:199-209``):
+    q_w [H*D*(2 if gated), d] (query and output gate interleaved per head), k_w, v_w [G*D, d], o_w [d, H*D],
+    optional biases, q_norm_w / k_norm_w [D] (ZNorm weights, zero-centred), rotary dims ``rot`` and base
+    ``theta``, ``eps``."""
+    q_w: torch.Tensor
+    k_w: torch.Tensor
+    v_w: torch.Tensor
+    o_w: torch.Tensor
+    q_norm_w: torch.Tensor
+    k_norm_w: torch.Tensor
+    rot: int
+    theta: float
+    eps: float = 1e-6
+    gated: bool = True
+    q_b: Optional[torch.Tensor] = None
+    k_b: Optional[torch.Tensor] = None
+    v_b: Optional[torch.Tensor] = None
+    o_b: Optional[torch.Tensor] = None
+
+
+def znorm(x, w, eps):
+    """Qwen3.5 RMSNorm with a zero-centred weight, ``ZNorm.forward`` (``heimdall/hibrit.py:105-116``):
+    x * rsqrt(mean(x^2) + eps) * (1 + w) in fp32, returned in x's dtype."""
+    xf = x.float()
+    return (xf * torch.rsqrt(xf.square().mean(-1, keepdim=True) + eps) * (1.0 + w.float())).to(x.dtype)
+
+
+def rope_inv_freq(d: int, base: float) -> torch.Tensor:
+    """Inverse frequencies of ``kernels.rope`` (``heimdall/kernels.py:40-49``), fp32: 1 / base^(2i/d)."""
+    return 1.0 / (base ** (torch.arange(0, d, 2, dtype=torch.float32) / d))
+
+
+def rope(x, pos, base: float):
+    """Half-rotation RoPE, restating ``kernels.rope`` (``heimdall/kernels.py:40-49``): x [B,H,T,d] and positions
+    [T]; (x1, x2) = halves of the last dim, out = (x1 cos - x2 sin, x1 sin + x2 cos), computed in fp32 and
+    returned in x's dtype."""
+    d = x.shape[-1]
+    ang = pos.to(torch.float32)[..., None] * rope_inv_freq(d, base)
+    cos, sin = ang.cos(), ang.sin()
+    x1, x2 = x.float().chunk(2, dim=-1)
+    return torch.cat((x1 * cos - x2 * sin, x1 * sin + x2 * cos), dim=-1).to(x.dtype)
+
+
+def partial_rope(x, pos, rot: int, base: float):
+    """``HybridAttention._rope`` (``heimdall/hibrit.py:246-252``): RoPE on the first ``rot`` dims only."""
+    if rot == 0:
+        return x
+    if rot == x.shape[-1]:
+        return rope(x, pos, base)
+    return torch.cat((rope(x[..., :rot], pos, base), x[..., rot:]), dim=-1)
+
+
+def proj(pp: ProjParams, x, start: int):
+    """``HybridAttention._proj`` (``heimdall/hibrit.py:254-268``): x [B,t,d] (bf16) -> q [B,t,H,D], k, v
+    [B,t,G,D], qr [B,H,t,D], kr [B,G,t,D] (ZNorm'd, partial RoPE) and the output gate [B,t,H*D] (or None),
+    all in x's dtype (the projections run in x's dtype, as the reference's bf16 Linear layers do)."""
+    B, t, _ = x.shape
+    D = pp.q_norm_w.shape[0]
+    G = pp.k_w.shape[0] // D
+    qg = F.linear(x, pp.q_w.to(x.dtype), None if pp.q_b is None else pp.q_b.to(x.dtype))
+    gate = None
+    if pp.gated:
+        H = qg.shape[-1] // (2 * D)
+        q, gate = qg.view(B, t, H, 2 * D).chunk(2, dim=-1)
+        gate = gate.reshape(B, t, H * D)
+    else:
+        H = qg.shape[-1] // D
+        q = qg.view(B, t, H, D)
+    q = znorm(q, pp.q_norm_w, pp.eps)
+    k = znorm(F.linear(x, pp.k_w.to(x.dtype), None if pp.k_b is None else pp.k_b.to(x.dtype)).view(B, t, G, D),
+              pp.k_norm_w, pp.eps)
+    v = F.linear(x, pp.v_w.to(x.dtype), None if pp.v_b is None else pp.v_b.to(x.dtype)).view(B, t, G, D)
+    pos = torch.arange(start, start + t)
+    return (q, k, v, partial_rope(q.transpose(1, 2), pos, pp.rot, pp.theta),
+            partial_rope(k.transpose(1, 2), pos, pp.rot, pp.theta), gate)
+
+
+def out(pp: ProjParams, o, gate, x):
+    """``HybridAttention._out`` (``heimdall/hibrit.py:270-272``): o [B,t,H,D] -> o_proj(o * sigmoid(gate)) in
+    x's dtype."""
+    o = o.reshape(*x.shape[:2], -1).to(x.dtype)
+    if gate is not None:
+        o = o * torch.sigmoid(gate)
+    return F.linear(o, pp.o_w.to(x.dtype), None if pp.o_b is None else pp.o_b.to(x.dtype))
+
+
+def attention_forward(p: LayerParams, pp: ProjParams, x, cache: Optional[dict], start: int = 0, memory: bool = True):
+    """``HybridAttention.forward`` of a converted layer in student mode (``memory=False``: window mode)
+    (``heimdall/hibrit.py:426-432``): _proj -> _student -> _out.  x [B,t,d] -> y [B,t,d] in x's dtype."""
+    q, k, v, qr, kr, gate = proj(pp, x, start)
+    o = student(p, x, q, k, v, qr, kr, start, cache, memory=memory)
+    return out(pp, o, gate, x)
 
 
 def rel_l2(a: torch.Tensor, b: torch.Tensor) -> float:

@@ -38,6 +38,12 @@ def golden_gdn():
 
 
 @pytest.fixture(scope="session")
+def golden_forward():
+    import torch
+    return torch.load(ROOT / "tests" / "golden" / "golden_forward.pt", weights_only=False)
+
+
+@pytest.fixture(scope="session")
 def golden_layer():
     import torch
     return torch.load(ROOT / "tests" / "golden" / "golden_layer.pt", weights_only=False)

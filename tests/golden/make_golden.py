@@ -24,7 +24,7 @@ import torch.nn.functional as F
 
 HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE))
-from params import make_module_params, module_config  # noqa: E402
+from params import make_module_params, make_module_proj, module_config  # noqa: E402
 
 
 def bf(x):
@@ -128,6 +128,27 @@ def layer_case(hb, name, H, G, D, d, window, sinks, archival, parts, seed, keep_
     return {name: rec}
 
 
+def forward_case(hb, name, H, G, D, d, window, sinks, archival, parts, seed, mode="student"):
+    """HybridAttention.forward of a converted layer (projections, ZNorm, partial RoPE, the core, the output gate
+    and o_proj) over mixed prefill/decode ``parts``, in fp32 (the reference creates the converted layer's
+    parameters in fp32) on bf16-valued inputs."""
+    a = hb.HybridAttention(hb.HybridConfig(module_config(H, G, D, d)))
+    make_module_params(a, window, sinks, archival, seed)
+    make_module_proj(a, seed)
+    a.mode = mode
+    T = sum(parts)
+    gen = torch.Generator().manual_seed(seed + 300)
+    x = bf(torch.randn(1, T, d, generator=gen))
+    with torch.no_grad():
+        cache, outs, s = {}, [], 0
+        for n in parts:
+            outs.append(a.forward(x[:, s:s + n], cache, s))
+            s += n
+    return {name: dict(H=H, G=G, D=D, d=d, window=window, sinks=sinks, archival=archival, seed=seed, mode=mode,
+                       rot=a.c.rot, theta=float(a.c.rope_theta), parts=list(parts), x=x,
+                       y_parts=torch.cat(outs, 1), cache={k_: v_.clone() for k_, v_ in cache.items()})}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("HEIMDALL_REFERENCE"))
@@ -150,6 +171,13 @@ def main():
     layers.update(layer_case(hb, "d256", H=24, G=4, D=256, d=128, window=16, sinks=4, archival=1,
                              parts=(10, 1, 13, 1, 5), seed=1))
     torch.save(layers, HERE / "golden_layer.pt")
+    fwd = {}
+    # the whole converted attention layer in bf16 (the prologue and epilogue around the core), Bifrost heads
+    fwd.update(forward_case(hb, "d256", H=24, G=4, D=256, d=64, window=16, sinks=4, archival=1,
+                            parts=(21, 1, 9, 1), seed=2))
+    fwd.update(forward_case(hb, "d256_window", H=24, G=4, D=256, d=64, window=16, sinks=4, archival=1,
+                            parts=(30, 1), seed=3, mode="window"))
+    torch.save(fwd, HERE / "golden_forward.pt")
     meta = {"torch": torch.__version__, "reference": "Heimdall (heimdall.kernels / motor / hibrit)"}
     (HERE / "golden_meta.txt").write_text("\n".join(f"{k}: {v}" for k, v in meta.items()) + "\n")
     for f in sorted(HERE.glob("golden_*.pt")):

@@ -15,7 +15,7 @@ import torch
 ROOT = Path(__file__).resolve().parents[2]
 if str(ROOT) not in sys.path:
     sys.path.insert(0, str(ROOT))
-from oracle.bifrost_oracle import LayerParams  # noqa: E402
+from oracle.bifrost_oracle import LayerParams, ProjParams  # noqa: E402
 
 
 def module_config(H: int, G: int, D: int, d: int) -> dict:
@@ -67,3 +67,30 @@ def make_module_params(attn, window: int, sinks: int, archival: int, seed: int) 
 def layer_params(H: int, G: int, D: int, d: int, window: int, sinks: int, archival: int, seed: int) -> LayerParams:
     """The same values as an oracle ``LayerParams`` (no reference needed)."""
     return LayerParams(window=window, sinks=sinks, **param_tensors(H, G, D, d, window, archival, seed))
+
+
+def proj_tensors(H: int, G: int, D: int, d: int, seed: int) -> dict:
+    """Deterministic projection weights of one attention layer (q/gate, k, v, o, the two ZNorm weights), scaled
+    so that the projections of unit-variance inputs have unit variance."""
+    gen = torch.Generator().manual_seed(2000 + seed)
+    n = lambda *s: torch.randn(*s, generator=gen)
+    return dict(q_w=n(2 * H * D, d) * d ** -0.5, k_w=n(G * D, d) * d ** -0.5, v_w=n(G * D, d) * d ** -0.5,
+                o_w=n(d, H * D) * (H * D) ** -0.5, q_norm_w=0.1 * n(D), k_norm_w=0.1 * n(D))
+
+
+def make_module_proj(attn, seed: int) -> None:
+    """Overwrite a reference ``HybridAttention``'s projections and norms with ``proj_tensors``."""
+    c = attn.c
+    t = proj_tensors(c.h, c.hkv, c.dh, c.d, seed)
+    with torch.no_grad():
+        attn.q_proj.weight.copy_(t["q_w"])
+        attn.k_proj.weight.copy_(t["k_w"])
+        attn.v_proj.weight.copy_(t["v_w"])
+        attn.o_proj.weight.copy_(t["o_w"])
+        attn.q_norm.weight.copy_(t["q_norm_w"])
+        attn.k_norm.weight.copy_(t["k_norm_w"])
+
+
+def proj_params(H: int, G: int, D: int, d: int, seed: int, rot: int, theta: float = 10000.0) -> ProjParams:
+    """The same values as an oracle ``ProjParams`` (no reference needed)."""
+    return ProjParams(rot=rot, theta=theta, **proj_tensors(H, G, D, d, seed))

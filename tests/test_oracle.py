@@ -159,3 +159,21 @@ def test_student_reference_form_equals_gqa_form(golden_layer):
     a = ob.student(p, f("x"), f("q"), f("k"), f("v"), f("qr"), f("kr"), 0, None)
     b = ob.student(p, f("x"), f("q"), f("k"), f("v"), f("qr"), f("kr"), 0, None, gqa_native=False)
     assert (a - b).abs().max() < 1e-5
+
+
+@pytest.mark.parametrize("name", ["d256", "d256_window"])
+def test_attention_forward_matches_reference(golden_forward, name):
+    """The whole converted attention layer (projections, ZNorm, partial RoPE, the core, output gate and o_proj;
+    HybridAttention.forward, hibrit.py:426-432) over mixed prefill/decode parts, against the reference."""
+    from params import proj_params
+    c = golden_forward[name]
+    p = layer_params(c["H"], c["G"], c["D"], c["d"], c["window"], c["sinks"], c["archival"], c["seed"])
+    pp = proj_params(c["H"], c["G"], c["D"], c["d"], c["seed"], c["rot"], c["theta"])
+    cache, outs, s = {}, [], 0
+    for n in c["parts"]:
+        outs.append(ob.attention_forward(p, pp, c["x"][:, s:s + n], cache, s, memory=c["mode"] != "window"))
+        s += n
+    y = torch.cat(outs, 1)
+    assert _close(y, c["y_parts"], 2e-5), (y - c["y_parts"]).abs().max()
+    for k, ref in c["cache"].items():
+        assert _close(cache[k].double(), ref.double(), 2e-5), k
