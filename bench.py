@@ -20,7 +20,8 @@ sample), ``e2e`` (the headline through the public API from pinned host buffers, 
 region), ``sp_131k`` (N > 1: a per-rank timeline of one step and an in-bench parity check against one prefill
 of the whole sequence on one GPU), ``sp_1m`` (config 3 at T = 1048576, same), ``decode`` (64
 sequences x 12 layers, sharded over the N GPUs), ``delta_rule`` (configs 0 and 4: the chunked delta-rule op),
-``clocks`` (nvidia-smi samples during the timed region) and ``gpu_launches``.
+``interchange`` (N = 1: the llama.cpp state rows of config 2's decode cache, packed and unpacked), ``clocks``
+(nvidia-smi samples during the timed region) and ``gpu_launches``.
 """
 from __future__ import annotations
 
@@ -563,6 +564,40 @@ def run_decode(device, ctx, steps=256, warmup=8, nseq=64, nlayers=12):
                               "frac": per_layer_bytes * nlayers / (us_step * 1e-6) / 1e9 / pk["hbm_gbs"]}}
 
 
+def run_interchange(device, nseq=64, steps=20, warmup=3):
+    """The llama.cpp state-row interchange at config-2 geometry (64 sequences, W = 2048, one layer): pack the
+    decode cache into the port's rows and unpack them again.  Both are HBM-bound copies (rows 43.7 MB per
+    sequence); algorithmic bytes = every byte read plus every byte written once."""
+    from heimdall_b200.interchange import llama_state_floats, pack_llama_state, unpack_llama_state
+    L = make_layer(device, seed=7)
+    gen = torch.Generator(device=device).manual_seed(7)
+    bf = torch.bfloat16
+    r = lambda *s: torch.randn(*s, generator=gen, device=device)
+    pos = torch.randint(4096, 131072, (nseq,), generator=gen, device=device, dtype=torch.int64)
+    ring_abs = pos[:, None] - W + torch.arange(W, device=device)[None]
+    rp = torch.empty(nseq, W, dtype=torch.int64, device=device).scatter_(1, ring_abs % W, ring_abs)
+    cache = dict(ring_k=r(nseq, G, W, D).to(bf), ring_v=r(nseq, G, W, D).to(bf), ring_km=r(nseq, W, G, D),
+                 ring_g=r(nseq, W, G), ring_beta=r(nseq, W, G), ring_pos=rp, sink_k=r(nseq, G, S, D).to(bf),
+                 sink_v=r(nseq, G, S, D).to(bf), S=r(nseq, G, D, D))
+    n = llama_state_floats(G, D, W, S)
+    rows = torch.empty(nseq, n, device=device)
+    back = {k: torch.empty_like(v) for k, v in cache.items()}
+    pack_ms = _time_device(lambda: pack_llama_state(L, cache, pos, rows=rows), steps, warmup)
+    unpack_ms = _time_device(lambda: unpack_llama_state(L, rows, pos, cache=back), steps, warmup)
+    ok = all(torch.equal(back[k], cache[k]) for k in cache)
+    C = 3 * G * D + 2 * G
+    cache_bytes = nseq * (2 * G * W * D * 2 + G * W * D * 4 + 2 * W * G * 4 + W * 8 + 2 * G * S * D * 2 + G * D * D * 4)
+    pack_bytes = cache_bytes + nseq * n * 4
+    unpack_bytes = cache_bytes + nseq * ((W + S) * C * 4 + G * D * D * 4)
+    pk, _ = peaks()
+    leg = lambda ms, nb: {"ms": ms, "bytes": nb, "achieved_gbs": nb / (ms * 1e-3) / 1e9,
+                          "frac": nb / (ms * 1e-3) / 1e9 / pk["hbm_gbs"]}
+    return {"workload": f"{nseq} sequences, W={W}, S={S}, G={G}, D={D}: one layer's decode cache <-> llama.cpp "
+                        f"state rows ({n * 4 / 1e6:.1f} MB per sequence)",
+            "pack": leg(pack_ms, pack_bytes), "unpack": leg(unpack_ms, unpack_bytes), "round_trip_exact": ok,
+            "peak_gbs": pk["hbm_gbs"]}
+
+
 # ---------------------------------------------------------------------------------------------- CPU arms
 def cpu_sample_tokens_per_s(n_new=2048, start=None, seed=0, threads=None):
     """The CPU oracle (a restatement of the reference's PyTorch path, in the reference's own form: the prefill
@@ -701,6 +736,7 @@ def main(argv=None):
     ap.add_argument("--no-sp", action="store_true", help="skip the 1M-token sequence-parallel leg")
     ap.add_argument("--no-delta", action="store_true")
     ap.add_argument("--no-config1", action="store_true")
+    ap.add_argument("--no-interchange", action="store_true", help="skip the llama.cpp state-row leg")
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":
@@ -911,6 +947,8 @@ def run_ours(args, ctx):
         out["delta_rule"] = run_delta_configs(dev)
     if decode is not None:
         out["decode"] = decode
+    if world == 1 and not args.no_interchange:
+        out["interchange"] = run_interchange(dev)
     print(json.dumps(out), flush=True)
 
 

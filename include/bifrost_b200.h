@@ -282,6 +282,33 @@ int bf_bifrost_layer_prefill_sp(const bf_layer* L, const void* x, const void* q,
                                 const void* sink_k, const void* sink_v, int ns, int phase, float* m_out,
                                 float* n_out, float* o, float* lse, void* ws, size_t ws_bytes, bf_stream_t stream);
 
+/* ---------------------------------------------------------------------------------------------
+ * Interchange with the llama.cpp port's per-sequence state row of one converted layer (reference
+ * llamacpp/bifrost.patch), so a sequence can move between this library's cache and a llama.cpp server.
+ * The row is fp32, ggml order: region [C, LR] (slot rows [k_rope | v | k_mem | g | beta], C = 3 G D + 2 G),
+ * K plane [D, LR, G], transposed V plane [LR, D, G], delta state [D, D, G] (key index fastest), with
+ * LR = round_up(sinks + window + 2, 32) slots: sinks | ring of window + 1 slots (slot = sinks + pos mod
+ * (window + 1)) | scratch + padding.
+ *
+ * bf_llama_state_floats replaces llama_hparams::bifrost_state (bifrost.patch:221-239): floats per row.
+ * bf_llama_state_pack: cache (ring_k/ring_v bf16; ring_pos [W] or [B,W]; sinks [B,G,ns,D] bf16 or ns = 0;
+ *   S [B,G,D,D] or NULL = zero state) of B sequences whose next positions are next_pos [B] (device int64) ->
+ *   rows (row b at rows + b * row_stride floats; row_stride >= bf_llama_state_floats).  Writes every float of
+ *   the rows: the ring rows of positions next_pos - W .. next_pos - 1 that the cache holds, the sink rows,
+ *   the delta state; zero elsewhere (what the port writes there is never read again).  Replaces the port's
+ *   writes of a prefill / decode into the row (bifrost.patch:1040-1085) for a sequence the library advanced.
+ * bf_llama_state_unpack: rows -> cache for sequences at next_pos (ring slot j <- the position of
+ *   [next_pos - W, next_pos) that is j mod W, ring_pos set, -1 and zeros for negative positions; sink rows
+ *   0 .. ns-1; S).  k_rope and v are rounded to bf16 (nearest even).  With ring_pos [W] (bstride 0) every
+ *   sequence must be at the same position.  S is required.
+ * D a multiple of 32, G * D <= 2048.  Both are layout copies on `stream` (HBM-bound).
+ */
+size_t bf_llama_state_floats(int G, int D, int window, int sinks);
+int bf_llama_state_pack(const bf_ring_cache* cache, const int64_t* next_pos, int B, int G, int D, int window,
+                        int sinks, float* rows, long long row_stride, bf_stream_t stream);
+int bf_llama_state_unpack(const float* rows, long long row_stride, const int64_t* next_pos, int B, int G, int D,
+                          int window, int sinks, bf_ring_cache* cache, bf_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -24,7 +24,7 @@ import torch.nn.functional as F
 
 HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE))
-from params import make_module_params, make_module_proj, module_config  # noqa: E402
+from params import make_module_params, make_module_proj, module_config, param_tensors  # noqa: E402
 
 
 def bf(x):
@@ -149,19 +149,48 @@ def forward_case(hb, name, H, G, D, d, window, sinks, archival, parts, seed, mod
                        y_parts=torch.cat(outs, 1), cache={k_: v_.clone() for k_, v_ in cache.items()})}
 
 
+def gguf_case(proj):
+    """The llama.cpp port's GGUF tensors of two converted layers, made by the reference's own
+    ``tensors_from_conv`` (llamacpp/bifrost_gguf.py:23-44) from a conversion-parameter dict."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("bifrost_gguf", proj / "llamacpp" / "bifrost_gguf.py")
+    bg = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bg)
+    names = {"fq": "fq", "fk": "fk", "ab_w": "ab.weight", "ab_b": "ab.bias", "mix_w": "mix.weight",
+             "mix_b": "mix.bias", "mix_lse": "mix_lse", "mem_scale": "mem_scale", "A_log": "A_log",
+             "dt_bias": "dt_bias"}
+    conv, params, layers = [], {}, {}
+    for i, (idx, archival) in enumerate(((3, 1), (7, 2))):
+        p = param_tensors(4, 2, 32, 64, 16, archival, seed=10 + i)
+        name = f"layers.{idx}"
+        conv.append({"name": name, "archival": archival, "window": 16, "sinks": 4})
+        for ours, theirs in names.items():
+            params[f"{name}.self_attn.{theirs}"] = p[ours].clone()
+        layers[idx] = p
+    out, window, sinks = bg.tensors_from_conv({"conv": conv, "params": params})
+    return {"layers": layers, "window": window, "sinks": sinks,
+            "tensors": {i: {k: torch.from_numpy(v.copy()) for k, v in t.items()} for i, t in out.items()}}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("HEIMDALL_REFERENCE"))
+    ap.add_argument("--cases", default="all", help="comma list of gdn, layer, forward, gguf (default all)")
     args = ap.parse_args()
     if not args.ref:
         ap.error("name the reference project with --ref or HEIMDALL_REFERENCE")
     ref = Path(args.ref)
-    sys.path.insert(0, str(ref / "Heimdall" if (ref / "Heimdall" / "heimdall").is_dir() else ref))
+    proj = ref / "Heimdall" if (ref / "Heimdall" / "heimdall").is_dir() else ref
+    sys.path.insert(0, str(proj))
     import heimdall.hibrit as hb
     import heimdall.kernels as hk
     import heimdall.motor as hm
     torch.set_num_threads(8)
-    torch.save(gdn_cases(hk, hm), HERE / "golden_gdn.pt")
+    cases = {"gdn", "layer", "forward", "gguf"} if args.cases == "all" else set(args.cases.split(","))
+    if "gguf" in cases:
+        torch.save(gguf_case(proj), HERE / "golden_gguf.pt")
+    if "gdn" in cases:
+        torch.save(gdn_cases(hk, hm), HERE / "golden_gdn.pt")
     layers = {}
     # tiny shapes of tests/test_hibrit.py (window 8, sinks 2, 4 Q / 2 KV heads, head_dim 32) with the
     # mixed prefill/decode part pattern of test_chunked_cache_equals_full
@@ -170,15 +199,18 @@ def main():
     # Bifrost head geometry (24 Q / 4 KV, D=256, 4 sinks), short window so memory is active
     layers.update(layer_case(hb, "d256", H=24, G=4, D=256, d=128, window=16, sinks=4, archival=1,
                              parts=(10, 1, 13, 1, 5), seed=1))
-    torch.save(layers, HERE / "golden_layer.pt")
+    if "layer" in cases:
+        torch.save(layers, HERE / "golden_layer.pt")
     fwd = {}
     # the whole converted attention layer in bf16 (the prologue and epilogue around the core), Bifrost heads
     fwd.update(forward_case(hb, "d256", H=24, G=4, D=256, d=64, window=16, sinks=4, archival=1,
                             parts=(21, 1, 9, 1), seed=2))
     fwd.update(forward_case(hb, "d256_window", H=24, G=4, D=256, d=64, window=16, sinks=4, archival=1,
                             parts=(30, 1), seed=3, mode="window"))
-    torch.save(fwd, HERE / "golden_forward.pt")
-    meta = {"torch": torch.__version__, "reference": "Heimdall (heimdall.kernels / motor / hibrit)"}
+    if "forward" in cases:
+        torch.save(fwd, HERE / "golden_forward.pt")
+    meta = {"torch": torch.__version__,
+            "reference": "Heimdall (heimdall.kernels / motor / hibrit; llamacpp/bifrost_gguf.py)"}
     (HERE / "golden_meta.txt").write_text("\n".join(f"{k}: {v}" for k, v in meta.items()) + "\n")
     for f in sorted(HERE.glob("golden_*.pt")):
         print(f.name, f.stat().st_size)
