@@ -70,9 +70,23 @@ __device__ __forceinline__ long long pmod(long long a, long long m) { return ((a
 
 constexpr int kLS_Slots = 32;     // slots per CTA
 constexpr int kLS_Threads = 256;
+constexpr int kLS_D = 256;        // head dim (float4 chunk i of a lane: head i / 2, dims ((i & 1) 32 + lane) 4 ..)
 
-__host__ __device__ inline int ls_vpitch(int GD) { return GD + 2; }   // bf16 elements; odd word pitch: no bank conflicts
+__host__ __device__ inline int ls_vpitch(int GD) { return GD + 4; }   // bf16 per slot row of the V staging
 
+__device__ __forceinline__ float4 bf16x4_to_f4(uint2 u) {
+  return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u), __uint_as_float(u.y << 16),
+                     __uint_as_float(u.y & 0xffff0000u));
+}
+__device__ __forceinline__ uint2 f4_to_bf16x4(float4 f) {
+  const __nv_bfloat162 lo = __floats2bfloat162_rn(f.x, f.y), hi = __floats2bfloat162_rn(f.z, f.w);
+  return make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+}
+__device__ __forceinline__ int ls_chunk_d(int i, int lane) { return (((i & 1) << 5) + lane) << 2; }
+
+// One warp per slot row: k_rope and v (bf16 -> fp32, into the region and the K plane; v also staged in shared
+// memory), k_mem, g, beta; loads are issued four chunks at a time ahead of their stores.  Then the CTA writes
+// the transposed V plane from the staging: channel row e holds slots l0 .. l0 + 31 (eight float4 per row).
 __global__ void __launch_bounds__(kLS_Threads) llama_pack_slots_kernel(LsArgs a) {
   const LsGeom& m = a.m;
   const int b = blockIdx.y;
@@ -80,7 +94,7 @@ __global__ void __launch_bounds__(kLS_Threads) llama_pack_slots_kernel(LsArgs a)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   __shared__ int s_kind[kLS_Slots], s_idx[kLS_Slots];
   extern __shared__ __align__(16) unsigned char ls_smem[];
-  __nv_bfloat16* s_v = reinterpret_cast<__nv_bfloat16*>(ls_smem);   // [32][GD + 2]
+  __nv_bfloat16* s_v = reinterpret_cast<__nv_bfloat16*>(ls_smem);   // [32][GD + 4]
   const long long P = a.next_pos[b];
   if (threadIdx.x < kLS_Slots) {
     const int l = l0 + threadIdx.x;
@@ -101,50 +115,66 @@ __global__ void __launch_bounds__(kLS_Threads) llama_pack_slots_kernel(LsArgs a)
   __syncthreads();
   float* row = a.rows + (long long)b * a.row_stride;
   const int vp = ls_vpitch(m.GD);
+  const int n4 = 2 * m.G;                      // float4 chunks per lane in a G*D part
   for (int s = warp; s < kLS_Slots; s += kLS_Threads / 32) {
-    const int l = l0 + s;
-    if (l >= m.LR) break;
+    const int l = l0 + s;                      // LR is a multiple of 32: every slot of the tile exists
     const int kind = s_kind[s], idx = s_idx[s];
     float* rr = row + (long long)l * m.C;
-    __nv_bfloat16* sv = s_v + s * vp;
-    for (int g = 0; g < m.G; ++g) {
-      const __nv_bfloat16 *ks = nullptr, *vs = nullptr;
-      if (kind == 2) {
-        const long long o = (((long long)b * m.G + g) * m.W + idx) * m.D;
-        ks = a.ring_k + o; vs = a.ring_v + o;
-      } else if (kind == 1) {
-        const long long o = (((long long)b * m.G + g) * a.ns + idx) * m.D;
-        ks = a.sink_k + o; vs = a.sink_v + o;
+    const __nv_bfloat16 *kb = nullptr, *vb = nullptr;
+    long long hs = 0;                          // head stride of the source
+    if (kind == 2) {
+      kb = a.ring_k + ((long long)b * m.G * m.W + idx) * kLS_D;
+      vb = a.ring_v + ((long long)b * m.G * m.W + idx) * kLS_D;
+      hs = (long long)m.W * kLS_D;
+    } else if (kind == 1) {
+      kb = a.sink_k + ((long long)b * m.G * a.ns + idx) * kLS_D;
+      vb = a.sink_v + ((long long)b * m.G * a.ns + idx) * kLS_D;
+      hs = (long long)a.ns * kLS_D;
+    }
+    for (int i0 = 0; i0 < n4; i0 += 4) {
+      uint2 kr[4], vr[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + u;
+        const long long o = (i >> 1) * hs + ls_chunk_d(i, lane);
+        kr[u] = kb ? __ldg(reinterpret_cast<const uint2*>(kb + o)) : make_uint2(0u, 0u);
+        vr[u] = vb ? __ldg(reinterpret_cast<const uint2*>(vb + o)) : make_uint2(0u, 0u);
       }
-      float* kpl = row + m.off_kp + ((long long)g * m.LR + l) * m.D;
-      for (int d = lane; d < m.D; d += 32) {
-        const __nv_bfloat16 kb = ks ? ks[d] : __float2bfloat16_rn(0.f);
-        const __nv_bfloat16 vb = vs ? vs[d] : __float2bfloat16_rn(0.f);
-        const float kf = __bfloat162float(kb);
-        rr[g * m.D + d] = kf;
-        kpl[d] = kf;
-        rr[m.GD + g * m.D + d] = __bfloat162float(vb);
-        sv[g * m.D + d] = vb;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + u, g = i >> 1, e = g * kLS_D + ls_chunk_d(i, lane);
+        const float4 kf = bf16x4_to_f4(kr[u]);
+        *reinterpret_cast<float4*>(rr + e) = kf;
+        *reinterpret_cast<float4*>(row + m.off_kp + ((long long)g * m.LR + l) * kLS_D + ls_chunk_d(i, lane)) = kf;
+        *reinterpret_cast<float4*>(rr + m.GD + e) = bf16x4_to_f4(vr[u]);
+        *reinterpret_cast<uint2*>(s_v + s * vp + e) = vr[u];
       }
     }
     const float* km = kind == 2 ? a.ring_km + ((long long)b * m.W + idx) * m.GD : nullptr;
-    for (int e = lane; e < m.GD; e += 32) rr[2 * m.GD + e] = km ? km[e] : 0.f;
-    for (int e = lane; e < 2 * m.G; e += 32) {
+    for (int i0 = 0; i0 < n4; i0 += 4) {
+      float4 r4[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        r4[u] = km ? __ldg(reinterpret_cast<const float4*>(km) + (i0 + u) * 32 + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) reinterpret_cast<float4*>(rr + 2 * m.GD)[(i0 + u) * 32 + lane] = r4[u];
+    }
+    if (lane < 2 * m.G) {
       float x = 0.f;
       if (kind == 2) {
         const long long o = ((long long)b * m.W + idx) * m.G;
-        x = e < m.G ? a.ring_g[o + e] : a.ring_beta[o + e - m.G];
+        x = lane < m.G ? a.ring_g[o + lane] : a.ring_beta[o + lane - m.G];
       }
-      rr[3 * m.GD + e] = x;
+      rr[3 * m.GD + lane] = x;
     }
   }
   __syncthreads();
-  // transposed V plane: channel row e = g D + d holds 32 consecutive slots l0 .. l0 + 31 of this tile
-  const int l = l0 + lane;
-  if (l < m.LR) {
-    float* vpl = row + m.off_vp + l;
-    for (int e = warp; e < m.GD; e += kLS_Threads / 32)
-      vpl[(long long)e * m.LR] = __bfloat162float(s_v[lane * vp + e]);
+  float* vpl = row + m.off_vp + l0;
+  for (int t = threadIdx.x; t < m.GD * 8; t += kLS_Threads) {
+    const int e = t >> 3, q = (t & 7) << 2;
+    const float4 o = make_float4(__bfloat162float(s_v[q * vp + e]), __bfloat162float(s_v[(q + 1) * vp + e]),
+                                 __bfloat162float(s_v[(q + 2) * vp + e]), __bfloat162float(s_v[(q + 3) * vp + e]));
+    *reinterpret_cast<float4*>(vpl + (long long)e * m.LR + q) = o;
   }
 }
 
@@ -170,47 +200,68 @@ __global__ void __launch_bounds__(256) llama_state_delta_kernel(LsArgs a) {
   }
 }
 
-// unpack: item i < W is the cache's ring slot j = i, item W + l its sink row l; one warp per item
+// unpack: item i < W is the cache's ring slot j = i, item W + l its sink row l; one warp per item, loads four
+// float4 chunks ahead of their stores
 __global__ void __launch_bounds__(kLS_Threads) llama_unpack_slots_kernel(LsArgs a) {
   const LsGeom& m = a.m;
   const int b = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long P = a.next_pos[b];
   const float* row = a.rows + (long long)b * a.row_stride;
+  const int n4 = 2 * m.G;
   for (int s = warp; s < kLS_Slots; s += kLS_Threads / 32) {
     const int i = blockIdx.x * kLS_Slots + s;
     if (i >= m.W + a.ns) break;
-    if (i < m.W) {
-      const int j = i;
-      const long long p = P - m.W + pmod(j - (P - m.W), m.W);        // the position of [P - W, P) at slot j
-      const bool ok = p >= 0;
-      const float* rr = ok ? row + (long long)(m.S + pmod(p, m.W + 1)) * m.C : nullptr;
-      for (int g = 0; g < m.G; ++g) {
-        const long long o = (((long long)b * m.G + g) * m.W + j) * m.D;
-        for (int d = lane; d < m.D; d += 32) {
-          a.ring_k[o + d] = __float2bfloat16_rn(ok ? rr[g * m.D + d] : 0.f);
-          a.ring_v[o + d] = __float2bfloat16_rn(ok ? rr[m.GD + g * m.D + d] : 0.f);
-        }
-      }
-      float* km = a.ring_km + ((long long)b * m.W + j) * m.GD;
-      for (int e = lane; e < m.GD; e += 32) km[e] = ok ? rr[2 * m.GD + e] : 0.f;
-      const long long o = ((long long)b * m.W + j) * m.G;
-      for (int e = lane; e < m.G; e += 32) {
-        a.ring_g[o + e] = ok ? rr[3 * m.GD + e] : 0.f;
-        a.ring_beta[o + e] = ok ? rr[3 * m.GD + m.G + e] : 0.f;
-      }
-      if (lane == 0 && (a.pos_bstride != 0 || b == 0)) a.ring_pos[(long long)b * a.pos_bstride + j] = ok ? p : -1;
+    const bool ring = i < m.W;
+    long long p = 0;
+    const float* rr;
+    __nv_bfloat16 *kb, *vb;
+    long long hs;
+    if (ring) {
+      p = P - m.W + pmod(i - (P - m.W), m.W);                       // the position of [P - W, P) at slot i
+      rr = p >= 0 ? row + (long long)(m.S + pmod(p, m.W + 1)) * m.C : nullptr;
+      kb = a.ring_k + ((long long)b * m.G * m.W + i) * kLS_D;
+      vb = a.ring_v + ((long long)b * m.G * m.W + i) * kLS_D;
+      hs = (long long)m.W * kLS_D;
     } else {
       const int l = i - m.W;
-      const float* rr = row + (long long)l * m.C;
-      for (int g = 0; g < m.G; ++g) {
-        const long long o = (((long long)b * m.G + g) * a.ns + l) * m.D;
-        for (int d = lane; d < m.D; d += 32) {
-          a.sink_k[o + d] = __float2bfloat16_rn(rr[g * m.D + d]);
-          a.sink_v[o + d] = __float2bfloat16_rn(rr[m.GD + g * m.D + d]);
-        }
+      rr = row + (long long)l * m.C;
+      kb = a.sink_k + ((long long)b * m.G * a.ns + l) * kLS_D;
+      vb = a.sink_v + ((long long)b * m.G * a.ns + l) * kLS_D;
+      hs = (long long)a.ns * kLS_D;
+    }
+    const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i0 = 0; i0 < n4; i0 += 4) {
+      float4 kr[4], vr[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int c = i0 + u, e = (c >> 1) * kLS_D + ls_chunk_d(c, lane);
+        kr[u] = rr ? *reinterpret_cast<const float4*>(rr + e) : z4;
+        vr[u] = rr ? *reinterpret_cast<const float4*>(rr + m.GD + e) : z4;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int c = i0 + u;
+        const long long o = (c >> 1) * hs + ls_chunk_d(c, lane);
+        *reinterpret_cast<uint2*>(kb + o) = f4_to_bf16x4(kr[u]);
+        *reinterpret_cast<uint2*>(vb + o) = f4_to_bf16x4(vr[u]);
       }
     }
+    if (!ring) continue;
+    float4* km = reinterpret_cast<float4*>(a.ring_km + ((long long)b * m.W + i) * m.GD);
+    for (int i0 = 0; i0 < n4; i0 += 4) {
+      float4 r4[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) r4[u] = rr ? reinterpret_cast<const float4*>(rr + 2 * m.GD)[(i0 + u) * 32 + lane] : z4;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) km[(i0 + u) * 32 + lane] = r4[u];
+    }
+    const long long o = ((long long)b * m.W + i) * m.G;
+    if (lane < m.G) {
+      a.ring_g[o + lane] = rr ? rr[3 * m.GD + lane] : 0.f;
+      a.ring_beta[o + lane] = rr ? rr[3 * m.GD + m.G + lane] : 0.f;
+    }
+    if (lane == 0 && (a.pos_bstride != 0 || b == 0)) a.ring_pos[(long long)b * a.pos_bstride + i] = rr ? p : -1;
   }
 }
 
@@ -222,7 +273,10 @@ static int ls_check(const bf_ring_cache* c, const int64_t* next_pos, int B, int 
   if (c->ns < 0 || c->ns > S || (c->ns > 0 && (!c->sink_k || !c->sink_v))) return BF_ERR_INVALID_ARGUMENT;
   if (c->ring_pos_bstride != 0 && c->ring_pos_bstride != W) return BF_ERR_INVALID_ARGUMENT;
   if (!pack && !c->S) return BF_ERR_INVALID_ARGUMENT;
-  if (D % 32 || G * D > 2048) return BF_ERR_UNSUPPORTED;
+  if (D != kLS_D || G % 2 || G > 8) return BF_ERR_UNSUPPORTED;
+  if (!aligned16(rows) || row_stride % 4 || !aligned16(c->ring_km) || ((uintptr_t)c->ring_k & 7) ||
+      ((uintptr_t)c->ring_v & 7) || ((uintptr_t)c->sink_k & 7) || ((uintptr_t)c->sink_v & 7))
+    return BF_ERR_ALIGNMENT;
   const LsGeom m = ls_geom(G, D, W, S);
   if (row_stride < m.nfloats) return BF_ERR_INVALID_ARGUMENT;
   LsArgs& a = *out;

@@ -301,7 +301,8 @@ int bf_bifrost_layer_prefill_sp(const bf_layer* L, const void* x, const void* q,
  *   [next_pos - W, next_pos) that is j mod W, ring_pos set, -1 and zeros for negative positions; sink rows
  *   0 .. ns-1; S).  k_rope and v are rounded to bf16 (nearest even).  With ring_pos [W] (bstride 0) every
  *   sequence must be at the same position.  S is required.
- * D a multiple of 32, G * D <= 2048.  Both are layout copies on `stream` (HBM-bound).
+ * D = 256, G even and at most 8; rows 16-byte aligned with row_stride a multiple of 4, ring_km 16-byte and the
+ * bf16 arrays 8-byte aligned (else BF_ERR_ALIGNMENT).  Both are layout copies on `stream` (HBM-bound).
  */
 size_t bf_llama_state_floats(int G, int D, int window, int sinks);
 int bf_llama_state_pack(const bf_ring_cache* cache, const int64_t* next_pos, int B, int G, int D, int window,
