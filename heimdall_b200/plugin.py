@@ -7,6 +7,7 @@ by value (heimdall/motor.py:37), so the patch points are that module attribute a
 methods that implement the converted (Bifrost) layer core:
 
   heimdall.motor.delta_rule_gqa                   (motor.py:70-102)     -> functional.delta_rule_gqa
+  heimdall.motor.window_attention                 (motor.py:105-115)    -> functional.window_attention
   HybridAttention._student                        (hibrit.py:363-424)   -> BifrostLayer.student
   HybridAttention._window                         (hibrit.py:336-361)   -> functional.window_attention
   HybridAttention._mem_inputs                     (hibrit.py:327-334)   -> BifrostLayer.mem_inputs
@@ -34,7 +35,7 @@ from .layer import BifrostLayer
 
 _SAVED: list = []          # (owner, attribute name, original value) in patch order
 # what install() replaces: (module key, attribute path)
-PATCHED_NAMES = (("motor", "delta_rule_gqa"), ("hibrit", "HybridAttention._student"),
+PATCHED_NAMES = (("motor", "delta_rule_gqa"), ("motor", "window_attention"), ("hibrit", "HybridAttention._student"),
                  ("hibrit", "HybridAttention._mem_inputs"), ("hibrit", "HybridAttention._window"))
 SELF_TEST_TOL = 0.03       # the reference's acceptance threshold (kernels.py:182)
 
@@ -120,19 +121,37 @@ def _window(self, qr, ext_k, ext_v, ext_pos, sink_k, sink_v, pos):
     _require_cuda(qr, ext_k, ext_v, ext_pos, sink_k, sink_v, pos)
     t, n_ext = qr.shape[2], ext_k.shape[2]
     p = pos.to(torch.int64)
-    qpos0 = int(p[0].item()) if t else 0
-    kpos0 = qpos0 - (n_ext - t)
+    # the positions are device tensors: their first value and the layout check come back in one read
     ar = torch.arange(max(t, n_ext), device=p.device, dtype=torch.int64)
-    expect = kpos0 + ar[:n_ext]
-    e = ext_pos.to(torch.int64)
-    bad = (t and bool((p != qpos0 + ar[:t]).any().item())) or \
-        bool(((e != expect) & (expect >= self.sinks)).any().item())
+    q0 = p[:1] if t else torch.zeros(1, dtype=torch.int64, device=p.device)
+    expect = q0 - (n_ext - t) + ar[:n_ext]
+    bad = ((ext_pos.to(torch.int64) != expect) & (expect >= self.sinks)).any()
+    if t:
+        bad = bad | (p != q0 + ar[:t]).any()
+    qpos0, bad = torch.stack((q0[0], bad.to(torch.int64))).tolist()
+    kpos0 = qpos0 - (n_ext - t)
     if bad:
         raise NotImplementedError("heimdall_b200 window: key/query positions must be contiguous "
                                   "(ring in time order followed by the new tokens)")
     if sink_k is not None and sink_k.shape[2] == 0:
         sink_k = sink_v = None
     return F_.window_attention(qr, ext_k, ext_v, qpos0, kpos0, self.sinks, self.window, sink_k, sink_v)
+
+
+def window_attention(a, qr, kr, v):
+    """heimdall.motor.window_attention (motor.py:105-115): the window and sinks of a whole sequence from an empty
+    ring (positions 0 .. t-1), the cache-free path of HybridAttention._student.  Returns o [B,t,H,D], lse [B,H,t].
+
+    The reference prepends W empty ring rows (position -1) and calls ``_window``; here the keys are the
+    sequence itself from position 0, which the kernels take directly (no host read of the positions, no
+    concatenated copies)."""
+    _require_cuda(qr, kr, v)
+    t = qr.shape[2]
+    n = min(a.sinks, t)
+    vt = v.transpose(1, 2)
+    sk = kr[:, :, :n] if n else None
+    sv = vt[:, :, :n] if n else None
+    return F_.window_attention(qr, kr, vt, 0, 0, a.sinks, a.window, sk, sv)
 
 
 # ---------------------------------------------------------------------------------------------- install
@@ -147,6 +166,7 @@ def install(modules=None) -> None:
     hibrit, motor = m["hibrit"], m["motor"]
     try:
         _patch(motor, "delta_rule_gqa", delta_rule_gqa)
+        _patch(motor, "window_attention", window_attention)
         cls = hibrit.HybridAttention
         _patch(cls, "_student", _student)
         _patch(cls, "_mem_inputs", _mem_inputs)

@@ -75,6 +75,20 @@ def test_prepare_installs_and_routes_every_entry_point():
         o_r, lse_r = ob.window_attention(f(qr), f(ext_k), f(ext_v), ext_pos, f(kr[:, :, :S]), f(vt[:, :, :S]), pos,
                                          W, S)
         assert ob.rel_l2(o.cpu(), o_r) < O_TOL and (lse.cpu() - lse_r).abs().max() < 1e-3
+        # motor.window_attention itself (patched: the sequence's own keys from position 0, no host read)
+        o2, lse2 = m["motor"].window_attention(attn, cu(qr), cu(kr), cu(v))
+        assert ob.rel_l2(o2.cpu(), o_r) < O_TOL and (lse2.cpu() - lse_r).abs().max() < 1e-3
+        # _window at a later start (ring of earlier positions, then the new tokens)
+        st = 1000
+        pos2 = torch.arange(st, st + T)
+        ext_pos2 = torch.cat((torch.arange(st - W, st), pos2))
+        ext_k2 = torch.cat((bf(rms(torch.randn(1, G, W, D, generator=gen))), kr), 2)
+        ext_v2 = torch.cat((bf(rms(torch.randn(1, G, W, D, generator=gen))), vt), 2)
+        o, lse = cls._window(attn, cu(qr), cu(ext_k2), cu(ext_v2), cu(ext_pos2), cu(kr[:, :, :S]), cu(vt[:, :, :S]),
+                             cu(pos2))
+        o_r, lse_r = ob.window_attention(f(qr), f(ext_k2), f(ext_v2), ext_pos2, f(kr[:, :, :S]), f(vt[:, :, :S]),
+                                         pos2, W, S)
+        assert ob.rel_l2(o.cpu(), o_r) < O_TOL and (lse.cpu() - lse_r).abs().max() < 1e-3
         bad = ext_pos.clone()
         bad[W + 5] = -1               # a hole inside the window: not the contiguous form
         with pytest.raises(NotImplementedError):

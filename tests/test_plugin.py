@@ -24,7 +24,7 @@ def fake_modules():
         _student = _window = _mem_inputs = orig
     hibrit.HybridAttention = HybridAttention
     motor = types.ModuleType("heimdall.motor")
-    motor.delta_rule_gqa = orig
+    motor.delta_rule_gqa = motor.window_attention = orig
     return {"kernels": kernels, "hibrit": hibrit, "motor": motor}, orig
 
 
@@ -38,6 +38,7 @@ def test_install_patches_and_uninstall_restores():
         assert m["kernels"].delta_rule is orig and m["kernels"].delta_rule_step is orig
         assert m["hibrit"].delta_rule is orig and m["hibrit"].delta_rule_step is orig
         assert m["motor"].delta_rule_gqa is plugin.delta_rule_gqa
+        assert m["motor"].window_attention is plugin.window_attention
         cls = m["hibrit"].HybridAttention
         assert cls._student is plugin._student and cls._window is plugin._window
         assert cls._mem_inputs is plugin._mem_inputs

@@ -35,6 +35,7 @@ def _names(m):
             ("kernels", "delta_rule_step"): m["kernels"].delta_rule_step,
             ("hibrit", "delta_rule"): hb.delta_rule, ("hibrit", "delta_rule_step"): hb.delta_rule_step,
             ("motor", "delta_rule_gqa"): m["motor"].delta_rule_gqa,
+            ("motor", "window_attention"): m["motor"].window_attention,
             ("hibrit", "HybridAttention._student"): A.__dict__["_student"],
             ("hibrit", "HybridAttention._mem_inputs"): A.__dict__["_mem_inputs"],
             ("hibrit", "HybridAttention._window"): A.__dict__["_window"]}
