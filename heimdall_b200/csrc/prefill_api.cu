@@ -170,8 +170,7 @@ size_t bf_window_workspace(int B, int G, int Tk, int D) {
 static int window_common(const void* qr, const void* k_ext, const __half* vt, const void* sink_k, const void* sink_v,
                          int ns, long long qpos0, long long kpos0, long long klo, int B, int H, int G, int Tq, int Tk,
                          int window, float* o, float* lse, unsigned int* err, cudaStream_t stream,
-                         __half* o_perm = nullptr, int perm_tile0 = 0, int perm_nch = 0, int persistent = 1,
-                         int qt0 = 0, int nqt = 0) {
+                         __half* o_perm = nullptr, int perm_tile0 = 0, int perm_nch = 0, int qt0 = 0, int nqt = 0) {
   WinPreArgs a{};
   a.B = B; a.H = H; a.G = G; a.Tq = Tq; a.Tk = Tk; a.Tkp = ((Tk + 63) / 64) * 64; a.W = window;
   a.qpos0 = qpos0; a.kpos0 = kpos0; a.klo = klo;
@@ -181,7 +180,7 @@ static int window_common(const void* qr, const void* k_ext, const __half* vt, co
   a.sk_b = (long long)G * ns * 256; a.sk_h = (long long)ns * 256; a.sk_k = 256;
   a.sv_b = a.sk_b; a.sv_h = a.sk_h; a.sv_k = 256;
   a.o = o; a.lse = lse;
-  a.o_perm = o_perm; a.perm_tile0 = perm_tile0; a.perm_nch = perm_nch; a.persistent = persistent;
+  a.o_perm = o_perm; a.perm_tile0 = perm_tile0; a.perm_nch = perm_nch;
   a.qt0 = qt0; a.nqt = nqt;
   a.err = err;
   return launch_window_prefill(qr, k_ext, vt, a, stream);
@@ -459,7 +458,7 @@ static int layer_prefill_impl(const bf_layer* L, const void* x, const void* q, c
     n_pieces = n_pieces < 1 ? 1 : (n_pieces > kWinPieces ? kWinPieces : n_pieces);
     if (n_pieces == 1) {
       rc = window_common(qr, kx, vt, sink_k, sink_v, ns, start, kpos0, L->sinks, B, H, G, T, Tk, W, o, lse_w, st.err,
-                         ws2, owp, ptile0, s.n_chunks, will_read ? 0 : 1);
+                         ws2, owp, ptile0, s.n_chunks);
       if (rc) return rc;
     } else {
       // the second least-priority stream starts after the V^T staging on ws2
@@ -477,7 +476,7 @@ static int layer_prefill_impl(const bf_layer* L, const void* x, const void* q, c
         cudaStream_t sk = (k & 1) ? ws3 : ws2;
         if (te > tb) {
           rc = window_common(qr, kx, vt, sink_k, sink_v, ns, start, kpos0, L->sinks, B, H, G, T, Tk, W, o, lse_w,
-                             st.err, sk, owp, ptile0, s.n_chunks, 0, tb, te - tb);
+                             st.err, sk, owp, ptile0, s.n_chunks, tb, te - tb);
           if (rc) return rc;
         }
         if (cudaEventCreateWithFlags(&evs.piece[k], cudaEventDisableTiming) != cudaSuccess ||

@@ -38,7 +38,11 @@ namespace bfb {
 constexpr int kWP_M = 128;       // queries per tile
 constexpr int kWP_N = 128;       // keys per tile
 constexpr int kWP_D = 256;
-constexpr int kWP_Threads = 384;
+constexpr int kWP_Threads = 512;
+// register split (setmaxnreg) of the 128 per thread at launch: warpgroup 0 (loaders, MMA issue) 96, the two
+// softmax warpgroups 168, the epilogue warpgroup 80 (128 x 96 + 256 x 168 + 128 x 80 = 512 x 128)
+constexpr uint32_t kWP_RegsCtl = 96, kWP_RegsSoftmax = 168, kWP_RegsEpi = 80;
+static_assert(128 * kWP_RegsCtl + 256 * kWP_RegsSoftmax + 128 * kWP_RegsEpi == kWP_Threads * 128, "register split");
 constexpr int kWP_MaxSinks = 8;
 constexpr int kWP_SinkRows = 16;                  // sink keys padded to the smallest MMA N
 constexpr int kWP_SmemQ = kWP_M * kWP_D * 2;      // 64 KB
@@ -47,7 +51,7 @@ constexpr int kWP_SmemV = kWP_D * kWP_N * 2;      // 64 KB
 constexpr int kWP_SmemSK = kWP_SinkRows * kWP_D * 2;      // 8 KB: sink keys, K-major 128-byte swizzle
 constexpr int kWP_SmemSV = kWP_D * kWP_SinkRows * 2;     // 8 KB: sink values^T fp16 [256][16], no swizzle
 constexpr int kWP_Tiles = kWP_SmemQ + kWP_SmemK + kWP_SmemV + kWP_SmemSK + kWP_SmemSV;
-constexpr int kWP_Smem = kWP_Tiles + 256 + 4096 + 1024;   // + barriers + row exchanges (3 KB) + alignment
+constexpr int kWP_Smem = kWP_Tiles + 256 + 5120 + 1024;   // + barriers + row exchanges (5 KB) + alignment
 constexpr float kRescaleLog2 = 8.0f;              // rescale O when the max grows by more than 2^8
 constexpr uint32_t kTmO = 256;                    // TMEM column of O
 
@@ -82,7 +86,7 @@ __device__ __forceinline__ uint64_t sdesc_sinkv(uint32_t smem_addr) {
   return d;
 }
 
-// one work item of the persistent kernel
+// one work item: (b, query tile, query head); a CTA runs the R items of one (b, query tile, KV group) group
 struct WItem {
   int b, h, g, i0, qt;
   long long P0, Plast;
@@ -116,6 +120,11 @@ __device__ __forceinline__ WItem win_item(const WinPreArgs& a, long long u, int 
   return it;
 }
 
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_inc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N)); }
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_dec() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N)); }
+
 __global__ void __launch_bounds__(kWP_Threads, 1)
     window_prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                           const __grid_constant__ CUtensorMap vmap, WinPreArgs a) {
@@ -135,25 +144,49 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
   uint64_t* v_empty = bars + 5;    // O += P_t V_t finished (V free, O stable)
   uint64_t* s_full = bars + 6;     // [2]
   uint64_t* p_full = bars + 8;     // [2] P_t in TMEM (one arrival per softmax warp)
-  uint64_t* bar_sk = bars + 10;    // sink keys staged (one arrival per softmax warp, per item)
+  uint64_t* bar_sk = bars + 10;    // sink keys and values staged (one arrival per softmax warp, once)
   uint64_t* bar_sink = bars + 11;  // the item's sink scores in TMEM (per item, with sinks)
   uint64_t* o_fin = bars + 12;     // the item's O is complete (per item)
-  uint64_t* o_free = bars + 13;    // O drained by the epilogue (one arrival per softmax warp, per item)
-  uint64_t* psink = bars + 14;     // sink scores read and P_sink staged (one arrival per softmax warp, per item)
-  uint64_t* osink = bars + 15;     // O = P_sink V_sink finished (per item, with sinks)
+  uint64_t* o_free = bars + 13;    // O drained by the epilogue (one arrival per epilogue warp, per item)
+  uint64_t* psink = bars + 14;     // P_sink staged (one arrival per half-0 softmax warp, per item, with sinks)
+  uint64_t* sread = bars + 15;     // the sink scores read (one arrival per softmax warp, per item, with sinks)
   uint64_t* pair = bars + 16;      // [4] sync of the two softmax warps on a lane quarter (one arrival per warp)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 21);
-  // row exchange: [2 tile parities][2 halves][128] running maxima, then [2 halves][128] final sums
+  // per stats slot (item parity): the slot's row sums and max written (one arrival per softmax warp) / read by
+  // the epilogue (one arrival per epilogue warp); one barrier pair per slot, so neither side runs two uses ahead
+  uint64_t* stats = bars + 20;     // [2]
+  uint64_t* sfree = bars + 22;     // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 24);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 25);
+  // [2 tile parities][2 halves][128] running maxima; [2 item slots][2 halves][128] row sums; [2 slots][128] max
   float* xch = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);
+  float* xl = xch + 512;
+  float* xmx = xl + 512;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int ntq = a.nqt > 0 ? a.nqt : (a.Tq + kWP_M - 1) / kWP_M;   // query tiles of this launch
-  const long long nitems = (long long)a.B * ntq * a.H;
+  const int R = a.H / a.G;
+  const long long u0 = (long long)blockIdx.x * R;                   // this CTA's items u0 .. u0 + R - 1
   const int ns = a.ns;
 
   if (tid == 0) {
-    for (int i = 0; i < 16; ++i) mbar_init(bars + i, (i == 8 || i == 9 || i == 10 || i == 13 || i == 14) ? 8 : 1);
+    mbar_init(bar_q, 1);
+    mbar_init(q_free, 1);
+    mbar_init(k_full, 1);
+    mbar_init(k_empty, 1);
+    mbar_init(v_full, 1);
+    mbar_init(v_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 8);
+      mbar_init(&sfree[i], 4);
+      mbar_init(&stats[i], 8);
+    }
+    mbar_init(bar_sk, 8);
+    mbar_init(bar_sink, 1);
+    mbar_init(o_fin, 1);
+    mbar_init(o_free, 4);
+    mbar_init(psink, 4);
+    mbar_init(sread, 8);
     for (int i = 0; i < 4; ++i) mbar_init(pair + i, 2);
     *abort_flag = 0;
     fence_barrier_init();
@@ -167,45 +200,40 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    // ---------------------------------------------------------------- Q and K tiles
-    if (lane == 0) {
+  if (warp < 4) {
+    setmaxnreg_dec<kWP_RegsCtl>();
+    if (warp == 0 && lane == 0) {
+      // ---------------------------------------------------------------- Q and K tiles
       tma_prefetch(&qmap);
       tma_prefetch(&kmap);
-      int it = 0, t = 0;
+      int t = 0;
       bool ok = true;
-      for (long long u = blockIdx.x; u < nitems && ok; u += gridDim.x, ++it) {
-        const WItem w = win_item(a, u, ntq);
+      for (int it = 0; it < R && ok; ++it) {
+        const WItem w = win_item(a, u0 + it, ntq);
         // Q of the previous item is free once its last score product (or sink product) has finished
         if (it >= 1 && !(ok = mbar_wait(q_free, (it - 1) & 1, abort_flag, a.err, 0x30))) break;
         mbar_expect_tx(bar_q, kWP_SmemQ);
         tma_load_3d(sQ, &qmap, bar_q, 0, (w.b * a.H + w.h) * a.Tq + w.i0, 0);
+        if (it + 1 < R) {   // the next head's queries into L2 behind this one's
+          const WItem wn = win_item(a, u0 + it + 1, ntq);
+          tma_prefetch_tile_3d(&qmap, 0, (wn.b * a.H + wn.h) * a.Tq + wn.i0, 0);
+        }
         for (int j = 0; j < w.n; ++j, ++t) {
           if (t >= 1 && !(ok = mbar_wait(k_empty, (t - 1) & 1, abort_flag, a.err, 0x31))) break;
           mbar_expect_tx(k_full, kWP_SmemK);
           tma_load_3d(sK, &kmap, k_full, 0, (w.b * a.G + w.g) * a.Tk + (w.jt0 + j) * kWP_N, 0);
-          // one item per CTA: behind this item's first loads, the item about one wave of CTAs later
-          // (pf_stride = the SM count) gets its queries and first key tile into L2, so that they arrive from L2
-          // when its CTA starts
-          if (j == 0 && a.pf_stride && u + a.pf_stride < nitems) {
-            const WItem wn = win_item(a, u + a.pf_stride, ntq);
-            tma_prefetch_tile_3d(&qmap, 0, (wn.b * a.H + wn.h) * a.Tq + wn.i0, 0);
-            if (wn.n > 0) tma_prefetch_tile_3d(&kmap, 0, (wn.b * a.G + wn.g) * a.Tk + wn.jt0 * kWP_N, 0);
-          }
         }
       }
       // drain: every load issued has landed before the CTA may exit
-      if (it > 0) mbar_wait(bar_q, (it - 1) & 1, nullptr, a.err, 0x32);
+      mbar_wait(bar_q, (R - 1) & 1, nullptr, a.err, 0x32);
       if (t > 0) mbar_wait(k_full, (t - 1) & 1, nullptr, a.err, 0x33);
-    }
-  } else if (warp == 2) {
-    // ---------------------------------------------------------------- V^T tiles
-    if (lane == 0) {
+    } else if (warp == 2 && lane == 0) {
+      // ---------------------------------------------------------------- V^T tiles
       tma_prefetch(&vmap);
       int t = 0;
       bool ok = true;
-      for (long long u = blockIdx.x; u < nitems && ok; u += gridDim.x) {
-        const WItem w = win_item(a, u, ntq);
+      for (int it = 0; it < R && ok; ++it) {
+        const WItem w = win_item(a, u0 + it, ntq);
         for (int j = 0; j < w.n; ++j, ++t) {
           if (t >= 1 && !(ok = mbar_wait(v_empty, (t - 1) & 1, abort_flag, a.err, 0x34))) break;
           mbar_expect_tx(v_full, kWP_SmemV);
@@ -213,88 +241,80 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
         }
       }
       if (t > 0) mbar_wait(v_full, (t - 1) & 1, nullptr, a.err, 0x35);
-    }
-  } else if (warp == 1) {
-    // ---------------------------------------------------------------- MMA issue
-    if (lane == 0) {
+    } else if (warp == 1 && lane == 0) {
+      // ---------------------------------------------------------------- MMA issue
       constexpr uint32_t idesc_qk = idesc_f16(kWP_M, kWP_N, 1);
       constexpr uint32_t idesc_sk = idesc_f16(kWP_M, kWP_SinkRows, 1);
       constexpr uint32_t idesc_pv = idesc_f16(kWP_M, kWP_D, 0);
       const uint32_t aQ = smem_u32(sQ), bK = smem_u32(sK), bV = smem_u32(sV), bSK = smem_u32(sSK);
       const uint64_t dSV = sdesc_sinkv(smem_u32(sSV));
-      int it = 0, t = 0;
+      int t = 0;
       bool ok = true;
-      for (long long u = blockIdx.x; u < nitems && ok; u += gridDim.x, ++it) {
-        const WItem w = win_item(a, u, ntq);
-        ok = mbar_wait(bar_q, it & 1, abort_flag, a.err, 0x36);
-        if (!ok) break;
-        // the S buffer of the item's second tile holds the sink scores (columns 0..15) and P_sink (16..23) until
-        // that tile's product; its previous P was read by a product issued before this item's
+      for (int it = 0; it < R && ok; ++it) {
+        const WItem w = win_item(a, u0 + it, ntq);
+        if (!(ok = mbar_wait(bar_q, it & 1, abort_flag, a.err, 0x36))) break;
+        // sink scores into columns 0..15 of the S buffer of the item's second tile (its earlier contents were read
+        // by products issued before this one); the softmax warps read them before that buffer is written again
         const uint32_t sb = tmem + (uint32_t)((t + 1) & 1) * kWP_N;
-        auto sink_scores = [&]() -> bool {
-          if (ns == 0) return true;
-          if (!mbar_wait(bar_sk, it & 1, abort_flag, a.err, 0x3c)) return false;
+        if (ns > 0) {
+          if (it == 0 && !(ok = mbar_wait(bar_sk, 0, abort_flag, a.err, 0x3c))) break;
           tc_fence_after();
 #pragma unroll
           for (int ks = 0; ks < kWP_D / 16; ++ks)
             umma_f16_ss(sb, sdesc_kstep(aQ, kWP_M, ks), sdesc_kstep(bSK, kWP_SinkRows, ks), idesc_sk, ks > 0);
           umma_commit(bar_sink);
-          return true;
-        };
-        // O is free once the previous item is drained; with sinks it starts as P_sink V_sink
-        auto sink_pv = [&]() -> bool {
-          if (it >= 1 && !mbar_wait(o_free, (it - 1) & 1, abort_flag, a.err, 0x3f)) return false;
-          if (ns == 0) return true;
-          if (!mbar_wait(psink, it & 1, abort_flag, a.err, 0x44)) return false;
-          tc_fence_after();
-          umma_f16_ts(tmem + kTmO, sb + 16, dSV, idesc_pv, 0u);
-          umma_commit(osink);
-          return true;
-        };
+        }
+        // O += P_jj V_jj; the item's first product into O waits until the previous item's O is drained
         auto issue_pv = [&](int jj, int tt) -> bool {
           const int s = tt & 1;
           if (!mbar_wait(&p_full[s], (tt >> 1) & 1, abort_flag, a.err, 0x37)) return false;
           if (!mbar_wait(v_full, tt & 1, abort_flag, a.err, 0x38)) return false;
+          if (jj == 0 && it >= 1 && !mbar_wait(o_free, (it - 1) & 1, abort_flag, a.err, 0x3f)) return false;
           tc_fence_after();
 #pragma unroll
           for (int ks = 0; ks < kWP_N / 16; ++ks)
             umma_f16_ts(tmem + kTmO, tmem + s * kWP_N + p_col(ks), sdesc_kstep(bV, kWP_D, ks), idesc_pv,
-                        (ns > 0 || (jj | ks) > 0) ? 1u : 0u);
+                        (jj | ks) > 0 ? 1u : 0u);
           umma_commit(v_empty);
-          if (jj == w.n - 1) umma_commit(o_fin);
           return true;
         };
-        if (w.n == 0) {   // no key tiles: O is P_sink V_sink (or zero); o_fin still marks the item once
-          ok = sink_scores() && sink_pv();
-          if (ok) {
-            umma_commit(q_free);
-            umma_commit(o_fin);
-          }
-        }
-        // the sink scores need only the queries and the staged sink keys: issued before the first key tile has
-        // landed, so the softmax warps form P_sink while it loads (the S buffer they use was last read by a
-        // product issued before this point)
-        if (w.n > 0) ok = sink_scores();
         for (int j = 0; j < w.n && ok; ++j) {
           const int tt = t + j, s = tt & 1;
-          ok = mbar_wait(k_full, tt & 1, abort_flag, a.err, 0x39);
-          if (!ok) break;
+          if (!(ok = mbar_wait(k_full, tt & 1, abort_flag, a.err, 0x39))) break;
           tc_fence_after();
 #pragma unroll
           for (int ks = 0; ks < kWP_D / 16; ++ks)
             umma_f16_ss(tmem + s * kWP_N, sdesc_kstep(aQ, kWP_M, ks), sdesc_kstep(bK, kWP_N, ks), idesc_qk, ks > 0);
           umma_commit(k_empty);
           umma_commit(&s_full[s]);
-          if (j == 0) ok = sink_pv();
-          if (ok && j == w.n - 1) umma_commit(q_free);
-          if (ok && j >= 1) ok = issue_pv(j - 1, tt - 1);
+          if (j == w.n - 1) umma_commit(q_free);
+          // nothing writes the sink scores' buffer again before they are read
+          if (j == 0 && ns > 0 && !(ok = mbar_wait(sread, it & 1, abort_flag, a.err, 0x44))) break;
+          if (j >= 1 && !(ok = issue_pv(j - 1, tt - 1))) break;
         }
-        if (ok && w.n > 0) ok = issue_pv(w.n - 1, t + w.n - 1);
+        if (!ok) break;
+        if (w.n > 0) {
+          if (!(ok = issue_pv(w.n - 1, t + w.n - 1))) break;
+        } else {
+          if (ns > 0 && !(ok = mbar_wait(sread, it & 1, abort_flag, a.err, 0x44))) break;
+          umma_commit(q_free);
+        }
+        // the sinks' product closes the item: O += P_sink V_sink (the item's only product when it has no tiles).
+        // O of an item is complete only after the previous item's O was drained, even with no product at all
+        if (ns > 0 && !(ok = mbar_wait(psink, it & 1, abort_flag, a.err, 0x45))) break;
+        if (w.n == 0 && it >= 1 && !(ok = mbar_wait(o_free, (it - 1) & 1, abort_flag, a.err, 0x3f))) break;
+        if (ns > 0) {
+          tc_fence_after();
+          const uint32_t psb = (uint32_t)((w.n > 0 ? t + w.n - 1 : t + 1) & 1) * kWP_N;
+          umma_f16_ts(tmem + kTmO, tmem + psb + 32, dSV, idesc_pv, w.n > 0 ? 1u : 0u);
+        }
+        umma_commit(o_fin);
         t += w.n;
       }
     }
-  } else if (warp >= 4) {
-    // ------------------------------------------------------------------ softmax + epilogue (warps 4..11)
+  } else if (warp < 12) {
+    setmaxnreg_inc<kWP_RegsSoftmax>();
+    // ------------------------------------------------------------------ softmax (warps 4..11)
     const int q4 = warp & 3;
     const int hh = (warp - 4) >> 2;
     const int r = q4 * 32 + lane;                // query row in the tile == TMEM lane
@@ -310,15 +330,10 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
       ++pair_phase;
       return ok;
     };
-    bool alive = true;
-    int it = 0, t = 0;
-    for (long long u = blockIdx.x; u < nitems && alive; u += gridDim.x, ++it) {
-      const WItem w = win_item(a, u, ntq);
-      const long long p = w.P0 + r;              // position of this query
-      const uint32_t sbc = (uint32_t)((t + 1) & 1) * kWP_N;   // S buffer of the sink scores and P_sink
-      // sink keys -> K-major swizzled B operand (rows >= ns zero); sink values^T -> fp16 B operand (keys >= ns
-      // zero).  The previous item's sink products finished before its O was complete.  Every load is issued
-      // before the first store, so the staging costs one round trip to L2
+    // sink keys -> K-major swizzled B operand (rows >= ns zero); sink values^T -> fp16 B operand (keys >= ns
+    // zero): once per CTA, as all its items share (b, g).  Every load is issued before the first store
+    {
+      const WItem w = win_item(a, u0, ntq);
       static_assert(kWP_SinkRows * (kWP_D / 8) == 2 * 256, "two 16-byte sink-key chunks per thread");
       uint4 skc[2];
 #pragma unroll
@@ -339,46 +354,46 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
         const int i = st + q * 256, e = i / (kWP_D / 8), c = i % (kWP_D / 8);
         *reinterpret_cast<uint4*>(sSK + (c >> 3) * (kWP_SinkRows * 128) + e * 128 + (((c & 7) ^ (e & 7)) << 4)) = skc[q];
       }
-      if (ns > 0) {
-        uint32_t hv[8];
+      uint32_t hv[8];
 #pragma unroll
-        for (int e2 = 0; e2 < 8; ++e2) hv[e2] = pack_half2(svl[2 * e2], svl[2 * e2 + 1]);
-        *reinterpret_cast<uint4*>(sSV + sv_off(st, 0)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-        *reinterpret_cast<uint4*>(sSV + sv_off(st, 8)) = make_uint4(hv[4], hv[5], hv[6], hv[7]);
-      }
+      for (int e2 = 0; e2 < 8; ++e2) hv[e2] = pack_half2(svl[2 * e2], svl[2 * e2 + 1]);
+      *reinterpret_cast<uint4*>(sSV + sv_off(st, 0)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+      *reinterpret_cast<uint4*>(sSV + sv_off(st, 8)) = make_uint4(hv[4], hv[5], hv[6], hv[7]);
       fence_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_sk);
+    }
+    bool alive = true;
+    int t = 0;
+    for (int it = 0; it < R && alive; ++it) {
+      const WItem w = win_item(a, u0 + it, ntq);
+      const long long p = w.P0 + r;              // position of this query
+      const uint32_t sbc = (uint32_t)((t + 1) & 1) * kWP_N;   // S buffer of the sink scores
       // sinks start the online softmax: m_ref = the row's largest visible sink score, l (half 0) = the sum of
-      // their weights, O = P_sink V_sink; half 0 stages P_sink beside the scores it read them from
+      // their weights; half 0 keeps the weights (rescaled with O) for the product that closes the item
       float m_ref = -INFINITY, l = 0.f;            // running max (log2 domain) and this half's sum
+      float wsk[kWP_MaxSinks];
+#pragma unroll
+      for (int e = 0; e < kWP_MaxSinks; ++e) wsk[e] = 0.f;
       if (ns > 0) {
         if (!(alive = mbar_wait_warp(bar_sink, it & 1, abort_flag, a.err, 0x3a))) break;
         tc_fence_after();
         uint32_t sw[16];
         tmem_ld16(trow + sbc, sw);
         tmem_wait_ld();
-        float se[kWP_SinkRows];
-#pragma unroll
-        for (int e = 0; e < kWP_SinkRows; ++e) {
-          se[e] = (e < ns && e <= p) ? __uint_as_float(sw[e]) * c2 : -INFINITY;
-          m_ref = fmaxf(m_ref, se[e]);
-        }
-        if (hh == 0) {
-          uint32_t pk8[8];
-#pragma unroll
-          for (int e = 0; e < kWP_SinkRows; e += 2) {
-            const float w0 = (se[e] == -INFINITY) ? 0.f : ex2_approx(se[e] - m_ref);
-            const float w1 = (se[e + 1] == -INFINITY) ? 0.f : ex2_approx(se[e + 1] - m_ref);
-            l += w0 + w1;
-            pk8[e / 2] = cvt_half2(w0, w1);
-          }
-          tmem_st8(trow + sbc + 16, pk8);
-          tmem_wait_st();
-        }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(psink);
+        if (lane == 0) mbar_arrive(sread);
+#pragma unroll
+        for (int e = 0; e < kWP_MaxSinks; ++e) {
+          wsk[e] = (e < ns && e <= p) ? __uint_as_float(sw[e]) * c2 : -INFINITY;
+          m_ref = fmaxf(m_ref, wsk[e]);
+        }
+#pragma unroll
+        for (int e = 0; e < kWP_MaxSinks; ++e) {
+          wsk[e] = (hh == 0 && wsk[e] != -INFINITY) ? ex2_approx(wsk[e] - m_ref) : 0.f;
+          l += wsk[e];
+        }
       }
 
       for (int j = 0; j < w.n && alive; ++j) {
@@ -424,12 +439,14 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
         float factor = 1.f;
         bool rescale = false;
         if (m_ref == -INFINITY) {
-          m_ref = mt;  // O holds nothing yet (or only zeros)
+          m_ref = mt;  // nothing accumulated yet
         } else if (mt > m_ref + kRescaleLog2) {
           factor = ex2_approx(m_ref - mt);
           rescale = true;
           m_ref = mt;
           l *= factor;
+#pragma unroll
+          for (int e = 0; e < kWP_MaxSinks; ++e) wsk[e] *= factor;
         }
         uint32_t pk[NH / 2];
         if (m_ref == -INFINITY) {
@@ -446,12 +463,11 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
           }
           l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
         }
-        // O rescale (warp-collective): after O += P_{t-1} V_{t-1} has finished (O += P_{t-2} V_{t-2} was
-        // issued before S_t, so this parity wait cannot pass early)
-        if (__any_sync(0xffffffffu, rescale)) {
-          // O += P_{t-1} V_{t-1} (or, at the item's first tile, O = P_sink V_sink) has finished
-          if (j >= 1 ? !mbar_wait_warp(v_empty, (tt - 1) & 1, abort_flag, a.err, 0x3e)
-                     : (ns > 0 && !mbar_wait_warp(osink, it & 1, abort_flag, a.err, 0x45))) {
+        // O rescale (warp-collective), from the item's second tile on: after O += P_{j-1} V_{j-1} has finished
+        // (O += P_{j-2} V_{j-2} was issued before S_j, so this parity wait cannot pass early); at the first tile
+        // the item has no O yet
+        if (j >= 1 && __any_sync(0xffffffffu, rescale)) {
+          if (!mbar_wait_warp(v_empty, (tt - 1) & 1, abort_flag, a.err, 0x3e)) {
             alive = false;
             break;
           }
@@ -474,25 +490,58 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
         if (lane == 0) mbar_arrive(&p_full[s]);
       }
       if (!alive) break;
+      // P_sink (half 0) beside the last P it wrote, or beside the sink scores when the item has no tiles
+      if (ns > 0 && hh == 0) {
+        const uint32_t psb = (uint32_t)((w.n > 0 ? t + w.n - 1 : t + 1) & 1) * kWP_N;
+        uint32_t pk8[8];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) pk8[e] = cvt_half2(wsk[2 * e], wsk[2 * e + 1]);
+#pragma unroll
+        for (int e = 4; e < 8; ++e) pk8[e] = 0u;
+        tmem_st8(trow + psb + 32, pk8);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(psink);
+      }
       t += w.n;
-      // ---------------------------------------------------------------- epilogue
+      // the row statistics for the epilogue (slot it & 1, free once the epilogue read item it - 2's)
+      const int slot = it & 1;
+      if (it >= 2 && !(alive = mbar_wait_warp(&sfree[slot], ((it >> 1) - 1) & 1, abort_flag, a.err, 0x46))) break;
+      xl[slot * 256 + hh * 128 + r] = l;
+      if (hh == 0) xmx[slot * 128 + r] = m_ref;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&stats[slot]);
+    }
+  } else {
+    setmaxnreg_dec<kWP_RegsEpi>();
+    // ------------------------------------------------------------------ epilogue (warps 12..15)
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;
+    const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
+    for (int it = 0; it < R; ++it) {
+      const WItem w = win_item(a, u0 + it, ntq);
       const bool has_o = w.n > 0 || ns > 0;
-      if (!(alive = mbar_wait_warp(o_fin, it & 1, abort_flag, a.err, 0x3d))) break;
+      if (!mbar_wait_warp(o_fin, it & 1, abort_flag, a.err, 0x3d)) break;
+      const int slot = it & 1;
+      if (!mbar_wait_warp(&stats[slot], (it >> 1) & 1, abort_flag, a.err, 0x43)) break;
+      const float l = xl[slot * 256 + r] + xl[slot * 256 + 128 + r];
+      const float m_ref = xmx[slot * 128 + r];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sfree[slot]);
       tc_fence_after();
-      xch[512 + hh * 128 + r] = l;
-      if (!(alive = pair_sync(0x43))) break;
-      l += xch[512 + (1 - hh) * 128 + r];
       const float inv = l > 0.f ? 1.f / l : 0.f;
       const float lse = l > 0.f ? (m_ref + log2f(l)) * kLn2 : -INFINITY;
       const int qi = w.i0 + r;
-      if (qi < a.Tq && a.lse && hh == 0) a.lse[((size_t)w.b * a.H + w.h) * a.Tq + qi] = lse;
+      if (qi < a.Tq && a.lse) a.lse[((size_t)w.b * a.H + w.h) * a.Tq + qi] = lse;
       // rows that the memory reads mix go to the workspace tile in their load order
       const int pcn = w.qt - a.perm_tile0;
       __half* const perm_dst = (a.o_perm && pcn >= 0 && pcn < a.perm_nch)
                                    ? a.o_perm + (((size_t)w.b * a.perm_nch + pcn) * a.H + w.h) * (size_t)(kWP_M * kWP_D)
                                    : nullptr;
 #pragma unroll 1
-      for (int c4 = 0; c4 < 4; ++c4) {
+      for (int c8 = 0; c8 < 8; ++c8) {
+        const int hh = c8 >> 2, c4 = c8 & 3;
         const int c = hh * 128 + c4 * 32;
         uint32_t ow[32];
         if (has_o) {
@@ -502,22 +551,20 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
 #pragma unroll
           for (int e = 0; e < 32; ++e) ow[e] = 0u;
         }
-        float ov[32];
-#pragma unroll
-        for (int e = 0; e < 32; ++e) ov[e] = __uint_as_float(ow[e]);
         if (perm_dst) {
           // 8-column group e8 of column block cb = c4 / 2 as fp16: [half][cb][row group][e8][row in group][8],
           // 512 contiguous bytes per warp store
           __half* dst = perm_dst + ((size_t)(((hh * 2 + (c4 >> 1)) * 4 + q4) * 8 + (c4 & 1) * 4) * 32 + lane) * 8;
 #pragma unroll
-          for (int k = 0; k < 4; ++k)
+          for (int k = 0; k < 4; ++k) {
+            const float* ov = reinterpret_cast<const float*>(ow) + 8 * k;
             *reinterpret_cast<uint4*>(dst + k * 256) =
-                make_uint4(cvt_half2(ov[8 * k] * inv, ov[8 * k + 1] * inv), cvt_half2(ov[8 * k + 2] * inv, ov[8 * k + 3] * inv),
-                           cvt_half2(ov[8 * k + 4] * inv, ov[8 * k + 5] * inv),
-                           cvt_half2(ov[8 * k + 6] * inv, ov[8 * k + 7] * inv));
+                make_uint4(cvt_half2(ov[0] * inv, ov[1] * inv), cvt_half2(ov[2] * inv, ov[3] * inv),
+                           cvt_half2(ov[4] * inv, ov[5] * inv), cvt_half2(ov[6] * inv, ov[7] * inv));
+          }
         } else {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) ow[e] = __float_as_uint(ov[e] * inv);
+          for (int e = 0; e < 32; ++e) ow[e] = __float_as_uint(__uint_as_float(ow[e]) * inv);
           tmem_st32(trow + kTmO + c, ow);
         }
       }
@@ -528,16 +575,15 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
 #pragma unroll 1
         for (int sg = 0; sg < 2; ++sg) {
 #pragma unroll 1
-          for (int c64 = 0; c64 < 2; ++c64) {
+          for (int c64 = 0; c64 < 4; ++c64) {
             uint32_t v[32];
-            tmem_ld_16x256b_x8(tmem + ((uint32_t)(q4 * 32 + sg * 16) << 16) + kTmO + hh * 128 + c64 * 64, v);
+            tmem_ld_16x256b_x8(tmem + ((uint32_t)(q4 * 32 + sg * 16) << 16) + kTmO + c64 * 64, v);
             tmem_wait_ld();
 #pragma unroll
             for (int hf = 0; hf < 2; ++hf) {
               const int row = q4 * 32 + sg * 16 + hf * 8 + (lane >> 2);
               if (w.i0 + row < a.Tq) {
-                float* op = a.o + (((size_t)w.b * a.Tq + w.i0 + row) * a.H + w.h) * kWP_D + hh * 128 + c64 * 64 +
-                            2 * (lane & 3);
+                float* op = a.o + (((size_t)w.b * a.Tq + w.i0 + row) * a.H + w.h) * kWP_D + c64 * 64 + 2 * (lane & 3);
 #pragma unroll
                 for (int k = 0; k < 8; ++k)
                   *reinterpret_cast<float2*>(op + 8 * k) =
@@ -561,49 +607,50 @@ __global__ void __launch_bounds__(kWP_Threads, 1)
 }
 
 // V (time-major [B,T,G,D] bf16, optionally preceded by a ring [B,G,W,D] read in time order) ->
-// V^T fp16 [B,G,D,Tkp], keys beyond Tk zero.  One CTA = 64 keys x 256 columns of one (b, g).
+// V^T fp16 [B,G,D,Tkp], keys beyond Tk zero.  One CTA = 64 keys x 256 columns of one (b, g): lane kp of every
+// warp holds the key pair (2 kp, 2 kp + 1), warp w the 8-column chunks w, w + 8, w + 16, w + 24 (all eight
+// 16-byte loads in flight); the fp16 pairs go through shared memory as [column][key pair] words (odd row pitch:
+// conflict-free both ways) and leave as one 128-byte row segment per warp store.
 __global__ void __launch_bounds__(256) vt_prep_kernel(const __nv_bfloat16* __restrict__ v, long long vb, long long vg,
                                                       long long vj, const __nv_bfloat16* __restrict__ ring_v, int nring,
                                                       long long ring_pos0, int W, int G, int Tk, int Tkp,
                                                       __half* __restrict__ vt) {
-  __shared__ __half tile[64][256 + 8];
+  __shared__ uint32_t tile[256][33];
   const int jb = blockIdx.x * 64, bg = blockIdx.y, b = bg / G, g = bg % G;
-  const int t = threadIdx.x;
-  // load 64 key rows (8 threads per row, 32 columns each)
-  for (int rr = t >> 3; rr < 64; rr += 32) {
-    const int j = jb + rr;
-    const int c0 = (t & 7) * 32;
-    const __nv_bfloat16* src = nullptr;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  auto row_src = [&](int j) -> const __nv_bfloat16* {
     if (j < nring) {
       const long long kp = ring_pos0 + j;
       const int slot = (int)(((kp % W) + W) % W);
-      src = ring_v + (((size_t)b * G + g) * W + slot) * 256 + c0;
-    } else if (j < Tk) {
-      src = v + (size_t)b * vb + (size_t)g * vg + (size_t)(j - nring) * vj + c0;
+      return ring_v + (((size_t)b * G + g) * W + slot) * 256;
     }
+    if (j < Tk) return v + (size_t)b * vb + (size_t)g * vg + (size_t)(j - nring) * vj;
+    return nullptr;
+  };
+  const __nv_bfloat16* s0 = row_src(jb + 2 * lane);
+  const __nv_bfloat16* s1 = row_src(jb + 2 * lane + 1);
+  uint4 r0[4], r1[4];
 #pragma unroll
-    for (int c = 0; c < 32; c += 8) {
-      uint4 u = src ? *reinterpret_cast<const uint4*>(src + c) : make_uint4(0, 0, 0, 0);
-      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+  for (int q = 0; q < 4; ++q) {
+    const int c = (warp + 8 * q) * 8;
+    r0[q] = s0 ? __ldg(reinterpret_cast<const uint4*>(s0 + c)) : make_uint4(0u, 0u, 0u, 0u);
+    r1[q] = s1 ? __ldg(reinterpret_cast<const uint4*>(s1 + c)) : make_uint4(0u, 0u, 0u, 0u);
+  }
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        tile[rr][c0 + c + 2 * e] = __float2half_rn(__uint_as_float(w[e] << 16));
-        tile[rr][c0 + c + 2 * e + 1] = __float2half_rn(__uint_as_float(w[e] & 0xffff0000u));
-      }
+  for (int q = 0; q < 4; ++q) {
+    const int c = (warp + 8 * q) * 8;
+    const uint32_t a0[4] = {r0[q].x, r0[q].y, r0[q].z, r0[q].w}, a1[4] = {r1[q].x, r1[q].y, r1[q].z, r1[q].w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      // columns c + 2e (low halves) and c + 2e + 1 (high halves) of keys 2 lane and 2 lane + 1
+      tile[c + 2 * e][lane] = pack_half2(__uint_as_float(a0[e] << 16), __uint_as_float(a1[e] << 16));
+      tile[c + 2 * e + 1][lane] = pack_half2(__uint_as_float(a0[e] & 0xffff0000u), __uint_as_float(a1[e] & 0xffff0000u));
     }
   }
   __syncthreads();
-  // write 256 rows (columns of V) x 64 keys: each thread one column, 64 keys = 128 bytes
-  const int d = t;
-  __half* dst = vt + (((size_t)b * G + g) * 256 + d) * Tkp + jb;
-  uint32_t w[32];
-#pragma unroll
-  for (int e = 0; e < 32; ++e) {
-    __half2 h2 = __halves2half2(tile[2 * e][d], tile[2 * e + 1][d]);
-    w[e] = *reinterpret_cast<uint32_t*>(&h2);
-  }
-#pragma unroll
-  for (int e = 0; e < 32; e += 4) *reinterpret_cast<uint4*>(dst + 2 * e) = make_uint4(w[e], w[e + 1], w[e + 2], w[e + 3]);
+  __half* dst = vt + ((size_t)b * G + g) * 256 * (size_t)Tkp + jb + 2 * lane;
+#pragma unroll 8
+  for (int d = warp; d < 256; d += 8) *reinterpret_cast<uint32_t*>(dst + (size_t)d * Tkp) = tile[d][lane];
 }
 
 // K of the extended sequence: ring (time order) then kr [B,G,T,D] -> kext [B,G,W+T,D] (only with a ring)
@@ -650,11 +697,10 @@ int launch_window_prefill(const void* qr, const void* kext, const __half* vt, Wi
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
     return cuda_fail();
-  const long long nitems = (long long)a.B * (a.nqt > 0 ? a.nqt : (a.Tq + kWP_M - 1) / kWP_M) * a.H;
-  if (nitems == 0) return BF_OK;
-  const long long grid = a.persistent ? (nitems < sms ? nitems : sms) : nitems;
-  a.pf_stride = a.persistent ? 0 : sms;
-  window_prefill_kernel<<<(unsigned)grid, kWP_Threads, kWP_Smem, stream>>>(qmap, kmap, vmap, a);
+  // one CTA per (b, query tile, KV group): its R query heads run back to back in the CTA
+  const long long ngroups = (long long)a.B * (a.nqt > 0 ? a.nqt : (a.Tq + kWP_M - 1) / kWP_M) * a.G;
+  if (ngroups == 0) return BF_OK;
+  window_prefill_kernel<<<(unsigned)ngroups, kWP_Threads, kWP_Smem, stream>>>(qmap, kmap, vmap, a);
   return launch_status();
 }
 

@@ -28,12 +28,8 @@ struct WinPreArgs {
   // memory-read epilogue loads it: [value half][64-column block][32-row group][8-column group][row in group][8]
   __half* o_perm;
   int perm_tile0, perm_nch;
-  // launch: one CTA per SM walking the items (fastest alone), or one CTA per item (lets concurrent kernels on
-  // other streams take SMs as CTAs finish: the layer prefill, where the memory chain runs beside the window)
   // query tiles qt0 .. qt0 + nqt - 1 only (nqt = 0: all tiles); items of other tiles are not this launch's
   int qt0, nqt;
-  int persistent;
-  int pf_stride;        // set by the launcher: one item per CTA prefetches item + pf_stride into L2 (0: none)
   unsigned int* err;
 };
 
