@@ -20,7 +20,8 @@ sample), ``e2e`` (the headline through the public API from pinned host buffers, 
 region), ``sp_131k`` (N > 1: a per-rank timeline of one step and an in-bench parity check against one prefill
 of the whole sequence on one GPU), ``sp_1m`` (config 3 at T = 1048576, same), ``decode`` (64
 sequences x 12 layers, sharded over the N GPUs), ``delta_rule`` (configs 0 and 4: the chunked delta-rule op),
-``interchange`` (N = 1: the llama.cpp state rows of config 2's decode cache, packed and unpacked), ``clocks``
+``interchange`` (N = 1: the llama.cpp state rows of config 2's decode cache, packed and unpacked),
+``retrieval`` (N = 1: a kept full-attention layer's retrieval decode at 128K context), ``clocks``
 (nvidia-smi samples during the timed region) and ``gpu_launches``.
 """
 from __future__ import annotations
@@ -564,6 +565,41 @@ def run_decode(device, ctx, steps=256, warmup=8, nseq=64, nlayers=12):
                               "frac": per_layer_bytes * nlayers / (us_step * 1e-6) / 1e9 / pk["hbm_gbs"]}}
 
 
+def run_retrieval(device, nseq=16, n=131072, steps=20, warmup=3):
+    """Retrieval decode of a kept full-attention layer (HybridAttention._teacher with set_retrieval defaults:
+    k = 16 blocks of 64, window 2048, 4 sinks) for nseq sequences at context n: block bounds from the summaries,
+    top-16 selection, exact attention over sinks + selected blocks + window.  HBM-bound: algorithmic bytes = the
+    summaries of the candidate blocks plus every attended key and value, read once."""
+    from heimdall_b200 import _lib
+    from heimdall_b200.functional import ptr
+    Sk, Wk, Lk, Kk = 4, 2048, 64, 16
+    gen = torch.Generator(device=device).manual_seed(11)
+    bf = torch.bfloat16
+    k = torch.randn(nseq, G, n, D, generator=gen, device=device, dtype=bf)
+    v = torch.randn(nseq, G, n, D, generator=gen, device=device, dtype=bf)
+    nbcap = (n - Sk) // Lk
+    kmin = torch.empty(nseq, G, nbcap, D, device=device, dtype=bf)
+    kmax = torch.empty_like(kmin)
+    _lib.call("bf_ret_summarize", ptr(k), n, nseq, G, D, Sk, Lk, 0, nbcap, ptr(kmin), ptr(kmax), nbcap, None)
+    q = torch.randn(nseq, H, D, generator=gen, device=device, dtype=bf)
+    o = torch.empty(nseq, H, D, device=device)
+    nws = _lib.size("bf_ret_decode_workspace", nseq, H, G, D, n, Sk, Wk, Lk, Kk)
+    ws = torch.empty(nws, dtype=torch.uint8, device=device)
+    call = lambda: _lib.call("bf_ret_decode", ptr(q), ptr(k), ptr(v), n, ptr(kmin), ptr(kmax), nbcap, nseq, H, G, D,
+                             n, Sk, Wk, Lk, Kk, ptr(o), ptr(ws), nws,
+                             torch.cuda.current_stream(device).cuda_stream)
+    ms = _time_device(call, steps, warmup)
+    nc = (n - Wk - Sk) // Lk
+    nk = Sk + Kk * Lk + (n - Sk - nc * Lk)
+    nbytes = nseq * G * (2 * nc * D * 2 + 2 * nk * D * 2) + nseq * H * D * (2 + 4)
+    pk, _ = peaks()
+    del k, v
+    return {"workload": f"{nseq} sequences at context {n}, one kept layer (24 query / 4 KV heads, D=256): "
+                        f"retrieval decode, top-{Kk} blocks of {Lk} + window {Wk} + {Sk} sinks ({nk} keys attended)",
+            "us_per_step": ms * 1e3, "us_per_token": ms * 1e3 / nseq, "bytes": nbytes,
+            "achieved_gbs": nbytes / (ms * 1e-3) / 1e9, "frac": nbytes / (ms * 1e-3) / 1e9 / pk["hbm_gbs"]}
+
+
 def run_interchange(device, nseq=64, steps=20, warmup=3):
     """The llama.cpp state-row interchange at config-2 geometry (64 sequences, W = 2048, one layer): pack the
     decode cache into the port's rows and unpack them again.  Both are HBM-bound copies (rows 43.7 MB per
@@ -737,6 +773,7 @@ def main(argv=None):
     ap.add_argument("--no-delta", action="store_true")
     ap.add_argument("--no-config1", action="store_true")
     ap.add_argument("--no-interchange", action="store_true", help="skip the llama.cpp state-row leg")
+    ap.add_argument("--no-retrieval", action="store_true", help="skip the kept layers' retrieval decode leg")
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":
@@ -949,6 +986,8 @@ def run_ours(args, ctx):
         out["decode"] = decode
     if world == 1 and not args.no_interchange:
         out["interchange"] = run_interchange(dev)
+    if world == 1 and not args.no_retrieval:
+        out["retrieval"] = run_retrieval(dev)
     print(json.dumps(out), flush=True)
 
 

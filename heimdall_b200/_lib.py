@@ -47,6 +47,9 @@ SIGNATURES = {
     "bf_gdn_apply_prefix": [_P, _P, _I, _P, _P, _I, _I, _I, _P],
     "bf_bifrost_layer_prefill_sp": [_P, _P, _P, _P, _P, _P, _P, _L, _I, _I, _P, _P, _P, _I, _I, _P, _P, _P, _P, _P,
                                     _Z, _P],
+    "bf_ret_summarize": [_P, _L, _I, _I, _I, _I, _I, _I, _I, _P, _P, _L, _P],
+    "bf_ret_decode_workspace": [_I, _I, _I, _I, _I, _I, _I, _I, _I],
+    "bf_ret_decode": [_P, _P, _P, _L, _P, _P, _L, _I, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _Z, _P],
     "bf_llama_state_floats": [_I, _I, _I, _I],
     "bf_llama_state_pack": [_P, _P, _I, _I, _I, _I, _I, _P, _L, _P],
     "bf_llama_state_unpack": [_P, _L, _P, _I, _I, _I, _I, _I, _P, _P],
@@ -54,7 +57,8 @@ SIGNATURES = {
 _RESTYPE = {"bf_strerror": ctypes.c_char_p, "bf_last_cuda_error": ctypes.c_char_p, "bf_layer_weights_bytes": _Z, "bf_layer_decode_workspace": _Z,
             "bf_gdn_chunk_workspace": _Z, "bf_window_workspace": _Z, "bf_layer_prefill_workspace": _Z,
             "bf_layer_prefill_sp_workspace": _Z,
-            "bf_gdn_segment_workspace": _Z, "bf_llama_state_floats": _Z}
+            "bf_gdn_segment_workspace": _Z, "bf_llama_state_floats": _Z,
+            "bf_ret_decode_workspace": _Z}
 
 _lock = threading.Lock()
 _lib = None

@@ -27,7 +27,8 @@ enum Stage { ST_XPROJ = 0, ST_HEADPROJ, ST_GDN_P1, ST_GDN_P2, ST_GDN_P3, ST_WIN_
 bool aligned16(const void* p);
 // Opts `fn` into `bytes` of dynamic shared memory on the current device.  cudaFuncSetAttribute applies to
 // the current device only, so this is done once per (kernel, device), under a lock; later calls only look
-// the pair up.  Returns BF_OK or BF_ERR_CUDA.
+// the pair up -- so `bytes` must be the kernel's largest launch size, the same on every call.  Returns BF_OK or
+// BF_ERR_CUDA.
 int ensure_smem_attr(const void* fn, int bytes);
 // BF_ERR_CUDA with the CUDA error recorded for bf_last_cuda_error (e: a failed call's result, or the pending
 // launch error when e is cudaSuccess); launch_status() is BF_OK or that

@@ -317,7 +317,8 @@ int bf_llama_state_pack(const bf_ring_cache* cache, const int64_t* next_pos, int
   DeviceState st;
   if ((rc = device_state(&st))) return rc;
   const int smem = kLS_Slots * ls_vpitch(a.m.GD) * 2;
-  if ((rc = ensure_smem_attr((const void*)llama_pack_slots_kernel, smem))) return rc;
+  // the attribute is set once per device, to the largest staging (G = 8)
+  if ((rc = ensure_smem_attr((const void*)llama_pack_slots_kernel, kLS_Slots * ls_vpitch(8 * kLS_D) * 2))) return rc;
   llama_pack_slots_kernel<<<dim3(a.m.LR / kLS_Slots, B), kLS_Threads, smem, stream>>>(a);
   if ((rc = launch_status())) return rc;
   llama_state_delta_kernel<true><<<dim3(D / 32, D / 32, B * G), dim3(32, 8), 0, stream>>>(a);

@@ -11,6 +11,8 @@ methods that implement the converted (Bifrost) layer core:
   HybridAttention._student                        (hibrit.py:363-424)   -> BifrostLayer.student
   HybridAttention._window                         (hibrit.py:336-361)   -> functional.window_attention
   HybridAttention._mem_inputs                     (hibrit.py:327-334)   -> BifrostLayer.mem_inputs
+  HybridAttention._teacher                        (hibrit.py:275-290)   -> retrieval.teacher (kept layers: causal
+                                                                           attention, retrieval decode)
 
 The module-level ``delta_rule`` / ``delta_rule_step`` of ``heimdall.kernels`` and their by-value copies in
 ``heimdall.hibrit`` (hibrit.py:32) are deliberately left alone: the model's linear-attention layers (Qwen3.5
@@ -31,12 +33,14 @@ import importlib
 import torch
 
 from . import functional as F_
+from . import retrieval as R_
 from .layer import BifrostLayer
 
 _SAVED: list = []          # (owner, attribute name, original value) in patch order
 # what install() replaces: (module key, attribute path)
 PATCHED_NAMES = (("motor", "delta_rule_gqa"), ("motor", "window_attention"), ("hibrit", "HybridAttention._student"),
-                 ("hibrit", "HybridAttention._mem_inputs"), ("hibrit", "HybridAttention._window"))
+                 ("hibrit", "HybridAttention._mem_inputs"), ("hibrit", "HybridAttention._window"),
+                 ("hibrit", "HybridAttention._teacher"))
 SELF_TEST_TOL = 0.03       # the reference's acceptance threshold (kernels.py:182)
 
 
@@ -138,6 +142,13 @@ def _window(self, qr, ext_k, ext_v, ext_pos, sink_k, sink_v, pos):
     return F_.window_attention(qr, ext_k, ext_v, qpos0, kpos0, self.sinks, self.window, sink_k, sink_v)
 
 
+def _teacher(self, qr, kr, v, cache):
+    """HybridAttention._teacher (hibrit.py:275-290): full attention of a kept layer over its growing cache, with
+    the retrieval branch of ``set_retrieval`` (hibrit.py:292-324) for single-token decode."""
+    _require_cuda(qr, kr, v)
+    return R_.teacher(qr, kr, v, cache, getattr(self, "retrieval", None))
+
+
 def window_attention(a, qr, kr, v):
     """heimdall.motor.window_attention (motor.py:105-115): the window and sinks of a whole sequence from an empty
     ring (positions 0 .. t-1), the cache-free path of HybridAttention._student.  Returns o [B,t,H,D], lse [B,H,t].
@@ -171,6 +182,7 @@ def install(modules=None) -> None:
         _patch(cls, "_student", _student)
         _patch(cls, "_mem_inputs", _mem_inputs)
         _patch(cls, "_window", _window)
+        _patch(cls, "_teacher", _teacher)
     except Exception:
         uninstall()
         raise

@@ -304,6 +304,27 @@ int bf_bifrost_layer_prefill_sp(const bf_layer* L, const void* x, const void* q,
  * D = 256, G even and at most 8; rows 16-byte aligned with row_stride a multiple of 4, ring_km 16-byte and the
  * bf16 arrays 8-byte aligned (else BF_ERR_ALIGNMENT).  Both are layout copies on `stream` (HBM-bound).
  */
+/* ---------------------------------------------------------------------------------------------
+ * Retrieval attention of the kept (not converted) full-attention layers, single-token decode: replaces the
+ * retrieval branch of HybridAttention._teacher (heimdall/hibrit.py:275-290) and _retrieval_mask (:301-324).
+ * The query at position n - 1 attends the sinks [0, sinks), the `topk` blocks of `block` keys with the largest
+ * upper bound of q.k (max over the group's query heads of sum_d max(q_d, 0) kmax_d + min(q_d, 0) kmin_d) among
+ * the nc = (n - window - sinks) / block blocks that end before the window, and the window
+ * [sinks + nc * block, n - 1]; exact softmax, scale D^-1/2.  Requires n - sinks - window >= topk * block.
+ *
+ * bf_ret_summarize: per-dim key min / max of full blocks nb0 .. nb1 - 1 after the sinks:
+ *   k [B,G,cap,D] bf16 -> kmin, kmax [B,G,nbcap,D] bf16 (exact).
+ * bf_ret_decode: q [B,H,D] bf16 (RoPE'd), k / v [B,G,cap,D] bf16 (the cache, n keys valid, the new token's at
+ *   n - 1), kmin / kmax of the first nc blocks -> o [B,H,D] fp32.  Workspace: bf_ret_decode_workspace().
+ * D = 256, H / G <= 8, topk <= 64.
+ */
+int bf_ret_summarize(const void* k, long long cap, int B, int G, int D, int sinks, int block, int nb0, int nb1,
+                     void* kmin, void* kmax, long long nbcap, bf_stream_t stream);
+size_t bf_ret_decode_workspace(int B, int H, int G, int D, int n, int sinks, int window, int block, int topk);
+int bf_ret_decode(const void* q, const void* k, const void* v, long long cap, const void* kmin, const void* kmax,
+                  long long nbcap, int B, int H, int G, int D, int n, int sinks, int window, int block, int topk,
+                  float* o, void* ws, size_t ws_bytes, bf_stream_t stream);
+
 size_t bf_llama_state_floats(int G, int D, int window, int sinks);
 int bf_llama_state_pack(const bf_ring_cache* cache, const int64_t* next_pos, int B, int G, int D, int window,
                         int sinks, float* rows, long long row_stride, bf_stream_t stream);

@@ -32,6 +32,12 @@ def pytest_configure(config):
 
 
 @pytest.fixture(scope="session")
+def golden_retrieval():
+    import torch
+    return torch.load(ROOT / "tests" / "golden" / "golden_retrieval.pt", weights_only=False)
+
+
+@pytest.fixture(scope="session")
 def golden_gdn():
     import torch
     return torch.load(ROOT / "tests" / "golden" / "golden_gdn.pt", weights_only=False)

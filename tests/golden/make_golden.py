@@ -172,10 +172,30 @@ def gguf_case(proj):
             "tensors": {i: {k: torch.from_numpy(v.copy()) for k, v in t.items()} for i, t in out.items()}}
 
 
+def retrieval_case(hb):
+    """The reference's retrieval mask (HybridAttention._retrieval_mask, hibrit.py:301-324) and the attention its
+    _teacher computes with it (scaled_dot_product_attention with enable_gqa, hibrit.py:283-284), on seeded
+    bf16-valued inputs: the test_hibrit.py shapes, a decode token at Bifrost head geometry and a prefill."""
+    out = {}
+    cases = [("small", 1, 4, 2, 8, 50, 3, dict(k=2, block=4, window=6, sinks=2)),
+             ("decode_d256", 1, 24, 4, 256, 600, 1, dict(k=4, block=16, window=256, sinks=4)),
+             ("prefill_d64", 1, 8, 2, 64, 700, 5, dict(k=3, block=32, window=128, sinks=4, prefill=True))]
+    for i, (name, B, H, G, D, n, t, ret) in enumerate(cases):
+        gen = torch.Generator().manual_seed(300 + i)
+        qr = bf(torch.randn(B, H, t, D, generator=gen))
+        kr = bf(torch.randn(B, G, n, D, generator=gen))
+        vt = bf(torch.randn(B, G, n, D, generator=gen))
+        mask = hb.HybridAttention._retrieval_mask(None, qr, kr, ret)
+        o = F.scaled_dot_product_attention(qr, kr, vt, attn_mask=mask, enable_gqa=True).transpose(1, 2)
+        b16 = lambda z: z.to(torch.bfloat16)   # bf16-valued: stored exactly in half the bytes
+        out[name] = dict(qr=b16(qr), kr=b16(kr), vt=b16(vt), ret=ret, mask=mask, o=o)
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("HEIMDALL_REFERENCE"))
-    ap.add_argument("--cases", default="all", help="comma list of gdn, layer, forward, gguf (default all)")
+    ap.add_argument("--cases", default="all", help="comma list of gdn, layer, forward, gguf, retrieval (default all)")
     args = ap.parse_args()
     if not args.ref:
         ap.error("name the reference project with --ref or HEIMDALL_REFERENCE")
@@ -186,9 +206,11 @@ def main():
     import heimdall.kernels as hk
     import heimdall.motor as hm
     torch.set_num_threads(8)
-    cases = {"gdn", "layer", "forward", "gguf"} if args.cases == "all" else set(args.cases.split(","))
+    cases = {"gdn", "layer", "forward", "gguf", "retrieval"} if args.cases == "all" else set(args.cases.split(","))
     if "gguf" in cases:
         torch.save(gguf_case(proj), HERE / "golden_gguf.pt")
+    if "retrieval" in cases:
+        torch.save(retrieval_case(hb), HERE / "golden_retrieval.pt")
     if "gdn" in cases:
         torch.save(gdn_cases(hk, hm), HERE / "golden_gdn.pt")
     layers = {}
@@ -210,7 +232,7 @@ def main():
     if "forward" in cases:
         torch.save(fwd, HERE / "golden_forward.pt")
     meta = {"torch": torch.__version__,
-            "reference": "Heimdall (heimdall.kernels / motor / hibrit; llamacpp/bifrost_gguf.py)"}
+            "reference": "Heimdall (heimdall.kernels / motor / hibrit incl. _retrieval_mask; llamacpp/bifrost_gguf.py)"}
     (HERE / "golden_meta.txt").write_text("\n".join(f"{k}: {v}" for k, v in meta.items()) + "\n")
     for f in sorted(HERE.glob("golden_*.pt")):
         print(f.name, f.stat().st_size)

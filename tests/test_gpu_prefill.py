@@ -184,6 +184,34 @@ def test_layer_mixed_parts_vs_oracle(parts, W):
     assert torch.equal(cache["ring_pos"].cpu(), cache_r["ring_pos"])
 
 
+@pytest.mark.parametrize("scale", [64.0, 512.0])
+def test_layer_large_values_vs_oracle(scale):
+    """Values as a real v_proj gives them (not normalised): v scaled up to 512 passes through the fp16 value
+    operands of the window (P V) and the delta rule (u, v', state copies) within tolerance; prefill with a ring,
+    then decode steps."""
+    dev = _dev()
+    from heimdall_b200 import BifrostLayer
+    H, G, D, d, S, W = 24, 4, 256, 128, 4, 128
+    p = layer_params(H, G, D, d, window=W, sinks=S, archival=1, seed=21)
+    parts = (300, 1, 200, 1)
+    x, q, k, v, qr, kr = _layer_inputs(H, G, D, d, sum(parts), seed=23)
+    v = (v.float() * scale).to(torch.bfloat16)
+    f = lambda z: z.float()
+    L = BifrostLayer.from_params(p, dev)
+    cache_r, cache, s = {}, {}, 0
+    for n in parts:
+        sl = slice(s, s + n)
+        o_ref = ob.student(p, f(x[:, sl]), f(q[:, sl]), f(k[:, sl]), f(v[:, sl]), f(qr[:, :, sl]), f(kr[:, :, sl]),
+                           s, cache_r, dtype=torch.float64)
+        o = L.student(x[:, sl].to(dev), q[:, sl].to(dev), k[:, sl].to(dev), v[:, sl].to(dev), qr[:, :, sl].to(dev),
+                      kr[:, :, sl].to(dev), s, cache)
+        torch.cuda.synchronize()
+        assert torch.isfinite(o).all()
+        assert ob.rel_l2(o.cpu(), o_ref) < O_TOL, (s, n)
+        s += n
+    assert ob.rel_l2(cache["S"].cpu(), cache_r["S"]) < S_TOL
+
+
 def test_batch_equals_single():
     """B=2 equals two B=1 runs (the reference's native multi-sequence check, done on the layer core)."""
     dev = _dev()

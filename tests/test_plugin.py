@@ -21,7 +21,7 @@ def fake_modules():
     hibrit.delta_rule = hibrit.delta_rule_step = orig
 
     class HybridAttention(torch.nn.Module):
-        _student = _window = _mem_inputs = orig
+        _student = _window = _mem_inputs = _teacher = orig
     hibrit.HybridAttention = HybridAttention
     motor = types.ModuleType("heimdall.motor")
     motor.delta_rule_gqa = motor.window_attention = orig
@@ -41,7 +41,7 @@ def test_install_patches_and_uninstall_restores():
         assert m["motor"].window_attention is plugin.window_attention
         cls = m["hibrit"].HybridAttention
         assert cls._student is plugin._student and cls._window is plugin._window
-        assert cls._mem_inputs is plugin._mem_inputs
+        assert cls._mem_inputs is plugin._mem_inputs and cls._teacher is plugin._teacher
         plugin.install(m)            # idempotent
     finally:
         plugin.uninstall()

@@ -38,7 +38,8 @@ def _names(m):
             ("motor", "window_attention"): m["motor"].window_attention,
             ("hibrit", "HybridAttention._student"): A.__dict__["_student"],
             ("hibrit", "HybridAttention._mem_inputs"): A.__dict__["_mem_inputs"],
-            ("hibrit", "HybridAttention._window"): A.__dict__["_window"]}
+            ("hibrit", "HybridAttention._window"): A.__dict__["_window"],
+            ("hibrit", "HybridAttention._teacher"): A.__dict__["_teacher"]}
 
 
 def test_install_replaces_only_the_bifrost_path(heimdall_modules):
