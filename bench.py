@@ -683,6 +683,11 @@ def cpu_baseline(min_seconds=10.0, n_new=2048):
 HEADLINE_T = 131072
 
 
+def _set_headline(T: int) -> None:
+    global HEADLINE_T
+    HEADLINE_T = int(T)
+
+
 def arm_config(world):
     return {"workload": f"BASELINE config 3 at T={HEADLINE_T}: one Bifrost layer prefill of one {HEADLINE_T}-token "
                         f"sequence (B=1, 24q/4kv heads, D=256, W=2048, 4 sinks, d=5120, from an empty cache) split "
@@ -763,6 +768,8 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--T", type=int, default=32768, help="config-1 sequence length")
+    ap.add_argument("--headline-T", type=int, default=HEADLINE_T,
+                    help="headline sequence length (default 131072; smaller only for profiling captures)")
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--decode-seqs", type=int, default=64)
     ap.add_argument("--decode-layers", type=int, default=12)
@@ -776,6 +783,7 @@ def main(argv=None):
     ap.add_argument("--no-retrieval", action="store_true", help="skip the kept layers' retrieval decode leg")
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)
+    _set_headline(args.headline_T)
     if args.impl == "reference":
         # the CPU arm touches no GPU and joins no process group: rank 0 runs, the others leave
         run_reference(args, int(os.environ.get("RANK", "0")))

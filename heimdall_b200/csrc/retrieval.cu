@@ -10,9 +10,10 @@
 //
 // Three kernels, all HBM-bound:
 //   ret_summary_kernel: the min / max of each new full block (bf16, exact), one CTA per block and KV head;
-//   ret_select_kernel:  per (batch, KV head) the bounds of all candidate blocks from the summaries, then the k
-//                       largest by k rounds of a block-wide argmax (selected blocks in ascending order);
-//   ret_attn_kernel:    split over the attended keys (sinks, selected blocks, window as one virtual sequence):
+//   ret_bounds_kernel:  per (batch, KV head, split of 256 candidate blocks) the bounds from the summaries (four
+//                       blocks per warp iteration, loads in flight), then the split's k largest;
+//   ret_merge_kernel:   per (batch, KV head) the k largest of the splits' candidates (ascending order);
+//   ret_attn_kernel:    split over the attended keys (sinks, selected blocks, window as one virtual sequence), 64 per CTA:
 //                       each CTA stages 64 keys and values at a time in shared memory, computes the R query
 //                       heads' scores (four threads per key, a quarter of D each), an online softmax per head
 //                       and P V (one thread per value column), and writes its partial (max, sum, acc);
@@ -26,8 +27,9 @@ namespace bfb {
 constexpr int kRA_D = 256;
 constexpr int kRA_MaxR = 8;
 constexpr int kRA_Chunk = 64;       // keys staged per step
-constexpr int kRA_Split = 256;      // keys per CTA of the attention
-constexpr int kRA_SelSmem = 200 * 1024;   // dynamic shared memory of the selection: the largest number of bounds
+constexpr int kRA_Split = 64;       // keys per CTA of the attention (one staged chunk: CTAs overlap each other's loads)
+constexpr int kRA_SelBlocks = 256;  // candidate blocks per CTA of the bounds kernel
+constexpr int kRA_MaxCand = 4096;   // candidates merged per (b, g): splits x k
 
 struct RetArgs {
   const __nv_bfloat16* q;     // [B, H, D]
@@ -36,10 +38,12 @@ struct RetArgs {
   const __nv_bfloat16* kmin;  // [B, G, nbcap, D]
   const __nv_bfloat16* kmax;
   int* sel;                   // [B, G, K]
+  float* cand_v;              // [B, G, nsel, K] per-split candidates (bound, block)
+  int* cand_i;
   float* part;                // [B, G, nsplit, R, D + 2]
   float* o;                   // [B, H, D]
   long long cap, nbcap;       // key / block capacity of the cache arrays
-  int B, H, G, R, n, S, W, L, K, nc, nk, nsplit;
+  int B, H, G, R, n, S, W, L, K, nc, nk, nsplit, nsel;
 };
 
 __global__ void __launch_bounds__(256) ret_summary_kernel(const __nv_bfloat16* __restrict__ k, long long cap,
@@ -66,15 +70,16 @@ __device__ __forceinline__ void bf16x8_to_f(const uint4& u, float (&f)[8]) {
   }
 }
 
-// one CTA per (b, g); dynamic shared memory: nc floats of bounds
-__global__ void __launch_bounds__(256) ret_select_kernel(RetArgs a) {
-  extern __shared__ float s_ub[];
+// bounds of one split of the candidate blocks, then the split's k largest (bound, index) pairs.  Grid
+// (B * G, nsel): split s takes candidates [s * kRA_SelBlocks, ...); each warp computes four blocks' bounds per
+// iteration with all eight summary loads in flight (lanes over D, one warp reduction per query head)
+__global__ void __launch_bounds__(256) ret_bounds_kernel(RetArgs a) {
+  __shared__ float s_ub[kRA_SelBlocks];
   __shared__ float s_wv[8];
   __shared__ int s_wi[8];
-  __shared__ int s_pick[64];
-  const int bg = blockIdx.x, b = bg / a.G, g = bg % a.G;
+  const int bg = blockIdx.x, b = bg / a.G, g = bg % a.G, split = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // the group's queries: lane l holds dims 8l .. 8l + 7 of each head
+  const int c0 = split * kRA_SelBlocks, nloc = min(kRA_SelBlocks, a.nc - c0);
   float qv[kRA_MaxR][8];
 #pragma unroll
   for (int r = 0; r < kRA_MaxR; ++r) {
@@ -85,30 +90,43 @@ __global__ void __launch_bounds__(256) ret_select_kernel(RetArgs a) {
       for (int e = 0; e < 8; ++e) qv[r][e] = 0.f;
     }
   }
-  const __nv_bfloat16* mnp = a.kmin + (size_t)bg * a.nbcap * kRA_D;
-  const __nv_bfloat16* mxp = a.kmax + (size_t)bg * a.nbcap * kRA_D;
-  for (int c = warp; c < a.nc; c += 8) {
-    float lo[8], hi[8];
-    bf16x8_to_f(__ldg(reinterpret_cast<const uint4*>(mnp + (size_t)c * kRA_D) + lane), lo);
-    bf16x8_to_f(__ldg(reinterpret_cast<const uint4*>(mxp + (size_t)c * kRA_D) + lane), hi);
-    float best = -INFINITY;
+  const __nv_bfloat16* mnp = a.kmin + ((size_t)bg * a.nbcap + c0) * kRA_D;
+  const __nv_bfloat16* mxp = a.kmax + ((size_t)bg * a.nbcap + c0) * kRA_D;
+  for (int c = warp * 4; c < nloc; c += 32) {
+    uint4 lo4[4], hi4[4];
 #pragma unroll
-    for (int r = 0; r < kRA_MaxR; ++r) {
-      if (r >= a.R) break;
-      float s = 0.f;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) s += fmaxf(qv[r][e], 0.f) * hi[e] + fminf(qv[r][e], 0.f) * lo[e];
-      s = warp_sum(s);
-      best = fmaxf(best, s);
+    for (int u = 0; u < 4; ++u) {
+      lo4[u] = hi4[u] = make_uint4(0u, 0u, 0u, 0u);
+      if (c + u < nloc) {
+        lo4[u] = __ldg(reinterpret_cast<const uint4*>(mnp + (size_t)(c + u) * kRA_D) + lane);
+        hi4[u] = __ldg(reinterpret_cast<const uint4*>(mxp + (size_t)(c + u) * kRA_D) + lane);
+      }
     }
-    if (lane == 0) s_ub[c] = best;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      float lo[8], hi[8];
+      bf16x8_to_f(lo4[u], lo);
+      bf16x8_to_f(hi4[u], hi);
+      float best = -INFINITY;
+#pragma unroll
+      for (int r = 0; r < kRA_MaxR; ++r) {
+        if (r >= a.R) break;
+        float s = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) s += fmaxf(qv[r][e], 0.f) * hi[e] + fminf(qv[r][e], 0.f) * lo[e];
+        best = fmaxf(best, warp_sum(s));
+      }
+      if (lane == 0 && c + u < nloc) s_ub[c + u] = best;
+    }
   }
   __syncthreads();
-  // the K largest bounds: K rounds of a block-wide argmax (ties to the smaller index)
+  // this split's k largest: k rounds of a block-wide argmax (ties to the smaller index)
+  float* out_v = a.cand_v + ((size_t)bg * a.nsel + split) * a.K;
+  int* out_i = a.cand_i + ((size_t)bg * a.nsel + split) * a.K;
   for (int kk = 0; kk < a.K; ++kk) {
     float bv = -INFINITY;
     int bi = 0x7fffffff;
-    for (int c = threadIdx.x; c < a.nc; c += 256) {
+    for (int c = threadIdx.x; c < nloc; c += 256) {
       const float x = s_ub[c];
       if (x > bv || (x == bv && c < bi)) { bv = x; bi = c; }
     }
@@ -125,12 +143,48 @@ __global__ void __launch_bounds__(256) ret_select_kernel(RetArgs a) {
       int i0 = s_wi[0];
       for (int w = 1; w < 8; ++w)
         if (s_wv[w] > v0 || (s_wv[w] == v0 && s_wi[w] < i0)) { v0 = s_wv[w]; i0 = s_wi[w]; }
-      s_pick[kk] = i0;
-      if (i0 >= 0 && i0 < a.nc) s_ub[i0] = -INFINITY;
+      const bool ok = i0 >= 0 && i0 < nloc;
+      out_v[kk] = ok ? v0 : -INFINITY;
+      out_i[kk] = ok ? c0 + i0 : 0x7fffffff;
+      if (ok) s_ub[i0] = -INFINITY;
     }
     __syncthreads();
   }
-  if (threadIdx.x == 0) {   // ascending order (insertion sort of at most 64)
+}
+
+// merge the splits' candidates of one (b, g) into the k selected blocks, in ascending order (one warp)
+__global__ void __launch_bounds__(32) ret_merge_kernel(RetArgs a) {
+  const int bg = blockIdx.x, lane = threadIdx.x;
+  const int ncand = a.nsel * a.K;
+  const float* cv = a.cand_v + (size_t)bg * ncand;
+  const int* ci = a.cand_i + (size_t)bg * ncand;
+  __shared__ int s_pick[64];
+  __shared__ unsigned char s_used[kRA_MaxCand];
+  for (int i = lane; i < ncand; i += 32) s_used[i] = 0;
+  __syncwarp();
+  for (int kk = 0; kk < a.K; ++kk) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff, bj = -1;
+    for (int i = lane; i < ncand; i += 32) {
+      if (s_used[i]) continue;
+      const float x = cv[i];
+      const int xi = ci[i];
+      if (x > bv || (x == bv && xi < bi)) { bv = x; bi = xi; bj = i; }
+    }
+#pragma unroll
+    for (int off = 16; off; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+      const int oj = __shfl_xor_sync(0xffffffffu, bj, off);
+      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; bj = oj; }
+    }
+    if (lane == 0) {
+      s_pick[kk] = bi;
+      if (bj >= 0) s_used[bj] = 1;
+    }
+    __syncwarp();
+  }
+  if (lane == 0) {   // ascending order (insertion sort of at most 64)
     for (int i = 1; i < a.K; ++i) {
       const int x = s_pick[i];
       int j = i - 1;
@@ -327,8 +381,10 @@ size_t bf_ret_decode_workspace(int B, int H, int G, int D, int n, int sinks, int
   const int nc = max(0, min((n - 1 - window + 1 - sinks) / block, nb));
   const long long nk = (long long)sinks + (long long)k * block + (n - sinks - (long long)nc * block);
   const long long nsplit = (nk + kRA_Split - 1) / kRA_Split;
+  const long long nsel = (nc + kRA_SelBlocks - 1) / kRA_SelBlocks;
   const size_t sel = ((size_t)B * G * k * 4 + 255) / 256 * 256;
-  return sel + (size_t)B * G * nsplit * (H / G) * (kRA_D + 2) * 4;
+  const size_t cand = ((size_t)B * G * (nsel > 0 ? nsel : 1) * k * 4 + 255) / 256 * 256;
+  return sel + 2 * cand + (size_t)B * G * nsplit * (H / G) * (kRA_D + 2) * 4;
 }
 
 int bf_ret_decode(const void* q, const void* k, const void* v, long long cap, const void* kmin, const void* kmax,
@@ -359,18 +415,21 @@ int bf_ret_decode(const void* q, const void* k, const void* v, long long cap, co
   if (a.nc > nbcap) return BF_ERR_INVALID_ARGUMENT;
   a.nk = sinks + topk * block + (n - sinks - a.nc * block);
   a.nsplit = (a.nk + kRA_Split - 1) / kRA_Split;
+  a.nsel = (a.nc + kRA_SelBlocks - 1) / kRA_SelBlocks;
+  if (a.nsel * topk > kRA_MaxCand) return BF_ERR_UNSUPPORTED;
+  const size_t sel_b = ((size_t)B * G * topk * 4 + 255) / 256 * 256;
+  const size_t cand_b = ((size_t)B * G * a.nsel * topk * 4 + 255) / 256 * 256;
   a.sel = static_cast<int*>(ws);
-  a.part = reinterpret_cast<float*>(static_cast<char*>(ws) + ((size_t)B * G * topk * 4 + 255) / 256 * 256);
+  a.cand_v = reinterpret_cast<float*>(static_cast<char*>(ws) + sel_b);
+  a.cand_i = reinterpret_cast<int*>(static_cast<char*>(ws) + sel_b + cand_b);
+  a.part = reinterpret_cast<float*>(static_cast<char*>(ws) + sel_b + 2 * cand_b);
   a.o = o;
   DeviceState st;
   int rc = device_state(&st);
   if (rc) return rc;
-  // the bounds of all candidate blocks live in shared memory: up to kRA_SelSmem / 4 blocks (3.3M tokens at
-  // block 64); the kernel's attribute is set once, to that maximum
-  const int sel_smem = a.nc * 4 > 16 ? a.nc * 4 : 16;
-  if (sel_smem > kRA_SelSmem) return BF_ERR_UNSUPPORTED;
-  if ((rc = ensure_smem_attr((const void*)ret_select_kernel, kRA_SelSmem))) return rc;
-  ret_select_kernel<<<B * G, 256, sel_smem, stream>>>(a);
+  ret_bounds_kernel<<<dim3(B * G, a.nsel), 256, 0, stream>>>(a);
+  if ((rc = launch_status())) return rc;
+  ret_merge_kernel<<<B * G, 32, 0, stream>>>(a);
   if ((rc = launch_status())) return rc;
   const int asmem = ret_smem_attn();
   if ((rc = ensure_smem_attr((const void*)ret_attn_kernel, asmem))) return rc;
