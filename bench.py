@@ -600,6 +600,36 @@ def run_retrieval(device, nseq=16, n=131072, steps=20, warmup=3):
             "achieved_gbs": nbytes / (ms * 1e-3) / 1e9, "frac": nbytes / (ms * 1e-3) / 1e9 / pk["hbm_gbs"]}
 
 
+def run_backward(device, T=8192, steps=3, warmup=3):
+    """Backward of ``delta_rule_gqa`` as seq_loss (motor.py:149-193) takes it: one segment of the conversion
+    engine's length (8192 tokens), 4 KV heads x 6 query heads, D = 256, fp32, with an initial state and the
+    final state's gradient.  The recurrence is sequential in the tokens (fp32, 32 CTAs of 32 value columns per
+    KV head); the figure that bounds it is the dependent chain per token, so the leg reports microseconds per
+    token beside the forward's time on the same inputs and the bytes the kernel moves (checkpoints, the
+    per-chunk state scratch, the per-token partials)."""
+    from heimdall_b200.functional import delta_rule_gqa, delta_rule_gqa_backward
+    gen = torch.Generator(device=device).manual_seed(5)
+    r = lambda *s: torch.randn(*s, generator=gen, device=device)
+    q = torch.nn.functional.normalize(r(1, T, G, R, D), dim=-1) * D ** -0.5
+    k = torch.nn.functional.normalize(r(1, T, G, D), dim=-1)
+    v = r(1, T, G, D)
+    g = -torch.rand(1, T, G, generator=gen, device=device) * 0.1
+    beta = torch.rand(1, T, G, generator=gen, device=device)
+    s0 = r(1, G, D, D) * 0.05
+    do = r(1, T, G, R, D)
+    dsT = r(1, G, D, D) * 0.05
+    bwd_ms = _time_device(lambda: delta_rule_gqa_backward(q, k, v, g, beta, s0, do, dsT), steps, warmup)
+    with torch.no_grad():
+        fwd_ms = _time_device(lambda: delta_rule_gqa(q, k, v, g, beta, 64, s0), steps, warmup)
+    state = G * D * D * 4
+    ncta, E = D // 32, (R + 1) * D + 2
+    nbytes = (T // 64) * state * 2 + T * state * 2 + T * G * ncta * E * 4 * 2 + T * G * (R * D * 2 + 3 * D) * 4 * 3
+    return {"workload": f"one {T}-token segment, {G} KV heads x {R} query heads, D={D}, fp32: dq, dk, dv, dg, dbeta, "
+                        "ds0 from dL/do and dL/dS_T",
+            "bwd_ms": bwd_ms, "fwd_ms": fwd_ms, "us_per_token": bwd_ms * 1e3 / T, "bytes": nbytes,
+            "achieved_gbs": nbytes / (bwd_ms * 1e-3) / 1e9, "bound": "latency (sequential in tokens)"}
+
+
 def run_interchange(device, nseq=64, steps=20, warmup=3):
     """The llama.cpp state-row interchange at config-2 geometry (64 sequences, W = 2048, one layer): pack the
     decode cache into the port's rows and unpack them again.  Both are HBM-bound copies (rows 43.7 MB per
@@ -781,6 +811,7 @@ def main(argv=None):
     ap.add_argument("--no-config1", action="store_true")
     ap.add_argument("--no-interchange", action="store_true", help="skip the llama.cpp state-row leg")
     ap.add_argument("--no-retrieval", action="store_true", help="skip the kept layers' retrieval decode leg")
+    ap.add_argument("--no-backward", action="store_true", help="skip the delta-rule backward leg")
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)
     _set_headline(args.headline_T)
@@ -996,6 +1027,8 @@ def run_ours(args, ctx):
         out["interchange"] = run_interchange(dev)
     if world == 1 and not args.no_retrieval:
         out["retrieval"] = run_retrieval(dev)
+    if world == 1 and not args.no_backward:
+        out["backward"] = run_backward(dev)
     print(json.dumps(out), flush=True)
 
 

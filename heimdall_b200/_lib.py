@@ -34,6 +34,8 @@ SIGNATURES = {
     "bf_bifrost_layer_decode_noalloc": [_P, _P, _P, _P, _P, _P, _P, _P, _I, _P, _I, _P, _P, _P],
     "bf_gdn_chunk_workspace": [_I, _I, _I, _I, _I, _I],
     "bf_gdn_chunk_fwd": [_P, _I, _P, _I, _P, _I, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _Z, _P],
+    "bf_gdn_bwd_workspace": [_I, _I, _I, _I, _I],
+    "bf_gdn_bwd": [_P] * 14 + [_I, _I, _I, _I, _I, _P, _Z, _P],
     "bf_window_workspace": [_I, _I, _I, _I],
     "bf_window_attn_fwd": [_P, _P, _P, _L, _L, _L, _P, _P, _I, _L, _L, _L, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P,
                            _Z, _P],
@@ -58,7 +60,7 @@ _RESTYPE = {"bf_strerror": ctypes.c_char_p, "bf_last_cuda_error": ctypes.c_char_
             "bf_gdn_chunk_workspace": _Z, "bf_window_workspace": _Z, "bf_layer_prefill_workspace": _Z,
             "bf_layer_prefill_sp_workspace": _Z,
             "bf_gdn_segment_workspace": _Z, "bf_llama_state_floats": _Z,
-            "bf_ret_decode_workspace": _Z}
+            "bf_ret_decode_workspace": _Z, "bf_gdn_bwd_workspace": _Z}
 
 _lock = threading.Lock()
 _lib = None

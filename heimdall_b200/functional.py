@@ -89,8 +89,18 @@ def delta_rule_gqa(q, k, v, g, beta, chunk: int = 64, state=None, cu_seqlens=Non
     depend on the chunk length).
     ``cu_seqlens`` (int tensor [n+1], cumulative lengths, B = 1): the T tokens are n packed sequences, each
     with its own recurrence; state and the returned final states are then [n,G,Dk,Dv].
+    Differentiable (as the reference's torch ops are, which seq_loss, motor.py:149-193, trains through): with
+    grad mode on and an input that requires grad, the backward runs ``bf_gdn_bwd`` (fp32, all six inputs).
     """
     check_cuda(q, k, v, g, beta, state, cu_seqlens)
+    if torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in (q, k, v, g, beta, state)):
+        if cu_seqlens is not None:
+            raise NotImplementedError("heimdall_b200: the delta-rule backward takes unpacked sequences (no cu_seqlens)")
+        return _DeltaRuleGQA.apply(q, k, v, g, beta, state)
+    return _delta_rule_gqa_fwd(q, k, v, g, beta, state, cu_seqlens)
+
+
+def _delta_rule_gqa_fwd(q, k, v, g, beta, state, cu_seqlens):
     B, T, G, R, D = q.shape
     if k.shape[-1] != D or v.shape[-1] != D:
         raise NotImplementedError("heimdall_b200 implements square states (Dk == Dv)")
@@ -116,6 +126,47 @@ def delta_rule_gqa(q, k, v, g, beta, chunk: int = 64, state=None, cu_seqlens=Non
     _lib.call("bf_gdn_chunk_fwd", ptr(qq), _dt(qq), ptr(kk), _dt(kk), ptr(vv), _dt(vv), ptr(gg), ptr(bb), ptr(s0),
               ptr(o), ptr(s_out), ptr(cu), n_seq, B, T, G, R, D, ptr(ws), nws, stream_handle())
     return o, s_out
+
+
+def delta_rule_gqa_backward(q, k, v, g, beta, state, do, dstate):
+    """Gradients of ``delta_rule_gqa`` (B sequences of T tokens): (dq, dk, dv, dg, dbeta, dstate0), all fp32 in the
+    inputs' shapes; ``do`` = dL/do [B,T,G,R,D] and ``dstate`` = dL/d(final state) [B,G,D,D], either may be None
+    (zero).  The torch autograd of motor.py:70-102 as seq_loss (motor.py:149-193) takes it, on ``bf_gdn_bwd``."""
+    check_cuda(q, k, v, g, beta, state, do, dstate)
+    B, T, G, R, D = q.shape
+    if D != 256 or k.shape[-1] != D or v.shape[-1] != D:
+        raise NotImplementedError("the delta-rule backward is built for head dim 256")
+    dev = q.device
+    f = lambda t: None if t is None else t.float().contiguous()
+    qq, kk, vv, gg, bb, s0, dd, dst = (f(t) for t in (q, k, v, g, beta, state, do, dstate))
+    if dd is None:
+        dd = torch.zeros(B, T, G, R, D, device=dev)
+    dq, dk, dv = torch.empty_like(qq), torch.empty_like(kk), torch.empty_like(vv)
+    dg, db = torch.empty_like(gg), torch.empty_like(bb)
+    ds0 = torch.empty(B, G, D, D, device=dev)
+    nws = _lib.size("bf_gdn_bwd_workspace", B, T, G, R, D)
+    ws = _ws(nws, dev)
+    _lib.call("bf_gdn_bwd", ptr(qq), ptr(kk), ptr(vv), ptr(gg), ptr(bb), ptr(s0), ptr(dd), ptr(dst), ptr(dq), ptr(dk),
+              ptr(dv), ptr(dg), ptr(db), ptr(ds0), B, T, G, R, D, ptr(ws), nws, stream_handle())
+    return dq, dk, dv, dg, db, ds0
+
+
+class _DeltaRuleGQA(torch.autograd.Function):
+    """delta_rule_gqa with its backward on the GPU: forward on the chunked tensor-core scan, backward on
+    ``bf_gdn_bwd`` from the saved inputs (the states are recomputed, none is kept)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, g, beta, state):
+        o, s = _delta_rule_gqa_fwd(q, k, v, g, beta, state, None)
+        ctx.save_for_backward(q, k, v, g, beta, state)
+        return o, s
+
+    @staticmethod
+    def backward(ctx, do, dstate):
+        q, k, v, g, beta, state = ctx.saved_tensors
+        dq, dk, dv, dg, db, ds0 = delta_rule_gqa_backward(q, k, v, g, beta, state, do, dstate)
+        return (dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype), dg.to(g.dtype), db.to(beta.dtype),
+                None if state is None else ds0.to(state.dtype))
 
 
 def delta_rule(q, k, v, g, beta, chunk_size: int = 64, initial_state=None, backend: str = "auto", cu_seqlens=None):

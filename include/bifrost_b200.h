@@ -190,6 +190,20 @@ int bf_gdn_chunk_fwd(const void* q, int q_dtype, const void* k, int k_dtype, con
                      bf_stream_t stream);
 
 /* ------------------------------------------------------------------------------------------
+ * Chunked gated delta rule, backward (GQA-native): the gradients that torch autograd takes through
+ * heimdall/motor.py:70-102 (delta_rule_gqa) when seq_loss (heimdall/motor.py:149-193) trains a layer.
+ * Inputs as the forward, all fp32: q [B,T,G*R,D], k [B,T,G,D], v [B,T,G,D], g, beta [B,T,G],
+ * s0 [B,G,D,D] or NULL (zero initial state); dout [B,T,G*R,D] = dL/do; dstate [B,G,D,D] = dL/d(final
+ * state) or NULL (zero).  Outputs fp32, same shapes as the inputs: dq, dk, dv, dg, dbeta and ds0
+ * (dL/ds0, written also when s0 is NULL).  D must be 256, R <= 8.  The recurrence runs token by token
+ * in fp32 (states recomputed from 64-token checkpoints); see bf_gdn_bwd_workspace for the scratch.
+ */
+size_t bf_gdn_bwd_workspace(int B, int T, int G, int R, int D);
+int bf_gdn_bwd(const float* q, const float* k, const float* v, const float* g, const float* beta, const float* s0,
+               const float* dout, const float* dstate, float* dq, float* dk, float* dv, float* dg, float* dbeta,
+               float* ds0, int B, int T, int G, int R, int D, void* ws, size_t ws_bytes, bf_stream_t stream);
+
+/* ------------------------------------------------------------------------------------------
  * Sliding-window + sink attention with log-sum-exp (fp32 softmax), replacing
  * heimdall/hibrit.py:336-361 (_window / _window_fp32).
  * qr [B,H,Tq,D] bf16, query i at position qpos0 + i.  k_ext [B,G,Tk,D] bf16, key j at position
