@@ -603,7 +603,7 @@ def run_retrieval(device, nseq=16, n=131072, steps=20, warmup=3):
 def run_backward(device, T=8192, steps=3, warmup=3):
     """Backward of ``delta_rule_gqa`` as seq_loss (motor.py:149-193) takes it: one segment of the conversion
     engine's length (8192 tokens), 4 KV heads x 6 query heads, D = 256, fp32, with an initial state and the
-    final state's gradient.  The recurrence is sequential in the tokens (fp32, 32 CTAs of 32 value columns per
+    final state's gradient.  The recurrence is sequential in the tokens (fp32, 32 CTAs of 8 value columns per
     KV head); the figure that bounds it is the dependent chain per token, so the leg reports microseconds per
     token beside the forward's time on the same inputs and the bytes the kernel moves (checkpoints, the
     per-chunk state scratch, the per-token partials)."""
@@ -622,7 +622,7 @@ def run_backward(device, T=8192, steps=3, warmup=3):
     with torch.no_grad():
         fwd_ms = _time_device(lambda: delta_rule_gqa(q, k, v, g, beta, 64, s0), steps, warmup)
     state = G * D * D * 4
-    ncta, E = D // 32, (R + 1) * D + 2
+    ncta, E = D // 8, (R + 1) * D + 2          # CTAs of 8 value columns per KV head
     nbytes = (T // 64) * state * 2 + T * state * 2 + T * G * ncta * E * 4 * 2 + T * G * (R * D * 2 + 3 * D) * 4 * 3
     return {"workload": f"one {T}-token segment, {G} KV heads x {R} query heads, D={D}, fp32: dq, dk, dv, dg, dbeta, "
                         "ds0 from dL/do and dL/dS_T",
