@@ -264,22 +264,26 @@ def run_sp(L, device, ctx, T_total, steps=5, warmup=2):
     world, rank = ctx["world"], ctx["rank"]
     T = T_total // world
     ins = make_inputs(T, seed=11 + rank, device=device)
-    if world > 1:
+    gr = None
+    if world > 1:   # timed: the captured step (StudentSPGraph); the instrumented step below runs eagerly
+        gr = sp.StudentSPGraph(L, *ins, warmup=warmup)
+        timed = gr.replay
         step = lambda **kw: sp.student_sp(L, *ins, **kw)
     else:
-        step = lambda **kw: (L.student(*ins, 0, {}), None)
-    for _ in range(warmup):
-        step()
+        timed = lambda: L.student(*ins, 0, {})
+        for _ in range(warmup):
+            timed()
     torch.cuda.synchronize()
     barrier(ctx)
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     for _ in range(steps):
-        step()
+        timed()
     b.record()
     torch.cuda.synchronize()
     t = torch.tensor([a.elapsed_time(b) / steps], device=device)
     if world > 1:
+        gr.check()
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     ms = float(t.item())
     res = {"workload": f"BASELINE config 3: one sequence of {T_total} tokens split over {world} GPU(s) "
@@ -297,9 +301,10 @@ def run_sp(L, device, ctx, T_total, steps=5, warmup=2):
     handles = [ctypes_array([e.cuda_event for e in es]) for es in evs]
     timeline = []
     barrier(ctx)
-    o, cache = step(timeline=timeline, phase_hook=_sp_stage_hook(handles))
+    step(timeline=timeline, phase_hook=_sp_stage_hook(handles))
     torch.cuda.synchronize()
     _lib.call("bf_stage_events", None, 0)
+    o, cache = gr.o, gr.cache          # parity below is checked on the timed (graph) step's results
     t0 = timeline[0][1]
     marks = {lab: round(t0.elapsed_time(ev), 4) for lab, ev in timeline}
     stages = {}
@@ -312,7 +317,8 @@ def run_sp(L, device, ctx, T_total, steps=5, warmup=2):
     per_rank = [None] * world
     torch.distributed.all_gather_object(per_rank, {"rank": rank, "marks_ms": marks, "stages_ms": stages})
     res["timeline"] = per_rank
-    res["timeline_note"] = ("ms from the start of one instrumented step on each rank; marks are student_sp's steps "
+    res["timeline_note"] = ("ms from the start of one instrumented step (eager, not the captured graph that is "
+                            "timed) on each rank; marks are student_sp's steps "
                             "on its stream, stages are [begin, end] of the kernels of phase 0 (memory inputs, P1, "
                             "state-map scan, window) and phase 1 (scan from the incoming state, memory reads)")
     # parity: the last rank's final state and last outputs against one pass over the whole sequence on rank 0
@@ -327,6 +333,8 @@ def run_sp(L, device, ctx, T_total, steps=5, warmup=2):
         torch.distributed.recv(S_last, last)
         torch.distributed.recv(o_last, last)
     del o, cache, ins
+    gr = None                          # the graph holds NCCL calls: released before any process-group teardown
+    torch.cuda.synchronize()
     if rank == 0:
         torch.cuda.empty_cache()
         full = [torch.empty(1, T_total, *shape[2:], device=device, dtype=torch.bfloat16) if i < 4 else
@@ -901,8 +909,10 @@ def run_headline(L, dev, ctx, args):
     world, rank = ctx["world"], ctx["rank"]
     T = HEADLINE_T // world
     ins = make_inputs(T, seed=11 + rank, device=dev)
-    if world > 1:
-        step = lambda: sp.student_sp(L, *ins)
+    gr = None
+    if world > 1:   # the sequence-parallel step captured once (collectives included) and replayed
+        gr = sp.StudentSPGraph(L, *ins, warmup=args.warmup)
+        step = gr.replay
     else:
         step = lambda: L.student(*ins, 0, {})
     for _ in range(args.warmup):
@@ -923,8 +933,9 @@ def run_headline(L, dev, ctx, args):
     per = [evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
     t = torch.tensor([evs[0].elapsed_time(evs[-1]) / args.steps], device=dev)
     if world > 1:
+        gr.check()
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    del ins
+    del ins, gr
     diag = {"step_ms_min": min(per), "step_ms_median": statistics.median(per), "step_ms_max": max(per),
             "host_enqueue_ms_per_step": (h1 - h0) * 1e3 / args.steps}
     return float(t.item()), clocks, diag

@@ -125,13 +125,12 @@ __device__ __forceinline__ unsigned long long ret_key(float v, int blk) {
 }
 __device__ __forceinline__ int ret_key_block(unsigned long long key) { return (int)(0xffffffffu - (uint32_t)key); }
 
+// warp-wide max of a 64-bit key: the high words' max, then the low words' max among the lanes holding it
 __device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long x) {
-#pragma unroll
-  for (int off = 16; off; off >>= 1) {
-    const unsigned long long o = __shfl_xor_sync(0xffffffffu, x, off);
-    x = o > x ? o : x;
-  }
-  return x;
+  const unsigned hi = (unsigned)(x >> 32), lo = (unsigned)x;
+  const unsigned mhi = __reduce_max_sync(0xffffffffu, hi);
+  const unsigned mlo = __reduce_max_sync(0xffffffffu, hi == mhi ? lo : 0u);
+  return ((unsigned long long)mhi << 32) | mlo;
 }
 
 // query heads of group g in the B-operand layout: lane (g, c) holds head g's dims [32p + 8c, +8) for p = 0..7
@@ -265,16 +264,12 @@ __global__ void __launch_bounds__(128) ret_merge_kernel(RetArgs a) {
     }
   }
   __syncwarp();
-  if (lane == 0) {   // ascending order (insertion sort of at most 64)
-    for (int i = 1; i < a.K; ++i) {
-      const int x = s_pick[i];
-      int j = i - 1;
-      while (j >= 0 && s_pick[j] > x) { s_pick[j + 1] = s_pick[j]; --j; }
-      s_pick[j + 1] = x;
-    }
+  for (int i = lane; i < a.K; i += 32) {   // ascending order: each pick goes to its rank (the blocks are distinct)
+    const int x = s_pick[i];
+    int rank = 0;
+    for (int j = 0; j < a.K; ++j) rank += s_pick[j] < x;
+    a.sel[(size_t)bg * a.K + rank] = x;
   }
-  __syncwarp();
-  for (int i = lane; i < a.K; i += 32) a.sel[(size_t)bg * a.K + i] = s_pick[i];
 }
 
 // key position of virtual index i: the sinks, then the selected blocks, then the window
@@ -424,24 +419,25 @@ __global__ void __launch_bounds__(128, 2) ret_attn_kernel(RetArgs a) {
   }
 }
 
-// grid B * H: merge the splits of one (b, query head) in one pass (running max; loads issued sixteen at a time)
-__global__ void __launch_bounds__(256) ret_combine_kernel(RetArgs a) {
+// grid (B * H, 2): merge the splits of one (b, query head) for 128 of its dims in one pass (running max; loads
+// issued eight splits at a time)
+__global__ void __launch_bounds__(128) ret_combine_kernel(RetArgs a) {
   const int bh = blockIdx.x, b = bh / a.H, h = bh % a.H, g = h / a.R, r = h % a.R;
-  const int bg = b * a.G + g;
+  const int bg = b * a.G + g, d = blockIdx.y * 128 + threadIdx.x;
   const float* pp = a.part + (size_t)bg * a.nsplit * a.R * (kRA_D + 2) + r * (kRA_D + 2);
   const size_t sstride = (size_t)a.R * (kRA_D + 2);
   float M = -INFINITY, Lsum = 0.f, acc = 0.f;
-  for (int s0 = 0; s0 < a.nsplit; s0 += 16) {   // sixteen splits' loads in flight, then their merge
-    float mv[16], lv[16], xv[16];
+  for (int s0 = 0; s0 < a.nsplit; s0 += 8) {
+    float mv[8], lv[8], xv[8];
 #pragma unroll
-    for (int u = 0; u < 16; ++u) {
+    for (int u = 0; u < 8; ++u) {
       const int s = s0 + u;
       mv[u] = s < a.nsplit ? pp[s * sstride + kRA_D] : -INFINITY;
       lv[u] = s < a.nsplit ? pp[s * sstride + kRA_D + 1] : 0.f;
-      xv[u] = s < a.nsplit ? pp[s * sstride + threadIdx.x] : 0.f;
+      xv[u] = s < a.nsplit ? pp[s * sstride + d] : 0.f;
     }
 #pragma unroll
-    for (int u = 0; u < 16; ++u) {
+    for (int u = 0; u < 8; ++u) {
       if (mv[u] > M) {
         const float sc = M == -INFINITY ? 0.f : ex2_approx(M - mv[u]);
         acc *= sc;
@@ -453,7 +449,7 @@ __global__ void __launch_bounds__(256) ret_combine_kernel(RetArgs a) {
       Lsum += lv[u] * w;
     }
   }
-  a.o[((size_t)b * a.H + h) * kRA_D + threadIdx.x] = Lsum > 0.f ? acc / Lsum : 0.f;
+  a.o[((size_t)b * a.H + h) * kRA_D + d] = Lsum > 0.f ? acc / Lsum : 0.f;
 }
 
 }  // namespace bfb
@@ -536,7 +532,7 @@ int bf_ret_decode(const void* q, const void* k, const void* v, long long cap, co
   if ((rc = launch_status())) return rc;
   ret_attn_kernel<<<dim3(B * G, a.nsplit), 128, 0, stream>>>(a);
   if ((rc = launch_status())) return rc;
-  ret_combine_kernel<<<B * H, kRA_D, 0, stream>>>(a);
+  ret_combine_kernel<<<dim3(B * H, kRA_D / 128), 128, 0, stream>>>(a);
   return launch_status();
 }
 

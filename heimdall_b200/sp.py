@@ -121,16 +121,17 @@ def student_sp(L, x, q, k, v, qr, kr, group=None, memory: bool = True, timeline=
     if validate not in ("deferred", "sync", "off"):
         raise ValueError("validate must be 'deferred', 'sync' or 'off'")
     if x.device.type != "cuda":   # the host logic on CPU tensors (a CPU restatement of the layer)
-        o, cache, finite = _student_sp(L, x, q, k, v, qr, kr, group, memory, None, None)
-        if finite is not None and validate != "off":
-            _raise_if_corrupted(finite)
+        o, cache, fin = _student_sp(L, x, q, k, v, qr, kr, group, memory, None, None)
+        if fin is not None and validate != "off":
+            _raise_if_corrupted((fin, None))
         return o, cache
     check_maps(x.device)          # the previous call's maps on this device
     cur = torch.cuda.current_stream(x.device)
     hp = _priority_stream(x.device)
     hp.wait_stream(cur)
     with torch.cuda.stream(hp):
-        o, cache, finite = _student_sp(L, x, q, k, v, qr, kr, group, memory, timeline, phase_hook)
+        o, cache, fin = _student_sp(L, x, q, k, v, qr, kr, group, memory, timeline, phase_hook)
+        finite = _flags_to_host(fin) if fin is not None and validate != "off" else None
     cur.wait_stream(hp)   # later work on the caller's stream (reuse of the inputs' memory included) waits
     for t in [o, *(z for z in cache.values() if isinstance(z, torch.Tensor))]:
         t.record_stream(cur)   # allocated on the priority stream, used on the caller's
@@ -143,6 +144,50 @@ def student_sp(L, x, q, k, v, qr, kr, group=None, memory: bool = True, timeline=
 
 
 _PENDING = {}   # device index -> (flags in pinned host memory, event) of the last call's gathered maps
+
+
+class StudentSPGraph:
+    """``student_sp`` captured once as a CUDA graph and replayed: the whole sequence-parallel step (sink
+    broadcast, halo exchange, both layer phases with the window on its side stream, the all-gather of the
+    state maps and the fold) is one graph launch per step.  The eager step issues about a hundred kernel,
+    copy and NCCL calls from Python, and at 16K tokens per GPU that enqueue (about 2.5 ms) is longer than the
+    GPU's work; the graph removes it.
+
+    The graph reads fixed input buffers: ``inputs`` = (x, q, k, v, qr, kr) as given (bf16, contiguous; copy
+    each step's tokens into them before ``replay()``).  ``o`` and ``cache`` are the graph's own tensors,
+    rewritten by every replay (the same layouts as ``student_sp``'s results).  ``check()`` raises the
+    corrupted-map error of the last replay (it waits for the device).  Every rank of ``group`` constructs it
+    and replays it in step: the graph holds the collectives.  Construction runs ``warmup`` eager steps first
+    (NCCL communicators, the point-to-point pairs included, side streams and kernel attributes are set up
+    outside the capture)."""
+
+    def __init__(self, L, x, q, k, v, qr, kr, group=None, memory: bool = True, warmup: int = 2):
+        if x.device.type != "cuda":
+            raise ValueError("StudentSPGraph needs CUDA tensors")
+        bf = torch.bfloat16
+        self.inputs = tuple(z if (z.dtype == bf and z.is_contiguous()) else z.to(bf).contiguous()
+                            for z in (x, q, k, v, qr, kr))
+        for _ in range(max(1, int(warmup))):
+            student_sp(L, *self.inputs, group=group, memory=memory, validate="sync")
+        torch.cuda.synchronize(x.device)
+        self.graph = torch.cuda.CUDAGraph()
+        hp = _priority_stream(x.device)
+        with torch.cuda.graph(self.graph, capture_error_mode="thread_local"):
+            cur = torch.cuda.current_stream(x.device)
+            hp.wait_stream(cur)
+            with torch.cuda.stream(hp):
+                self.o, self.cache, self._fin = _student_sp(L, *self.inputs, group, memory, None, None)
+            cur.wait_stream(hp)
+        torch.cuda.synchronize(x.device)
+
+    def replay(self) -> None:
+        """One step on the current stream."""
+        self.graph.replay()
+
+    def check(self) -> None:
+        """Raise if a rank sent a non-finite state map in the last replay (waits for the device)."""
+        if self._fin is not None:
+            _raise_if_corrupted((self._fin.cpu(), None))
 
 
 def check_maps(device=None) -> None:
@@ -232,12 +277,13 @@ def _student_sp(L, x, q, k, v, qr, kr, group, memory, timeline, phase_hook):
 
 
 def _maps_finite(Ms, Ns):
-    """Per segment, whether its gathered state map is finite (a rank that sent NaN or inf).  On a GPU the
-    flags are computed on the device and copied to pinned host memory behind an event, so the check does not
-    hold back the second phase: ``_raise_if_corrupted`` waits for the flags only, after it is launched."""
-    fin = torch.isfinite(Ms).flatten(1).all(1) & torch.isfinite(Ns).flatten(1).all(1)
-    if not fin.is_cuda:
-        return fin, None
+    """Per segment, whether its gathered state map is finite (a rank that sent NaN or inf), on the maps' device."""
+    return torch.isfinite(Ms).flatten(1).all(1) & torch.isfinite(Ns).flatten(1).all(1)
+
+
+def _flags_to_host(fin):
+    """The flags copied to pinned host memory behind an event, so the check does not hold back the second
+    phase: ``_raise_if_corrupted`` waits for the flags only, after it is launched."""
     host = torch.empty(fin.shape, dtype=torch.bool, pin_memory=True)
     host.copy_(fin, non_blocking=True)
     ev = torch.cuda.Event()

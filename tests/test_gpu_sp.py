@@ -178,6 +178,75 @@ def test_student_sp_two_gpus(tmp_path):
     assert ob.rel_l2(parts[1]["S"], cache["S"].cpu()) < S_TOL
 
 
+def _sp_graph_rank(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import datetime
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    gr = None
+    try:
+        from heimdall_b200 import BifrostLayer, sp
+        H, G, D, d, W, S, T = 24, 4, 256, 128, 256, 4, 512
+        p = layer_params(H, G, D, d, window=W, sinks=S, archival=1, seed=8)
+        L = BifrostLayer.from_params(p, dev)
+        sl = slice(rank * T, (rank + 1) * T)
+        part = lambda seed: [z.to(dev, torch.bfloat16).contiguous() for z in (lambda a: (
+            a[0][:, sl], a[1][:, sl], a[2][:, sl], a[3][:, sl], a[4][:, :, sl], a[5][:, :, sl]))(
+            _layer_inputs(H, G, D, d, world * T, seed=seed))]
+        a, b = part(9), part(10)
+        gr = sp.StudentSPGraph(L, *[z.clone() for z in a])
+        res = {}
+        for name, ins in (("a", a), ("b", b), ("a2", a)):      # new tokens copied into the graph's inputs
+            for dst, src in zip(gr.inputs, ins):
+                dst.copy_(src)
+            gr.replay()
+            gr.check()
+            torch.cuda.synchronize()
+            res[name] = {"o": gr.o.cpu(), "S": gr.cache["S"].cpu()}
+        o_e, c_e = sp.student_sp(L, *b)
+        torch.cuda.synchronize()
+        res["eager_b"] = {"o": o_e.cpu(), "S": c_e["S"].cpu()}
+        torch.save(res, f"{out}.{rank}")
+        dist.barrier()
+    finally:
+        gr = None                 # the graph holds NCCL calls: release it before the process group
+        torch.cuda.synchronize()
+        dist.destroy_process_group()
+
+
+def test_student_sp_graph_two_gpus(tmp_path):
+    """The captured step (StudentSPGraph) replayed with two sets of tokens equals the eager step and one
+    prefill of the whole sequence on one GPU."""
+    dev = _dev()
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    out = str(tmp_path / "spg")
+    mp.spawn(_sp_graph_rank, args=(2, port, out), nprocs=2, join=True)
+    from heimdall_b200 import BifrostLayer
+    H, G, D, d, W, S, T = 24, 4, 256, 128, 256, 4, 512
+    p = layer_params(H, G, D, d, window=W, sinks=S, archival=1, seed=8)
+    L = BifrostLayer.from_params(p, dev)
+    parts = [torch.load(f"{out}.{r}") for r in range(2)]
+    for seed, name in ((9, "a"), (10, "b"), (9, "a2")):
+        x, q, k, v, qr, kr = (z.to(dev) for z in _layer_inputs(H, G, D, d, 2 * T, seed=seed))
+        cache = {}
+        o_ref = L.student(x, q, k, v, qr, kr, 0, cache)
+        torch.cuda.synchronize()
+        assert ob.rel_l2(torch.cat([pt[name]["o"] for pt in parts], 1), o_ref.cpu()) < O_TOL, name
+        assert ob.rel_l2(parts[1][name]["S"], cache["S"].cpu()) < S_TOL, name
+    for r in range(2):
+        assert ob.rel_l2(parts[r]["b"]["o"], parts[r]["eager_b"]["o"]) < 1e-5
+        assert ob.rel_l2(parts[r]["b"]["S"], parts[r]["eager_b"]["S"]) < 1e-5
+
+
 def _cache_cpu(c):
     return {k_: (v_.cpu().float() if v_.is_floating_point() else v_.cpu()) for k_, v_ in c.items()}
 

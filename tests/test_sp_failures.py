@@ -115,8 +115,8 @@ def test_finite_check_flags_only_bad_segments():
     N[2, 0, 1, 3, 3] = float("inf")
     flags = sp._maps_finite(M, N)
     try:
-        sp._raise_if_corrupted(flags)
+        sp._raise_if_corrupted((flags, None))
         raise AssertionError("no error raised")
     except RuntimeError as e:
         assert "segment(s) [2]" in str(e)
-    sp._raise_if_corrupted(sp._maps_finite(M, torch.zeros_like(M)))
+    sp._raise_if_corrupted((sp._maps_finite(M, torch.zeros_like(M)), None))
