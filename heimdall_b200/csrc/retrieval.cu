@@ -327,12 +327,16 @@ __global__ void __launch_bounds__(128, 2) ret_attn_kernel(RetArgs a) {
       v2[j] = ldg_stream(vb + (size_t)pv2 * kRA_D + 64 * j + 8 * rg);
       v3[j] = ldg_stream(vb + (size_t)pv3 * kRA_D + 64 * j + 8 * rg);
     }
-    float s[4] = {0.f, 0.f, 0.f, 0.f};   // S[key rg | rg + 8][heads 2c, 2c + 1]
+    // S[key rg | rg + 8][heads 2c, 2c + 1], accumulated in four independent tiles (short dependent chains)
+    float sp4[4][4] = {};
 #pragma unroll
     for (int p = 0; p < 8; ++p) {
-      mma_bf16_16816(s, ka[p].x, kc[p].x, ka[p].y, kc[p].y, qu[p].x, qu[p].y);
-      mma_bf16_16816(s, ka[p].z, kc[p].z, ka[p].w, kc[p].w, qu[p].z, qu[p].w);
+      mma_bf16_16816(sp4[(2 * p) & 3], ka[p].x, kc[p].x, ka[p].y, kc[p].y, qu[p].x, qu[p].y);
+      mma_bf16_16816(sp4[(2 * p + 1) & 3], ka[p].z, kc[p].z, ka[p].w, kc[p].w, qu[p].z, qu[p].w);
     }
+    float s[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) s[e] = (sp4[0][e] + sp4[1][e]) + (sp4[2][e] + sp4[3][e]);
     const bool ok0 = k0 + rg < cnt, ok1 = k0 + rg + 8 < cnt;
     s[0] = ok0 ? s[0] * qs : -INFINITY;
     s[1] = ok0 ? s[1] * qs : -INFINITY;
