@@ -320,9 +320,9 @@ static int layer_prefill_impl(const bf_layer* L, const void* x, const void* q, c
   // the fork/join events are released when the call returns, on every path (an event recorded for work still
   // in flight may be destroyed: the release is deferred until that work completes)
   struct Events {
-    cudaEvent_t fork = nullptr, win = nullptr, mem = nullptr, vt = nullptr, piece[kWinPieces] = {};
+    cudaEvent_t fork = nullptr, win = nullptr, mem = nullptr, vt = nullptr, p1 = nullptr, piece[kWinPieces] = {};
     ~Events() {
-      for (cudaEvent_t e : {fork, win, mem, vt})
+      for (cudaEvent_t e : {fork, win, mem, vt, p1})
         if (e) cudaEventDestroy(e);
       for (cudaEvent_t e : piece)
         if (e) cudaEventDestroy(e);
@@ -403,7 +403,18 @@ static int layer_prefill_impl(const bf_layer* L, const void* x, const void* q, c
       const int parts = phase == kPhaseBegin ? (kGdnP1 | kGdnP2)
                         : phase == kPhaseFinish ? (s.s0 ? kGdnFix : 0)
                                                 : (kGdnP1 | kGdnP2);
-      rc = launch_gdn_prefill(s, wsm, parts);
+      if (phase == kPhaseBegin && will_read && win_here && (parts & kGdnP1)) {
+        // sequence-parallel first phase: the window starts once P1 is done, so the projections and P1 have the
+        // whole GPU and the window's CTAs fill the SMs that the latency-bound map scan leaves idle
+        rc = launch_gdn_prefill(s, wsm, kGdnP1);
+        if (rc) return rc;
+        if (cudaEventCreateWithFlags(&evs.p1, cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventRecord(evs.p1, wsm) != cudaSuccess || cudaStreamWaitEvent(ws2, evs.p1, 0) != cudaSuccess)
+          return cuda_fail();
+        rc = launch_gdn_prefill(s, wsm, parts & ~kGdnP1);
+      } else {
+        rc = launch_gdn_prefill(s, wsm, parts);
+      }
       if (rc) return rc;
       if (phase == kPhaseFinish) {
         float* s_fin = reinterpret_cast<float*>(extra + gdn_prefill_fix_workspace(B, G, s.n_steps));
