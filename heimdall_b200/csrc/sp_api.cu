@@ -28,8 +28,10 @@ __global__ void sp_bf16_to_f32_kernel(const __nv_bfloat16* __restrict__ x, float
     y[i] = __bfloat162float(x[i]);
 }
 
-// out = A @ S + N for one (b, g) matrix of a batch: 64 x 64 output tile per CTA, 4 x 4 per thread, fp32
-constexpr int kSM_T = 64, kSM_K = 16;
+// out = A @ S + N for one (b, g) matrix of a batch: 64 x 64 output tile per CTA, 4 x 4 per thread, fp32; k in
+// slabs of 64 (four load rounds for D = 256, each thread's 16 + 16 loads issued before its stores): the fold of
+// the segment maps runs these one after another on the critical path, so each launch is latency-bound
+constexpr int kSM_T = 64, kSM_K = 64;
 __global__ void __launch_bounds__(256) state_map_kernel(const float* __restrict__ A, const float* __restrict__ S,
                                                         const float* __restrict__ N, float* __restrict__ out,
                                                         int D) {
@@ -42,11 +44,21 @@ __global__ void __launch_bounds__(256) state_map_kernel(const float* __restrict_
   const int t = threadIdx.x, ti = (t >> 4) * 4, tj = (t & 15) * 4;
   float acc[4][4] = {};
   for (int k0 = 0; k0 < D; k0 += kSM_K) {
-    for (int e = t; e < kSM_T * kSM_K; e += 256) {
+    constexpr int kPer = kSM_T * kSM_K / 256;
+    float av_[kPer], sv_[kPer];
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+      const int e = t + 256 * u;
       const int r = e / kSM_K, c = e % kSM_K;        // A[i0 + r][k0 + c]
-      As[c][r] = A[(size_t)(i0 + r) * D + k0 + c];
+      av_[u] = A[(size_t)(i0 + r) * D + k0 + c];
       const int r2 = e / kSM_T, c2 = e % kSM_T;      // S[k0 + r2][j0 + c2]
-      Ss[r2][c2] = S[(size_t)(k0 + r2) * D + j0 + c2];
+      sv_[u] = S[(size_t)(k0 + r2) * D + j0 + c2];
+    }
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+      const int e = t + 256 * u;
+      As[e % kSM_K][e / kSM_K] = av_[u];
+      Ss[e / kSM_T][e % kSM_T] = sv_[u];
     }
     __syncthreads();
 #pragma unroll
